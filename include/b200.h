@@ -1,0 +1,164 @@
+/*
+ * b200.h — C ABI of the B200-native backend for speech.cpp's quantized matrix products.
+ *
+ * speech.cpp computes every weight product as a ggml node inside a ggml backend: MUL_MAT (src/common/graph.h:15-19),
+ * MUL_MAT_ID (src/common/graph.h:22-26) and quantized GET_ROWS (src/families/qwen3-tts/talker.cpp:131-133,
+ * src/families/qwen3-asr/decoder.cpp:319), run by ggml_backend_graph_compute (src/common/graph.cpp:145-147). A ggml
+ * backend ("ggml-b200") forwards those nodes to the functions below; INTEGRATION.md gives the ggml_backend_i /
+ * buffer-type glue. Everything here takes plain pointers and sizes: no C++ or torch types, no exceptions.
+ *
+ * Conventions
+ *  - Type ids are GGUF / ggml type ids (the reference lists them in checks/compare/quantize_compare.py:27).
+ *  - A matrix of `type` has ne0 = K values per row and ne1 = N rows; ne2 = E stacks E such matrices (experts).
+ *  - Activations and outputs are float32, row-major: x [M][K] is M rows of K values (ggml src1 [K, M]); dst [M][N]
+ *    (ggml dst [N, M]).
+ *  - Pointers named dev_* or documented as device pointers live in the context's GPU memory; *_host functions take
+ *    host memory and copy inside the call.
+ *  - Calls are asynchronous on the context's stream unless they say otherwise. b200_synchronize() waits and reports
+ *    errors found on the device (an id out of range, a bounded wait that gave up).
+ *  - Results are computed as ggml's CPU backend computes them: each activation row is quantized to the weight type's
+ *    vec_dot type (q8_0 for Q8_0, q8_K for Q4_K / Q6_K, bf16 for BF16) bit-identically, each (sub-)block's int32 sum
+ *    is exact, and sums are scaled and accumulated in float32.
+ */
+#ifndef SPEECH_B200_H
+#define SPEECH_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+/* Status codes. A ggml adapter maps B200_ERR_ALLOC to GGML_STATUS_ALLOC_FAILED and every other error to
+ * GGML_STATUS_FAILED, which speech.cpp turns into Fault::OutOfMemory / Fault::Device (src/common/graph.cpp:139-140). */
+typedef enum b200_status {
+    B200_OK = 0,
+    B200_ERR_INVALID = -1,     /* a null pointer, a bad shape, a row length that is not whole blocks */
+    B200_ERR_UNSUPPORTED = -2, /* a type or op this backend does not compute */
+    B200_ERR_ALLOC = -3,       /* device memory could not be allocated */
+    B200_ERR_DEVICE = -4,      /* a CUDA error (b200_last_error() has the text) */
+    B200_ERR_RANGE = -5,       /* an id (row or expert) outside its table, found on the device */
+    B200_ERR_TIMEOUT = -6      /* a bounded device-side wait gave up */
+} b200_status;
+
+enum {
+    B200_TYPE_F32 = 0,
+    B200_TYPE_F16 = 1,
+    B200_TYPE_Q8_0 = 8,
+    B200_TYPE_Q4_K = 12,
+    B200_TYPE_Q6_K = 14,
+    B200_TYPE_Q8_K = 15,
+    B200_TYPE_BF16 = 30
+};
+
+/* ------------------------------------------------------------------------------------------------------------
+ * Devices. Replaces the ggml device registry speech.cpp enumerates once (src/common/backend.cpp:113-131) and the
+ * free-memory query Drama 3's placement uses (src/engines/drama3-engine.cpp:56-58: ggml_backend_dev_memory).
+ * ------------------------------------------------------------------------------------------------------------ */
+int b200_device_count(void);
+/* name: e.g. "B200_0" (up to name_len bytes with the NUL); free / total device bytes. Any output may be NULL. */
+b200_status b200_device_info(int device, char * name, size_t name_len, size_t * free_bytes, size_t * total_bytes);
+
+/* ------------------------------------------------------------------------------------------------------------
+ * Contexts: one device, one stream, a scratch pool. Replaces ggml_backend_dev_init (src/common/backend.cpp:158-163),
+ * whose NULL return speech.cpp maps to Fault::Device. One request per context at a time (include/speech.h:27).
+ * ------------------------------------------------------------------------------------------------------------ */
+typedef struct b200_context b200_context;
+
+b200_status b200_context_create(int device, b200_context ** out);
+void b200_context_destroy(b200_context * ctx);
+/* The context's cudaStream_t. */
+void * b200_context_stream(b200_context * ctx);
+/* Waits for the stream; returns the first device-side error recorded since the last call (then clears it). */
+b200_status b200_synchronize(b200_context * ctx);
+/* Text of the last error on this context ("" when none). */
+const char * b200_last_error(b200_context * ctx);
+/* Device memory helpers for callers without another allocator (ggml_backend_buffer alloc / free / memset). */
+b200_status b200_malloc(b200_context * ctx, size_t bytes, void ** dev_out);
+b200_status b200_free(b200_context * ctx, void * dev);
+b200_status b200_memcpy_h2d(b200_context * ctx, void * dev_dst, const void * host_src, size_t bytes);
+b200_status b200_memcpy_d2h(b200_context * ctx, void * host_dst, const void * dev_src, size_t bytes);
+
+/* ------------------------------------------------------------------------------------------------------------
+ * Weight tensors: the backend's weight buffer type. speech.cpp allocates weights in the backend's default buffer
+ * type (src/common/model-file.cpp:222-245) and uploads them with ggml_backend_tensor_set in 16 MiB pieces at any
+ * byte offset (src/common/model-file.cpp:247-268). b200_weight_set / _get accept the same GGUF bytes at the same
+ * offsets; on the device the blocks are stored field by field (a documented repacked layout), which is
+ * a byte permutation, so any piece boundary works and the device holds exactly the GGUF bytes plus alignment.
+ * ------------------------------------------------------------------------------------------------------------ */
+typedef struct b200_weight {
+    int32_t type;   /* B200_TYPE_* */
+    int32_t device;
+    int64_t ne0;    /* K: values per row */
+    int64_t ne1;    /* N: rows per matrix */
+    int64_t ne2;    /* E: matrices (experts); 1 for a plain matrix */
+    void * data;    /* device allocation holding the repacked fields */
+    size_t nbytes;  /* GGUF bytes (ggml_nbytes) */
+    size_t dbytes;  /* device bytes (GGUF bytes + field alignment) */
+    int64_t field_off[4]; /* byte offset of each field in data */
+} b200_weight;
+
+/* GGUF bytes of a [ne0, ne1, ne2] tensor of `type` (ggml_nbytes); 0 when rows are not whole blocks. */
+size_t b200_weight_nbytes(int type, int64_t ne0, int64_t ne1, int64_t ne2);
+b200_status b200_weight_alloc(b200_context * ctx, int type, int64_t ne0, int64_t ne1, int64_t ne2, b200_weight * out);
+b200_status b200_weight_free(b200_context * ctx, b200_weight * w);
+/* Writes GGUF bytes [offset, offset + size) of the tensor from host memory (ggml_backend_tensor_set). */
+b200_status b200_weight_set(b200_context * ctx, b200_weight * w, const void * host_src, size_t offset, size_t size);
+/* Same, with the source bytes already in device memory. */
+b200_status b200_weight_set_device(b200_context * ctx, b200_weight * w, const void * dev_src, size_t offset, size_t size);
+/* Reads GGUF bytes [offset, offset + size) back into host memory (ggml_backend_tensor_get). Synchronous. */
+b200_status b200_weight_get(b200_context * ctx, const b200_weight * w, void * host_dst, size_t offset, size_t size);
+
+/* ------------------------------------------------------------------------------------------------------------
+ * Ops. All pointers are device pointers. These are the nodes the ggml adapter forwards.
+ * ------------------------------------------------------------------------------------------------------------ */
+
+/* MUL_MAT (src/common/graph.h:15-19; ggml_mul_mat with GGML_PREC_F32): dst[m][n] = sum_k W[n][k] x[m][k] for
+ * x [M][K], dst [M][N], W of weight matrix 0 (ne2 == 1). */
+b200_status b200_mul_mat(b200_context * ctx, const b200_weight * w, const float * x, int64_t M, float * dst);
+
+/* MUL_MAT on rows [row0, row0 + n) of W only: dst [M][n] (a column shard of the output; multi-GPU column split). */
+b200_status b200_mul_mat_rows(b200_context * ctx, const b200_weight * w, int64_t row0, int64_t n, const float * x,
+                              int64_t M, float * dst, int64_t ld_dst);
+
+/* MUL_MAT_ID (src/common/graph.h:22-26, used at src/families/drama3/text-model.cpp:208-210):
+ *   experts: W [E][N][K]; b [T][nb1][K] with nb1 == 1 (one row per token shared by its chosen experts) or top_k;
+ *   ids [T][top_k] int32 expert numbers; dst [T][top_k][N].
+ * Routes by sorting (token, slot) pairs by expert on the device, then runs each expert's rows once over all of its
+ * pairs. An id outside [0, E) is skipped and reported by the next b200_synchronize() as B200_ERR_RANGE. */
+b200_status b200_mul_mat_id(b200_context * ctx, const b200_weight * experts, const float * b, int64_t nb1,
+                            const int32_t * ids, int64_t top_k, int64_t T, float * dst);
+
+/* GET_ROWS of a weight table (talker.cpp:131-133, decoder.cpp:319): dst [n][K] = dequantize(row ids[i]), bit for bit
+ * as ggml's CPU dequantizers. An id outside [0, N * E) is skipped (its row is left untouched) and reported by
+ * b200_synchronize() as B200_ERR_RANGE. */
+b200_status b200_get_rows(b200_context * ctx, const b200_weight * table, const int32_t * ids, int64_t n, float * dst);
+
+/* The CPU backend's activation quantization (src1 -> vec_dot type): M rows of K floats -> GGUF blocks of
+ * B200_TYPE_Q8_0 (34 B / 32) or B200_TYPE_Q8_K (292 B / 256), bit for bit. dst holds M * row bytes. */
+b200_status b200_quantize_rows(b200_context * ctx, int type, const float * x, int64_t K, int64_t M, void * dst);
+
+/* Test hook for the bit-exactness of integer partials: the int32 (sub-)block sums the product of W's rows with
+ * activation row x forms — Q8_0: one per 32-block; Q4_K: (sum_s sc_s I_s, sum_s m_s bsum_s) per super-block; Q6_K:
+ * sum_g sc_g I_g per super-block — written to sums [N][per_row]. */
+b200_status b200_block_sums(b200_context * ctx, const b200_weight * w, const float * x, int32_t * sums);
+
+/* ------------------------------------------------------------------------------------------------------------
+ * Host-buffer entry points (the end-to-end path a CPU caller takes: copies in, product, copy out, synchronous).
+ * ------------------------------------------------------------------------------------------------------------ */
+b200_status b200_mul_mat_host(b200_context * ctx, const b200_weight * w, const float * x_host, int64_t M, float * dst_host);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPEECH_B200_H */

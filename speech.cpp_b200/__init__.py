@@ -1,0 +1,295 @@
+"""speech.cpp_b200 — Python host side of the B200 backend for speech.cpp's quantized matrix products.
+
+A thin ctypes layer over the C ABI in include/b200.h (libb200.so, built from csrc/ for sm_100a). It mirrors the ggml
+ops speech.cpp builds its graphs from — ggml_mul_mat (src/common/graph.h:15-19), ggml_mul_mat_id (graph.h:22-26),
+ggml_get_rows of quantized tables (src/families/qwen3-tts/talker.cpp:131-133) — and the weight buffer's
+set_tensor / get_tensor (src/common/model-file.cpp:247-268), with the same argument meaning: a weight has ne0 = K
+values per row and ne1 = N rows; activations are float32 [M][K]; results [M][N].
+
+Device memory and streams come from torch (plumbing only): every op takes torch CUDA tensors and runs on the
+context's own stream. There is no CPU fallback: if libb200.so is missing or no B200 is present, calls raise.
+"""
+
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libb200.so")
+
+F32, F16, Q8_0, Q4_K, Q6_K, Q8_K, BF16 = 0, 1, 8, 12, 14, 15, 30
+TYPE_NAMES = {F32: "F32", F16: "F16", Q8_0: "Q8_0", Q4_K: "Q4_K", Q6_K: "Q6_K", Q8_K: "Q8_K", BF16: "BF16"}
+BLOCK = {F32: (1, 4), F16: (1, 2), BF16: (1, 2), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210), Q8_K: (256, 292)}
+
+OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_ALLOC, ERR_DEVICE, ERR_RANGE, ERR_TIMEOUT = 0, -1, -2, -3, -4, -5, -6
+STATUS_NAMES = {0: "OK", -1: "INVALID", -2: "UNSUPPORTED", -3: "ALLOC", -4: "DEVICE", -5: "RANGE", -6: "TIMEOUT"}
+
+# Every symbol include/b200.h declares (tests check the library exports each one).
+EXPORTS = [
+    "b200_device_count", "b200_device_info", "b200_context_create", "b200_context_destroy", "b200_context_stream",
+    "b200_synchronize", "b200_last_error", "b200_malloc", "b200_free", "b200_memcpy_h2d", "b200_memcpy_d2h",
+    "b200_weight_nbytes", "b200_weight_alloc", "b200_weight_free", "b200_weight_set", "b200_weight_set_device",
+    "b200_weight_get", "b200_mul_mat", "b200_mul_mat_rows", "b200_mul_mat_id", "b200_get_rows", "b200_quantize_rows",
+    "b200_block_sums", "b200_mul_mat_host",
+]
+
+
+class B200Error(RuntimeError):
+    def __init__(self, status, message):
+        super().__init__(f"b200 {STATUS_NAMES.get(status, status)}: {message}")
+        self.status = status
+
+
+class Weight(ctypes.Structure):
+    """struct b200_weight (include/b200.h)."""
+
+    _fields_ = [
+        ("type", ctypes.c_int32),
+        ("device", ctypes.c_int32),
+        ("ne0", ctypes.c_int64),
+        ("ne1", ctypes.c_int64),
+        ("ne2", ctypes.c_int64),
+        ("data", ctypes.c_void_p),
+        ("nbytes", ctypes.c_size_t),
+        ("dbytes", ctypes.c_size_t),
+        ("field_off", ctypes.c_int64 * 4),
+    ]
+
+
+_lib = None
+
+
+def build():
+    """Compiles libb200.so (nvcc, sm_100a)."""
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("_b200_build", os.path.join(HERE, "build.py"))
+    m = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(m)
+    return m.build()
+
+
+def lib():
+    """The loaded C ABI. Raises if libb200.so is missing: there is no other implementation."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(f"{LIB_PATH} is missing: run speech.cpp_b200/build.py (no CPU fallback exists)")
+    L = ctypes.CDLL(LIB_PATH)
+    vp, i64, i32, sz = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_size_t
+    W = ctypes.POINTER(Weight)
+    sig = {
+        "b200_device_count": (i32, []),
+        "b200_device_info": (i32, [i32, ctypes.c_char_p, sz, ctypes.POINTER(sz), ctypes.POINTER(sz)]),
+        "b200_context_create": (i32, [i32, ctypes.POINTER(vp)]),
+        "b200_context_destroy": (None, [vp]),
+        "b200_context_stream": (vp, [vp]),
+        "b200_synchronize": (i32, [vp]),
+        "b200_last_error": (ctypes.c_char_p, [vp]),
+        "b200_malloc": (i32, [vp, sz, ctypes.POINTER(vp)]),
+        "b200_free": (i32, [vp, vp]),
+        "b200_memcpy_h2d": (i32, [vp, vp, vp, sz]),
+        "b200_memcpy_d2h": (i32, [vp, vp, vp, sz]),
+        "b200_weight_nbytes": (sz, [i32, i64, i64, i64]),
+        "b200_weight_alloc": (i32, [vp, i32, i64, i64, i64, W]),
+        "b200_weight_free": (i32, [vp, W]),
+        "b200_weight_set": (i32, [vp, W, vp, sz, sz]),
+        "b200_weight_set_device": (i32, [vp, W, vp, sz, sz]),
+        "b200_weight_get": (i32, [vp, W, vp, sz, sz]),
+        "b200_mul_mat": (i32, [vp, W, vp, i64, vp]),
+        "b200_mul_mat_rows": (i32, [vp, W, i64, i64, vp, i64, vp, i64]),
+        "b200_mul_mat_id": (i32, [vp, W, vp, i64, vp, i64, i64, vp]),
+        "b200_get_rows": (i32, [vp, W, vp, i64, vp]),
+        "b200_quantize_rows": (i32, [vp, i32, vp, i64, i64, vp]),
+        "b200_block_sums": (i32, [vp, W, vp, vp]),
+        "b200_mul_mat_host": (i32, [vp, W, vp, i64, vp]),
+    }
+    for name, (res, args) in sig.items():
+        f = getattr(L, name)
+        f.restype = res
+        f.argtypes = args
+    _lib = L
+    return L
+
+
+def row_size(qtype, k):
+    bv, bb = BLOCK[qtype]
+    if k % bv:
+        raise ValueError(f"{TYPE_NAMES[qtype]} rows need a multiple of {bv} values")
+    return k // bv * bb
+
+
+def _ptr(t):
+    if t is None:
+        return None
+    if hasattr(t, "data_ptr"):
+        if not t.is_cuda:
+            raise ValueError("expected a CUDA tensor")
+        if not t.is_contiguous():
+            raise ValueError("expected a contiguous tensor")
+        return ctypes.c_void_p(t.data_ptr())
+    return ctypes.c_void_p(t)
+
+
+class Context:
+    """One B200 device, one stream, a scratch pool (b200_context)."""
+
+    def __init__(self, device=0):
+        self.L = lib()
+        self.device = device
+        h = ctypes.c_void_p()
+        s = self.L.b200_context_create(device, ctypes.byref(h))
+        if s != OK:
+            raise B200Error(s, self.L.b200_last_error(None).decode())
+        self.h = h
+
+    def check(self, status):
+        if status != OK:
+            raise B200Error(status, self.L.b200_last_error(self.h).decode())
+
+    @property
+    def stream_handle(self):
+        return self.L.b200_context_stream(self.h)
+
+    def torch_stream(self):
+        import torch
+
+        return torch.cuda.ExternalStream(self.stream_handle, device=torch.device("cuda", self.device))
+
+    def synchronize(self):
+        self.check(self.L.b200_synchronize(self.h))
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.L.b200_context_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # -- weights --------------------------------------------------------------------------------------------------
+    def weight(self, qtype, ne0, ne1, ne2=1, data=None):
+        """Allocates a weight tensor; `data` (GGUF block bytes: numpy uint8, or a CUDA uint8 tensor) is uploaded."""
+        w = Weight()
+        self.check(self.L.b200_weight_alloc(self.h, qtype, ne0, ne1, ne2, ctypes.byref(w)))
+        if data is not None:
+            self.set_weight(w, data)
+        return w
+
+    def set_weight(self, w, data, offset=0):
+        if hasattr(data, "is_cuda") and data.is_cuda:
+            self.check(self.L.b200_weight_set_device(self.h, ctypes.byref(w), _ptr(data), offset, data.numel() * data.element_size()))
+        else:
+            import numpy as np
+
+            a = np.ascontiguousarray(data).view(np.uint8).reshape(-1)
+            self.check(self.L.b200_weight_set(self.h, ctypes.byref(w), a.ctypes.data_as(ctypes.c_void_p), offset, a.size))
+
+    def get_weight(self, w, offset=0, size=None):
+        import numpy as np
+
+        size = w.nbytes - offset if size is None else size
+        out = np.empty(size, dtype=np.uint8)
+        self.check(self.L.b200_weight_get(self.h, ctypes.byref(w), out.ctypes.data_as(ctypes.c_void_p), offset, size))
+        return out
+
+    def free_weight(self, w):
+        self.check(self.L.b200_weight_free(self.h, ctypes.byref(w)))
+
+    # -- ops (torch CUDA tensors; run on the context's stream) ----------------------------------------------------
+    def _sync_in(self):
+        """Orders the context's stream after torch's current stream (inputs written by torch)."""
+        import torch
+
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.device))
+        self.torch_stream().wait_event(ev)
+
+    def _sync_out(self):
+        import torch
+
+        ev = torch.cuda.Event()
+        ev.record(self.torch_stream())
+        torch.cuda.current_stream(self.device).wait_event(ev)
+
+    def mul_mat(self, w, x, out=None):
+        """ggml_mul_mat(w, x): x float32 [M, K] -> [M, N]."""
+        import torch
+
+        x = x.reshape(-1, w.ne0)
+        M = x.shape[0]
+        out = torch.empty((M, w.ne1), dtype=torch.float32, device=x.device) if out is None else out
+        self._sync_in()
+        self.check(self.L.b200_mul_mat(self.h, ctypes.byref(w), _ptr(x), M, _ptr(out)))
+        self._sync_out()
+        return out
+
+    def mul_mat_rows(self, w, row0, n, x, out=None):
+        import torch
+
+        x = x.reshape(-1, w.ne0)
+        M = x.shape[0]
+        out = torch.empty((M, n), dtype=torch.float32, device=x.device) if out is None else out
+        self._sync_in()
+        self.check(self.L.b200_mul_mat_rows(self.h, ctypes.byref(w), row0, n, _ptr(x), M, _ptr(out), out.stride(0)))
+        self._sync_out()
+        return out
+
+    def mul_mat_id(self, experts, b, ids, out=None):
+        """ggml_mul_mat_id(experts, b, ids): b float32 [T, nb1, K] (nb1 = 1 or top_k), ids int32 [T, top_k]."""
+        import torch
+
+        T, top_k = ids.shape
+        nb1 = b.shape[1]
+        out = torch.empty((T, top_k, experts.ne1), dtype=torch.float32, device=b.device) if out is None else out
+        self._sync_in()
+        self.check(self.L.b200_mul_mat_id(self.h, ctypes.byref(experts), _ptr(b), nb1, _ptr(ids), top_k, T, _ptr(out)))
+        self._sync_out()
+        return out
+
+    def get_rows(self, table, ids, out=None):
+        import torch
+
+        out = torch.empty((ids.numel(), table.ne0), dtype=torch.float32, device=ids.device) if out is None else out
+        self._sync_in()
+        self.check(self.L.b200_get_rows(self.h, ctypes.byref(table), _ptr(ids), ids.numel(), _ptr(out)))
+        self._sync_out()
+        return out
+
+    def quantize_rows(self, qtype, x):
+        """The CPU backend's activation quantization: float32 [M, K] -> uint8 [M, row bytes] (Q8_0 or Q8_K)."""
+        import torch
+
+        M, K = x.shape
+        out = torch.empty((M, row_size(qtype, K)), dtype=torch.uint8, device=x.device)
+        self._sync_in()
+        self.check(self.L.b200_quantize_rows(self.h, qtype, _ptr(x), K, M, _ptr(out)))
+        self._sync_out()
+        return out
+
+    def block_sums(self, w, x):
+        import torch
+
+        per_row = {Q8_0: w.ne0 // 32, Q4_K: 2 * (w.ne0 // 256), Q6_K: w.ne0 // 256}[w.type]
+        out = torch.empty((w.ne1 * w.ne2, per_row), dtype=torch.int32, device=x.device)
+        self._sync_in()
+        self.check(self.L.b200_block_sums(self.h, ctypes.byref(w), _ptr(x), _ptr(out)))
+        self._sync_out()
+        return out
+
+    def mul_mat_host(self, w, x):
+        """End-to-end host path: numpy float32 [M, K] -> numpy [M, N] (copies inside the call)."""
+        import numpy as np
+
+        x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, w.ne0)
+        out = np.empty((x.shape[0], w.ne1), dtype=np.float32)
+        self.check(self.L.b200_mul_mat_host(self.h, ctypes.byref(w), x.ctypes.data_as(ctypes.c_void_p), x.shape[0],
+                                            out.ctypes.data_as(ctypes.c_void_p)))
+        return out
+
+
+def device_count():
+    return lib().b200_device_count()

@@ -1,0 +1,484 @@
+// api.cu — the C ABI (include/b200.h): devices, contexts, weight buffers, and op dispatch.
+#include <cstdio>
+#include <cstring>
+
+#include "internal.h"
+
+using namespace b200;
+
+namespace {
+
+thread_local std::string g_error;  // errors before a context exists
+
+b200_status fail(b200_context * ctx, b200_status s, const char * what) {
+    if (ctx) ctx->last_error = what;
+    else g_error = what;
+    return s;
+}
+
+b200_status cuda_fail(b200_context * ctx, cudaError_t e, const char * where) {
+    char buf[256];
+    std::snprintf(buf, sizeof buf, "%s: %s", where, cudaGetErrorString(e));
+    return fail(ctx, e == cudaErrorMemoryAllocation ? B200_ERR_ALLOC : B200_ERR_DEVICE, buf);
+}
+
+#define CK(ctx, call)                                           \
+    do {                                                        \
+        cudaError_t e_ = (call);                                \
+        if (e_ != cudaSuccess) return cuda_fail(ctx, e_, #call); \
+    } while (0)
+
+bool known_weight_type(int t) {
+    return t == B200_TYPE_Q8_0 || t == B200_TYPE_Q4_K || t == B200_TYPE_Q6_K || t == B200_TYPE_BF16 || t == B200_TYPE_F32;
+}
+
+int64_t block_values(int t) {
+    switch (t) {
+    case B200_TYPE_Q8_0: return 32;
+    case B200_TYPE_Q4_K:
+    case B200_TYPE_Q6_K:
+    case B200_TYPE_Q8_K: return 256;
+    default: return 1;
+    }
+}
+
+int64_t block_bytes(int t) {
+    switch (t) {
+    case B200_TYPE_Q8_0: return 34;
+    case B200_TYPE_Q4_K: return 144;
+    case B200_TYPE_Q6_K: return 210;
+    case B200_TYPE_Q8_K: return 292;
+    case B200_TYPE_BF16:
+    case B200_TYPE_F16: return 2;
+    case B200_TYPE_F32: return 4;
+    default: return 0;
+    }
+}
+
+// Grows the context's scratch to at least `bytes` (synchronizes the stream when it has to reallocate).
+b200_status ensure_scratch(b200_context * ctx, size_t bytes) {
+    if (ctx->scratch_bytes >= bytes) return B200_OK;
+    CK(ctx, cudaStreamSynchronize(ctx->stream));
+    if (ctx->scratch) cudaFree(ctx->scratch);
+    ctx->scratch = nullptr;
+    ctx->scratch_bytes = 0;
+    size_t want = bytes < ((size_t) 1 << 20) ? ((size_t) 1 << 20) : bytes;
+    CK(ctx, cudaMalloc(&ctx->scratch, want));
+    ctx->scratch_bytes = want;
+    return B200_OK;
+}
+
+b200_status ensure_staging(b200_context * ctx, size_t bytes) {
+    if (ctx->staging_bytes >= bytes) return B200_OK;
+    CK(ctx, cudaStreamSynchronize(ctx->stream));
+    if (ctx->staging) cudaFree(ctx->staging);
+    ctx->staging = nullptr;
+    ctx->staging_bytes = 0;
+    CK(ctx, cudaMalloc(&ctx->staging, bytes));
+    ctx->staging_bytes = bytes;
+    return B200_OK;
+}
+
+// Sub-allocation from scratch, 256-byte aligned.
+struct Carve {
+    uint8_t * base;
+    size_t used = 0;
+    template <class T>
+    T * take(size_t count) {
+        T * p = reinterpret_cast<T *>(base + used);
+        used += (count * sizeof(T) + 255) & ~(size_t) 255;
+        return p;
+    }
+};
+
+size_t quantized_act_bytes(int kind, int64_t K, int64_t rows) {
+    size_t b = (((size_t) rows * K + 255) & ~(size_t) 255);
+    if (kind == B200_TYPE_Q8_0) b += (((size_t) rows * (K / 32) * 4 + 255) & ~(size_t) 255);
+    else b += (((size_t) rows * (K / 256) * 4 + 255) & ~(size_t) 255) + (((size_t) rows * (K / 16) * 2 + 255) & ~(size_t) 255);
+    return b;
+}
+
+bool check_weight(b200_context * ctx, const b200_weight * w) {
+    return ctx && w && w->data && known_weight_type(w->type) && w->ne0 > 0 && w->ne1 > 0 && w->ne2 > 0 &&
+           w->ne0 % block_values(w->type) == 0;
+}
+
+GemvParams base_params(const b200_weight * w) {
+    GemvParams p;
+    std::memset(&p, 0, sizeof p);
+    p.w = view_of(w);
+    p.eps = 0.0f;
+    return p;
+}
+
+int pow2_at_least(int64_t m) {
+    int nc = 1;
+    while (nc < m) nc <<= 1;
+    return nc;
+}
+
+// The product of rows [row0, row0 + n) of matrix 0 with M activation rows, through the GEMV kernels.
+b200_status mul_mat_impl(b200_context * ctx, const b200_weight * w, int64_t row0, int64_t n, const float * x, int64_t M,
+                         float * dst, int64_t ld_dst) {
+    if (!check_weight(ctx, w)) return fail(ctx, B200_ERR_INVALID, "mul_mat: bad weight");
+    if (w->type == B200_TYPE_F32) return fail(ctx, B200_ERR_UNSUPPORTED, "mul_mat: F32 weights are not on this path");
+    if (M < 0 || row0 < 0 || n < 0 || row0 + n > w->ne1 * w->ne2 || (M > 0 && (!x || !dst)))
+        return fail(ctx, B200_ERR_INVALID, "mul_mat: bad shape");
+    if (M == 0 || n == 0) return B200_OK;
+    const int64_t K = w->ne0;
+    GemvParams p = base_params(w);
+    p.N = n;
+    p.row0 = row0;
+    p.x = x;
+    p.ldx = K;
+    p.y = dst;
+    p.ldy = ld_dst;
+    const int maxnc = gemv_max_columns(w->type, K);
+    if (maxnc == 0) return fail(ctx, B200_ERR_UNSUPPORTED, "mul_mat: rows too long for the staging buffer");
+    if (M <= maxnc) {
+        p.ncols = (int) M;
+        CK(ctx, launch_gemv(p, pow2_at_least(M), 1, ctx->stream, false, ctx->num_sms));
+        return B200_OK;
+    }
+    // Many columns: quantize them once, then stream the weights once per chunk of `maxnc` columns.
+    const int kind = act_kind(w->type);
+    if (kind == B200_TYPE_BF16) {
+        p.ncols = (int) M;
+        CK(ctx, launch_gemv(p, maxnc, 1, ctx->stream, false, ctx->num_sms));
+        return B200_OK;
+    }
+    b200_status s = ensure_scratch(ctx, quantized_act_bytes(kind, K, M));
+    if (s != B200_OK) return s;
+    Carve c{(uint8_t *) ctx->scratch};
+    int8_t * q = c.take<int8_t>((size_t) M * K);
+    float * d = c.take<float>((size_t) M * (K / (kind == B200_TYPE_Q8_0 ? 32 : 256)));
+    int16_t * bs = kind == B200_TYPE_Q8_K ? c.take<int16_t>((size_t) M * (K / 16)) : nullptr;
+    CK(ctx, launch_quantize(kind, x, K, M, nullptr, q, d, bs, ctx->stream));
+    p.aq = q;
+    p.ad = d;
+    p.abs = bs;
+    p.ncols = (int) M;
+    CK(ctx, launch_gemv(p, maxnc, 1, ctx->stream, false, ctx->num_sms));
+    return B200_OK;
+}
+
+}  // namespace
+
+namespace b200 {
+
+WeightView view_of(const b200_weight * w) {
+    WeightView v;
+    v.type = w->type;
+    v.K = w->ne0;
+    v.rows = w->ne1 * w->ne2;
+    const uint8_t * base = (const uint8_t *) w->data;
+    v.f0 = base + w->field_off[0];
+    v.f1 = base + w->field_off[1];
+    v.f2 = base + w->field_off[2];
+    v.f3 = base + w->field_off[3];
+    return v;
+}
+
+}  // namespace b200
+
+extern "C" {
+
+int b200_device_count(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) return 0;
+    return n;
+}
+
+b200_status b200_device_info(int device, char * name, size_t name_len, size_t * free_bytes, size_t * total_bytes) {
+    int n = b200_device_count();
+    if (device < 0 || device >= n) return fail(nullptr, B200_ERR_INVALID, "device_info: no such device");
+    if (name && name_len) std::snprintf(name, name_len, "B200_%d", device);
+    if (free_bytes || total_bytes) {
+        int prev = 0;
+        cudaGetDevice(&prev);
+        if (cudaSetDevice(device) != cudaSuccess) return fail(nullptr, B200_ERR_DEVICE, "device_info: cudaSetDevice");
+        size_t f = 0, t = 0;
+        cudaError_t e = cudaMemGetInfo(&f, &t);
+        cudaSetDevice(prev);
+        if (e != cudaSuccess) return fail(nullptr, B200_ERR_DEVICE, "device_info: cudaMemGetInfo");
+        if (free_bytes) *free_bytes = f;
+        if (total_bytes) *total_bytes = t;
+    }
+    return B200_OK;
+}
+
+b200_status b200_context_create(int device, b200_context ** out) {
+    if (!out) return fail(nullptr, B200_ERR_INVALID, "context_create: out is NULL");
+    *out = nullptr;
+    if (device < 0 || device >= b200_device_count()) return fail(nullptr, B200_ERR_INVALID, "context_create: no such device");
+    if (cudaSetDevice(device) != cudaSuccess) return fail(nullptr, B200_ERR_DEVICE, "context_create: cudaSetDevice");
+    b200_context * ctx = new b200_context();
+    ctx->device = device;
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, device) != cudaSuccess || prop.major < 10) {
+        delete ctx;
+        return fail(nullptr, B200_ERR_UNSUPPORTED, "context_create: the device is not sm_100 (B200)");
+    }
+    ctx->num_sms = prop.multiProcessorCount;
+    if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaMalloc(&ctx->dev_err, sizeof(unsigned)) != cudaSuccess || cudaMallocHost(&ctx->host_err, sizeof(unsigned)) != cudaSuccess ||
+        cudaMemsetAsync(ctx->dev_err, 0, sizeof(unsigned), ctx->stream) != cudaSuccess) {
+        b200_context_destroy(ctx);
+        return fail(nullptr, B200_ERR_DEVICE, "context_create: stream / memory setup failed");
+    }
+    *out = ctx;
+    return B200_OK;
+}
+
+void b200_context_destroy(b200_context * ctx) {
+    if (!ctx) return;
+    cudaSetDevice(ctx->device);
+    if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    if (ctx->scratch) cudaFree(ctx->scratch);
+    if (ctx->staging) cudaFree(ctx->staging);
+    if (ctx->dev_err) cudaFree(ctx->dev_err);
+    if (ctx->host_err) cudaFreeHost(ctx->host_err);
+    if (ctx->stream) cudaStreamDestroy(ctx->stream);
+    delete ctx;
+}
+
+void * b200_context_stream(b200_context * ctx) { return ctx ? (void *) ctx->stream : nullptr; }
+
+b200_status b200_synchronize(b200_context * ctx) {
+    if (!ctx) return fail(nullptr, B200_ERR_INVALID, "synchronize: NULL context");
+    CK(ctx, cudaMemcpyAsync(ctx->host_err, ctx->dev_err, sizeof(unsigned), cudaMemcpyDeviceToHost, ctx->stream));
+    CK(ctx, cudaStreamSynchronize(ctx->stream));
+    const unsigned bits = *ctx->host_err;
+    if (bits) {
+        CK(ctx, cudaMemsetAsync(ctx->dev_err, 0, sizeof(unsigned), ctx->stream));
+        CK(ctx, cudaStreamSynchronize(ctx->stream));
+        if (bits & B200_DEVERR_TIMEOUT) return fail(ctx, B200_ERR_TIMEOUT, "a bounded device wait gave up");
+        if (bits & B200_DEVERR_EXPERT) return fail(ctx, B200_ERR_RANGE, "mul_mat_id: an expert id is outside [0, E)");
+        return fail(ctx, B200_ERR_RANGE, "get_rows: a row id is outside the table");
+    }
+    return B200_OK;
+}
+
+const char * b200_last_error(b200_context * ctx) { return ctx ? ctx->last_error.c_str() : g_error.c_str(); }
+
+b200_status b200_malloc(b200_context * ctx, size_t bytes, void ** dev_out) {
+    if (!ctx || !dev_out) return fail(ctx, B200_ERR_INVALID, "malloc: NULL argument");
+    CK(ctx, cudaSetDevice(ctx->device));
+    CK(ctx, cudaMalloc(dev_out, bytes ? bytes : 1));
+    return B200_OK;
+}
+
+b200_status b200_free(b200_context * ctx, void * dev) {
+    if (!ctx) return fail(ctx, B200_ERR_INVALID, "free: NULL context");
+    if (dev) CK(ctx, cudaFree(dev));
+    return B200_OK;
+}
+
+b200_status b200_memcpy_h2d(b200_context * ctx, void * dev_dst, const void * host_src, size_t bytes) {
+    if (!ctx || (bytes && (!dev_dst || !host_src))) return fail(ctx, B200_ERR_INVALID, "memcpy_h2d: NULL argument");
+    CK(ctx, cudaMemcpyAsync(dev_dst, host_src, bytes, cudaMemcpyHostToDevice, ctx->stream));
+    return B200_OK;
+}
+
+b200_status b200_memcpy_d2h(b200_context * ctx, void * host_dst, const void * dev_src, size_t bytes) {
+    if (!ctx || (bytes && (!dev_src || !host_dst))) return fail(ctx, B200_ERR_INVALID, "memcpy_d2h: NULL argument");
+    CK(ctx, cudaMemcpyAsync(host_dst, dev_src, bytes, cudaMemcpyDeviceToHost, ctx->stream));
+    CK(ctx, cudaStreamSynchronize(ctx->stream));
+    return B200_OK;
+}
+
+size_t b200_weight_nbytes(int type, int64_t ne0, int64_t ne1, int64_t ne2) {
+    const int64_t bv = block_values(type), bb = block_bytes(type);
+    if (!bb || ne0 <= 0 || ne1 < 0 || ne2 < 0 || ne0 % bv) return 0;
+    return (size_t) (ne0 / bv) * (size_t) bb * (size_t) ne1 * (size_t) ne2;
+}
+
+b200_status b200_weight_alloc(b200_context * ctx, int type, int64_t ne0, int64_t ne1, int64_t ne2, b200_weight * out) {
+    if (!ctx || !out) return fail(ctx, B200_ERR_INVALID, "weight_alloc: NULL argument");
+    std::memset(out, 0, sizeof *out);
+    if (!known_weight_type(type)) return fail(ctx, B200_ERR_UNSUPPORTED, "weight_alloc: unsupported type");
+    const size_t nbytes = b200_weight_nbytes(type, ne0, ne1, ne2);
+    if (!nbytes || ne1 <= 0 || ne2 <= 0) return fail(ctx, B200_ERR_INVALID, "weight_alloc: rows are not whole blocks");
+    int64_t sz[4] = {0, 0, 0, 0};
+    const int nf = field_sizes(type, ne0, ne1 * ne2, sz);
+    int64_t off = 0;
+    for (int i = 0; i < 4; i++) {
+        out->field_off[i] = off;
+        if (i < nf) off += align256(sz[i]);
+    }
+    CK(ctx, cudaSetDevice(ctx->device));
+    void * p = nullptr;
+    CK(ctx, cudaMalloc(&p, (size_t) off));
+    out->type = type;
+    out->device = ctx->device;
+    out->ne0 = ne0;
+    out->ne1 = ne1;
+    out->ne2 = ne2;
+    out->data = p;
+    out->nbytes = nbytes;
+    out->dbytes = (size_t) off;
+    return B200_OK;
+}
+
+b200_status b200_weight_free(b200_context * ctx, b200_weight * w) {
+    if (!ctx || !w) return fail(ctx, B200_ERR_INVALID, "weight_free: NULL argument");
+    if (w->data) CK(ctx, cudaFree(w->data));
+    w->data = nullptr;
+    return B200_OK;
+}
+
+static const size_t kStagingPiece = (size_t) 64 << 20;
+
+b200_status b200_weight_set(b200_context * ctx, b200_weight * w, const void * host_src, size_t offset, size_t size) {
+    if (!ctx || !w || !w->data || (size && !host_src)) return fail(ctx, B200_ERR_INVALID, "weight_set: NULL argument");
+    if (offset > w->nbytes || size > w->nbytes - offset) return fail(ctx, B200_ERR_INVALID, "weight_set: range outside the tensor");
+    if (w->type == B200_TYPE_BF16 || w->type == B200_TYPE_F32) {
+        CK(ctx, cudaMemcpyAsync((uint8_t *) w->data + offset, host_src, size, cudaMemcpyHostToDevice, ctx->stream));
+        return B200_OK;
+    }
+    const size_t piece = size < kStagingPiece ? size : kStagingPiece;
+    b200_status s = ensure_staging(ctx, piece ? piece : 1);
+    if (s != B200_OK) return s;
+    for (size_t done = 0; done < size;) {
+        const size_t n = size - done < kStagingPiece ? size - done : kStagingPiece;
+        CK(ctx, cudaMemcpyAsync(ctx->staging, (const uint8_t *) host_src + done, n, cudaMemcpyHostToDevice, ctx->stream));
+        CK(ctx, launch_repack(w->type, w, (const uint8_t *) ctx->staging, (int64_t) (offset + done), (int64_t) n, true, nullptr, ctx->stream));
+        done += n;
+    }
+    return B200_OK;
+}
+
+b200_status b200_weight_set_device(b200_context * ctx, b200_weight * w, const void * dev_src, size_t offset, size_t size) {
+    if (!ctx || !w || !w->data || (size && !dev_src)) return fail(ctx, B200_ERR_INVALID, "weight_set_device: NULL argument");
+    if (offset > w->nbytes || size > w->nbytes - offset) return fail(ctx, B200_ERR_INVALID, "weight_set_device: range outside the tensor");
+    if (w->type == B200_TYPE_BF16 || w->type == B200_TYPE_F32) {
+        CK(ctx, cudaMemcpyAsync((uint8_t *) w->data + offset, dev_src, size, cudaMemcpyDeviceToDevice, ctx->stream));
+        return B200_OK;
+    }
+    CK(ctx, launch_repack(w->type, w, (const uint8_t *) dev_src, (int64_t) offset, (int64_t) size, true, nullptr, ctx->stream));
+    return B200_OK;
+}
+
+b200_status b200_weight_get(b200_context * ctx, const b200_weight * w, void * host_dst, size_t offset, size_t size) {
+    if (!ctx || !w || !w->data || (size && !host_dst)) return fail(ctx, B200_ERR_INVALID, "weight_get: NULL argument");
+    if (offset > w->nbytes || size > w->nbytes - offset) return fail(ctx, B200_ERR_INVALID, "weight_get: range outside the tensor");
+    if (w->type == B200_TYPE_BF16 || w->type == B200_TYPE_F32) {
+        CK(ctx, cudaMemcpyAsync(host_dst, (const uint8_t *) w->data + offset, size, cudaMemcpyDeviceToHost, ctx->stream));
+        CK(ctx, cudaStreamSynchronize(ctx->stream));
+        return B200_OK;
+    }
+    const size_t piece = size < kStagingPiece ? size : kStagingPiece;
+    b200_status s = ensure_staging(ctx, piece ? piece : 1);
+    if (s != B200_OK) return s;
+    for (size_t done = 0; done < size;) {
+        const size_t n = size - done < kStagingPiece ? size - done : kStagingPiece;
+        CK(ctx, launch_repack(w->type, w, nullptr, (int64_t) (offset + done), (int64_t) n, false, (uint8_t *) ctx->staging, ctx->stream));
+        CK(ctx, cudaMemcpyAsync((uint8_t *) host_dst + done, ctx->staging, n, cudaMemcpyDeviceToHost, ctx->stream));
+        CK(ctx, cudaStreamSynchronize(ctx->stream));
+        done += n;
+    }
+    return B200_OK;
+}
+
+b200_status b200_mul_mat(b200_context * ctx, const b200_weight * w, const float * x, int64_t M, float * dst) {
+    if (!check_weight(ctx, w)) return fail(ctx, B200_ERR_INVALID, "mul_mat: bad weight");
+    if (w->ne2 != 1) return fail(ctx, B200_ERR_INVALID, "mul_mat: a stack of matrices needs mul_mat_id");
+    return mul_mat_impl(ctx, w, 0, w->ne1, x, M, dst, w->ne1);
+}
+
+b200_status b200_mul_mat_rows(b200_context * ctx, const b200_weight * w, int64_t row0, int64_t n, const float * x, int64_t M,
+                              float * dst, int64_t ld_dst) {
+    if (ld_dst < n) return fail(ctx, B200_ERR_INVALID, "mul_mat_rows: ld_dst < n");
+    return mul_mat_impl(ctx, w, row0, n, x, M, dst, ld_dst);
+}
+
+b200_status b200_mul_mat_id(b200_context * ctx, const b200_weight * experts, const float * b, int64_t nb1, const int32_t * ids,
+                            int64_t top_k, int64_t T, float * dst) {
+    if (!check_weight(ctx, experts)) return fail(ctx, B200_ERR_INVALID, "mul_mat_id: bad experts");
+    if (experts->type == B200_TYPE_F32) return fail(ctx, B200_ERR_UNSUPPORTED, "mul_mat_id: F32 experts are not on this path");
+    if (top_k <= 0 || T < 0 || (nb1 != 1 && nb1 != top_k)) return fail(ctx, B200_ERR_INVALID, "mul_mat_id: bad shape");
+    if (T == 0) return B200_OK;
+    if (!b || !ids || !dst) return fail(ctx, B200_ERR_INVALID, "mul_mat_id: NULL argument");
+    const int64_t K = experts->ne0, N = experts->ne1, E = experts->ne2, P = T * top_k;
+    const int kind = act_kind(experts->type);
+    const int nc = gemv_max_columns(experts->type, K);
+    if (nc == 0) return fail(ctx, B200_ERR_UNSUPPORTED, "mul_mat_id: rows too long for the staging buffer");
+    size_t need = (((size_t) (E + 1) * 4 + 255) & ~(size_t) 255) + 2 * (((size_t) P * 4 + 255) & ~(size_t) 255);
+    if (kind != B200_TYPE_BF16) need += quantized_act_bytes(kind, K, T * nb1);
+    b200_status s = ensure_scratch(ctx, need);
+    if (s != B200_OK) return s;
+    Carve c{(uint8_t *) ctx->scratch};
+    int32_t * grp_off = c.take<int32_t>((size_t) E + 1);
+    int32_t * col_src = c.take<int32_t>((size_t) P);
+    int32_t * col_dst = c.take<int32_t>((size_t) P);
+    GemvParams p = base_params(experts);
+    if (kind != B200_TYPE_BF16) {
+        int8_t * q = c.take<int8_t>((size_t) T * nb1 * K);
+        float * d = c.take<float>((size_t) T * nb1 * (K / (kind == B200_TYPE_Q8_0 ? 32 : 256)));
+        int16_t * bs = kind == B200_TYPE_Q8_K ? c.take<int16_t>((size_t) T * nb1 * (K / 16)) : nullptr;
+        CK(ctx, launch_quantize(kind, b, K, T * nb1, nullptr, q, d, bs, ctx->stream));
+        p.aq = q;
+        p.ad = d;
+        p.abs = bs;
+    }
+    CK(ctx, launch_route(ids, T, top_k, nb1, E, grp_off, col_src, col_dst, ctx->dev_err, ctx->stream));
+    p.N = N;
+    p.row0 = 0;
+    p.x = b;
+    p.ldx = K;
+    p.y = dst;
+    p.ldy = N;
+    p.col_src = col_src;
+    p.col_dst = col_dst;
+    p.grp_off = grp_off;
+    p.grp_rows = N;
+    CK(ctx, launch_gemv(p, nc, (int) E, ctx->stream, false, ctx->num_sms));
+    return B200_OK;
+}
+
+b200_status b200_get_rows(b200_context * ctx, const b200_weight * table, const int32_t * ids, int64_t n, float * dst) {
+    if (!check_weight(ctx, table)) return fail(ctx, B200_ERR_INVALID, "get_rows: bad table");
+    if (n < 0 || (n > 0 && (!ids || !dst))) return fail(ctx, B200_ERR_INVALID, "get_rows: bad arguments");
+    CK(ctx, launch_get_rows(view_of(table), ids, n, dst, ctx->dev_err, ctx->stream));
+    return B200_OK;
+}
+
+b200_status b200_quantize_rows(b200_context * ctx, int type, const float * x, int64_t K, int64_t M, void * dst) {
+    if (!ctx || (M > 0 && (!x || !dst)) || M < 0) return fail(ctx, B200_ERR_INVALID, "quantize_rows: bad arguments");
+    if (type != B200_TYPE_Q8_0 && type != B200_TYPE_Q8_K) return fail(ctx, B200_ERR_UNSUPPORTED, "quantize_rows: type must be Q8_0 or Q8_K");
+    if (K <= 0 || K % block_values(type)) return fail(ctx, B200_ERR_INVALID, "quantize_rows: K is not whole blocks");
+    CK(ctx, launch_quantize(type, x, K, M, (uint8_t *) dst, nullptr, nullptr, nullptr, ctx->stream));
+    return B200_OK;
+}
+
+b200_status b200_block_sums(b200_context * ctx, const b200_weight * w, const float * x, int32_t * sums) {
+    if (!check_weight(ctx, w) || !x || !sums) return fail(ctx, B200_ERR_INVALID, "block_sums: bad arguments");
+    if (w->type != B200_TYPE_Q8_0 && w->type != B200_TYPE_Q4_K && w->type != B200_TYPE_Q6_K)
+        return fail(ctx, B200_ERR_UNSUPPORTED, "block_sums: integer types only");
+    GemvParams p = base_params(w);
+    p.N = w->ne1 * w->ne2;
+    p.x = x;
+    p.ldx = w->ne0;
+    p.sums = sums;
+    p.ncols = 1;
+    CK(ctx, launch_gemv(p, 1, 1, ctx->stream, false, ctx->num_sms));
+    return B200_OK;
+}
+
+b200_status b200_mul_mat_host(b200_context * ctx, const b200_weight * w, const float * x_host, int64_t M, float * dst_host) {
+    if (!check_weight(ctx, w) || (M > 0 && (!x_host || !dst_host))) return fail(ctx, B200_ERR_INVALID, "mul_mat_host: bad arguments");
+    if (M == 0) return B200_OK;
+    const size_t xb = (size_t) M * w->ne0 * 4, yb = (size_t) M * w->ne1 * 4;
+    const size_t need = ((xb + 255) & ~(size_t) 255) + ((yb + 255) & ~(size_t) 255);
+    b200_status s = ensure_staging(ctx, need);
+    if (s != B200_OK) return s;
+    float * dx = (float *) ctx->staging;
+    float * dy = (float *) ((uint8_t *) ctx->staging + ((xb + 255) & ~(size_t) 255));
+    CK(ctx, cudaMemcpyAsync(dx, x_host, xb, cudaMemcpyHostToDevice, ctx->stream));
+    s = b200_mul_mat(ctx, w, dx, M, dy);
+    if (s != B200_OK) return s;
+    CK(ctx, cudaMemcpyAsync(dst_host, dy, yb, cudaMemcpyDeviceToHost, ctx->stream));
+    return b200_synchronize(ctx);
+}
+
+}  // extern "C"

@@ -1,0 +1,511 @@
+// gemv.cuh — batch-1..8 dequant-fused matrix-vector products (ggml MUL_MAT with few src1 columns).
+//
+// Replaces the decode-step products of speech.cpp (src/common/qwen3-decoder.cpp:362-364, 403, 406-407, 410, 426, and
+// the kept step graph :462-490) that ggml runs as mul_mat nodes (src/common/graph.h:15-19).
+//
+// Per launch: every CTA first stages the NC activation columns in shared memory, already quantized to the weight
+// type's vec_dot type exactly as the CPU oracle does (q8_0 for Q8_0, q8_K for Q4_K/Q6_K, bf16 for BF16), optionally
+// after a fused prologue (RMSNorm x weight, SwiGLU, or the grouped-query broadcast of a one-position attention).
+// Warps then stream weight rows with 128-bit non-allocating loads (double-buffered, so the next unit's bytes are in
+// flight while the current one is reduced), form the exact int32 (sub-)block sums with dp4a, scale them in float32,
+// and warp-reduce each output. No tensor cores: one weight byte meets NC <= 8 activations, far below the ridge.
+//
+// With PDL, each CTA issues its first weight loads before griddepcontrol.wait, so a chain of products (a decode
+// step) overlaps the next product's weight stream with the tail of the previous one.
+#pragma once
+
+#include "common.cuh"
+
+namespace b200 {
+
+enum Prologue : int {
+    PRO_COPY = 0,     // x as given
+    PRO_RMSNORM = 1,  // (x * 1/sqrt(mean(x^2) + eps)) * norm_w      (ggml_rms_norm then ggml_mul)
+    PRO_SWIGLU = 2,   // silu(x[k]) * x[pro_k + k]                     (ggml_swiglu_split of gate | up)
+    PRO_GQA = 3,      // x[(k / (pro_k * pro_rep)) * pro_k + k % pro_k] (attention over one position: o = v per head)
+};
+
+struct GemvParams {
+    WeightView w;
+    int64_t N;       // output rows of this launch
+    int64_t row0;    // first weight row (expert offset / column shard)
+    const float * x;
+    int64_t ldx;     // floats between activation columns
+    int pro;
+    const float * norm_w;
+    float eps;
+    int64_t pro_k;
+    int pro_rep;
+    float * y;
+    int64_t ldy;     // floats between output columns
+    const float * res;
+    int64_t ldres;
+    int32_t * sums;  // when set: int32 (sub-)block sums of column 0, [N][sums_per_row], instead of y
+    int ncols;                // activation columns (without groups)
+    const int32_t * col_src;  // optional: column c reads x row col_src[c]
+    const int32_t * col_dst;  // optional: column c writes y (and reads res) row col_dst[c]
+    const int32_t * grp_off;  // optional: CTA row blockIdx.y computes group g's columns [grp_off[g], grp_off[g+1])
+    int64_t grp_rows;         //   with weight rows row0 + g * grp_rows (one expert's matrix)
+    // optional: activations already quantized (b200 internal layout, rows of x): aq int8 [R][K], ad float
+    // [R][K/32 or K/256], abs int16 [R][K/16]. Column c uses row col_src[c] (or c). Prologues do not apply.
+    const int8_t * aq;
+    const float * ad;
+    const int16_t * abs;
+};
+
+// Shared-memory staging of NC quantized activation columns.
+struct Act {
+    int8_t * q;           // [NC][K]
+    float * d;            // [NC][K/32] (q8_0) or [NC][K/256] (q8_K)
+    int16_t * bs;         // [NC][K/16] (q8_K)
+    __nv_bfloat16 * b;    // [NC][K] (bf16)
+    int64_t K;
+};
+
+inline __host__ __device__ int act_kind(int wtype) {
+    return wtype == B200_TYPE_Q8_0 ? B200_TYPE_Q8_0 : wtype == B200_TYPE_BF16 ? B200_TYPE_BF16 : B200_TYPE_Q8_K;
+}
+
+inline __host__ __device__ size_t act_smem_bytes(int wtype, int64_t K, int nc) {
+    const int kind = act_kind(wtype);
+    if (kind == B200_TYPE_BF16) return (size_t) nc * K * 2 + 64;
+    size_t s = (size_t) nc * K;                                   // q
+    s = (s + 15) & ~(size_t) 15;
+    if (kind == B200_TYPE_Q8_0) s += (size_t) nc * (K / 32) * 4;  // d
+    else s += (size_t) nc * (K / 256) * 4 + (size_t) nc * (K / 16) * 2;
+    return s + 64 + 16 * 8;                                       // + rms scales
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Prologue value of column c at index k.
+// ---------------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ float pro_value(const GemvParams & p, const float * xc, int c, int64_t k, const float * rms) {
+    if (!xc) return 0.0f;
+    switch (p.pro) {
+    case PRO_RMSNORM: return __fmul_rn(__fmul_rn(xc[k], rms[c]), p.norm_w[k]);
+    case PRO_SWIGLU: return __fmul_rn(silu(xc[k]), xc[p.pro_k + k]);
+    case PRO_GQA: {
+        const int64_t span = p.pro_k * p.pro_rep;
+        return xc[(k / span) * p.pro_k + k % p.pro_k];
+    }
+    default: return xc[k];
+    }
+}
+
+// Stages NC columns (block-wide; ends with __syncthreads).
+__device__ __forceinline__ const float * column_src(const GemvParams & p, int64_t c) {
+    return p.x + (p.col_src ? (int64_t) p.col_src[c] : c) * p.ldx;
+}
+
+// Stages columns c0 .. c0+nc-1 (nc <= NC; the rest are zeros). Block-wide; ends with __syncthreads.
+template <int NC>
+__device__ void stage_activations(const GemvParams & p, const Act & a, int kind, int64_t c0, int nc) {
+    __shared__ float rms[NC];
+    __shared__ const float * xcol[NC];
+    if (threadIdx.x < NC) xcol[threadIdx.x] = (int) threadIdx.x < nc ? column_src(p, c0 + threadIdx.x) : nullptr;
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    const int64_t K = a.K;
+    if (p.pro == PRO_RMSNORM) {
+        __shared__ float part[NC][32];
+        for (int c = 0; c < NC; c++) {
+            const float * xc = xcol[c];
+            float s = 0.0f;
+            if (xc)
+                for (int64_t k = threadIdx.x; k < K; k += blockDim.x) s = fmaf(xc[k], xc[k], s);
+            s = warp_sum(s);
+            if (lane == 0) part[c][warp] = s;
+        }
+        __syncthreads();
+        if (warp == 0) {
+            for (int c = 0; c < NC; c++) {
+                float s = lane < nwarps ? part[c][lane] : 0.0f;
+                s = warp_sum(s);
+                if (lane == 0) rms[c] = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(s, (float) K), p.eps)));
+            }
+        }
+        __syncthreads();
+    }
+    if (p.aq) {
+        // prequantized rows: copy into shared memory
+        for (int c = 0; c < NC; c++) {
+            const int64_t row = c < nc ? (p.col_src ? (int64_t) p.col_src[c0 + c] : c0 + c) : -1;
+            const int4 * src = row >= 0 ? reinterpret_cast<const int4 *>(p.aq + row * K) : nullptr;
+            int4 * dst = reinterpret_cast<int4 *>(a.q + (int64_t) c * K);
+            for (int64_t i = threadIdx.x; i < K / 16; i += blockDim.x) dst[i] = src ? src[i] : make_int4(0, 0, 0, 0);
+            const int64_t nd = kind == B200_TYPE_Q8_0 ? K / 32 : K / 256;
+            for (int64_t i = threadIdx.x; i < nd; i += blockDim.x) a.d[(int64_t) c * nd + i] = src ? p.ad[row * nd + i] : 0.0f;
+            if (kind == B200_TYPE_Q8_K)
+                for (int64_t i = threadIdx.x; i < K / 16; i += blockDim.x)
+                    a.bs[(int64_t) c * (K / 16) + i] = src ? p.abs[row * (K / 16) + i] : (int16_t) 0;
+        }
+    } else if (kind == B200_TYPE_Q8_0) {
+        const int64_t nb = K / 32;
+        for (int64_t i = warp; i < NC * nb; i += nwarps) {
+            const int c = (int) (i / nb);
+            const int64_t b = i % nb;
+            const float v = pro_value(p, xcol[c], c, b * 32 + lane, rms);
+            float d;
+            uint16_t dh;
+            const int8_t q = quantize_q8_0_lane(v, &d, &dh);
+            a.q[(int64_t) c * K + b * 32 + lane] = q;
+            if (lane == 0) a.d[(int64_t) c * nb + b] = d;
+        }
+    } else if (kind == B200_TYPE_Q8_K) {
+        const int64_t nb = K / 256;
+        for (int64_t i = warp; i < NC * nb; i += nwarps) {
+            const int c = (int) (i / nb);
+            const int64_t b = i % nb;
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) v[j] = pro_value(p, xcol[c], c, b * 256 + lane * 8 + j, rms);
+            int8_t q[8];
+            int16_t bsum;
+            float d;
+            quantize_q8_K_warp(v, q, &bsum, &d);
+            int2 packed;
+            packed.x = (int) (uint8_t) q[0] | ((int) (uint8_t) q[1] << 8) | ((int) (uint8_t) q[2] << 16) | ((int) (uint8_t) q[3] << 24);
+            packed.y = (int) (uint8_t) q[4] | ((int) (uint8_t) q[5] << 8) | ((int) (uint8_t) q[6] << 16) | ((int) (uint8_t) q[7] << 24);
+            *reinterpret_cast<int2 *>(a.q + (int64_t) c * K + b * 256 + lane * 8) = packed;
+            if ((lane & 1) == 0) a.bs[(int64_t) c * (K / 16) + b * 16 + lane / 2] = bsum;
+            if (lane == 0) a.d[(int64_t) c * nb + b] = d;
+        }
+    } else {
+        for (int64_t i = threadIdx.x; i < NC * K; i += blockDim.x) {
+            const int c = (int) (i / K);
+            a.b[i] = __float2bfloat16_rn(pro_value(p, xcol[c], c, i % K, rms));
+        }
+    }
+    __syncthreads();
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Per-type streaming units. A "unit" is what one lane loads per step; lanes of one (sub-)block cooperate through
+// shuffles, so every lane calls dot() for every step (invalid units contribute zero).
+// ---------------------------------------------------------------------------------------------------------------
+
+struct TQ8_0 {
+    // unit = 16 bytes of one 32-block (2 lanes per block)
+    struct Unit { int4 q; uint16_t d; };
+    static constexpr int kSumsPerBlockRow = 32;  // values per int32 sum
+    __device__ static int64_t units_per_row(int64_t K) { return K / 16; }
+    __device__ static int sums_per_row(int64_t K) { return (int) (K / 32); }
+    __device__ static Unit load(const WeightView & w, int64_t row, int64_t u, bool valid) {
+        Unit r;
+        if (valid) {
+            r.q = ld_stream(w.f0 + row * w.K + u * 16);
+            r.d = (u & 1) ? 0 : __ldg(reinterpret_cast<const unsigned short *>(w.f1) + row * (w.K / 32) + u / 2);
+        } else {
+            r.q = make_int4(0, 0, 0, 0);
+            r.d = 0;
+        }
+        return r;
+    }
+    template <int NC>
+    __device__ static void dot(const Unit & U, int64_t u, bool valid, const Act & a, float * acc, int32_t * sums) {
+        const int * wq = reinterpret_cast<const int *>(&U.q);
+        const float dw = __half2float(__ushort_as_half(U.d));
+#pragma unroll
+        for (int c = 0; c < NC; c++) {
+            int s = 0;
+            if (valid) {
+                const int4 xv = *reinterpret_cast<const int4 *>(a.q + (int64_t) c * a.K + u * 16);
+                s = __dp4a(wq[0], xv.x, s);
+                s = __dp4a(wq[1], xv.y, s);
+                s = __dp4a(wq[2], xv.z, s);
+                s = __dp4a(wq[3], xv.w, s);
+            }
+            s += __shfl_xor_sync(0xffffffffu, s, 1);
+            if (valid && (u & 1) == 0) {
+                const float dx = a.d[(int64_t) c * (a.K / 32) + u / 2];
+                acc[c] += (float) s * __fmul_rn(dw, dx);
+                if (c == 0 && sums) sums[u / 2] = s;
+            }
+        }
+    }
+};
+
+struct TQ4_K {
+    // unit = 16 bytes of qs: super-block u/8, byte chunk (u%8)*16 (8 lanes per super-block); plus the 16-byte meta
+    struct Unit { int4 q; int4 m; };
+    __device__ static int64_t units_per_row(int64_t K) { return K / 32; }  // K/2 bytes of nibbles, 16 per unit
+    __device__ static int sums_per_row(int64_t K) { return (int) (2 * (K / 256)); }
+    __device__ static Unit load(const WeightView & w, int64_t row, int64_t u, bool valid) {
+        Unit r;
+        if (valid) {
+            r.q = ld_stream(w.f0 + row * (w.K / 2) + u * 16);
+            r.m = __ldg(reinterpret_cast<const int4 *>(w.f1 + (row * (w.K / 256) + u / 8) * 16));
+        } else {
+            r.q = make_int4(0, 0, 0, 0);
+            r.m = make_int4(0, 0, 0, 0);
+        }
+        return r;
+    }
+    __device__ static void scale_min(const uint8_t * s, int j, int & sc, int & m) {
+        if (j < 4) {
+            sc = s[j] & 63;
+            m = s[j + 4] & 63;
+        } else {
+            sc = (s[j + 4] & 15) | ((s[j - 4] >> 6) << 4);
+            m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+        }
+    }
+    template <int NC>
+    __device__ static void dot(const Unit & U, int64_t u, bool valid, const Act & a, float * acc, int32_t * sums) {
+        const int * wq = reinterpret_cast<const int *>(&U.q);
+        const uint8_t * meta = reinterpret_cast<const uint8_t *>(&U.m);
+        const int64_t sb = u / 8;
+        const int j = (int) (u & 7), g = j >> 1, h = j & 1;
+        const int s0 = 2 * g, s1 = 2 * g + 1;
+        int sc0 = 0, m0 = 0, sc1 = 0, m1 = 0;
+        if (valid) {
+            scale_min(meta + 4, s0, sc0, m0);
+            scale_min(meta + 4, s1, sc1, m1);
+        }
+        const float dw = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t *>(meta)));
+        const float dmw = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t *>(meta + 2)));
+#pragma unroll
+        for (int c = 0; c < NC; c++) {
+            int si = 0, sm = 0;
+            if (valid) {
+                const int8_t * xq = a.q + (int64_t) c * a.K + sb * 256;
+                const int4 xl = *reinterpret_cast<const int4 *>(xq + s0 * 32 + h * 16);
+                const int4 xh = *reinterpret_cast<const int4 *>(xq + s1 * 32 + h * 16);
+                int il = 0, ih = 0;
+                il = __dp4a(wq[0] & 0x0F0F0F0F, xl.x, il);
+                il = __dp4a(wq[1] & 0x0F0F0F0F, xl.y, il);
+                il = __dp4a(wq[2] & 0x0F0F0F0F, xl.z, il);
+                il = __dp4a(wq[3] & 0x0F0F0F0F, xl.w, il);
+                ih = __dp4a((wq[0] >> 4) & 0x0F0F0F0F, xh.x, ih);
+                ih = __dp4a((wq[1] >> 4) & 0x0F0F0F0F, xh.y, ih);
+                ih = __dp4a((wq[2] >> 4) & 0x0F0F0F0F, xh.z, ih);
+                ih = __dp4a((wq[3] >> 4) & 0x0F0F0F0F, xh.w, ih);
+                si = sc0 * il + sc1 * ih;
+                if (h == 0) {
+                    const int16_t * bs = a.bs + (int64_t) c * (a.K / 16) + sb * 16;
+                    sm = m0 * ((int) bs[2 * s0] + (int) bs[2 * s0 + 1]) + m1 * ((int) bs[2 * s1] + (int) bs[2 * s1 + 1]);
+                }
+            }
+            si += __shfl_xor_sync(0xffffffffu, si, 1);
+            si += __shfl_xor_sync(0xffffffffu, si, 2);
+            si += __shfl_xor_sync(0xffffffffu, si, 4);
+            sm += __shfl_xor_sync(0xffffffffu, sm, 1);
+            sm += __shfl_xor_sync(0xffffffffu, sm, 2);
+            sm += __shfl_xor_sync(0xffffffffu, sm, 4);
+            if (valid && j == 0) {
+                const float dx = a.d[(int64_t) c * (a.K / 256) + sb];
+                acc[c] += __fmul_rn(dx, dw) * (float) si;
+                acc[c] -= __fmul_rn(dx, dmw) * (float) sm;
+                if (c == 0 && sums) {
+                    sums[2 * sb] = si;
+                    sums[2 * sb + 1] = sm;
+                }
+            }
+        }
+    }
+};
+
+struct TQ6_K {
+    // unit = a quarter of a super-block: half h = (u%4)/2, values l in [lq, lq+16), lq = (u%2)*16, all four t:
+    // 16 bytes of ql (t = 0, 2), 16 bytes of ql (t = 1, 3), 16 bytes of qh, and the 16 scales.
+    struct Unit { int4 a; int4 b; int4 h; int4 s; uint16_t d; };
+    __device__ static int64_t units_per_row(int64_t K) { return K / 64; }
+    __device__ static int sums_per_row(int64_t K) { return (int) (K / 256); }
+    __device__ static Unit load(const WeightView & w, int64_t row, int64_t u, bool valid) {
+        Unit r;
+        if (valid) {
+            const int64_t sb = u / 4;
+            const int j = (int) (u & 3), h = j >> 1, lq = (j & 1) * 16;
+            const int64_t nsb = w.K / 256;
+            const uint8_t * ql = w.f0 + row * (w.K / 2) + sb * 128 + h * 64 + lq;
+            r.a = ld_stream(ql);
+            r.b = ld_stream(ql + 32);
+            r.h = ld_stream(w.f1 + row * (w.K / 4) + sb * 64 + h * 32 + lq);
+            r.s = __ldg(reinterpret_cast<const int4 *>(w.f2 + (row * nsb + sb) * 16));
+            r.d = __ldg(reinterpret_cast<const unsigned short *>(w.f3) + row * nsb + sb);
+        } else {
+            r.a = r.b = r.h = r.s = make_int4(0, 0, 0, 0);
+            r.d = 0;
+        }
+        return r;
+    }
+    template <int NC>
+    __device__ static void dot(const Unit & U, int64_t u, bool valid, const Act & a, float * acc, int32_t * sums) {
+        const int * A = reinterpret_cast<const int *>(&U.a);
+        const int * B = reinterpret_cast<const int *>(&U.b);
+        const int * H = reinterpret_cast<const int *>(&U.h);
+        const int8_t * sc = reinterpret_cast<const int8_t *>(&U.s);
+        const int64_t sb = u / 4;
+        const int j = (int) (u & 3), h = j >> 1, lh = j & 1;
+        const float dw = __half2float(__ushort_as_half(U.d));
+#pragma unroll
+        for (int c = 0; c < NC; c++) {
+            int si = 0;
+            if (valid) {
+                const int8_t * xq = a.q + (int64_t) c * a.K + sb * 256 + h * 128 + lh * 16;
+                const int16_t * bs = a.bs + (int64_t) c * (a.K / 16) + sb * 16 + h * 8 + lh;
+#pragma unroll
+                for (int t = 0; t < 4; t++) {
+                    const int4 xv = *reinterpret_cast<const int4 *>(xq + t * 32);
+                    const int * src = (t & 1) ? B : A;
+                    const int shift = (t >> 1) * 4;
+                    int s = 0;
+                    const int xs[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const int v = ((src[i] >> shift) & 0x0F0F0F0F) | (((H[i] >> (2 * t)) & 0x03030303) << 4);
+                        s = __dp4a(v, xs[i], s);
+                    }
+                    // sum (q - 32) x = sum q x - 32 sum x; sum x over these 16 values is their q8_K bsum
+                    s -= 32 * (int) bs[2 * t];
+                    si += (int) sc[h * 8 + 2 * t + lh] * s;
+                }
+            }
+            si += __shfl_xor_sync(0xffffffffu, si, 1);
+            si += __shfl_xor_sync(0xffffffffu, si, 2);
+            if (valid && j == 0) {
+                const float dx = a.d[(int64_t) c * (a.K / 256) + sb];
+                acc[c] += __fmul_rn(dw, dx) * (float) si;
+                if (c == 0 && sums) sums[sb] = si;
+            }
+        }
+    }
+};
+
+struct TBF16 {
+    struct Unit { int4 q; };
+    __device__ static int64_t units_per_row(int64_t K) { return K / 8; }
+    __device__ static int sums_per_row(int64_t) { return 0; }
+    __device__ static Unit load(const WeightView & w, int64_t row, int64_t u, bool valid) {
+        Unit r;
+        r.q = valid ? ld_stream(w.f0 + (row * w.K + u * 8) * 2) : make_int4(0, 0, 0, 0);
+        return r;
+    }
+    template <int NC>
+    __device__ static void dot(const Unit & U, int64_t u, bool valid, const Act & a, float * acc, int32_t *) {
+        if (!valid) return;
+        const __nv_bfloat162 * wv = reinterpret_cast<const __nv_bfloat162 *>(&U.q);
+#pragma unroll
+        for (int c = 0; c < NC; c++) {
+            const int4 xr = *reinterpret_cast<const int4 *>(a.b + (int64_t) c * a.K + u * 8);
+            const __nv_bfloat162 * xv = reinterpret_cast<const __nv_bfloat162 *>(&xr);
+            float s = acc[c];
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const float2 wf = __bfloat1622float2(wv[i]);
+                const float2 xf = __bfloat1622float2(xv[i]);
+                s = fmaf(wf.x, xf.x, s);  // bf16 x bf16 is exact in f32: one rounding either way
+                s = fmaf(wf.y, xf.y, s);
+            }
+            acc[c] = s;
+        }
+    }
+};
+
+// ---------------------------------------------------------------------------------------------------------------
+// The kernel: each warp walks a flat sequence of (row, unit batch) steps with a two-deep register pipeline.
+// Without groups, CTAs split the N rows (grid.x); with groups (MUL_MAT_ID), grid.y is the expert and each CTA runs
+// that expert's routed columns in chunks of NC against its slice of the expert's rows.
+// ---------------------------------------------------------------------------------------------------------------
+constexpr int kGemvThreads = 512;
+constexpr int kGemvUnroll = 2;  // units per lane per step
+
+template <class T, int NC>
+__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvParams p) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int lane = threadIdx.x & 31;
+    const int64_t warps_total = (int64_t) gridDim.x * (blockDim.x >> 5);
+    const int64_t gwarp = (int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int64_t upr = T::units_per_row(p.w.K);
+    const int64_t per_step = 32 * kGemvUnroll;
+    const int64_t steps_per_row = (upr + per_step - 1) / per_step;
+    const int64_t my_rows = gwarp < p.N ? (p.N - gwarp + warps_total - 1) / warps_total : 0;
+    const int64_t my_steps = my_rows * steps_per_row;
+    const bool grouped = p.grp_off != nullptr;
+    int64_t row0 = p.row0;
+
+    typename T::Unit cur[kGemvUnroll], nxt[kGemvUnroll];
+    auto load_step = [&](int64_t s, typename T::Unit * dst) {
+        const int64_t r = gwarp + (s / steps_per_row) * warps_total;
+        const int64_t u0 = (s % steps_per_row) * per_step;
+#pragma unroll
+        for (int i = 0; i < kGemvUnroll; i++) {
+            const int64_t u = u0 + i * 32 + lane;
+            dst[i] = T::load(p.w, row0 + r, u, s < my_steps && u < upr);
+        }
+    };
+    // Weight bytes depend on nothing: start streaming before waiting for the previous kernel. (With groups the
+    // routing is the previous kernel's output, so the stream starts after the wait.)
+    if (!grouped) load_step(0, cur);
+    pdl_launch_dependents();
+    pdl_wait();
+
+    int64_t cbeg = 0, cend = p.ncols;
+    if (grouped) {
+        cbeg = p.grp_off[blockIdx.y];
+        cend = p.grp_off[blockIdx.y + 1];
+        row0 += (int64_t) blockIdx.y * p.grp_rows;
+    }
+
+    Act a;
+    const int kind = act_kind(p.w.type);
+    {
+        const int64_t K = p.w.K;
+        uint8_t * s = smem;
+        a.K = K;
+        a.q = nullptr; a.d = nullptr; a.bs = nullptr; a.b = nullptr;
+        if (kind == B200_TYPE_BF16) {
+            a.b = reinterpret_cast<__nv_bfloat16 *>(s);
+        } else {
+            a.q = reinterpret_cast<int8_t *>(s);
+            s += ((size_t) NC * K + 15) & ~(size_t) 15;
+            a.d = reinterpret_cast<float *>(s);
+            if (kind == B200_TYPE_Q8_K) {
+                s += (size_t) NC * (K / 256) * 4;
+                a.bs = reinterpret_cast<int16_t *>(s);
+            }
+        }
+    }
+    const int nsums = T::sums_per_row(p.w.K);
+
+    for (int64_t c0 = cbeg; c0 < cend; c0 += NC) {
+        const int nc = (int) ((cend - c0) < NC ? (cend - c0) : NC);
+        if (grouped || c0 != cbeg) {
+            __syncthreads();  // the previous chunk's staging is no longer read
+            load_step(0, cur);
+        }
+        stage_activations<NC>(p, a, kind, c0, nc);
+
+        float acc[NC];
+#pragma unroll
+        for (int c = 0; c < NC; c++) acc[c] = 0.0f;
+        for (int64_t s = 0; s < my_steps; s++) {
+            if (s + 1 < my_steps) load_step(s + 1, nxt);
+            const int64_t r = gwarp + (s / steps_per_row) * warps_total;
+            const int64_t u0 = (s % steps_per_row) * per_step;
+            int32_t * sums = p.sums ? p.sums + r * nsums : nullptr;
+#pragma unroll
+            for (int i = 0; i < kGemvUnroll; i++) {
+                const int64_t u = u0 + i * 32 + lane;
+                T::template dot<NC>(cur[i], u, u < upr, a, acc, sums);
+            }
+            if (s % steps_per_row == steps_per_row - 1) {
+#pragma unroll
+                for (int c = 0; c < NC; c++) {
+                    const float v = warp_sum(acc[c]);
+                    if (lane == 0 && c < nc && !p.sums) {
+                        const int64_t col = p.col_dst ? (int64_t) p.col_dst[c0 + c] : c0 + c;
+                        float out = v;
+                        if (p.res) out = __fadd_rn(p.res[col * p.ldres + r], v);
+                        p.y[col * p.ldy + r] = out;
+                    }
+                    acc[c] = 0.0f;
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < kGemvUnroll; i++) cur[i] = nxt[i];
+        }
+    }
+}
+
+}  // namespace b200

@@ -1,0 +1,46 @@
+// internal.h — host-side declarations shared by the backend's translation units (not part of the C ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <string>
+
+#include "../../include/b200.h"
+#include "common.cuh"
+#include "gemv.cuh"
+
+// Device error bits, OR-ed by kernels into b200_context::dev_err and reported by b200_synchronize().
+#define B200_DEVERR_ROWS 1u     // GET_ROWS id out of range
+#define B200_DEVERR_EXPERT 2u   // MUL_MAT_ID id out of range
+#define B200_DEVERR_TIMEOUT 4u  // a bounded wait gave up
+
+struct b200_context {
+    int device = 0;
+    int num_sms = 0;
+    cudaStream_t stream = nullptr;
+    std::string last_error;
+    unsigned * dev_err = nullptr;     // device word of B200_DEVERR_* bits
+    unsigned * host_err = nullptr;    // pinned mirror
+    void * scratch = nullptr;         // per-op scratch (quantized activations, routing tables)
+    size_t scratch_bytes = 0;
+    void * staging = nullptr;         // device staging for weight uploads
+    size_t staging_bytes = 0;
+};
+
+namespace b200 {
+
+WeightView view_of(const b200_weight * w);
+
+// Kernel launchers (ops.cu). Each returns the launch's cudaError_t.
+cudaError_t launch_gemv(const GemvParams & p, int nc, int grid_y, cudaStream_t st, bool pdl, int num_sms);
+int gemv_max_columns(int wtype, int64_t K);  // largest NC whose staging fits in shared memory
+cudaError_t launch_repack(int type, const b200_weight * w, const uint8_t * src, int64_t off0, int64_t n, bool to_device_layout,
+                          uint8_t * gather_dst, cudaStream_t st);
+cudaError_t launch_get_rows(const WeightView & w, const int32_t * ids, int64_t n, float * dst, unsigned * err, cudaStream_t st);
+// Activation quantization: gguf != null writes GGUF blocks there; else the internal layout (q, d, bs).
+cudaError_t launch_quantize(int kind, const float * x, int64_t K, int64_t M, uint8_t * gguf, int8_t * q, float * d, int16_t * bs,
+                            cudaStream_t st);
+cudaError_t launch_route(const int32_t * ids, int64_t T, int64_t top_k, int64_t nb1, int64_t E, int32_t * grp_off,
+                         int32_t * col_src, int32_t * col_dst, unsigned * err, cudaStream_t st);
+
+}  // namespace b200

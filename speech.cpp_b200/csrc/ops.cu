@@ -1,0 +1,307 @@
+// ops.cu — kernels of the non-GEMV ops and the GEMV launchers.
+//
+//  - repack_scatter / repack_gather: the weight buffer's set_tensor / get_tensor (src/common/model-file.cpp:247-268
+//    uploads GGUF bytes in 16 MiB pieces at any offset). The repacked layout (common.cuh) is a byte permutation of the
+//    GGUF bytes, so a piece maps byte by byte.
+//  - get_rows: quantized GET_ROWS (src/families/qwen3-tts/talker.cpp:131-133, src/families/qwen3-asr/decoder.cpp:319),
+//    dequantizing with the same float operations, in the same order, as the CPU dequantizers (bit-identical).
+//  - quantize_act: the CPU backend's src1 quantization (q8_0 / q8_K), bit-identical to the oracle.
+//  - route: MUL_MAT_ID's router sort (src/families/drama3/text-model.cpp:208-210): (token, slot) pairs grouped by
+//    expert with a shared-memory histogram and scan, so each expert's rows stream once over all of its pairs.
+#include "internal.h"
+
+namespace b200 {
+
+// ------------------------------------------------------------------------------------------------------------------
+// Layout
+// ------------------------------------------------------------------------------------------------------------------
+struct FieldOff {
+    int64_t f[4];
+};
+
+__device__ __forceinline__ int64_t repacked_offset(int type, int64_t o, const FieldOff & fo) {
+    switch (type) {
+    case B200_TYPE_Q8_0: {
+        const int64_t b = o / 34, w = o % 34;
+        return w < 2 ? fo.f[1] + b * 2 + w : fo.f[0] + b * 32 + (w - 2);
+    }
+    case B200_TYPE_Q4_K: {
+        const int64_t b = o / 144, w = o % 144;
+        return w < 16 ? fo.f[1] + b * 16 + w : fo.f[0] + b * 128 + (w - 16);
+    }
+    case B200_TYPE_Q6_K: {
+        const int64_t b = o / 210, w = o % 210;
+        if (w < 128) return fo.f[0] + b * 128 + w;
+        if (w < 192) return fo.f[1] + b * 64 + (w - 128);
+        if (w < 208) return fo.f[2] + b * 16 + (w - 192);
+        return fo.f[3] + b * 2 + (w - 208);
+    }
+    default: return o;
+    }
+}
+
+__global__ void repack_kernel(int type, FieldOff fo, const uint8_t * __restrict__ src, int64_t off0, int64_t n,
+                              uint8_t * __restrict__ dev, uint8_t * __restrict__ gather_dst) {
+    for (int64_t i = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t) gridDim.x * blockDim.x) {
+        const int64_t d = repacked_offset(type, off0 + i, fo);
+        if (gather_dst) gather_dst[i] = dev[d];
+        else dev[d] = src[i];
+    }
+}
+
+cudaError_t launch_repack(int type, const b200_weight * w, const uint8_t * src, int64_t off0, int64_t n, bool to_device_layout,
+                          uint8_t * gather_dst, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    FieldOff fo;
+    for (int i = 0; i < 4; i++) fo.f[i] = w->field_off[i];
+    const int threads = 256;
+    const int64_t blocks = (n + threads - 1) / threads < 148 * 16 ? (n + threads - 1) / threads : 148 * 16;
+    repack_kernel<<<(unsigned) blocks, threads, 0, st>>>(type, fo, src, off0, n, (uint8_t *) w->data,
+                                                          to_device_layout ? nullptr : gather_dst);
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// GET_ROWS
+// ------------------------------------------------------------------------------------------------------------------
+__global__ void get_rows_kernel(WeightView w, const int32_t * __restrict__ ids, float * __restrict__ dst, unsigned * err) {
+    const int64_t i = blockIdx.x;
+    const int64_t r = ids[i];
+    if (r < 0 || r >= w.rows) {
+        if (threadIdx.x == 0) atomicOr(err, B200_DEVERR_ROWS);
+        return;
+    }
+    const int64_t K = w.K;
+    float * out = dst + i * K;
+    for (int64_t k = threadIdx.x; k < K; k += blockDim.x) {
+        float v;
+        switch (w.type) {
+        case B200_TYPE_Q8_0: {
+            const float d = __half2float(__ushort_as_half(reinterpret_cast<const uint16_t *>(w.f1)[r * (K / 32) + k / 32]));
+            v = __fmul_rn((float) reinterpret_cast<const int8_t *>(w.f0)[r * K + k], d);
+            break;
+        }
+        case B200_TYPE_Q4_K: {
+            const int64_t sb = k / 256;
+            const int s = (int) ((k % 256) / 32), l = (int) (k % 32);
+            const uint8_t * meta = w.f1 + (r * (K / 256) + sb) * 16;
+            const int q = (w.f0[r * (K / 2) + sb * 128 + (s >> 1) * 32 + l] >> ((s & 1) * 4)) & 15;
+            int sc, m;
+            TQ4_K::scale_min(meta + 4, s, sc, m);
+            const float d = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t *>(meta)));
+            const float dmin = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t *>(meta + 2)));
+            v = __fsub_rn(__fmul_rn(__fmul_rn(d, (float) sc), (float) q), __fmul_rn(dmin, (float) m));
+            break;
+        }
+        case B200_TYPE_Q6_K: {
+            const int64_t sb = k / 256;
+            const int vv = (int) (k % 256), h = vv >> 7, t = (vv >> 5) & 3, l = vv & 31;
+            const int lo = (w.f0[r * (K / 2) + sb * 128 + h * 64 + (t & 1) * 32 + l] >> ((t >> 1) * 4)) & 15;
+            const int hi = (w.f1[r * (K / 4) + sb * 64 + h * 32 + l] >> (2 * t)) & 3;
+            const int q = (lo | (hi << 4)) - 32;
+            const int sc = reinterpret_cast<const int8_t *>(w.f2)[(r * (K / 256) + sb) * 16 + vv / 16];
+            const float d = __half2float(__ushort_as_half(reinterpret_cast<const uint16_t *>(w.f3)[r * (K / 256) + sb]));
+            v = __fmul_rn(__fmul_rn(d, (float) sc), (float) q);
+            break;
+        }
+        case B200_TYPE_BF16:
+            v = __uint_as_float((unsigned) reinterpret_cast<const uint16_t *>(w.f0)[r * K + k] << 16);
+            break;
+        default:
+            v = reinterpret_cast<const float *>(w.f0)[r * K + k];
+            break;
+        }
+        out[k] = v;
+    }
+}
+
+cudaError_t launch_get_rows(const WeightView & w, const int32_t * ids, int64_t n, float * dst, unsigned * err, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    get_rows_kernel<<<(unsigned) n, 256, 0, st>>>(w, ids, dst, err);
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// Activation quantization (one warp per block)
+// ------------------------------------------------------------------------------------------------------------------
+__global__ void quantize_act_kernel(int kind, const float * __restrict__ x, int64_t K, int64_t M, uint8_t * gguf, int8_t * q,
+                                    float * d, int16_t * bs) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t) gridDim.x * (blockDim.x >> 5);
+    const int64_t bsz = kind == B200_TYPE_Q8_0 ? 32 : 256;
+    const int64_t nb = K / bsz;
+    for (int64_t i = (int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); i < M * nb; i += warps) {
+        const int64_t r = i / nb, b = i % nb;
+        const float * xb = x + r * K + b * bsz;
+        if (kind == B200_TYPE_Q8_0) {
+            float df;
+            uint16_t dh;
+            const int8_t qv = quantize_q8_0_lane(xb[lane], &df, &dh);
+            if (gguf) {
+                uint8_t * blk = gguf + i * 34;
+                blk[2 + lane] = (uint8_t) qv;
+                if (lane == 0) *reinterpret_cast<uint16_t *>(blk) = dh;
+            } else {
+                q[r * K + b * 32 + lane] = qv;
+                if (lane == 0) d[i] = df;
+            }
+        } else {
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) v[j] = xb[lane * 8 + j];
+            int8_t qv[8];
+            int16_t bsum;
+            float df;
+            quantize_q8_K_warp(v, qv, &bsum, &df);
+            if (gguf) {
+                uint8_t * blk = gguf + i * 292;
+#pragma unroll
+                for (int j = 0; j < 8; j++) blk[4 + lane * 8 + j] = (uint8_t) qv[j];
+                if ((lane & 1) == 0) reinterpret_cast<int16_t *>(blk + 260)[lane / 2] = bsum;
+                if (lane == 0) *reinterpret_cast<float *>(blk) = df;
+            } else {
+#pragma unroll
+                for (int j = 0; j < 8; j++) q[r * K + b * 256 + lane * 8 + j] = qv[j];
+                if ((lane & 1) == 0) bs[r * (K / 16) + b * 16 + lane / 2] = bsum;
+                if (lane == 0) d[i] = df;
+            }
+        }
+    }
+}
+
+cudaError_t launch_quantize(int kind, const float * x, int64_t K, int64_t M, uint8_t * gguf, int8_t * q, float * d, int16_t * bs,
+                            cudaStream_t st) {
+    const int64_t nb = M * (K / (kind == B200_TYPE_Q8_0 ? 32 : 256));
+    if (nb <= 0) return cudaSuccess;
+    const int threads = 256;
+    int64_t blocks = (nb + 7) / 8;
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    quantize_act_kernel<<<(unsigned) blocks, threads, 0, st>>>(kind, x, K, M, gguf, q, d, bs);
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// MUL_MAT_ID routing: one CTA histograms the expert ids, scans, and places each (token, slot) pair in its expert's
+// segment. Pairs of one expert are independent products, so the order inside a segment does not change any result.
+// ------------------------------------------------------------------------------------------------------------------
+__global__ void route_kernel(const int32_t * __restrict__ ids, int64_t P, int64_t top_k, int64_t nb1, int E, int32_t * grp_off,
+                             int32_t * col_src, int32_t * col_dst, unsigned * err) {
+    extern __shared__ int cnt[];  // [E] counts, then [E] cursors
+    int * pos = cnt + E;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+    __syncthreads();
+    for (int64_t p = threadIdx.x; p < P; p += blockDim.x) {
+        const int e = ids[p];
+        if (e < 0 || e >= E) {
+            atomicOr(err, B200_DEVERR_EXPERT);
+            continue;
+        }
+        atomicAdd(&cnt[e], 1);
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        // warp-parallel exclusive scan over E counts, 32 at a time
+        int carry = 0;
+        for (int base = 0; base < E; base += 32) {
+            const int e = base + (int) threadIdx.x;
+            const int v = e < E ? cnt[e] : 0;
+            int incl = v;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int t = __shfl_up_sync(0xffffffffu, incl, o);
+                if ((int) threadIdx.x >= o) incl += t;
+            }
+            if (e < E) {
+                grp_off[e] = carry + incl - v;
+                pos[e] = carry + incl - v;
+            }
+            carry += __shfl_sync(0xffffffffu, incl, 31);
+        }
+        if (threadIdx.x == 0) grp_off[E] = carry;
+    }
+    __syncthreads();
+    for (int64_t p = threadIdx.x; p < P; p += blockDim.x) {
+        const int e = ids[p];
+        if (e < 0 || e >= E) continue;
+        const int slot = atomicAdd(&pos[e], 1);
+        const int64_t t = p / top_k, s = p % top_k;
+        col_src[slot] = (int32_t) (t * nb1 + (nb1 == 1 ? 0 : s));
+        col_dst[slot] = (int32_t) p;
+    }
+}
+
+cudaError_t launch_route(const int32_t * ids, int64_t T, int64_t top_k, int64_t nb1, int64_t E, int32_t * grp_off,
+                         int32_t * col_src, int32_t * col_dst, unsigned * err, cudaStream_t st) {
+    route_kernel<<<1, 1024, (size_t) 2 * E * sizeof(int), st>>>(ids, T * top_k, top_k, nb1, (int) E, grp_off, col_src, col_dst, err);
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// GEMV launchers
+// ------------------------------------------------------------------------------------------------------------------
+template <class T, int NC>
+static cudaError_t launch_one(const GemvParams & p, int grid_y, cudaStream_t st, bool pdl, int num_sms) {
+    auto kern = gemv_kernel<T, NC>;
+    const size_t smem = act_smem_bytes(p.w.type, p.w.K, NC);
+    static int configured_smem = 0;  // per instantiation
+    static int ctas_per_sm = 0;
+    if ((int) smem > configured_smem) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+        if (e != cudaSuccess) return e;
+        configured_smem = (int) smem;
+        ctas_per_sm = 0;
+    }
+    if (ctas_per_sm == 0) {
+        int n = 0;
+        cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kGemvThreads, configured_smem);
+        if (e != cudaSuccess) return e;
+        ctas_per_sm = n > 0 ? n : 1;
+    }
+    const int warps_per_cta = kGemvThreads / 32;
+    int64_t gx = (p.N + warps_per_cta - 1) / warps_per_cta;
+    const int64_t cap = grid_y > 1 ? gx : (int64_t) num_sms * ctas_per_sm;
+    if (gx > cap) gx = cap;
+    if (gx < 1) gx = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned) gx, (unsigned) grid_y, 1);
+    cfg.blockDim = dim3(kGemvThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
+template <class T>
+static cudaError_t launch_nc(const GemvParams & p, int nc, int grid_y, cudaStream_t st, bool pdl, int num_sms) {
+    switch (nc) {
+    case 1: return launch_one<T, 1>(p, grid_y, st, pdl, num_sms);
+    case 2: return launch_one<T, 2>(p, grid_y, st, pdl, num_sms);
+    case 4: return launch_one<T, 4>(p, grid_y, st, pdl, num_sms);
+    case 8: return launch_one<T, 8>(p, grid_y, st, pdl, num_sms);
+    case 16: return launch_one<T, 16>(p, grid_y, st, pdl, num_sms);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t launch_gemv(const GemvParams & p, int nc, int grid_y, cudaStream_t st, bool pdl, int num_sms) {
+    switch (p.w.type) {
+    case B200_TYPE_Q8_0: return launch_nc<TQ8_0>(p, nc, grid_y, st, pdl, num_sms);
+    case B200_TYPE_Q4_K: return launch_nc<TQ4_K>(p, nc, grid_y, st, pdl, num_sms);
+    case B200_TYPE_Q6_K: return launch_nc<TQ6_K>(p, nc, grid_y, st, pdl, num_sms);
+    case B200_TYPE_BF16: return launch_nc<TBF16>(p, nc, grid_y, st, pdl, num_sms);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+int gemv_max_columns(int wtype, int64_t K) {
+    const size_t limit = 200 * 1024;
+    for (int nc = 16; nc >= 1; nc >>= 1)
+        if (act_smem_bytes(wtype, K, nc) <= limit) return nc;
+    return 0;
+}
+
+}  // namespace b200
