@@ -1,0 +1,341 @@
+"""bench.py — decode tokens/s of the Qwen3-TTS 0.6B talker decode-step matmul stack on B200.
+
+Contract (the driver's): `python bench.py --gpus N --steps K --warmup W [--impl reference]` prints ONE JSON line.
+A step is one decode step: 28 layers x {q|k|v, o, gate|up, down} Q8_0 products plus the 1024 -> 3072 codec head,
+with the decoder's glue (RMSNorm, SwiGLU, residuals) fused into the products, for one token. Weights are random
+N(0, 0.02) quantized on the device by the backend's own Q8_0 quantizer (bit-identical to ggml's reference row
+quantizer); the input row is N(0, 1). The weights (471 MB) are larger than L2 (126 MB), so every step streams them
+from HBM. The single-stream step does not shard: with N > 1 each rank runs an independent replica ("replicas only")
+and `value` is the sum over ranks (N x steps / max-over-ranks time).
+
+`--impl reference` times the CPU restatement of ggml's CPU backend (oracle/, the reference's own CPU path restated;
+ggml itself is absent from the reference checkout) on a bounded sample of the same step, with all host threads.
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIG = "tts06"
+METRIC = "decode tok/s, Qwen3-TTS 0.6B talker decode-step matmul stack (Q8_0, batch 1)"
+UNIT = "tok/s"
+
+
+def load_package():
+    import importlib.util
+
+    name = "speechcpp_b200"
+    if name in sys.modules:
+        return sys.modules[name]
+    path = os.path.join(ROOT, "speech.cpp_b200", "__init__.py")
+    spec = importlib.util.spec_from_file_location(name, path, submodule_search_locations=[os.path.dirname(path)])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def profile_traffic():
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary (profiles/), when present."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f)
+    except Exception:
+        return None
+
+
+class Clocks:
+    """Samples nvidia-smi during the timed region (SM clock, throttle reasons)."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.p = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.p:
+            time.sleep(0.25)
+            self.p.terminate()
+            try:
+                out, _ = self.p.communicate(timeout=5)
+            except Exception:
+                out = ""
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+class CpuStep:
+    """The oracle's CPU step on a bounded sample (2 of the 28 layers + the head), scaled to tokens/s of the full step:
+    per token = median layer time x 28 + head time. All host threads (OpenMP) unless nthreads is given."""
+
+    def __init__(self, nthreads=0):
+        import numpy as np
+
+        from oracle import oracle, stack
+
+        self.stack = stack
+        self.c = stack.CONFIGS[CONFIG]
+        self.nthreads = nthreads
+        self.model = stack.random_model(self.c, seed=99, n_layer=2, nthreads=nthreads)
+        self.x = np.random.default_rng(5).normal(0, 1, size=self.c["hidden"]).astype(np.float32)
+        self.cores = oracle.max_threads() if nthreads <= 0 else nthreads
+        self.t_layer, self.t_head = [], []
+
+    def once(self):
+        st, c = self.stack, self.c
+        for L in self.model["layers"]:
+            a = time.perf_counter()
+            st.layer(c, L, self.x, 1e-6, self.nthreads)
+            self.t_layer.append(time.perf_counter() - a)
+        a = time.perf_counter()
+        st.head(c, self.model, self.x, 1e-6, self.nthreads)
+        self.t_head.append(time.perf_counter() - a)
+        return 1.0 / ((self.t_layer[-1] + self.t_layer[-2]) / 2 * c["n_layer"] + self.t_head[-1])
+
+    def rate(self):
+        return 1.0 / (statistics.median(self.t_layer) * self.c["n_layer"] + statistics.median(self.t_head))
+
+    def sample_text(self, reps):
+        return f"{reps} passes of 2 of the 28 layers + the head (Q8_0, batch 1); median layer x 28 + median head"
+
+
+def cpu_sample(seconds_target=12.0, nthreads=0):
+    cs = CpuStep(nthreads)
+    cs.once()
+    reps = 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < seconds_target or reps < 3:
+        cs.once()
+        reps += 1
+    return cs.rate(), cs.cores, cs.sample_text(reps)
+
+
+def run_reference(args):
+    world, rank, local = dist_setup(args)
+    if rank != 0:
+        return 0
+    cs = CpuStep()
+    for _ in range(args.warmup):
+        cs.once()
+    cs.t_layer, cs.t_head = [], []
+    t0 = time.perf_counter()
+    vals = [cs.once() for _ in range(args.steps)]
+    wall = time.perf_counter() - t0
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1000.0 / value, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8xint8->int32, f32 accumulate", "data": "synthetic",
+        "config": {"workload": "qwen3-tts-0.6b talker decode step (config 2), Q8_0, batch 1", "global_batch": 1,
+                   "seq_len": 1, "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cs.cores, "kind": "port", "sample": cs.sample_text(args.steps)},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "wall_s": wall,
+        "note": "CPU restatement of ggml's CPU quantized vec_dot (oracle/); ggml itself is absent from the reference checkout",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def make_decoder(pkg, ctx, seed):
+    """Config 2's stack with device-generated random weights (quantized on the device by b200_quantize_rows)."""
+    import torch
+
+    from oracle import stack
+
+    c = stack.CONFIGS[CONFIG]
+    d = pkg.Decoder(ctx, **c)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    sh = stack.tensor_shapes(c)
+    names = ["attn_q", "attn_k", "attn_v", "attn_o", "ffn_gate", "ffn_up", "ffn_down"]
+    for l in range(c["n_layer"]):
+        for i, n in enumerate(names):
+            t, k, rows = sh[n]
+            w = torch.randn((rows, k), generator=g, device="cuda", dtype=torch.float32) * 0.02
+            d.set_tensor(l, i, ctx.quantize_rows(t, w))
+        d.set_tensor(l, pkg.DEC_ATTN_NORM, 1.0 + 0.1 * torch.randn(c["hidden"], generator=g, device="cuda"))
+        d.set_tensor(l, pkg.DEC_FFN_NORM, 1.0 + 0.1 * torch.randn(c["hidden"], generator=g, device="cuda"))
+    t, k, rows = sh["output"]
+    d.set_tensor(0, pkg.DEC_OUTPUT, ctx.quantize_rows(t, torch.randn((rows, k), generator=g, device="cuda") * 0.02))
+    d.set_tensor(0, pkg.DEC_OUTPUT_NORM, 1.0 + 0.1 * torch.randn(c["hidden"], generator=g, device="cuda"))
+    ctx.synchronize()
+    return d, c
+
+
+def run_b200(args):
+    import torch
+
+    world, rank, local = dist_setup(args)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(local)
+
+    def barrier():
+        if dist:
+            dist.barrier()
+
+    pkg = load_package()
+    ctx = pkg.Context(local)
+    dec, c = make_decoder(pkg, ctx, seed=1234 + rank)
+    stream = ctx.torch_stream()
+    x = torch.randn(c["hidden"], generator=torch.Generator(device="cuda").manual_seed(7), device="cuda")
+    logits = torch.empty(c["n_vocab"], device="cuda")
+    torch.cuda.synchronize()
+    for _ in range(max(args.warmup, 3)):
+        dec.step_raw(x.data_ptr(), logits.data_ptr())
+    ctx.synchronize()
+
+    # ---- device-resident timing: K steps back to back on the context stream ----
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            dec.step_raw(x.data_ptr(), logits.data_ptr())
+        ev1.record(stream)
+        ev1.synchronize()
+    torch.cuda.synchronize()
+    barrier()
+    ms = ev0.elapsed_time(ev1)
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+    value = world * args.steps / (ms / 1000.0)
+
+    # ---- end to end through the public host API: pinned input in, logits out, every step ----
+    import numpy as np
+
+    xh = x.cpu().numpy()
+    out = np.empty(c["n_vocab"], dtype=np.float32)
+    for _ in range(2):
+        dec.step_host(xh, out)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record(stream)
+    for _ in range(args.steps):
+        dec.step_host(xh, out)
+    e1.record(stream)
+    e1.synchronize()
+    ems = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([ems], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ems = float(t.item())
+    e2e_value = world * args.steps / (ems / 1000.0)
+
+    wbytes = dec.weight_bytes
+    launches = dec.launches
+    peak, peak_kind = peaks()
+    achieved = wbytes / (ms_step / 1000.0) / 1e9  # GB/s of algorithmic weight bytes, per GPU
+    traffic = profile_traffic()
+    result = None
+    if rank == 0:
+        result = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8xint8->int32, f32 accumulate", "data": "synthetic",
+            "config": {"workload": "qwen3-tts-0.6b talker decode step (config 2): 28 x {q|k|v 1024->4096, o 2048->1024, "
+                                   "gate|up 1024->6144, down 3072->1024} + head 1024->3072, Q8_0, batch 1",
+                       "global_batch": world, "seq_len": 1, "parallelism": f"replicas x{world}" if world > 1 else "single",
+                       "l2": "weights 471 MB > 126 MB L2 each step (no flush needed)"},
+            "roofline": {"bound": "hbm", "kernel": "gemv_kernel<TQ8_0,1> (every launch of the step)",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6650",
+                         "algorithmic_bytes_per_step": wbytes, "launches_per_step": launches,
+                         "traffic": traffic.get("dram_bytes_per_step") if traffic else None,
+                         "traffic_source": traffic.get("source") if traffic else None},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": c["hidden"] * 4, "d2h_bytes_per_step": c["n_vocab"] * 4},
+            "gpu_launches": launches * args.steps,
+            "clocks": clk.summary(),
+        }
+    del dec
+    ctx.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        if world == 1 and not args.no_cpu:
+            v, cores, sample = cpu_sample(12.0)
+            result["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+        print(json.dumps(result), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_b200(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

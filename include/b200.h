@@ -149,6 +149,64 @@ b200_status b200_quantize_rows(b200_context * ctx, int type, const float * x, in
 b200_status b200_block_sums(b200_context * ctx, const b200_weight * w, const float * x, int32_t * sums);
 
 /* ------------------------------------------------------------------------------------------------------------
+ * Decoder step: the matmul stack of one Qwen3 decoder step for one token, as Qwen3Decoder::layers / outputs build it
+ * (src/common/qwen3-decoder.cpp:350-413, 422-438) and Qwen3Decoder::step keeps it as one graph on a GPU
+ * (:462-490): per layer RMSNorm * attn_norm -> q, k, v -> attention -> o (+ residual) -> RMSNorm * ffn_norm ->
+ * gate, up -> SwiGLU -> down (+ residual); then RMSNorm * output_norm -> head. Attention is taken at the first
+ * position of a sequence, where each query head's output is its key/value head's value row; q/k norms, RoPE and
+ * the KV cache do not change that output and stay with the rest of the ggml graph. The Qwen3-TTS talker step
+ * (src/families/qwen3-tts/talker.cpp:119-138) and the Qwen3-ASR decoder step (qwen3-asr/decoder.cpp:383-449) run
+ * this stack. Weights are set with GGUF bytes, per tensor, like ggml_backend_tensor_set.
+ * ------------------------------------------------------------------------------------------------------------ */
+typedef struct b200_decoder_shape {
+    int32_t n_layer;
+    int32_t hidden;
+    int32_t n_head;
+    int32_t n_kv_head;
+    int32_t head_dim;
+    int32_t ffn;
+    int64_t n_vocab;
+    float eps;            /* rms_norm epsilon */
+    int32_t type_attn;    /* q, k, v, o */
+    int32_t type_ffn_up;  /* gate, up */
+    int32_t type_ffn_down;
+    int32_t type_head;
+} b200_decoder_shape;
+
+enum {
+    B200_DEC_ATTN_Q = 0,
+    B200_DEC_ATTN_K = 1,
+    B200_DEC_ATTN_V = 2,
+    B200_DEC_ATTN_O = 3,
+    B200_DEC_FFN_GATE = 4,
+    B200_DEC_FFN_UP = 5,
+    B200_DEC_FFN_DOWN = 6,
+    B200_DEC_ATTN_NORM = 7,   /* float32 [hidden] */
+    B200_DEC_FFN_NORM = 8,    /* float32 [hidden] */
+    B200_DEC_OUTPUT_NORM = 9, /* float32 [hidden], layer ignored */
+    B200_DEC_OUTPUT = 10      /* head [hidden -> n_vocab], layer ignored */
+};
+
+typedef struct b200_decoder b200_decoder;
+
+b200_status b200_decoder_create(b200_context * ctx, const b200_decoder_shape * shape, b200_decoder ** out);
+void b200_decoder_destroy(b200_decoder * d);
+/* Writes bytes [offset, offset + size) of tensor `which` of `layer` (GGUF blocks for matrices, float32 for norms).
+ * on_device != 0: data is a device pointer. */
+b200_status b200_decoder_set_tensor(b200_decoder * d, int layer, int which, const void * data, int on_device, size_t offset,
+                                    size_t size);
+/* One step on device buffers: x [hidden] -> logits [n_vocab] (logits may be NULL). Asynchronous; the first call
+ * captures the step's launches in a CUDA graph, later calls replay it. */
+b200_status b200_decoder_step(b200_decoder * d, const float * x, float * logits);
+/* One step from host memory to host memory (copies in, step, copies out; synchronous). */
+b200_status b200_decoder_step_host(b200_decoder * d, const float * x_host, float * logits_host);
+/* Kernel launches of one step, and the GGUF weight bytes one step streams. */
+int64_t b200_decoder_launches(const b200_decoder * d);
+size_t b200_decoder_weight_bytes(const b200_decoder * d);
+/* Launch options: programmatic dependent launch on/off, CTAs per SM per product (0: as many as fit). */
+b200_status b200_decoder_set_launch(b200_decoder * d, int pdl, int ctas_per_sm);
+
+/* ------------------------------------------------------------------------------------------------------------
  * Host-buffer entry points (the end-to-end path a CPU caller takes: copies in, product, copy out, synchronous).
  * ------------------------------------------------------------------------------------------------------------ */
 b200_status b200_mul_mat_host(b200_context * ctx, const b200_weight * w, const float * x_host, int64_t M, float * dst_host);

@@ -29,8 +29,13 @@ EXPORTS = [
     "b200_synchronize", "b200_last_error", "b200_malloc", "b200_free", "b200_memcpy_h2d", "b200_memcpy_d2h",
     "b200_weight_nbytes", "b200_weight_alloc", "b200_weight_free", "b200_weight_set", "b200_weight_set_device",
     "b200_weight_get", "b200_mul_mat", "b200_mul_mat_rows", "b200_mul_mat_id", "b200_get_rows", "b200_quantize_rows",
-    "b200_block_sums", "b200_mul_mat_host",
+    "b200_block_sums", "b200_mul_mat_host", "b200_decoder_create", "b200_decoder_destroy", "b200_decoder_set_tensor",
+    "b200_decoder_step", "b200_decoder_step_host", "b200_decoder_launches", "b200_decoder_weight_bytes",
+    "b200_decoder_set_launch",
 ]
+
+DEC_ATTN_Q, DEC_ATTN_K, DEC_ATTN_V, DEC_ATTN_O, DEC_FFN_GATE, DEC_FFN_UP, DEC_FFN_DOWN = range(7)
+DEC_ATTN_NORM, DEC_FFN_NORM, DEC_OUTPUT_NORM, DEC_OUTPUT = 7, 8, 9, 10
 
 
 class B200Error(RuntimeError):
@@ -52,6 +57,17 @@ class Weight(ctypes.Structure):
         ("nbytes", ctypes.c_size_t),
         ("dbytes", ctypes.c_size_t),
         ("field_off", ctypes.c_int64 * 4),
+    ]
+
+
+class DecoderShape(ctypes.Structure):
+    """struct b200_decoder_shape (include/b200.h)."""
+
+    _fields_ = [
+        ("n_layer", ctypes.c_int32), ("hidden", ctypes.c_int32), ("n_head", ctypes.c_int32), ("n_kv_head", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32), ("ffn", ctypes.c_int32), ("n_vocab", ctypes.c_int64), ("eps", ctypes.c_float),
+        ("type_attn", ctypes.c_int32), ("type_ffn_up", ctypes.c_int32), ("type_ffn_down", ctypes.c_int32),
+        ("type_head", ctypes.c_int32),
     ]
 
 
@@ -103,6 +119,14 @@ def lib():
         "b200_quantize_rows": (i32, [vp, i32, vp, i64, i64, vp]),
         "b200_block_sums": (i32, [vp, W, vp, vp]),
         "b200_mul_mat_host": (i32, [vp, W, vp, i64, vp]),
+        "b200_decoder_create": (i32, [vp, ctypes.POINTER(DecoderShape), ctypes.POINTER(vp)]),
+        "b200_decoder_destroy": (None, [vp]),
+        "b200_decoder_set_tensor": (i32, [vp, i32, i32, vp, i32, sz, sz]),
+        "b200_decoder_step": (i32, [vp, vp, vp]),
+        "b200_decoder_step_host": (i32, [vp, vp, vp]),
+        "b200_decoder_launches": (i64, [vp]),
+        "b200_decoder_weight_bytes": (sz, [vp]),
+        "b200_decoder_set_launch": (i32, [vp, i32, i32]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -289,6 +313,77 @@ class Context:
         self.check(self.L.b200_mul_mat_host(self.h, ctypes.byref(w), x.ctypes.data_as(ctypes.c_void_p), x.shape[0],
                                             out.ctypes.data_as(ctypes.c_void_p)))
         return out
+
+
+class Decoder:
+    """The matmul stack of one Qwen3 decoder step (b200_decoder): Qwen3Decoder::layers / outputs for one token at a
+    sequence's first position (src/common/qwen3-decoder.cpp:350-438)."""
+
+    def __init__(self, ctx, n_layer, hidden, n_head, n_kv_head, head_dim, ffn, n_vocab, eps=1e-6, type_attn=Q8_0,
+                 type_ffn_up=Q8_0, type_ffn_down=Q8_0, type_head=Q8_0):
+        self.ctx = ctx
+        self.L = ctx.L
+        self.shape = DecoderShape(n_layer, hidden, n_head, n_kv_head, head_dim, ffn, n_vocab, eps, type_attn, type_ffn_up,
+                                  type_ffn_down, type_head)
+        h = ctypes.c_void_p()
+        ctx.check(self.L.b200_decoder_create(ctx.h, ctypes.byref(self.shape), ctypes.byref(h)))
+        self.h = h
+
+    def set_tensor(self, layer, which, data, offset=0):
+        """data: numpy (host) or a CUDA tensor; GGUF block bytes for matrices, float32 for norms."""
+        if hasattr(data, "is_cuda") and data.is_cuda:
+            n = data.numel() * data.element_size()
+            self.ctx.check(self.L.b200_decoder_set_tensor(self.h, layer, which, _ptr(data), 1, offset, n))
+        else:
+            import numpy as np
+
+            a = np.ascontiguousarray(data)
+            self.ctx.check(self.L.b200_decoder_set_tensor(self.h, layer, which, a.ctypes.data_as(ctypes.c_void_p), 0, offset,
+                                                          a.nbytes))
+
+    def step(self, x, logits=None):
+        """x: CUDA float32 [hidden]; returns CUDA float32 [n_vocab] (on the context stream, ordered after torch's)."""
+        import torch
+
+        out = torch.empty(self.shape.n_vocab, dtype=torch.float32, device=x.device) if logits is None else logits
+        self.ctx._sync_in()
+        self.ctx.check(self.L.b200_decoder_step(self.h, _ptr(x), _ptr(out)))
+        self.ctx._sync_out()
+        return out
+
+    def step_raw(self, x_ptr, logits_ptr):
+        """Enqueues one step on the context stream with no stream ordering (for timing loops)."""
+        self.ctx.check(self.L.b200_decoder_step(self.h, ctypes.c_void_p(x_ptr), ctypes.c_void_p(logits_ptr) if logits_ptr else None))
+
+    def step_host(self, x, out=None):
+        import numpy as np
+
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.empty(self.shape.n_vocab, dtype=np.float32) if out is None else out
+        self.ctx.check(self.L.b200_decoder_step_host(self.h, x.ctypes.data_as(ctypes.c_void_p), out.ctypes.data_as(ctypes.c_void_p)))
+        return out
+
+    @property
+    def launches(self):
+        return self.L.b200_decoder_launches(self.h)
+
+    @property
+    def weight_bytes(self):
+        return self.L.b200_decoder_weight_bytes(self.h)
+
+    def set_launch(self, pdl=True, ctas_per_sm=1):
+        self.ctx.check(self.L.b200_decoder_set_launch(self.h, int(bool(pdl)), ctas_per_sm))
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.L.b200_decoder_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def device_count():

@@ -12,6 +12,7 @@
 // value broadcast) and whose epilogue adds the residual. Launches carry the programmatic-serialization attribute:
 // a product's CTAs issue their weight loads before griddepcontrol.wait, overlapping the previous product's tail.
 // The whole step is captured once in a CUDA graph and replayed.
+#include <cstring>
 #include <vector>
 
 #include "internal.h"
@@ -34,6 +35,7 @@ struct b200_decoder {
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
     bool pdl = true;
+    int cap = 1;  // CTAs per SM per product: the next product's CTA fits beside the running one
     int64_t launches = 0;
 };
 
@@ -80,33 +82,33 @@ b200_status enqueue_step(b200_decoder * d) {
         a.pro = PRO_RMSNORM;
         a.norm_w = d->attn_norm[l];
         a.eps = s.eps;
-        DCK(d, launch_gemv(a, 1, 1, st, d->pdl, sms));
+        DCK(d, launch_gemv(a, 1, 1, st, d->pdl, sms, d->cap));
 
         GemvParams b = stage(d->o[l], d->qkv_out + (int64_t) (s.n_head + s.n_kv_head) * s.head_dim, d->h);
         b.pro = PRO_GQA;
         b.pro_k = s.head_dim;
         b.pro_rep = s.n_head / s.n_kv_head;
         b.res = x;
-        DCK(d, launch_gemv(b, 1, 1, st, d->pdl, sms));
+        DCK(d, launch_gemv(b, 1, 1, st, d->pdl, sms, d->cap));
 
         GemvParams c = stage(d->gu[l], d->h, d->gu_out);
         c.pro = PRO_RMSNORM;
         c.norm_w = d->ffn_norm[l];
         c.eps = s.eps;
-        DCK(d, launch_gemv(c, 1, 1, st, d->pdl, sms));
+        DCK(d, launch_gemv(c, 1, 1, st, d->pdl, sms, d->cap));
 
         GemvParams e = stage(d->down[l], d->gu_out, d->h);
         e.pro = PRO_SWIGLU;
         e.pro_k = s.ffn;
         e.res = d->h;
-        DCK(d, launch_gemv(e, 1, 1, st, d->pdl, sms));
+        DCK(d, launch_gemv(e, 1, 1, st, d->pdl, sms, d->cap));
         d->launches += 4;
     }
     GemvParams hd = stage(d->head, s.n_layer > 0 ? d->h : d->x_in, d->logits);
     hd.pro = PRO_RMSNORM;
     hd.norm_w = d->out_norm;
     hd.eps = s.eps;
-    DCK(d, launch_gemv(hd, 1, 1, st, d->pdl, sms));
+    DCK(d, launch_gemv(hd, 1, 1, st, d->pdl, sms, d->cap));
     d->launches += 1;
     return B200_OK;
 }
@@ -266,9 +268,10 @@ size_t b200_decoder_weight_bytes(const b200_decoder * d) {
     return b;
 }
 
-b200_status b200_decoder_set_pdl(b200_decoder * d, int enable) {
-    if (!d) return B200_ERR_INVALID;
-    d->pdl = enable != 0;
+b200_status b200_decoder_set_launch(b200_decoder * d, int pdl, int ctas_per_sm) {
+    if (!d || ctas_per_sm < 0) return B200_ERR_INVALID;
+    d->pdl = pdl != 0;
+    d->cap = ctas_per_sm;
     if (d->exec) {
         cudaStreamSynchronize(d->ctx->stream);
         cudaGraphExecDestroy(d->exec);

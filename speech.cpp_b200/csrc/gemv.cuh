@@ -140,16 +140,33 @@ __device__ void stage_activations(const GemvParams & p, const Act & a, int kind,
                     a.bs[(int64_t) c * (K / 16) + i] = src ? p.abs[row * (K / 16) + i] : (int16_t) 0;
         }
     } else if (kind == B200_TYPE_Q8_0) {
+        // one thread per 32-block: the shortest critical path when a step's products wait on one another
         const int64_t nb = K / 32;
-        for (int64_t i = warp; i < NC * nb; i += nwarps) {
+        for (int64_t i = threadIdx.x; i < NC * nb; i += blockDim.x) {
             const int c = (int) (i / nb);
             const int64_t b = i % nb;
-            const float v = pro_value(p, xcol[c], c, b * 32 + lane, rms);
-            float d;
-            uint16_t dh;
-            const int8_t q = quantize_q8_0_lane(v, &d, &dh);
-            a.q[(int64_t) c * K + b * 32 + lane] = q;
-            if (lane == 0) a.d[(int64_t) c * nb + b] = d;
+            const float * xc = xcol[c];
+            float v[32];
+            float amax = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 32; j++) {
+                v[j] = pro_value(p, xc, c, b * 32 + j, rms);
+                amax = fmaxf(amax, fabsf(v[j]));
+            }
+            const float d = __fdiv_rn(amax, 127.0f);
+            const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+            int packed[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                int w = 0;
+#pragma unroll
+                for (int t = 0; t < 4; t++) w |= ((int) (uint8_t) (int8_t) (int) roundf(__fmul_rn(v[4 * j + t], id))) << (8 * t);
+                packed[j] = w;
+            }
+            int4 * dst = reinterpret_cast<int4 *>(a.q + (int64_t) c * K + b * 32);
+            dst[0] = make_int4(packed[0], packed[1], packed[2], packed[3]);
+            dst[1] = make_int4(packed[4], packed[5], packed[6], packed[7]);
+            a.d[(int64_t) c * nb + b] = __half2float(__float2half_rn(d));
         }
     } else if (kind == B200_TYPE_Q8_K) {
         const int64_t nb = K / 256;
@@ -184,10 +201,16 @@ __device__ void stage_activations(const GemvParams & p, const Act & a, int kind,
 // shuffles, so every lane calls dot() for every step (invalid units contribute zero).
 // ---------------------------------------------------------------------------------------------------------------
 
+// Byte i (0..15) of a 16-byte register value, without spilling it to local memory.
+__device__ __forceinline__ int byte_of(const int4 & v, int i) {
+    const int w = i < 4 ? v.x : i < 8 ? v.y : i < 12 ? v.z : v.w;
+    return (w >> (8 * (i & 3))) & 0xFF;
+}
+
 struct TQ8_0 {
     // unit = 16 bytes of one 32-block (2 lanes per block)
     struct Unit { int4 q; uint16_t d; };
-    static constexpr int kSumsPerBlockRow = 32;  // values per int32 sum
+    static constexpr int kUnroll = 4;
     __device__ static int64_t units_per_row(int64_t K) { return K / 16; }
     __device__ static int sums_per_row(int64_t K) { return (int) (K / 32); }
     __device__ static Unit load(const WeightView & w, int64_t row, int64_t u, bool valid) {
@@ -228,6 +251,7 @@ struct TQ8_0 {
 struct TQ4_K {
     // unit = 16 bytes of qs: super-block u/8, byte chunk (u%8)*16 (8 lanes per super-block); plus the 16-byte meta
     struct Unit { int4 q; int4 m; };
+    static constexpr int kUnroll = 2;
     __device__ static int64_t units_per_row(int64_t K) { return K / 32; }  // K/2 bytes of nibbles, 16 per unit
     __device__ static int sums_per_row(int64_t K) { return (int) (2 * (K / 256)); }
     __device__ static Unit load(const WeightView & w, int64_t row, int64_t u, bool valid) {
@@ -250,20 +274,29 @@ struct TQ4_K {
             m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
         }
     }
+    // six-bit scale and min of sub-block j from the 12 scale bytes, which are bytes 4..15 of the meta value
+    __device__ static void scale_min_reg(const int4 & m, int j, int & sc, int & mn) {
+        if (j < 4) {
+            sc = byte_of(m, 4 + j) & 63;
+            mn = byte_of(m, 8 + j) & 63;
+        } else {
+            sc = (byte_of(m, 12 + j - 4) & 15) | ((byte_of(m, 4 + j - 4) >> 6) << 4);
+            mn = (byte_of(m, 12 + j - 4) >> 4) | ((byte_of(m, 8 + j - 4) >> 6) << 4);
+        }
+    }
     template <int NC>
     __device__ static void dot(const Unit & U, int64_t u, bool valid, const Act & a, float * acc, int32_t * sums) {
         const int * wq = reinterpret_cast<const int *>(&U.q);
-        const uint8_t * meta = reinterpret_cast<const uint8_t *>(&U.m);
         const int64_t sb = u / 8;
         const int j = (int) (u & 7), g = j >> 1, h = j & 1;
         const int s0 = 2 * g, s1 = 2 * g + 1;
         int sc0 = 0, m0 = 0, sc1 = 0, m1 = 0;
         if (valid) {
-            scale_min(meta + 4, s0, sc0, m0);
-            scale_min(meta + 4, s1, sc1, m1);
+            scale_min_reg(U.m, s0, sc0, m0);
+            scale_min_reg(U.m, s1, sc1, m1);
         }
-        const float dw = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t *>(meta)));
-        const float dmw = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t *>(meta + 2)));
+        const float dw = __half2float(__ushort_as_half((unsigned short) (U.m.x & 0xFFFF)));
+        const float dmw = __half2float(__ushort_as_half((unsigned short) ((unsigned) U.m.x >> 16)));
 #pragma unroll
         for (int c = 0; c < NC; c++) {
             int si = 0, sm = 0;
@@ -309,6 +342,7 @@ struct TQ6_K {
     // unit = a quarter of a super-block: half h = (u%4)/2, values l in [lq, lq+16), lq = (u%2)*16, all four t:
     // 16 bytes of ql (t = 0, 2), 16 bytes of ql (t = 1, 3), 16 bytes of qh, and the 16 scales.
     struct Unit { int4 a; int4 b; int4 h; int4 s; uint16_t d; };
+    static constexpr int kUnroll = 1;
     __device__ static int64_t units_per_row(int64_t K) { return K / 64; }
     __device__ static int sums_per_row(int64_t K) { return (int) (K / 256); }
     __device__ static Unit load(const WeightView & w, int64_t row, int64_t u, bool valid) {
@@ -334,7 +368,6 @@ struct TQ6_K {
         const int * A = reinterpret_cast<const int *>(&U.a);
         const int * B = reinterpret_cast<const int *>(&U.b);
         const int * H = reinterpret_cast<const int *>(&U.h);
-        const int8_t * sc = reinterpret_cast<const int8_t *>(&U.s);
         const int64_t sb = u / 4;
         const int j = (int) (u & 3), h = j >> 1, lh = j & 1;
         const float dw = __half2float(__ushort_as_half(U.d));
@@ -358,7 +391,7 @@ struct TQ6_K {
                     }
                     // sum (q - 32) x = sum q x - 32 sum x; sum x over these 16 values is their q8_K bsum
                     s -= 32 * (int) bs[2 * t];
-                    si += (int) sc[h * 8 + 2 * t + lh] * s;
+                    si += (int) (int8_t) byte_of(U.s, h * 8 + 2 * t + lh) * s;
                 }
             }
             si += __shfl_xor_sync(0xffffffffu, si, 1);
@@ -374,6 +407,7 @@ struct TQ6_K {
 
 struct TBF16 {
     struct Unit { int4 q; };
+    static constexpr int kUnroll = 4;
     __device__ static int64_t units_per_row(int64_t K) { return K / 8; }
     __device__ static int sums_per_row(int64_t) { return 0; }
     __device__ static Unit load(const WeightView & w, int64_t row, int64_t u, bool valid) {
@@ -407,29 +441,28 @@ struct TBF16 {
 // Without groups, CTAs split the N rows (grid.x); with groups (MUL_MAT_ID), grid.y is the expert and each CTA runs
 // that expert's routed columns in chunks of NC against its slice of the expert's rows.
 // ---------------------------------------------------------------------------------------------------------------
-constexpr int kGemvThreads = 512;
-constexpr int kGemvUnroll = 2;  // units per lane per step
+constexpr int kGemvThreads = 256;
 
 template <class T, int NC>
-__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvParams p) {
+__global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(GemvParams p) {
     extern __shared__ __align__(16) uint8_t smem[];
     const int lane = threadIdx.x & 31;
     const int64_t warps_total = (int64_t) gridDim.x * (blockDim.x >> 5);
     const int64_t gwarp = (int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int64_t upr = T::units_per_row(p.w.K);
-    const int64_t per_step = 32 * kGemvUnroll;
+    const int64_t per_step = 32 * T::kUnroll;
     const int64_t steps_per_row = (upr + per_step - 1) / per_step;
     const int64_t my_rows = gwarp < p.N ? (p.N - gwarp + warps_total - 1) / warps_total : 0;
     const int64_t my_steps = my_rows * steps_per_row;
     const bool grouped = p.grp_off != nullptr;
     int64_t row0 = p.row0;
 
-    typename T::Unit cur[kGemvUnroll], nxt[kGemvUnroll];
+    typename T::Unit cur[T::kUnroll], nxt[T::kUnroll];
     auto load_step = [&](int64_t s, typename T::Unit * dst) {
         const int64_t r = gwarp + (s / steps_per_row) * warps_total;
         const int64_t u0 = (s % steps_per_row) * per_step;
 #pragma unroll
-        for (int i = 0; i < kGemvUnroll; i++) {
+        for (int i = 0; i < T::kUnroll; i++) {
             const int64_t u = u0 + i * 32 + lane;
             dst[i] = T::load(p.w, row0 + r, u, s < my_steps && u < upr);
         }
@@ -485,7 +518,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvParams p) {
             const int64_t u0 = (s % steps_per_row) * per_step;
             int32_t * sums = p.sums ? p.sums + r * nsums : nullptr;
 #pragma unroll
-            for (int i = 0; i < kGemvUnroll; i++) {
+            for (int i = 0; i < T::kUnroll; i++) {
                 const int64_t u = u0 + i * 32 + lane;
                 T::template dot<NC>(cur[i], u, u < upr, a, acc, sums);
             }
@@ -503,7 +536,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvParams p) {
                 }
             }
 #pragma unroll
-            for (int i = 0; i < kGemvUnroll; i++) cur[i] = nxt[i];
+            for (int i = 0; i < T::kUnroll; i++) cur[i] = nxt[i];
         }
     }
 }

@@ -32,7 +32,8 @@ namespace b200 {
 WeightView view_of(const b200_weight * w);
 
 // Kernel launchers (ops.cu). Each returns the launch's cudaError_t.
-cudaError_t launch_gemv(const GemvParams & p, int nc, int grid_y, cudaStream_t st, bool pdl, int num_sms);
+// ctas_per_sm > 0 caps the grid at num_sms * ctas_per_sm CTAs (leaves room for a dependent launch's CTAs).
+cudaError_t launch_gemv(const GemvParams & p, int nc, int grid_y, cudaStream_t st, bool pdl, int num_sms, int ctas_per_sm = 0);
 int gemv_max_columns(int wtype, int64_t K);  // largest NC whose staging fits in shared memory
 cudaError_t launch_repack(int type, const b200_weight * w, const uint8_t * src, int64_t off0, int64_t n, bool to_device_layout,
                           uint8_t * gather_dst, cudaStream_t st);

@@ -240,7 +240,7 @@ cudaError_t launch_route(const int32_t * ids, int64_t T, int64_t top_k, int64_t 
 // GEMV launchers
 // ------------------------------------------------------------------------------------------------------------------
 template <class T, int NC>
-static cudaError_t launch_one(const GemvParams & p, int grid_y, cudaStream_t st, bool pdl, int num_sms) {
+static cudaError_t launch_one(const GemvParams & p, int grid_y, cudaStream_t st, bool pdl, int num_sms, int cap_per_sm) {
     auto kern = gemv_kernel<T, NC>;
     const size_t smem = act_smem_bytes(p.w.type, p.w.K, NC);
     static int configured_smem = 0;  // per instantiation
@@ -259,7 +259,8 @@ static cudaError_t launch_one(const GemvParams & p, int grid_y, cudaStream_t st,
     }
     const int warps_per_cta = kGemvThreads / 32;
     int64_t gx = (p.N + warps_per_cta - 1) / warps_per_cta;
-    const int64_t cap = grid_y > 1 ? gx : (int64_t) num_sms * ctas_per_sm;
+    const int per_sm = cap_per_sm > 0 && cap_per_sm < ctas_per_sm ? cap_per_sm : ctas_per_sm;
+    const int64_t cap = grid_y > 1 ? gx : (int64_t) num_sms * per_sm;
     if (gx > cap) gx = cap;
     if (gx < 1) gx = 1;
     cudaLaunchConfig_t cfg = {};
@@ -276,23 +277,23 @@ static cudaError_t launch_one(const GemvParams & p, int grid_y, cudaStream_t st,
 }
 
 template <class T>
-static cudaError_t launch_nc(const GemvParams & p, int nc, int grid_y, cudaStream_t st, bool pdl, int num_sms) {
+static cudaError_t launch_nc(const GemvParams & p, int nc, int grid_y, cudaStream_t st, bool pdl, int num_sms, int cap) {
     switch (nc) {
-    case 1: return launch_one<T, 1>(p, grid_y, st, pdl, num_sms);
-    case 2: return launch_one<T, 2>(p, grid_y, st, pdl, num_sms);
-    case 4: return launch_one<T, 4>(p, grid_y, st, pdl, num_sms);
-    case 8: return launch_one<T, 8>(p, grid_y, st, pdl, num_sms);
-    case 16: return launch_one<T, 16>(p, grid_y, st, pdl, num_sms);
+    case 1: return launch_one<T, 1>(p, grid_y, st, pdl, num_sms, cap);
+    case 2: return launch_one<T, 2>(p, grid_y, st, pdl, num_sms, cap);
+    case 4: return launch_one<T, 4>(p, grid_y, st, pdl, num_sms, cap);
+    case 8: return launch_one<T, 8>(p, grid_y, st, pdl, num_sms, cap);
+    case 16: return launch_one<T, 16>(p, grid_y, st, pdl, num_sms, cap);
     default: return cudaErrorInvalidValue;
     }
 }
 
-cudaError_t launch_gemv(const GemvParams & p, int nc, int grid_y, cudaStream_t st, bool pdl, int num_sms) {
+cudaError_t launch_gemv(const GemvParams & p, int nc, int grid_y, cudaStream_t st, bool pdl, int num_sms, int ctas_per_sm) {
     switch (p.w.type) {
-    case B200_TYPE_Q8_0: return launch_nc<TQ8_0>(p, nc, grid_y, st, pdl, num_sms);
-    case B200_TYPE_Q4_K: return launch_nc<TQ4_K>(p, nc, grid_y, st, pdl, num_sms);
-    case B200_TYPE_Q6_K: return launch_nc<TQ6_K>(p, nc, grid_y, st, pdl, num_sms);
-    case B200_TYPE_BF16: return launch_nc<TBF16>(p, nc, grid_y, st, pdl, num_sms);
+    case B200_TYPE_Q8_0: return launch_nc<TQ8_0>(p, nc, grid_y, st, pdl, num_sms, ctas_per_sm);
+    case B200_TYPE_Q4_K: return launch_nc<TQ4_K>(p, nc, grid_y, st, pdl, num_sms, ctas_per_sm);
+    case B200_TYPE_Q6_K: return launch_nc<TQ6_K>(p, nc, grid_y, st, pdl, num_sms, ctas_per_sm);
+    case B200_TYPE_BF16: return launch_nc<TBF16>(p, nc, grid_y, st, pdl, num_sms, ctas_per_sm);
     default: return cudaErrorInvalidValue;
     }
 }
