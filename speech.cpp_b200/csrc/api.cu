@@ -103,11 +103,12 @@ bool check_weight(b200_context * ctx, const b200_weight * w) {
            w->ne0 % block_values(w->type) == 0;
 }
 
-GemvParams base_params(const b200_weight * w) {
+GemvParams base_params(b200_context * ctx, const b200_weight * w) {
     GemvParams p;
     std::memset(&p, 0, sizeof p);
     p.w = view_of(w);
     p.eps = 0.0f;
+    p.err = ctx->dev_err;
     return p;
 }
 
@@ -126,7 +127,7 @@ b200_status mul_mat_impl(b200_context * ctx, const b200_weight * w, int64_t row0
         return fail(ctx, B200_ERR_INVALID, "mul_mat: bad shape");
     if (M == 0 || n == 0) return B200_OK;
     const int64_t K = w->ne0;
-    GemvParams p = base_params(w);
+    GemvParams p = base_params(ctx, w);
     p.N = n;
     p.row0 = row0;
     p.x = x;
@@ -411,7 +412,7 @@ b200_status b200_mul_mat_id(b200_context * ctx, const b200_weight * experts, con
     int32_t * grp_off = c.take<int32_t>((size_t) E + 1);
     int32_t * col_src = c.take<int32_t>((size_t) P);
     int32_t * col_dst = c.take<int32_t>((size_t) P);
-    GemvParams p = base_params(experts);
+    GemvParams p = base_params(ctx, experts);
     if (kind != B200_TYPE_BF16) {
         int8_t * q = c.take<int8_t>((size_t) T * nb1 * K);
         float * d = c.take<float>((size_t) T * nb1 * (K / (kind == B200_TYPE_Q8_0 ? 32 : 256)));
@@ -455,7 +456,7 @@ b200_status b200_block_sums(b200_context * ctx, const b200_weight * w, const flo
     if (!check_weight(ctx, w) || !x || !sums) return fail(ctx, B200_ERR_INVALID, "block_sums: bad arguments");
     if (w->type != B200_TYPE_Q8_0 && w->type != B200_TYPE_Q4_K && w->type != B200_TYPE_Q6_K)
         return fail(ctx, B200_ERR_UNSUPPORTED, "block_sums: integer types only");
-    GemvParams p = base_params(w);
+    GemvParams p = base_params(ctx, w);
     p.N = w->ne1 * w->ne2;
     p.x = x;
     p.ldx = w->ne0;

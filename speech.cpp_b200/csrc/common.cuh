@@ -67,6 +67,53 @@ __host__ __device__ inline int64_t align256(int64_t v) { return (v + 255) & ~(in
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 
+// ------------------------------------------------------------------------------------------------------------------
+// mbarriers and bulk (TMA) copies, global -> shared, no multicast. Waits are bounded: after kSpinLimit polls a wait
+// gives up and reports false, so no kernel can hang on a copy that never lands.
+// ------------------------------------------------------------------------------------------------------------------
+constexpr uint32_t kSpinLimit = 1u << 26;
+
+__device__ __forceinline__ uint32_t smem_addr(const void * p) { return (uint32_t) __cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t * bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t * bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t * bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+// Waits for the phase with the given parity to complete; false if it did not within kSpinLimit polls.
+__device__ __forceinline__ bool mbar_wait(uint64_t * bar, uint32_t parity) {
+    const uint32_t a = smem_addr(bar);
+    for (uint32_t i = 0; i < kSpinLimit; i++) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(a), "r"(parity)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
+// One bulk copy of `bytes` (multiple of 16; both addresses 16-byte aligned) from global to this CTA's shared memory,
+// completing `bytes` of the barrier's transaction count.
+__device__ __forceinline__ void bulk_g2s(void * dst, const void * src, uint32_t bytes, uint64_t * bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_addr(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_addr(bar))
+                 : "memory");
+}
+
 // 128-bit streaming load of weight bytes: read once, do not keep in L1.
 __device__ __forceinline__ int4 ld_stream(const void * p) {
     int4 r;

@@ -57,9 +57,10 @@ b200_status dfail(b200_decoder * d, b200_status s, const char * what) {
 
 int64_t qkv_rows(const b200_decoder_shape & s) { return (int64_t) (s.n_head + 2 * s.n_kv_head) * s.head_dim; }
 
-GemvParams stage(const b200_weight & w, const float * x, float * y) {
+GemvParams stage(const b200_decoder * d, const b200_weight & w, const float * x, float * y) {
     GemvParams p;
     std::memset(&p, 0, sizeof p);
+    p.err = d->ctx->dev_err;
     p.w = view_of(&w);
     p.N = w.ne1;
     p.x = x;
@@ -78,33 +79,33 @@ b200_status enqueue_step(b200_decoder * d) {
     d->launches = 0;
     for (int l = 0; l < s.n_layer; l++) {
         const float * x = l == 0 ? d->x_in : d->h;
-        GemvParams a = stage(d->qkv[l], x, d->qkv_out);
+        GemvParams a = stage(d, d->qkv[l], x, d->qkv_out);
         a.pro = PRO_RMSNORM;
         a.norm_w = d->attn_norm[l];
         a.eps = s.eps;
         DCK(d, launch_gemv(a, 1, 1, st, d->pdl, sms, d->cap));
 
-        GemvParams b = stage(d->o[l], d->qkv_out + (int64_t) (s.n_head + s.n_kv_head) * s.head_dim, d->h);
+        GemvParams b = stage(d, d->o[l], d->qkv_out + (int64_t) (s.n_head + s.n_kv_head) * s.head_dim, d->h);
         b.pro = PRO_GQA;
         b.pro_k = s.head_dim;
         b.pro_rep = s.n_head / s.n_kv_head;
         b.res = x;
         DCK(d, launch_gemv(b, 1, 1, st, d->pdl, sms, d->cap));
 
-        GemvParams c = stage(d->gu[l], d->h, d->gu_out);
+        GemvParams c = stage(d, d->gu[l], d->h, d->gu_out);
         c.pro = PRO_RMSNORM;
         c.norm_w = d->ffn_norm[l];
         c.eps = s.eps;
         DCK(d, launch_gemv(c, 1, 1, st, d->pdl, sms, d->cap));
 
-        GemvParams e = stage(d->down[l], d->gu_out, d->h);
+        GemvParams e = stage(d, d->down[l], d->gu_out, d->h);
         e.pro = PRO_SWIGLU;
         e.pro_k = s.ffn;
         e.res = d->h;
         DCK(d, launch_gemv(e, 1, 1, st, d->pdl, sms, d->cap));
         d->launches += 4;
     }
-    GemvParams hd = stage(d->head, s.n_layer > 0 ? d->h : d->x_in, d->logits);
+    GemvParams hd = stage(d, d->head, s.n_layer > 0 ? d->h : d->x_in, d->logits);
     hd.pro = PRO_RMSNORM;
     hd.norm_w = d->out_norm;
     hd.eps = s.eps;

@@ -41,6 +41,10 @@ struct GemvParams {
     const float * res;
     int64_t ldres;
     int32_t * sums;  // when set: int32 (sub-)block sums of column 0, [N][sums_per_row], instead of y
+    unsigned * err;  // device error word (bounded waits that give up set B200 timeout bits here)
+    int rows_per_cta;     // TMA path: contiguous rows of one CTA
+    int rows_per_stage;   // TMA path: rows per ring stage
+    int stages;           // TMA path: ring stages
     int ncols;                // activation columns (without groups)
     const int32_t * col_src;  // optional: column c reads x row col_src[c]
     const int32_t * col_dst;  // optional: column c writes y (and reads res) row col_dst[c]
@@ -66,14 +70,25 @@ inline __host__ __device__ int act_kind(int wtype) {
     return wtype == B200_TYPE_Q8_0 ? B200_TYPE_Q8_0 : wtype == B200_TYPE_BF16 ? B200_TYPE_BF16 : B200_TYPE_Q8_K;
 }
 
-inline __host__ __device__ size_t act_smem_bytes(int wtype, int64_t K, int nc) {
+// The single-column path (a decode step's products) first copies its raw input rows into shared memory with
+// coalesced 128-bit loads (up to 2K floats of input and K floats of norm weights), so that the prologue and the
+// quantization read shared memory instead of waiting on global loads one after another.
+inline __host__ __device__ bool single_fast(int64_t K) { return K % 32 == 0 && K * 13 + 4096 <= 180 * 1024; }
+
+inline __host__ __device__ size_t act_base_bytes(int wtype, int64_t K, int nc) {
     const int kind = act_kind(wtype);
-    if (kind == B200_TYPE_BF16) return (size_t) nc * K * 2 + 64;
+    if (kind == B200_TYPE_BF16) return (((size_t) nc * K * 2) + 15) & ~(size_t) 15;
     size_t s = (size_t) nc * K;                                   // q
     s = (s + 15) & ~(size_t) 15;
     if (kind == B200_TYPE_Q8_0) s += (size_t) nc * (K / 32) * 4;  // d
     else s += (size_t) nc * (K / 256) * 4 + (size_t) nc * (K / 16) * 2;
-    return s + 64 + 16 * 8;                                       // + rms scales
+    return (s + 15) & ~(size_t) 15;
+}
+
+inline __host__ __device__ size_t act_smem_bytes(int wtype, int64_t K, int nc) {
+    size_t s = act_base_bytes(wtype, K, nc);
+    if (nc == 1 && single_fast(K)) s += (size_t) 12 * K;  // xs [2K] + ws [K]
+    return s + 64;
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -97,14 +112,114 @@ __device__ __forceinline__ const float * column_src(const GemvParams & p, int64_
     return p.x + (p.col_src ? (int64_t) p.col_src[c] : c) * p.ldx;
 }
 
+// Single-column staging (nc == 1, no prequantized rows, single_fast(K)). Block-wide; ends with __syncthreads.
+// Arithmetic is that of the general path below (and of the CPU oracle), value by value.
+// Barrier over the first nthr threads of the CTA (all of them: __syncthreads; fewer: named barrier 1).
+__device__ __forceinline__ void sync_threads(int nthr) {
+    if (nthr == (int) blockDim.x) __syncthreads();
+    else asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
+}
+
+__device__ __forceinline__ void stage_one(const GemvParams & p, const Act & a, int kind, const float * xc, float * xs, float * ws,
+                                          int nthr) {
+    __shared__ float part[32];
+    __shared__ float rms;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = nthr >> 5;
+    const int K = (int) a.K;
+    const int hd = (int) p.pro_k, rep = p.pro_rep;
+    // raw input -> xs; norm weights -> ws
+    const int lin = p.pro == PRO_GQA ? K / rep : K;
+    auto copy = [&](float * dst, const float * src, int n) {
+        if ((((uintptr_t) src) & 15) == 0 && (n & 3) == 0) {
+            const float4 * s4 = reinterpret_cast<const float4 *>(src);
+            float4 * d4 = reinterpret_cast<float4 *>(dst);
+            for (int i = tid; i < n / 4; i += nthr) d4[i] = s4[i];
+        } else {
+            for (int i = tid; i < n; i += nthr) dst[i] = src[i];
+        }
+    };
+    copy(xs, xc, lin);
+    if (p.pro == PRO_SWIGLU) copy(xs + K, xc + p.pro_k, K);
+    if (p.pro == PRO_RMSNORM) copy(ws, p.norm_w, K);
+    sync_threads(nthr);
+    if (p.pro == PRO_RMSNORM) {
+        float sq = 0.0f;
+        for (int k = tid; k < K; k += nthr) sq = fmaf(xs[k], xs[k], sq);
+        sq = warp_sum(sq);
+        if (lane == 0) part[warp] = sq;
+        sync_threads(nthr);
+        if (warp == 0) {
+            float t = lane < nwarps ? part[lane] : 0.0f;
+            t = warp_sum(t);
+            if (lane == 0) rms = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(t, (float) K), p.eps)));
+        }
+        sync_threads(nthr);
+    }
+    auto value = [&](int k) -> float {
+        switch (p.pro) {
+        case PRO_RMSNORM: return __fmul_rn(__fmul_rn(xs[k], rms), ws[k]);
+        case PRO_SWIGLU: return __fmul_rn(silu(xs[k]), xs[K + k]);
+        case PRO_GQA: return xs[(k / (hd * rep)) * hd + k % hd];
+        default: return xs[k];
+        }
+    };
+    if (kind == B200_TYPE_Q8_0) {
+        // 8 threads per 32-block, 4 values each; the loop bound is uniform per warp so shuffles see all lanes
+        const int nb = K / 32;
+        for (int base = warp * 4; base < nb; base += nwarps * 4) {
+            const int b = base + (lane >> 3), j = lane & 7;
+            const bool on = b < nb;
+            float v[4];
+            float amax = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                v[i] = on ? value(b * 32 + 4 * j + i) : 0.0f;
+                amax = fmaxf(amax, fabsf(v[i]));
+            }
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+            if (on) {
+                const float d = __fdiv_rn(amax, 127.0f);
+                const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+                int w = 0;
+#pragma unroll
+                for (int i = 0; i < 4; i++) w |= ((int) (uint8_t) (int8_t) (int) roundf(__fmul_rn(v[i], id))) << (8 * i);
+                reinterpret_cast<int *>(a.q)[b * 8 + j] = w;
+                if (j == 0) a.d[b] = __half2float(__float2half_rn(d));
+            }
+        }
+    } else if (kind == B200_TYPE_Q8_K) {
+        const int nb = K / 256;
+        for (int b = warp; b < nb; b += nwarps) {
+            float v[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) v[i] = value(b * 256 + lane * 8 + i);
+            int8_t q[8];
+            int16_t bsum;
+            float d;
+            quantize_q8_K_warp(v, q, &bsum, &d);
+            int2 packed;
+            packed.x = (int) (uint8_t) q[0] | ((int) (uint8_t) q[1] << 8) | ((int) (uint8_t) q[2] << 16) | ((int) (uint8_t) q[3] << 24);
+            packed.y = (int) (uint8_t) q[4] | ((int) (uint8_t) q[5] << 8) | ((int) (uint8_t) q[6] << 16) | ((int) (uint8_t) q[7] << 24);
+            *reinterpret_cast<int2 *>(a.q + b * 256 + lane * 8) = packed;
+            if ((lane & 1) == 0) a.bs[b * 16 + lane / 2] = bsum;
+            if (lane == 0) a.d[b] = d;
+        }
+    } else {
+        for (int k = tid; k < K; k += nthr) a.b[k] = __float2bfloat16_rn(value(k));
+    }
+    sync_threads(nthr);
+}
+
 // Stages columns c0 .. c0+nc-1 (nc <= NC; the rest are zeros). Block-wide; ends with __syncthreads.
 template <int NC>
-__device__ void stage_activations(const GemvParams & p, const Act & a, int kind, int64_t c0, int nc) {
+__device__ void stage_activations(const GemvParams & p, const Act & a, int kind, int64_t c0, int nc, int nthr) {
     __shared__ float rms[NC];
     __shared__ const float * xcol[NC];
     if (threadIdx.x < NC) xcol[threadIdx.x] = (int) threadIdx.x < nc ? column_src(p, c0 + threadIdx.x) : nullptr;
-    __syncthreads();
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    sync_threads(nthr);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = nthr >> 5;
     const int64_t K = a.K;
     if (p.pro == PRO_RMSNORM) {
         __shared__ float part[NC][32];
@@ -112,11 +227,11 @@ __device__ void stage_activations(const GemvParams & p, const Act & a, int kind,
             const float * xc = xcol[c];
             float s = 0.0f;
             if (xc)
-                for (int64_t k = threadIdx.x; k < K; k += blockDim.x) s = fmaf(xc[k], xc[k], s);
+                for (int64_t k = threadIdx.x; k < K; k += nthr) s = fmaf(xc[k], xc[k], s);
             s = warp_sum(s);
             if (lane == 0) part[c][warp] = s;
         }
-        __syncthreads();
+        sync_threads(nthr);
         if (warp == 0) {
             for (int c = 0; c < NC; c++) {
                 float s = lane < nwarps ? part[c][lane] : 0.0f;
@@ -124,7 +239,7 @@ __device__ void stage_activations(const GemvParams & p, const Act & a, int kind,
                 if (lane == 0) rms[c] = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(s, (float) K), p.eps)));
             }
         }
-        __syncthreads();
+        sync_threads(nthr);
     }
     if (p.aq) {
         // prequantized rows: copy into shared memory
@@ -132,17 +247,17 @@ __device__ void stage_activations(const GemvParams & p, const Act & a, int kind,
             const int64_t row = c < nc ? (p.col_src ? (int64_t) p.col_src[c0 + c] : c0 + c) : -1;
             const int4 * src = row >= 0 ? reinterpret_cast<const int4 *>(p.aq + row * K) : nullptr;
             int4 * dst = reinterpret_cast<int4 *>(a.q + (int64_t) c * K);
-            for (int64_t i = threadIdx.x; i < K / 16; i += blockDim.x) dst[i] = src ? src[i] : make_int4(0, 0, 0, 0);
+            for (int64_t i = threadIdx.x; i < K / 16; i += nthr) dst[i] = src ? src[i] : make_int4(0, 0, 0, 0);
             const int64_t nd = kind == B200_TYPE_Q8_0 ? K / 32 : K / 256;
-            for (int64_t i = threadIdx.x; i < nd; i += blockDim.x) a.d[(int64_t) c * nd + i] = src ? p.ad[row * nd + i] : 0.0f;
+            for (int64_t i = threadIdx.x; i < nd; i += nthr) a.d[(int64_t) c * nd + i] = src ? p.ad[row * nd + i] : 0.0f;
             if (kind == B200_TYPE_Q8_K)
-                for (int64_t i = threadIdx.x; i < K / 16; i += blockDim.x)
+                for (int64_t i = threadIdx.x; i < K / 16; i += nthr)
                     a.bs[(int64_t) c * (K / 16) + i] = src ? p.abs[row * (K / 16) + i] : (int16_t) 0;
         }
     } else if (kind == B200_TYPE_Q8_0) {
         // one thread per 32-block: the shortest critical path when a step's products wait on one another
         const int64_t nb = K / 32;
-        for (int64_t i = threadIdx.x; i < NC * nb; i += blockDim.x) {
+        for (int64_t i = threadIdx.x; i < NC * nb; i += nthr) {
             const int c = (int) (i / nb);
             const int64_t b = i % nb;
             const float * xc = xcol[c];
@@ -188,12 +303,12 @@ __device__ void stage_activations(const GemvParams & p, const Act & a, int kind,
             if (lane == 0) a.d[(int64_t) c * nb + b] = d;
         }
     } else {
-        for (int64_t i = threadIdx.x; i < NC * K; i += blockDim.x) {
+        for (int64_t i = threadIdx.x; i < NC * K; i += nthr) {
             const int c = (int) (i / K);
             a.b[i] = __float2bfloat16_rn(pro_value(p, xcol[c], c, i % K, rms));
         }
     }
-    __syncthreads();
+    sync_threads(nthr);
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -222,6 +337,15 @@ struct TQ8_0 {
             r.q = make_int4(0, 0, 0, 0);
             r.d = 0;
         }
+        return r;
+    }
+    // shared-memory staging of rows (TMA path): field 0 = qs [rows][K], field 1 = d [rows][K/32]
+    static constexpr int kFields = 2;
+    __host__ __device__ static int64_t field_row_bytes(int64_t K, int i) { return i == 0 ? K : i == 1 ? K / 16 : 0; }
+    __device__ static Unit load_s(const uint8_t * const * f, int64_t K, int64_t row, int64_t u) {
+        Unit r;
+        r.q = *reinterpret_cast<const int4 *>(f[0] + row * K + u * 16);
+        r.d = (u & 1) ? 0 : reinterpret_cast<const uint16_t *>(f[1])[row * (K / 32) + u / 2];
         return r;
     }
     template <int NC>
@@ -273,6 +397,14 @@ struct TQ4_K {
             sc = (s[j + 4] & 15) | ((s[j - 4] >> 6) << 4);
             m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
         }
+    }
+    static constexpr int kFields = 2;  // qs [rows][K/2], meta [rows][K/256][16]
+    __host__ __device__ static int64_t field_row_bytes(int64_t K, int i) { return i == 0 ? K / 2 : i == 1 ? K / 16 : 0; }
+    __device__ static Unit load_s(const uint8_t * const * f, int64_t K, int64_t row, int64_t u) {
+        Unit r;
+        r.q = *reinterpret_cast<const int4 *>(f[0] + row * (K / 2) + u * 16);
+        r.m = *reinterpret_cast<const int4 *>(f[1] + (row * (K / 256) + u / 8) * 16);
+        return r;
     }
     // six-bit scale and min of sub-block j from the 12 scale bytes, which are bytes 4..15 of the meta value
     __device__ static void scale_min_reg(const int4 & m, int j, int & sc, int & mn) {
@@ -363,6 +495,22 @@ struct TQ6_K {
         }
         return r;
     }
+    static constexpr int kFields = 4;  // ql [rows][K/2], qh [rows][K/4], sc [rows][K/256][16], d [rows][K/256]
+    __host__ __device__ static int64_t field_row_bytes(int64_t K, int i) {
+        return i == 0 ? K / 2 : i == 1 ? K / 4 : i == 2 ? K / 16 : K / 128;
+    }
+    __device__ static Unit load_s(const uint8_t * const * f, int64_t K, int64_t row, int64_t u) {
+        Unit r;
+        const int64_t sb = u / 4, nsb = K / 256;
+        const int j = (int) (u & 3), h = j >> 1, lq = (j & 1) * 16;
+        const uint8_t * ql = f[0] + row * (K / 2) + sb * 128 + h * 64 + lq;
+        r.a = *reinterpret_cast<const int4 *>(ql);
+        r.b = *reinterpret_cast<const int4 *>(ql + 32);
+        r.h = *reinterpret_cast<const int4 *>(f[1] + row * (K / 4) + sb * 64 + h * 32 + lq);
+        r.s = *reinterpret_cast<const int4 *>(f[2] + (row * nsb + sb) * 16);
+        r.d = reinterpret_cast<const uint16_t *>(f[3])[row * nsb + sb];
+        return r;
+    }
     template <int NC>
     __device__ static void dot(const Unit & U, int64_t u, bool valid, const Act & a, float * acc, int32_t * sums) {
         const int * A = reinterpret_cast<const int *>(&U.a);
@@ -413,6 +561,13 @@ struct TBF16 {
     __device__ static Unit load(const WeightView & w, int64_t row, int64_t u, bool valid) {
         Unit r;
         r.q = valid ? ld_stream(w.f0 + (row * w.K + u * 8) * 2) : make_int4(0, 0, 0, 0);
+        return r;
+    }
+    static constexpr int kFields = 1;  // w [rows][K] bf16
+    __host__ __device__ static int64_t field_row_bytes(int64_t K, int i) { return i == 0 ? 2 * K : 0; }
+    __device__ static Unit load_s(const uint8_t * const * f, int64_t K, int64_t row, int64_t u) {
+        Unit r;
+        r.q = *reinterpret_cast<const int4 *>(f[0] + (row * K + u * 8) * 2);
         return r;
     }
     template <int NC>
@@ -499,6 +654,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(GemvParams p) {
             }
         }
     }
+    float * xs = reinterpret_cast<float *>(smem + act_base_bytes(p.w.type, p.w.K, NC));
     const int nsums = T::sums_per_row(p.w.K);
 
     for (int64_t c0 = cbeg; c0 < cend; c0 += NC) {
@@ -507,7 +663,11 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(GemvParams p) {
             __syncthreads();  // the previous chunk's staging is no longer read
             load_step(0, cur);
         }
-        stage_activations<NC>(p, a, kind, c0, nc);
+        if (NC == 1 && !p.aq && single_fast(a.K)) {
+            stage_one(p, a, kind, nc > 0 ? column_src(p, c0) : p.x, xs, xs + 2 * a.K, blockDim.x);
+        } else {
+            stage_activations<NC>(p, a, kind, c0, nc, blockDim.x);
+        }
 
         float acc[NC];
 #pragma unroll

@@ -9,6 +9,7 @@
 //  - route: MUL_MAT_ID's router sort (src/families/drama3/text-model.cpp:208-210): (token, slot) pairs grouped by
 //    expert with a shared-memory histogram and scan, so each expert's rows stream once over all of its pairs.
 #include "internal.h"
+#include "gemv_tma.cuh"
 
 namespace b200 {
 
@@ -276,14 +277,71 @@ static cudaError_t launch_one(const GemvParams & p, int grid_y, cudaStream_t st,
     return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
+// TMA-streamed launch (gemv_tma.cuh): grid and ring geometry.
+template <class T, int NC>
+static cudaError_t launch_tma(const GemvParams & p0, cudaStream_t st, bool pdl, int num_sms, int cap_per_sm) {
+    auto kern = gemv_tma_kernel<T, NC>;
+    GemvParams p = p0;
+    const int64_t K = p.w.K;
+    const int64_t row_bytes = tma_row_bytes<T>(K);
+    const int per_sm = cap_per_sm > 0 ? (cap_per_sm < 2 ? cap_per_sm : 2) : 2;
+    int64_t gx = (int64_t) num_sms * per_sm;
+    if (gx > p.N) gx = p.N;
+    if (gx < 1) gx = 1;
+    int64_t rpc = (p.N + gx - 1) / gx;
+    gx = (p.N + rpc - 1) / rpc;
+    const int64_t target = 16 * 1024, ring_budget = 96 * 1024;
+    int64_t rps = target / row_bytes;
+    if (rps < 1) rps = 1;
+    if (rps > rpc) rps = rpc;
+    int64_t stages = ring_budget / (rps * row_bytes);
+    const int64_t chunks = (rpc + rps - 1) / rps;
+    if (stages > chunks) stages = chunks;
+    if (stages < 1) stages = 1;
+    if (stages > 8) stages = 8;
+    p.rows_per_cta = (int) rpc;
+    p.rows_per_stage = (int) rps;
+    p.stages = (int) stages;
+    const size_t smem = tma_smem_bytes<T, NC>(p.w.type, K, (int) rps, (int) stages);
+    if (smem > 220 * 1024) return cudaErrorInvalidValue;
+    static int configured = 0;
+    if ((int) smem > configured) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+        if (e != cudaSuccess) return e;
+        configured = 220 * 1024;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned) gx, 1, 1);
+    cfg.blockDim = dim3(kTmaThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
+template <class T, int NC>
+static cudaError_t launch_pick(const GemvParams & p, int grid_y, cudaStream_t st, bool pdl, int num_sms, int cap) {
+    // the TMA path needs whole 16-byte field rows, no expert groups, and its geometry must fit shared memory
+    if (p.grp_off == nullptr && grid_y == 1 && p.err && tma_fits<T>(p.w.K) && tma_row_bytes<T>(p.w.K) <= 64 * 1024 &&
+        p.ncols <= NC) {
+        const cudaError_t e = launch_tma<T, NC>(p, st, pdl, num_sms, cap);
+        if (e != cudaErrorInvalidValue) return e;
+    }
+    return launch_one<T, NC>(p, grid_y, st, pdl, num_sms, cap);
+}
+
 template <class T>
 static cudaError_t launch_nc(const GemvParams & p, int nc, int grid_y, cudaStream_t st, bool pdl, int num_sms, int cap) {
     switch (nc) {
-    case 1: return launch_one<T, 1>(p, grid_y, st, pdl, num_sms, cap);
-    case 2: return launch_one<T, 2>(p, grid_y, st, pdl, num_sms, cap);
-    case 4: return launch_one<T, 4>(p, grid_y, st, pdl, num_sms, cap);
-    case 8: return launch_one<T, 8>(p, grid_y, st, pdl, num_sms, cap);
-    case 16: return launch_one<T, 16>(p, grid_y, st, pdl, num_sms, cap);
+    case 1: return launch_pick<T, 1>(p, grid_y, st, pdl, num_sms, cap);
+    case 2: return launch_pick<T, 2>(p, grid_y, st, pdl, num_sms, cap);
+    case 4: return launch_pick<T, 4>(p, grid_y, st, pdl, num_sms, cap);
+    case 8: return launch_pick<T, 8>(p, grid_y, st, pdl, num_sms, cap);
+    case 16: return launch_pick<T, 16>(p, grid_y, st, pdl, num_sms, cap);
     default: return cudaErrorInvalidValue;
     }
 }

@@ -114,6 +114,9 @@ SHAPES = [
     (BF16, 1024, 100, 1),
     (BF16, 64, 7, 4),
     (BF16, 512, 64, 24),
+    (Q6_K, 2048, 40000, 1),   # the TMA ring wraps many times per CTA
+    (Q8_0, 1024, 50000, 2),
+    (Q4_K, 4096, 20000, 3),
 ]
 
 
