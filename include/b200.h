@@ -211,6 +211,22 @@ b200_status b200_decoder_set_launch(b200_decoder * d, int pdl, int ctas_per_sm);
  * ------------------------------------------------------------------------------------------------------------ */
 b200_status b200_mul_mat_host(b200_context * ctx, const b200_weight * w, const float * x_host, int64_t M, float * dst_host);
 
+/* ------------------------------------------------------------------------------------------------------------
+ * MUL_MAT_ID without allocation. No counterpart in the reference: speech.cpp's ggml backends allocate their scratch
+ * themselves. This entry point is for callers that cannot call cudaMalloc — a serving runtime that owns all device
+ * memory through its own arena, a latency-critical path where an allocation could synchronize the device, a process
+ * whose weights already fill the GPU. It computes exactly what b200_mul_mat_id computes (same kernels, same
+ * results) on `stream` (a cudaStream_t of the current device, which must be the experts' device), with its scratch in
+ * a static device array of B200_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds until exit. The
+ * first call on a device looks up that array's device address (cudaGetSymbolAddress); make it before any stream
+ * capture. A call needs about T*nb1*K bytes of quantized activations plus 8*T*top_k + 4*E bytes of routing tables;
+ * a call that needs more than the array returns B200_ERR_INVALID. Calls share the array: two calls that overlap on
+ * the GPU race. Ids outside [0, E) are skipped (their dst rows are left unchanged) and not reported.
+ * ------------------------------------------------------------------------------------------------------------ */
+#define B200_NOALLOC_SCRATCH_BYTES (16u << 20)
+b200_status b200_mul_mat_id_noalloc(void * stream, const b200_weight * experts, const float * b, int64_t nb1,
+                                    const int32_t * ids, int64_t top_k, int64_t T, float * dst);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

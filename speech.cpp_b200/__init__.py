@@ -31,7 +31,7 @@ EXPORTS = [
     "b200_weight_get", "b200_mul_mat", "b200_mul_mat_rows", "b200_mul_mat_id", "b200_get_rows", "b200_quantize_rows",
     "b200_block_sums", "b200_mul_mat_host", "b200_decoder_create", "b200_decoder_destroy", "b200_decoder_set_tensor",
     "b200_decoder_step", "b200_decoder_step_host", "b200_decoder_launches", "b200_decoder_weight_bytes",
-    "b200_decoder_set_launch",
+    "b200_decoder_set_launch", "b200_mul_mat_id_noalloc",
 ]
 
 DEC_ATTN_Q, DEC_ATTN_K, DEC_ATTN_V, DEC_ATTN_O, DEC_FFN_GATE, DEC_FFN_UP, DEC_FFN_DOWN = range(7)
@@ -127,6 +127,7 @@ def lib():
         "b200_decoder_launches": (i64, [vp]),
         "b200_decoder_weight_bytes": (sz, [vp]),
         "b200_decoder_set_launch": (i32, [vp, i32, i32]),
+        "b200_mul_mat_id_noalloc": (i32, [vp, W, vp, i64, vp, i64, i64, vp]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)

@@ -167,6 +167,8 @@ b200_status mul_mat_impl(b200_context * ctx, const b200_weight * w, int64_t row0
 
 namespace b200 {
 
+void set_thread_error(const char * what) { g_error = what; }
+
 WeightView view_of(const b200_weight * w) {
     WeightView v;
     v.type = w->type;

@@ -3,6 +3,7 @@
 
 #include <cuda_runtime.h>
 
+#include <cstring>
 #include <string>
 
 #include "../../include/b200.h"
@@ -30,6 +31,8 @@ struct b200_context {
 namespace b200 {
 
 WeightView view_of(const b200_weight * w);
+// Records the text b200_last_error(NULL) returns on this thread (errors outside any context).
+void set_thread_error(const char * what);
 
 // Kernel launchers (ops.cu). Each returns the launch's cudaError_t.
 // ctas_per_sm > 0 caps the grid at num_sms * ctas_per_sm CTAs (leaves room for a dependent launch's CTAs).
