@@ -203,8 +203,13 @@ b200_status b200_decoder_step_host(b200_decoder * d, const float * x_host, float
 /* Kernel launches of one step, and the GGUF weight bytes one step streams. */
 int64_t b200_decoder_launches(const b200_decoder * d);
 size_t b200_decoder_weight_bytes(const b200_decoder * d);
-/* Launch options: programmatic dependent launch on/off, CTAs per SM per product (0: as many as fit). */
-b200_status b200_decoder_set_launch(b200_decoder * d, int pdl, int ctas_per_sm);
+/* How a step runs. B200_DEC_MODE_CHAIN: one launch per product, chained with programmatic dependent launch
+ * (pdl != 0) and ctas_per_sm CTAs per SM (0: as many as fit). B200_DEC_MODE_PERSISTENT: the whole step as one
+ * persistent kernel, one CTA per SM, products separated by device-side completion counters; needs K % 1024 == 0
+ * (K % 2048 for Q4_K / Q6_K) and K <= 8192 for every product. -1 (the default): persistent when every product fits,
+ * else chain. */
+enum { B200_DEC_MODE_CHAIN = 0, B200_DEC_MODE_PERSISTENT = 1 };
+b200_status b200_decoder_set_launch(b200_decoder * d, int mode, int pdl, int ctas_per_sm);
 
 /* ------------------------------------------------------------------------------------------------------------
  * Host-buffer entry points (the end-to-end path a CPU caller takes: copies in, product, copy out, synchronous).

@@ -36,6 +36,7 @@ EXPORTS = [
 
 DEC_ATTN_Q, DEC_ATTN_K, DEC_ATTN_V, DEC_ATTN_O, DEC_FFN_GATE, DEC_FFN_UP, DEC_FFN_DOWN = range(7)
 DEC_ATTN_NORM, DEC_FFN_NORM, DEC_OUTPUT_NORM, DEC_OUTPUT = 7, 8, 9, 10
+DEC_MODE_CHAIN, DEC_MODE_PERSISTENT = 0, 1
 
 
 class B200Error(RuntimeError):
@@ -126,7 +127,7 @@ def lib():
         "b200_decoder_step_host": (i32, [vp, vp, vp]),
         "b200_decoder_launches": (i64, [vp]),
         "b200_decoder_weight_bytes": (sz, [vp]),
-        "b200_decoder_set_launch": (i32, [vp, i32, i32]),
+        "b200_decoder_set_launch": (i32, [vp, i32, i32, i32]),
         "b200_mul_mat_id_noalloc": (i32, [vp, W, vp, i64, vp, i64, i64, vp]),
     }
     for name, (res, args) in sig.items():
@@ -372,8 +373,9 @@ class Decoder:
     def weight_bytes(self):
         return self.L.b200_decoder_weight_bytes(self.h)
 
-    def set_launch(self, pdl=True, ctas_per_sm=1):
-        self.ctx.check(self.L.b200_decoder_set_launch(self.h, int(bool(pdl)), ctas_per_sm))
+    def set_launch(self, mode=-1, pdl=True, ctas_per_sm=2):
+        """mode: -1 automatic, DEC_MODE_CHAIN (one launch per product) or DEC_MODE_PERSISTENT (one kernel)."""
+        self.ctx.check(self.L.b200_decoder_set_launch(self.h, mode, int(bool(pdl)), ctas_per_sm))
 
     def close(self):
         if getattr(self, "h", None):

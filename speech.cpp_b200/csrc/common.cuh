@@ -71,7 +71,7 @@ __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepc
 // mbarriers and bulk (TMA) copies, global -> shared, no multicast. Waits are bounded: after kSpinLimit polls a wait
 // gives up and reports false, so no kernel can hang on a copy that never lands.
 // ------------------------------------------------------------------------------------------------------------------
-constexpr uint32_t kSpinLimit = 1u << 26;
+constexpr uint32_t kSpinLimit = 1u << 22;
 
 __device__ __forceinline__ uint32_t smem_addr(const void * p) { return (uint32_t) __cvta_generic_to_shared(p); }
 

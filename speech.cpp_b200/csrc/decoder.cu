@@ -16,6 +16,7 @@
 #include <vector>
 
 #include "internal.h"
+#include "decoder_mk.cuh"
 
 using namespace b200;
 
@@ -35,8 +36,12 @@ struct b200_decoder {
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
     bool pdl = true;
-    int cap = 1;  // CTAs per SM per product: the next product's CTA fits beside the running one
+    int cap = 2;      // CTAs per SM per product (chain mode)
+    int mode = -1;    // B200_DEC_MODE_*; -1: persistent when every product fits it, else chain
     int64_t launches = 0;
+    MkStage * mk_stages = nullptr;  // device table of the step's products (persistent mode)
+    unsigned * mk_done = nullptr;   // per-product completion counters
+    int mk_n = 0;
 };
 
 namespace {
@@ -71,46 +76,129 @@ GemvParams stage(const b200_decoder * d, const b200_weight & w, const float * x,
     return p;
 }
 
-// Enqueues the step's products on the context stream.
-b200_status enqueue_step(b200_decoder * d) {
+// The step's products in chain order, as GemvParams (both modes are built from this one list).
+std::vector<GemvParams> step_products(b200_decoder * d) {
     const b200_decoder_shape & s = d->s;
-    cudaStream_t st = d->ctx->stream;
-    const int sms = d->ctx->num_sms;
-    d->launches = 0;
+    std::vector<GemvParams> v;
     for (int l = 0; l < s.n_layer; l++) {
         const float * x = l == 0 ? d->x_in : d->h;
         GemvParams a = stage(d, d->qkv[l], x, d->qkv_out);
         a.pro = PRO_RMSNORM;
         a.norm_w = d->attn_norm[l];
         a.eps = s.eps;
-        DCK(d, launch_gemv(a, 1, 1, st, d->pdl, sms, d->cap));
-
+        v.push_back(a);
         GemvParams b = stage(d, d->o[l], d->qkv_out + (int64_t) (s.n_head + s.n_kv_head) * s.head_dim, d->h);
         b.pro = PRO_GQA;
         b.pro_k = s.head_dim;
         b.pro_rep = s.n_head / s.n_kv_head;
         b.res = x;
-        DCK(d, launch_gemv(b, 1, 1, st, d->pdl, sms, d->cap));
-
+        v.push_back(b);
         GemvParams c = stage(d, d->gu[l], d->h, d->gu_out);
         c.pro = PRO_RMSNORM;
         c.norm_w = d->ffn_norm[l];
         c.eps = s.eps;
-        DCK(d, launch_gemv(c, 1, 1, st, d->pdl, sms, d->cap));
-
+        v.push_back(c);
         GemvParams e = stage(d, d->down[l], d->gu_out, d->h);
         e.pro = PRO_SWIGLU;
         e.pro_k = s.ffn;
         e.res = d->h;
-        DCK(d, launch_gemv(e, 1, 1, st, d->pdl, sms, d->cap));
-        d->launches += 4;
+        v.push_back(e);
     }
     GemvParams hd = stage(d, d->head, s.n_layer > 0 ? d->h : d->x_in, d->logits);
     hd.pro = PRO_RMSNORM;
     hd.norm_w = d->out_norm;
     hd.eps = s.eps;
-    DCK(d, launch_gemv(hd, 1, 1, st, d->pdl, sms, d->cap));
-    d->launches += 1;
+    v.push_back(hd);
+    return v;
+}
+
+// Whether product p can run in the persistent step (staging layout, slot size, alignment of its input).
+bool mk_fits(const GemvParams & p) {
+    const int64_t K = p.w.K;
+    const int kind = act_kind(p.w.type);
+    if (K > kMkMaxK || (kind == B200_TYPE_Q8_K ? K % 2048 : K % 1024) != 0) return false;
+    if (p.pro == PRO_GQA && (p.pro_k % 4 != 0 || p.pro_rep <= 0)) return false;
+    if (p.pro == PRO_SWIGLU && p.pro_k % 4 != 0) return false;
+    if ((((uintptr_t) p.x) & 15) != 0) return false;
+    switch (p.w.type) {
+    case B200_TYPE_Q8_0: return mk_type_fits<TQ8_0>(K);
+    case B200_TYPE_Q4_K: return mk_type_fits<TQ4_K>(K);
+    case B200_TYPE_Q6_K: return mk_type_fits<TQ6_K>(K);
+    case B200_TYPE_BF16: return mk_type_fits<TBF16>(K);
+    default: return false;
+    }
+}
+
+b200_status prepare_mk(b200_decoder * d, const std::vector<GemvParams> & v) {
+    if (d->mk_stages) return B200_OK;
+    std::vector<MkStage> st(v.size());
+    for (size_t i = 0; i < v.size(); i++) {
+        const GemvParams & p = v[i];
+        MkStage & m = st[i];
+        std::memset(&m, 0, sizeof m);
+        m.w = p.w;
+        m.N = p.N;
+        m.pro = p.pro;
+        m.pro_k = (int) p.pro_k;
+        m.pro_rep = p.pro_rep;
+        m.eps = p.eps;
+        m.x = p.x;
+        m.norm_w = p.norm_w;
+        m.res = p.res;
+        m.y = p.y;
+    }
+    DCK(d, cudaMalloc(&d->mk_stages, sizeof(MkStage) * st.size()));
+    DCK(d, cudaMalloc(&d->mk_done, sizeof(unsigned) * st.size()));
+    DCK(d, cudaMemcpy(d->mk_stages, st.data(), sizeof(MkStage) * st.size(), cudaMemcpyHostToDevice));
+    d->mk_n = (int) st.size();
+    DCK(d, cudaFuncSetAttribute(decoder_mk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) kMkSmemBytes));
+    return B200_OK;
+}
+
+b200_status enqueue_mk(b200_decoder * d) {
+    cudaStream_t st = d->ctx->stream;
+    DCK(d, cudaMemsetAsync(d->mk_done, 0, sizeof(unsigned) * d->mk_n, st));
+    MkParams P;
+    P.stages = d->mk_stages;
+    P.nstages = d->mk_n;
+    P.done = d->mk_done;
+    P.err = d->ctx->dev_err;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned) d->ctx->num_sms, 1, 1);
+    cfg.blockDim = dim3(kMkThreads, 1, 1);
+    cfg.dynamicSmemBytes = kMkSmemBytes;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    DCK(d, cudaLaunchKernelEx(&cfg, decoder_mk_kernel, P));
+    d->launches = 1;
+    return B200_OK;
+}
+
+// Enqueues the step's products on the context stream.
+b200_status enqueue_step(b200_decoder * d) {
+    std::vector<GemvParams> prods = step_products(d);
+    bool persistent = d->mode == B200_DEC_MODE_PERSISTENT;
+    if (d->mode < 0) {
+        persistent = true;
+        for (const GemvParams & p : prods) persistent = persistent && mk_fits(p);
+    }
+    if (persistent) {
+        for (const GemvParams & p : prods)
+            if (!mk_fits(p)) return dfail(d, B200_ERR_UNSUPPORTED, "decoder: a product does not fit the persistent step");
+        b200_status s = prepare_mk(d, prods);
+        if (s != B200_OK) return s;
+        return enqueue_mk(d);
+    }
+    cudaStream_t st0 = d->ctx->stream;
+    d->launches = 0;
+    for (const GemvParams & p : prods) {
+        DCK(d, launch_gemv(p, 1, 1, st0, d->pdl, d->ctx->num_sms, d->cap));
+        d->launches++;
+    }
     return B200_OK;
 }
 
@@ -180,6 +268,8 @@ void b200_decoder_destroy(b200_decoder * d) {
     for (float * p : d->ffn_norm) if (p) cudaFree(p);
     if (d->head.data) cudaFree(d->head.data);
     for (float * p : {d->out_norm, d->x_in, d->h, d->qkv_out, d->gu_out, d->logits}) if (p) cudaFree(p);
+    if (d->mk_stages) cudaFree(d->mk_stages);
+    if (d->mk_done) cudaFree(d->mk_done);
     if (d->host_io) cudaFreeHost(d->host_io);
     delete d;
 }
@@ -269,8 +359,9 @@ size_t b200_decoder_weight_bytes(const b200_decoder * d) {
     return b;
 }
 
-b200_status b200_decoder_set_launch(b200_decoder * d, int pdl, int ctas_per_sm) {
-    if (!d || ctas_per_sm < 0) return B200_ERR_INVALID;
+b200_status b200_decoder_set_launch(b200_decoder * d, int mode, int pdl, int ctas_per_sm) {
+    if (!d || ctas_per_sm < 0 || mode < -1 || mode > 1) return B200_ERR_INVALID;
+    d->mode = mode;
     d->pdl = pdl != 0;
     d->cap = ctas_per_sm;
     if (d->exec) {

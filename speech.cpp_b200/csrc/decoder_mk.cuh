@@ -1,0 +1,372 @@
+// decoder_mk.cuh — the decode step as ONE persistent kernel (one CTA per SM for the whole step).
+//
+// A decode step is a chain of dependent products (4 per layer + head, 113 for the 28-layer talker), each needing the
+// complete output of the one before it. Launching them one by one pays a kernel boundary per product. Here every
+// CTA runs the whole chain:
+//   - its producer warp streams the CTA's row slice of EVERY product's weights, in order, through one ring of
+//     shared-memory slots with bulk async copies (cp.async.bulk, no multicast; mbarrier transaction counts). Weights
+//     depend on nothing, so the ring runs ahead of the computation by up to its capacity;
+//   - its consumer warps, for product s, wait until all CTAs have finished product s-1 (a global completion counter
+//     per product, polled with a bounded spin), load the input vector from L2 into registers, apply the fused
+//     prologue (RMSNorm * weight, SwiGLU, grouped-query value broadcast), quantize it to the vec_dot type
+//     bit-identically to the CPU oracle, reduce their rows from the ring, write the outputs (+ residual), and publish
+//     completion (__threadfence + atomicAdd).
+// All CTAs must be co-resident: the kernel is launched cooperatively with one CTA per SM. Every wait is bounded; a
+// wait that gives up records B200_DEVERR_TIMEOUT and the CTA leaves the chain, so the others give up in turn.
+#pragma once
+
+#include "gemv.cuh"
+
+namespace b200 {
+
+struct MkStage {
+    WeightView w;
+    int64_t N;
+    int pro;
+    int pro_k;
+    int pro_rep;
+    float eps;
+    const float * x;       // input vector (written earlier in the chain: read through L2)
+    const float * norm_w;  // RMSNorm weights
+    const float * res;     // residual (same rows as y) or null
+    float * y;
+};
+
+struct MkParams {
+    const MkStage * stages;
+    int nstages;
+    unsigned * done;  // [nstages] CTAs that finished each product (zeroed before the launch)
+    unsigned * err;
+};
+
+constexpr int kMkConsumerWarps = 8;
+constexpr int kMkThreads = 32 * (kMkConsumerWarps + 1);
+constexpr int kMkSlotBytes = 16 * 1024;
+constexpr int kMkSlots = 12;
+constexpr int kMkMaxK = 8192;
+constexpr size_t kMkActBytes = 2 * kMkMaxK + (kMkMaxK / 32) * 4 + (kMkMaxK / 16) * 2 + 256;  // bf16 needs 2K bytes
+constexpr size_t kMkSmemBytes = (size_t) kMkSlots * kMkSlotBytes + kMkActBytes + 2 * kMkSlots * 8 + 64;
+
+// Conditions under which a product can run in the persistent step (host and device agree).
+template <class T>
+__host__ __device__ inline bool mk_type_fits(int64_t K) {
+    int64_t rb = 0;
+    for (int i = 0; i < T::kFields; i++) {
+        if (T::field_row_bytes(K, i) % 16 != 0) return false;
+        rb += T::field_row_bytes(K, i);
+    }
+    return rb <= kMkSlotBytes;
+}
+
+__host__ __device__ inline int64_t mk_row_bytes(int type, int64_t K) {
+    switch (type) {
+    case B200_TYPE_Q8_0: return K + K / 16;
+    case B200_TYPE_Q4_K: return K / 2 + K / 16;
+    case B200_TYPE_Q6_K: return K / 2 + K / 4 + K / 16 + K / 128;
+    case B200_TYPE_BF16: return 2 * K;
+    default: return 0;
+    }
+}
+
+__device__ __forceinline__ unsigned ld_acquire(const unsigned * p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void mk_sync() { asm volatile("bar.sync 1, %0;" ::"r"(32 * kMkConsumerWarps) : "memory"); }
+
+// Rows [r0, r1) of product s that CTA `cta` of `G` computes (contiguous, balanced).
+__device__ __forceinline__ void mk_slice(int64_t N, int G, int cta, int64_t & r0, int64_t & r1) {
+    const int64_t base = N / G, extra = N % G;
+    r0 = cta * base + (cta < extra ? cta : extra);
+    r1 = r0 + base + (cta < extra ? 1 : 0);
+}
+
+// Input value k of product S for its prologue (global loads through L2: these vectors were written in this kernel).
+__device__ __forceinline__ float4 mk_load4(const MkStage & S, int k, float rms) {
+    float4 v;
+    switch (S.pro) {
+    case PRO_SWIGLU: {
+        const float4 g = __ldcg(reinterpret_cast<const float4 *>(S.x + k));
+        const float4 u = __ldcg(reinterpret_cast<const float4 *>(S.x + S.pro_k + k));
+        v.x = __fmul_rn(silu(g.x), u.x);
+        v.y = __fmul_rn(silu(g.y), u.y);
+        v.z = __fmul_rn(silu(g.z), u.z);
+        v.w = __fmul_rn(silu(g.w), u.w);
+        return v;
+    }
+    case PRO_GQA: {
+        const int span = S.pro_k * S.pro_rep;
+        return __ldcg(reinterpret_cast<const float4 *>(S.x + (k / span) * S.pro_k + k % S.pro_k));
+    }
+    default:
+        return __ldcg(reinterpret_cast<const float4 *>(S.x + k));
+    }
+}
+
+// Stages product S's quantized input in the act arrays (consumer threads only; ends with mk_sync()).
+// q8_0 (K % 1024 == 0): thread t holds values 4t + 1024 i; eight consecutive threads form one 32-block.
+// q8_K (K % 2048 == 0): thread t holds values 8t + 2048 i; one warp forms one 256-block.
+__device__ __forceinline__ void mk_stage_input(const MkStage & S, const Act & a, float * part) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int K = (int) S.w.K;
+    const int kind = act_kind(S.w.type);
+    const bool rmsnorm = S.pro == PRO_RMSNORM;
+    if (kind == B200_TYPE_Q8_K) {
+        constexpr int kMax = kMkMaxK / 2048;
+        float v[kMax][8];
+        float sq = 0.0f;
+#pragma unroll
+        for (int i = 0; i < kMax; i++) {
+            if (i < K / 2048) {
+                const int k = 8 * tid + 2048 * i;
+                const float4 lo = mk_load4(S, k, 0.0f), hi = mk_load4(S, k + 4, 0.0f);
+                v[i][0] = lo.x; v[i][1] = lo.y; v[i][2] = lo.z; v[i][3] = lo.w;
+                v[i][4] = hi.x; v[i][5] = hi.y; v[i][6] = hi.z; v[i][7] = hi.w;
+#pragma unroll
+                for (int j = 0; j < 8; j++) sq = fmaf(v[i][j], v[i][j], sq);
+            }
+        }
+        float rms = 0.0f;
+        if (rmsnorm) {
+            sq = warp_sum(sq);
+            if (lane == 0) part[warp] = sq;
+            mk_sync();
+            float t = 0.0f;
+            for (int w = 0; w < kMkConsumerWarps; w++) t += part[w];
+            rms = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(t, (float) K), S.eps)));
+        }
+#pragma unroll
+        for (int i = 0; i < kMax; i++) {
+            if (i < K / 2048) {
+                const int k = 8 * tid + 2048 * i;
+                if (rmsnorm) {
+                    const float4 w0 = __ldg(reinterpret_cast<const float4 *>(S.norm_w + k));
+                    const float4 w1 = __ldg(reinterpret_cast<const float4 *>(S.norm_w + k + 4));
+                    const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+                    for (int j = 0; j < 8; j++) v[i][j] = __fmul_rn(__fmul_rn(v[i][j], rms), wv[j]);
+                }
+                int8_t q[8];
+                int16_t bsum;
+                float d;
+                quantize_q8_K_warp(v[i], q, &bsum, &d);
+                int2 packed;
+                packed.x = (int) (uint8_t) q[0] | ((int) (uint8_t) q[1] << 8) | ((int) (uint8_t) q[2] << 16) | ((int) (uint8_t) q[3] << 24);
+                packed.y = (int) (uint8_t) q[4] | ((int) (uint8_t) q[5] << 8) | ((int) (uint8_t) q[6] << 16) | ((int) (uint8_t) q[7] << 24);
+                *reinterpret_cast<int2 *>(a.q + k) = packed;
+                const int b = k / 256;
+                if ((lane & 1) == 0) a.bs[b * 16 + lane / 2] = bsum;
+                if (lane == 0) a.d[b] = d;
+            }
+        }
+    } else {
+        constexpr int kMax = kMkMaxK / 1024;
+        float4 v[kMax];
+        float sq = 0.0f;
+#pragma unroll
+        for (int i = 0; i < kMax; i++) {
+            if (i < K / 1024) {
+                v[i] = mk_load4(S, 4 * tid + 1024 * i, 0.0f);
+                sq = fmaf(v[i].x, v[i].x, sq);
+                sq = fmaf(v[i].y, v[i].y, sq);
+                sq = fmaf(v[i].z, v[i].z, sq);
+                sq = fmaf(v[i].w, v[i].w, sq);
+            }
+        }
+        float rms = 0.0f;
+        if (rmsnorm) {
+            sq = warp_sum(sq);
+            if (lane == 0) part[warp] = sq;
+            mk_sync();
+            float t = 0.0f;
+            for (int w = 0; w < kMkConsumerWarps; w++) t += part[w];
+            rms = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(t, (float) K), S.eps)));
+        }
+#pragma unroll
+        for (int i = 0; i < kMax; i++) {
+            if (i < K / 1024) {
+                const int k = 4 * tid + 1024 * i;
+                float e[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+                if (rmsnorm) {
+                    const float4 w = __ldg(reinterpret_cast<const float4 *>(S.norm_w + k));
+                    e[0] = __fmul_rn(__fmul_rn(e[0], rms), w.x);
+                    e[1] = __fmul_rn(__fmul_rn(e[1], rms), w.y);
+                    e[2] = __fmul_rn(__fmul_rn(e[2], rms), w.z);
+                    e[3] = __fmul_rn(__fmul_rn(e[3], rms), w.w);
+                }
+                if (kind == B200_TYPE_BF16) {
+#pragma unroll
+                    for (int j = 0; j < 4; j++) a.b[k + j] = __float2bfloat16_rn(e[j]);
+                    continue;
+                }
+                float amax = fmaxf(fmaxf(fabsf(e[0]), fabsf(e[1])), fmaxf(fabsf(e[2]), fabsf(e[3])));
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+                const float d = __fdiv_rn(amax, 127.0f);
+                const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+                int w = 0;
+#pragma unroll
+                for (int j = 0; j < 4; j++) w |= ((int) (uint8_t) (int8_t) (int) roundf(__fmul_rn(e[j], id))) << (8 * j);
+                *reinterpret_cast<int *>(a.q + k) = w;
+                if ((tid & 7) == 0) a.d[k / 32] = __half2float(__float2half_rn(d));
+            }
+        }
+    }
+    mk_sync();
+}
+
+// Rows of one landed chunk: warps take rows j = warp, warp + 8, ...
+template <class T>
+__device__ __forceinline__ void mk_rows(const MkStage & S, const Act & a, const uint8_t * slot, int64_t rps, int64_t rows,
+                                        int64_t first) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t K = S.w.K;
+    const uint8_t * f[4];
+    const uint8_t * b = slot;
+    for (int i = 0; i < 4; i++) {
+        f[i] = b;
+        if (i < T::kFields) b += rps * T::field_row_bytes(K, i);
+    }
+    const int64_t upr = T::units_per_row(K);
+    for (int64_t j = warp; j < rows; j += kMkConsumerWarps) {
+        float acc[1] = {0.0f};
+        for (int64_t u0 = 0; u0 < upr; u0 += 32) {
+            const int64_t u = u0 + lane;
+            const bool valid = u < upr;
+            typename T::Unit U;
+            if (valid) U = T::load_s(f, K, j, u);
+            else U = T::load(S.w, 0, 0, false);
+            T::template dot<1>(U, u, valid, a, acc, nullptr);
+        }
+        const float v = warp_sum(acc[0]);
+        if (lane == 0) {
+            const int64_t r = first + j;
+            S.y[r] = S.res ? __fadd_rn(__ldcg(S.res + r), v) : v;
+        }
+    }
+}
+
+template <class T>
+__device__ __forceinline__ void mk_issue(const MkStage & S, uint8_t * slot, int64_t rps, int64_t first, int64_t rows, uint64_t * bar) {
+    const uint8_t * fb[4] = {S.w.f0, S.w.f1, S.w.f2, S.w.f3};
+    uint8_t * dst = slot;
+    for (int i = 0; i < T::kFields; i++) {
+        const int64_t rb = T::field_row_bytes(S.w.K, i);
+        bulk_g2s(dst, fb[i] + first * rb, (uint32_t) (rows * rb), bar);
+        dst += rps * rb;
+    }
+}
+
+__global__ void __launch_bounds__(kMkThreads, 1) decoder_mk_kernel(MkParams P) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ float part[kMkConsumerWarps];
+    __shared__ int give_up;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int G = gridDim.x, cta = blockIdx.x;
+    uint8_t * ring = smem;
+    uint8_t * act = smem + (size_t) kMkSlots * kMkSlotBytes;
+    uint64_t * full = reinterpret_cast<uint64_t *>(act + kMkActBytes);
+    uint64_t * empty = full + kMkSlots;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kMkSlots; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kMkConsumerWarps);
+        }
+        fence_mbar_init();
+        give_up = 0;
+    }
+    __syncthreads();
+
+    if (warp == kMkConsumerWarps) {
+        // ---- producer: every product's slice of weights, in chain order ----
+        if (lane == 0) {
+            uint32_t ctr = 0;
+            for (int s = 0; s < P.nstages; s++) {
+                const MkStage & S = P.stages[s];
+                const int64_t rb = mk_row_bytes(S.w.type, S.w.K);
+                const int64_t rps = kMkSlotBytes / rb;
+                int64_t r0, r1;
+                mk_slice(S.N, G, cta, r0, r1);
+                for (int64_t first = r0; first < r1; first += rps, ctr++) {
+                    const int slot = (int) (ctr % kMkSlots);
+                    const uint32_t it = ctr / kMkSlots;
+                    if (it > 0 && !mbar_wait(&empty[slot], (it - 1) & 1)) {
+                        atomicOr(P.err, 4u);
+                        return;
+                    }
+                    const int64_t rows = r1 - first < rps ? r1 - first : rps;
+                    mbar_arrive_expect_tx(&full[slot], (uint32_t) (rows * rb));
+                    uint8_t * dst = ring + (size_t) slot * kMkSlotBytes;
+                    switch (S.w.type) {
+                    case B200_TYPE_Q8_0: mk_issue<TQ8_0>(S, dst, rps, first, rows, &full[slot]); break;
+                    case B200_TYPE_Q4_K: mk_issue<TQ4_K>(S, dst, rps, first, rows, &full[slot]); break;
+                    case B200_TYPE_Q6_K: mk_issue<TQ6_K>(S, dst, rps, first, rows, &full[slot]); break;
+                    default: mk_issue<TBF16>(S, dst, rps, first, rows, &full[slot]); break;
+                    }
+                }
+            }
+        }
+        return;
+    }
+
+    // ---- consumers ----
+    uint32_t ctr = 0;
+    for (int s = 0; s < P.nstages; s++) {
+        const MkStage S = P.stages[s];
+        if (s > 0) {
+            if (threadIdx.x == 0) {
+                uint32_t i = 0;
+                while (ld_acquire(&P.done[s - 1]) < (unsigned) G) {
+                    if (++i >= kSpinLimit) {
+                        atomicOr(P.err, 4u);
+                        give_up = 1;
+                        break;
+                    }
+                }
+            }
+            mk_sync();
+            if (give_up) break;
+        }
+        Act a;
+        a.K = S.w.K;
+        a.q = reinterpret_cast<int8_t *>(act);
+        a.d = reinterpret_cast<float *>(act + 2 * kMkMaxK);
+        a.bs = reinterpret_cast<int16_t *>(act + 2 * kMkMaxK + (kMkMaxK / 32) * 4);
+        a.b = reinterpret_cast<__nv_bfloat16 *>(act);
+        mk_stage_input(S, a, part);
+
+        const int64_t rb = mk_row_bytes(S.w.type, S.w.K);
+        const int64_t rps = kMkSlotBytes / rb;
+        int64_t r0, r1;
+        mk_slice(S.N, G, cta, r0, r1);
+        for (int64_t first = r0; first < r1; first += rps, ctr++) {
+            const int slot = (int) (ctr % kMkSlots);
+            if (!mbar_wait(&full[slot], (ctr / kMkSlots) & 1)) {
+                if (lane == 0) atomicOr(P.err, 4u);
+                give_up = 1;
+                break;
+            }
+            const int64_t rows = r1 - first < rps ? r1 - first : rps;
+            const uint8_t * sp = ring + (size_t) slot * kMkSlotBytes;
+            switch (S.w.type) {
+            case B200_TYPE_Q8_0: mk_rows<TQ8_0>(S, a, sp, rps, rows, first); break;
+            case B200_TYPE_Q4_K: mk_rows<TQ4_K>(S, a, sp, rps, rows, first); break;
+            case B200_TYPE_Q6_K: mk_rows<TQ6_K>(S, a, sp, rps, rows, first); break;
+            default: mk_rows<TBF16>(S, a, sp, rps, rows, first); break;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+        mk_sync();  // all outputs of this CTA for product s are written; the act arrays may be reused
+        if (give_up) break;
+        if (threadIdx.x == 0) {
+            __threadfence();
+            atomicAdd(&P.done[s], 1u);
+        }
+    }
+}
+
+}  // namespace b200

@@ -12,10 +12,16 @@ from conftest import load_package
 pytestmark = pytest.mark.gpu
 
 SMALL = {
+    # rows too short for the persistent step: chain mode only
     "q8": dict(n_layer=3, hidden=256, n_head=4, n_kv_head=2, head_dim=64, ffn=512, n_vocab=300,
                type_attn=8, type_ffn_up=8, type_ffn_down=8, type_head=8),
     "kquant": dict(n_layer=2, hidden=512, n_head=8, n_kv_head=2, head_dim=64, ffn=1024, n_vocab=1000,
                    type_attn=12, type_ffn_up=12, type_ffn_down=14, type_head=14),
+    # shapes the persistent step takes (K % 1024, K % 2048 for K-quants)
+    "q8_mk": dict(n_layer=2, hidden=1024, n_head=8, n_kv_head=2, head_dim=128, ffn=3072, n_vocab=500,
+                  type_attn=8, type_ffn_up=8, type_ffn_down=8, type_head=8),
+    "kquant_mk": dict(n_layer=2, hidden=2048, n_head=16, n_kv_head=4, head_dim=128, ffn=2048, n_vocab=700,
+                      type_attn=12, type_ffn_up=12, type_ffn_down=14, type_head=14),
 }
 
 
@@ -65,15 +71,34 @@ def test_decoder_step_matches_cpu(b200, ctx, name):
     x = rng.normal(0, 1, size=c["hidden"]).astype(np.float32)
     want = stack.step(c, model, x)
     d = load(b200, ctx, c, model)
-    got = d.step(torch.from_numpy(x).cuda()).cpu().numpy()
+    xd = torch.from_numpy(x).cuda()
+    d.set_launch(mode=b200.DEC_MODE_CHAIN)
+    got = d.step(xd).cpu().numpy()
     assert d.launches == 4 * c["n_layer"] + 1
     assert cosine(got, want) >= 0.9999
     host = d.step_host(x)
     assert np.array_equal(host, got)
-    # launch options change scheduling only, never results
-    d.set_launch(pdl=False, ctas_per_sm=0)
-    again = d.step(torch.from_numpy(x).cuda()).cpu().numpy()
+    # chain launch options change scheduling only, never results
+    d.set_launch(mode=b200.DEC_MODE_CHAIN, pdl=False, ctas_per_sm=0)
+    again = d.step(xd).cpu().numpy()
     assert np.array_equal(again, got)
+    if name.endswith("_mk"):
+        d.set_launch(mode=-1)
+        pers = d.step(xd).cpu().numpy()
+        assert d.launches == 1  # the automatic choice is the persistent step
+        ctx.synchronize()
+        assert cosine(pers, want) >= 0.9999
+        assert cosine(pers, got) >= 0.99999
+        for _ in range(3):  # replays of the captured step are deterministic
+            assert np.array_equal(d.step(xd).cpu().numpy(), pers)
+        assert np.array_equal(d.step_host(x), pers)
+    else:
+        d.set_launch(mode=-1)
+        d.step(xd)
+        assert d.launches == 4 * c["n_layer"] + 1  # not eligible: the automatic choice is the chain
+        with pytest.raises(b200.B200Error):
+            d.set_launch(mode=b200.DEC_MODE_PERSISTENT)
+            d.step(xd)
     d.close()
 
 
