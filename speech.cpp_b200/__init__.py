@@ -12,6 +12,7 @@ context's own stream. There is no CPU fallback: if libb200.so is missing or no B
 
 import ctypes
 import os
+import weakref
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libb200.so")
@@ -168,6 +169,7 @@ class Context:
         if s != OK:
             raise B200Error(s, self.L.b200_last_error(None).decode())
         self.h = h
+        self._children = weakref.WeakSet()  # decoders built on this context: closed before it
 
     def check(self, status):
         if status != OK:
@@ -187,6 +189,8 @@ class Context:
 
     def close(self):
         if getattr(self, "h", None):
+            for child in list(getattr(self, "_children", ())):
+                child.close()
             self.L.b200_context_destroy(self.h)
             self.h = None
 
@@ -330,6 +334,7 @@ class Decoder:
         h = ctypes.c_void_p()
         ctx.check(self.L.b200_decoder_create(ctx.h, ctypes.byref(self.shape), ctypes.byref(h)))
         self.h = h
+        ctx._children.add(self)
 
     def set_tensor(self, layer, which, data, offset=0):
         """data: numpy (host) or a CUDA tensor; GGUF block bytes for matrices, float32 for norms."""
@@ -378,8 +383,10 @@ class Decoder:
         self.ctx.check(self.L.b200_decoder_set_launch(self.h, mode, int(bool(pdl)), ctas_per_sm))
 
     def close(self):
+        # a decoder's memory belongs to its context: destroy it only while the context is alive
         if getattr(self, "h", None):
-            self.L.b200_decoder_destroy(self.h)
+            if getattr(self.ctx, "h", None):
+                self.L.b200_decoder_destroy(self.h)
             self.h = None
 
     def __del__(self):

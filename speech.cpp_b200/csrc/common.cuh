@@ -198,7 +198,14 @@ __device__ __forceinline__ void quantize_q8_K_warp(const float v[8], int8_t q[8]
     *bsum = (int16_t) s;
 }
 
-// SiLU as ggml's CPU defines it: x / (1 + exp(-x)).
-__device__ __forceinline__ float silu(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x))); }
+// SiLU as ggml's CPU defines it, x / (1 + exp(-x)), with the hardware exponential and division (relative error
+// ~1e-6: the decoder-stack parity is judged by cosine similarity, not bit equality).
+__device__ __forceinline__ float silu(float x) { return __fdividef(x, __fadd_rn(1.0f, __expf(-x))); }
+
+// Asynchronous 4-byte global -> shared copy (completes at cp_async_wait_all; the issuing thread does not stall).
+__device__ __forceinline__ void cp_async4(void * smem_dst, const void * gmem_src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(smem_dst)), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 }  // namespace b200

@@ -20,6 +20,11 @@
 
 using namespace b200;
 
+#ifdef B200_MK_PROBE
+static long long * b200_mk_probe_buffer = nullptr;
+extern "C" __attribute__((visibility("default"))) void b200_mk_probe_set(void * p) { b200_mk_probe_buffer = (long long *) p; }
+#endif
+
 struct b200_decoder {
     b200_context * ctx = nullptr;
     b200_decoder_shape s{};
@@ -146,6 +151,13 @@ b200_status prepare_mk(b200_decoder * d, const std::vector<GemvParams> & v) {
         m.norm_w = p.norm_w;
         m.res = p.res;
         m.y = p.y;
+        m.row_bytes = (int) mk_row_bytes(p.w.type, p.w.K);
+        m.rps = kMkSlotBytes / m.row_bytes;
+        m.slice_base = (int) (p.N / d->ctx->num_sms);
+        m.slice_extra = (int) (p.N % d->ctx->num_sms);
+        auto log2_exact = [](int64_t v) { int s = 0; while ((1ll << s) < v) s++; return (v > 0 && (1ll << s) == v) ? s : -1; };
+        m.gqa_shift = p.pro == PRO_GQA ? log2_exact(p.pro_k * p.pro_rep) : -1;
+        m.hd_shift = p.pro == PRO_GQA ? log2_exact(p.pro_k) : -1;
     }
     DCK(d, cudaMalloc(&d->mk_stages, sizeof(MkStage) * st.size()));
     DCK(d, cudaMalloc(&d->mk_done, sizeof(unsigned) * st.size()));
@@ -159,6 +171,9 @@ b200_status enqueue_mk(b200_decoder * d) {
     cudaStream_t st = d->ctx->stream;
     DCK(d, cudaMemsetAsync(d->mk_done, 0, sizeof(unsigned) * d->mk_n, st));
     MkParams P;
+#ifdef B200_MK_PROBE
+    P.probe = b200_mk_probe_buffer;
+#endif
     P.stages = d->mk_stages;
     P.nstages = d->mk_n;
     P.done = d->mk_done;

@@ -15,7 +15,7 @@
 // wait that gives up records B200_DEVERR_TIMEOUT and the CTA leaves the chain, so the others give up in turn.
 #pragma once
 
-#include "gemv.cuh"
+#include "gemv_tma.cuh"
 
 namespace b200 {
 
@@ -30,9 +30,28 @@ struct MkStage {
     const float * norm_w;  // RMSNorm weights
     const float * res;     // residual (same rows as y) or null
     float * y;
+    // precomputed by the host (no divisions on the device's critical path)
+    int row_bytes;    // GGUF bytes of one weight row
+    int rps;          // rows per ring slot
+    int slice_base;   // N / G
+    int slice_extra;  // N % G
+    int gqa_shift;    // log2(pro_k * pro_rep) for PRO_GQA (-1: not a power of two)
+    int hd_shift;     // log2(pro_k) for PRO_GQA (-1: not a power of two)
 };
 
+// Phase timestamps for latency studies (clock64 of the CTA's thread 0 / producer lane), compiled in only with
+// -DB200_MK_PROBE: probe[cta][product][8].
+#ifdef B200_MK_PROBE
+#define MK_PROBE(slot) \
+    do { if (P.probe) P.probe[((size_t) blockIdx.x * P.nstages + s) * 8 + (slot)] = clock64(); } while (0)
+#else
+#define MK_PROBE(slot) do { } while (0)
+#endif
+
 struct MkParams {
+#ifdef B200_MK_PROBE
+    long long * probe;
+#endif
     const MkStage * stages;
     int nstages;
     unsigned * done;  // [nstages] CTAs that finished each product (zeroed before the launch)
@@ -41,9 +60,9 @@ struct MkParams {
 
 constexpr int kMkConsumerWarps = 8;
 constexpr int kMkThreads = 32 * (kMkConsumerWarps + 1);
-constexpr int kMkSlotBytes = 16 * 1024;
-constexpr int kMkSlots = 12;
-constexpr int kMkMaxK = 8192;
+constexpr int kMkSlotBytes = 32 * 1024;
+constexpr int kMkSlots = 6;
+constexpr int kMkMaxK = 6144;
 constexpr size_t kMkActBytes = 2 * kMkMaxK + (kMkMaxK / 32) * 4 + (kMkMaxK / 16) * 2 + 256;  // bf16 needs 2K bytes
 constexpr size_t kMkSmemBytes = (size_t) kMkSlots * kMkSlotBytes + kMkActBytes + 2 * kMkSlots * 8 + 64;
 
@@ -76,10 +95,10 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned * p) {
 
 __device__ __forceinline__ void mk_sync() { asm volatile("bar.sync 1, %0;" ::"r"(32 * kMkConsumerWarps) : "memory"); }
 
-// Rows [r0, r1) of product s that CTA `cta` of `G` computes (contiguous, balanced).
-__device__ __forceinline__ void mk_slice(int64_t N, int G, int cta, int64_t & r0, int64_t & r1) {
-    const int64_t base = N / G, extra = N % G;
-    r0 = cta * base + (cta < extra ? cta : extra);
+// Rows [r0, r1) of a product that CTA `cta` computes (contiguous, balanced; base = N / G, extra = N % G).
+__device__ __forceinline__ void mk_slice(const MkStage & S, int cta, int64_t & r0, int64_t & r1) {
+    const int base = S.slice_base, extra = S.slice_extra;
+    r0 = (int64_t) cta * base + (cta < extra ? cta : extra);
     r1 = r0 + base + (cta < extra ? 1 : 0);
 }
 
@@ -97,6 +116,8 @@ __device__ __forceinline__ float4 mk_load4(const MkStage & S, int k, float rms) 
         return v;
     }
     case PRO_GQA: {
+        if (S.gqa_shift >= 0 && S.hd_shift >= 0)
+            return __ldcg(reinterpret_cast<const float4 *>(S.x + ((k >> S.gqa_shift) << S.hd_shift) + (k & (S.pro_k - 1))));
         const int span = S.pro_k * S.pro_rep;
         return __ldcg(reinterpret_cast<const float4 *>(S.x + (k / span) * S.pro_k + k % S.pro_k));
     }
@@ -116,7 +137,16 @@ __device__ __forceinline__ void mk_stage_input(const MkStage & S, const Act & a,
     if (kind == B200_TYPE_Q8_K) {
         constexpr int kMax = kMkMaxK / 2048;
         float v[kMax][8];
+        float4 nw[kMax][2];
         float sq = 0.0f;
+#pragma unroll
+        for (int i = 0; i < kMax; i++) {
+            if (i < K / 2048 && rmsnorm) {
+                const int k = 8 * tid + 2048 * i;
+                nw[i][0] = __ldg(reinterpret_cast<const float4 *>(S.norm_w + k));
+                nw[i][1] = __ldg(reinterpret_cast<const float4 *>(S.norm_w + k + 4));
+            }
+        }
 #pragma unroll
         for (int i = 0; i < kMax; i++) {
             if (i < K / 2048) {
@@ -142,8 +172,7 @@ __device__ __forceinline__ void mk_stage_input(const MkStage & S, const Act & a,
             if (i < K / 2048) {
                 const int k = 8 * tid + 2048 * i;
                 if (rmsnorm) {
-                    const float4 w0 = __ldg(reinterpret_cast<const float4 *>(S.norm_w + k));
-                    const float4 w1 = __ldg(reinterpret_cast<const float4 *>(S.norm_w + k + 4));
+                    const float4 w0 = nw[i][0], w1 = nw[i][1];
                     const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
                     for (int j = 0; j < 8; j++) v[i][j] = __fmul_rn(__fmul_rn(v[i][j], rms), wv[j]);
@@ -163,8 +192,11 @@ __device__ __forceinline__ void mk_stage_input(const MkStage & S, const Act & a,
         }
     } else {
         constexpr int kMax = kMkMaxK / 1024;
-        float4 v[kMax];
+        float4 v[kMax], nw[kMax];
         float sq = 0.0f;
+#pragma unroll
+        for (int i = 0; i < kMax; i++)
+            if (i < K / 1024 && rmsnorm) nw[i] = __ldg(reinterpret_cast<const float4 *>(S.norm_w + 4 * tid + 1024 * i));
 #pragma unroll
         for (int i = 0; i < kMax; i++) {
             if (i < K / 1024) {
@@ -190,7 +222,7 @@ __device__ __forceinline__ void mk_stage_input(const MkStage & S, const Act & a,
                 const int k = 4 * tid + 1024 * i;
                 float e[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
                 if (rmsnorm) {
-                    const float4 w = __ldg(reinterpret_cast<const float4 *>(S.norm_w + k));
+                    const float4 w = nw[i];
                     e[0] = __fmul_rn(__fmul_rn(e[0], rms), w.x);
                     e[1] = __fmul_rn(__fmul_rn(e[1], rms), w.y);
                     e[2] = __fmul_rn(__fmul_rn(e[2], rms), w.z);
@@ -215,13 +247,16 @@ __device__ __forceinline__ void mk_stage_input(const MkStage & S, const Act & a,
             }
         }
     }
+    cp_async_wait_all();  // this thread's residual copies (issued before staging) have landed
     mk_sync();
 }
 
-// Rows of one landed chunk: warps take rows j = warp, warp + 8, ...
+constexpr int kMkResRows = 64;  // residual values of a CTA's slice kept in shared memory (more: read from L2)
+
+// Rows of one landed chunk, two per warp at a time. res_s holds the residuals of the CTA's rows [r0, r0 + 64).
 template <class T>
 __device__ __forceinline__ void mk_rows(const MkStage & S, const Act & a, const uint8_t * slot, int64_t rps, int64_t rows,
-                                        int64_t first) {
+                                        int64_t first, int64_t r0, const float * res_s) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t K = S.w.K;
     const uint8_t * f[4];
@@ -230,23 +265,14 @@ __device__ __forceinline__ void mk_rows(const MkStage & S, const Act & a, const 
         f[i] = b;
         if (i < T::kFields) b += rps * T::field_row_bytes(K, i);
     }
-    const int64_t upr = T::units_per_row(K);
-    for (int64_t j = warp; j < rows; j += kMkConsumerWarps) {
-        float acc[1] = {0.0f};
-        for (int64_t u0 = 0; u0 < upr; u0 += 32) {
-            const int64_t u = u0 + lane;
-            const bool valid = u < upr;
-            typename T::Unit U;
-            if (valid) U = T::load_s(f, K, j, u);
-            else U = T::load(S.w, 0, 0, false);
-            T::template dot<1>(U, u, valid, a, acc, nullptr);
-        }
-        const float v = warp_sum(acc[0]);
-        if (lane == 0) {
+    smem_rows<T>(f, K, (int) rows, a, S.w, warp, kMkConsumerWarps, [&](int j, float v) {
+        {
             const int64_t r = first + j;
-            S.y[r] = S.res ? __fadd_rn(__ldcg(S.res + r), v) : v;
+            float out = v;
+            if (S.res) out = __fadd_rn(r - r0 < kMkResRows ? res_s[r - r0] : __ldcg(S.res + r), v);
+            S.y[r] = out;
         }
-    }
+    });
 }
 
 template <class T>
@@ -264,6 +290,8 @@ __global__ void __launch_bounds__(kMkThreads, 1) decoder_mk_kernel(MkParams P) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float part[kMkConsumerWarps];
     __shared__ int give_up;
+    __shared__ float res_s[kMkResRows];
+    __shared__ __align__(16) MkStage desc[3];  // this product's, the next one's, and the one after (being copied)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = gridDim.x, cta = blockIdx.x;
     uint8_t * ring = smem;
@@ -286,10 +314,10 @@ __global__ void __launch_bounds__(kMkThreads, 1) decoder_mk_kernel(MkParams P) {
             uint32_t ctr = 0;
             for (int s = 0; s < P.nstages; s++) {
                 const MkStage & S = P.stages[s];
-                const int64_t rb = mk_row_bytes(S.w.type, S.w.K);
-                const int64_t rps = kMkSlotBytes / rb;
+                const int64_t rb = S.row_bytes;
+                const int64_t rps = S.rps;
                 int64_t r0, r1;
-                mk_slice(S.N, G, cta, r0, r1);
+                mk_slice(S, cta, r0, r1);
                 for (int64_t first = r0; first < r1; first += rps, ctr++) {
                     const int slot = (int) (ctr % kMkSlots);
                     const uint32_t it = ctr / kMkSlots;
@@ -297,6 +325,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decoder_mk_kernel(MkParams P) {
                         atomicOr(P.err, 4u);
                         return;
                     }
+                    if (first == r0) MK_PROBE(6);
                     const int64_t rows = r1 - first < rps ? r1 - first : rps;
                     mbar_arrive_expect_tx(&full[slot], (uint32_t) (rows * rb));
                     uint8_t * dst = ring + (size_t) slot * kMkSlotBytes;
@@ -313,9 +342,18 @@ __global__ void __launch_bounds__(kMkThreads, 1) decoder_mk_kernel(MkParams P) {
     }
 
     // ---- consumers ----
+    constexpr int kDescWords = sizeof(MkStage) / 4;
+    static_assert(sizeof(MkStage) % 4 == 0, "descriptor copy by words");
+    if (threadIdx.x < kDescWords) {
+        reinterpret_cast<uint32_t *>(&desc[0])[threadIdx.x] = reinterpret_cast<const uint32_t *>(&P.stages[0])[threadIdx.x];
+        if (P.nstages > 1)
+            reinterpret_cast<uint32_t *>(&desc[1])[threadIdx.x] = reinterpret_cast<const uint32_t *>(&P.stages[1])[threadIdx.x];
+    }
+    mk_sync();
     uint32_t ctr = 0;
     for (int s = 0; s < P.nstages; s++) {
-        const MkStage S = P.stages[s];
+        if (threadIdx.x == 0) MK_PROBE(0);
+        const MkStage & S = desc[s % 3];
         if (s > 0) {
             if (threadIdx.x == 0) {
                 uint32_t i = 0;
@@ -330,18 +368,24 @@ __global__ void __launch_bounds__(kMkThreads, 1) decoder_mk_kernel(MkParams P) {
             mk_sync();
             if (give_up) break;
         }
+        if (threadIdx.x == 0) MK_PROBE(1);
+        int64_t r0, r1;
+        mk_slice(S, cta, r0, r1);
+        // residuals of this CTA's rows: asynchronous copies, complete before the staging barrier below
+        if (S.res && (int64_t) threadIdx.x < r1 - r0 && threadIdx.x < kMkResRows) cp_async4(&res_s[threadIdx.x], S.res + r0 + threadIdx.x);
         Act a;
         a.K = S.w.K;
         a.q = reinterpret_cast<int8_t *>(act);
         a.d = reinterpret_cast<float *>(act + 2 * kMkMaxK);
         a.bs = reinterpret_cast<int16_t *>(act + 2 * kMkMaxK + (kMkMaxK / 32) * 4);
         a.b = reinterpret_cast<__nv_bfloat16 *>(act);
-        mk_stage_input(S, a, part);
+        mk_stage_input(S, a, part);  // ends with a barrier: res_s is complete
+        if (threadIdx.x == 0) MK_PROBE(2);
+        // the descriptor after next goes to the third buffer (this one, s % 3, stays readable during product s)
+        if (s + 2 < P.nstages && threadIdx.x < kDescWords)
+            cp_async4(reinterpret_cast<uint32_t *>(&desc[(s + 2) % 3]) + threadIdx.x, reinterpret_cast<const uint32_t *>(&P.stages[s + 2]) + threadIdx.x);
 
-        const int64_t rb = mk_row_bytes(S.w.type, S.w.K);
-        const int64_t rps = kMkSlotBytes / rb;
-        int64_t r0, r1;
-        mk_slice(S.N, G, cta, r0, r1);
+        const int64_t rps = S.rps;
         for (int64_t first = r0; first < r1; first += rps, ctr++) {
             const int slot = (int) (ctr % kMkSlots);
             if (!mbar_wait(&full[slot], (ctr / kMkSlots) & 1)) {
@@ -349,22 +393,25 @@ __global__ void __launch_bounds__(kMkThreads, 1) decoder_mk_kernel(MkParams P) {
                 give_up = 1;
                 break;
             }
+            if (threadIdx.x == 0 && first == r0) MK_PROBE(3);
             const int64_t rows = r1 - first < rps ? r1 - first : rps;
             const uint8_t * sp = ring + (size_t) slot * kMkSlotBytes;
             switch (S.w.type) {
-            case B200_TYPE_Q8_0: mk_rows<TQ8_0>(S, a, sp, rps, rows, first); break;
-            case B200_TYPE_Q4_K: mk_rows<TQ4_K>(S, a, sp, rps, rows, first); break;
-            case B200_TYPE_Q6_K: mk_rows<TQ6_K>(S, a, sp, rps, rows, first); break;
-            default: mk_rows<TBF16>(S, a, sp, rps, rows, first); break;
+            case B200_TYPE_Q8_0: mk_rows<TQ8_0>(S, a, sp, rps, rows, first, r0, res_s); break;
+            case B200_TYPE_Q4_K: mk_rows<TQ4_K>(S, a, sp, rps, rows, first, r0, res_s); break;
+            case B200_TYPE_Q6_K: mk_rows<TQ6_K>(S, a, sp, rps, rows, first, r0, res_s); break;
+            default: mk_rows<TBF16>(S, a, sp, rps, rows, first, r0, res_s); break;
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
         }
+        cp_async_wait_all();  // the next descriptor has landed
         mk_sync();  // all outputs of this CTA for product s are written; the act arrays may be reused
+        if (threadIdx.x == 0) MK_PROBE(4);
         if (give_up) break;
         if (threadIdx.x == 0) {
-            __threadfence();
-            atomicAdd(&P.done[s], 1u);
+            // release: this CTA's outputs (ordered before by the barrier) are visible before the count rises
+            asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(&P.done[s]), "r"(1u) : "memory");
         }
     }
 }

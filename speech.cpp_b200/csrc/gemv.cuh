@@ -323,18 +323,21 @@ __device__ __forceinline__ int byte_of(const int4 & v, int i) {
 }
 
 struct TQ8_0 {
-    // unit = 16 bytes of one 32-block (2 lanes per block)
-    struct Unit { int4 q; uint16_t d; };
-    static constexpr int kUnroll = 4;
-    __device__ static int64_t units_per_row(int64_t K) { return K / 16; }
+    // unit = one whole 32-block: 32 bytes of qs and its fp16 scale (one lane per block, no shuffles)
+    struct Unit { int4 q0; int4 q1; uint16_t d; };
+    static constexpr int kUnroll = 2;
+    static constexpr int kSmemUnroll = 2;  // units in flight per lane when reducing rows from shared memory
+    __device__ static int64_t units_per_row(int64_t K) { return K / 32; }
     __device__ static int sums_per_row(int64_t K) { return (int) (K / 32); }
     __device__ static Unit load(const WeightView & w, int64_t row, int64_t u, bool valid) {
         Unit r;
         if (valid) {
-            r.q = ld_stream(w.f0 + row * w.K + u * 16);
-            r.d = (u & 1) ? 0 : __ldg(reinterpret_cast<const unsigned short *>(w.f1) + row * (w.K / 32) + u / 2);
+            const uint8_t * p = w.f0 + row * w.K + u * 32;
+            r.q0 = ld_stream(p);
+            r.q1 = ld_stream(p + 16);
+            r.d = __ldg(reinterpret_cast<const unsigned short *>(w.f1) + row * (w.K / 32) + u);
         } else {
-            r.q = make_int4(0, 0, 0, 0);
+            r.q0 = r.q1 = make_int4(0, 0, 0, 0);
             r.d = 0;
         }
         return r;
@@ -344,66 +347,63 @@ struct TQ8_0 {
     __host__ __device__ static int64_t field_row_bytes(int64_t K, int i) { return i == 0 ? K : i == 1 ? K / 16 : 0; }
     __device__ static Unit load_s(const uint8_t * const * f, int64_t K, int64_t row, int64_t u) {
         Unit r;
-        r.q = *reinterpret_cast<const int4 *>(f[0] + row * K + u * 16);
-        r.d = (u & 1) ? 0 : reinterpret_cast<const uint16_t *>(f[1])[row * (K / 32) + u / 2];
+        const int off = (int) row * (int) K + (int) u * 32;
+        r.q0 = *reinterpret_cast<const int4 *>(f[0] + off);
+        r.q1 = *reinterpret_cast<const int4 *>(f[0] + off + 16);
+        r.d = reinterpret_cast<const uint16_t *>(f[1])[(int) row * (int) (K / 32) + (int) u];
         return r;
     }
     template <int NC>
     __device__ static void dot(const Unit & U, int64_t u, bool valid, const Act & a, float * acc, int32_t * sums) {
-        const int * wq = reinterpret_cast<const int *>(&U.q);
+        if (!valid) return;
         const float dw = __half2float(__ushort_as_half(U.d));
+        const int ui = (int) u, K = (int) a.K;
 #pragma unroll
         for (int c = 0; c < NC; c++) {
-            int s = 0;
-            if (valid) {
-                const int4 xv = *reinterpret_cast<const int4 *>(a.q + (int64_t) c * a.K + u * 16);
-                s = __dp4a(wq[0], xv.x, s);
-                s = __dp4a(wq[1], xv.y, s);
-                s = __dp4a(wq[2], xv.z, s);
-                s = __dp4a(wq[3], xv.w, s);
-            }
-            s += __shfl_xor_sync(0xffffffffu, s, 1);
-            if (valid && (u & 1) == 0) {
-                const float dx = a.d[(int64_t) c * (a.K / 32) + u / 2];
-                acc[c] += (float) s * __fmul_rn(dw, dx);
-                if (c == 0 && sums) sums[u / 2] = s;
-            }
+            const int4 * xp = reinterpret_cast<const int4 *>(a.q + c * K + ui * 32);
+            const int4 x0 = xp[0], x1 = xp[1];
+            int s = __dp4a(U.q0.x, x0.x, 0);
+            s = __dp4a(U.q0.y, x0.y, s);
+            s = __dp4a(U.q0.z, x0.z, s);
+            s = __dp4a(U.q0.w, x0.w, s);
+            s = __dp4a(U.q1.x, x1.x, s);
+            s = __dp4a(U.q1.y, x1.y, s);
+            s = __dp4a(U.q1.z, x1.z, s);
+            s = __dp4a(U.q1.w, x1.w, s);
+            acc[c] += (float) s * __fmul_rn(dw, a.d[c * (K / 32) + ui]);
+            if (c == 0 && sums) sums[ui] = s;
         }
     }
 };
 
 struct TQ4_K {
-    // unit = 16 bytes of qs: super-block u/8, byte chunk (u%8)*16 (8 lanes per super-block); plus the 16-byte meta
-    struct Unit { int4 q; int4 m; };
+    // unit = 32 bytes of qs: super-block u/4, chunk g = u%4 holding sub-blocks 2g (low nibbles) and 2g+1 (high
+    // nibbles), all 32 values of each; plus the super-block's 16-byte meta. Four lanes per super-block.
+    struct Unit { int4 q0; int4 q1; int4 m; };
     static constexpr int kUnroll = 2;
-    __device__ static int64_t units_per_row(int64_t K) { return K / 32; }  // K/2 bytes of nibbles, 16 per unit
+    static constexpr int kSmemUnroll = 2;
+    __device__ static int64_t units_per_row(int64_t K) { return K / 64; }
     __device__ static int sums_per_row(int64_t K) { return (int) (2 * (K / 256)); }
     __device__ static Unit load(const WeightView & w, int64_t row, int64_t u, bool valid) {
         Unit r;
         if (valid) {
-            r.q = ld_stream(w.f0 + row * (w.K / 2) + u * 16);
-            r.m = __ldg(reinterpret_cast<const int4 *>(w.f1 + (row * (w.K / 256) + u / 8) * 16));
+            const uint8_t * p = w.f0 + row * (w.K / 2) + u * 32;
+            r.q0 = ld_stream(p);
+            r.q1 = ld_stream(p + 16);
+            r.m = __ldg(reinterpret_cast<const int4 *>(w.f1 + (row * (w.K / 256) + u / 4) * 16));
         } else {
-            r.q = make_int4(0, 0, 0, 0);
-            r.m = make_int4(0, 0, 0, 0);
+            r.q0 = r.q1 = r.m = make_int4(0, 0, 0, 0);
         }
         return r;
-    }
-    __device__ static void scale_min(const uint8_t * s, int j, int & sc, int & m) {
-        if (j < 4) {
-            sc = s[j] & 63;
-            m = s[j + 4] & 63;
-        } else {
-            sc = (s[j + 4] & 15) | ((s[j - 4] >> 6) << 4);
-            m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
-        }
     }
     static constexpr int kFields = 2;  // qs [rows][K/2], meta [rows][K/256][16]
     __host__ __device__ static int64_t field_row_bytes(int64_t K, int i) { return i == 0 ? K / 2 : i == 1 ? K / 16 : 0; }
     __device__ static Unit load_s(const uint8_t * const * f, int64_t K, int64_t row, int64_t u) {
         Unit r;
-        r.q = *reinterpret_cast<const int4 *>(f[0] + row * (K / 2) + u * 16);
-        r.m = *reinterpret_cast<const int4 *>(f[1] + (row * (K / 256) + u / 8) * 16);
+        const int off = (int) row * (int) (K / 2) + (int) u * 32;
+        r.q0 = *reinterpret_cast<const int4 *>(f[0] + off);
+        r.q1 = *reinterpret_cast<const int4 *>(f[0] + off + 16);
+        r.m = *reinterpret_cast<const int4 *>(f[1] + ((int) row * (int) (K / 256) + (int) u / 4) * 16);
         return r;
     }
     // six-bit scale and min of sub-block j from the 12 scale bytes, which are bytes 4..15 of the meta value
@@ -416,12 +416,20 @@ struct TQ4_K {
             mn = (byte_of(m, 12 + j - 4) >> 4) | ((byte_of(m, 8 + j - 4) >> 6) << 4);
         }
     }
+    // the same from a byte pointer (GET_ROWS)
+    __device__ static void scale_min(const uint8_t * s, int j, int & sc, int & m) {
+        if (j < 4) {
+            sc = s[j] & 63;
+            m = s[j + 4] & 63;
+        } else {
+            sc = (s[j + 4] & 15) | ((s[j - 4] >> 6) << 4);
+            m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+        }
+    }
     template <int NC>
     __device__ static void dot(const Unit & U, int64_t u, bool valid, const Act & a, float * acc, int32_t * sums) {
-        const int * wq = reinterpret_cast<const int *>(&U.q);
-        const int64_t sb = u / 8;
-        const int j = (int) (u & 7), g = j >> 1, h = j & 1;
-        const int s0 = 2 * g, s1 = 2 * g + 1;
+        const int ui = (int) u, K = (int) a.K;
+        const int sb = ui >> 2, g = ui & 3, s0 = 2 * g, s1 = 2 * g + 1;
         int sc0 = 0, m0 = 0, sc1 = 0, m1 = 0;
         if (valid) {
             scale_min_reg(U.m, s0, sc0, m0);
@@ -429,36 +437,34 @@ struct TQ4_K {
         }
         const float dw = __half2float(__ushort_as_half((unsigned short) (U.m.x & 0xFFFF)));
         const float dmw = __half2float(__ushort_as_half((unsigned short) ((unsigned) U.m.x >> 16)));
+        const int w[8] = {U.q0.x, U.q0.y, U.q0.z, U.q0.w, U.q1.x, U.q1.y, U.q1.z, U.q1.w};
 #pragma unroll
         for (int c = 0; c < NC; c++) {
             int si = 0, sm = 0;
             if (valid) {
-                const int8_t * xq = a.q + (int64_t) c * a.K + sb * 256;
-                const int4 xl = *reinterpret_cast<const int4 *>(xq + s0 * 32 + h * 16);
-                const int4 xh = *reinterpret_cast<const int4 *>(xq + s1 * 32 + h * 16);
+                const int8_t * xq = a.q + c * K + sb * 256;
+                const int4 * xl = reinterpret_cast<const int4 *>(xq + s0 * 32);
+                const int4 * xh = reinterpret_cast<const int4 *>(xq + s1 * 32);
+                const int4 l0 = xl[0], l1 = xl[1], h0 = xh[0], h1 = xh[1];
+                const int xlv[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+                const int xhv[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
                 int il = 0, ih = 0;
-                il = __dp4a(wq[0] & 0x0F0F0F0F, xl.x, il);
-                il = __dp4a(wq[1] & 0x0F0F0F0F, xl.y, il);
-                il = __dp4a(wq[2] & 0x0F0F0F0F, xl.z, il);
-                il = __dp4a(wq[3] & 0x0F0F0F0F, xl.w, il);
-                ih = __dp4a((wq[0] >> 4) & 0x0F0F0F0F, xh.x, ih);
-                ih = __dp4a((wq[1] >> 4) & 0x0F0F0F0F, xh.y, ih);
-                ih = __dp4a((wq[2] >> 4) & 0x0F0F0F0F, xh.z, ih);
-                ih = __dp4a((wq[3] >> 4) & 0x0F0F0F0F, xh.w, ih);
-                si = sc0 * il + sc1 * ih;
-                if (h == 0) {
-                    const int16_t * bs = a.bs + (int64_t) c * (a.K / 16) + sb * 16;
-                    sm = m0 * ((int) bs[2 * s0] + (int) bs[2 * s0 + 1]) + m1 * ((int) bs[2 * s1] + (int) bs[2 * s1 + 1]);
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    il = __dp4a(w[i] & 0x0F0F0F0F, xlv[i], il);
+                    ih = __dp4a((w[i] >> 4) & 0x0F0F0F0F, xhv[i], ih);
                 }
+                si = sc0 * il + sc1 * ih;
+                const int16_t * bs = a.bs + c * (K / 16) + sb * 16;
+                sm = m0 * ((int) bs[2 * s0] + (int) bs[2 * s0 + 1]) + m1 * ((int) bs[2 * s1] + (int) bs[2 * s1 + 1]);
             }
+            // the super-block's exact int32 sums over its four lanes
             si += __shfl_xor_sync(0xffffffffu, si, 1);
             si += __shfl_xor_sync(0xffffffffu, si, 2);
-            si += __shfl_xor_sync(0xffffffffu, si, 4);
             sm += __shfl_xor_sync(0xffffffffu, sm, 1);
             sm += __shfl_xor_sync(0xffffffffu, sm, 2);
-            sm += __shfl_xor_sync(0xffffffffu, sm, 4);
-            if (valid && j == 0) {
-                const float dx = a.d[(int64_t) c * (a.K / 256) + sb];
+            if (valid && g == 0) {
+                const float dx = a.d[c * (K / 256) + sb];
                 acc[c] += __fmul_rn(dx, dw) * (float) si;
                 acc[c] -= __fmul_rn(dx, dmw) * (float) sm;
                 if (c == 0 && sums) {
@@ -475,6 +481,7 @@ struct TQ6_K {
     // 16 bytes of ql (t = 0, 2), 16 bytes of ql (t = 1, 3), 16 bytes of qh, and the 16 scales.
     struct Unit { int4 a; int4 b; int4 h; int4 s; uint16_t d; };
     static constexpr int kUnroll = 1;
+    static constexpr int kSmemUnroll = 1;
     __device__ static int64_t units_per_row(int64_t K) { return K / 64; }
     __device__ static int sums_per_row(int64_t K) { return (int) (K / 256); }
     __device__ static Unit load(const WeightView & w, int64_t row, int64_t u, bool valid) {
@@ -556,6 +563,7 @@ struct TQ6_K {
 struct TBF16 {
     struct Unit { int4 q; };
     static constexpr int kUnroll = 4;
+    static constexpr int kSmemUnroll = 4;
     __device__ static int64_t units_per_row(int64_t K) { return K / 8; }
     __device__ static int sums_per_row(int64_t) { return 0; }
     __device__ static Unit load(const WeightView & w, int64_t row, int64_t u, bool valid) {

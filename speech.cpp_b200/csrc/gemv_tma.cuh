@@ -39,6 +39,60 @@ __host__ __device__ inline size_t tma_smem_bytes(int wtype, int64_t K, int rows_
     return ring + ((act_smem_bytes(wtype, K, NC) + 15) & ~(size_t) 15) + 16 * (size_t) stages + 16;
 }
 
+// Two warp sums at once (their shuffles interleave, halving the reduction's latency per row).
+__device__ __forceinline__ void warp_sum2(float & a, float & b) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ta = __shfl_xor_sync(0xffffffffu, a, o);
+        const float tb = __shfl_xor_sync(0xffffffffu, b, o);
+        a += ta;
+        b += tb;
+    }
+}
+
+// Single-column products of `rows` landed rows (field pointers f, row j at local index j). A warp works on 32 / LPR
+// rows at once, LPR lanes per row, each lane taking every LPR-th unit of its row (independent units: their loads and
+// dp4a chains overlap), then an LPR-lane reduction. LPR = 8 for rows of up to 64 units, else 32. store(j, value).
+template <class T, int LPR, class Store>
+__device__ __forceinline__ void smem_rows_lpr(const uint8_t * const * f, int64_t K, int rows, const Act & a, const WeightView & w,
+                                              int warp, int nwarps, Store store) {
+    const int lane = threadIdx.x & 31;
+    const int upr = (int) T::units_per_row(K);
+    constexpr int kRowsPerPass = 32 / LPR;
+    const int sub = lane / LPR, li = lane % LPR;
+    for (int j0 = warp * kRowsPerPass; j0 < rows; j0 += nwarps * kRowsPerPass) {
+        const int j = j0 + sub;
+        const bool row_ok = j < rows;
+        float acc[1] = {0.0f};
+        constexpr int kU = T::kSmemUnroll;
+        for (int u0 = 0; u0 < upr; u0 += LPR * kU) {
+            typename T::Unit U[kU];
+#pragma unroll
+            for (int t = 0; t < kU; t++) {
+                const int u = u0 + t * LPR + li;
+                if (row_ok && u < upr) U[t] = T::load_s(f, K, j, u);
+                else U[t] = T::load(w, 0, 0, false);
+            }
+#pragma unroll
+            for (int t = 0; t < kU; t++) {
+                const int u = u0 + t * LPR + li;
+                T::template dot<1>(U[t], u, row_ok && u < upr, a, acc, nullptr);
+            }
+        }
+        float v = acc[0];
+#pragma unroll
+        for (int o = LPR / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (row_ok && li == 0) store(j, v);
+    }
+}
+
+template <class T, class Store>
+__device__ __forceinline__ void smem_rows(const uint8_t * const * f, int64_t K, int rows, const Act & a, const WeightView & w,
+                                          int warp, int nwarps, Store store) {
+    if (T::units_per_row(K) <= 64) smem_rows_lpr<T, 8>(f, K, rows, a, w, warp, nwarps, store);
+    else smem_rows_lpr<T, 32>(f, K, rows, a, w, warp, nwarps, store);
+}
+
 template <class T, int NC>
 __global__ void __launch_bounds__(kTmaThreads, 2) gemv_tma_kernel(GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -137,27 +191,37 @@ __global__ void __launch_bounds__(kTmaThreads, 2) gemv_tma_kernel(GemvParams p) 
                 if (i < T::kFields) b += (int64_t) rps * T::field_row_bytes(K, i);
             }
         }
-        for (int64_t j = warp; j < rows; j += kTmaConsumerWarps) {
-            const int64_t r = r_begin + c * rps + j;  // output row
-            int32_t * sums = p.sums ? p.sums + r * nsums : nullptr;
-            float acc[NC];
+        if (NC == 1 && !p.sums) {
+            const int64_t base = r_begin + c * rps;
+            smem_rows<T>(f, K, (int) rows, a, p.w, warp, kTmaConsumerWarps, [&](int j, float v) {
+                if (nc > 0) {
+                    const int64_t r = base + j;
+                    p.y[r] = p.res ? __fadd_rn(p.res[r], v) : v;
+                }
+            });
+        } else {
+            for (int64_t j = warp; j < rows; j += kTmaConsumerWarps) {
+                const int64_t r = r_begin + c * rps + j;  // output row
+                int32_t * sums = p.sums ? p.sums + r * nsums : nullptr;
+                float acc[NC];
 #pragma unroll
-            for (int q = 0; q < NC; q++) acc[q] = 0.0f;
-            for (int64_t u0 = 0; u0 < upr; u0 += 32) {
-                const int64_t u = u0 + lane;
-                const bool valid = u < upr;
-                typename T::Unit U;
-                if (valid) U = T::load_s(f, K, j, u);
-                else U = T::load(p.w, 0, 0, false);
-                T::template dot<NC>(U, u, valid, a, acc, sums);
-            }
+                for (int q = 0; q < NC; q++) acc[q] = 0.0f;
+                for (int64_t u0 = 0; u0 < upr; u0 += 32) {
+                    const int64_t u = u0 + lane;
+                    const bool valid = u < upr;
+                    typename T::Unit U;
+                    if (valid) U = T::load_s(f, K, j, u);
+                    else U = T::load(p.w, 0, 0, false);
+                    T::template dot<NC>(U, u, valid, a, acc, sums);
+                }
 #pragma unroll
-            for (int q = 0; q < NC; q++) {
-                const float v = warp_sum(acc[q]);
-                if (lane == 0 && q < nc && !p.sums) {
-                    float out = v;
-                    if (p.res) out = __fadd_rn(p.res[(int64_t) q * p.ldres + r], v);
-                    p.y[(int64_t) q * p.ldy + r] = out;
+                for (int q = 0; q < NC; q++) {
+                    const float v = warp_sum(acc[q]);
+                    if (lane == 0 && q < nc && !p.sums) {
+                        float out = v;
+                        if (p.res) out = __fadd_rn(p.res[(int64_t) q * p.ldres + r], v);
+                        p.y[(int64_t) q * p.ldy + r] = out;
+                    }
                 }
             }
         }
