@@ -215,6 +215,59 @@ def make_decoder(pkg, ctx, seed):
     return d, c
 
 
+def large_gemv(pkg, ctx, stream, reps=20):
+    """Weight GB/s of single large products (matrices far larger than L2), one launch each, CUDA events on the
+    context stream: the HBM-bound GEMV kernels without the decode step's dependency chain."""
+    import ctypes
+
+    import torch
+
+    out = {}
+    cases = [("q8_0", pkg.Q8_0, 4096, 65536), ("q4_k", pkg.Q4_K, 4096, 65536),
+             ("q6_k_head_asr17", pkg.Q6_K, 2048, 151936)]
+    g = torch.Generator(device="cuda").manual_seed(3)
+    for name, t, K, N in cases:
+        w = ctx.weight(t, K, N)
+        for r0 in range(0, N, 16384):  # quantize in pieces (device-side, bit-identical to the oracle's quantizer)
+            rows = min(16384, N - r0)
+            if t == pkg.Q8_0:
+                blocks = ctx.quantize_rows(t, torch.randn((rows, K), generator=g, device="cuda") * 0.02)
+            else:  # K-quant weights: random valid blocks (uniform bytes, small positive fp16 scales)
+                blocks = _random_kquant_blocks(t, rows, K, g)
+            ctx.set_weight(w, blocks, offset=r0 * pkg.row_size(t, K))
+        x = torch.randn((1, K), generator=g, device="cuda")
+        y = torch.empty((1, N), device="cuda")
+        ctx.synchronize()
+        call = lambda: ctx.check(ctx.L.b200_mul_mat(ctx.h, ctypes.byref(w), ctypes.c_void_p(x.data_ptr()), 1, ctypes.c_void_p(y.data_ptr())))
+        for _ in range(3):
+            call()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            call()
+        e1.record(stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        out[name] = {"K": K, "N": N, "weight_bytes": w.nbytes, "us": ms * 1000.0, "gbs": w.nbytes / ms / 1e6}
+        ctx.free_weight(w)
+    return out
+
+
+def _random_kquant_blocks(t, rows, K, g):
+    import torch
+
+    bb = {12: 144, 14: 210}[t]
+    nb = rows * (K // 256)
+    b = torch.randint(0, 256, (nb, bb), generator=g, device="cuda", dtype=torch.int32).to(torch.uint8)
+    scale = (torch.rand((nb,), generator=g, device="cuda") * 1e-3 + 1e-4).to(torch.float16).view(torch.uint8).view(nb, 2)
+    if t == 12:
+        b[:, 0:2] = scale
+        b[:, 2:4] = scale
+    else:
+        b[:, 208:210] = scale
+    return b.reshape(-1)
+
+
 def run_b200(args):
     import torch
 
@@ -288,6 +341,7 @@ def run_b200(args):
 
     wbytes = dec.weight_bytes
     launches = dec.launches
+    gemv = large_gemv(pkg, ctx, stream) if world == 1 or rank == 0 else None
     peak, peak_kind = peaks()
     achieved = wbytes / (ms_step / 1000.0) / 1e9  # GB/s of algorithmic weight bytes, per GPU
     traffic = profile_traffic()
@@ -301,7 +355,7 @@ def run_b200(args):
                                    "gate|up 1024->6144, down 3072->1024} + head 1024->3072, Q8_0, batch 1",
                        "global_batch": world, "seq_len": 1, "parallelism": f"replicas x{world}" if world > 1 else "single",
                        "l2": "weights 471 MB > 126 MB L2 each step (no flush needed)"},
-            "roofline": {"bound": "hbm", "kernel": "gemv_kernel<TQ8_0,1> (every launch of the step)",
+            "roofline": {"bound": "hbm", "kernel": "decoder_mk_kernel (the whole step, one launch)" if launches == 1 else "gemv_tma_kernel<TQ8_0,1> (every launch of the step)",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6650",
                          "algorithmic_bytes_per_step": wbytes, "launches_per_step": launches,
@@ -309,6 +363,7 @@ def run_b200(args):
                          "traffic_source": traffic.get("source") if traffic else None},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": c["hidden"] * 4, "d2h_bytes_per_step": c["n_vocab"] * 4},
             "gpu_launches": launches * args.steps,
+            "gemv_large": {k: dict(v, frac=v["gbs"] / peak) for k, v in (gemv or {}).items()},
             "clocks": clk.summary(),
         }
     del dec

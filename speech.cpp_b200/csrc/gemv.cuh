@@ -323,7 +323,9 @@ __device__ __forceinline__ int byte_of(const int4 & v, int i) {
 }
 
 struct TQ8_0 {
-    // unit = one whole 32-block: 32 bytes of qs and its fp16 scale (one lane per block, no shuffles)
+    // unit = one whole 32-block: 32 bytes of qs and its fp16 scale (one lane per block, no shuffles). Lanes 4..7 of
+    // every 8 read the block's second 16 bytes first: each 8-lane phase of a 128-bit shared load then covers all 32
+    // banks once (blocks are 32 bytes apart), for the weights and the activations alike.
     struct Unit { int4 q0; int4 q1; uint16_t d; };
     static constexpr int kUnroll = 2;
     static constexpr int kSmemUnroll = 2;  // units in flight per lane when reducing rows from shared memory
@@ -333,8 +335,9 @@ struct TQ8_0 {
         Unit r;
         if (valid) {
             const uint8_t * p = w.f0 + row * w.K + u * 32;
-            r.q0 = ld_stream(p);
-            r.q1 = ld_stream(p + 16);
+            const int h = (threadIdx.x >> 2) & 1;
+            r.q0 = ld_stream(p + 16 * h);
+            r.q1 = ld_stream(p + 16 * (1 - h));
             r.d = __ldg(reinterpret_cast<const unsigned short *>(w.f1) + row * (w.K / 32) + u);
         } else {
             r.q0 = r.q1 = make_int4(0, 0, 0, 0);
@@ -348,8 +351,9 @@ struct TQ8_0 {
     __device__ static Unit load_s(const uint8_t * const * f, int64_t K, int64_t row, int64_t u) {
         Unit r;
         const int off = (int) row * (int) K + (int) u * 32;
-        r.q0 = *reinterpret_cast<const int4 *>(f[0] + off);
-        r.q1 = *reinterpret_cast<const int4 *>(f[0] + off + 16);
+        const int h = (threadIdx.x >> 2) & 1;
+        r.q0 = *reinterpret_cast<const int4 *>(f[0] + off + 16 * h);
+        r.q1 = *reinterpret_cast<const int4 *>(f[0] + off + 16 * (1 - h));
         r.d = reinterpret_cast<const uint16_t *>(f[1])[(int) row * (int) (K / 32) + (int) u];
         return r;
     }
@@ -360,8 +364,9 @@ struct TQ8_0 {
         const int ui = (int) u, K = (int) a.K;
 #pragma unroll
         for (int c = 0; c < NC; c++) {
+            const int h = (threadIdx.x >> 2) & 1;
             const int4 * xp = reinterpret_cast<const int4 *>(a.q + c * K + ui * 32);
-            const int4 x0 = xp[0], x1 = xp[1];
+            const int4 x0 = xp[h], x1 = xp[1 - h];
             int s = __dp4a(U.q0.x, x0.x, 0);
             s = __dp4a(U.q0.y, x0.y, s);
             s = __dp4a(U.q0.z, x0.z, s);

@@ -114,7 +114,7 @@ __global__ void __launch_bounds__(kTmaThreads, 2) gemv_tma_kernel(GemvParams p) 
     if (threadIdx.x == 0) {
         for (int s = 0; s < stages; s++) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kTmaConsumerWarps);
+            mbar_init(&empty[s], 1);  // released by the one warp that consumed it
         }
         fence_mbar_init();
     }
@@ -176,7 +176,11 @@ __global__ void __launch_bounds__(kTmaThreads, 2) gemv_tma_kernel(GemvParams p) 
 
     const int64_t upr = T::units_per_row(K);
     const int nsums = T::sums_per_row(K);
-    for (int64_t c = 0; c < nchunks; c++) {
+    // chunk c belongs to consumer warp c % W (W = min(8, stages); the host makes stages a multiple of W), so every
+    // ring slot is consumed by one warp, which waits for the slot's phases strictly in order (a parity wait cannot
+    // tell phase n from phase n + 2: a slot shared between warps could be taken a phase early)
+    const int W = stages < kTmaConsumerWarps ? stages : kTmaConsumerWarps;
+    for (int64_t c = warp; warp < W && c < nchunks; c += W) {
         const int s = (int) (c % stages);
         if (!mbar_wait(&full[s], (uint32_t) ((c / stages) & 1))) {
             if (lane == 0) atomicOr(p.err, kDevErrTimeout);
@@ -191,17 +195,17 @@ __global__ void __launch_bounds__(kTmaThreads, 2) gemv_tma_kernel(GemvParams p) 
                 if (i < T::kFields) b += (int64_t) rps * T::field_row_bytes(K, i);
             }
         }
+        const int64_t base = r_begin + c * rps;
         if (NC == 1 && !p.sums) {
-            const int64_t base = r_begin + c * rps;
-            smem_rows<T>(f, K, (int) rows, a, p.w, warp, kTmaConsumerWarps, [&](int j, float v) {
+            smem_rows<T>(f, K, (int) rows, a, p.w, 0, 1, [&](int j, float v) {
                 if (nc > 0) {
                     const int64_t r = base + j;
                     p.y[r] = p.res ? __fadd_rn(p.res[r], v) : v;
                 }
             });
         } else {
-            for (int64_t j = warp; j < rows; j += kTmaConsumerWarps) {
-                const int64_t r = r_begin + c * rps + j;  // output row
+            for (int64_t j = 0; j < rows; j++) {
+                const int64_t r = base + j;  // output row
                 int32_t * sums = p.sums ? p.sums + r * nsums : nullptr;
                 float acc[NC];
 #pragma unroll

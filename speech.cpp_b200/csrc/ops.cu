@@ -11,6 +11,8 @@
 #include "internal.h"
 #include "gemv_tma.cuh"
 
+#include <cstdlib>
+
 namespace b200 {
 
 // ------------------------------------------------------------------------------------------------------------------
@@ -284,21 +286,34 @@ static cudaError_t launch_tma(const GemvParams & p0, cudaStream_t st, bool pdl, 
     GemvParams p = p0;
     const int64_t K = p.w.K;
     const int64_t row_bytes = tma_row_bytes<T>(K);
-    const int per_sm = cap_per_sm > 0 ? (cap_per_sm < 2 ? cap_per_sm : 2) : 2;
+    static const int env_cta0 = [] { const char * e = getenv("B200_TMA_CTAS_PER_SM"); return e ? atoi(e) : 1; }();
+    // a caller's cap (a chain of products wants two CTAs per SM, so the next product's CTA fits beside the running
+    // one) wins over the default of one CTA per SM with the large ring
+    const int per_sm = cap_per_sm > 0 ? (cap_per_sm < 2 ? cap_per_sm : 2) : env_cta0;
     int64_t gx = (int64_t) num_sms * per_sm;
     if (gx > p.N) gx = p.N;
     if (gx < 1) gx = 1;
     int64_t rpc = (p.N + gx - 1) / gx;
     gx = (p.N + rpc - 1) / rpc;
-    const int64_t target = 16 * 1024, ring_budget = 96 * 1024;
-    int64_t rps = target / row_bytes;
+    // Ring geometry: 8 stages (one chunk in flight per consumer warp) of ring / 8 bytes; measured on B200 with large
+    // Q8_0 / Q4_K / Q6_K products, a 192 KB ring of 24 KB stages at one CTA per SM streamed fastest.
+    // B200_TMA_RING_KB / B200_TMA_STAGES / B200_TMA_CTAS_PER_SM override it (tuning).
+    static const int64_t env_ring = [] { const char * e = getenv("B200_TMA_RING_KB"); return e ? atoll(e) * 1024 : 0; }();
+    static const int64_t env_stages = [] { const char * e = getenv("B200_TMA_STAGES"); return e ? atoll(e) : 8; }();
+    const size_t act = act_smem_bytes(p.w.type, K, NC) + 256;
+    int64_t ring_budget = env_ring > 0 ? env_ring : (per_sm >= 2 ? 96 * 1024 : 192 * 1024);
+    if ((int64_t) (ring_budget + act) > 220 * 1024) ring_budget = 220 * 1024 - (int64_t) act;
+    const int64_t max_stages = env_stages < 1 ? 1 : env_stages;
+    int64_t rps = (ring_budget / max_stages) / row_bytes;
     if (rps < 1) rps = 1;
     if (rps > rpc) rps = rpc;
     int64_t stages = ring_budget / (rps * row_bytes);
     const int64_t chunks = (rpc + rps - 1) / rps;
     if (stages > chunks) stages = chunks;
+    if (stages > max_stages) stages = max_stages;
     if (stages < 1) stages = 1;
-    if (stages > 8) stages = 8;
+    // each slot must belong to one consumer warp: a multiple of the 8 warps, or fewer slots than warps
+    if (stages > kTmaConsumerWarps) stages -= stages % kTmaConsumerWarps;
     p.rows_per_cta = (int) rpc;
     p.rows_per_stage = (int) rps;
     p.stages = (int) stages;
