@@ -431,14 +431,26 @@ struct TQ4_K {
             m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
         }
     }
+    // six-bit scale and min of sub-block j (0..7) from the meta words y = bytes 4..7, z = 8..11, w = 12..15
+    __device__ static void scale_min_words(int y, int z, int w, int j, int & sc, int & mn) {
+        const int sh = 8 * (j & 3);
+        const int by = (y >> sh) & 0xFF, bz = (z >> sh) & 0xFF, bw = (w >> sh) & 0xFF;
+        if (j < 4) {
+            sc = by & 63;
+            mn = bz & 63;
+        } else {
+            sc = (bw & 15) | ((by >> 6) << 4);
+            mn = (bw >> 4) | ((bz >> 6) << 4);
+        }
+    }
     template <int NC>
     __device__ static void dot(const Unit & U, int64_t u, bool valid, const Act & a, float * acc, int32_t * sums) {
         const int ui = (int) u, K = (int) a.K;
         const int sb = ui >> 2, g = ui & 3, s0 = 2 * g, s1 = 2 * g + 1;
         int sc0 = 0, m0 = 0, sc1 = 0, m1 = 0;
         if (valid) {
-            scale_min_reg(U.m, s0, sc0, m0);
-            scale_min_reg(U.m, s1, sc1, m1);
+            scale_min_words(U.m.y, U.m.z, U.m.w, s0, sc0, m0);
+            scale_min_words(U.m.y, U.m.z, U.m.w, s1, sc1, m1);
         }
         const float dw = __half2float(__ushort_as_half((unsigned short) (U.m.x & 0xFFFF)));
         const float dmw = __half2float(__ushort_as_half((unsigned short) ((unsigned) U.m.x >> 16)));
@@ -460,22 +472,27 @@ struct TQ4_K {
                     ih = __dp4a((w[i] >> 4) & 0x0F0F0F0F, xhv[i], ih);
                 }
                 si = sc0 * il + sc1 * ih;
-                const int16_t * bs = a.bs + c * (K / 16) + sb * 16;
-                sm = m0 * ((int) bs[2 * s0] + (int) bs[2 * s0 + 1]) + m1 * ((int) bs[2 * s1] + (int) bs[2 * s1 + 1]);
+                // sums of each 32 activations: bsums 2s and 2s+1 are adjacent int16, one 32-bit load each
+                const int * bs2 = reinterpret_cast<const int *>(a.bs + c * (K / 16) + sb * 16);
+                const int p0 = bs2[s0], p1 = bs2[s1];
+                sm = m0 * ((int) (int16_t) (p0 & 0xFFFF) + (p0 >> 16)) + m1 * ((int) (int16_t) (p1 & 0xFFFF) + (p1 >> 16));
             }
-            // the super-block's exact int32 sums over its four lanes
-            si += __shfl_xor_sync(0xffffffffu, si, 1);
-            si += __shfl_xor_sync(0xffffffffu, si, 2);
-            sm += __shfl_xor_sync(0xffffffffu, sm, 1);
-            sm += __shfl_xor_sync(0xffffffffu, sm, 2);
-            if (valid && g == 0) {
-                const float dx = a.d[c * (K / 256) + sb];
-                acc[c] += __fmul_rn(dx, dw) * (float) si;
-                acc[c] -= __fmul_rn(dx, dmw) * (float) sm;
-                if (c == 0 && sums) {
+            if (sums) {
+                // the block-sums path forms the super-block's exact int32 sums over its four lanes
+                si += __shfl_xor_sync(0xffffffffu, si, 1);
+                si += __shfl_xor_sync(0xffffffffu, si, 2);
+                sm += __shfl_xor_sync(0xffffffffu, sm, 1);
+                sm += __shfl_xor_sync(0xffffffffu, sm, 2);
+                if (valid && g == 0 && c == 0) {
                     sums[2 * sb] = si;
                     sums[2 * sb + 1] = sm;
                 }
+            }
+            if (valid && (!sums || g == 0)) {
+                // each lane's exact partial sums, scaled in float (the super-block's scale is common to its lanes)
+                const float dx = a.d[c * (K / 256) + sb];
+                acc[c] += __fmul_rn(dx, dw) * (float) si;
+                acc[c] -= __fmul_rn(dx, dmw) * (float) sm;
             }
         }
     }
@@ -554,12 +571,14 @@ struct TQ6_K {
                     si += (int) (int8_t) byte_of(U.s, h * 8 + 2 * t + lh) * s;
                 }
             }
-            si += __shfl_xor_sync(0xffffffffu, si, 1);
-            si += __shfl_xor_sync(0xffffffffu, si, 2);
-            if (valid && j == 0) {
+            if (sums) {
+                si += __shfl_xor_sync(0xffffffffu, si, 1);
+                si += __shfl_xor_sync(0xffffffffu, si, 2);
+                if (valid && j == 0 && c == 0) sums[sb] = si;
+            }
+            if (valid && (!sums || j == 0)) {
                 const float dx = a.d[(int64_t) c * (a.K / 256) + sb];
                 acc[c] += __fmul_rn(dw, dx) * (float) si;
-                if (c == 0 && sums) sums[sb] = si;
             }
         }
     }
