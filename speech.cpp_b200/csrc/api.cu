@@ -141,8 +141,35 @@ b200_status mul_mat_impl(b200_context * ctx, const b200_weight * w, int64_t row0
         CK(ctx, launch_gemv(p, pow2_at_least(M), 1, ctx->stream, false, ctx->num_sms));
         return B200_OK;
     }
-    // Many columns: quantize them once, then stream the weights once per chunk of `maxnc` columns.
     const int kind = act_kind(w->type);
+    // Many columns of Q8_0: int8 tensor cores (tcgen05) over the once-quantized activations.
+    if (gemm_tc_supported(p.w, M)) {
+        const int64_t tiles = gemm_tc_tiles(n, M);
+        const size_t qb = quantized_act_bytes(kind, K, M), wsb = gemm_tc_workspace_bytes(n, M);
+        b200_status s = ensure_scratch(ctx, qb + wsb + 256);
+        if (s != B200_OK) return s;
+        if ((size_t) tiles > ctx->ntickets) {
+            CK(ctx, cudaStreamSynchronize(ctx->stream));
+            if (ctx->tickets) cudaFree(ctx->tickets);
+            ctx->tickets = nullptr;
+            ctx->ntickets = 0;
+            const size_t nt = (size_t) tiles < 4096 ? 4096 : (size_t) tiles;
+            CK(ctx, cudaMalloc(&ctx->tickets, nt * sizeof(unsigned)));
+            CK(ctx, cudaMemset(ctx->tickets, 0, nt * sizeof(unsigned)));
+            ctx->ntickets = nt;
+        }
+        Carve c{(uint8_t *) ctx->scratch};
+        int8_t * q = c.take<int8_t>((size_t) M * K);
+        float * d = c.take<float>((size_t) M * (K / 32));
+        void * ws = c.take<uint8_t>(wsb);
+        CK(ctx, launch_quantize(kind, x, K, M, nullptr, q, d, nullptr, ctx->stream));
+        const cudaError_t e = launch_gemm_tc(p.w, row0, n, q, d, M, dst, ld_dst, ctx->dev_err, ws, wsb, ctx->tickets, ctx->num_sms,
+                                             ctx->stream);
+        if (e == cudaSuccess) return B200_OK;
+        if (e != cudaErrorInvalidValue) return cuda_fail(ctx, e, "launch_gemm_tc");
+        // a tensor map the driver refused: the GEMV path below computes the same product
+    }
+    // Many columns: quantize them once, then stream the weights once per chunk of `maxnc` columns.
     if (kind == B200_TYPE_BF16) {
         p.ncols = (int) M;
         CK(ctx, launch_gemv(p, maxnc, 1, ctx->stream, false, ctx->num_sms));
@@ -240,6 +267,7 @@ void b200_context_destroy(b200_context * ctx) {
     if (ctx->scratch) cudaFree(ctx->scratch);
     if (ctx->staging) cudaFree(ctx->staging);
     if (ctx->dev_err) cudaFree(ctx->dev_err);
+    if (ctx->tickets) cudaFree(ctx->tickets);
     if (ctx->host_err) cudaFreeHost(ctx->host_err);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
     delete ctx;

@@ -26,6 +26,8 @@ struct b200_context {
     size_t scratch_bytes = 0;
     void * staging = nullptr;         // device staging for weight uploads
     size_t staging_bytes = 0;
+    unsigned * tickets = nullptr;     // split-K tile tickets of the tensor-core GEMM (zero between launches)
+    size_t ntickets = 0;
 };
 
 namespace b200 {
@@ -44,6 +46,12 @@ cudaError_t launch_get_rows(const WeightView & w, const int32_t * ids, int64_t n
 // Activation quantization: gguf != null writes GGUF blocks there; else the internal layout (q, d, bs).
 cudaError_t launch_quantize(int kind, const float * x, int64_t K, int64_t M, uint8_t * gguf, int8_t * q, float * d, int16_t * bs,
                             cudaStream_t st);
+// Tensor-core Q8_0 GEMM (gemm_tc.cu): x quantized to q (int8 [M][K]) and dx (float [M][K/32]).
+bool gemm_tc_supported(const WeightView & w, int64_t M);
+size_t gemm_tc_workspace_bytes(int64_t N, int64_t M);
+int64_t gemm_tc_tiles(int64_t N, int64_t M);
+cudaError_t launch_gemm_tc(const WeightView & w, int64_t row0, int64_t N, const int8_t * q, const float * dx, int64_t M, float * y,
+                           int64_t ldy, unsigned * err, void * ws, size_t ws_bytes, unsigned * tickets, int num_sms, cudaStream_t st);
 cudaError_t launch_route(const int32_t * ids, int64_t T, int64_t top_k, int64_t nb1, int64_t E, int32_t * grp_off,
                          int32_t * col_src, int32_t * col_dst, unsigned * err, cudaStream_t st);
 

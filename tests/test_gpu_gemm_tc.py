@@ -1,0 +1,46 @@
+"""Q8_0 products with M >= 32 activation rows take the int8 tensor-core path (tcgen05.mma kind::i8, TMEM accumulators,
+TMA operands, optional split-K). Same bar as every product: |err| <= 1e-4 * sum |w x| per element against the oracle."""
+
+import numpy as np
+import pytest
+
+from conftest import load_package
+
+pytestmark = pytest.mark.gpu
+
+CASES = [
+    (256, 128, 32),     # one tile, one stage
+    (1024, 3072, 64),   # config 4-like rows, split-K
+    (2048, 1000, 100),  # ragged rows and tokens
+    (6144, 2048, 64),   # config 4's down projection
+    (2048, 384, 257),   # several token tiles
+]
+
+
+@pytest.mark.parametrize("K,N,M", CASES)
+def test_q8_0_tensor_core_products(oracle, K, N, M):
+    import torch
+
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    b200 = load_package()
+    ctx = b200.Context(0)
+    try:
+        rng = np.random.default_rng(K + N + M)
+        wb = oracle.quantize(8, rng.normal(0, 0.02, size=(N, K)).astype(np.float32))
+        x = rng.normal(0, 1, size=(M, K)).astype(np.float32)
+        w = ctx.weight(8, K, N, data=wb)
+        got = ctx.mul_mat(w, torch.from_numpy(x).cuda()).cpu().numpy()
+        ctx.synchronize()
+        want = oracle.mul_mat(8, wb, K, N, x)
+        wd = oracle.dequantize(8, wb, K).astype(np.float64)
+        xd = oracle.dequantize(8, oracle.quantize(8, x), K).astype(np.float64)
+        bound = 1e-4 * (np.abs(xd) @ np.abs(wd).T) + 1e-30
+        err = np.abs(got.astype(np.float64) - want)
+        assert np.all(err <= bound), f"max err/bound {np.max(err / bound):.3g}"
+        # run again: split-K tickets were left at zero, results are identical
+        again = ctx.mul_mat(w, torch.from_numpy(x).cuda()).cpu().numpy()
+        assert np.array_equal(again, got)
+        ctx.free_weight(w)
+    finally:
+        ctx.close()
