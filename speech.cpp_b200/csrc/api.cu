@@ -145,7 +145,7 @@ b200_status mul_mat_impl(b200_context * ctx, const b200_weight * w, int64_t row0
     // Many columns of Q8_0: int8 tensor cores (tcgen05) over the once-quantized activations.
     if (gemm_tc_supported(p.w, M)) {
         const int64_t tiles = gemm_tc_tiles(n, M);
-        const size_t qb = quantized_act_bytes(kind, K, M), wsb = gemm_tc_workspace_bytes(n, M);
+        const size_t qb = quantized_act_bytes(kind, K, M + 4), wsb = gemm_tc_workspace_bytes(n, M);
         b200_status s = ensure_scratch(ctx, qb + wsb + 256);
         if (s != B200_OK) return s;
         if ((size_t) tiles > ctx->ntickets) {
@@ -160,9 +160,10 @@ b200_status mul_mat_impl(b200_context * ctx, const b200_weight * w, int64_t row0
         }
         Carve c{(uint8_t *) ctx->scratch};
         int8_t * q = c.take<int8_t>((size_t) M * K);
-        float * d = c.take<float>((size_t) M * (K / 32));
+        const int64_t ld = gemm_tc_dx_ld(M);
+        float * d = c.take<float>((size_t) ld * (K / 32));
         void * ws = c.take<uint8_t>(wsb);
-        CK(ctx, launch_quantize(kind, x, K, M, nullptr, q, d, nullptr, ctx->stream));
+        CK(ctx, launch_quantize(kind, x, K, M, nullptr, q, d, nullptr, ctx->stream, ld));
         const cudaError_t e = launch_gemm_tc(p.w, row0, n, q, d, M, dst, ld_dst, ctx->dev_err, ws, wsb, ctx->tickets, ctx->num_sms,
                                              ctx->stream);
         if (e == cudaSuccess) return B200_OK;

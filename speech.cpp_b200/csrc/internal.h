@@ -45,8 +45,10 @@ cudaError_t launch_repack(int type, const b200_weight * w, const uint8_t * src, 
 cudaError_t launch_get_rows(const WeightView & w, const int32_t * ids, int64_t n, float * dst, unsigned * err, cudaStream_t st);
 // Activation quantization: gguf != null writes GGUF blocks there; else the internal layout (q, d, bs).
 cudaError_t launch_quantize(int kind, const float * x, int64_t K, int64_t M, uint8_t * gguf, int8_t * q, float * d, int16_t * bs,
-                            cudaStream_t st);
-// Tensor-core Q8_0 GEMM (gemm_tc.cu): x quantized to q (int8 [M][K]) and dx (float [M][K/32]).
+                            cudaStream_t st, int64_t dT_ld = 0);
+// Tensor-core Q8_0 GEMM (gemm_tc.cu): x quantized to q (int8 [M][K]) and dxT (float [K/32][gemm_tc_dx_ld(M)], the
+// block scales transposed so that one block's scales of all tokens are contiguous).
+int64_t gemm_tc_dx_ld(int64_t M);
 bool gemm_tc_supported(const WeightView & w, int64_t M);
 size_t gemm_tc_workspace_bytes(int64_t N, int64_t M);
 int64_t gemm_tc_tiles(int64_t N, int64_t M);

@@ -128,7 +128,7 @@ cudaError_t launch_get_rows(const WeightView & w, const int32_t * ids, int64_t n
 // Activation quantization (one warp per block)
 // ------------------------------------------------------------------------------------------------------------------
 __global__ void quantize_act_kernel(int kind, const float * __restrict__ x, int64_t K, int64_t M, uint8_t * gguf, int8_t * q,
-                                    float * d, int16_t * bs) {
+                                    float * d, int16_t * bs, int64_t dT_ld) {
     const int lane = threadIdx.x & 31;
     const int64_t warps = (int64_t) gridDim.x * (blockDim.x >> 5);
     const int64_t bsz = kind == B200_TYPE_Q8_0 ? 32 : 256;
@@ -146,7 +146,10 @@ __global__ void quantize_act_kernel(int kind, const float * __restrict__ x, int6
                 if (lane == 0) *reinterpret_cast<uint16_t *>(blk) = dh;
             } else {
                 q[r * K + b * 32 + lane] = qv;
-                if (lane == 0) d[i] = df;
+                if (lane == 0) {
+                    if (dT_ld) d[b * dT_ld + r] = df;  // transposed: [K/32][dT_ld]
+                    else d[i] = df;
+                }
             }
         } else {
             float v[8];
@@ -173,13 +176,13 @@ __global__ void quantize_act_kernel(int kind, const float * __restrict__ x, int6
 }
 
 cudaError_t launch_quantize(int kind, const float * x, int64_t K, int64_t M, uint8_t * gguf, int8_t * q, float * d, int16_t * bs,
-                            cudaStream_t st) {
+                            cudaStream_t st, int64_t dT_ld) {
     const int64_t nb = M * (K / (kind == B200_TYPE_Q8_0 ? 32 : 256));
     if (nb <= 0) return cudaSuccess;
     const int threads = 256;
     int64_t blocks = (nb + 7) / 8;
     if (blocks > 148 * 8) blocks = 148 * 8;
-    quantize_act_kernel<<<(unsigned) blocks, threads, 0, st>>>(kind, x, K, M, gguf, q, d, bs);
+    quantize_act_kernel<<<(unsigned) blocks, threads, 0, st>>>(kind, x, K, M, gguf, q, d, bs, dT_ld);
     return cudaGetLastError();
 }
 
