@@ -268,6 +268,223 @@ def _random_kquant_blocks(t, rows, K, g):
     return b.reshape(-1)
 
 
+# ---------------------------------------------------------------------------------------------------------------------
+# Config 5: Drama3-like MoE FFN stack (TextModel::experts, src/families/drama3/text-model.cpp:198-221)
+# ---------------------------------------------------------------------------------------------------------------------
+MOE = {"n_expert": 128, "top_k": 8, "hidden": 2048, "ffn": 768, "n_layer": 48, "tokens": 256}
+MOE_METRIC = "MoE tok/s, Drama3-like MoE FFN stack (48 layers x 128 Q8_0 experts, top-8, 2048<->768), 256 tokens per step"
+
+
+def moe_routes(c, seed=11):
+    """Per layer: router logits N(0, 1) -> softmax -> top-k (ties broken by a seeded permutation of the experts)
+    -> weights renormalised over the chosen k. Returns ids int32 [L, T, k], w float32 [L, T, k]."""
+    import numpy as np
+
+    rng = np.random.default_rng(seed)
+    L, T, E, k = c["n_layer"], c["tokens"], c["n_expert"], c["top_k"]
+    ids = np.empty((L, T, k), dtype=np.int32)
+    w = np.empty((L, T, k), dtype=np.float32)
+    for l in range(L):
+        logits = rng.normal(0, 1, size=(T, E)).astype(np.float32)
+        p = np.exp(logits - logits.max(1, keepdims=True))
+        p /= p.sum(1, keepdims=True)
+        rank = rng.permutation(E)
+        order = np.lexsort((np.broadcast_to(rank, (T, E)), -p), axis=1)[:, :k]
+        ids[l] = order
+        sel = np.take_along_axis(p, order, 1)
+        w[l] = sel / sel.sum(1, keepdims=True)
+    return ids, w
+
+
+def moe_weights(pkg, ctx, c, e0, E_local):
+    """Layer weights of experts [e0, e0 + E_local): gate|up [H, 2F, E_local] and down [F, H, E_local], Q8_0. Each
+    expert's values are N(0, 0.02) from a generator seeded by (layer, expert), quantized on the device by the backend's
+    Q8_0 quantizer, so a shard holds exactly the bytes the same experts have on one GPU."""
+    import torch
+
+    H, F = c["hidden"], c["ffn"]
+    g = torch.Generator(device="cuda")
+    gus, dns = [], []
+    rs_gu, rs_dn = 2 * F * pkg.row_size(pkg.Q8_0, H), H * pkg.row_size(pkg.Q8_0, F)
+    for l in range(c["n_layer"]):
+        gu = ctx.weight(pkg.Q8_0, H, 2 * F, E_local)
+        dn = ctx.weight(pkg.Q8_0, F, H, E_local)
+        for j in range(E_local):
+            g.manual_seed(1_000_003 * l + e0 + j)
+            ctx.set_weight(gu, ctx.quantize_rows(pkg.Q8_0, torch.randn((2 * F, H), generator=g, device="cuda") * 0.02), offset=j * rs_gu)
+            ctx.set_weight(dn, ctx.quantize_rows(pkg.Q8_0, torch.randn((H, F), generator=g, device="cuda") * 0.02), offset=j * rs_dn)
+        gus.append(gu)
+        dns.append(dn)
+    ctx.synchronize()
+    return gus, dns
+
+
+class CpuMoe:
+    """The oracle's MoE layer (two MUL_MAT_ID products + SwiGLU + weighted sum) on one layer's worth of random valid
+    Q8_0 expert blocks, all host threads; tokens/s of the 48-layer step = 1 / (median layer time x 48)."""
+
+    def __init__(self, c):
+        import numpy as np
+
+        from oracle import oracle
+
+        self.o, self.c = oracle, c
+        rng = np.random.default_rng(17)
+        H, F, E = c["hidden"], c["ffn"], c["n_expert"]
+
+        def blocks(rows, K):
+            b = rng.integers(-127, 128, size=(rows * (K // 32), 34), dtype=np.int8).view(np.uint8)
+            b[:, :2] = (rng.random(rows * (K // 32)) * 2e-4 + 1e-4).astype(np.float16).view(np.uint8).reshape(-1, 2)
+            return b.reshape(rows, -1)
+
+        self.gu, self.dn = blocks(E * 2 * F, H), blocks(E * H, F)
+        self.x = rng.normal(0, 1, size=(c["tokens"], H)).astype(np.float32)
+        ids, w = moe_routes(dict(c, n_layer=1), seed=23)
+        self.ids, self.w = ids[0], w[0]
+        self.cores = oracle.max_threads()
+        self.t = []
+
+    def once(self):
+        import numpy as np
+
+        c, o = self.c, self.o
+        H, F, E = c["hidden"], c["ffn"], c["n_expert"]
+        a = time.perf_counter()
+        gu = o.mul_mat_id(o.Q8_0, self.gu, H, 2 * F, E, self.x[:, None, :], self.ids)
+        g, u = gu[..., :F], gu[..., F:]
+        act = (g / (np.float32(1.0) + np.exp(-g)) * u).astype(np.float32)
+        dn = o.mul_mat_id(o.Q8_0, self.dn, F, H, E, act, self.ids)
+        (dn * self.w[..., None]).sum(1)
+        self.t.append(time.perf_counter() - a)
+        return c["tokens"] / (self.t[-1] * c["n_layer"])
+
+    def rate(self):
+        return self.c["tokens"] / (statistics.median(self.t) * self.c["n_layer"])
+
+    def sample_text(self, reps):
+        return f"{reps} passes of 1 of the 48 MoE layers (128 experts, 256 tokens x top-8); median layer x 48"
+
+
+def run_moe(args, pkg, ctx, dist, world, rank, local):
+    """Expert parallelism: rank r holds experts [r E/N, (r+1) E/N) of every layer; activations and routes are
+    replicated (the router runs on every rank), so dispatch moves nothing; each rank's b200_moe_ffn leaves its
+    experts' partial sum and one all-reduce per layer combines them into the next layer's input. The 48-layer step
+    is captured in one CUDA graph. Strong scaling: the same 256 tokens per step at every N."""
+    import numpy as np
+    import torch
+
+    c = dict(MOE, n_layer=args.moe_layers)
+    E, T, H, k, L = c["n_expert"], c["tokens"], c["hidden"], c["top_k"], c["n_layer"]
+    if E % world:
+        raise SystemExit(f"{E} experts do not split over {world} GPUs")
+    E_local = E // world
+    e0 = rank * E_local
+    gus, dns = moe_weights(pkg, ctx, c, e0, E_local)
+    ids_h, w_h = moe_routes(c)
+    ids = torch.from_numpy(ids_h).cuda()
+    wts = torch.from_numpy(w_h).cuda()
+    xs = [torch.randn((T, H), generator=torch.Generator(device="cuda").manual_seed(7), device="cuda")]
+    xs += [torch.empty((T, H), device="cuda") for _ in range(L)]
+    stream = ctx.torch_stream()
+
+    def step():
+        for l in range(L):
+            ctx.moe_ffn(gus[l], dns[l], xs[l], ids[l], wts[l], expert0=e0, n_expert_total=E, out=xs[l + 1])
+            if dist:
+                dist.all_reduce(xs[l + 1])
+
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            step()
+    torch.cuda.synchronize()
+    ctx.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    torch.cuda.synchronize()
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize()
+
+    steps = args.moe_steps
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for _ in range(steps):
+                graph.replay()
+            ev1.record(stream)
+        ev1.synchronize()
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    if dist:
+        dist.barrier()
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / steps
+    value = T * steps / (ms / 1000.0)
+
+    # end to end: pinned host activations and routes in, the last layer's output out, every step
+    x_pin = torch.empty((T, H), pin_memory=True).copy_(xs[0].cpu())
+    ids_pin = torch.from_numpy(ids_h).pin_memory()
+    w_pin = torch.from_numpy(w_h).pin_memory()
+    out_pin = torch.empty((T, H), pin_memory=True)
+
+    def e2e_step():
+        with torch.cuda.stream(stream):
+            xs[0].copy_(x_pin, non_blocking=True)
+            ids.copy_(ids_pin, non_blocking=True)
+            wts.copy_(w_pin, non_blocking=True)
+            graph.replay()
+            out_pin.copy_(xs[L], non_blocking=True)
+        stream.synchronize()
+
+    for _ in range(2):
+        e2e_step()
+    if dist:
+        dist.barrier()
+    e0v, e1v = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0v.record(stream)
+    for _ in range(steps):
+        e2e_step()
+    e1v.record(stream)
+    e1v.synchronize()
+    ems = e0v.elapsed_time(e1v)
+    if dist:
+        dist.barrier()
+        t = torch.tensor([ems], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ems = float(t.item())
+    del graph
+    torch.cuda.synchronize()
+    wbytes = sum(w.nbytes for w in gus) + sum(w.nbytes for w in dns)
+    for w in gus + dns:
+        ctx.free_weight(w)
+    peak, peak_kind = peaks()
+    achieved = wbytes / (ms_step / 1000.0) / 1e9
+    res = {
+        "metric": MOE_METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": steps, "ms_per_step": ms_step,
+        "higher_is_better": True, "scaling": "strong", "dtype": "int8xint8->int32, f32 accumulate", "data": "synthetic",
+        "config": {"workload": f"config 5: {L} x b200_moe_ffn (gate|up 2048->1536, SwiGLU, down 768->2048, weighted sum) "
+                               "over 128 Q8_0 experts, top-8 of N(0,1) router logits, 256 N(0,1) tokens",
+                   "global_batch": T, "parallelism": f"expert-parallel x{world} (all-reduce of combined outputs)" if world > 1 else "single",
+                   "l2": f"expert weights {wbytes / 1e9:.1f} GB per GPU > 126 MB L2 (no flush needed)"},
+        "roofline": {"bound": "hbm", "kernel": "grouped gemv_kernel<TQ8_0> (gate|up and down of every layer)", "achieved": achieved,
+                     "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6650",
+                     "algorithmic_bytes_per_step": wbytes, "traffic": None},
+        "e2e": {"value": T * steps / (ems / 1000.0), "unit": UNIT, "h2d_bytes_per_step": T * H * 4 + ids_h.nbytes + w_h.nbytes,
+                "d2h_bytes_per_step": T * H * 4},
+        "gpu_launches": 6 * L * steps,
+        "clocks": clk.summary(),
+    }
+    return res
+
+
 def run_b200(args):
     import torch
 
@@ -289,6 +506,25 @@ def run_b200(args):
 
     pkg = load_package()
     ctx = pkg.Context(local)
+    if args.workload == "moe":
+        res = run_moe(args, pkg, ctx, dist, world, rank, local)
+        ctx.close()
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
+        if rank == 0:
+            res.update(warmup=args.warmup, vs_baseline=None)
+            if world == 1 and not args.no_cpu:
+                cm = CpuMoe(MOE)
+                cm.once()
+                t0 = time.perf_counter()
+                reps = 0
+                while time.perf_counter() - t0 < 12.0 or reps < 3:
+                    cm.once()
+                    reps += 1
+                res["cpu_baseline"] = {"value": cm.rate(), "unit": UNIT, "cores": cm.cores, "kind": "port", "sample": cm.sample_text(reps)}
+            print(json.dumps(res), flush=True)
+        return 0
     dec, c = make_decoder(pkg, ctx, seed=1234 + rank)
     stream = ctx.torch_stream()
     x = torch.randn(c["hidden"], generator=torch.Generator(device="cuda").manual_seed(7), device="cuda")
@@ -386,6 +622,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--workload", default="decode", choices=["decode", "moe"],
+                    help="decode: config 2 decode step (the headline line); moe: config 5 MoE FFN stack, expert-parallel")
+    ap.add_argument("--moe-steps", type=int, default=20, help="timed steps of the MoE workload")
+    ap.add_argument("--moe-layers", type=int, default=48, help="MoE layers per step (48 = config 5; fewer only for profiling)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)

@@ -134,6 +134,18 @@ b200_status b200_mul_mat_rows(b200_context * ctx, const b200_weight * w, int64_t
 b200_status b200_mul_mat_id(b200_context * ctx, const b200_weight * experts, const float * b, int64_t nb1,
                             const int32_t * ids, int64_t top_k, int64_t T, float * dst);
 
+/* The routed-expert block of a mixture-of-experts FFN, as TextModel::experts builds it from ggml nodes
+ * (src/families/drama3/text-model.cpp:198-221): for each token t and slot s with expert e = ids[t][s],
+ *   out[t] = sum over s (in slot order) of w[t][s] * Wdown_e (silu(Wgate_e x_t) * Wup_e x_t),
+ * with gate and up stored as one expert matrix: gate_up [H, 2F, E] (rows 0..F-1 gate, F..2F-1 up; any quantized
+ * type) and down [F, H, E] (Q8_0). x [T][H], ids int32 [T][top_k], w float [T][top_k] (the router's softmax weights,
+ * computed upstream), out [T][H]. Expert parallelism: these experts are experts [expert0, expert0 + E) of
+ * n_expert_total (0: all); pairs routed to other experts are skipped, so out is this shard's partial sum, and the
+ * shards' outputs add up to the full result. Ids outside [0, n_expert_total) are reported by b200_synchronize(). */
+b200_status b200_moe_ffn(b200_context * ctx, const b200_weight * gate_up, const b200_weight * down, int64_t expert0,
+                         int64_t n_expert_total, const float * x, const int32_t * ids, const float * w, int64_t top_k, int64_t T,
+                         float * out);
+
 /* GET_ROWS of a weight table (talker.cpp:131-133, decoder.cpp:319): dst [n][K] = dequantize(row ids[i]), bit for bit
  * as ggml's CPU dequantizers. An id outside [0, N * E) is skipped (its row is left untouched) and reported by
  * b200_synchronize() as B200_ERR_RANGE. */

@@ -32,7 +32,7 @@ EXPORTS = [
     "b200_weight_get", "b200_mul_mat", "b200_mul_mat_rows", "b200_mul_mat_id", "b200_get_rows", "b200_quantize_rows",
     "b200_block_sums", "b200_mul_mat_host", "b200_decoder_create", "b200_decoder_destroy", "b200_decoder_set_tensor",
     "b200_decoder_step", "b200_decoder_step_host", "b200_decoder_launches", "b200_decoder_weight_bytes",
-    "b200_decoder_set_launch", "b200_mul_mat_id_noalloc",
+    "b200_decoder_set_launch", "b200_mul_mat_id_noalloc", "b200_moe_ffn",
 ]
 
 DEC_ATTN_Q, DEC_ATTN_K, DEC_ATTN_V, DEC_ATTN_O, DEC_FFN_GATE, DEC_FFN_UP, DEC_FFN_DOWN = range(7)
@@ -130,6 +130,7 @@ def lib():
         "b200_decoder_weight_bytes": (sz, [vp]),
         "b200_decoder_set_launch": (i32, [vp, i32, i32, i32]),
         "b200_mul_mat_id_noalloc": (i32, [vp, W, vp, i64, vp, i64, i64, vp]),
+        "b200_moe_ffn": (i32, [vp, W, W, i64, i64, vp, vp, vp, i64, i64, vp]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -277,6 +278,19 @@ class Context:
         out = torch.empty((T, top_k, experts.ne1), dtype=torch.float32, device=b.device) if out is None else out
         self._sync_in()
         self.check(self.L.b200_mul_mat_id(self.h, ctypes.byref(experts), _ptr(b), nb1, _ptr(ids), top_k, T, _ptr(out)))
+        self._sync_out()
+        return out
+
+    def moe_ffn(self, gate_up, down, x, ids, w, expert0=0, n_expert_total=0, out=None):
+        """The routed-expert block of TextModel::experts: x float32 [T, H], ids int32 [T, top_k], w float32 [T, top_k]
+        -> [T, H] (this shard's partial sum when the experts are a shard)."""
+        import torch
+
+        T, top_k = ids.shape
+        out = torch.empty((T, gate_up.ne0), dtype=torch.float32, device=x.device) if out is None else out
+        self._sync_in()
+        self.check(self.L.b200_moe_ffn(self.h, ctypes.byref(gate_up), ctypes.byref(down), expert0, n_expert_total, _ptr(x), _ptr(ids),
+                                       _ptr(w), top_k, T, _ptr(out)))
         self._sync_out()
         return out
 

@@ -468,6 +468,77 @@ b200_status b200_mul_mat_id(b200_context * ctx, const b200_weight * experts, con
     return B200_OK;
 }
 
+b200_status b200_moe_ffn(b200_context * ctx, const b200_weight * gate_up, const b200_weight * down, int64_t expert0,
+                         int64_t n_expert_total, const float * x, const int32_t * ids, const float * w, int64_t top_k, int64_t T,
+                         float * out) {
+    if (!check_weight(ctx, gate_up) || !check_weight(ctx, down)) return fail(ctx, B200_ERR_INVALID, "moe_ffn: bad experts");
+    const int64_t H = gate_up->ne0, F2 = gate_up->ne1, E = gate_up->ne2, F = F2 / 2;
+    if (F2 % 2 || down->ne0 != F || down->ne1 != H || down->ne2 != E || F % 32)
+        return fail(ctx, B200_ERR_INVALID, "moe_ffn: gate_up must be [H, 2F, E] and down [F, H, E]");
+    if (down->type != B200_TYPE_Q8_0 || gate_up->type == B200_TYPE_F32 || gate_up->type == B200_TYPE_BF16)
+        return fail(ctx, B200_ERR_UNSUPPORTED, "moe_ffn: quantized gate_up and Q8_0 down experts");
+    if (top_k <= 0 || T < 0 || expert0 < 0 || (n_expert_total > 0 && expert0 + E > n_expert_total))
+        return fail(ctx, B200_ERR_INVALID, "moe_ffn: bad shape or expert range");
+    if (T == 0) return B200_OK;
+    if (!x || !ids || !w || !out) return fail(ctx, B200_ERR_INVALID, "moe_ffn: NULL argument");
+    const int64_t P = T * top_k, total = n_expert_total > 0 ? n_expert_total : E;
+    const int kind = act_kind(gate_up->type);
+    const int nc1 = gemv_max_columns(gate_up->type, H), nc2 = gemv_max_columns(down->type, F);
+    if (!nc1 || !nc2) return fail(ctx, B200_ERR_UNSUPPORTED, "moe_ffn: rows too long for the staging buffer");
+    auto up = [](size_t v) { return (v + 255) & ~(size_t) 255; };
+    const size_t need = up((size_t) (E + 1) * 4) + 3 * up((size_t) P * 4) + quantized_act_bytes(kind, H, T) + up((size_t) P * F2 * 4) +
+                        quantized_act_bytes(B200_TYPE_Q8_0, F, P) + up((size_t) P * H * 4);
+    b200_status s = ensure_scratch(ctx, need);
+    if (s != B200_OK) return s;
+    Carve c{(uint8_t *) ctx->scratch};
+    int32_t * grp_off = c.take<int32_t>((size_t) E + 1);
+    int32_t * col_src = c.take<int32_t>((size_t) P);
+    int32_t * col_dst = c.take<int32_t>((size_t) P);
+    int32_t * col_tok = c.take<int32_t>((size_t) P);
+    int8_t * xq = c.take<int8_t>((size_t) T * H);
+    float * xd = c.take<float>((size_t) T * (H / (kind == B200_TYPE_Q8_0 ? 32 : 256)));
+    int16_t * xbs = kind == B200_TYPE_Q8_K ? c.take<int16_t>((size_t) T * (H / 16)) : nullptr;
+    float * gu = c.take<float>((size_t) P * F2);
+    int8_t * aq = c.take<int8_t>((size_t) P * F);
+    float * ad = c.take<float>((size_t) P * (F / 32));
+    float * dn = c.take<float>((size_t) P * H);
+    cudaStream_t st = ctx->stream;
+    CK(ctx, launch_quantize(kind, x, H, T, nullptr, xq, xd, xbs, st));
+    CK(ctx, launch_route(ids, T, top_k, top_k, E, grp_off, col_src, col_dst, ctx->dev_err, st, expert0, total, col_tok));
+    // gate|up of every routed pair: rows p of gu
+    GemvParams p1 = base_params(ctx, gate_up);
+    p1.N = F2;
+    p1.x = x;
+    p1.ldx = H;
+    p1.aq = xq;
+    p1.ad = xd;
+    p1.abs = xbs;
+    p1.y = gu;
+    p1.ldy = F2;
+    p1.col_src = col_tok;
+    p1.col_dst = col_dst;
+    p1.grp_off = grp_off;
+    p1.grp_rows = F2;
+    CK(ctx, launch_gemv(p1, nc1, (int) E, st, false, ctx->num_sms));
+    CK(ctx, launch_swiglu_quant_pairs(gu, F, col_dst, grp_off + E, P, aq, ad, st));
+    // down of every routed pair: rows p of dn
+    GemvParams p2 = base_params(ctx, down);
+    p2.N = H;
+    p2.x = nullptr;
+    p2.ldx = F;
+    p2.aq = aq;
+    p2.ad = ad;
+    p2.y = dn;
+    p2.ldy = H;
+    p2.col_src = col_dst;
+    p2.col_dst = col_dst;
+    p2.grp_off = grp_off;
+    p2.grp_rows = H;
+    CK(ctx, launch_gemv(p2, nc2, (int) E, st, false, ctx->num_sms));
+    CK(ctx, launch_moe_combine(dn, w, ids, T, top_k, H, expert0, E, out, st));
+    return B200_OK;
+}
+
 b200_status b200_get_rows(b200_context * ctx, const b200_weight * table, const int32_t * ids, int64_t n, float * dst) {
     if (!check_weight(ctx, table)) return fail(ctx, B200_ERR_INVALID, "get_rows: bad table");
     if (n < 0 || (n > 0 && (!ids || !dst))) return fail(ctx, B200_ERR_INVALID, "get_rows: bad arguments");

@@ -55,6 +55,11 @@ int64_t gemm_tc_tiles(int64_t N, int64_t M);
 cudaError_t launch_gemm_tc(const WeightView & w, int64_t row0, int64_t N, const int8_t * q, const float * dx, int64_t M, float * y,
                            int64_t ldy, unsigned * err, void * ws, size_t ws_bytes, unsigned * tickets, int num_sms, cudaStream_t st);
 cudaError_t launch_route(const int32_t * ids, int64_t T, int64_t top_k, int64_t nb1, int64_t E, int32_t * grp_off,
-                         int32_t * col_src, int32_t * col_dst, unsigned * err, cudaStream_t st);
+                         int32_t * col_src, int32_t * col_dst, unsigned * err, cudaStream_t st, int64_t e0 = 0, int64_t total = 0,
+                         int32_t * col_tok = nullptr);
+cudaError_t launch_swiglu_quant_pairs(const float * gu, int64_t F, const int32_t * col_dst, const int32_t * n_pairs, int64_t max_pairs,
+                                      int8_t * q, float * d, cudaStream_t st);
+cudaError_t launch_moe_combine(const float * down, const float * w, const int32_t * ids, int64_t T, int64_t top_k, int64_t H, int64_t e0,
+                               int64_t E, float * out, cudaStream_t st);
 
 }  // namespace b200

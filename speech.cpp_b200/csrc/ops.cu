@@ -190,18 +190,22 @@ cudaError_t launch_quantize(int kind, const float * x, int64_t K, int64_t M, uin
 // MUL_MAT_ID routing: one CTA histograms the expert ids, scans, and places each (token, slot) pair in its expert's
 // segment. Pairs of one expert are independent products, so the order inside a segment does not change any result.
 // ------------------------------------------------------------------------------------------------------------------
-__global__ void route_kernel(const int32_t * __restrict__ ids, int64_t P, int64_t top_k, int64_t nb1, int E, int32_t * grp_off,
-                             int32_t * col_src, int32_t * col_dst, unsigned * err) {
+// With expert sharding (expert parallelism), this GPU holds experts [e0, e0 + E) of `total`: pairs routed to other
+// GPUs' experts are skipped; only ids outside [0, total) are errors. col_tok (optional) receives each pair's token.
+__global__ void route_kernel(const int32_t * __restrict__ ids, int64_t P, int64_t top_k, int64_t nb1, int E, int e0, int total,
+                             int32_t * grp_off, int32_t * col_src, int32_t * col_dst, int32_t * col_tok, unsigned * err) {
     extern __shared__ int cnt[];  // [E] counts, then [E] cursors
     int * pos = cnt + E;
     for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
     __syncthreads();
     for (int64_t p = threadIdx.x; p < P; p += blockDim.x) {
-        const int e = ids[p];
-        if (e < 0 || e >= E) {
+        const int g = ids[p];
+        if (g < 0 || g >= total) {
             atomicOr(err, B200_DEVERR_EXPERT);
             continue;
         }
+        const int e = g - e0;
+        if (e < 0 || e >= E) continue;
         atomicAdd(&cnt[e], 1);
     }
     __syncthreads();
@@ -227,18 +231,77 @@ __global__ void route_kernel(const int32_t * __restrict__ ids, int64_t P, int64_
     }
     __syncthreads();
     for (int64_t p = threadIdx.x; p < P; p += blockDim.x) {
-        const int e = ids[p];
-        if (e < 0 || e >= E) continue;
+        const int e = ids[p] - e0;
+        if (ids[p] < 0 || ids[p] >= total || e < 0 || e >= E) continue;
         const int slot = atomicAdd(&pos[e], 1);
         const int64_t t = p / top_k, s = p % top_k;
         col_src[slot] = (int32_t) (t * nb1 + (nb1 == 1 ? 0 : s));
         col_dst[slot] = (int32_t) p;
+        if (col_tok) col_tok[slot] = (int32_t) t;
     }
 }
 
 cudaError_t launch_route(const int32_t * ids, int64_t T, int64_t top_k, int64_t nb1, int64_t E, int32_t * grp_off,
-                         int32_t * col_src, int32_t * col_dst, unsigned * err, cudaStream_t st) {
-    route_kernel<<<1, 1024, (size_t) 2 * E * sizeof(int), st>>>(ids, T * top_k, top_k, nb1, (int) E, grp_off, col_src, col_dst, err);
+                         int32_t * col_src, int32_t * col_dst, unsigned * err, cudaStream_t st, int64_t e0, int64_t total,
+                         int32_t * col_tok) {
+    route_kernel<<<1, 1024, (size_t) 2 * E * sizeof(int), st>>>(ids, T * top_k, top_k, nb1, (int) E, (int) e0,
+                                                                 (int) (total > 0 ? total : E), grp_off, col_src, col_dst, col_tok, err);
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// MoE glue (TextModel::experts, src/families/drama3/text-model.cpp:198-221): SwiGLU of each routed pair's gate|up row,
+// quantized to q8_0 for the down product; and the router-weighted sum of a token's down rows, in slot order.
+// ------------------------------------------------------------------------------------------------------------------
+__global__ void swiglu_quant_pairs_kernel(const float * __restrict__ gu, int64_t F, const int32_t * __restrict__ col_dst,
+                                          const int32_t * __restrict__ n_pairs, int8_t * q, float * d) {
+    // one warp per (pair slot, 32-block); pairs come in routed order, their rows are the pair index p
+    const int lane = threadIdx.x & 31;
+    const int64_t nb = F / 32;
+    const int64_t total = (int64_t) (*n_pairs) * nb;
+    const int64_t warps = (int64_t) gridDim.x * (blockDim.x >> 5);
+    for (int64_t i = (int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); i < total; i += warps) {
+        const int64_t p = col_dst[i / nb], b = i % nb;
+        const float * row = gu + p * 2 * F;
+        const float v = __fmul_rn(silu(row[b * 32 + lane]), row[F + b * 32 + lane]);
+        float df;
+        uint16_t dh;
+        const int8_t qv = quantize_q8_0_lane(v, &df, &dh);
+        q[p * F + b * 32 + lane] = qv;
+        if (lane == 0) d[p * nb + b] = df;
+    }
+}
+
+__global__ void moe_combine_kernel(const float * __restrict__ down, const float * __restrict__ w, const int32_t * __restrict__ ids,
+                                   int64_t top_k, int64_t H, int e0, int E, float * __restrict__ out) {
+    const int64_t t = blockIdx.x;
+    for (int64_t h = threadIdx.x; h < H; h += blockDim.x) {
+        float sum = 0.0f;
+        bool any = false;
+        for (int64_t s = 0; s < top_k; s++) {
+            const int e = ids[t * top_k + s] - e0;
+            if (e < 0 || e >= E) continue;
+            const float v = __fmul_rn(down[(t * top_k + s) * H + h], w[t * top_k + s]);
+            sum = any ? __fadd_rn(sum, v) : v;
+            any = true;
+        }
+        out[t * H + h] = sum;
+    }
+}
+
+cudaError_t launch_swiglu_quant_pairs(const float * gu, int64_t F, const int32_t * col_dst, const int32_t * n_pairs, int64_t max_pairs,
+                                      int8_t * q, float * d, cudaStream_t st) {
+    int64_t blocks = (max_pairs * (F / 32) + 7) / 8;
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    if (blocks < 1) blocks = 1;
+    swiglu_quant_pairs_kernel<<<(unsigned) blocks, 256, 0, st>>>(gu, F, col_dst, n_pairs, q, d);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_moe_combine(const float * down, const float * w, const int32_t * ids, int64_t T, int64_t top_k, int64_t H, int64_t e0,
+                               int64_t E, float * out, cudaStream_t st) {
+    if (T <= 0) return cudaSuccess;
+    moe_combine_kernel<<<(unsigned) T, 256, 0, st>>>(down, w, ids, top_k, H, (int) e0, (int) E, out);
     return cudaGetLastError();
 }
 
@@ -264,7 +327,9 @@ static cudaError_t launch_one(const GemvParams & p, int grid_y, cudaStream_t st,
         ctas_per_sm = n > 0 ? n : 1;
     }
     const int warps_per_cta = kGemvThreads / 32;
-    int64_t gx = (p.N + warps_per_cta - 1) / warps_per_cta;
+    // expert groups: 64 rows per CTA, so one staging of an expert's activation columns serves many weight rows
+    const int rows_per_cta = grid_y > 1 ? 64 : warps_per_cta;
+    int64_t gx = (p.N + rows_per_cta - 1) / rows_per_cta;
     const int per_sm = cap_per_sm > 0 && cap_per_sm < ctas_per_sm ? cap_per_sm : ctas_per_sm;
     const int64_t cap = grid_y > 1 ? gx : (int64_t) num_sms * per_sm;
     if (gx > cap) gx = cap;
