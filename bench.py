@@ -375,11 +375,12 @@ def run_moe(args, pkg, ctx, dist, world, rank, local):
 
     c = dict(MOE, n_layer=args.moe_layers)
     E, T, H, k, L = c["n_expert"], c["tokens"], c["hidden"], c["top_k"], c["n_layer"]
-    if E % world:
-        raise SystemExit(f"{E} experts do not split over {world} GPUs")
-    E_local = E // world
-    e0 = rank * E_local
+    import importlib
+
+    ep = importlib.import_module(pkg.__name__ + ".expert_parallel")
+    e0, E_local = ep.expert_shard(E, world, rank)
     gus, dns = moe_weights(pkg, ctx, c, e0, E_local)
+    moe = ep.ExpertParallelMoe(ctx, zip(gus, dns), e0, E, group=dist.group.WORLD if dist else None)
     ids_h, w_h = moe_routes(c)
     ids = torch.from_numpy(ids_h).cuda()
     wts = torch.from_numpy(w_h).cuda()
@@ -388,10 +389,7 @@ def run_moe(args, pkg, ctx, dist, world, rank, local):
     stream = ctx.torch_stream()
 
     def step():
-        for l in range(L):
-            ctx.moe_ffn(gus[l], dns[l], xs[l], ids[l], wts[l], expert0=e0, n_expert_total=E, out=xs[l + 1])
-            if dist:
-                dist.all_reduce(xs[l + 1])
+        moe.step(xs, ids, wts)
 
     with torch.cuda.stream(stream):
         for _ in range(2):

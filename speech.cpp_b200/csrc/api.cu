@@ -424,6 +424,73 @@ b200_status b200_mul_mat_rows(b200_context * ctx, const b200_weight * w, int64_t
     return mul_mat_impl(ctx, w, row0, n, x, M, dst, ld_dst);
 }
 
+namespace {
+
+// Pairs from which MUL_MAT_ID of Q8_0 experts runs on the tensor cores (fewer: the grouped GEMV).
+constexpr int64_t kMoeTcMinPairs = 128;
+
+// Slot-ordered scratch of the tensor-core expert path, carved in a fixed order.
+struct MoeSlots {
+    int32_t * grp_off;
+    int32_t * col_src;
+    int32_t * col_dst;
+    int32_t * inv;
+    int4 * tiles;
+    int * ntiles;
+    int64_t max_slots;
+    static size_t bytes(int64_t P, int64_t E) {
+        auto up = [](size_t v) { return (v + 255) & ~(size_t) 255; };
+        const int64_t S = moe_max_slots(P, E);
+        return up((size_t) (E + 1) * 4) + 2 * up((size_t) S * 4) + up((size_t) P * 4) + up((size_t) moe_max_tiles(P, E) * 16) + 256;
+    }
+    void carve(Carve & c, int64_t P, int64_t E) {
+        max_slots = moe_max_slots(P, E);
+        grp_off = c.take<int32_t>((size_t) E + 1);
+        col_src = c.take<int32_t>((size_t) max_slots);
+        col_dst = c.take<int32_t>((size_t) max_slots);
+        inv = c.take<int32_t>((size_t) P);
+        tiles = c.take<int4>((size_t) moe_max_tiles(P, E));
+        ntiles = c.take<int>(1);
+    }
+};
+
+// The expert FFN on the tensor cores: route into padded slots, quantize x per slot, gate|up grouped GEMM, SwiGLU +
+// re-quantization per slot, down grouped GEMM, weighted combine. Both expert matrices Q8_0 with K % 256 == 0.
+b200_status moe_ffn_tc(b200_context * ctx, const b200_weight * gate_up, const b200_weight * down, int64_t expert0, int64_t total,
+                       const float * x, const int32_t * ids, const float * w, int64_t top_k, int64_t T, float * out) {
+    const int64_t H = gate_up->ne0, F2 = gate_up->ne1, E = gate_up->ne2, F = F2 / 2, P = T * top_k;
+    const int64_t S = moe_max_slots(P, E);
+    auto up = [](size_t v) { return (v + 255) & ~(size_t) 255; };
+    const size_t need = MoeSlots::bytes(P, E) + up((size_t) S * H) + up((size_t) (H / 32) * S * 4) + up((size_t) S * F2 * 4) +
+                        up((size_t) S * F) + up((size_t) (F / 32) * S * 4) + up((size_t) S * H * 4);
+    b200_status s = ensure_scratch(ctx, need);
+    if (s != B200_OK) return s;
+    Carve c{(uint8_t *) ctx->scratch};
+    MoeSlots m;
+    m.carve(c, P, E);
+    int8_t * q1 = c.take<int8_t>((size_t) S * H);
+    float * d1 = c.take<float>((size_t) (H / 32) * S);
+    float * gu = c.take<float>((size_t) S * F2);
+    int8_t * q2 = c.take<int8_t>((size_t) S * F);
+    float * d2 = c.take<float>((size_t) (F / 32) * S);
+    float * dn = c.take<float>((size_t) S * H);
+    cudaStream_t st = ctx->stream;
+    CK(ctx, launch_moe_route(ids, T, top_k, 1, E, expert0, total, m.grp_off, m.col_src, m.col_dst, m.inv, m.tiles, m.ntiles,
+                             ctx->dev_err, st));
+    CK(ctx, launch_moe_quant_slots(x, H, H, m.col_src, m.grp_off + E, S, q1, d1, S, ctx->num_sms, st));
+    cudaError_t e = launch_gemm_tc_grouped(view_of(gate_up), F2, m.tiles, m.ntiles, q1, d1, S, S, nullptr, gu, F2, ctx->dev_err,
+                                           ctx->num_sms, st);
+    if (e == cudaErrorInvalidValue) return B200_ERR_UNSUPPORTED;  // a tensor map the driver refused: the GEMV path runs
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "gemm_tc_grouped");
+    CK(ctx, launch_moe_swiglu_slots(gu, F, m.col_src, m.grp_off + E, S, q2, d2, S, ctx->num_sms, st));
+    e = launch_gemm_tc_grouped(view_of(down), H, m.tiles, m.ntiles, q2, d2, S, S, nullptr, dn, H, ctx->dev_err, ctx->num_sms, st);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "gemm_tc_grouped");
+    CK(ctx, launch_moe_combine_slots(dn, w, m.inv, T, top_k, H, out, st));
+    return B200_OK;
+}
+
+}  // namespace
+
 b200_status b200_mul_mat_id(b200_context * ctx, const b200_weight * experts, const float * b, int64_t nb1, const int32_t * ids,
                             int64_t top_k, int64_t T, float * dst) {
     if (!check_weight(ctx, experts)) return fail(ctx, B200_ERR_INVALID, "mul_mat_id: bad experts");
@@ -432,6 +499,26 @@ b200_status b200_mul_mat_id(b200_context * ctx, const b200_weight * experts, con
     if (T == 0) return B200_OK;
     if (!b || !ids || !dst) return fail(ctx, B200_ERR_INVALID, "mul_mat_id: NULL argument");
     const int64_t K = experts->ne0, N = experts->ne1, E = experts->ne2, P = T * top_k;
+    // Many pairs of Q8_0 experts: tensor cores over expert-sorted, slot-quantized activations.
+    if (P >= kMoeTcMinPairs && gemm_tc_grouped_supported(view_of(experts))) {
+        const int64_t S = moe_max_slots(P, E);
+        auto up = [](size_t v) { return (v + 255) & ~(size_t) 255; };
+        b200_status s = ensure_scratch(ctx, MoeSlots::bytes(P, E) + up((size_t) S * K) + up((size_t) (K / 32) * S * 4));
+        if (s != B200_OK) return s;
+        Carve c{(uint8_t *) ctx->scratch};
+        MoeSlots m;
+        m.carve(c, P, E);
+        int8_t * q = c.take<int8_t>((size_t) S * K);
+        float * d = c.take<float>((size_t) (K / 32) * S);
+        CK(ctx, launch_moe_route(ids, T, top_k, nb1, E, 0, E, m.grp_off, m.col_src, m.col_dst, m.inv, m.tiles, m.ntiles, ctx->dev_err,
+                                 ctx->stream));
+        CK(ctx, launch_moe_quant_slots(b, K, K, m.col_src, m.grp_off + E, S, q, d, S, ctx->num_sms, ctx->stream));
+        const cudaError_t e = launch_gemm_tc_grouped(view_of(experts), N, m.tiles, m.ntiles, q, d, S, S, m.col_dst, dst, N, ctx->dev_err,
+                                                     ctx->num_sms, ctx->stream);
+        if (e == cudaSuccess) return B200_OK;
+        if (e != cudaErrorInvalidValue) return cuda_fail(ctx, e, "gemm_tc_grouped");
+        // a tensor map the driver refused: the GEMV path below computes the same product
+    }
     const int kind = act_kind(experts->type);
     const int nc = gemv_max_columns(experts->type, K);
     if (nc == 0) return fail(ctx, B200_ERR_UNSUPPORTED, "mul_mat_id: rows too long for the staging buffer");
@@ -482,6 +569,10 @@ b200_status b200_moe_ffn(b200_context * ctx, const b200_weight * gate_up, const 
     if (T == 0) return B200_OK;
     if (!x || !ids || !w || !out) return fail(ctx, B200_ERR_INVALID, "moe_ffn: NULL argument");
     const int64_t P = T * top_k, total = n_expert_total > 0 ? n_expert_total : E;
+    if (gemm_tc_grouped_supported(view_of(gate_up)) && gemm_tc_grouped_supported(view_of(down)) && F % 256 == 0) {
+        b200_status s = moe_ffn_tc(ctx, gate_up, down, expert0, total, x, ids, w, top_k, T, out);
+        if (s != B200_ERR_UNSUPPORTED) return s;
+    }
     const int kind = act_kind(gate_up->type);
     const int nc1 = gemv_max_columns(gate_up->type, H), nc2 = gemv_max_columns(down->type, F);
     if (!nc1 || !nc2) return fail(ctx, B200_ERR_UNSUPPORTED, "moe_ffn: rows too long for the staging buffer");

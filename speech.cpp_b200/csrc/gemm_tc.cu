@@ -13,14 +13,12 @@
 // last to finish (an atomic ticket) adds the S partials in split order, so results do not depend on timing.
 // Every wait is bounded; one that gives up records B200_DEVERR_TIMEOUT and the CTA runs to its end (freeing its
 // tensor memory) without further waits.
-#include <cuda.h>
-#include <cudaTypedefs.h>
-
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
 
 #include "internal.h"
+#include "tcgen05.cuh"
 
 namespace b200 {
 
@@ -60,24 +58,6 @@ struct TcParams {
     unsigned * tickets;  // one per tile, zero between launches
 };
 
-__device__ __forceinline__ void tma_load_2d(void * dst, const CUtensorMap * map, int c0, int c1, uint64_t * bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            smem_addr(dst)),
-        "l"(map), "r"(c0), "r"(c1), "r"(smem_addr(bar))
-        : "memory");
-}
-
-// Shared-memory matrix descriptor of one K = 32 slice of a K-major tile whose rows are 128 bytes (four K blocks),
-// written by TMA with 128-byte swizzle into a 1024-byte-aligned tile: start address (tile + 32 * block) >> 4, leading
-// byte offset 16 B (unused by swizzled K-major layouts), stride byte offset 1024 B (eight 128-byte rows), descriptor
-// version 1, layout SWIZZLE_128B (2). The swizzle is a function of the address bits, so stepping the start address
-// by 32 bytes inside the atom selects the next K block.
-__device__ __forceinline__ uint64_t smem_desc_sw128(const void * tile, int block) {
-    const uint64_t a = (uint64_t) ((smem_addr(tile) + 32 * block) & 0x3FFFF) >> 4;
-    return a | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
-}
-
 // Phase timestamps for latency studies, compiled in only with -DB200_TC_PROBE: tc_probe[cta][block][4].
 #ifdef B200_TC_PROBE
 __device__ long long * tc_probe_buf;
@@ -86,41 +66,6 @@ __device__ long long * tc_probe_buf;
 #else
 #define TC_PROBE(blk, slot) do { } while (0)
 #endif
-
-// Instruction descriptor of tcgen05.mma kind::i8: D s32, A s8, B s8, both K-major, N = NT, M = 128.
-template <int NT>
-__device__ __forceinline__ uint32_t idesc_i8() {
-    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t) (NT >> 3) << 17) | ((uint32_t) (kTcM >> 4) << 24);
-}
-
-__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, 0, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(idesc)
-        : "memory");
-}
-
-__device__ __forceinline__ void mma_commit(uint64_t * bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// 32 lanes x 32 columns of 32-bit values from tensor memory (this warp's lane quarter), one column per register.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, int * r) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,"
-        "%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]),
-          "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
-          "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
-          "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-}
-
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 template <int NT>
 __global__ void __launch_bounds__(kTcThreads, 2)
@@ -314,6 +259,52 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     }
 }
 
+template <int NT>
+cudaError_t launch_nt(const WeightView & w, int64_t row0, int64_t N, const int8_t * q, const float * dx, int64_t dx_ld, int64_t M,
+                      float * y, int64_t ldy, unsigned * err, void * ws, size_t ws_bytes, unsigned * tickets, int num_sms, cudaStream_t st) {
+    using L = TcLayout<NT>;
+    const int64_t K = w.K, KB = K / 32;
+    CUtensorMap ta, tb, tdw, tdx;
+    if (!make_map_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.f0, (uint64_t) K, (uint64_t) w.rows, (uint64_t) K, 128, kTcM,
+                     CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, q, (uint64_t) K, (uint64_t) M, (uint64_t) K, 128, NT, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map_2d(&tdw, CU_TENSOR_MAP_DATA_TYPE_UINT16, w.f1, (uint64_t) KB, (uint64_t) w.rows, (uint64_t) KB * 2, kTcKB, kTcM,
+                     CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !make_map_2d(&tdx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, dx, (uint64_t) M, (uint64_t) KB, (uint64_t) dx_ld * 4, NT, kTcKB,
+                     CU_TENSOR_MAP_SWIZZLE_NONE))
+        return cudaErrorInvalidValue;
+    const int tn = (int) ((N + kTcM - 1) / kTcM), tm = (int) ((M + NT - 1) / NT);
+    const int stages_total = (int) (KB / kTcKB);
+    // split K (in whole stages, dividing them evenly) while the grid still fits one wave of two CTAs per SM
+    int splits = 1;
+    while (splits * 2 <= stages_total && (int64_t) tn * tm * splits * 2 <= 2 * (int64_t) num_sms && stages_total % (splits * 2) == 0)
+        splits *= 2;
+    const size_t ws_need = splits > 1 ? (size_t) tn * tm * splits * NT * kTcM * 4 : 0;
+    if (ws_need > ws_bytes || !tickets) splits = 1;
+    TcParams p;
+    p.N = N;
+    p.M = M;
+    p.K = K;
+    p.row0 = row0;
+    p.y = y;
+    p.ldy = ldy;
+    p.err = err;
+    p.splits = splits;
+    p.kb_per_split = (int) (KB / splits);
+    p.ws = splits > 1 ? (float *) ws : nullptr;
+    p.tickets = splits > 1 ? tickets : nullptr;
+    static int configured = 0;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_q8_0_tc_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
+        if (e != cudaSuccess) return e;
+        configured = 1;
+    }
+    gemm_q8_0_tc_kernel<NT><<<dim3(tn, tm, splits), kTcThreads, L::kTotal, st>>>(ta, tb, tdw, tdx, p);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     static std::once_flag once;
@@ -381,51 +372,7 @@ bool make_map_2d_uncached(CUtensorMap * m, CUtensorMapDataType dt, const void * 
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int NT>
-cudaError_t launch_nt(const WeightView & w, int64_t row0, int64_t N, const int8_t * q, const float * dx, int64_t dx_ld, int64_t M,
-                      float * y, int64_t ldy, unsigned * err, void * ws, size_t ws_bytes, unsigned * tickets, int num_sms, cudaStream_t st) {
-    using L = TcLayout<NT>;
-    const int64_t K = w.K, KB = K / 32;
-    CUtensorMap ta, tb, tdw, tdx;
-    if (!make_map_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.f0, (uint64_t) K, (uint64_t) w.rows, (uint64_t) K, 128, kTcM,
-                     CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !make_map_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, q, (uint64_t) K, (uint64_t) M, (uint64_t) K, 128, NT, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !make_map_2d(&tdw, CU_TENSOR_MAP_DATA_TYPE_UINT16, w.f1, (uint64_t) KB, (uint64_t) w.rows, (uint64_t) KB * 2, kTcKB, kTcM,
-                     CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !make_map_2d(&tdx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, dx, (uint64_t) M, (uint64_t) KB, (uint64_t) dx_ld * 4, NT, kTcKB,
-                     CU_TENSOR_MAP_SWIZZLE_NONE))
-        return cudaErrorInvalidValue;
-    const int tn = (int) ((N + kTcM - 1) / kTcM), tm = (int) ((M + NT - 1) / NT);
-    const int stages_total = (int) (KB / kTcKB);
-    // split K (in whole stages, dividing them evenly) while the grid still fits one wave of two CTAs per SM
-    int splits = 1;
-    while (splits * 2 <= stages_total && (int64_t) tn * tm * splits * 2 <= 2 * (int64_t) num_sms && stages_total % (splits * 2) == 0)
-        splits *= 2;
-    const size_t ws_need = splits > 1 ? (size_t) tn * tm * splits * NT * kTcM * 4 : 0;
-    if (ws_need > ws_bytes || !tickets) splits = 1;
-    TcParams p;
-    p.N = N;
-    p.M = M;
-    p.K = K;
-    p.row0 = row0;
-    p.y = y;
-    p.ldy = ldy;
-    p.err = err;
-    p.splits = splits;
-    p.kb_per_split = (int) (KB / splits);
-    p.ws = splits > 1 ? (float *) ws : nullptr;
-    p.tickets = splits > 1 ? tickets : nullptr;
-    static int configured = 0;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_q8_0_tc_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
-        if (e != cudaSuccess) return e;
-        configured = 1;
-    }
-    gemm_q8_0_tc_kernel<NT><<<dim3(tn, tm, splits), kTcThreads, L::kTotal, st>>>(ta, tb, tdw, tdx, p);
-    return cudaGetLastError();
-}
-
-}  // namespace
+bool tensor_maps_available() { return encode_fn() != nullptr; }
 
 bool gemm_tc_supported(const WeightView & w, int64_t M) {
     return w.type == B200_TYPE_Q8_0 && M >= 32 && w.K % (32 * kTcKB) == 0 && w.K <= (int64_t) 1 << 30 && encode_fn() != nullptr;

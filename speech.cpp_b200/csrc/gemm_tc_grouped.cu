@@ -1,0 +1,299 @@
+// gemm_tc_grouped.cu — expert-grouped Q8_0 products (MUL_MAT_ID, the MoE FFN of TextModel::experts,
+// src/families/drama3/text-model.cpp:198-221) on the tensor cores.
+//
+// The (token, slot) pairs are sorted by expert (moe.cu): expert e's pairs occupy slots [grp_off[e], grp_off[e+1]),
+// each segment padded to a multiple of 16 slots, and the pairs' activations are quantized to q8_0 in slot order
+// (q [slots][K] int8, dT [K/32][ldP] float block scales, transposed). A token tile is up to 64 consecutive slots of one
+// expert; the route kernel lists the tiles. One work item = one token tile x one 128-row tile of the expert's weight
+// matrix. Per 32-wide K block, one tcgen05.mma kind::i8 of shape M = 128 (weight rows) x N = the tile's token count
+// (16..64, a run-time field of the instruction descriptor) x K = 32 computes the block's exact int32 sums into one of
+// four tensor-memory buffers; epilogue warps read them (tcgen05.ld), scale them by d_w[row][b] * d_x[slot][b] and add
+// them to float32 registers in block order, as ggml's CPU vec_dot does. Operands come by TMA (2-D tensor maps, 128-byte
+// swizzle, no multicast). The grid is persistent (two CTAs per SM) and walks the items in a fixed order; every role of
+// a CTA derives the same item sequence from the tile list, so they need no other coordination than the stage and
+// accumulator barriers. Warp roles: 0 = TMA producer, 1 = tensor-memory allocator and MMA issuer (one thread),
+// 2..9 = epilogue. Every wait is bounded; one that gives up records B200_DEVERR_TIMEOUT and the CTA runs to its end
+// (freeing its tensor memory) without further waits.
+#include "internal.h"
+#include "tcgen05.cuh"
+
+namespace b200 {
+
+namespace {
+
+constexpr int kGM = 128;       // weight rows per tile (MMA M)
+constexpr int kGKB = 8;        // 32-wide K blocks per pipeline stage
+constexpr int kGStages = 2;
+constexpr int kGThreads = 320; // producer, MMA, 8 epilogue warps
+constexpr int kGEpiWarps = 8;
+constexpr int kGBufs = 4;      // tensor-memory accumulators in flight, kGNT columns each
+constexpr int kGNT = 64;       // slots per token tile (largest MMA N used)
+constexpr unsigned kErrTimeout = 4u;
+
+struct GLayout {
+    static constexpr int kA = kGKB * kGM * 32;   // weights: two [128 rows][128 B] swizzled tiles
+    static constexpr int kB = kGKB * kGNT * 32;  // activations: two [64 rows][128 B] swizzled tiles
+    static constexpr int kDw = kGM * kGKB * 2;   // fp16 weight scales [128][8]
+    static constexpr int kDx = kGKB * kGNT * 4;  // f32 activation scales [8][64]
+    static constexpr int kStage = kA + kB + kDw + kDx;
+    static constexpr int kTotal = kGStages * kStage + 1024 + 1024;  // + barriers + alignment slack
+    static_assert(kA % 1024 == 0 && kB % 1024 == 0 && kStage % 1024 == 0, "stage regions stay 1024-aligned");
+};
+
+struct GroupedParams {
+    int64_t N;                // rows per expert (output width)
+    int64_t K;
+    const int4 * tiles;       // {expert, first slot, slots (multiple of 16, <= 64), 0}
+    const int * ntiles;       // number of tiles (device)
+    int tiles_n;              // 128-row tiles per expert
+    const int32_t * row_map;  // output row of each slot (< 0: none); null: the slot itself
+    float * y;
+    int64_t ldy;
+    unsigned * err;
+};
+
+__global__ void __launch_bounds__(kGThreads, 2)
+    gemm_q8_0_tc_grouped_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                                const __grid_constant__ CUtensorMap tmDw, const __grid_constant__ CUtensorMap tmDx, GroupedParams p) {
+    using L = GLayout;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t * smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t) 1023);
+    uint64_t * bars = reinterpret_cast<uint64_t *>(smem + kGStages * L::kStage);
+    uint64_t * full = bars;
+    uint64_t * empty = bars + kGStages;
+    uint64_t * acc_full = bars + 2 * kGStages;
+    uint64_t * acc_empty = acc_full + kGBufs;
+    uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + kGBufs);
+    __shared__ volatile int give_up;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nstage = (int) (p.K / 32 / kGKB);
+    const int items = *p.ntiles * p.tiles_n;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kGStages; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1 + kGEpiWarps);
+        }
+        for (int b = 0; b < kGBufs; b++) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], kGEpiWarps);
+        }
+        fence_mbar_init();
+        give_up = 0;
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)), "r"(kGBufs * kGNT));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---- TMA producer ----
+        if (lane == 0) {
+            int sg = 0;
+            for (int it = blockIdx.x; it < items && !give_up; it += gridDim.x) {
+                const int4 t = p.tiles[it / p.tiles_n];
+                const int arow = (int) ((int64_t) t.x * p.N + (int64_t) (it % p.tiles_n) * kGM);
+                const int nsub = t.z / 16;
+                const uint32_t bytes = (uint32_t) (L::kA + t.z * 256 + L::kDw + L::kDx);
+                for (int st = 0; st < nstage; st++, sg++) {
+                    const int s = sg % kGStages, use = sg / kGStages;
+                    if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) {
+                        atomicOr(p.err, kErrTimeout);
+                        give_up = 1;
+                        break;
+                    }
+                    uint8_t * base = smem + s * L::kStage;
+                    mbar_arrive_expect_tx(&full[s], bytes);
+                    const int kbs = st * kGKB;
+                    for (int jj = 0; jj < 2; jj++) {
+                        tma_load_2d(base + jj * kGM * 128, &tmA, (kbs + 4 * jj) * 32, arow, &full[s]);
+                        for (int r = 0; r < nsub; r++)
+                            tma_load_2d(base + L::kA + jj * kGNT * 128 + r * 16 * 128, &tmB, (kbs + 4 * jj) * 32, t.y + 16 * r, &full[s]);
+                    }
+                    tma_load_2d(base + L::kA + L::kB, &tmDw, kbs, arow, &full[s]);
+                    tma_load_2d(base + L::kA + L::kB + L::kDw, &tmDx, t.y, kbs, &full[s]);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---- MMA issuer: one K block per MMA, into tensor-memory buffer b % 4 ----
+        if (lane == 0) {
+            int sg = 0, b = 0;
+            for (int it = blockIdx.x; it < items && !give_up; it += gridDim.x) {
+                const int4 t = p.tiles[it / p.tiles_n];
+                const uint32_t idesc = idesc_i8_n(t.z);
+                for (int st = 0; st < nstage && !give_up; st++, sg++) {
+                    const int s = sg % kGStages;
+                    if (!mbar_wait(&full[s], (sg / kGStages) & 1)) {
+                        atomicOr(p.err, kErrTimeout);
+                        give_up = 1;
+                        break;
+                    }
+                    tc_fence_after();
+                    uint8_t * base = smem + s * L::kStage;
+                    for (int j = 0; j < kGKB; j++, b++) {
+                        const int buf = b % kGBufs, use = b / kGBufs;
+                        if (use > 0 && !mbar_wait(&acc_empty[buf], (use - 1) & 1)) {
+                            atomicOr(p.err, kErrTimeout);
+                            give_up = 1;
+                            break;
+                        }
+                        tc_fence_after();
+                        mma_i8(tmem + buf * kGNT, smem_desc_sw128(base + (j / 4) * kGM * 128, j % 4),
+                               smem_desc_sw128(base + L::kA + (j / 4) * kGNT * 128, j % 4), idesc);
+                        mma_commit(&acc_full[buf]);
+                    }
+                    if (give_up) break;
+                    mma_commit(&empty[s]);
+                }
+            }
+        }
+    } else {
+        // ---- epilogue: lane quarter q = warp % 4 owns tile rows 32 q .. 32 q + 31 (one per lane); warp half h takes
+        // the 16-slot column chunks h and h + 2 of the tile ----
+        const int q = warp & 3, h = (warp - 2) >> 2;
+        const int row = 32 * q + lane;
+        const float2 neg_magic = make_float2(-12582912.0f, -12582912.0f);
+        int sg = 0, b = 0;
+        for (int it = blockIdx.x; it < items && !give_up; it += gridDim.x) {
+            const int4 t = p.tiles[it / p.tiles_n];
+            const int tn = it % p.tiles_n;
+            const int nch = t.z / 16;
+            const bool has0 = h < nch, has1 = h + 2 < nch;
+            float2 acc[16];
+#pragma unroll
+            for (int i = 0; i < 16; i++) acc[i] = make_float2(0.0f, 0.0f);
+            for (int st = 0; st < nstage && !give_up; st++, sg++) {
+                const int s = sg % kGStages;
+                const uint8_t * base = smem + s * L::kStage;
+                const __half * dw = reinterpret_cast<const __half *>(base + L::kA + L::kB);
+                const float * dxT = reinterpret_cast<const float *>(base + L::kA + L::kB + L::kDw);
+                for (int j = 0; j < kGKB; j++, b++) {
+                    const int buf = b % kGBufs, use = b / kGBufs;
+                    if (!mbar_wait(&acc_full[buf], use & 1)) {
+                        if (lane == 0) atomicOr(p.err, kErrTimeout);
+                        give_up = 1;
+                        break;
+                    }
+                    tc_fence_after();
+                    int v0[16], v1[16];
+                    const uint32_t ta = tmem + ((uint32_t) (32 * q) << 16) + buf * kGNT;
+                    if (has0) tmem_ld16(ta + 16 * h, v0);
+                    if (has1) tmem_ld16(ta + 16 * (h + 2), v1);
+                    tmem_wait_ld();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&acc_empty[buf]);
+                    // acc += float(sum) * (d_x * d_w); |sum| <= 32 * 127 * 128 < 2^22 converts exactly through the
+                    // float 12582912 + sum (bit pattern 0x4B400000 + sum)
+                    const float dwr = __half2float(dw[row * kGKB + j]);
+                    const float2 w2 = make_float2(dwr, dwr);
+                    if (has0) {
+                        const float4 * dx4 = reinterpret_cast<const float4 *>(dxT + j * kGNT + 16 * h);
+#pragma unroll
+                        for (int t4 = 0; t4 < 4; t4++) {
+                            const float4 d = dx4[t4];
+                            const float2 s01 = __fmul2_rn(make_float2(d.x, d.y), w2);
+                            const float2 s23 = __fmul2_rn(make_float2(d.z, d.w), w2);
+                            const float2 f01 = __fadd2_rn(
+                                make_float2(__int_as_float(v0[4 * t4] + 0x4B400000), __int_as_float(v0[4 * t4 + 1] + 0x4B400000)), neg_magic);
+                            const float2 f23 = __fadd2_rn(
+                                make_float2(__int_as_float(v0[4 * t4 + 2] + 0x4B400000), __int_as_float(v0[4 * t4 + 3] + 0x4B400000)), neg_magic);
+                            acc[2 * t4] = __ffma2_rn(f01, s01, acc[2 * t4]);
+                            acc[2 * t4 + 1] = __ffma2_rn(f23, s23, acc[2 * t4 + 1]);
+                        }
+                    }
+                    if (has1) {
+                        const float4 * dx4 = reinterpret_cast<const float4 *>(dxT + j * kGNT + 16 * (h + 2));
+#pragma unroll
+                        for (int t4 = 0; t4 < 4; t4++) {
+                            const float4 d = dx4[t4];
+                            const float2 s01 = __fmul2_rn(make_float2(d.x, d.y), w2);
+                            const float2 s23 = __fmul2_rn(make_float2(d.z, d.w), w2);
+                            const float2 f01 = __fadd2_rn(
+                                make_float2(__int_as_float(v1[4 * t4] + 0x4B400000), __int_as_float(v1[4 * t4 + 1] + 0x4B400000)), neg_magic);
+                            const float2 f23 = __fadd2_rn(
+                                make_float2(__int_as_float(v1[4 * t4 + 2] + 0x4B400000), __int_as_float(v1[4 * t4 + 3] + 0x4B400000)), neg_magic);
+                            acc[8 + 2 * t4] = __ffma2_rn(f01, s01, acc[8 + 2 * t4]);
+                            acc[8 + 2 * t4 + 1] = __ffma2_rn(f23, s23, acc[8 + 2 * t4 + 1]);
+                        }
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[s]);
+            }
+            if (give_up) break;
+            // ---- output: one weight row per lane, so each slot's store is one coalesced 128-byte line ----
+            const int64_t grow = (int64_t) tn * kGM + row;
+            if (grow < p.N) {
+#pragma unroll
+                for (int c = 0; c < 2; c++) {
+                    if (!(c == 0 ? has0 : has1)) continue;
+                    const int col0 = 16 * (h + 2 * c);
+#pragma unroll
+                    for (int i = 0; i < 16; i++) {
+                        const int slot = t.y + col0 + i;
+                        const int64_t orow = p.row_map ? (int64_t) p.row_map[slot] : (int64_t) slot;
+                        const float2 a = acc[8 * c + i / 2];
+                        if (orow >= 0) p.y[orow * p.ldy + grow] = (i & 1) ? a.y : a.x;
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kGBufs * kGNT));
+    }
+}
+
+}  // namespace
+
+bool gemm_tc_grouped_supported(const WeightView & w) {
+    return w.type == B200_TYPE_Q8_0 && w.K % (32 * kGKB) == 0 && w.K <= (int64_t) 1 << 30 && w.rows < ((int64_t) 1 << 31) &&
+           tensor_maps_available();
+}
+
+cudaError_t launch_gemm_tc_grouped(const WeightView & w, int64_t N, const int4 * tiles, const int * ntiles, const int8_t * q,
+                                   const float * dT, int64_t ldP, int64_t slots, const int32_t * row_map, float * y, int64_t ldy,
+                                   unsigned * err, int num_sms, cudaStream_t st) {
+    using L = GLayout;
+    const int64_t K = w.K, KB = K / 32;
+    if (!gemm_tc_grouped_supported(w) || ldP % 16 || slots % 16 || slots > ldP) return cudaErrorInvalidValue;
+    CUtensorMap ta, tb, tdw, tdx;
+    if (!make_map_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.f0, (uint64_t) K, (uint64_t) w.rows, (uint64_t) K, 128, kGM,
+                     CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, q, (uint64_t) K, (uint64_t) slots, (uint64_t) K, 128, 16, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map_2d(&tdw, CU_TENSOR_MAP_DATA_TYPE_UINT16, w.f1, (uint64_t) KB, (uint64_t) w.rows, (uint64_t) KB * 2, kGKB, kGM,
+                     CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !make_map_2d(&tdx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, dT, (uint64_t) ldP, (uint64_t) KB, (uint64_t) ldP * 4, kGNT, kGKB,
+                     CU_TENSOR_MAP_SWIZZLE_NONE))
+        return cudaErrorInvalidValue;
+    GroupedParams p;
+    p.N = N;
+    p.K = K;
+    p.tiles = tiles;
+    p.ntiles = ntiles;
+    p.tiles_n = (int) ((N + kGM - 1) / kGM);
+    p.row_map = row_map;
+    p.y = y;
+    p.ldy = ldy;
+    p.err = err;
+    static int configured = 0;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_q8_0_tc_grouped_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
+        if (e != cudaSuccess) return e;
+        configured = 1;
+    }
+    gemm_q8_0_tc_grouped_kernel<<<2 * num_sms, kGThreads, L::kTotal, st>>>(ta, tb, tdw, tdx, p);
+    return cudaGetLastError();
+}
+
+}  // namespace b200

@@ -61,5 +61,22 @@ cudaError_t launch_swiglu_quant_pairs(const float * gu, int64_t F, const int32_t
                                       int8_t * q, float * d, cudaStream_t st);
 cudaError_t launch_moe_combine(const float * down, const float * w, const int32_t * ids, int64_t T, int64_t top_k, int64_t H, int64_t e0,
                                int64_t E, float * out, cudaStream_t st);
+// Tensor-core expert products (gemm_tc_grouped.cu) and their routing/glue (moe.cu). Slots: pairs sorted by expert,
+// each expert's segment padded to a multiple of 16; at most moe_max_slots(P, E) slots and moe_max_tiles(P, E) tiles.
+bool gemm_tc_grouped_supported(const WeightView & w);
+cudaError_t launch_gemm_tc_grouped(const WeightView & w, int64_t N, const int4 * tiles, const int * ntiles, const int8_t * q,
+                                   const float * dT, int64_t ldP, int64_t slots, const int32_t * row_map, float * y, int64_t ldy,
+                                   unsigned * err, int num_sms, cudaStream_t st);
+int64_t moe_max_slots(int64_t P, int64_t E);
+int64_t moe_max_tiles(int64_t P, int64_t E);
+cudaError_t launch_moe_route(const int32_t * ids, int64_t T, int64_t top_k, int64_t nb1, int64_t E, int64_t e0, int64_t total,
+                             int32_t * grp_off, int32_t * col_src, int32_t * col_dst, int32_t * inv, int4 * tiles, int * ntiles,
+                             unsigned * err, cudaStream_t st);
+cudaError_t launch_moe_quant_slots(const float * x, int64_t K, int64_t ldx, const int32_t * col_src, const int32_t * n_slots,
+                                   int64_t max_slots, int8_t * q, float * dT, int64_t ldP, int num_sms, cudaStream_t st);
+cudaError_t launch_moe_swiglu_slots(const float * gu, int64_t F, const int32_t * col_src, const int32_t * n_slots, int64_t max_slots,
+                                    int8_t * q, float * dT, int64_t ldP, int num_sms, cudaStream_t st);
+cudaError_t launch_moe_combine_slots(const float * down, const float * w, const int32_t * inv, int64_t T, int64_t top_k, int64_t H,
+                                     float * out, cudaStream_t st);
 
 }  // namespace b200

@@ -1,0 +1,175 @@
+// moe.cu — routing and glue of the tensor-core expert path (TextModel::experts, src/families/drama3/text-model.cpp:198-221;
+// MUL_MAT_ID, src/common/graph.h:22-26): pairs sorted by expert into 16-slot-padded segments, activations quantized in
+// slot order, SwiGLU re-quantization between the two expert products, and the router-weighted combine.
+#include "internal.h"
+
+namespace b200 {
+
+// One CTA: histogram of the local experts' pairs, exclusive scan of the counts rounded up to 16, placement of every
+// pair in its expert's segment, the padding slots marked empty, and the list of token tiles (<= 64 slots each).
+// Pair p = t * top_k + s reads activation row t * nb1 + (nb1 == 1 ? 0 : s). Pairs of experts outside
+// [e0, e0 + E) are skipped (another shard's); ids outside [0, total) are reported. inv[p] = slot, or -1.
+__global__ void moe_route_kernel(const int32_t * __restrict__ ids, int64_t P, int64_t top_k, int64_t nb1, int E, int e0, int total,
+                                 int32_t * grp_off, int32_t * col_src, int32_t * col_dst, int32_t * inv, int4 * tiles, int * ntiles,
+                                 unsigned * err) {
+    extern __shared__ int sh[];
+    int * cnt = sh;      // [E]
+    int * pos = sh + E;  // [E]
+    for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+    __syncthreads();
+    for (int64_t p = threadIdx.x; p < P; p += blockDim.x) {
+        inv[p] = -1;
+        const int g = ids[p];
+        if (g < 0 || g >= total) {
+            atomicOr(err, B200_DEVERR_EXPERT);
+            continue;
+        }
+        const int e = g - e0;
+        if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        int carry = 0;
+        for (int base = 0; base < E; base += 32) {
+            const int e = base + (int) threadIdx.x;
+            const int v = e < E ? (cnt[e] + 15) & ~15 : 0;
+            int incl = v;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int t = __shfl_up_sync(0xffffffffu, incl, o);
+                if ((int) threadIdx.x >= o) incl += t;
+            }
+            if (e < E) {
+                grp_off[e] = carry + incl - v;
+                pos[e] = carry + incl - v;
+            }
+            carry += __shfl_sync(0xffffffffu, incl, 31);
+        }
+        if (threadIdx.x == 0) grp_off[E] = carry;
+    }
+    __syncthreads();
+    for (int64_t p = threadIdx.x; p < P; p += blockDim.x) {
+        const int g = ids[p];
+        const int e = g - e0;
+        if (g < 0 || g >= total || e < 0 || e >= E) continue;
+        const int slot = atomicAdd(&pos[e], 1);
+        const int64_t t = p / top_k, s = p % top_k;
+        col_src[slot] = (int32_t) (t * nb1 + (nb1 == 1 ? 0 : s));
+        col_dst[slot] = (int32_t) p;
+        inv[p] = slot;
+    }
+    __syncthreads();
+    // padding slots (pos[e] is now the end of expert e's pairs)
+    for (int e = threadIdx.x; e < E; e += blockDim.x)
+        for (int slot = pos[e]; slot < grp_off[e + 1]; slot++) {
+            col_src[slot] = -1;
+            col_dst[slot] = -1;
+        }
+    if (threadIdx.x == 0) {
+        int n = 0;
+        for (int e = 0; e < E; e++) {
+            const int len = grp_off[e + 1] - grp_off[e];
+            for (int o = 0; o < len; o += 64) tiles[n++] = make_int4(e, grp_off[e] + o, min(64, len - o), 0);
+        }
+        *ntiles = n;
+    }
+}
+
+// q8_0 quantization of each slot's activation row (zeros for padding), in slot order: q [slots][K], dT [K/32][ldP].
+// One warp per (slot, 32-block); bit-identical to the CPU backend's quantize_row_q8_0 of the same row.
+__global__ void moe_quant_slots_kernel(const float * __restrict__ x, int64_t K, int64_t ldx, const int32_t * __restrict__ col_src,
+                                       const int32_t * __restrict__ n_slots, int8_t * q, float * dT, int64_t ldP) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nb = K / 32, total = (int64_t) (*n_slots) * nb;
+    const int64_t warps = (int64_t) gridDim.x * (blockDim.x >> 5);
+    for (int64_t i = (int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); i < total; i += warps) {
+        const int64_t slot = i / nb, b = i % nb;
+        const int32_t src = col_src[slot];
+        const float v = src >= 0 ? x[(int64_t) src * ldx + b * 32 + lane] : 0.0f;
+        float df;
+        uint16_t dh;
+        const int8_t qv = quantize_q8_0_lane(v, &df, &dh);
+        q[slot * K + b * 32 + lane] = qv;
+        if (lane == 0) dT[b * ldP + slot] = df;
+    }
+}
+
+// SwiGLU of each slot's gate|up row (gu [slots][2F]: gate F, then up F), re-quantized to q8_0 in slot order for the
+// down product: q [slots][F], dT [F/32][ldP]; zeros for padding.
+__global__ void moe_swiglu_slots_kernel(const float * __restrict__ gu, int64_t F, const int32_t * __restrict__ col_src,
+                                        const int32_t * __restrict__ n_slots, int8_t * q, float * dT, int64_t ldP) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nb = F / 32, total = (int64_t) (*n_slots) * nb;
+    const int64_t warps = (int64_t) gridDim.x * (blockDim.x >> 5);
+    for (int64_t i = (int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); i < total; i += warps) {
+        const int64_t slot = i / nb, b = i % nb;
+        float v = 0.0f;
+        if (col_src[slot] >= 0) {
+            const float * row = gu + slot * 2 * F;
+            v = __fmul_rn(silu(row[b * 32 + lane]), row[F + b * 32 + lane]);
+        }
+        float df;
+        uint16_t dh;
+        const int8_t qv = quantize_q8_0_lane(v, &df, &dh);
+        q[slot * F + b * 32 + lane] = qv;
+        if (lane == 0) dT[b * ldP + slot] = df;
+    }
+}
+
+// out[t] = sum over s (slot order) of w[t][s] * down row of pair (t, s), over the pairs this shard computed.
+__global__ void moe_combine_slots_kernel(const float * __restrict__ down, const float * __restrict__ w, const int32_t * __restrict__ inv,
+                                         int64_t top_k, int64_t H, float * __restrict__ out) {
+    const int64_t t = blockIdx.x;
+    for (int64_t h = threadIdx.x; h < H; h += blockDim.x) {
+        float sum = 0.0f;
+        bool any = false;
+        for (int64_t s = 0; s < top_k; s++) {
+            const int32_t slot = inv[t * top_k + s];
+            if (slot < 0) continue;
+            const float v = __fmul_rn(down[(int64_t) slot * H + h], w[t * top_k + s]);
+            sum = any ? __fadd_rn(sum, v) : v;
+            any = true;
+        }
+        out[t * H + h] = sum;
+    }
+}
+
+int64_t moe_max_slots(int64_t P, int64_t E) { return ((P + 15 * E) + 15) & ~(int64_t) 15; }
+int64_t moe_max_tiles(int64_t P, int64_t E) { return moe_max_slots(P, E) / 16 + E + 1; }
+
+cudaError_t launch_moe_route(const int32_t * ids, int64_t T, int64_t top_k, int64_t nb1, int64_t E, int64_t e0, int64_t total,
+                             int32_t * grp_off, int32_t * col_src, int32_t * col_dst, int32_t * inv, int4 * tiles, int * ntiles,
+                             unsigned * err, cudaStream_t st) {
+    moe_route_kernel<<<1, 1024, (size_t) 2 * E * sizeof(int), st>>>(ids, T * top_k, top_k, nb1, (int) E, (int) e0,
+                                                                    (int) (total > 0 ? total : E), grp_off, col_src, col_dst, inv,
+                                                                    tiles, ntiles, err);
+    return cudaGetLastError();
+}
+
+static unsigned glue_blocks(int64_t work_warps, int num_sms) {
+    int64_t blocks = (work_warps + 7) / 8;
+    const int64_t cap = (int64_t) num_sms * 8;
+    if (blocks > cap) blocks = cap;
+    return (unsigned) (blocks < 1 ? 1 : blocks);
+}
+
+cudaError_t launch_moe_quant_slots(const float * x, int64_t K, int64_t ldx, const int32_t * col_src, const int32_t * n_slots,
+                                   int64_t max_slots, int8_t * q, float * dT, int64_t ldP, int num_sms, cudaStream_t st) {
+    moe_quant_slots_kernel<<<glue_blocks(max_slots * (K / 32), num_sms), 256, 0, st>>>(x, K, ldx, col_src, n_slots, q, dT, ldP);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_moe_swiglu_slots(const float * gu, int64_t F, const int32_t * col_src, const int32_t * n_slots, int64_t max_slots,
+                                    int8_t * q, float * dT, int64_t ldP, int num_sms, cudaStream_t st) {
+    moe_swiglu_slots_kernel<<<glue_blocks(max_slots * (F / 32), num_sms), 256, 0, st>>>(gu, F, col_src, n_slots, q, dT, ldP);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_moe_combine_slots(const float * down, const float * w, const int32_t * inv, int64_t T, int64_t top_k, int64_t H,
+                                     float * out, cudaStream_t st) {
+    if (T <= 0) return cudaSuccess;
+    moe_combine_slots_kernel<<<(unsigned) T, 256, 0, st>>>(down, w, inv, top_k, H, out);
+    return cudaGetLastError();
+}
+
+}  // namespace b200

@@ -233,3 +233,29 @@ def test_invalid_shapes_are_errors_not_aborts(ctx, b200):
     with pytest.raises(b200.B200Error):
         ctx.weight(Q8_0, 100, 8)  # not whole blocks
     ctx.free_weight(w)
+
+
+@pytest.mark.parametrize("nb1,skew", [(1, False), (4, False), (1, True)])
+def test_mul_mat_id_tensor_cores(ctx, oracle, nb1, skew):
+    """MUL_MAT_ID of Q8_0 experts with >= 128 (token, slot) pairs runs on the tensor cores (expert-sorted slots padded
+    to 16, token tiles of <= 64 slots). N = 192 leaves a partial 128-row tile; with skew, expert 0 takes every token's
+    first slot (100 pairs: two token tiles) and experts 13..15 get none."""
+    rng = np.random.default_rng(77 + nb1 + 10 * skew)
+    E, K, N, T, top_k = 16, 1024, 192, 100, 4
+    wb = rand_w(rng, Q8_0, E * N, K, oracle)
+    if skew:
+        ids = np.stack([np.concatenate([[0], 1 + rng.permutation(12)[:top_k - 1]]) for _ in range(T)]).astype(np.int32)
+    else:
+        ids = np.stack([rng.permutation(E)[:top_k] for _ in range(T)]).astype(np.int32)
+    b = rng.normal(0, 1, size=(T, nb1, K)).astype(np.float32)
+    w = ctx.weight(Q8_0, K, N, E, data=wb)
+    got = ctx.mul_mat_id(w, cuda(b), cuda(ids)).cpu().numpy()
+    ctx.synchronize()
+    want = oracle.mul_mat_id(Q8_0, wb, K, N, E, b, ids)
+    for t in range(T):
+        for s in range(top_k):
+            e = ids[t, s]
+            xb = b[t, 0 if nb1 == 1 else s][None]
+            bd = bound(oracle, Q8_0, wb[e * N:(e + 1) * N], K, xb)[0]
+            assert np.all(np.abs(got[t, s] - want[t, s]) <= bd), (t, s)
+    ctx.free_weight(w)
