@@ -89,6 +89,11 @@ __device__ __forceinline__ void mbar_arrive(uint64_t * bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
+// `count` arrivals at once (a thread arriving for itself and for threads that skip the phase).
+__device__ __forceinline__ void mbar_arrive_n(uint64_t * bar, uint32_t count) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
 // Waits for the phase with the given parity to complete; false if it did not within kSpinLimit polls.
 __device__ __forceinline__ bool mbar_wait(uint64_t * bar, uint32_t parity) {
     const uint32_t a = smem_addr(bar);
@@ -156,6 +161,24 @@ __device__ __forceinline__ int8_t quantize_q8_0_lane(float v, float * d_out, uin
     *d_out = __half2float(dh);
     *d_half = __half_as_ushort(dh);
     return (int8_t) (int) roundf(__fmul_rn(v, id));
+}
+
+// q8_0 of one 32-value block held 4 per lane by 8 consecutive lanes (lanes 8k .. 8k + 7, lane 8k + i holding values
+// 4i .. 4i + 3): the arithmetic of quantize_q8_0_lane. Returns the 4 int8 packed little-endian; *d_out = the fp16 scale
+// as float. All 32 lanes must call it.
+__device__ __forceinline__ uint32_t quantize_q8_0_quad(float4 v, float * d_out) {
+    float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    *d_out = __half2float(__float2half_rn(d));
+    const uint32_t q0 = (uint32_t) (int) roundf(__fmul_rn(v.x, id)) & 0xFFu;
+    const uint32_t q1 = (uint32_t) (int) roundf(__fmul_rn(v.y, id)) & 0xFFu;
+    const uint32_t q2 = (uint32_t) (int) roundf(__fmul_rn(v.z, id)) & 0xFFu;
+    const uint32_t q3 = (uint32_t) (int) roundf(__fmul_rn(v.w, id)) & 0xFFu;
+    return q0 | (q1 << 8) | (q2 << 16) | (q3 << 24);
 }
 
 // One q8_K block of 256 values held 8 per lane (lane l holds values 8l .. 8l+7): the largest magnitude (first index on

@@ -6,10 +6,10 @@
 // (q [slots][K] int8, dT [K/32][ldP] float block scales, transposed). A token tile is up to 64 consecutive slots of one
 // expert; the route kernel lists the tiles. One work item = one token tile x one 128-row tile of the expert's weight
 // matrix. Per 32-wide K block, one tcgen05.mma kind::i8 of shape M = 128 (weight rows) x N = the tile's token count
-// (16..64, a run-time field of the instruction descriptor) x K = 32 computes the block's exact int32 sums into one of
-// four tensor-memory buffers; epilogue warps read them (tcgen05.ld), scale them by d_w[row][b] * d_x[slot][b] and add
-// them to float32 registers in block order, as ggml's CPU vec_dot does. Operands come by TMA (2-D tensor maps, 128-byte
-// swizzle, no multicast). The grid is persistent (two CTAs per SM) and walks the items in a fixed order; every role of
+// (16..64, a run-time field of the instruction descriptor) x K = 32 computes the block's exact int32 sums. Blocks go in
+// pairs into one of two tensor-memory buffers (2 x 64 columns each), one barrier round trip per pair; epilogue warps
+// read a pair's sums (tcgen05.ld), scale them by d_w[row][b] * d_x[slot][b] and add them to float32 registers in
+// block order, as ggml's CPU vec_dot does. Operands come by TMA (2-D tensor maps, 128-byte swizzle, no multicast). The grid is persistent (two CTAs per SM) and walks the items in a fixed order; every role of
 // a CTA derives the same item sequence from the tile list, so they need no other coordination than the stage and
 // accumulator barriers. Warp roles: 0 = TMA producer, 1 = tensor-memory allocator and MMA issuer (one thread),
 // 2..9 = epilogue. Every wait is bounded; one that gives up records B200_DEVERR_TIMEOUT and the CTA runs to its end
@@ -26,7 +26,7 @@ constexpr int kGKB = 8;        // 32-wide K blocks per pipeline stage
 constexpr int kGStages = 2;
 constexpr int kGThreads = 320; // producer, MMA, 8 epilogue warps
 constexpr int kGEpiWarps = 8;
-constexpr int kGBufs = 4;      // tensor-memory accumulators in flight, kGNT columns each
+constexpr int kGBufs = 2;      // tensor-memory accumulators in flight, one K-block pair (2 x kGNT columns) each
 constexpr int kGNT = 64;       // slots per token tile (largest MMA N used)
 constexpr unsigned kErrTimeout = 4u;
 
@@ -61,8 +61,8 @@ __global__ void __launch_bounds__(kGThreads, 2)
     uint64_t * bars = reinterpret_cast<uint64_t *>(smem + kGStages * L::kStage);
     uint64_t * full = bars;
     uint64_t * empty = bars + kGStages;
-    uint64_t * acc_full = bars + 2 * kGStages;
-    uint64_t * acc_empty = acc_full + kGBufs;
+    uint64_t * acc_full = bars + 2 * kGStages;   // [bufs] a block pair's int32 sums ready in tensor memory
+    uint64_t * acc_empty = acc_full + kGBufs;    // [bufs] epilogue has read them
     uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + kGBufs);
     __shared__ volatile int give_up;
 
@@ -83,7 +83,7 @@ __global__ void __launch_bounds__(kGThreads, 2)
         give_up = 0;
     }
     if (warp == 1) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)), "r"(kGBufs * kGNT));
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)), "r"(2 * kGBufs * kGNT));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     tc_fence_before();
@@ -121,9 +121,10 @@ __global__ void __launch_bounds__(kGThreads, 2)
             }
         }
     } else if (warp == 1) {
-        // ---- MMA issuer: one K block per MMA, into tensor-memory buffer b % 4 ----
+        // ---- MMA issuer: one K block per MMA; block pair g goes to tensor-memory buffer g % 2 (columns 0..63 and
+        // 64..127 of it), one commit per pair ----
         if (lane == 0) {
-            int sg = 0, b = 0;
+            int sg = 0, g2 = 0;
             for (int it = blockIdx.x; it < items && !give_up; it += gridDim.x) {
                 const int4 t = p.tiles[it / p.tiles_n];
                 const uint32_t idesc = idesc_i8_n(t.z);
@@ -136,16 +137,18 @@ __global__ void __launch_bounds__(kGThreads, 2)
                     }
                     tc_fence_after();
                     uint8_t * base = smem + s * L::kStage;
-                    for (int j = 0; j < kGKB; j++, b++) {
-                        const int buf = b % kGBufs, use = b / kGBufs;
+                    for (int j = 0; j < kGKB; j += 2, g2++) {
+                        const int buf = g2 % kGBufs, use = g2 / kGBufs;
                         if (use > 0 && !mbar_wait(&acc_empty[buf], (use - 1) & 1)) {
                             atomicOr(p.err, kErrTimeout);
                             give_up = 1;
                             break;
                         }
                         tc_fence_after();
-                        mma_i8(tmem + buf * kGNT, smem_desc_sw128(base + (j / 4) * kGM * 128, j % 4),
-                               smem_desc_sw128(base + L::kA + (j / 4) * kGNT * 128, j % 4), idesc);
+#pragma unroll
+                        for (int jj = 0; jj < 2; jj++)
+                            mma_i8(tmem + buf * 2 * kGNT + jj * kGNT, smem_desc_sw128(base + ((j + jj) / 4) * kGM * 128, (j + jj) % 4),
+                                   smem_desc_sw128(base + L::kA + ((j + jj) / 4) * kGNT * 128, (j + jj) % 4), idesc);
                         mma_commit(&acc_full[buf]);
                     }
                     if (give_up) break;
@@ -155,11 +158,13 @@ __global__ void __launch_bounds__(kGThreads, 2)
         }
     } else {
         // ---- epilogue: lane quarter q = warp % 4 owns tile rows 32 q .. 32 q + 31 (one per lane); warp half h takes
-        // the 16-slot column chunks h and h + 2 of the tile ----
+        // the 16-slot column chunks h and h + 2 of the tile. A warp without columns in a tile (h = 1 in a tile of one
+        // chunk) still waits and arrives on every barrier, so no warp runs a phase ahead of the others: parity waits
+        // cannot tell phase n from phase n + 2 ----
         const int q = warp & 3, h = (warp - 2) >> 2;
         const int row = 32 * q + lane;
         const float2 neg_magic = make_float2(-12582912.0f, -12582912.0f);
-        int sg = 0, b = 0;
+        int sg = 0, g2 = 0;
         for (int it = blockIdx.x; it < items && !give_up; it += gridDim.x) {
             const int4 t = p.tiles[it / p.tiles_n];
             const int tn = it % p.tiles_n;
@@ -171,69 +176,70 @@ __global__ void __launch_bounds__(kGThreads, 2)
             for (int st = 0; st < nstage && !give_up; st++, sg++) {
                 const int s = sg % kGStages;
                 const uint8_t * base = smem + s * L::kStage;
-                const __half * dw = reinterpret_cast<const __half *>(base + L::kA + L::kB);
+                const __half2 * dw2 = reinterpret_cast<const __half2 *>(base + L::kA + L::kB) + row * (kGKB / 2);
                 const float * dxT = reinterpret_cast<const float *>(base + L::kA + L::kB + L::kDw);
-                for (int j = 0; j < kGKB; j++, b++) {
-                    const int buf = b % kGBufs, use = b / kGBufs;
+                for (int j = 0; j < kGKB; j += 2, g2++) {
+                    const int buf = g2 % kGBufs, use = g2 / kGBufs;
                     if (!mbar_wait(&acc_full[buf], use & 1)) {
                         if (lane == 0) atomicOr(p.err, kErrTimeout);
                         give_up = 1;
                         break;
                     }
                     tc_fence_after();
-                    int v0[16], v1[16];
-                    const uint32_t ta = tmem + ((uint32_t) (32 * q) << 16) + buf * kGNT;
-                    if (has0) tmem_ld16(ta + 16 * h, v0);
-                    if (has1) tmem_ld16(ta + 16 * (h + 2), v1);
-                    tmem_wait_ld();
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&acc_empty[buf]);
-                    // acc += float(sum) * (d_x * d_w); |sum| <= 32 * 127 * 128 < 2^22 converts exactly through the
-                    // float 12582912 + sum (bit pattern 0x4B400000 + sum)
-                    const float dwr = __half2float(dw[row * kGKB + j]);
-                    const float2 w2 = make_float2(dwr, dwr);
-                    if (has0) {
-                        const float4 * dx4 = reinterpret_cast<const float4 *>(dxT + j * kGNT + 16 * h);
-#pragma unroll
-                        for (int t4 = 0; t4 < 4; t4++) {
-                            const float4 d = dx4[t4];
-                            const float2 s01 = __fmul2_rn(make_float2(d.x, d.y), w2);
-                            const float2 s23 = __fmul2_rn(make_float2(d.z, d.w), w2);
-                            const float2 f01 = __fadd2_rn(
-                                make_float2(__int_as_float(v0[4 * t4] + 0x4B400000), __int_as_float(v0[4 * t4 + 1] + 0x4B400000)), neg_magic);
-                            const float2 f23 = __fadd2_rn(
-                                make_float2(__int_as_float(v0[4 * t4 + 2] + 0x4B400000), __int_as_float(v0[4 * t4 + 3] + 0x4B400000)), neg_magic);
-                            acc[2 * t4] = __ffma2_rn(f01, s01, acc[2 * t4]);
-                            acc[2 * t4 + 1] = __ffma2_rn(f23, s23, acc[2 * t4 + 1]);
-                        }
+                    if (!has0) {  // no columns in this tile: only the barrier protocol, which keeps this warp in step
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&acc_empty[buf]);
+                        continue;
                     }
-                    if (has1) {
-                        const float4 * dx4 = reinterpret_cast<const float4 *>(dxT + j * kGNT + 16 * (h + 2));
+                    // the pair's blocks one at a time (registers: 2 chunks x 16 sums); the buffer is released once
+                    // the second block's sums are in registers
+                    const float2 dwp = __half22float2(dw2[j / 2]);
+                    const uint32_t ta = tmem + ((uint32_t) (32 * q) << 16) + buf * 2 * kGNT;
 #pragma unroll
-                        for (int t4 = 0; t4 < 4; t4++) {
-                            const float4 d = dx4[t4];
-                            const float2 s01 = __fmul2_rn(make_float2(d.x, d.y), w2);
-                            const float2 s23 = __fmul2_rn(make_float2(d.z, d.w), w2);
-                            const float2 f01 = __fadd2_rn(
-                                make_float2(__int_as_float(v1[4 * t4] + 0x4B400000), __int_as_float(v1[4 * t4 + 1] + 0x4B400000)), neg_magic);
-                            const float2 f23 = __fadd2_rn(
-                                make_float2(__int_as_float(v1[4 * t4 + 2] + 0x4B400000), __int_as_float(v1[4 * t4 + 3] + 0x4B400000)), neg_magic);
-                            acc[8 + 2 * t4] = __ffma2_rn(f01, s01, acc[8 + 2 * t4]);
-                            acc[8 + 2 * t4 + 1] = __ffma2_rn(f23, s23, acc[8 + 2 * t4 + 1]);
+                    for (int jj = 0; jj < 2; jj++) {
+                        int v[2][16];  // [chunk][column]
+                        tmem_ld16(ta + jj * kGNT + 16 * h, v[0]);
+                        if (has1) tmem_ld16(ta + jj * kGNT + 16 * (h + 2), v[1]);
+                        tmem_wait_ld();
+                        if (jj == 1) {
+                            tc_fence_before();
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(&acc_empty[buf]);
+                        }
+                        // acc += float(sum) * (d_x * d_w), in block order; |sum| <= 32 * 127 * 128 < 2^22 converts
+                        // exactly through the float 12582912 + sum (bit pattern 0x4B400000 + sum)
+                        const float dwr = jj ? dwp.y : dwp.x;
+                        const float2 w2 = make_float2(dwr, dwr);
+#pragma unroll
+                        for (int c = 0; c < 2; c++) {
+                            if (c == 1 && !has1) continue;
+                            const float4 * dx4 = reinterpret_cast<const float4 *>(dxT + (j + jj) * kGNT + 16 * (h + 2 * c));
+#pragma unroll
+                            for (int t4 = 0; t4 < 4; t4++) {
+                                const float4 d = dx4[t4];
+                                const int * vv = v[c] + 4 * t4;
+                                const float2 s01 = __fmul2_rn(make_float2(d.x, d.y), w2);
+                                const float2 s23 = __fmul2_rn(make_float2(d.z, d.w), w2);
+                                const float2 f01 = __fadd2_rn(make_float2(__int_as_float(vv[0] + 0x4B400000), __int_as_float(vv[1] + 0x4B400000)),
+                                                              neg_magic);
+                                const float2 f23 = __fadd2_rn(make_float2(__int_as_float(vv[2] + 0x4B400000), __int_as_float(vv[3] + 0x4B400000)),
+                                                              neg_magic);
+                                acc[8 * c + 2 * t4] = __ffma2_rn(f01, s01, acc[8 * c + 2 * t4]);
+                                acc[8 * c + 2 * t4 + 1] = __ffma2_rn(f23, s23, acc[8 * c + 2 * t4 + 1]);
+                            }
                         }
                     }
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[s]);
             }
-            if (give_up) break;
+            if (give_up || !has0) continue;
             // ---- output: one weight row per lane, so each slot's store is one coalesced 128-byte line ----
             const int64_t grow = (int64_t) tn * kGM + row;
             if (grow < p.N) {
 #pragma unroll
                 for (int c = 0; c < 2; c++) {
-                    if (!(c == 0 ? has0 : has1)) continue;
+                    if (c == 1 && !has1) continue;
                     const int col0 = 16 * (h + 2 * c);
 #pragma unroll
                     for (int i = 0; i < 16; i++) {
@@ -250,7 +256,7 @@ __global__ void __launch_bounds__(kGThreads, 2)
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kGBufs * kGNT));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kGBufs * kGNT));
     }
 }
 

@@ -5,16 +5,19 @@
 
 namespace b200 {
 
-// One CTA: histogram of the local experts' pairs, exclusive scan of the counts rounded up to 16, placement of every
-// pair in its expert's segment, the padding slots marked empty, and the list of token tiles (<= 64 slots each).
-// Pair p = t * top_k + s reads activation row t * nb1 + (nb1 == 1 ? 0 : s). Pairs of experts outside
-// [e0, e0 + E) are skipped (another shard's); ids outside [0, total) are reported. inv[p] = slot, or -1.
+// One CTA: histogram of the local experts' pairs, exclusive scans of the counts rounded up to 16 (segment starts) and
+// of the segments' tile counts, placement of every pair in its expert's segment, the padding slots marked empty, and
+// the list of token tiles (<= 64 slots each, in expert order). Pair p = t * top_k + s reads activation row
+// t * nb1 + (nb1 == 1 ? 0 : s). Pairs of experts outside [e0, e0 + E) are skipped (another shard's); ids outside
+// [0, total) are reported. inv[p] = the pair's slot, or -1.
 __global__ void moe_route_kernel(const int32_t * __restrict__ ids, int64_t P, int64_t top_k, int64_t nb1, int E, int e0, int total,
                                  int32_t * grp_off, int32_t * col_src, int32_t * col_dst, int32_t * inv, int4 * tiles, int * ntiles,
                                  unsigned * err) {
     extern __shared__ int sh[];
-    int * cnt = sh;      // [E]
-    int * pos = sh + E;  // [E]
+    int * cnt = sh;            // [E] pairs
+    int * pos = sh + E;        // [E] placement cursor
+    int * start = sh + 2 * E;  // [E] segment start
+    int * toff = sh + 3 * E;   // [E] first tile
     for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
     __syncthreads();
     for (int64_t p = threadIdx.x; p < P; p += blockDim.x) {
@@ -29,23 +32,32 @@ __global__ void moe_route_kernel(const int32_t * __restrict__ ids, int64_t P, in
     }
     __syncthreads();
     if (threadIdx.x < 32) {
-        int carry = 0;
+        int carry = 0, tcarry = 0;
         for (int base = 0; base < E; base += 32) {
             const int e = base + (int) threadIdx.x;
-            const int v = e < E ? (cnt[e] + 15) & ~15 : 0;
-            int incl = v;
+            const int len = e < E ? (cnt[e] + 15) & ~15 : 0;
+            const int nt = (len + 63) / 64;
+            int incl = len, tincl = nt;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
-                const int t = __shfl_up_sync(0xffffffffu, incl, o);
-                if ((int) threadIdx.x >= o) incl += t;
+                const int a = __shfl_up_sync(0xffffffffu, incl, o);
+                const int b = __shfl_up_sync(0xffffffffu, tincl, o);
+                if ((int) threadIdx.x >= o) {
+                    incl += a;
+                    tincl += b;
+                }
             }
             if (e < E) {
-                grp_off[e] = carry + incl - v;
-                pos[e] = carry + incl - v;
+                start[e] = pos[e] = grp_off[e] = carry + incl - len;
+                toff[e] = tcarry + tincl - nt;
             }
             carry += __shfl_sync(0xffffffffu, incl, 31);
+            tcarry += __shfl_sync(0xffffffffu, tincl, 31);
         }
-        if (threadIdx.x == 0) grp_off[E] = carry;
+        if (threadIdx.x == 0) {
+            grp_off[E] = carry;
+            *ntiles = tcarry;
+        }
     }
     __syncthreads();
     for (int64_t p = threadIdx.x; p < P; p += blockDim.x) {
@@ -59,67 +71,92 @@ __global__ void moe_route_kernel(const int32_t * __restrict__ ids, int64_t P, in
         inv[p] = slot;
     }
     __syncthreads();
-    // padding slots (pos[e] is now the end of expert e's pairs)
-    for (int e = threadIdx.x; e < E; e += blockDim.x)
-        for (int slot = pos[e]; slot < grp_off[e + 1]; slot++) {
+    // padding slots (pos[e] is now the end of expert e's pairs) and the expert's token tiles
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        const int len = (cnt[e] + 15) & ~15;
+        for (int slot = pos[e]; slot < start[e] + len; slot++) {
             col_src[slot] = -1;
             col_dst[slot] = -1;
         }
-    if (threadIdx.x == 0) {
-        int n = 0;
-        for (int e = 0; e < E; e++) {
-            const int len = grp_off[e + 1] - grp_off[e];
-            for (int o = 0; o < len; o += 64) tiles[n++] = make_int4(e, grp_off[e] + o, min(64, len - o), 0);
-        }
-        *ntiles = n;
+        for (int o = 0, k = toff[e]; o < len; o += 64, k++) tiles[k] = make_int4(e, start[e] + o, min(64, len - o), 0);
     }
 }
 
 // q8_0 quantization of each slot's activation row (zeros for padding), in slot order: q [slots][K], dT [K/32][ldP].
-// One warp per (slot, 32-block); bit-identical to the CPU backend's quantize_row_q8_0 of the same row.
-__global__ void moe_quant_slots_kernel(const float * __restrict__ x, int64_t K, int64_t ldx, const int32_t * __restrict__ col_src,
+// One warp per slot row, 128 values per step (a block per 8 lanes); bit-identical to the CPU backend's
+// quantize_row_q8_0 of the same row. vec: x and ldx allow 16-byte loads.
+__global__ void moe_quant_slots_kernel(const float * __restrict__ x, int64_t K, int64_t ldx, int vec, const int32_t * __restrict__ col_src,
                                        const int32_t * __restrict__ n_slots, int8_t * q, float * dT, int64_t ldP) {
     const int lane = threadIdx.x & 31;
-    const int64_t nb = K / 32, total = (int64_t) (*n_slots) * nb;
-    const int64_t warps = (int64_t) gridDim.x * (blockDim.x >> 5);
-    for (int64_t i = (int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); i < total; i += warps) {
-        const int64_t slot = i / nb, b = i % nb;
+    const int warps = gridDim.x * (blockDim.x >> 5);
+    const int S = *n_slots;
+    for (int slot = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); slot < S; slot += warps) {
         const int32_t src = col_src[slot];
-        const float v = src >= 0 ? x[(int64_t) src * ldx + b * 32 + lane] : 0.0f;
-        float df;
-        uint16_t dh;
-        const int8_t qv = quantize_q8_0_lane(v, &df, &dh);
-        q[slot * K + b * 32 + lane] = qv;
-        if (lane == 0) dT[b * ldP + slot] = df;
+        const float * xr = src >= 0 ? x + (int64_t) src * ldx : nullptr;
+        for (int64_t k0 = 0; k0 < K; k0 += 128) {
+            const int64_t k = k0 + 4 * lane;
+            float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (xr && k < K) v = vec ? *reinterpret_cast<const float4 *>(xr + k) : make_float4(xr[k], xr[k + 1], xr[k + 2], xr[k + 3]);
+            float d;
+            const uint32_t packed = quantize_q8_0_quad(v, &d);
+            if (k < K) {
+                *reinterpret_cast<uint32_t *>(q + (int64_t) slot * K + k) = packed;
+                if ((lane & 7) == 0) dT[(k >> 5) * ldP + slot] = d;
+            }
+        }
     }
 }
 
 // SwiGLU of each slot's gate|up row (gu [slots][2F]: gate F, then up F), re-quantized to q8_0 in slot order for the
-// down product: q [slots][F], dT [F/32][ldP]; zeros for padding.
+// down product: q [slots][F], dT [F/32][ldP]; zeros for padding. One warp per slot row, 128 values per step.
 __global__ void moe_swiglu_slots_kernel(const float * __restrict__ gu, int64_t F, const int32_t * __restrict__ col_src,
                                         const int32_t * __restrict__ n_slots, int8_t * q, float * dT, int64_t ldP) {
     const int lane = threadIdx.x & 31;
-    const int64_t nb = F / 32, total = (int64_t) (*n_slots) * nb;
-    const int64_t warps = (int64_t) gridDim.x * (blockDim.x >> 5);
-    for (int64_t i = (int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); i < total; i += warps) {
-        const int64_t slot = i / nb, b = i % nb;
-        float v = 0.0f;
-        if (col_src[slot] >= 0) {
-            const float * row = gu + slot * 2 * F;
-            v = __fmul_rn(silu(row[b * 32 + lane]), row[F + b * 32 + lane]);
+    const int warps = gridDim.x * (blockDim.x >> 5);
+    const int S = *n_slots;
+    for (int slot = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); slot < S; slot += warps) {
+        const bool live = col_src[slot] >= 0;
+        const float * row = gu + (int64_t) slot * 2 * F;
+        for (int64_t k0 = 0; k0 < F; k0 += 128) {
+            const int64_t k = k0 + 4 * lane;
+            float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (live && k < F) {
+                const float4 g = *reinterpret_cast<const float4 *>(row + k);
+                const float4 u = *reinterpret_cast<const float4 *>(row + F + k);
+                v = make_float4(__fmul_rn(silu(g.x), u.x), __fmul_rn(silu(g.y), u.y), __fmul_rn(silu(g.z), u.z), __fmul_rn(silu(g.w), u.w));
+            }
+            float d;
+            const uint32_t packed = quantize_q8_0_quad(v, &d);
+            if (k < F) {
+                *reinterpret_cast<uint32_t *>(q + (int64_t) slot * F + k) = packed;
+                if ((lane & 7) == 0) dT[(k >> 5) * ldP + slot] = d;
+            }
         }
-        float df;
-        uint16_t dh;
-        const int8_t qv = quantize_q8_0_lane(v, &df, &dh);
-        q[slot * F + b * 32 + lane] = qv;
-        if (lane == 0) dT[b * ldP + slot] = df;
     }
 }
 
 // out[t] = sum over s (slot order) of w[t][s] * down row of pair (t, s), over the pairs this shard computed.
+// vec: out allows 16-byte stores and H % 4 == 0.
 __global__ void moe_combine_slots_kernel(const float * __restrict__ down, const float * __restrict__ w, const int32_t * __restrict__ inv,
-                                         int64_t top_k, int64_t H, float * __restrict__ out) {
+                                         int64_t top_k, int64_t H, int vec, float * __restrict__ out) {
     const int64_t t = blockIdx.x;
+    if (vec) {
+        for (int64_t h = 4 * (int64_t) threadIdx.x; h < H; h += 4 * (int64_t) blockDim.x) {
+            float4 sum = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            bool any = false;
+            for (int64_t s = 0; s < top_k; s++) {
+                const int32_t slot = inv[t * top_k + s];
+                if (slot < 0) continue;
+                const float ws = w[t * top_k + s];
+                const float4 d = *reinterpret_cast<const float4 *>(down + (int64_t) slot * H + h);
+                const float4 v = make_float4(__fmul_rn(d.x, ws), __fmul_rn(d.y, ws), __fmul_rn(d.z, ws), __fmul_rn(d.w, ws));
+                sum = any ? make_float4(__fadd_rn(sum.x, v.x), __fadd_rn(sum.y, v.y), __fadd_rn(sum.z, v.z), __fadd_rn(sum.w, v.w)) : v;
+                any = true;
+            }
+            *reinterpret_cast<float4 *>(out + t * H + h) = sum;
+        }
+        return;
+    }
     for (int64_t h = threadIdx.x; h < H; h += blockDim.x) {
         float sum = 0.0f;
         bool any = false;
@@ -140,13 +177,14 @@ int64_t moe_max_tiles(int64_t P, int64_t E) { return moe_max_slots(P, E) / 16 + 
 cudaError_t launch_moe_route(const int32_t * ids, int64_t T, int64_t top_k, int64_t nb1, int64_t E, int64_t e0, int64_t total,
                              int32_t * grp_off, int32_t * col_src, int32_t * col_dst, int32_t * inv, int4 * tiles, int * ntiles,
                              unsigned * err, cudaStream_t st) {
-    moe_route_kernel<<<1, 1024, (size_t) 2 * E * sizeof(int), st>>>(ids, T * top_k, top_k, nb1, (int) E, (int) e0,
+    moe_route_kernel<<<1, 1024, (size_t) 4 * E * sizeof(int), st>>>(ids, T * top_k, top_k, nb1, (int) E, (int) e0,
                                                                     (int) (total > 0 ? total : E), grp_off, col_src, col_dst, inv,
                                                                     tiles, ntiles, err);
     return cudaGetLastError();
 }
 
 static unsigned glue_blocks(int64_t work_warps, int num_sms) {
+    // one warp per slot row, eight warps per block
     int64_t blocks = (work_warps + 7) / 8;
     const int64_t cap = (int64_t) num_sms * 8;
     if (blocks > cap) blocks = cap;
@@ -155,20 +193,22 @@ static unsigned glue_blocks(int64_t work_warps, int num_sms) {
 
 cudaError_t launch_moe_quant_slots(const float * x, int64_t K, int64_t ldx, const int32_t * col_src, const int32_t * n_slots,
                                    int64_t max_slots, int8_t * q, float * dT, int64_t ldP, int num_sms, cudaStream_t st) {
-    moe_quant_slots_kernel<<<glue_blocks(max_slots * (K / 32), num_sms), 256, 0, st>>>(x, K, ldx, col_src, n_slots, q, dT, ldP);
+    const int vec = ((uintptr_t) x % 16 == 0 && ldx % 4 == 0) ? 1 : 0;
+    moe_quant_slots_kernel<<<glue_blocks(max_slots, num_sms), 256, 0, st>>>(x, K, ldx, vec, col_src, n_slots, q, dT, ldP);
     return cudaGetLastError();
 }
 
 cudaError_t launch_moe_swiglu_slots(const float * gu, int64_t F, const int32_t * col_src, const int32_t * n_slots, int64_t max_slots,
                                     int8_t * q, float * dT, int64_t ldP, int num_sms, cudaStream_t st) {
-    moe_swiglu_slots_kernel<<<glue_blocks(max_slots * (F / 32), num_sms), 256, 0, st>>>(gu, F, col_src, n_slots, q, dT, ldP);
+    moe_swiglu_slots_kernel<<<glue_blocks(max_slots, num_sms), 256, 0, st>>>(gu, F, col_src, n_slots, q, dT, ldP);
     return cudaGetLastError();
 }
 
 cudaError_t launch_moe_combine_slots(const float * down, const float * w, const int32_t * inv, int64_t T, int64_t top_k, int64_t H,
                                      float * out, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
-    moe_combine_slots_kernel<<<(unsigned) T, 256, 0, st>>>(down, w, inv, top_k, H, out);
+    const int vec = ((uintptr_t) out % 16 == 0 && H % 4 == 0) ? 1 : 0;
+    moe_combine_slots_kernel<<<(unsigned) T, 256, 0, st>>>(down, w, inv, top_k, H, vec, out);
     return cudaGetLastError();
 }
 
