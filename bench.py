@@ -189,30 +189,106 @@ def run_reference(args):
     return 0
 
 
-def make_decoder(pkg, ctx, seed):
-    """Config 2's stack with device-generated random weights (quantized on the device by b200_quantize_rows)."""
+def make_decoder(pkg, ctx, seed, name=CONFIG):
+    """A decoder stack of stack.CONFIGS[name] with device-generated random weights: Q8_0 tensors are N(0, 0.02)
+    quantized on the device by b200_quantize_rows; K-quant tensors are random valid blocks."""
     import torch
 
     from oracle import stack
 
-    c = stack.CONFIGS[CONFIG]
+    c = stack.CONFIGS[name]
     d = pkg.Decoder(ctx, **c)
     g = torch.Generator(device="cuda")
     g.manual_seed(seed)
     sh = stack.tensor_shapes(c)
+
+    def blocks(t, k, rows):
+        if t == pkg.Q8_0:
+            return ctx.quantize_rows(t, torch.randn((rows, k), generator=g, device="cuda", dtype=torch.float32) * 0.02)
+        return _random_kquant_blocks(t, rows, k, g)
+
     names = ["attn_q", "attn_k", "attn_v", "attn_o", "ffn_gate", "ffn_up", "ffn_down"]
     for l in range(c["n_layer"]):
         for i, n in enumerate(names):
             t, k, rows = sh[n]
-            w = torch.randn((rows, k), generator=g, device="cuda", dtype=torch.float32) * 0.02
-            d.set_tensor(l, i, ctx.quantize_rows(t, w))
+            d.set_tensor(l, i, blocks(t, k, rows))
         d.set_tensor(l, pkg.DEC_ATTN_NORM, 1.0 + 0.1 * torch.randn(c["hidden"], generator=g, device="cuda"))
         d.set_tensor(l, pkg.DEC_FFN_NORM, 1.0 + 0.1 * torch.randn(c["hidden"], generator=g, device="cuda"))
     t, k, rows = sh["output"]
-    d.set_tensor(0, pkg.DEC_OUTPUT, ctx.quantize_rows(t, torch.randn((rows, k), generator=g, device="cuda") * 0.02))
+    d.set_tensor(0, pkg.DEC_OUTPUT, blocks(t, k, rows))
     d.set_tensor(0, pkg.DEC_OUTPUT_NORM, 1.0 + 0.1 * torch.randn(c["hidden"], generator=g, device="cuda"))
     ctx.synchronize()
     return d, c
+
+
+def config1_gemv(pkg, ctx, stream, copies=64, calls=256, reps=10):
+    """Config 1's single product (Q8_0, K = 1024, N = 3072, one activation row): 256 back-to-back b200_mul_mat calls
+    in one CUDA graph over 64 distinct weight copies (214 MB > L2), so every call streams its weights from HBM."""
+    import ctypes
+
+    import torch
+
+    K, N = 1024, 3072
+    g = torch.Generator(device="cuda").manual_seed(11)
+    ws = [ctx.weight(pkg.Q8_0, K, N, data=ctx.quantize_rows(pkg.Q8_0, torch.randn((N, K), generator=g, device="cuda") * 0.02))
+          for _ in range(copies)]
+    x = torch.randn((1, K), generator=g, device="cuda")
+    ys = [torch.empty((1, N), device="cuda") for _ in range(copies)]
+    ctx.synchronize()
+    fn, h = ctx.L.b200_mul_mat, ctx.h
+    args = [(ctypes.byref(ws[i % copies]), ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(ys[i % copies].data_ptr())) for i in range(calls)]
+
+    def run():
+        for w, xp, yp in args:
+            ctx.check(fn(h, w, xp, 1, yp))
+
+    run()
+    ctx.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        run()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / (reps * calls)
+    nbytes = ws[0].nbytes
+    del graph
+    for w in ws:
+        ctx.free_weight(w)
+    return {"K": K, "N": N, "weight_bytes": nbytes, "copies": copies, "calls_per_graph": calls, "us_per_call": us,
+            "gbs": nbytes / us / 1e3}
+
+
+def config3_decode(pkg, ctx, stream, steps=128):
+    """Config 3's decode phase: 128 batch-1 steps of the Qwen3-ASR 1.7B-shaped decoder (Q4_K attention and gate|up,
+    Q6_K down and the 2048 -> 151936 head; random valid blocks), one persistent launch per step."""
+    import torch
+
+    dec, c = make_decoder(pkg, ctx, seed=4321, name="asr17")
+    x = torch.randn(c["hidden"], generator=torch.Generator(device="cuda").manual_seed(9), device="cuda")
+    logits = torch.empty(c["n_vocab"], device="cuda")
+    for _ in range(3):
+        dec.step_raw(x.data_ptr(), logits.data_ptr())
+    ctx.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        dec.step_raw(x.data_ptr(), logits.data_ptr())
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    wb = dec.weight_bytes
+    out = {"steps": steps, "ms_per_step": ms, "tok_s": 1000.0 / ms, "weight_bytes": wb, "gbs": wb / ms / 1e6,
+           "launches_per_step": dec.launches}
+    del dec
+    return out
 
 
 def large_gemv(pkg, ctx, stream, reps=20):
@@ -576,6 +652,11 @@ def run_b200(args):
     wbytes = dec.weight_bytes
     launches = dec.launches
     gemv = large_gemv(pkg, ctx, stream) if world == 1 or rank == 0 else None
+    extra = None
+    if world == 1 and not args.no_configs:
+        del dec
+        dec = None
+        extra = {"c1_gemv_q8_0": config1_gemv(pkg, ctx, stream), "c3_asr17_decode": config3_decode(pkg, ctx, stream)}
     peak, peak_kind = peaks()
     achieved = wbytes / (ms_step / 1000.0) / 1e9  # GB/s of algorithmic weight bytes, per GPU
     traffic = profile_traffic()
@@ -598,6 +679,7 @@ def run_b200(args):
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": c["hidden"] * 4, "d2h_bytes_per_step": c["n_vocab"] * 4},
             "gpu_launches": launches * args.steps,
             "gemv_large": {k: dict(v, frac=v["gbs"] / peak) for k, v in (gemv or {}).items()},
+            "configs": {k: dict(v, frac=v["gbs"] / peak) for k, v in (extra or {}).items()},
             "clocks": clk.summary(),
         }
     del dec
@@ -620,6 +702,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--no-configs", action="store_true", help="skip the config 1 and config 3 side measurements")
     ap.add_argument("--workload", default="decode", choices=["decode", "moe"],
                     help="decode: config 2 decode step (the headline line); moe: config 5 MoE FFN stack, expert-parallel")
     ap.add_argument("--moe-steps", type=int, default=20, help="timed steps of the MoE workload")

@@ -111,6 +111,25 @@ __device__ __forceinline__ bool mbar_wait(uint64_t * bar, uint32_t parity) {
     return false;
 }
 
+// The same wait with a suspend-time hint: a thread whose phase is not complete sleeps (up to ~0.5 us per poll, woken
+// early when the phase completes) instead of re-polling, which leaves issue slots to the warps doing work. Bounded by
+// kSpinLimit polls.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t * bar, uint32_t parity) {
+    const uint32_t a = smem_addr(bar);
+    for (uint32_t i = 0; i < kSpinLimit; i++) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(a), "r"(parity), "r"(500u)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
 // One bulk copy of `bytes` (multiple of 16; both addresses 16-byte aligned) from global to this CTA's shared memory,
 // completing `bytes` of the barrier's transaction count.
 __device__ __forceinline__ void bulk_g2s(void * dst, const void * src, uint32_t bytes, uint64_t * bar) {

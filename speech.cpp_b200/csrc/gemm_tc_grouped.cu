@@ -43,7 +43,7 @@ struct GLayout {
 struct GroupedParams {
     int64_t N;                // rows per expert (output width)
     int64_t K;
-    const int4 * tiles;       // {expert, first slot, slots (multiple of 16, <= 64), 0}
+    const int4 * tiles;       // {expert, first slot, slots (multiple of 16, <= 64), routed slots (the rest is padding)}
     const int * ntiles;       // number of tiles (device)
     int tiles_n;              // 128-row tiles per expert
     const int32_t * row_map;  // output row of each slot (< 0: none); null: the slot itself
@@ -102,7 +102,7 @@ __global__ void __launch_bounds__(kGThreads, 2)
                 const uint32_t bytes = (uint32_t) (L::kA + t.z * 256 + L::kDw + L::kDx);
                 for (int st = 0; st < nstage; st++, sg++) {
                     const int s = sg % kGStages, use = sg / kGStages;
-                    if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) {
+                    if (use > 0 && !mbar_wait_sleep(&empty[s], (use - 1) & 1)) {
                         atomicOr(p.err, kErrTimeout);
                         give_up = 1;
                         break;
@@ -130,7 +130,7 @@ __global__ void __launch_bounds__(kGThreads, 2)
                 const uint32_t idesc = idesc_i8_n(t.z);
                 for (int st = 0; st < nstage && !give_up; st++, sg++) {
                     const int s = sg % kGStages;
-                    if (!mbar_wait(&full[s], (sg / kGStages) & 1)) {
+                    if (!mbar_wait_sleep(&full[s], (sg / kGStages) & 1)) {
                         atomicOr(p.err, kErrTimeout);
                         give_up = 1;
                         break;
@@ -139,7 +139,7 @@ __global__ void __launch_bounds__(kGThreads, 2)
                     uint8_t * base = smem + s * L::kStage;
                     for (int j = 0; j < kGKB; j += 2, g2++) {
                         const int buf = g2 % kGBufs, use = g2 / kGBufs;
-                        if (use > 0 && !mbar_wait(&acc_empty[buf], (use - 1) & 1)) {
+                        if (use > 0 && !mbar_wait_sleep(&acc_empty[buf], (use - 1) & 1)) {
                             atomicOr(p.err, kErrTimeout);
                             give_up = 1;
                             break;
@@ -170,6 +170,7 @@ __global__ void __launch_bounds__(kGThreads, 2)
             const int tn = it % p.tiles_n;
             const int nch = t.z / 16;
             const bool has0 = h < nch, has1 = h + 2 < nch;
+            const int live = t.w;  // slots before this one are routed pairs; later ones are padding (no math)
             float2 acc[16];
 #pragma unroll
             for (int i = 0; i < 16; i++) acc[i] = make_float2(0.0f, 0.0f);
@@ -180,7 +181,7 @@ __global__ void __launch_bounds__(kGThreads, 2)
                 const float * dxT = reinterpret_cast<const float *>(base + L::kA + L::kB + L::kDw);
                 for (int j = 0; j < kGKB; j += 2, g2++) {
                     const int buf = g2 % kGBufs, use = g2 / kGBufs;
-                    if (!mbar_wait(&acc_full[buf], use & 1)) {
+                    if (!mbar_wait_sleep(&acc_full[buf], use & 1)) {
                         if (lane == 0) atomicOr(p.err, kErrTimeout);
                         give_up = 1;
                         break;
@@ -216,6 +217,7 @@ __global__ void __launch_bounds__(kGThreads, 2)
                             const float4 * dx4 = reinterpret_cast<const float4 *>(dxT + (j + jj) * kGNT + 16 * (h + 2 * c));
 #pragma unroll
                             for (int t4 = 0; t4 < 4; t4++) {
+                                if (16 * (h + 2 * c) + 4 * t4 >= live) break;
                                 const float4 d = dx4[t4];
                                 const int * vv = v[c] + 4 * t4;
                                 const float2 s01 = __fmul2_rn(make_float2(d.x, d.y), w2);

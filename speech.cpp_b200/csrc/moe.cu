@@ -7,7 +7,7 @@ namespace b200 {
 
 // One CTA: histogram of the local experts' pairs, exclusive scans of the counts rounded up to 16 (segment starts) and
 // of the segments' tile counts, placement of every pair in its expert's segment, the padding slots marked empty, and
-// the list of token tiles (<= 64 slots each, in expert order). Pair p = t * top_k + s reads activation row
+// the list of token tiles (<= 64 slots each, in expert order; .w = how many of them hold routed pairs). Pair p = t * top_k + s reads activation row
 // t * nb1 + (nb1 == 1 ? 0 : s). Pairs of experts outside [e0, e0 + E) are skipped (another shard's); ids outside
 // [0, total) are reported. inv[p] = the pair's slot, or -1.
 __global__ void moe_route_kernel(const int32_t * __restrict__ ids, int64_t P, int64_t top_k, int64_t nb1, int E, int e0, int total,
@@ -78,13 +78,15 @@ __global__ void moe_route_kernel(const int32_t * __restrict__ ids, int64_t P, in
             col_src[slot] = -1;
             col_dst[slot] = -1;
         }
-        for (int o = 0, k = toff[e]; o < len; o += 64, k++) tiles[k] = make_int4(e, start[e] + o, min(64, len - o), 0);
+        for (int o = 0, k = toff[e]; o < len; o += 64, k++)
+            tiles[k] = make_int4(e, start[e] + o, min(64, len - o), max(0, min(64, cnt[e] - o)));
     }
 }
 
 // q8_0 quantization of each slot's activation row (zeros for padding), in slot order: q [slots][K], dT [K/32][ldP].
 // One warp per slot row, 128 values per step (a block per 8 lanes); bit-identical to the CPU backend's
 // quantize_row_q8_0 of the same row. vec: x and ldx allow 16-byte loads.
+template <int U>
 __global__ void moe_quant_slots_kernel(const float * __restrict__ x, int64_t K, int64_t ldx, int vec, const int32_t * __restrict__ col_src,
                                        const int32_t * __restrict__ n_slots, int8_t * q, float * dT, int64_t ldP) {
     const int lane = threadIdx.x & 31;
@@ -93,15 +95,24 @@ __global__ void moe_quant_slots_kernel(const float * __restrict__ x, int64_t K, 
     for (int slot = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); slot < S; slot += warps) {
         const int32_t src = col_src[slot];
         const float * xr = src >= 0 ? x + (int64_t) src * ldx : nullptr;
-        for (int64_t k0 = 0; k0 < K; k0 += 128) {
-            const int64_t k = k0 + 4 * lane;
-            float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            if (xr && k < K) v = vec ? *reinterpret_cast<const float4 *>(xr + k) : make_float4(xr[k], xr[k + 1], xr[k + 2], xr[k + 3]);
-            float d;
-            const uint32_t packed = quantize_q8_0_quad(v, &d);
-            if (k < K) {
-                *reinterpret_cast<uint32_t *>(q + (int64_t) slot * K + k) = packed;
-                if ((lane & 7) == 0) dT[(k >> 5) * ldP + slot] = d;
+        for (int64_t k0 = 0; k0 < K; k0 += 128 * U) {
+            float4 v[U];  // U loads in flight before any arithmetic
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int64_t k = k0 + 128 * u + 4 * lane;
+                v[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (xr && k < K) v[u] = vec ? *reinterpret_cast<const float4 *>(xr + k) : make_float4(xr[k], xr[k + 1], xr[k + 2], xr[k + 3]);
+            }
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int64_t k = k0 + 128 * u + 4 * lane;
+                if (k0 + 128 * u >= K) break;
+                float d;
+                const uint32_t packed = quantize_q8_0_quad(v[u], &d);
+                if (k < K) {
+                    *reinterpret_cast<uint32_t *>(q + (int64_t) slot * K + k) = packed;
+                    if ((lane & 7) == 0) dT[(k >> 5) * ldP + slot] = d;
+                }
             }
         }
     }
@@ -109,6 +120,7 @@ __global__ void moe_quant_slots_kernel(const float * __restrict__ x, int64_t K, 
 
 // SwiGLU of each slot's gate|up row (gu [slots][2F]: gate F, then up F), re-quantized to q8_0 in slot order for the
 // down product: q [slots][F], dT [F/32][ldP]; zeros for padding. One warp per slot row, 128 values per step.
+template <int U>
 __global__ void moe_swiglu_slots_kernel(const float * __restrict__ gu, int64_t F, const int32_t * __restrict__ col_src,
                                         const int32_t * __restrict__ n_slots, int8_t * q, float * dT, int64_t ldP) {
     const int lane = threadIdx.x & 31;
@@ -117,19 +129,29 @@ __global__ void moe_swiglu_slots_kernel(const float * __restrict__ gu, int64_t F
     for (int slot = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); slot < S; slot += warps) {
         const bool live = col_src[slot] >= 0;
         const float * row = gu + (int64_t) slot * 2 * F;
-        for (int64_t k0 = 0; k0 < F; k0 += 128) {
-            const int64_t k = k0 + 4 * lane;
-            float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            if (live && k < F) {
-                const float4 g = *reinterpret_cast<const float4 *>(row + k);
-                const float4 u = *reinterpret_cast<const float4 *>(row + F + k);
-                v = make_float4(__fmul_rn(silu(g.x), u.x), __fmul_rn(silu(g.y), u.y), __fmul_rn(silu(g.z), u.z), __fmul_rn(silu(g.w), u.w));
+        for (int64_t k0 = 0; k0 < F; k0 += 128 * U) {
+            float4 g[U], u4[U];  // U gate and up loads in flight before any arithmetic
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int64_t k = k0 + 128 * u + 4 * lane;
+                g[u] = u4[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (live && k < F) {
+                    g[u] = *reinterpret_cast<const float4 *>(row + k);
+                    u4[u] = *reinterpret_cast<const float4 *>(row + F + k);
+                }
             }
-            float d;
-            const uint32_t packed = quantize_q8_0_quad(v, &d);
-            if (k < F) {
-                *reinterpret_cast<uint32_t *>(q + (int64_t) slot * F + k) = packed;
-                if ((lane & 7) == 0) dT[(k >> 5) * ldP + slot] = d;
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int64_t k = k0 + 128 * u + 4 * lane;
+                if (k0 + 128 * u >= F) break;
+                const float4 v = make_float4(__fmul_rn(silu(g[u].x), u4[u].x), __fmul_rn(silu(g[u].y), u4[u].y),
+                                             __fmul_rn(silu(g[u].z), u4[u].z), __fmul_rn(silu(g[u].w), u4[u].w));
+                float d;
+                const uint32_t packed = quantize_q8_0_quad(v, &d);
+                if (k < F) {
+                    *reinterpret_cast<uint32_t *>(q + (int64_t) slot * F + k) = packed;
+                    if ((lane & 7) == 0) dT[(k >> 5) * ldP + slot] = d;
+                }
             }
         }
     }
@@ -139,19 +161,35 @@ __global__ void moe_swiglu_slots_kernel(const float * __restrict__ gu, int64_t F
 // vec: out allows 16-byte stores and H % 4 == 0.
 __global__ void moe_combine_slots_kernel(const float * __restrict__ down, const float * __restrict__ w, const int32_t * __restrict__ inv,
                                          int64_t top_k, int64_t H, int vec, float * __restrict__ out) {
+    extern __shared__ int cslot[];  // [top_k] slots, then [top_k] weights
+    float * cw = reinterpret_cast<float *>(cslot + top_k);
     const int64_t t = blockIdx.x;
+    for (int64_t s = threadIdx.x; s < top_k; s += blockDim.x) {
+        cslot[s] = inv[t * top_k + s];
+        cw[s] = w[t * top_k + s];
+    }
+    __syncthreads();
     if (vec) {
         for (int64_t h = 4 * (int64_t) threadIdx.x; h < H; h += 4 * (int64_t) blockDim.x) {
             float4 sum = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
             bool any = false;
-            for (int64_t s = 0; s < top_k; s++) {
-                const int32_t slot = inv[t * top_k + s];
-                if (slot < 0) continue;
-                const float ws = w[t * top_k + s];
-                const float4 d = *reinterpret_cast<const float4 *>(down + (int64_t) slot * H + h);
-                const float4 v = make_float4(__fmul_rn(d.x, ws), __fmul_rn(d.y, ws), __fmul_rn(d.z, ws), __fmul_rn(d.w, ws));
-                sum = any ? make_float4(__fadd_rn(sum.x, v.x), __fadd_rn(sum.y, v.y), __fadd_rn(sum.z, v.z), __fadd_rn(sum.w, v.w)) : v;
-                any = true;
+            for (int64_t s0 = 0; s0 < top_k; s0 += 8) {
+                float4 d[8];  // eight rows in flight
+#pragma unroll
+                for (int u = 0; u < 8; u++) {
+                    const int64_t s = s0 + u;
+                    d[u] = (s < top_k && cslot[s] >= 0) ? *reinterpret_cast<const float4 *>(down + (int64_t) cslot[s] * H + h)
+                                                        : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                }
+#pragma unroll
+                for (int u = 0; u < 8; u++) {
+                    const int64_t s = s0 + u;
+                    if (s >= top_k || cslot[s] < 0) continue;
+                    const float ws = cw[s];
+                    const float4 v = make_float4(__fmul_rn(d[u].x, ws), __fmul_rn(d[u].y, ws), __fmul_rn(d[u].z, ws), __fmul_rn(d[u].w, ws));
+                    sum = any ? make_float4(__fadd_rn(sum.x, v.x), __fadd_rn(sum.y, v.y), __fadd_rn(sum.z, v.z), __fadd_rn(sum.w, v.w)) : v;
+                    any = true;
+                }
             }
             *reinterpret_cast<float4 *>(out + t * H + h) = sum;
         }
@@ -161,9 +199,9 @@ __global__ void moe_combine_slots_kernel(const float * __restrict__ down, const 
         float sum = 0.0f;
         bool any = false;
         for (int64_t s = 0; s < top_k; s++) {
-            const int32_t slot = inv[t * top_k + s];
+            const int32_t slot = cslot[s];
             if (slot < 0) continue;
-            const float v = __fmul_rn(down[(int64_t) slot * H + h], w[t * top_k + s]);
+            const float v = __fmul_rn(down[(int64_t) slot * H + h], cw[s]);
             sum = any ? __fadd_rn(sum, v) : v;
             any = true;
         }
@@ -194,13 +232,13 @@ static unsigned glue_blocks(int64_t work_warps, int num_sms) {
 cudaError_t launch_moe_quant_slots(const float * x, int64_t K, int64_t ldx, const int32_t * col_src, const int32_t * n_slots,
                                    int64_t max_slots, int8_t * q, float * dT, int64_t ldP, int num_sms, cudaStream_t st) {
     const int vec = ((uintptr_t) x % 16 == 0 && ldx % 4 == 0) ? 1 : 0;
-    moe_quant_slots_kernel<<<glue_blocks(max_slots, num_sms), 256, 0, st>>>(x, K, ldx, vec, col_src, n_slots, q, dT, ldP);
+    moe_quant_slots_kernel<8><<<glue_blocks(max_slots, num_sms), 256, 0, st>>>(x, K, ldx, vec, col_src, n_slots, q, dT, ldP);
     return cudaGetLastError();
 }
 
 cudaError_t launch_moe_swiglu_slots(const float * gu, int64_t F, const int32_t * col_src, const int32_t * n_slots, int64_t max_slots,
                                     int8_t * q, float * dT, int64_t ldP, int num_sms, cudaStream_t st) {
-    moe_swiglu_slots_kernel<<<glue_blocks(max_slots, num_sms), 256, 0, st>>>(gu, F, col_src, n_slots, q, dT, ldP);
+    moe_swiglu_slots_kernel<4><<<glue_blocks(max_slots, num_sms), 256, 0, st>>>(gu, F, col_src, n_slots, q, dT, ldP);
     return cudaGetLastError();
 }
 
@@ -208,7 +246,7 @@ cudaError_t launch_moe_combine_slots(const float * down, const float * w, const 
                                      float * out, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
     const int vec = ((uintptr_t) out % 16 == 0 && H % 4 == 0) ? 1 : 0;
-    moe_combine_slots_kernel<<<(unsigned) T, 256, 0, st>>>(down, w, inv, top_k, H, vec, out);
+    moe_combine_slots_kernel<<<(unsigned) T, 256, (size_t) top_k * 8, st>>>(down, w, inv, top_k, H, vec, out);
     return cudaGetLastError();
 }
 
