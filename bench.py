@@ -51,14 +51,19 @@ def peaks():
         return 6650.0, "fallback"
 
 
+# DRAM bytes (read + write) of one decoder_mk_kernel launch of this step, from the ncu capture summarised in
+# profiles/decoder_mk_kernel_tts06_decode_step.md (dram__bytes_read.sum + dram__bytes_write.sum).
+DECODE_TRAFFIC = {"dram_bytes_per_step": 471604992 + 4361472,
+                  "source": "ncu --set full of one decoder_mk_kernel launch (profiles/decoder_mk_kernel_tts06_decode_step.md)"}
+
+
+# DRAM bytes of one layer's two gemm_q8_0_tc_grouped_kernel launches (gate|up + down) from the ncu capture of the
+# 2-layer case summarised in profiles/gemm_q8_0_tc_grouped_config5.md; the step's traffic scales with its layers.
+MOE_TRAFFIC_PER_LAYER = 434741504 + 16279808 + 216521216 + 16315904
+
+
 def profile_traffic():
-    """DRAM bytes per launch of the dominant kernel from the committed ncu summary (profiles/), when present."""
-    path = os.path.join(ROOT, "profiles", "traffic.json")
-    try:
-        with open(path) as f:
-            return json.load(f)
-    except Exception:
-        return None
+    return DECODE_TRAFFIC
 
 
 class Clocks:
@@ -547,10 +552,12 @@ def run_moe(args, pkg, ctx, dist, world, rank, local):
                                "over 128 Q8_0 experts, top-8 of N(0,1) router logits, 256 N(0,1) tokens",
                    "global_batch": T, "parallelism": f"expert-parallel x{world} (all-reduce of combined outputs)" if world > 1 else "single",
                    "l2": f"expert weights {wbytes / 1e9:.1f} GB per GPU > 126 MB L2 (no flush needed)"},
-        "roofline": {"bound": "hbm", "kernel": "grouped gemv_kernel<TQ8_0> (gate|up and down of every layer)", "achieved": achieved,
-                     "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+        "roofline": {"bound": "hbm", "kernel": "the b200_moe_ffn stack (gemm_q8_0_tc_grouped_kernel x 2 + 4 glue kernels per layer)",
+                     "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6650",
-                     "algorithmic_bytes_per_step": wbytes, "traffic": None},
+                     "algorithmic_bytes_per_step": wbytes,
+                     "traffic": MOE_TRAFFIC_PER_LAYER * L // world,
+                     "traffic_source": "ncu capture of the 2-layer case (profiles/gemm_q8_0_tc_grouped_config5.md), scaled by layers and shards"},
         "e2e": {"value": T * steps / (ems / 1000.0), "unit": UNIT, "h2d_bytes_per_step": T * H * 4 + ids_h.nbytes + w_h.nbytes,
                 "d2h_bytes_per_step": T * H * 4},
         "gpu_launches": 6 * L * steps,
