@@ -9,7 +9,8 @@
 // (16..64, a run-time field of the instruction descriptor) x K = 32 computes the block's exact int32 sums. Blocks go in
 // pairs into one of two tensor-memory buffers (2 x 64 columns each), one barrier round trip per pair; epilogue warps
 // read a pair's sums (tcgen05.ld), scale them by d_w[row][b] * d_x[slot][b] and add them to float32 registers in
-// block order, as ggml's CPU vec_dot does. Operands come by TMA (2-D tensor maps, 128-byte swizzle, no multicast). The grid is persistent (two CTAs per SM) and walks the items in a fixed order; every role of
+// block order, as ggml's CPU vec_dot does. Operands come by TMA (2-D tensor maps, 128-byte swizzle, no multicast).
+// The grid is persistent (two CTAs per SM) and walks the items in a fixed order; every role of
 // a CTA derives the same item sequence from the tile list, so they need no other coordination than the stage and
 // accumulator barriers. Warp roles: 0 = TMA producer, 1 = tensor-memory allocator and MMA issuer (one thread),
 // 2..9 = epilogue. Every wait is bounded; one that gives up records B200_DEVERR_TIMEOUT and the CTA runs to its end
