@@ -8,8 +8,8 @@
 // matrix. Per 32-wide K block, one tcgen05.mma kind::i8 of shape M = 128 (weight rows) x N = the tile's token count
 // (16..64, a run-time field of the instruction descriptor) x K = 32 computes the block's exact int32 sums. Blocks go in
 // pairs into one of two tensor-memory buffers (2 x 64 columns each), one barrier round trip per pair; epilogue warps
-// read a pair's sums (tcgen05.ld), scale them by d_w[row][b] * d_x[slot][b] and add them to float32 registers in
-// block order, as ggml's CPU vec_dot does. Operands come by TMA (2-D tensor maps, 128-byte swizzle, no multicast).
+// read a pair's sums (tcgen05.ld), scale them by d_w[row][b] * d_x[slot][b] and add them to float32 registers, as
+// ggml's CPU vec_dot does (block order within each of the two halves of K a tile of <= 32 slots is split into). Operands come by TMA (2-D tensor maps, 128-byte swizzle, no multicast).
 // The grid is persistent (two CTAs per SM) and walks the items in a fixed order; every role of
 // a CTA derives the same item sequence from the tile list, so they need no other coordination than the stage and
 // accumulator barriers. Warp roles: 0 = TMA producer, 1 = tensor-memory allocator and MMA issuer (one thread),
@@ -64,7 +64,8 @@ __global__ void __launch_bounds__(kGThreads, 2)
     uint64_t * empty = bars + kGStages;
     uint64_t * acc_full = bars + 2 * kGStages;   // [bufs] a block pair's int32 sums ready in tensor memory
     uint64_t * acc_empty = acc_full + kGBufs;    // [bufs] epilogue has read them
-    uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + kGBufs);
+    uint64_t * xchg = acc_empty + kGBufs;        // [4] split-K tiles: group 1's partial sums of lane quarter q stored
+    uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(xchg + 4);
     __shared__ volatile int give_up;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -80,6 +81,7 @@ __global__ void __launch_bounds__(kGThreads, 2)
             mbar_init(&acc_full[b], 1);
             mbar_init(&acc_empty[b], kGEpiWarps);
         }
+        for (int q = 0; q < 4; q++) mbar_init(&xchg[q], 1);
         fence_mbar_init();
         give_up = 0;
     }
@@ -158,19 +160,25 @@ __global__ void __launch_bounds__(kGThreads, 2)
             }
         }
     } else {
-        // ---- epilogue: lane quarter q = warp % 4 owns tile rows 32 q .. 32 q + 31 (one per lane); warp half h takes
-        // the 16-slot column chunks h and h + 2 of the tile. A warp without columns in a tile (h = 1 in a tile of one
-        // chunk) still waits and arrives on every barrier, so no warp runs a phase ahead of the others: parity waits
-        // cannot tell phase n from phase n + 2 ----
+        // ---- epilogue: lane quarter q = warp % 4 owns tile rows 32 q .. 32 q + 31 (one per lane); h = warp group.
+        // Tiles of up to two 16-slot chunks are split along K: group h takes the block pairs of parity h (pair g sits in
+        // buffer g % 2, so each buffer has one group of consumers, which arrive for the other group too), all columns;
+        // at the tile's end group 1 stores its partial sums and group 0 adds its own (a two-term sum: the result does
+        // not depend on timing). Wider tiles are split along columns: group h takes chunks h and h + 2 of every pair;
+        // a warp without columns still waits and arrives on every barrier. Every consumer of a barrier consumes each
+        // of its phases in order, so no warp runs a phase ahead: parity waits cannot tell phase n from n + 2 ----
         const int q = warp & 3, h = (warp - 2) >> 2;
         const int row = 32 * q + lane;
         const float2 neg_magic = make_float2(-12582912.0f, -12582912.0f);
-        int sg = 0, g2 = 0;
+        int sg = 0, g2 = 0, xi = 0;
         for (int it = blockIdx.x; it < items && !give_up; it += gridDim.x) {
             const int4 t = p.tiles[it / p.tiles_n];
             const int tn = it % p.tiles_n;
             const int nch = t.z / 16;
-            const bool has0 = h < nch, has1 = h + 2 < nch;
+            const bool split = nch <= 2;
+            const int ch0 = split ? 0 : h, ch1 = split ? 1 : h + 2;  // the (up to) two chunks this warp reduces
+            const bool has0 = split || h < nch, has1 = split ? nch == 2 : h + 2 < nch;
+            const uint32_t arrivals = split ? 2u : 1u;
             const int live = t.w;  // slots before this one are routed pairs; later ones are padding (no math)
             float2 acc[16];
 #pragma unroll
@@ -182,13 +190,14 @@ __global__ void __launch_bounds__(kGThreads, 2)
                 const float * dxT = reinterpret_cast<const float *>(base + L::kA + L::kB + L::kDw);
                 for (int j = 0; j < kGKB; j += 2, g2++) {
                     const int buf = g2 % kGBufs, use = g2 / kGBufs;
+                    if (split && buf != h) continue;  // the other group's pair (its consumers arrive for this warp)
                     if (!mbar_wait_sleep(&acc_full[buf], use & 1)) {
                         if (lane == 0) atomicOr(p.err, kErrTimeout);
                         give_up = 1;
                         break;
                     }
                     tc_fence_after();
-                    if (!has0) {  // no columns in this tile: only the barrier protocol, which keeps this warp in step
+                    if (!has0) {  // no columns in this tile: only the barrier protocol
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&acc_empty[buf]);
                         continue;
@@ -200,13 +209,13 @@ __global__ void __launch_bounds__(kGThreads, 2)
 #pragma unroll
                     for (int jj = 0; jj < 2; jj++) {
                         int v[2][16];  // [chunk][column]
-                        tmem_ld16(ta + jj * kGNT + 16 * h, v[0]);
-                        if (has1) tmem_ld16(ta + jj * kGNT + 16 * (h + 2), v[1]);
+                        tmem_ld16(ta + jj * kGNT + 16 * ch0, v[0]);
+                        if (has1) tmem_ld16(ta + jj * kGNT + 16 * ch1, v[1]);
                         tmem_wait_ld();
                         if (jj == 1) {
                             tc_fence_before();
                             __syncwarp();
-                            if (lane == 0) mbar_arrive(&acc_empty[buf]);
+                            if (lane == 0) mbar_arrive_n(&acc_empty[buf], arrivals);
                         }
                         // acc += float(sum) * (d_x * d_w), in block order; |sum| <= 32 * 127 * 128 < 2^22 converts
                         // exactly through the float 12582912 + sum (bit pattern 0x4B400000 + sum)
@@ -215,10 +224,11 @@ __global__ void __launch_bounds__(kGThreads, 2)
 #pragma unroll
                         for (int c = 0; c < 2; c++) {
                             if (c == 1 && !has1) continue;
-                            const float4 * dx4 = reinterpret_cast<const float4 *>(dxT + (j + jj) * kGNT + 16 * (h + 2 * c));
+                            const int col0 = 16 * (c ? ch1 : ch0);
+                            const float4 * dx4 = reinterpret_cast<const float4 *>(dxT + (j + jj) * kGNT + col0);
 #pragma unroll
                             for (int t4 = 0; t4 < 4; t4++) {
-                                if (16 * (h + 2 * c) + 4 * t4 >= live) break;
+                                if (col0 + 4 * t4 >= live) break;
                                 const float4 d = dx4[t4];
                                 const int * vv = v[c] + 4 * t4;
                                 const float2 s01 = __fmul2_rn(make_float2(d.x, d.y), w2);
@@ -236,23 +246,57 @@ __global__ void __launch_bounds__(kGThreads, 2)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[s]);
             }
-            if (give_up || !has0) continue;
+            if (give_up) break;
+            if (!has0) continue;
             // ---- output: one weight row per lane, so each slot's store is one coalesced 128-byte line ----
             const int64_t grow = (int64_t) tn * kGM + row;
-            if (grow < p.N) {
+            const bool in_rows = grow < p.N;
+            if (split && h == 1) {  // store the partial sums for group 0, then signal it
+                if (in_rows)
+#pragma unroll
+                    for (int c = 0; c < 2; c++) {
+                        if (c == 1 && !has1) continue;
+#pragma unroll
+                        for (int i = 0; i < 16; i++) {
+                            const int col = 16 * c + i;
+                            if (col >= live) break;
+                            const int64_t orow = p.row_map ? (int64_t) p.row_map[t.y + col] : (int64_t) (t.y + col);
+                            const float2 a = acc[8 * c + i / 2];
+                            if (orow >= 0) p.y[orow * p.ldy + grow] = (i & 1) ? a.y : a.x;
+                        }
+                    }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&xchg[q]);
+                xi++;
+                continue;
+            }
+            if (split) {  // group 0: wait for group 1's partial sums of these rows
+                if (!mbar_wait_sleep(&xchg[q], xi & 1)) {
+                    if (lane == 0) atomicOr(p.err, kErrTimeout);
+                    give_up = 1;
+                    break;
+                }
+                xi++;
+            }
+            if (in_rows)
 #pragma unroll
                 for (int c = 0; c < 2; c++) {
                     if (c == 1 && !has1) continue;
-                    const int col0 = 16 * (h + 2 * c);
+                    const int col0 = 16 * (c ? ch1 : ch0);
 #pragma unroll
                     for (int i = 0; i < 16; i++) {
-                        const int slot = t.y + col0 + i;
-                        const int64_t orow = p.row_map ? (int64_t) p.row_map[slot] : (int64_t) slot;
+                        const int col = col0 + i;
+                        if (col >= live) break;
+                        const int64_t orow = p.row_map ? (int64_t) p.row_map[t.y + col] : (int64_t) (t.y + col);
                         const float2 a = acc[8 * c + i / 2];
-                        if (orow >= 0) p.y[orow * p.ldy + grow] = (i & 1) ? a.y : a.x;
+                        float v = (i & 1) ? a.y : a.x;
+                        if (orow >= 0) {
+                            float * dst = p.y + orow * p.ldy + grow;
+                            if (split) v = __fadd_rn(v, *reinterpret_cast<volatile float *>(dst));
+                            *dst = v;
+                        }
                     }
                 }
-            }
         }
     }
     tc_fence_before();
