@@ -8,8 +8,8 @@
 // matrix. Per 32-wide K block, one tcgen05.mma kind::i8 of shape M = 128 (weight rows) x N = the tile's token count
 // (16..64, a run-time field of the instruction descriptor) x K = 32 computes the block's exact int32 sums. Blocks go in
 // pairs into one of two tensor-memory buffers (2 x 64 columns each), one barrier round trip per pair; epilogue warps
-// read a pair's sums (tcgen05.ld), scale them by d_w[row][b] * d_x[slot][b] and add them to float32 registers, as
-// ggml's CPU vec_dot does (block order within each of the two halves of K a tile of <= 32 slots is split into). Operands come by TMA (2-D tensor maps, 128-byte swizzle, no multicast).
+// read a pair's sums (tcgen05.ld), scale them by d_w[row][b] * d_x[slot][b] and add them to float32 registers in
+// block order, as ggml's CPU vec_dot does. Operands come by TMA (2-D tensor maps, 128-byte swizzle, no multicast).
 // The grid is persistent (two CTAs per SM) and walks the items in a fixed order; every role of
 // a CTA derives the same item sequence from the tile list, so they need no other coordination than the stage and
 // accumulator barriers. Warp roles: 0 = TMA producer, 1 = tensor-memory allocator and MMA issuer (one thread),
@@ -23,8 +23,8 @@ namespace b200 {
 namespace {
 
 constexpr int kGM = 128;       // weight rows per tile (MMA M)
-constexpr int kGKB = 8;        // 32-wide K blocks per pipeline stage
-constexpr int kGStages = 2;
+constexpr int kGKB = 4;        // 32-wide K blocks per pipeline stage (one 128-byte row of each operand)
+constexpr int kGStages = 4;    // three stages stream while one is consumed
 constexpr int kGThreads = 320; // producer, MMA, 8 epilogue warps
 constexpr int kGEpiWarps = 8;
 constexpr int kGBufs = 2;      // tensor-memory accumulators in flight, one K-block pair (2 x kGNT columns) each
@@ -32,12 +32,13 @@ constexpr int kGNT = 64;       // slots per token tile (largest MMA N used)
 constexpr unsigned kErrTimeout = 4u;
 
 struct GLayout {
-    static constexpr int kA = kGKB * kGM * 32;   // weights: two [128 rows][128 B] swizzled tiles
-    static constexpr int kB = kGKB * kGNT * 32;  // activations: two [64 rows][128 B] swizzled tiles
-    static constexpr int kDw = kGM * kGKB * 2;   // fp16 weight scales [128][8]
-    static constexpr int kDx = kGKB * kGNT * 4;  // f32 activation scales [8][64]
+    static constexpr int kA = kGKB * kGM * 32;   // weights: one [128 rows][128 B] swizzled tile
+    static constexpr int kB = kGKB * kGNT * 32;  // activations: one [64 rows][128 B] swizzled tile
+    static constexpr int kDw = kGM * 8 * 2;      // fp16 weight scales [128][8]: the 16-byte box of 8 blocks that
+                                                 // holds this stage's 4 (TMA boxes start 16-byte aligned)
+    static constexpr int kDx = kGKB * kGNT * 4;  // f32 activation scales [4][64]
     static constexpr int kStage = kA + kB + kDw + kDx;
-    static constexpr int kTotal = kGStages * kStage + 1024 + 1024;  // + barriers + alignment slack
+    static constexpr int kTotal = kGStages * kStage + 1024 + 1024;  // + barriers + alignment slack (2 CTAs per SM fit)
     static_assert(kA % 1024 == 0 && kB % 1024 == 0 && kStage % 1024 == 0, "stage regions stay 1024-aligned");
 };
 
@@ -64,8 +65,7 @@ __global__ void __launch_bounds__(kGThreads, 2)
     uint64_t * empty = bars + kGStages;
     uint64_t * acc_full = bars + 2 * kGStages;   // [bufs] a block pair's int32 sums ready in tensor memory
     uint64_t * acc_empty = acc_full + kGBufs;    // [bufs] epilogue has read them
-    uint64_t * xchg = acc_empty + kGBufs;        // [4] split-K tiles: group 1's partial sums of lane quarter q stored
-    uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(xchg + 4);
+    uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + kGBufs);
     __shared__ volatile int give_up;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -81,7 +81,6 @@ __global__ void __launch_bounds__(kGThreads, 2)
             mbar_init(&acc_full[b], 1);
             mbar_init(&acc_empty[b], kGEpiWarps);
         }
-        for (int q = 0; q < 4; q++) mbar_init(&xchg[q], 1);
         fence_mbar_init();
         give_up = 0;
     }
@@ -102,7 +101,7 @@ __global__ void __launch_bounds__(kGThreads, 2)
                 const int4 t = p.tiles[it / p.tiles_n];
                 const int arow = (int) ((int64_t) t.x * p.N + (int64_t) (it % p.tiles_n) * kGM);
                 const int nsub = t.z / 16;
-                const uint32_t bytes = (uint32_t) (L::kA + t.z * 256 + L::kDw + L::kDx);
+                const uint32_t bytes = (uint32_t) (L::kA + t.z * 128 + L::kDw + L::kDx);
                 for (int st = 0; st < nstage; st++, sg++) {
                     const int s = sg % kGStages, use = sg / kGStages;
                     if (use > 0 && !mbar_wait_sleep(&empty[s], (use - 1) & 1)) {
@@ -113,12 +112,9 @@ __global__ void __launch_bounds__(kGThreads, 2)
                     uint8_t * base = smem + s * L::kStage;
                     mbar_arrive_expect_tx(&full[s], bytes);
                     const int kbs = st * kGKB;
-                    for (int jj = 0; jj < 2; jj++) {
-                        tma_load_2d(base + jj * kGM * 128, &tmA, (kbs + 4 * jj) * 32, arow, &full[s]);
-                        for (int r = 0; r < nsub; r++)
-                            tma_load_2d(base + L::kA + jj * kGNT * 128 + r * 16 * 128, &tmB, (kbs + 4 * jj) * 32, t.y + 16 * r, &full[s]);
-                    }
-                    tma_load_2d(base + L::kA + L::kB, &tmDw, kbs, arow, &full[s]);
+                    tma_load_2d(base, &tmA, kbs * 32, arow, &full[s]);
+                    for (int r = 0; r < nsub; r++) tma_load_2d(base + L::kA + r * 16 * 128, &tmB, kbs * 32, t.y + 16 * r, &full[s]);
+                    tma_load_2d(base + L::kA + L::kB, &tmDw, kbs & ~7, arow, &full[s]);
                     tma_load_2d(base + L::kA + L::kB + L::kDw, &tmDx, t.y, kbs, &full[s]);
                 }
             }
@@ -150,8 +146,7 @@ __global__ void __launch_bounds__(kGThreads, 2)
                         tc_fence_after();
 #pragma unroll
                         for (int jj = 0; jj < 2; jj++)
-                            mma_i8(tmem + buf * 2 * kGNT + jj * kGNT, smem_desc_sw128(base + ((j + jj) / 4) * kGM * 128, (j + jj) % 4),
-                                   smem_desc_sw128(base + L::kA + ((j + jj) / 4) * kGNT * 128, (j + jj) % 4), idesc);
+                            mma_i8(tmem + buf * 2 * kGNT + jj * kGNT, smem_desc_sw128(base, j + jj), smem_desc_sw128(base + L::kA, j + jj), idesc);
                         mma_commit(&acc_full[buf]);
                     }
                     if (give_up) break;
@@ -160,25 +155,19 @@ __global__ void __launch_bounds__(kGThreads, 2)
             }
         }
     } else {
-        // ---- epilogue: lane quarter q = warp % 4 owns tile rows 32 q .. 32 q + 31 (one per lane); h = warp group.
-        // Tiles of up to two 16-slot chunks are split along K: group h takes the block pairs of parity h (pair g sits in
-        // buffer g % 2, so each buffer has one group of consumers, which arrive for the other group too), all columns;
-        // at the tile's end group 1 stores its partial sums and group 0 adds its own (a two-term sum: the result does
-        // not depend on timing). Wider tiles are split along columns: group h takes chunks h and h + 2 of every pair;
-        // a warp without columns still waits and arrives on every barrier. Every consumer of a barrier consumes each
-        // of its phases in order, so no warp runs a phase ahead: parity waits cannot tell phase n from n + 2 ----
+        // ---- epilogue: lane quarter q = warp % 4 owns tile rows 32 q .. 32 q + 31 (one per lane); warp half h takes
+        // the 16-slot column chunks h and h + 2 of the tile. A warp without columns in a tile (h = 1 in a tile of one
+        // chunk) still waits and arrives on every barrier, so no warp runs a phase ahead of the others: parity waits
+        // cannot tell phase n from phase n + 2 ----
         const int q = warp & 3, h = (warp - 2) >> 2;
         const int row = 32 * q + lane;
         const float2 neg_magic = make_float2(-12582912.0f, -12582912.0f);
-        int sg = 0, g2 = 0, xi = 0;
+        int sg = 0, g2 = 0;
         for (int it = blockIdx.x; it < items && !give_up; it += gridDim.x) {
             const int4 t = p.tiles[it / p.tiles_n];
             const int tn = it % p.tiles_n;
             const int nch = t.z / 16;
-            const bool split = nch <= 2;
-            const int ch0 = split ? 0 : h, ch1 = split ? 1 : h + 2;  // the (up to) two chunks this warp reduces
-            const bool has0 = split || h < nch, has1 = split ? nch == 2 : h + 2 < nch;
-            const uint32_t arrivals = split ? 2u : 1u;
+            const bool has0 = h < nch, has1 = h + 2 < nch;
             const int live = t.w;  // slots before this one are routed pairs; later ones are padding (no math)
             float2 acc[16];
 #pragma unroll
@@ -186,18 +175,17 @@ __global__ void __launch_bounds__(kGThreads, 2)
             for (int st = 0; st < nstage && !give_up; st++, sg++) {
                 const int s = sg % kGStages;
                 const uint8_t * base = smem + s * L::kStage;
-                const __half2 * dw2 = reinterpret_cast<const __half2 *>(base + L::kA + L::kB) + row * (kGKB / 2);
+                const __half2 * dw2 = reinterpret_cast<const __half2 *>(base + L::kA + L::kB) + row * 4 + ((st * kGKB) & 7) / 2;
                 const float * dxT = reinterpret_cast<const float *>(base + L::kA + L::kB + L::kDw);
                 for (int j = 0; j < kGKB; j += 2, g2++) {
                     const int buf = g2 % kGBufs, use = g2 / kGBufs;
-                    if (split && buf != h) continue;  // the other group's pair (its consumers arrive for this warp)
                     if (!mbar_wait_sleep(&acc_full[buf], use & 1)) {
                         if (lane == 0) atomicOr(p.err, kErrTimeout);
                         give_up = 1;
                         break;
                     }
                     tc_fence_after();
-                    if (!has0) {  // no columns in this tile: only the barrier protocol
+                    if (!has0) {  // no columns in this tile: only the barrier protocol, which keeps this warp in step
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&acc_empty[buf]);
                         continue;
@@ -209,13 +197,13 @@ __global__ void __launch_bounds__(kGThreads, 2)
 #pragma unroll
                     for (int jj = 0; jj < 2; jj++) {
                         int v[2][16];  // [chunk][column]
-                        tmem_ld16(ta + jj * kGNT + 16 * ch0, v[0]);
-                        if (has1) tmem_ld16(ta + jj * kGNT + 16 * ch1, v[1]);
+                        tmem_ld16(ta + jj * kGNT + 16 * h, v[0]);
+                        if (has1) tmem_ld16(ta + jj * kGNT + 16 * (h + 2), v[1]);
                         tmem_wait_ld();
                         if (jj == 1) {
                             tc_fence_before();
                             __syncwarp();
-                            if (lane == 0) mbar_arrive_n(&acc_empty[buf], arrivals);
+                            if (lane == 0) mbar_arrive(&acc_empty[buf]);
                         }
                         // acc += float(sum) * (d_x * d_w), in block order; |sum| <= 32 * 127 * 128 < 2^22 converts
                         // exactly through the float 12582912 + sum (bit pattern 0x4B400000 + sum)
@@ -224,11 +212,10 @@ __global__ void __launch_bounds__(kGThreads, 2)
 #pragma unroll
                         for (int c = 0; c < 2; c++) {
                             if (c == 1 && !has1) continue;
-                            const int col0 = 16 * (c ? ch1 : ch0);
-                            const float4 * dx4 = reinterpret_cast<const float4 *>(dxT + (j + jj) * kGNT + col0);
+                            const float4 * dx4 = reinterpret_cast<const float4 *>(dxT + (j + jj) * kGNT + 16 * (h + 2 * c));
 #pragma unroll
                             for (int t4 = 0; t4 < 4; t4++) {
-                                if (col0 + 4 * t4 >= live) break;
+                                if (16 * (h + 2 * c) + 4 * t4 >= live) break;
                                 const float4 d = dx4[t4];
                                 const int * vv = v[c] + 4 * t4;
                                 const float2 s01 = __fmul2_rn(make_float2(d.x, d.y), w2);
@@ -246,57 +233,23 @@ __global__ void __launch_bounds__(kGThreads, 2)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[s]);
             }
-            if (give_up) break;
-            if (!has0) continue;
+            if (give_up || !has0) continue;
             // ---- output: one weight row per lane, so each slot's store is one coalesced 128-byte line ----
             const int64_t grow = (int64_t) tn * kGM + row;
-            const bool in_rows = grow < p.N;
-            if (split && h == 1) {  // store the partial sums for group 0, then signal it
-                if (in_rows)
-#pragma unroll
-                    for (int c = 0; c < 2; c++) {
-                        if (c == 1 && !has1) continue;
-#pragma unroll
-                        for (int i = 0; i < 16; i++) {
-                            const int col = 16 * c + i;
-                            if (col >= live) break;
-                            const int64_t orow = p.row_map ? (int64_t) p.row_map[t.y + col] : (int64_t) (t.y + col);
-                            const float2 a = acc[8 * c + i / 2];
-                            if (orow >= 0) p.y[orow * p.ldy + grow] = (i & 1) ? a.y : a.x;
-                        }
-                    }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&xchg[q]);
-                xi++;
-                continue;
-            }
-            if (split) {  // group 0: wait for group 1's partial sums of these rows
-                if (!mbar_wait_sleep(&xchg[q], xi & 1)) {
-                    if (lane == 0) atomicOr(p.err, kErrTimeout);
-                    give_up = 1;
-                    break;
-                }
-                xi++;
-            }
-            if (in_rows)
+            if (grow < p.N) {
 #pragma unroll
                 for (int c = 0; c < 2; c++) {
                     if (c == 1 && !has1) continue;
-                    const int col0 = 16 * (c ? ch1 : ch0);
+                    const int col0 = 16 * (h + 2 * c);
 #pragma unroll
                     for (int i = 0; i < 16; i++) {
-                        const int col = col0 + i;
-                        if (col >= live) break;
-                        const int64_t orow = p.row_map ? (int64_t) p.row_map[t.y + col] : (int64_t) (t.y + col);
+                        const int slot = t.y + col0 + i;
+                        const int64_t orow = p.row_map ? (int64_t) p.row_map[slot] : (int64_t) slot;
                         const float2 a = acc[8 * c + i / 2];
-                        float v = (i & 1) ? a.y : a.x;
-                        if (orow >= 0) {
-                            float * dst = p.y + orow * p.ldy + grow;
-                            if (split) v = __fadd_rn(v, *reinterpret_cast<volatile float *>(dst));
-                            *dst = v;
-                        }
+                        if (orow >= 0) p.y[orow * p.ldy + grow] = (i & 1) ? a.y : a.x;
                     }
                 }
+            }
         }
     }
     tc_fence_before();
@@ -310,7 +263,7 @@ __global__ void __launch_bounds__(kGThreads, 2)
 }  // namespace
 
 bool gemm_tc_grouped_supported(const WeightView & w) {
-    return w.type == B200_TYPE_Q8_0 && w.K % (32 * kGKB) == 0 && w.K <= (int64_t) 1 << 30 && w.rows < ((int64_t) 1 << 31) &&
+    return w.type == B200_TYPE_Q8_0 && w.K % 256 == 0 && w.K <= (int64_t) 1 << 30 && w.rows < ((int64_t) 1 << 31) &&
            tensor_maps_available();
 }
 
@@ -324,7 +277,7 @@ cudaError_t launch_gemm_tc_grouped(const WeightView & w, int64_t N, const int4 *
     if (!make_map_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.f0, (uint64_t) K, (uint64_t) w.rows, (uint64_t) K, 128, kGM,
                      CU_TENSOR_MAP_SWIZZLE_128B) ||
         !make_map_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, q, (uint64_t) K, (uint64_t) slots, (uint64_t) K, 128, 16, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !make_map_2d(&tdw, CU_TENSOR_MAP_DATA_TYPE_UINT16, w.f1, (uint64_t) KB, (uint64_t) w.rows, (uint64_t) KB * 2, kGKB, kGM,
+        !make_map_2d(&tdw, CU_TENSOR_MAP_DATA_TYPE_UINT16, w.f1, (uint64_t) KB, (uint64_t) w.rows, (uint64_t) KB * 2, 8, kGM,
                      CU_TENSOR_MAP_SWIZZLE_NONE) ||
         !make_map_2d(&tdx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, dT, (uint64_t) ldP, (uint64_t) KB, (uint64_t) ldP * 4, kGNT, kGKB,
                      CU_TENSOR_MAP_SWIZZLE_NONE))
