@@ -3,11 +3,12 @@
 //
 // The (token, slot) pairs are sorted by expert (moe.cu): expert e's pairs occupy slots [grp_off[e], grp_off[e+1]),
 // each segment padded to a multiple of 16 slots, and the pairs' activations are quantized to q8_0 in slot order
-// (q [slots][K] int8, dT [K/32][ldP] float block scales, transposed). A token tile is up to 64 consecutive slots of one
-// expert; the route kernel lists the tiles. One work item = one token tile x one 128-row tile of the expert's weight
+// (q [slots][K] int8, dT [K/32][ldP] float block scales, transposed). A token tile is 16 or 32 consecutive slots of
+// one expert; the route kernel lists the tiles. One work item = one token tile x one 128-row tile of the expert's weight
 // matrix. Per 32-wide K block, one tcgen05.mma kind::i8 of shape M = 128 (weight rows) x N = the tile's token count
-// (16..64, a run-time field of the instruction descriptor) x K = 32 computes the block's exact int32 sums. Blocks go in
-// pairs into one of two tensor-memory buffers (2 x 64 columns each), one barrier round trip per pair; epilogue warps
+// (16 or 32, a run-time field of the instruction descriptor) x K = 32 computes the block's exact int32 sums. Blocks go
+// in pairs into one of four tensor-memory buffers (2 x 32 columns each; eight blocks in flight between the MMA and the
+// epilogue), one barrier round trip per pair; epilogue warps
 // read a pair's sums (tcgen05.ld), scale them by d_w[row][b] * d_x[slot][b] and add them to float32 registers in
 // block order, as ggml's CPU vec_dot does. Operands come by TMA (2-D tensor maps, 128-byte swizzle, no multicast).
 // The grid is persistent (two CTAs per SM) and walks the items in a fixed order; every role of
@@ -23,29 +24,28 @@ namespace b200 {
 namespace {
 
 constexpr int kGM = 128;       // weight rows per tile (MMA M)
-constexpr int kGKB = 4;        // 32-wide K blocks per pipeline stage (one 128-byte row of each operand)
-constexpr int kGStages = 4;    // three stages stream while one is consumed
+constexpr int kGKB = 8;        // 32-wide K blocks per pipeline stage
+constexpr int kGStages = 2;
 constexpr int kGThreads = 320; // producer, MMA, 8 epilogue warps
 constexpr int kGEpiWarps = 8;
-constexpr int kGBufs = 2;      // tensor-memory accumulators in flight, one K-block pair (2 x kGNT columns) each
-constexpr int kGNT = 64;       // slots per token tile (largest MMA N used)
+constexpr int kGBufs = 4;      // tensor-memory accumulators in flight, one K-block pair (2 x kGNT columns) each
+constexpr int kGNT = 32;       // slots per token tile (largest MMA N used)
 constexpr unsigned kErrTimeout = 4u;
 
 struct GLayout {
-    static constexpr int kA = kGKB * kGM * 32;   // weights: one [128 rows][128 B] swizzled tile
-    static constexpr int kB = kGKB * kGNT * 32;  // activations: one [64 rows][128 B] swizzled tile
-    static constexpr int kDw = kGM * 8 * 2;      // fp16 weight scales [128][8]: the 16-byte box of 8 blocks that
-                                                 // holds this stage's 4 (TMA boxes start 16-byte aligned)
-    static constexpr int kDx = kGKB * kGNT * 4;  // f32 activation scales [4][64]
+    static constexpr int kA = kGKB * kGM * 32;   // weights: two [128 rows][128 B] swizzled tiles
+    static constexpr int kB = kGKB * kGNT * 32;  // activations: two [32 rows][128 B] swizzled tiles
+    static constexpr int kDw = kGM * kGKB * 2;   // fp16 weight scales [128][8]
+    static constexpr int kDx = kGKB * kGNT * 4;  // f32 activation scales [8][32]
     static constexpr int kStage = kA + kB + kDw + kDx;
-    static constexpr int kTotal = kGStages * kStage + 1024 + 1024;  // + barriers + alignment slack (2 CTAs per SM fit)
+    static constexpr int kTotal = kGStages * kStage + 1024 + 1024;  // + barriers + alignment slack
     static_assert(kA % 1024 == 0 && kB % 1024 == 0 && kStage % 1024 == 0, "stage regions stay 1024-aligned");
 };
 
 struct GroupedParams {
     int64_t N;                // rows per expert (output width)
     int64_t K;
-    const int4 * tiles;       // {expert, first slot, slots (multiple of 16, <= 64), routed slots (the rest is padding)}
+    const int4 * tiles;       // {expert, first slot, slots (16 or 32), routed slots (the rest is padding)}
     const int * ntiles;       // number of tiles (device)
     int tiles_n;              // 128-row tiles per expert
     const int32_t * row_map;  // output row of each slot (< 0: none); null: the slot itself
@@ -101,7 +101,7 @@ __global__ void __launch_bounds__(kGThreads, 2)
                 const int4 t = p.tiles[it / p.tiles_n];
                 const int arow = (int) ((int64_t) t.x * p.N + (int64_t) (it % p.tiles_n) * kGM);
                 const int nsub = t.z / 16;
-                const uint32_t bytes = (uint32_t) (L::kA + t.z * 128 + L::kDw + L::kDx);
+                const uint32_t bytes = (uint32_t) (L::kA + t.z * 256 + L::kDw + L::kDx);
                 for (int st = 0; st < nstage; st++, sg++) {
                     const int s = sg % kGStages, use = sg / kGStages;
                     if (use > 0 && !mbar_wait_sleep(&empty[s], (use - 1) & 1)) {
@@ -112,9 +112,12 @@ __global__ void __launch_bounds__(kGThreads, 2)
                     uint8_t * base = smem + s * L::kStage;
                     mbar_arrive_expect_tx(&full[s], bytes);
                     const int kbs = st * kGKB;
-                    tma_load_2d(base, &tmA, kbs * 32, arow, &full[s]);
-                    for (int r = 0; r < nsub; r++) tma_load_2d(base + L::kA + r * 16 * 128, &tmB, kbs * 32, t.y + 16 * r, &full[s]);
-                    tma_load_2d(base + L::kA + L::kB, &tmDw, kbs & ~7, arow, &full[s]);
+                    for (int jj = 0; jj < 2; jj++) {
+                        tma_load_2d(base + jj * kGM * 128, &tmA, (kbs + 4 * jj) * 32, arow, &full[s]);
+                        for (int r = 0; r < nsub; r++)
+                            tma_load_2d(base + L::kA + jj * kGNT * 128 + r * 16 * 128, &tmB, (kbs + 4 * jj) * 32, t.y + 16 * r, &full[s]);
+                    }
+                    tma_load_2d(base + L::kA + L::kB, &tmDw, kbs, arow, &full[s]);
                     tma_load_2d(base + L::kA + L::kB + L::kDw, &tmDx, t.y, kbs, &full[s]);
                 }
             }
@@ -146,7 +149,8 @@ __global__ void __launch_bounds__(kGThreads, 2)
                         tc_fence_after();
 #pragma unroll
                         for (int jj = 0; jj < 2; jj++)
-                            mma_i8(tmem + buf * 2 * kGNT + jj * kGNT, smem_desc_sw128(base, j + jj), smem_desc_sw128(base + L::kA, j + jj), idesc);
+                            mma_i8(tmem + buf * 2 * kGNT + jj * kGNT, smem_desc_sw128(base + ((j + jj) / 4) * kGM * 128, (j + jj) % 4),
+                                   smem_desc_sw128(base + L::kA + ((j + jj) / 4) * kGNT * 128, (j + jj) % 4), idesc);
                         mma_commit(&acc_full[buf]);
                     }
                     if (give_up) break;
@@ -156,9 +160,9 @@ __global__ void __launch_bounds__(kGThreads, 2)
         }
     } else {
         // ---- epilogue: lane quarter q = warp % 4 owns tile rows 32 q .. 32 q + 31 (one per lane); warp half h takes
-        // the 16-slot column chunks h and h + 2 of the tile. A warp without columns in a tile (h = 1 in a tile of one
-        // chunk) still waits and arrives on every barrier, so no warp runs a phase ahead of the others: parity waits
-        // cannot tell phase n from phase n + 2 ----
+        // the tile's 16-slot column chunk h. A warp without columns (h = 1 in a tile of 16 slots) still waits and
+        // arrives on every barrier, so no warp runs a phase ahead of the others: parity waits cannot tell phase n
+        // from phase n + 2 ----
         const int q = warp & 3, h = (warp - 2) >> 2;
         const int row = 32 * q + lane;
         const float2 neg_magic = make_float2(-12582912.0f, -12582912.0f);
@@ -166,16 +170,15 @@ __global__ void __launch_bounds__(kGThreads, 2)
         for (int it = blockIdx.x; it < items && !give_up; it += gridDim.x) {
             const int4 t = p.tiles[it / p.tiles_n];
             const int tn = it % p.tiles_n;
-            const int nch = t.z / 16;
-            const bool has0 = h < nch, has1 = h + 2 < nch;
-            const int live = t.w;  // slots before this one are routed pairs; later ones are padding (no math)
-            float2 acc[16];
+            const bool has = h < t.z / 16;
+            const int live = t.w - 16 * h;  // routed slots in this warp's chunk (the rest is padding: no math)
+            float2 acc[8];
 #pragma unroll
-            for (int i = 0; i < 16; i++) acc[i] = make_float2(0.0f, 0.0f);
+            for (int i = 0; i < 8; i++) acc[i] = make_float2(0.0f, 0.0f);
             for (int st = 0; st < nstage && !give_up; st++, sg++) {
                 const int s = sg % kGStages;
                 const uint8_t * base = smem + s * L::kStage;
-                const __half2 * dw2 = reinterpret_cast<const __half2 *>(base + L::kA + L::kB) + row * 4 + ((st * kGKB) & 7) / 2;
+                const __half2 * dw2 = reinterpret_cast<const __half2 *>(base + L::kA + L::kB) + row * (kGKB / 2);
                 const float * dxT = reinterpret_cast<const float *>(base + L::kA + L::kB + L::kDw);
                 for (int j = 0; j < kGKB; j += 2, g2++) {
                     const int buf = g2 % kGBufs, use = g2 / kGBufs;
@@ -185,69 +188,59 @@ __global__ void __launch_bounds__(kGThreads, 2)
                         break;
                     }
                     tc_fence_after();
-                    if (!has0) {  // no columns in this tile: only the barrier protocol, which keeps this warp in step
+                    if (!has) {  // no columns in this tile: only the barrier protocol
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&acc_empty[buf]);
                         continue;
                     }
-                    // the pair's blocks one at a time (registers: 2 chunks x 16 sums); the buffer is released once
-                    // the second block's sums are in registers
+                    // both blocks of the pair in registers, then the buffer is released
+                    int v[2][16];
+                    const uint32_t ta = tmem + ((uint32_t) (32 * q) << 16) + buf * 2 * kGNT + 16 * h;
+                    tmem_ld16(ta, v[0]);
+                    tmem_ld16(ta + kGNT, v[1]);
+                    tmem_wait_ld();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&acc_empty[buf]);
                     const float2 dwp = __half22float2(dw2[j / 2]);
-                    const uint32_t ta = tmem + ((uint32_t) (32 * q) << 16) + buf * 2 * kGNT;
+                    // acc += float(sum) * (d_x * d_w), in block order; |sum| <= 32 * 127 * 128 < 2^22 converts exactly
+                    // through the float 12582912 + sum (bit pattern 0x4B400000 + sum)
 #pragma unroll
                     for (int jj = 0; jj < 2; jj++) {
-                        int v[2][16];  // [chunk][column]
-                        tmem_ld16(ta + jj * kGNT + 16 * h, v[0]);
-                        if (has1) tmem_ld16(ta + jj * kGNT + 16 * (h + 2), v[1]);
-                        tmem_wait_ld();
-                        if (jj == 1) {
-                            tc_fence_before();
-                            __syncwarp();
-                            if (lane == 0) mbar_arrive(&acc_empty[buf]);
-                        }
-                        // acc += float(sum) * (d_x * d_w), in block order; |sum| <= 32 * 127 * 128 < 2^22 converts
-                        // exactly through the float 12582912 + sum (bit pattern 0x4B400000 + sum)
                         const float dwr = jj ? dwp.y : dwp.x;
                         const float2 w2 = make_float2(dwr, dwr);
+                        const float4 * dx4 = reinterpret_cast<const float4 *>(dxT + (j + jj) * kGNT + 16 * h);
 #pragma unroll
-                        for (int c = 0; c < 2; c++) {
-                            if (c == 1 && !has1) continue;
-                            const float4 * dx4 = reinterpret_cast<const float4 *>(dxT + (j + jj) * kGNT + 16 * (h + 2 * c));
-#pragma unroll
-                            for (int t4 = 0; t4 < 4; t4++) {
-                                if (16 * (h + 2 * c) + 4 * t4 >= live) break;
-                                const float4 d = dx4[t4];
-                                const int * vv = v[c] + 4 * t4;
-                                const float2 s01 = __fmul2_rn(make_float2(d.x, d.y), w2);
-                                const float2 s23 = __fmul2_rn(make_float2(d.z, d.w), w2);
-                                const float2 f01 = __fadd2_rn(make_float2(__int_as_float(vv[0] + 0x4B400000), __int_as_float(vv[1] + 0x4B400000)),
-                                                              neg_magic);
-                                const float2 f23 = __fadd2_rn(make_float2(__int_as_float(vv[2] + 0x4B400000), __int_as_float(vv[3] + 0x4B400000)),
-                                                              neg_magic);
-                                acc[8 * c + 2 * t4] = __ffma2_rn(f01, s01, acc[8 * c + 2 * t4]);
-                                acc[8 * c + 2 * t4 + 1] = __ffma2_rn(f23, s23, acc[8 * c + 2 * t4 + 1]);
-                            }
+                        for (int t4 = 0; t4 < 4; t4++) {
+                            if (4 * t4 >= live) break;
+                            const float4 d = dx4[t4];
+                            const int * vv = v[jj] + 4 * t4;
+                            const float2 s01 = __fmul2_rn(make_float2(d.x, d.y), w2);
+                            const float2 s23 = __fmul2_rn(make_float2(d.z, d.w), w2);
+                            const float2 f01 = __fadd2_rn(make_float2(__int_as_float(vv[0] + 0x4B400000), __int_as_float(vv[1] + 0x4B400000)),
+                                                          neg_magic);
+                            const float2 f23 = __fadd2_rn(make_float2(__int_as_float(vv[2] + 0x4B400000), __int_as_float(vv[3] + 0x4B400000)),
+                                                          neg_magic);
+                            acc[2 * t4] = __ffma2_rn(f01, s01, acc[2 * t4]);
+                            acc[2 * t4 + 1] = __ffma2_rn(f23, s23, acc[2 * t4 + 1]);
                         }
                     }
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[s]);
             }
-            if (give_up || !has0) continue;
+            if (give_up) break;
+            if (!has) continue;
             // ---- output: one weight row per lane, so each slot's store is one coalesced 128-byte line ----
             const int64_t grow = (int64_t) tn * kGM + row;
             if (grow < p.N) {
 #pragma unroll
-                for (int c = 0; c < 2; c++) {
-                    if (c == 1 && !has1) continue;
-                    const int col0 = 16 * (h + 2 * c);
-#pragma unroll
-                    for (int i = 0; i < 16; i++) {
-                        const int slot = t.y + col0 + i;
-                        const int64_t orow = p.row_map ? (int64_t) p.row_map[slot] : (int64_t) slot;
-                        const float2 a = acc[8 * c + i / 2];
-                        if (orow >= 0) p.y[orow * p.ldy + grow] = (i & 1) ? a.y : a.x;
-                    }
+                for (int i = 0; i < 16; i++) {
+                    if (i >= live) break;
+                    const int slot = t.y + 16 * h + i;
+                    const int64_t orow = p.row_map ? (int64_t) p.row_map[slot] : (int64_t) slot;
+                    const float2 a = acc[i / 2];
+                    if (orow >= 0) p.y[orow * p.ldy + grow] = (i & 1) ? a.y : a.x;
                 }
             }
         }
@@ -263,7 +256,7 @@ __global__ void __launch_bounds__(kGThreads, 2)
 }  // namespace
 
 bool gemm_tc_grouped_supported(const WeightView & w) {
-    return w.type == B200_TYPE_Q8_0 && w.K % 256 == 0 && w.K <= (int64_t) 1 << 30 && w.rows < ((int64_t) 1 << 31) &&
+    return w.type == B200_TYPE_Q8_0 && w.K % (32 * kGKB) == 0 && w.K <= (int64_t) 1 << 30 && w.rows < ((int64_t) 1 << 31) &&
            tensor_maps_available();
 }
 
@@ -277,7 +270,7 @@ cudaError_t launch_gemm_tc_grouped(const WeightView & w, int64_t N, const int4 *
     if (!make_map_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.f0, (uint64_t) K, (uint64_t) w.rows, (uint64_t) K, 128, kGM,
                      CU_TENSOR_MAP_SWIZZLE_128B) ||
         !make_map_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, q, (uint64_t) K, (uint64_t) slots, (uint64_t) K, 128, 16, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !make_map_2d(&tdw, CU_TENSOR_MAP_DATA_TYPE_UINT16, w.f1, (uint64_t) KB, (uint64_t) w.rows, (uint64_t) KB * 2, 8, kGM,
+        !make_map_2d(&tdw, CU_TENSOR_MAP_DATA_TYPE_UINT16, w.f1, (uint64_t) KB, (uint64_t) w.rows, (uint64_t) KB * 2, kGKB, kGM,
                      CU_TENSOR_MAP_SWIZZLE_NONE) ||
         !make_map_2d(&tdx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, dT, (uint64_t) ldP, (uint64_t) KB, (uint64_t) ldP * 4, kGNT, kGKB,
                      CU_TENSOR_MAP_SWIZZLE_NONE))

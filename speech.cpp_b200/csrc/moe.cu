@@ -7,7 +7,7 @@ namespace b200 {
 
 // One CTA: histogram of the local experts' pairs, exclusive scans of the counts rounded up to 16 (segment starts) and
 // of the segments' tile counts, placement of every pair in its expert's segment, the padding slots marked empty, and
-// the list of token tiles (<= 64 slots each, in expert order; .w = how many of them hold routed pairs). Pair p = t * top_k + s reads activation row
+// the list of token tiles (16 or 32 slots each, in expert order; .w = how many of them hold routed pairs). Pair p = t * top_k + s reads activation row
 // t * nb1 + (nb1 == 1 ? 0 : s). Pairs of experts outside [e0, e0 + E) are skipped (another shard's); ids outside
 // [0, total) are reported. inv[p] = the pair's slot, or -1.
 __global__ void moe_route_kernel(const int32_t * __restrict__ ids, int64_t P, int64_t top_k, int64_t nb1, int E, int e0, int total,
@@ -36,7 +36,7 @@ __global__ void moe_route_kernel(const int32_t * __restrict__ ids, int64_t P, in
         for (int base = 0; base < E; base += 32) {
             const int e = base + (int) threadIdx.x;
             const int len = e < E ? (cnt[e] + 15) & ~15 : 0;
-            const int nt = (len + 63) / 64;
+            const int nt = (len + 31) / 32;
             int incl = len, tincl = nt;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
@@ -78,8 +78,8 @@ __global__ void moe_route_kernel(const int32_t * __restrict__ ids, int64_t P, in
             col_src[slot] = -1;
             col_dst[slot] = -1;
         }
-        for (int o = 0, k = toff[e]; o < len; o += 64, k++)
-            tiles[k] = make_int4(e, start[e] + o, min(64, len - o), max(0, min(64, cnt[e] - o)));
+        for (int o = 0, k = toff[e]; o < len; o += 32, k++)
+            tiles[k] = make_int4(e, start[e] + o, min(32, len - o), max(0, min(32, cnt[e] - o)));
     }
 }
 
