@@ -137,8 +137,14 @@ b200_status mul_mat_impl(b200_context * ctx, const b200_weight * w, int64_t row0
     const int maxnc = gemv_max_columns(w->type, K);
     if (maxnc == 0) return fail(ctx, B200_ERR_UNSUPPORTED, "mul_mat: rows too long for the staging buffer");
     if (M <= maxnc) {
+        // Few columns: one GEMV launch. Launched with programmatic dependent launch (its CTAs start streaming weights
+        // while the previous kernel finishes; activations are read after griddepcontrol.wait), except right after an
+        // upload; a product of at most 64 MB of weights runs two CTAs per SM so the next launch's CTAs fit beside.
         p.ncols = (int) M;
-        CK(ctx, launch_gemv(p, pow2_at_least(M), 1, ctx->stream, false, ctx->num_sms));
+        const bool pdl = !ctx->upload_pending;
+        const bool small = (double) n * (double) w->nbytes / (double) (w->ne1 * w->ne2) <= 64.0 * 1024 * 1024;
+        CK(ctx, launch_gemv(p, pow2_at_least(M), 1, ctx->stream, pdl, ctx->num_sms, small ? 2 : 0));
+        ctx->upload_pending = false;
         return B200_OK;
     }
     const int kind = act_kind(w->type);
@@ -375,6 +381,7 @@ b200_status b200_weight_set(b200_context * ctx, b200_weight * w, const void * ho
         const size_t n = size - done < kStagingPiece ? size - done : kStagingPiece;
         CK(ctx, cudaMemcpyAsync(ctx->staging, (const uint8_t *) host_src + done, n, cudaMemcpyHostToDevice, ctx->stream));
         CK(ctx, launch_repack(w->type, w, (const uint8_t *) ctx->staging, (int64_t) (offset + done), (int64_t) n, true, nullptr, ctx->stream));
+        ctx->upload_pending = true;
         done += n;
     }
     return B200_OK;
@@ -388,6 +395,7 @@ b200_status b200_weight_set_device(b200_context * ctx, b200_weight * w, const vo
         return B200_OK;
     }
     CK(ctx, launch_repack(w->type, w, (const uint8_t *) dev_src, (int64_t) offset, (int64_t) size, true, nullptr, ctx->stream));
+    ctx->upload_pending = true;
     return B200_OK;
 }
 

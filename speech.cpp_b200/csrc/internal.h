@@ -28,6 +28,9 @@ struct b200_context {
     size_t staging_bytes = 0;
     unsigned * tickets = nullptr;     // split-K tile tickets of the tensor-core GEMM (zero between launches)
     size_t ntickets = 0;
+    // The last kernel launched on the stream wrote weight bytes (an upload). A product launched with programmatic
+    // dependent launch reads weights before griddepcontrol.wait, so it must not directly follow an upload.
+    bool upload_pending = false;
 };
 
 namespace b200 {
