@@ -45,7 +45,12 @@ struct b200_decoder {
     int mode = -1;    // B200_DEC_MODE_*; -1: persistent when every product fits it, else chain
     int64_t launches = 0;
     MkStage * mk_stages = nullptr;  // device table of the step's products (persistent mode)
-    unsigned * mk_done = nullptr;   // per-product completion counters
+    unsigned * mk_epoch = nullptr;     // persistent steps completed (the tags' epoch)
+    unsigned * mk_finished = nullptr;  // CTAs that finished the running step
+    uint2 * t_h0 = nullptr;   // tagged vectors of the persistent step: residual stream at layer inputs,
+    uint2 * t_h1 = nullptr;   // residual stream after attention,
+    uint2 * t_qkv = nullptr;  // q|k|v outputs,
+    uint2 * t_gu = nullptr;   // gate|up outputs
     int mk_n = 0;
 };
 
@@ -136,6 +141,27 @@ bool mk_fits(const GemvParams & p) {
 
 b200_status prepare_mk(b200_decoder * d, const std::vector<GemvParams> & v) {
     if (d->mk_stages) return B200_OK;
+    const b200_decoder_shape & sh = d->s;
+    DCK(d, cudaMalloc(&d->t_h0, sizeof(uint2) * (size_t) sh.hidden));
+    DCK(d, cudaMalloc(&d->t_h1, sizeof(uint2) * (size_t) sh.hidden));
+    DCK(d, cudaMalloc(&d->t_qkv, sizeof(uint2) * (size_t) qkv_rows(sh)));
+    DCK(d, cudaMalloc(&d->t_gu, sizeof(uint2) * 2 * (size_t) sh.ffn));
+    DCK(d, cudaMalloc(&d->mk_epoch, 2 * sizeof(unsigned)));
+    d->mk_finished = d->mk_epoch + 1;
+    // Tags are never zero-based stale matches: epoch starts at 1 and the tagged vectors start with tag 0.
+    DCK(d, cudaMemset(d->t_h0, 0, sizeof(uint2) * (size_t) sh.hidden));
+    DCK(d, cudaMemset(d->t_h1, 0, sizeof(uint2) * (size_t) sh.hidden));
+    DCK(d, cudaMemset(d->t_qkv, 0, sizeof(uint2) * (size_t) qkv_rows(sh)));
+    DCK(d, cudaMemset(d->t_gu, 0, sizeof(uint2) * 2 * (size_t) sh.ffn));
+    const unsigned init[2] = {1u, 0u};
+    DCK(d, cudaMemcpy(d->mk_epoch, init, sizeof init, cudaMemcpyHostToDevice));
+    // Vectors between products, tagged. Per layer: A q|k|v (x: h0) -> qkv; B o (x: the v part of qkv, res h0) -> h1;
+    // C gate|up (x: h1) -> gu; D down (x: gu, res h1) -> h0. A CTA can be one product ahead of the slowest, so no
+    // product writes a vector that the product before it reads: h1 (written by B) is not read by A, and h0 (written
+    // by D) is read by A and B only, which every CTA has finished before any CTA can start D (D's input gu needs
+    // every CTA's C). Layer 0 reads the step input, and the head writes the logits, untagged.
+    const int64_t v_off = (int64_t) (sh.n_head + sh.n_kv_head) * sh.head_dim;
+    const float * h0 = reinterpret_cast<const float *>(d->t_h0);
     std::vector<MkStage> st(v.size());
     for (size_t i = 0; i < v.size(); i++) {
         const GemvParams & p = v[i];
@@ -147,10 +173,39 @@ b200_status prepare_mk(b200_decoder * d, const std::vector<GemvParams> & v) {
         m.pro_k = (int) p.pro_k;
         m.pro_rep = p.pro_rep;
         m.eps = p.eps;
-        m.x = p.x;
         m.norm_w = p.norm_w;
-        m.res = p.res;
-        m.y = p.y;
+        const bool head = i + 1 == v.size();
+        const int l = (int) (i / 4), role = (int) (i % 4);
+        if (head) {
+            m.x = sh.n_layer > 0 ? h0 : d->x_in;
+            m.x_tagged = sh.n_layer > 0;
+            m.y = d->logits;
+        } else if (role == 0) {
+            m.x = l == 0 ? d->x_in : h0;
+            m.x_tagged = l > 0;
+            m.y = reinterpret_cast<float *>(d->t_qkv);
+            m.y_tagged = 1;
+        } else if (role == 1) {
+            m.x = reinterpret_cast<const float *>(d->t_qkv) + 2 * v_off;
+            m.x_tagged = 1;
+            m.res = l == 0 ? d->x_in : h0;
+            m.res_tagged = l > 0;
+            m.y = reinterpret_cast<float *>(d->t_h1);
+            m.y_tagged = 1;
+        } else if (role == 2) {
+            m.x = reinterpret_cast<const float *>(d->t_h1);
+            m.x_tagged = 1;
+            m.y = reinterpret_cast<float *>(d->t_gu);
+            m.y_tagged = 1;
+        } else {
+            m.x = reinterpret_cast<const float *>(d->t_gu);
+            m.x_tagged = 1;
+            m.res = reinterpret_cast<const float *>(d->t_h1);
+            m.res_tagged = 1;
+            m.y = reinterpret_cast<float *>(d->t_h0);
+            m.y_tagged = 1;
+        }
+        if ((((uintptr_t) m.x) & 15) != 0) return dfail(d, B200_ERR_UNSUPPORTED, "decoder: persistent step input not 16-byte aligned");
         m.row_bytes = (int) mk_row_bytes(p.w.type, p.w.K);
         m.rps = kMkSlotBytes / m.row_bytes;
         m.slice_base = (int) (p.N / d->ctx->num_sms);
@@ -160,7 +215,6 @@ b200_status prepare_mk(b200_decoder * d, const std::vector<GemvParams> & v) {
         m.hd_shift = p.pro == PRO_GQA ? log2_exact(p.pro_k) : -1;
     }
     DCK(d, cudaMalloc(&d->mk_stages, sizeof(MkStage) * st.size()));
-    DCK(d, cudaMalloc(&d->mk_done, sizeof(unsigned) * st.size()));
     DCK(d, cudaMemcpy(d->mk_stages, st.data(), sizeof(MkStage) * st.size(), cudaMemcpyHostToDevice));
     d->mk_n = (int) st.size();
     DCK(d, cudaFuncSetAttribute(decoder_mk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) kMkSmemBytes));
@@ -169,14 +223,14 @@ b200_status prepare_mk(b200_decoder * d, const std::vector<GemvParams> & v) {
 
 b200_status enqueue_mk(b200_decoder * d) {
     cudaStream_t st = d->ctx->stream;
-    DCK(d, cudaMemsetAsync(d->mk_done, 0, sizeof(unsigned) * d->mk_n, st));
     MkParams P;
 #ifdef B200_MK_PROBE
     P.probe = b200_mk_probe_buffer;
 #endif
     P.stages = d->mk_stages;
     P.nstages = d->mk_n;
-    P.done = d->mk_done;
+    P.epoch = d->mk_epoch;
+    P.finished = d->mk_finished;
     P.err = d->ctx->dev_err;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned) d->ctx->num_sms, 1, 1);
@@ -284,7 +338,11 @@ void b200_decoder_destroy(b200_decoder * d) {
     if (d->head.data) cudaFree(d->head.data);
     for (float * p : {d->out_norm, d->x_in, d->h, d->qkv_out, d->gu_out, d->logits}) if (p) cudaFree(p);
     if (d->mk_stages) cudaFree(d->mk_stages);
-    if (d->mk_done) cudaFree(d->mk_done);
+    if (d->mk_epoch) cudaFree(d->mk_epoch);
+    if (d->t_h0) cudaFree(d->t_h0);
+    if (d->t_h1) cudaFree(d->t_h1);
+    if (d->t_qkv) cudaFree(d->t_qkv);
+    if (d->t_gu) cudaFree(d->t_gu);
     if (d->host_io) cudaFreeHost(d->host_io);
     delete d;
 }

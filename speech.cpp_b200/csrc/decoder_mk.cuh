@@ -6,11 +6,16 @@
 //   - its producer warp streams the CTA's row slice of EVERY product's weights, in order, through one ring of
 //     shared-memory slots with bulk async copies (cp.async.bulk, no multicast; mbarrier transaction counts). Weights
 //     depend on nothing, so the ring runs ahead of the computation by up to its capacity;
-//   - its consumer warps, for product s, wait until all CTAs have finished product s-1 (a global completion counter
-//     per product, polled with a bounded spin), load the input vector from L2 into registers, apply the fused
-//     prologue (RMSNorm * weight, SwiGLU, grouped-query value broadcast), quantize it to the vec_dot type
-//     bit-identically to the CPU oracle, reduce their rows from the ring, write the outputs (+ residual), and publish
-//     completion (__threadfence + atomicAdd).
+//   - its consumer warps, for product s, load the input vector from L2 into registers, apply the fused prologue
+//     (RMSNorm * weight, SwiGLU, grouped-query value broadcast), quantize it to the vec_dot type bit-identically to
+//     the CPU oracle, reduce their rows from the ring and write the outputs (+ residual).
+// Vectors passed between products are tagged: element k is one 8-byte word {value, tag}, written by a single store,
+// with tag = epoch * nstages + s + 1 for the product s that wrote it. A consumer's load of its input both fetches the
+// values and proves they are ready (each word carries its own tag), so no completion counter and no second round trip
+// to L2 sits between two products. Every product reads its whole input vector, so a CTA can run at most one product
+// ahead of the slowest; the buffers are laid out so that no vector is rewritten while a CTA may still read it (the
+// host's product list). The epoch is a device word, advanced at the end of every launch, so tags never repeat
+// between steps (also under graph replay).
 // All CTAs must be co-resident: the kernel is launched cooperatively with one CTA per SM. Every wait is bounded; a
 // wait that gives up records B200_DEVERR_TIMEOUT and the CTA leaves the chain, so the others give up in turn.
 #pragma once
@@ -26,10 +31,14 @@ struct MkStage {
     int pro_k;
     int pro_rep;
     float eps;
-    const float * x;       // input vector (written earlier in the chain: read through L2)
+    const float * x;       // input vector (written earlier in the chain: read through L2); tagged: {value, tag} words
     const float * norm_w;  // RMSNorm weights
-    const float * res;     // residual (same rows as y) or null
-    float * y;
+    const float * res;     // residual (same rows as y, written by this CTA) or null; tagged: {value, tag} words
+    float * y;             // output; tagged: {value, tag} words
+    int x_tagged;
+    int res_tagged;
+    int y_tagged;
+    int pad_;
     // precomputed by the host (no divisions on the device's critical path)
     int row_bytes;    // GGUF bytes of one weight row
     int rps;          // rows per ring slot
@@ -54,7 +63,8 @@ struct MkParams {
 #endif
     const MkStage * stages;
     int nstages;
-    unsigned * done;  // [nstages] CTAs that finished each product (zeroed before the launch)
+    unsigned * epoch;      // steps completed (tags of this launch: epoch * nstages + s + 1)
+    unsigned * finished;   // CTAs that finished this launch (zero between launches)
     unsigned * err;
 };
 
@@ -95,6 +105,17 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned * p) {
 
 __device__ __forceinline__ void mk_sync() { asm volatile("bar.sync 1, %0;" ::"r"(32 * kMkConsumerWarps) : "memory"); }
 
+// The same barrier, returning whether v was non-zero in any consumer thread.
+__device__ __forceinline__ int mk_sync_or(int v) {
+    int r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.s32 q, %1, 0;\n\tbar.red.or.pred p, 1, %2, q;\n\tselp.s32 %0, 1, 0, p;\n\t}"
+        : "=r"(r)
+        : "r"(v), "r"(32 * kMkConsumerWarps)
+        : "memory");
+    return r;
+}
+
 // Rows [r0, r1) of a product that CTA `cta` computes (contiguous, balanced; base = N / G, extra = N % G).
 __device__ __forceinline__ void mk_slice(const MkStage & S, int cta, int64_t & r0, int64_t & r1) {
     const int base = S.slice_base, extra = S.slice_extra;
@@ -102,13 +123,34 @@ __device__ __forceinline__ void mk_slice(const MkStage & S, int cta, int64_t & r
     r1 = r0 + base + (cta < extra ? 1 : 0);
 }
 
+// Four tagged values starting at element k (16-byte aligned pairs of {value, tag} words), re-read until every tag is
+// `tag`; bounded: after kSpinLimit reads it records a timeout in *fail and returns what it has.
+__device__ __forceinline__ float4 mk_ll4(const float * base, int k, unsigned tag, int * fail) {
+    const uint32_t * p = reinterpret_cast<const uint32_t *>(base) + 2 * (int64_t) k;
+    uint32_t a0, t0, a1, t1, a2, t2, a3, t3;
+    for (uint32_t i = 0;; i++) {
+        asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(a0), "=r"(t0), "=r"(a1), "=r"(t1) : "l"(p) : "memory");
+        asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(a2), "=r"(t2), "=r"(a3), "=r"(t3) : "l"(p + 4) : "memory");
+        if (((t0 ^ tag) | (t1 ^ tag) | (t2 ^ tag) | (t3 ^ tag)) == 0) break;
+        if (i >= kSpinLimit) {
+            *fail = 1;
+            break;
+        }
+    }
+    return make_float4(__uint_as_float(a0), __uint_as_float(a1), __uint_as_float(a2), __uint_as_float(a3));
+}
+
 // Input value k of product S for its prologue (global loads through L2: these vectors were written in this kernel).
-__device__ __forceinline__ float4 mk_load4(const MkStage & S, int k, float rms) {
+__device__ __forceinline__ float4 mk_raw4(const MkStage & S, const float * base, int k, unsigned tag, int * fail) {
+    return S.x_tagged ? mk_ll4(base, k, tag, fail) : __ldcg(reinterpret_cast<const float4 *>(base + k));
+}
+
+__device__ __forceinline__ float4 mk_load4(const MkStage & S, int k, unsigned tag, int * fail) {
     float4 v;
     switch (S.pro) {
     case PRO_SWIGLU: {
-        const float4 g = __ldcg(reinterpret_cast<const float4 *>(S.x + k));
-        const float4 u = __ldcg(reinterpret_cast<const float4 *>(S.x + S.pro_k + k));
+        const float4 g = mk_raw4(S, S.x, k, tag, fail);
+        const float4 u = mk_raw4(S, S.x, S.pro_k + k, tag, fail);
         v.x = __fmul_rn(silu(g.x), u.x);
         v.y = __fmul_rn(silu(g.y), u.y);
         v.z = __fmul_rn(silu(g.z), u.z);
@@ -116,20 +158,20 @@ __device__ __forceinline__ float4 mk_load4(const MkStage & S, int k, float rms) 
         return v;
     }
     case PRO_GQA: {
-        if (S.gqa_shift >= 0 && S.hd_shift >= 0)
-            return __ldcg(reinterpret_cast<const float4 *>(S.x + ((k >> S.gqa_shift) << S.hd_shift) + (k & (S.pro_k - 1))));
+        if (S.gqa_shift >= 0 && S.hd_shift >= 0) return mk_raw4(S, S.x, ((k >> S.gqa_shift) << S.hd_shift) + (k & (S.pro_k - 1)), tag, fail);
         const int span = S.pro_k * S.pro_rep;
-        return __ldcg(reinterpret_cast<const float4 *>(S.x + (k / span) * S.pro_k + k % S.pro_k));
+        return mk_raw4(S, S.x, (k / span) * S.pro_k + k % S.pro_k, tag, fail);
     }
     default:
-        return __ldcg(reinterpret_cast<const float4 *>(S.x + k));
+        return mk_raw4(S, S.x, k, tag, fail);
     }
 }
 
-// Stages product S's quantized input in the act arrays (consumer threads only; ends with mk_sync()).
+// Stages product S's quantized input in the act arrays (consumer threads only; ends with a barrier, whose result is
+// whether any thread's tagged loads timed out).
 // q8_0 (K % 1024 == 0): thread t holds values 4t + 1024 i; eight consecutive threads form one 32-block.
 // q8_K (K % 2048 == 0): thread t holds values 8t + 2048 i; one warp forms one 256-block.
-__device__ __forceinline__ void mk_stage_input(const MkStage & S, const Act & a, float * part) {
+__device__ __forceinline__ int mk_stage_input(const MkStage & S, const Act & a, float * part, unsigned tag, int * fail) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int K = (int) S.w.K;
     const int kind = act_kind(S.w.type);
@@ -151,7 +193,7 @@ __device__ __forceinline__ void mk_stage_input(const MkStage & S, const Act & a,
         for (int i = 0; i < kMax; i++) {
             if (i < K / 2048) {
                 const int k = 8 * tid + 2048 * i;
-                const float4 lo = mk_load4(S, k, 0.0f), hi = mk_load4(S, k + 4, 0.0f);
+                const float4 lo = mk_load4(S, k, tag, fail), hi = mk_load4(S, k + 4, tag, fail);
                 v[i][0] = lo.x; v[i][1] = lo.y; v[i][2] = lo.z; v[i][3] = lo.w;
                 v[i][4] = hi.x; v[i][5] = hi.y; v[i][6] = hi.z; v[i][7] = hi.w;
 #pragma unroll
@@ -200,7 +242,7 @@ __device__ __forceinline__ void mk_stage_input(const MkStage & S, const Act & a,
 #pragma unroll
         for (int i = 0; i < kMax; i++) {
             if (i < K / 1024) {
-                v[i] = mk_load4(S, 4 * tid + 1024 * i, 0.0f);
+                v[i] = mk_load4(S, 4 * tid + 1024 * i, tag, fail);
                 sq = fmaf(v[i].x, v[i].x, sq);
                 sq = fmaf(v[i].y, v[i].y, sq);
                 sq = fmaf(v[i].z, v[i].z, sq);
@@ -248,7 +290,7 @@ __device__ __forceinline__ void mk_stage_input(const MkStage & S, const Act & a,
         }
     }
     cp_async_wait_all();  // this thread's residual copies (issued before staging) have landed
-    mk_sync();
+    return mk_sync_or(*fail);
 }
 
 constexpr int kMkResRows = 64;  // residual values of a CTA's slice kept in shared memory (more: read from L2)
@@ -256,7 +298,7 @@ constexpr int kMkResRows = 64;  // residual values of a CTA's slice kept in shar
 // Rows of one landed chunk, two per warp at a time. res_s holds the residuals of the CTA's rows [r0, r0 + 64).
 template <class T>
 __device__ __forceinline__ void mk_rows(const MkStage & S, const Act & a, const uint8_t * slot, int64_t rps, int64_t rows,
-                                        int64_t first, int64_t r0, const float * res_s) {
+                                        int64_t first, int64_t r0, const float * res_s, unsigned tag) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t K = S.w.K;
     const uint8_t * f[4];
@@ -269,8 +311,11 @@ __device__ __forceinline__ void mk_rows(const MkStage & S, const Act & a, const 
         {
             const int64_t r = first + j;
             float out = v;
-            if (S.res) out = __fadd_rn(r - r0 < kMkResRows ? res_s[r - r0] : __ldcg(S.res + r), v);
-            S.y[r] = out;
+            if (S.res) out = __fadd_rn(r - r0 < kMkResRows ? res_s[r - r0] : __ldcg(S.res + (S.res_tagged ? 2 * r : r)), v);
+            if (S.y_tagged)
+                asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(S.y + 2 * r), "r"(__float_as_uint(out)), "r"(tag) : "memory");
+            else
+                S.y[r] = out;
         }
     });
 }
@@ -349,37 +394,32 @@ __global__ void __launch_bounds__(kMkThreads, 1) decoder_mk_kernel(MkParams P) {
         if (P.nstages > 1)
             reinterpret_cast<uint32_t *>(&desc[1])[threadIdx.x] = reinterpret_cast<const uint32_t *>(&P.stages[1])[threadIdx.x];
     }
+    const unsigned epoch = *reinterpret_cast<volatile unsigned *>(P.epoch);
     mk_sync();
     uint32_t ctr = 0;
     for (int s = 0; s < P.nstages; s++) {
         if (threadIdx.x == 0) MK_PROBE(0);
         const MkStage & S = desc[s % 3];
-        if (s > 0) {
-            if (threadIdx.x == 0) {
-                uint32_t i = 0;
-                while (ld_acquire(&P.done[s - 1]) < (unsigned) G) {
-                    if (++i >= kSpinLimit) {
-                        atomicOr(P.err, 4u);
-                        give_up = 1;
-                        break;
-                    }
-                }
-            }
-            mk_sync();
-            if (give_up) break;
-        }
+        const unsigned in_tag = epoch * (unsigned) P.nstages + (unsigned) s;  // written by product s - 1
+        const unsigned out_tag = in_tag + 1u;
         if (threadIdx.x == 0) MK_PROBE(1);
         int64_t r0, r1;
         mk_slice(S, cta, r0, r1);
-        // residuals of this CTA's rows: asynchronous copies, complete before the staging barrier below
-        if (S.res && (int64_t) threadIdx.x < r1 - r0 && threadIdx.x < kMkResRows) cp_async4(&res_s[threadIdx.x], S.res + r0 + threadIdx.x);
+        // residuals of this CTA's rows (its own earlier outputs): asynchronous copies, complete before the staging
+        // barrier below
+        if (S.res && (int64_t) threadIdx.x < r1 - r0 && threadIdx.x < kMkResRows)
+            cp_async4(&res_s[threadIdx.x], S.res + (S.res_tagged ? 2 * (r0 + threadIdx.x) : r0 + threadIdx.x));
         Act a;
         a.K = S.w.K;
         a.q = reinterpret_cast<int8_t *>(act);
         a.d = reinterpret_cast<float *>(act + 2 * kMkMaxK);
         a.bs = reinterpret_cast<int16_t *>(act + 2 * kMkMaxK + (kMkMaxK / 32) * 4);
         a.b = reinterpret_cast<__nv_bfloat16 *>(act);
-        mk_stage_input(S, a, part);  // ends with a barrier: res_s is complete
+        int fail = 0;
+        if (mk_stage_input(S, a, part, in_tag, &fail)) {  // ends with a barrier: res_s is complete
+            if (threadIdx.x == 0) atomicOr(P.err, 4u);
+            break;
+        }
         if (threadIdx.x == 0) MK_PROBE(2);
         // the descriptor after next goes to the third buffer (this one, s % 3, stays readable during product s)
         if (s + 2 < P.nstages && threadIdx.x < kDescWords)
@@ -397,10 +437,10 @@ __global__ void __launch_bounds__(kMkThreads, 1) decoder_mk_kernel(MkParams P) {
             const int64_t rows = r1 - first < rps ? r1 - first : rps;
             const uint8_t * sp = ring + (size_t) slot * kMkSlotBytes;
             switch (S.w.type) {
-            case B200_TYPE_Q8_0: mk_rows<TQ8_0>(S, a, sp, rps, rows, first, r0, res_s); break;
-            case B200_TYPE_Q4_K: mk_rows<TQ4_K>(S, a, sp, rps, rows, first, r0, res_s); break;
-            case B200_TYPE_Q6_K: mk_rows<TQ6_K>(S, a, sp, rps, rows, first, r0, res_s); break;
-            default: mk_rows<TBF16>(S, a, sp, rps, rows, first, r0, res_s); break;
+            case B200_TYPE_Q8_0: mk_rows<TQ8_0>(S, a, sp, rps, rows, first, r0, res_s, out_tag); break;
+            case B200_TYPE_Q4_K: mk_rows<TQ4_K>(S, a, sp, rps, rows, first, r0, res_s, out_tag); break;
+            case B200_TYPE_Q6_K: mk_rows<TQ6_K>(S, a, sp, rps, rows, first, r0, res_s, out_tag); break;
+            default: mk_rows<TBF16>(S, a, sp, rps, rows, first, r0, res_s, out_tag); break;
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
@@ -409,9 +449,21 @@ __global__ void __launch_bounds__(kMkThreads, 1) decoder_mk_kernel(MkParams P) {
         mk_sync();  // all outputs of this CTA for product s are written; the act arrays may be reused
         if (threadIdx.x == 0) MK_PROBE(4);
         if (give_up) break;
-        if (threadIdx.x == 0) {
-            // release: this CTA's outputs (ordered before by the barrier) are visible before the count rises
-            asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(&P.done[s]), "r"(1u) : "memory");
+    }
+    // ---- end of the launch: once every CTA is here (all have read the epoch), CTA 0 advances it ----
+    if (threadIdx.x == 0) {
+        __threadfence();
+        asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(P.finished), "r"(1u) : "memory");
+        if (cta == 0) {
+            uint32_t i = 0;
+            while (ld_acquire(P.finished) < (unsigned) G)
+                if (++i >= kSpinLimit) {
+                    atomicOr(P.err, 4u);
+                    break;
+                }
+            *reinterpret_cast<volatile unsigned *>(P.finished) = 0u;
+            __threadfence();
+            atomicAdd(P.epoch, 1u);
         }
     }
 }
