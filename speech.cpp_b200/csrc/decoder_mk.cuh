@@ -123,8 +123,19 @@ __device__ __forceinline__ void mk_slice(const MkStage & S, int cta, int64_t & r
     r1 = r0 + base + (cta < extra ? 1 : 0);
 }
 
-// Four tagged values starting at element k (16-byte aligned pairs of {value, tag} words), re-read until every tag is
-// `tag`; bounded: after kSpinLimit reads it records a timeout in *fail and returns what it has.
+// Four tagged values starting at element k (16-byte aligned pairs of {value, tag} words). mk_ll4_try reads them once
+// and reports whether every tag is `tag` (the asm is not volatile, so the compiler may issue a thread's first reads of
+// all its chunks back to back: one L2 round trip, not one per chunk); mk_ll4 re-reads until they all are, bounded:
+// after kSpinLimit reads it records a timeout in *fail and returns what it has.
+__device__ __forceinline__ float4 mk_ll4_try(const float * base, int k, unsigned tag, int & ok) {
+    const uint32_t * p = reinterpret_cast<const uint32_t *>(base) + 2 * (int64_t) k;
+    uint32_t a0, t0, a1, t1, a2, t2, a3, t3;
+    asm("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(a0), "=r"(t0), "=r"(a1), "=r"(t1) : "l"(p));
+    asm("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(a2), "=r"(t2), "=r"(a3), "=r"(t3) : "l"(p + 4));
+    ok = ((t0 ^ tag) | (t1 ^ tag) | (t2 ^ tag) | (t3 ^ tag)) == 0;
+    return make_float4(__uint_as_float(a0), __uint_as_float(a1), __uint_as_float(a2), __uint_as_float(a3));
+}
+
 __device__ __forceinline__ float4 mk_ll4(const float * base, int k, unsigned tag, int * fail) {
     const uint32_t * p = reinterpret_cast<const uint32_t *>(base) + 2 * (int64_t) k;
     uint32_t a0, t0, a1, t1, a2, t2, a3, t3;
@@ -140,30 +151,38 @@ __device__ __forceinline__ float4 mk_ll4(const float * base, int k, unsigned tag
     return make_float4(__uint_as_float(a0), __uint_as_float(a1), __uint_as_float(a2), __uint_as_float(a3));
 }
 
-// Input value k of product S for its prologue (global loads through L2: these vectors were written in this kernel).
-__device__ __forceinline__ float4 mk_raw4(const MkStage & S, const float * base, int k, unsigned tag, int * fail) {
-    return S.x_tagged ? mk_ll4(base, k, tag, fail) : __ldcg(reinterpret_cast<const float4 *>(base + k));
+// Four raw input values at element k of the input vector: one read (ok: they are the ones this product waits for;
+// untagged inputs are always ready), or re-read until ready (wait == true).
+__device__ __forceinline__ float4 mk_raw4(const MkStage & S, int k, unsigned tag, bool wait, int & ok, int * fail) {
+    if (!S.x_tagged) {
+        ok = 1;
+        return __ldcg(reinterpret_cast<const float4 *>(S.x + k));
+    }
+    if (wait) {
+        ok = 1;
+        return mk_ll4(S.x, k, tag, fail);
+    }
+    return mk_ll4_try(S.x, k, tag, ok);
 }
 
-__device__ __forceinline__ float4 mk_load4(const MkStage & S, int k, unsigned tag, int * fail) {
-    float4 v;
+// Input values k .. k + 3 of product S after its prologue's element-wise part (SwiGLU, the grouped-query broadcast).
+__device__ __forceinline__ float4 mk_load4(const MkStage & S, int k, unsigned tag, bool wait, int & ok, int * fail) {
     switch (S.pro) {
     case PRO_SWIGLU: {
-        const float4 g = mk_raw4(S, S.x, k, tag, fail);
-        const float4 u = mk_raw4(S, S.x, S.pro_k + k, tag, fail);
-        v.x = __fmul_rn(silu(g.x), u.x);
-        v.y = __fmul_rn(silu(g.y), u.y);
-        v.z = __fmul_rn(silu(g.z), u.z);
-        v.w = __fmul_rn(silu(g.w), u.w);
-        return v;
+        int ok2;
+        const float4 g = mk_raw4(S, k, tag, wait, ok, fail);
+        const float4 u = mk_raw4(S, S.pro_k + k, tag, wait, ok2, fail);
+        ok &= ok2;
+        return make_float4(__fmul_rn(silu(g.x), u.x), __fmul_rn(silu(g.y), u.y), __fmul_rn(silu(g.z), u.z), __fmul_rn(silu(g.w), u.w));
     }
     case PRO_GQA: {
-        if (S.gqa_shift >= 0 && S.hd_shift >= 0) return mk_raw4(S, S.x, ((k >> S.gqa_shift) << S.hd_shift) + (k & (S.pro_k - 1)), tag, fail);
+        if (S.gqa_shift >= 0 && S.hd_shift >= 0)
+            return mk_raw4(S, ((k >> S.gqa_shift) << S.hd_shift) + (k & (S.pro_k - 1)), tag, wait, ok, fail);
         const int span = S.pro_k * S.pro_rep;
-        return mk_raw4(S, S.x, (k / span) * S.pro_k + k % S.pro_k, tag, fail);
+        return mk_raw4(S, (k / span) * S.pro_k + k % S.pro_k, tag, wait, ok, fail);
     }
     default:
-        return mk_raw4(S, S.x, k, tag, fail);
+        return mk_raw4(S, k, tag, wait, ok, fail);
     }
 }
 
@@ -179,27 +198,29 @@ __device__ __forceinline__ int mk_stage_input(const MkStage & S, const Act & a, 
     if (kind == B200_TYPE_Q8_K) {
         constexpr int kMax = kMkMaxK / 2048;
         float v[kMax][8];
-        float4 nw[kMax][2];
         float sq = 0.0f;
+        // every chunk read once (all reads in flight together), then re-read until ready if any was early
+        int ready = 1;
 #pragma unroll
-        for (int i = 0; i < kMax; i++) {
-            if (i < K / 2048 && rmsnorm) {
-                const int k = 8 * tid + 2048 * i;
-                nw[i][0] = __ldg(reinterpret_cast<const float4 *>(S.norm_w + k));
-                nw[i][1] = __ldg(reinterpret_cast<const float4 *>(S.norm_w + k + 4));
+        for (int pass = 0; pass < 2; pass++) {
+            if (pass == 1 && ready) break;
+#pragma unroll
+            for (int i = 0; i < kMax; i++) {
+                if (i < K / 2048) {
+                    const int k = 8 * tid + 2048 * i;
+                    int ok0, ok1;
+                    const float4 lo = mk_load4(S, k, tag, pass == 1, ok0, fail), hi = mk_load4(S, k + 4, tag, pass == 1, ok1, fail);
+                    ready &= ok0 & ok1;
+                    v[i][0] = lo.x; v[i][1] = lo.y; v[i][2] = lo.z; v[i][3] = lo.w;
+                    v[i][4] = hi.x; v[i][5] = hi.y; v[i][6] = hi.z; v[i][7] = hi.w;
+                }
             }
         }
 #pragma unroll
-        for (int i = 0; i < kMax; i++) {
-            if (i < K / 2048) {
-                const int k = 8 * tid + 2048 * i;
-                const float4 lo = mk_load4(S, k, tag, fail), hi = mk_load4(S, k + 4, tag, fail);
-                v[i][0] = lo.x; v[i][1] = lo.y; v[i][2] = lo.z; v[i][3] = lo.w;
-                v[i][4] = hi.x; v[i][5] = hi.y; v[i][6] = hi.z; v[i][7] = hi.w;
+        for (int i = 0; i < kMax; i++)
+            if (i < K / 2048)
 #pragma unroll
                 for (int j = 0; j < 8; j++) sq = fmaf(v[i][j], v[i][j], sq);
-            }
-        }
         float rms = 0.0f;
         if (rmsnorm) {
             sq = warp_sum(sq);
@@ -213,8 +234,9 @@ __device__ __forceinline__ int mk_stage_input(const MkStage & S, const Act & a, 
         for (int i = 0; i < kMax; i++) {
             if (i < K / 2048) {
                 const int k = 8 * tid + 2048 * i;
-                if (rmsnorm) {
-                    const float4 w0 = nw[i][0], w1 = nw[i][1];
+                if (rmsnorm) {  // norm weights: read-only, cached after the first step
+                    const float4 w0 = __ldg(reinterpret_cast<const float4 *>(S.norm_w + k));
+                    const float4 w1 = __ldg(reinterpret_cast<const float4 *>(S.norm_w + k + 4));
                     const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
                     for (int j = 0; j < 8; j++) v[i][j] = __fmul_rn(__fmul_rn(v[i][j], rms), wv[j]);
@@ -234,15 +256,25 @@ __device__ __forceinline__ int mk_stage_input(const MkStage & S, const Act & a, 
         }
     } else {
         constexpr int kMax = kMkMaxK / 1024;
-        float4 v[kMax], nw[kMax];
+        float4 v[kMax];
         float sq = 0.0f;
+        // every chunk read once (all reads in flight together), then re-read until ready if any was early
+        int ready = 1;
 #pragma unroll
-        for (int i = 0; i < kMax; i++)
-            if (i < K / 1024 && rmsnorm) nw[i] = __ldg(reinterpret_cast<const float4 *>(S.norm_w + 4 * tid + 1024 * i));
+        for (int pass = 0; pass < 2; pass++) {
+            if (pass == 1 && ready) break;
+#pragma unroll
+            for (int i = 0; i < kMax; i++) {
+                if (i < K / 1024) {
+                    int ok;
+                    v[i] = mk_load4(S, 4 * tid + 1024 * i, tag, pass == 1, ok, fail);
+                    ready &= ok;
+                }
+            }
+        }
 #pragma unroll
         for (int i = 0; i < kMax; i++) {
             if (i < K / 1024) {
-                v[i] = mk_load4(S, 4 * tid + 1024 * i, tag, fail);
                 sq = fmaf(v[i].x, v[i].x, sq);
                 sq = fmaf(v[i].y, v[i].y, sq);
                 sq = fmaf(v[i].z, v[i].z, sq);
@@ -263,8 +295,8 @@ __device__ __forceinline__ int mk_stage_input(const MkStage & S, const Act & a, 
             if (i < K / 1024) {
                 const int k = 4 * tid + 1024 * i;
                 float e[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
-                if (rmsnorm) {
-                    const float4 w = nw[i];
+                if (rmsnorm) {  // norm weights: read-only, cached after the first step
+                    const float4 w = __ldg(reinterpret_cast<const float4 *>(S.norm_w + k));
                     e[0] = __fmul_rn(__fmul_rn(e[0], rms), w.x);
                     e[1] = __fmul_rn(__fmul_rn(e[1], rms), w.y);
                     e[2] = __fmul_rn(__fmul_rn(e[2], rms), w.z);
