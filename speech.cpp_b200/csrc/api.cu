@@ -148,7 +148,21 @@ b200_status mul_mat_impl(b200_context * ctx, const b200_weight * w, int64_t row0
         return B200_OK;
     }
     const int kind = act_kind(w->type);
-    // Many columns of Q8_0: int8 tensor cores (tcgen05) over the once-quantized activations.
+    // Many columns of Q8_0: int8 tensor cores (tcgen05) over the once-quantized activations, on the persistent
+    // tile kernel (32-token tiles x 128-row weight tiles).
+    if (M >= 32 && gemm_tc_grouped_supported(p.w)) {
+        const int64_t ld = (M + 15) & ~(int64_t) 15;
+        b200_status s = ensure_scratch(ctx, quantized_act_bytes(B200_TYPE_Q8_0, K, ld) + 512);
+        if (s != B200_OK) return s;
+        Carve c{(uint8_t *) ctx->scratch};
+        int8_t * q = c.take<int8_t>((size_t) M * K);
+        float * d = c.take<float>((size_t) ld * (K / 32));
+        CK(ctx, launch_quantize(kind, x, K, M, nullptr, q, d, nullptr, ctx->stream, ld));
+        const cudaError_t e = launch_gemm_tc_dense(p.w, row0, n, q, d, ld, M, dst, ld_dst, ctx->dev_err, ctx->num_sms, ctx->stream);
+        if (e == cudaSuccess) return B200_OK;
+        if (e != cudaErrorInvalidValue) return cuda_fail(ctx, e, "launch_gemm_tc_dense");
+        // a tensor map the driver refused: the paths below compute the same product
+    }
     if (gemm_tc_supported(p.w, M)) {
         const int64_t tiles = gemm_tc_tiles(n, M);
         const size_t qb = quantized_act_bytes(kind, K, M + 4), wsb = gemm_tc_workspace_bytes(n, M);

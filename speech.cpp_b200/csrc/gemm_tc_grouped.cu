@@ -5,7 +5,8 @@
 // each segment padded to a multiple of 16 slots, and the pairs' activations are quantized to q8_0 in slot order
 // (q [slots][K] int8, dT [K/32][ldP] float block scales, transposed). A token tile is 16 or 32 consecutive slots of
 // one expert; the route kernel lists the tiles. One work item = one token tile x one 128-row tile of the expert's weight
-// matrix. Per 32-wide K block, one tcgen05.mma kind::i8 of shape M = 128 (weight rows) x N = the tile's token count
+// matrix. A dense product (MUL_MAT with many activation rows) is one expert whose tiles are 32 consecutive tokens.
+// Per 32-wide K block, one tcgen05.mma kind::i8 of shape M = 128 (weight rows) x N = the tile's token count
 // (16 or 32, a run-time field of the instruction descriptor) x K = 32 computes the block's exact int32 sums. Blocks go
 // in pairs into one of four tensor-memory buffers (2 x 32 columns each; eight blocks in flight between the MMA and the
 // epilogue), one barrier round trip per pair; epilogue warps
@@ -45,6 +46,8 @@ struct GLayout {
 struct GroupedParams {
     int64_t N;                // rows per expert (output width)
     int64_t K;
+    int64_t row0;             // first weight row (dense products of a row range)
+    int dense_m;              // > 0: one dense product of dense_m tokens in token order; tiles is null
     const int4 * tiles;       // {expert, first slot, slots (16 or 32), routed slots (the rest is padding)}
     const int * ntiles;       // number of tiles (device)
     int tiles_n;              // 128-row tiles per expert
@@ -53,6 +56,14 @@ struct GroupedParams {
     int64_t ldy;
     unsigned * err;
 };
+
+// Token tile i: from the route kernel's list, or (dense products) 32 consecutive tokens.
+__device__ __forceinline__ int4 g_tile(const GroupedParams & p, int i) {
+    if (p.tiles) return p.tiles[i];
+    const int m0 = 32 * i, rem = p.dense_m - m0;
+    const int live = rem < 32 ? rem : 32;
+    return make_int4(0, m0, (live + 15) & ~15, live);
+}
 
 __global__ void __launch_bounds__(kGThreads, 2)
     gemm_q8_0_tc_grouped_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -70,7 +81,7 @@ __global__ void __launch_bounds__(kGThreads, 2)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nstage = (int) (p.K / 32 / kGKB);
-    const int items = *p.ntiles * p.tiles_n;
+    const int items = (p.tiles ? *p.ntiles : (p.dense_m + 31) / 32) * p.tiles_n;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kGStages; s++) {
@@ -98,8 +109,8 @@ __global__ void __launch_bounds__(kGThreads, 2)
         if (lane == 0) {
             int sg = 0;
             for (int it = blockIdx.x; it < items && !give_up; it += gridDim.x) {
-                const int4 t = p.tiles[it / p.tiles_n];
-                const int arow = (int) ((int64_t) t.x * p.N + (int64_t) (it % p.tiles_n) * kGM);
+                const int4 t = g_tile(p, it / p.tiles_n);
+                const int arow = (int) ((int64_t) t.x * p.N + p.row0 + (int64_t) (it % p.tiles_n) * kGM);
                 const int nsub = t.z / 16;
                 const uint32_t bytes = (uint32_t) (L::kA + t.z * 256 + L::kDw + L::kDx);
                 for (int st = 0; st < nstage; st++, sg++) {
@@ -128,7 +139,7 @@ __global__ void __launch_bounds__(kGThreads, 2)
         if (lane == 0) {
             int sg = 0, g2 = 0;
             for (int it = blockIdx.x; it < items && !give_up; it += gridDim.x) {
-                const int4 t = p.tiles[it / p.tiles_n];
+                const int4 t = g_tile(p, it / p.tiles_n);
                 const uint32_t idesc = idesc_i8_n(t.z);
                 for (int st = 0; st < nstage && !give_up; st++, sg++) {
                     const int s = sg % kGStages;
@@ -168,7 +179,7 @@ __global__ void __launch_bounds__(kGThreads, 2)
         const float2 neg_magic = make_float2(-12582912.0f, -12582912.0f);
         int sg = 0, g2 = 0;
         for (int it = blockIdx.x; it < items && !give_up; it += gridDim.x) {
-            const int4 t = p.tiles[it / p.tiles_n];
+            const int4 t = g_tile(p, it / p.tiles_n);
             const int tn = it % p.tiles_n;
             const bool has = h < t.z / 16;
             const int live = t.w - 16 * h;  // routed slots in this warp's chunk (the rest is padding: no math)
@@ -260,12 +271,14 @@ bool gemm_tc_grouped_supported(const WeightView & w) {
            tensor_maps_available();
 }
 
-cudaError_t launch_gemm_tc_grouped(const WeightView & w, int64_t N, const int4 * tiles, const int * ntiles, const int8_t * q,
-                                   const float * dT, int64_t ldP, int64_t slots, const int32_t * row_map, float * y, int64_t ldy,
-                                   unsigned * err, int num_sms, cudaStream_t st) {
+namespace {
+
+cudaError_t launch_grouped(const WeightView & w, int64_t N, int64_t row0, int dense_m, const int4 * tiles, const int * ntiles,
+                           const int8_t * q, const float * dT, int64_t ldP, int64_t slots, const int32_t * row_map, float * y,
+                           int64_t ldy, unsigned * err, int num_sms, cudaStream_t st) {
     using L = GLayout;
     const int64_t K = w.K, KB = K / 32;
-    if (!gemm_tc_grouped_supported(w) || ldP % 16 || slots % 16 || slots > ldP) return cudaErrorInvalidValue;
+    if (!gemm_tc_grouped_supported(w) || ldP % 16 || slots > ldP || slots < 1) return cudaErrorInvalidValue;
     CUtensorMap ta, tb, tdw, tdx;
     if (!make_map_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.f0, (uint64_t) K, (uint64_t) w.rows, (uint64_t) K, 128, kGM,
                      CU_TENSOR_MAP_SWIZZLE_128B) ||
@@ -278,6 +291,8 @@ cudaError_t launch_gemm_tc_grouped(const WeightView & w, int64_t N, const int4 *
     GroupedParams p;
     p.N = N;
     p.K = K;
+    p.row0 = row0;
+    p.dense_m = dense_m;
     p.tiles = tiles;
     p.ntiles = ntiles;
     p.tiles_n = (int) ((N + kGM - 1) / kGM);
@@ -293,6 +308,21 @@ cudaError_t launch_gemm_tc_grouped(const WeightView & w, int64_t N, const int4 *
     }
     gemm_q8_0_tc_grouped_kernel<<<2 * num_sms, kGThreads, L::kTotal, st>>>(ta, tb, tdw, tdx, p);
     return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_gemm_tc_grouped(const WeightView & w, int64_t N, const int4 * tiles, const int * ntiles, const int8_t * q,
+                                   const float * dT, int64_t ldP, int64_t slots, const int32_t * row_map, float * y, int64_t ldy,
+                                   unsigned * err, int num_sms, cudaStream_t st) {
+    if (slots % 16) return cudaErrorInvalidValue;
+    return launch_grouped(w, N, 0, 0, tiles, ntiles, q, dT, ldP, slots, row_map, y, ldy, err, num_sms, st);
+}
+
+cudaError_t launch_gemm_tc_dense(const WeightView & w, int64_t row0, int64_t N, const int8_t * q, const float * dT, int64_t ldP,
+                                 int64_t M, float * y, int64_t ldy, unsigned * err, int num_sms, cudaStream_t st) {
+    if (M < 1 || M > (1 << 30) || row0 + N > w.rows) return cudaErrorInvalidValue;
+    return launch_grouped(w, N, row0, (int) M, nullptr, nullptr, q, dT, ldP, M, nullptr, y, ldy, err, num_sms, st);
 }
 
 }  // namespace b200

@@ -70,6 +70,9 @@ bool gemm_tc_grouped_supported(const WeightView & w);
 cudaError_t launch_gemm_tc_grouped(const WeightView & w, int64_t N, const int4 * tiles, const int * ntiles, const int8_t * q,
                                    const float * dT, int64_t ldP, int64_t slots, const int32_t * row_map, float * y, int64_t ldy,
                                    unsigned * err, int num_sms, cudaStream_t st);
+// A dense Q8_0 product on the same kernel: q int8 [M][K] in token order, dT [K/32][ldP] (ldP % 16 == 0, >= M).
+cudaError_t launch_gemm_tc_dense(const WeightView & w, int64_t row0, int64_t N, const int8_t * q, const float * dT, int64_t ldP,
+                                 int64_t M, float * y, int64_t ldy, unsigned * err, int num_sms, cudaStream_t st);
 int64_t moe_max_slots(int64_t P, int64_t E);
 int64_t moe_max_tiles(int64_t P, int64_t E);
 cudaError_t launch_moe_route(const int32_t * ids, int64_t T, int64_t top_k, int64_t nb1, int64_t E, int64_t e0, int64_t total,
