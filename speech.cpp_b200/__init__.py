@@ -211,8 +211,13 @@ class Context:
         return w
 
     def set_weight(self, w, data, offset=0):
+        """Uploads GGUF block bytes at a byte offset: numpy (host) or a CUDA uint8 tensor. A CUDA tensor is read on the
+        context's stream, ordered after torch's current stream, and torch's stream then waits for the copy, so the
+        caller may free or overwrite the tensor as soon as this returns."""
         if hasattr(data, "is_cuda") and data.is_cuda:
+            self._sync_in()
             self.check(self.L.b200_weight_set_device(self.h, ctypes.byref(w), _ptr(data), offset, data.numel() * data.element_size()))
+            self._sync_out()
         else:
             import numpy as np
 
@@ -354,7 +359,9 @@ class Decoder:
         """data: numpy (host) or a CUDA tensor; GGUF block bytes for matrices, float32 for norms."""
         if hasattr(data, "is_cuda") and data.is_cuda:
             n = data.numel() * data.element_size()
+            self.ctx._sync_in()  # the tensor's writes (torch's stream) come first; its reuse (after return) comes after
             self.ctx.check(self.L.b200_decoder_set_tensor(self.h, layer, which, _ptr(data), 1, offset, n))
+            self.ctx._sync_out()
         else:
             import numpy as np
 

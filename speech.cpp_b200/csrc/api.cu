@@ -148,9 +148,12 @@ b200_status mul_mat_impl(b200_context * ctx, const b200_weight * w, int64_t row0
         return B200_OK;
     }
     const int kind = act_kind(w->type);
-    // Many columns of Q8_0: int8 tensor cores (tcgen05) over the once-quantized activations, on the persistent
-    // tile kernel (32-token tiles x 128-row weight tiles).
-    if (M >= 32 && gemm_tc_grouped_supported(p.w)) {
+    // Many columns of Q8_0: int8 tensor cores (tcgen05) over the once-quantized activations: the persistent tile
+    // kernel (32-token tiles x 128-row weight tiles, eight K blocks in flight) or the split-K GEMM.
+    // Used for up to 128 rows with at least 48 (token tile x 128-row tile) items; fewer items (long K, few rows) or
+    // more rows run faster on the split-K GEMM below (measured on B200).
+    const int64_t tile_items = ((M + 31) / 32) * ((n + 127) / 128);
+    if (M >= 32 && M <= 128 && tile_items >= 48 && gemm_tc_grouped_supported(p.w)) {
         const int64_t ld = (M + 15) & ~(int64_t) 15;
         b200_status s = ensure_scratch(ctx, quantized_act_bytes(B200_TYPE_Q8_0, K, ld) + 512);
         if (s != B200_OK) return s;

@@ -14,6 +14,8 @@ CASES = [
     (2048, 1000, 100),  # ragged rows and tokens
     (6144, 2048, 64),   # config 4's down projection
     (2048, 384, 257),   # several token tiles
+    (2048, 6144, 64),   # the 32-token tile kernel (96 items), config 4's gate|up shape
+    (1024, 6000, 100),  # tile kernel: ragged rows and a 4-token last tile
 ]
 
 

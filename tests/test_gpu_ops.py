@@ -134,6 +134,24 @@ def test_mul_mat_within_tolerance(ctx, oracle, qtype, K, N, M):
     ctx.free_weight(w)
 
 
+def test_upload_from_device_tensor_survives_reuse(ctx, oracle):
+    """set_weight from a CUDA tensor: the caller may overwrite or free the tensor as soon as the call returns."""
+    import torch
+
+    rng = np.random.default_rng(8)
+    K, N = 2048, 4096
+    wb = rand_w(rng, Q8_0, N, K, oracle)
+    w = ctx.weight(Q8_0, K, N)
+    t = torch.from_numpy(wb.reshape(-1)).cuda()
+    ctx.set_weight(w, t)
+    t.fill_(0)  # on torch's stream, right after the call
+    del t
+    junk = torch.full((wb.size,), 255, dtype=torch.uint8, device="cuda")  # likely reuses the freed block
+    assert np.array_equal(ctx.get_weight(w), wb.reshape(-1))
+    del junk
+    ctx.free_weight(w)
+
+
 def test_mul_mat_rows_shard(ctx, oracle):
     rng = np.random.default_rng(3)
     K, N, M = 1024, 512, 4
