@@ -271,6 +271,106 @@ def config1_gemv(pkg, ctx, stream, copies=64, calls=256, reps=10):
             "gbs": nbytes / us / 1e3}
 
 
+def _product_stack(pkg, ctx, shapes, n_layer, seed):
+    """n_layer x the given (type, K, N) products with device-generated weights (Q8_0: N(0, 0.02) quantized on the device;
+    K-quants: random valid blocks)."""
+    import torch
+
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    layers = []
+    for _ in range(n_layer):
+        ws = []
+        for t, K, N in shapes:
+            w = ctx.weight(t, K, N)
+            for r0 in range(0, N, 8192):
+                rows = min(8192, N - r0)
+                blocks = (ctx.quantize_rows(t, torch.randn((rows, K), generator=g, device="cuda") * 0.02) if t == pkg.Q8_0
+                          else _random_kquant_blocks(t, rows, K, g))
+                ctx.set_weight(w, blocks, offset=r0 * pkg.row_size(t, K))
+            ws.append(w)
+        layers.append(ws)
+    ctx.synchronize()
+    return layers
+
+
+def _time_products(pkg, ctx, stream, layers, M, reps, graph=True):
+    """Event-timed passes over every product of the stack with M activation rows (inputs resident, one output
+    buffer per shape); returns (ms per pass, weight bytes per pass)."""
+    import ctypes
+
+    import torch
+
+    xs, ys, calls = {}, {}, []
+    for ws in layers:
+        for w in ws:
+            if w.ne0 not in xs:
+                xs[w.ne0] = torch.randn((M, w.ne0), device="cuda")
+            if w.ne1 not in ys:
+                ys[w.ne1] = torch.empty((M, w.ne1), device="cuda")
+            calls.append((ctypes.byref(w), ctypes.c_void_p(xs[w.ne0].data_ptr()), ctypes.c_void_p(ys[w.ne1].data_ptr())))
+    fn, h = ctx.L.b200_mul_mat, ctx.h
+
+    def run():
+        for w, x, y in calls:
+            ctx.check(fn(h, w, x, M, y))
+
+    run()
+    ctx.synchronize()
+    g = None
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            run()
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(reps):
+            if g is not None:
+                g.replay()
+            else:
+                run()
+        e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    del g
+    return ms, sum(w.nbytes for ws in layers for w in ws)
+
+
+def config4_batched(pkg, ctx, stream, reps=10):
+    """Config 4: the Qwen3-TTS 1.7B-shaped talker's products (28 x {q|k|v 2048->4096, o 2048->2048,
+    gate|up 2048->12288, down 6144->2048}, Q8_0) for M = 64 concurrent streams: int8 tensor-core products."""
+    layers = _product_stack(pkg, ctx, [(pkg.Q8_0, 2048, 4096), (pkg.Q8_0, 2048, 2048), (pkg.Q8_0, 2048, 12288),
+                                       (pkg.Q8_0, 6144, 2048)], 28, 41)
+    ms, nbytes = _time_products(pkg, ctx, stream, layers, 64, reps)
+    ops = 2.0 * 64 * sum(w.ne0 * w.ne1 for ws in layers for w in ws)
+    for ws in layers:
+        for w in ws:
+            ctx.free_weight(w)
+    return {"M": 64, "ms_per_step": ms, "tok_s": 64 * 1000.0 / ms, "weight_bytes": nbytes, "gbs": nbytes / ms / 1e6,
+            "int8_tops": ops / ms / 1e9}
+
+
+def config3_prefill(pkg, ctx, stream, reps=2):
+    """Config 3's prefill: the Qwen3-ASR 1.7B-shaped decoder's products (28 x {q|k|v 2048->4096, o 2048->2048,
+    gate|up 2048->12288 Q4_K; down 6144->2048 Q6_K}) for M = 1500 rows (the head runs on the last row only: one
+    2048 -> 151936 Q6_K product, M = 1). K-quant products with many rows run on the GEMV kernels in column chunks."""
+    layers = _product_stack(pkg, ctx, [(pkg.Q4_K, 2048, 4096), (pkg.Q4_K, 2048, 2048), (pkg.Q4_K, 2048, 12288),
+                                       (pkg.Q6_K, 6144, 2048)], 28, 43)
+    head = _product_stack(pkg, ctx, [(pkg.Q6_K, 2048, 151936)], 1, 44)
+    ms, nbytes = _time_products(pkg, ctx, stream, layers, 1500, reps, graph=False)
+    ms_head, head_bytes = _time_products(pkg, ctx, stream, head, 1, 5)
+    ops = 2.0 * 1500 * sum(w.ne0 * w.ne1 for ws in layers for w in ws) + 2.0 * 2048 * 151936
+    for ws in layers + head:
+        for w in ws:
+            ctx.free_weight(w)
+    total = ms + ms_head
+    return {"M": 1500, "ms": total, "rows_per_s": 1500 * 1000.0 / total, "weight_bytes": nbytes + head_bytes,
+            "gbs": (nbytes + head_bytes) / total / 1e6, "int8_tops": ops / total / 1e9,
+            "path": "GEMV kernels in 16-column chunks (no K-quant tensor-core path yet)"}
+
+
 def config3_decode(pkg, ctx, stream, steps=128):
     """Config 3's decode phase: 128 batch-1 steps of the Qwen3-ASR 1.7B-shaped decoder (Q4_K attention and gate|up,
     Q6_K down and the 2048 -> 151936 head; random valid blocks), one persistent launch per step."""
@@ -663,7 +763,8 @@ def run_b200(args):
     if world == 1 and not args.no_configs:
         del dec
         dec = None
-        extra = {"c1_gemv_q8_0": config1_gemv(pkg, ctx, stream), "c3_asr17_decode": config3_decode(pkg, ctx, stream)}
+        extra = {"c1_gemv_q8_0": config1_gemv(pkg, ctx, stream), "c3_asr17_decode": config3_decode(pkg, ctx, stream),
+                 "c4_batched_m64": config4_batched(pkg, ctx, stream), "c3_asr17_prefill": config3_prefill(pkg, ctx, stream)}
     peak, peak_kind = peaks()
     achieved = wbytes / (ms_step / 1000.0) / 1e9  # GB/s of algorithmic weight bytes, per GPU
     traffic = profile_traffic()
