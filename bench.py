@@ -190,7 +190,7 @@ def run_reference(args):
         "wall_s": wall,
         "note": "CPU restatement of ggml's CPU quantized vec_dot (oracle/); ggml itself is absent from the reference checkout",
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0
 
 
@@ -666,6 +666,89 @@ def run_moe(args, pkg, ctx, dist, world, rank, local):
     return res
 
 
+def run_batched(args, pkg, ctx, dist, world, rank, local):
+    """Config 4 over N GPUs: the Qwen3-TTS 1.7B-shaped talker's products (28 x {q|k|v 2048->4096, o 2048->2048,
+    gate|up 2048->12288, down 6144->2048}, Q8_0) for M = 64 streams, every product split by output rows (rank r holds
+    rows [r N/G, (r+1) N/G)) with one all-gather + assembly per product (speech.cpp_b200/column_parallel.py). Inputs
+    are resident and replicated; the step is one CUDA graph; strong scaling (the same 64 streams at every N)."""
+    import importlib
+
+    import torch
+
+    cp = importlib.import_module(pkg.__name__ + ".column_parallel")
+    M, L = 64, 28
+    shapes = [(2048, 4096), (2048, 2048), (2048, 12288), (6144, 2048)]
+    g = torch.Generator(device="cuda").manual_seed(4000 + rank)
+    group = dist.group.WORLD if dist else None
+    prods, bufs = [], []
+    xs = {K: torch.randn((M, K), generator=g, device="cuda") for K in (2048, 6144)}
+    outs = {N: torch.empty((M, N), device="cuda") for _, N in shapes}
+    for _ in range(L):
+        for K, N in shapes:
+            r0, n = cp.row_shard(N, world, rank)
+            w = ctx.weight(pkg.Q8_0, K, n)
+            for q0 in range(0, n, 4096):
+                rows = min(4096, n - q0)
+                ctx.set_weight(w, ctx.quantize_rows(pkg.Q8_0, torch.randn((rows, K), generator=g, device="cuda") * 0.02),
+                               offset=q0 * pkg.row_size(pkg.Q8_0, K))
+            prods.append((cp.ColumnParallelProduct(lambda w, x, out: ctx.mul_mat(w, x, out=out), w, N, group=group), K, N))
+            bufs.append((torch.empty((M, n), device="cuda"), torch.empty((world, M, n), device="cuda")))
+    ctx.synchronize()
+    stream = ctx.torch_stream()
+
+    def step():
+        for (prod, K, N), (lo, ga) in zip(prods, bufs):
+            prod(xs[K], lo, ga, outs[N])
+
+    with torch.cuda.stream(stream):
+        step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize()
+    steps = args.moe_steps
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for _ in range(steps):
+                graph.replay()
+            ev1.record(stream)
+        ev1.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    if dist:
+        dist.barrier()
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    del graph
+    torch.cuda.synchronize()
+    ms_step = ms / steps
+    wbytes = sum(p[0].w.nbytes for p in prods)
+    for p in prods:
+        ctx.free_weight(p[0].w)
+    peak, peak_kind = peaks()
+    achieved = wbytes / (ms_step / 1000.0) / 1e9
+    return {
+        "metric": "batched decode tok/s, Qwen3-TTS 1.7B-shaped talker products (Q8_0, M = 64 streams)", "value": M * 1000.0 / ms_step,
+        "unit": UNIT, "n_gpus": world, "steps": steps, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
+        "dtype": "int8xint8->int32, f32 accumulate", "data": "synthetic",
+        "config": {"workload": "config 4: 28 x {q|k|v 2048->4096, o 2048->2048, gate|up 2048->12288, down 6144->2048}, Q8_0, M = 64",
+                   "global_batch": M, "parallelism": f"column split x{world} (all-gather per product)" if world > 1 else "single",
+                   "l2": f"weights {wbytes / 1e9:.2f} GB per GPU > 126 MB L2"},
+        "roofline": {"bound": "hbm", "kernel": "the product stack (tensor-core GEMMs + all-gathers)", "achieved": achieved, "peak": peak,
+                     "unit": "GB/s", "frac": achieved / peak, "algorithmic_bytes_per_step": wbytes, "traffic": None,
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6650"},
+        "gpu_launches": 2 * L * len(shapes) * steps, "clocks": clk.summary(),
+    }
+
+
 def run_b200(args):
     import torch
 
@@ -687,15 +770,15 @@ def run_b200(args):
 
     pkg = load_package()
     ctx = pkg.Context(local)
-    if args.workload == "moe":
-        res = run_moe(args, pkg, ctx, dist, world, rank, local)
+    if args.workload in ("moe", "batched"):
+        res = (run_moe if args.workload == "moe" else run_batched)(args, pkg, ctx, dist, world, rank, local)
         ctx.close()
         if dist:
             dist.barrier()
             dist.destroy_process_group()
         if rank == 0:
             res.update(warmup=args.warmup, vs_baseline=None)
-            if world == 1 and not args.no_cpu:
+            if world == 1 and not args.no_cpu and args.workload == "moe":
                 cm = CpuMoe(MOE)
                 cm.once()
                 t0 = time.perf_counter()
@@ -704,7 +787,7 @@ def run_b200(args):
                     cm.once()
                     reps += 1
                 res["cpu_baseline"] = {"value": cm.rate(), "unit": UNIT, "cores": cm.cores, "kind": "port", "sample": cm.sample_text(reps)}
-            print(json.dumps(res), flush=True)
+            emit(res)
         return 0
     dec, c = make_decoder(pkg, ctx, seed=1234 + rank)
     stream = ctx.torch_stream()
@@ -799,11 +882,38 @@ def run_b200(args):
         if world == 1 and not args.no_cpu:
             v, cores, sample = cpu_sample(12.0)
             result["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
-        print(json.dumps(result), flush=True)
+        emit(result)
     return 0
 
 
+class _StdoutToStderr:
+    """Points file descriptor 1 at stderr until restore(): libraries (NCCL's version banner, warnings) write to stdout,
+    and the driver reads rank 0's stdout for the one JSON line."""
+
+    def __init__(self):
+        sys.stdout.flush()
+        self.saved = os.dup(1)
+        os.dup2(2, 1)
+
+    def restore(self):
+        sys.stdout.flush()
+        os.dup2(self.saved, 1)
+        os.close(self.saved)
+
+
+def emit(line):
+    """Prints the result line on the real stdout."""
+    if _QUIET is not None:
+        _QUIET.restore()
+    print(json.dumps(line), flush=True)
+
+
+_QUIET = None
+
+
 def main():
+    global _QUIET
+    _QUIET = _StdoutToStderr()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
@@ -811,9 +921,10 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-configs", action="store_true", help="skip the config 1 and config 3 side measurements")
-    ap.add_argument("--workload", default="decode", choices=["decode", "moe"],
-                    help="decode: config 2 decode step (the headline line); moe: config 5 MoE FFN stack, expert-parallel")
-    ap.add_argument("--moe-steps", type=int, default=20, help="timed steps of the MoE workload")
+    ap.add_argument("--workload", default="decode", choices=["decode", "moe", "batched"],
+                    help="decode: config 2 decode step (the headline line); moe: config 5 MoE FFN stack, expert-parallel; "
+                         "batched: config 4 product stack, column-split")
+    ap.add_argument("--moe-steps", type=int, default=20, help="timed steps of the MoE and batched workloads")
     ap.add_argument("--moe-layers", type=int, default=48, help="MoE layers per step (48 = config 5; fewer only for profiling)")
     args = ap.parse_args()
     if args.impl == "reference":
