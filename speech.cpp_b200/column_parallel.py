@@ -36,11 +36,12 @@ class ColumnParallelProduct:
     def __call__(self, x, local_out, gathered, out):
         """x [M][K] -> out [M][n_rows] on every rank; local_out [M][n_rows / G] and gathered [G][M][n_rows / G] are
         the caller's buffers (kept across calls: a CUDA graph can hold them)."""
-        self.mm(self.w, x, local_out)
-        if self.group is None:
-            out.copy_(local_out)
-            return out
         import torch.distributed as dist
+
+        if self.group is None or dist.get_world_size(self.group) == 1:
+            self.mm(self.w, x, out)
+            return out
+        self.mm(self.w, x, local_out)
 
         G, M, n = gathered.shape
         dist.all_gather_into_tensor(gathered.view(G * M, n), local_out, group=self.group)
