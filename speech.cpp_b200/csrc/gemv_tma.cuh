@@ -86,12 +86,21 @@ __device__ __forceinline__ void smem_rows_lpr(const uint8_t * const * f, int64_t
     }
 }
 
-// Lanes per row: 8 for rows of up to 64 units (a warp reduces 4 rows at once), but more when the chunk has few rows,
-// so that its rows spread over all warps (a chunk of at most one row per warp takes a whole warp per row), and 32 for
-// longer rows.
+// Lanes per row: 8 for rows of up to 64 units (a warp reduces 4 rows at once), 32 for longer rows. A function of K
+// alone, so a row's summation order does not depend on how rows are chunked (launch geometry never changes results).
 template <class T, class Store>
 __device__ __forceinline__ void smem_rows(const uint8_t * const * f, int64_t K, int rows, const Act & a, const WeightView & w,
                                           int warp, int nwarps, Store store) {
+    if (T::units_per_row(K) <= 64) smem_rows_lpr<T, 8>(f, K, rows, a, w, warp, nwarps, store);
+    else smem_rows_lpr<T, 32>(f, K, rows, a, w, warp, nwarps, store);
+}
+
+// The same with lanes per row also chosen from the chunk's row count, for callers whose chunking is fixed per product
+// (the persistent decode step): a chunk of few rows spreads them over all warps (at most one row per warp: a whole
+// warp per row) instead of leaving warps idle.
+template <class T, class Store>
+__device__ __forceinline__ void smem_rows_spread(const uint8_t * const * f, int64_t K, int rows, const Act & a, const WeightView & w,
+                                                 int warp, int nwarps, Store store) {
     if (T::units_per_row(K) > 64 || rows <= nwarps) smem_rows_lpr<T, 32>(f, K, rows, a, w, warp, nwarps, store);
     else if (rows <= 2 * nwarps) smem_rows_lpr<T, 16>(f, K, rows, a, w, warp, nwarps, store);
     else smem_rows_lpr<T, 8>(f, K, rows, a, w, warp, nwarps, store);
