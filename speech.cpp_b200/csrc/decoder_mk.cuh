@@ -339,7 +339,7 @@ __device__ __forceinline__ void mk_rows(const MkStage & S, const Act & a, const 
         f[i] = b;
         if (i < T::kFields) b += rps * T::field_row_bytes(K, i);
     }
-    smem_rows_spread<T>(f, K, (int) rows, a, S.w, warp, kMkConsumerWarps, [&](int j, float v) {
+    smem_rows<T>(f, K, (int) rows, a, S.w, warp, kMkConsumerWarps, [&](int j, float v) {
         {
             const int64_t r = first + j;
             float out = v;

@@ -95,17 +95,6 @@ __device__ __forceinline__ void smem_rows(const uint8_t * const * f, int64_t K, 
     else smem_rows_lpr<T, 32>(f, K, rows, a, w, warp, nwarps, store);
 }
 
-// The same with lanes per row also chosen from the chunk's row count, for callers whose chunking is fixed per product
-// (the persistent decode step): a chunk of few rows spreads them over all warps (at most one row per warp: a whole
-// warp per row) instead of leaving warps idle.
-template <class T, class Store>
-__device__ __forceinline__ void smem_rows_spread(const uint8_t * const * f, int64_t K, int rows, const Act & a, const WeightView & w,
-                                                 int warp, int nwarps, Store store) {
-    if (T::units_per_row(K) > 64 || rows <= nwarps) smem_rows_lpr<T, 32>(f, K, rows, a, w, warp, nwarps, store);
-    else if (rows <= 2 * nwarps) smem_rows_lpr<T, 16>(f, K, rows, a, w, warp, nwarps, store);
-    else smem_rows_lpr<T, 8>(f, K, rows, a, w, warp, nwarps, store);
-}
-
 template <class T, int NC>
 __global__ void __launch_bounds__(kTmaThreads, 2) gemv_tma_kernel(GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
