@@ -148,6 +148,15 @@ b200_status mul_mat_impl(b200_context * ctx, const b200_weight * w, int64_t row0
         return B200_OK;
     }
     const int kind = act_kind(w->type);
+    // Many columns of Q4_K / Q6_K: int8 tensor cores over an expanded copy of the weights (made once, cached).
+    if (gemm_kq_tc_supported(p.w, M) && ((uintptr_t) x & 15) == 0) {
+        b200_status s = ensure_scratch(ctx, gemm_kq_tc_act_bytes(K, M) + 256);
+        if (s != B200_OK) return s;
+        const cudaError_t e = launch_gemm_kq_tc(ctx, w, row0, n, x, M, dst, ld_dst, ctx->scratch);
+        if (e == cudaSuccess) return B200_OK;
+        if (e != cudaErrorInvalidValue) return cuda_fail(ctx, e, "launch_gemm_kq_tc");
+        // a tensor map the driver refused: the GEMV path below computes the same product
+    }
     // Many columns of Q8_0: int8 tensor cores (tcgen05) over the once-quantized activations: the persistent tile
     // kernel (32-token tiles x 128-row weight tiles, eight K blocks in flight) or the split-K GEMM.
     // Used for up to 128 rows with at least 48 (token tile x 128-row tile) items; fewer items (long K, few rows) or
@@ -288,6 +297,7 @@ void b200_context_destroy(b200_context * ctx) {
     if (!ctx) return;
     cudaSetDevice(ctx->device);
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    b200::kq_release_all(ctx);
     if (ctx->scratch) cudaFree(ctx->scratch);
     if (ctx->staging) cudaFree(ctx->staging);
     if (ctx->dev_err) cudaFree(ctx->dev_err);
@@ -377,6 +387,7 @@ b200_status b200_weight_alloc(b200_context * ctx, int type, int64_t ne0, int64_t
 
 b200_status b200_weight_free(b200_context * ctx, b200_weight * w) {
     if (!ctx || !w) return fail(ctx, B200_ERR_INVALID, "weight_free: NULL argument");
+    if (w->data) kq_release(ctx, w->data);
     if (w->data) CK(ctx, cudaFree(w->data));
     w->data = nullptr;
     return B200_OK;
@@ -387,6 +398,7 @@ static const size_t kStagingPiece = (size_t) 64 << 20;
 b200_status b200_weight_set(b200_context * ctx, b200_weight * w, const void * host_src, size_t offset, size_t size) {
     if (!ctx || !w || !w->data || (size && !host_src)) return fail(ctx, B200_ERR_INVALID, "weight_set: NULL argument");
     if (offset > w->nbytes || size > w->nbytes - offset) return fail(ctx, B200_ERR_INVALID, "weight_set: range outside the tensor");
+    kq_release(ctx, w->data);  // an expanded copy of the old bytes is stale
     if (w->type == B200_TYPE_BF16 || w->type == B200_TYPE_F32) {
         CK(ctx, cudaMemcpyAsync((uint8_t *) w->data + offset, host_src, size, cudaMemcpyHostToDevice, ctx->stream));
         return B200_OK;
@@ -407,6 +419,7 @@ b200_status b200_weight_set(b200_context * ctx, b200_weight * w, const void * ho
 b200_status b200_weight_set_device(b200_context * ctx, b200_weight * w, const void * dev_src, size_t offset, size_t size) {
     if (!ctx || !w || !w->data || (size && !dev_src)) return fail(ctx, B200_ERR_INVALID, "weight_set_device: NULL argument");
     if (offset > w->nbytes || size > w->nbytes - offset) return fail(ctx, B200_ERR_INVALID, "weight_set_device: range outside the tensor");
+    kq_release(ctx, w->data);  // an expanded copy of the old bytes is stale
     if (w->type == B200_TYPE_BF16 || w->type == B200_TYPE_F32) {
         CK(ctx, cudaMemcpyAsync((uint8_t *) w->data + offset, dev_src, size, cudaMemcpyDeviceToDevice, ctx->stream));
         return B200_OK;

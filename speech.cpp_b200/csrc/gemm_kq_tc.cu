@@ -1,0 +1,519 @@
+// gemm_kq_tc.cu — Q4_K and Q6_K products with many activation rows (prefill) on the int8 tensor cores.
+//
+// ggml's CPU backend multiplies K-quant weights by q8_K activations (one float scale per 256 values, int8 values,
+// int16 sums of 16) with exact integer sums per super-block of 256:
+//   Q4_K: sumi = sum_s sc_s * (sum_l q_l x_l) and summ = sum_s m_s * (bsum_2s + bsum_2s+1) over the 8 sub-blocks s of
+//         32 (q in 0..15, six-bit scale sc and min m), then sumf += (dx * d) * sumi - (dx * dmin) * summ;
+//   Q6_K: sumi = sum_g sc_g * (sum_l (q_l - 32) x_l) over the 16 groups g of 16 (int8 scales), then
+//         sumf += (d * dx) * sumi.
+// Here the same integers come from the tensor cores. Each weight matrix is expanded once (on the first product with
+// many rows; cached until the weight is written or freed) into int8 values: Q4_K's nibbles as 0..15; Q6_K's q - 32 as
+// two zero-masked 32-value blocks per 32 values ([q_0..q_15, 0 x 16] and [0 x 16, q_16..q_31]), because its scale
+// changes every 16 values while one tcgen05.mma kind::i8 spans K = 32. One MMA (two for Q6_K) of M = 128 weight rows x
+// N = 32 tokens x K = 32 gives exact int32 sums into tensor memory; epilogue warps fold them into int32 super-block
+// sums with the integer scales (and, for Q4_K, the mins times the activations' 32-value sums), and convert once per
+// super-block to float, in super-block order. Pipeline as in the grouped Q8_0 kernel (gemm_tc_grouped.cu): warp 0 =
+// TMA producer (no multicast), warp 1 = tensor-memory allocator and MMA issuer, warps 2..9 = epilogue; four
+// accumulator buffers of 2 x 32 columns; every wait bounded.
+#include <unordered_map>
+
+#include "internal.h"
+#include "tcgen05.cuh"
+
+namespace b200 {
+
+// ------------------------------------------------------------------------------------------------------------------
+// Expansion
+// ------------------------------------------------------------------------------------------------------------------
+// Q4_K: q int8 [rows][K] (0..15), scm uint16 [rows][K/32] (sc | m << 8), dd float4 [rows][K/256] (d, dmin, 0, 0).
+__global__ void expand_q4k_kernel(WeightView w, int8_t * q, uint16_t * scm, float4 * dd) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nsb = w.K / 256, total = w.rows * nsb;
+    const int64_t warps = (int64_t) gridDim.x * (blockDim.x >> 5);
+    for (int64_t i = (int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); i < total; i += warps) {
+        const int64_t r = i / nsb, sb = i % nsb;
+        const uint8_t * qs = w.f0 + r * (w.K / 2) + sb * 128;
+        const uint8_t * meta = w.f1 + (r * nsb + sb) * 16;  // d, dmin (fp16), 12 scale bytes
+        const int s = lane >> 2, l0 = (lane & 3) * 8;  // this lane: values 8 lane .. 8 lane + 7 = sub-block s, l0..
+        const uint8_t * src = qs + (s >> 1) * 32 + l0;
+        const int shift = (s & 1) * 4;
+        uint32_t lo = 0, hi = 0;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            lo |= (uint32_t) ((src[j] >> shift) & 15) << (8 * j);
+            hi |= (uint32_t) ((src[4 + j] >> shift) & 15) << (8 * j);
+        }
+        *reinterpret_cast<uint2 *>(q + r * w.K + sb * 256 + lane * 8) = make_uint2(lo, hi);
+        if (lane < 8) {
+            int sc, m;
+            TQ4_K::scale_min(meta + 4, lane, sc, m);
+            scm[r * (w.K / 32) + sb * 8 + lane] = (uint16_t) (sc | (m << 8));
+        }
+        if (lane == 0) {
+            const float d = __half2float(*reinterpret_cast<const __half *>(meta));
+            const float dmin = __half2float(*reinterpret_cast<const __half *>(meta + 2));
+            dd[r * nsb + sb] = make_float4(d, dmin, 0.0f, 0.0f);
+        }
+    }
+}
+
+// Q6_K: q int8 [rows][2K] (32-value block b -> expanded blocks 2b = [q - 32 of values 0..15, 0 x 16] and
+// 2b + 1 = [0 x 16, q - 32 of values 16..31]), dd float4 [rows][K/256] (d, 0, 0, 0). The int8 scales stay in the
+// weight's own sc field, [rows][K/16].
+__global__ void expand_q6k_kernel(WeightView w, int8_t * q, float4 * dd) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nsb = w.K / 256, total = w.rows * nsb;
+    const int64_t warps = (int64_t) gridDim.x * (blockDim.x >> 5);
+    for (int64_t i = (int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); i < total; i += warps) {
+        const int64_t r = i / nsb, sb = i % nsb;
+        const uint8_t * ql = w.f0 + r * (w.K / 2) + sb * 128;
+        const uint8_t * qh = w.f1 + r * (w.K / 4) + sb * 64;
+        const int b = lane >> 2, p0 = (lane & 3) * 8;  // values 8 lane .. 8 lane + 7: block b, positions p0..p0+7
+        const int h = b >> 2, t = b & 3;
+        uint32_t v0 = 0, v1 = 0;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const int l = p0 + j;
+            const int lo4 = (ql[h * 64 + (t & 1) * 32 + l] >> ((t >> 1) * 4)) & 15;
+            const int hi2 = (qh[h * 32 + l] >> (2 * t)) & 3;
+            const uint32_t v = (uint32_t) (uint8_t) (int8_t) ((lo4 | (hi2 << 4)) - 32);
+            if (j < 4) v0 |= v << (8 * j);
+            else v1 |= v << (8 * (j - 4));
+        }
+        int8_t * base = q + r * (2 * w.K) + sb * 512 + b * 64;
+        const uint2 vals = make_uint2(v0, v1), zero = make_uint2(0u, 0u);
+        *reinterpret_cast<uint2 *>(base + p0) = p0 < 16 ? vals : zero;
+        *reinterpret_cast<uint2 *>(base + 32 + p0) = p0 < 16 ? zero : vals;
+        if (lane == 0) dd[r * nsb + sb] = make_float4(__half2float(reinterpret_cast<const __half *>(w.f3)[r * nsb + sb]), 0.0f, 0.0f, 0.0f);
+    }
+}
+
+// q8_K of M activation rows for the tensor-core products: q int8 [M][K], dxT float [K/256][ld] (transposed scales),
+// bsT int32 [K/32][ld] (sums of each 32 values). One warp per 256-block; bit-identical to quantize_row_q8_K.
+__global__ void quantize_q8k_tc_kernel(const float * __restrict__ x, int64_t K, int64_t M, int8_t * q, float * dxT, int32_t * bsT, int64_t ld) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nsb = K / 256;
+    const int64_t warps = (int64_t) gridDim.x * (blockDim.x >> 5);
+    for (int64_t i = (int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); i < M * nsb; i += warps) {
+        const int64_t m = i / nsb, sb = i % nsb;
+        const float * xb = x + m * K + sb * 256 + lane * 8;
+        const float4 a = *reinterpret_cast<const float4 *>(xb), c = *reinterpret_cast<const float4 *>(xb + 4);
+        const float v[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+        int8_t qv[8];
+        int16_t bsum;
+        float df;
+        quantize_q8_K_warp(v, qv, &bsum, &df);
+        uint32_t lo = 0, hi = 0;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            lo |= (uint32_t) (uint8_t) qv[j] << (8 * j);
+            hi |= (uint32_t) (uint8_t) qv[4 + j] << (8 * j);
+        }
+        *reinterpret_cast<uint2 *>(q + m * K + sb * 256 + lane * 8) = make_uint2(lo, hi);
+        // lanes 4j .. 4j + 3 hold the 32 values of block j; bsum is the sum of the lane pair's 16
+        const int s32 = (int) bsum + __shfl_down_sync(0xffffffffu, (int) bsum, 2);
+        if ((lane & 3) == 0) bsT[(sb * 8 + lane / 4) * ld + m] = s32;
+        if (lane == 0) dxT[sb * ld + m] = df;
+    }
+}
+
+namespace {
+
+constexpr int kQM = 128;       // weight rows per tile
+constexpr int kQNT = 32;       // tokens per tile
+constexpr int kQKB = 4;        // 32-value blocks per stage
+constexpr int kQThreads = 320; // producer, MMA, 8 epilogue warps
+constexpr int kQEpiWarps = 8;
+constexpr int kQBufs = 4;      // tensor-memory buffers of 2 x kQNT columns
+constexpr unsigned kErrTimeout = 4u;
+
+template <int KIND>
+struct KqLayout {
+    static constexpr int kAT = KIND == 6 ? 2 : 1;          // A tiles ([128 rows][128 B], swizzled) per stage
+    static constexpr int kA = kAT * kQM * 128;
+    static constexpr int kB = kQKB * kQNT * 32;            // activations: [32 rows][128 B] swizzled
+    static constexpr int kSc = kQM * 16;                   // 16-byte box per row of scales (this stage's half)
+    static constexpr int kDd = kQM * 16;                   // float4 (d, dmin) per row
+    static constexpr int kDx = kQNT * 4;                   // the super-block's activation scales
+    static constexpr int kBs = KIND == 4 ? kQKB * kQNT * 4 : 0;  // activation sums of 32 (Q4_K's min term)
+    static constexpr int kStage = (kA + kB + kSc + kDd + kDx + kBs + 1023) & ~1023;
+    static constexpr int kStages = KIND == 4 ? 3 : 2;
+    static constexpr int kTotal = kStages * kStage + 1024 + 1024;
+};
+
+struct KqParams {
+    int64_t N, K, row0;
+    int M;
+    int tiles_m, tiles_n;
+    float * y;
+    int64_t ldy;
+    unsigned * err;
+};
+
+template <int KIND>
+__global__ void __launch_bounds__(kQThreads, 2)
+    gemm_kq_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const __grid_constant__ CUtensorMap tmSc, const __grid_constant__ CUtensorMap tmDd,
+                      const __grid_constant__ CUtensorMap tmDx, const __grid_constant__ CUtensorMap tmBs, KqParams p) {
+    using L = KqLayout<KIND>;
+    constexpr int S = L::kStages;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t * smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t) 1023);
+    uint64_t * bars = reinterpret_cast<uint64_t *>(smem + S * L::kStage);
+    uint64_t * full = bars;
+    uint64_t * empty = bars + S;
+    uint64_t * acc_full = bars + 2 * S;
+    uint64_t * acc_empty = acc_full + kQBufs;
+    uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + kQBufs);
+    __shared__ volatile int give_up;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nstage = (int) (p.K / 32 / kQKB);
+    const int items = p.tiles_m * p.tiles_n;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1 + kQEpiWarps);
+        }
+        for (int b = 0; b < kQBufs; b++) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], kQEpiWarps);
+        }
+        fence_mbar_init();
+        give_up = 0;
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)), "r"(2 * kQBufs * kQNT));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    // item -> (token tile, row tile): consecutive items share a weight tile (its 128 rows come from L2 for the
+    // other token tiles)
+    auto tile_of = [&](int it, int & m0, int & nz, int & live, int & tn) {
+        const int tm = it % p.tiles_m;
+        tn = it / p.tiles_m;
+        m0 = tm * kQNT;
+        live = p.M - m0 < kQNT ? p.M - m0 : kQNT;
+        nz = (live + 15) & ~15;
+    };
+
+    if (warp == 0) {
+        // ---- TMA producer ----
+        if (lane == 0) {
+            int sg = 0;
+            for (int it = blockIdx.x; it < items && !give_up; it += gridDim.x) {
+                int m0, nz, live, tn;
+                tile_of(it, m0, nz, live, tn);
+                const int arow = (int) (p.row0 + (int64_t) tn * kQM);
+                const uint32_t bytes = (uint32_t) (L::kA + nz * 128 + L::kSc + L::kDd + L::kDx + L::kBs);
+                for (int st = 0; st < nstage; st++, sg++) {
+                    const int s = sg % S, use = sg / S;
+                    if (use > 0 && !mbar_wait_sleep(&empty[s], (use - 1) & 1)) {
+                        atomicOr(p.err, kErrTimeout);
+                        give_up = 1;
+                        break;
+                    }
+                    uint8_t * base = smem + s * L::kStage;
+                    mbar_arrive_expect_tx(&full[s], bytes);
+                    const int kbs = st * kQKB;  // first 32-value block of the stage
+                    if (KIND == 4) {
+                        tma_load_2d(base, &tmA, kbs * 32, arow, &full[s]);
+                    } else {
+                        tma_load_2d(base, &tmA, 2 * kbs * 32, arow, &full[s]);
+                        tma_load_2d(base + kQM * 128, &tmA, 2 * kbs * 32 + 128, arow, &full[s]);
+                    }
+                    for (int r = 0; r < nz / 16; r++) tma_load_2d(base + L::kA + r * 16 * 128, &tmB, kbs * 32, m0 + 16 * r, &full[s]);
+                    uint8_t * sc = base + L::kA + L::kB;
+                    if (KIND == 4) tma_load_2d(sc, &tmSc, kbs & ~7, arow, &full[s]);         // 8 (sc | m << 8)
+                    else tma_load_2d(sc, &tmSc, (2 * kbs) & ~15, arow, &full[s]);             // 16 int8 scales
+                    tma_load_2d(sc + L::kSc, &tmDd, 4 * (kbs / 8), arow, &full[s]);
+                    tma_load_2d(sc + L::kSc + L::kDd, &tmDx, m0, kbs / 8, &full[s]);
+                    if (KIND == 4) tma_load_2d(sc + L::kSc + L::kDd + L::kDx, &tmBs, m0, kbs, &full[s]);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---- MMA issuer: a buffer takes two accumulators: Q4_K two blocks, Q6_K one block's two halves ----
+        if (lane == 0) {
+            int sg = 0, g2 = 0;
+            for (int it = blockIdx.x; it < items && !give_up; it += gridDim.x) {
+                int m0, nz, live, tn;
+                tile_of(it, m0, nz, live, tn);
+                const uint32_t idesc = idesc_i8_n(nz);
+                for (int st = 0; st < nstage && !give_up; st++, sg++) {
+                    const int s = sg % S;
+                    if (!mbar_wait_sleep(&full[s], (sg / S) & 1)) {
+                        atomicOr(p.err, kErrTimeout);
+                        give_up = 1;
+                        break;
+                    }
+                    tc_fence_after();
+                    uint8_t * base = smem + s * L::kStage;
+                    constexpr int kPerStage = KIND == 4 ? kQKB / 2 : kQKB;  // buffers per stage
+                    for (int u = 0; u < kPerStage; u++, g2++) {
+                        const int buf = g2 % kQBufs, use = g2 / kQBufs;
+                        if (use > 0 && !mbar_wait_sleep(&acc_empty[buf], (use - 1) & 1)) {
+                            atomicOr(p.err, kErrTimeout);
+                            give_up = 1;
+                            break;
+                        }
+                        tc_fence_after();
+#pragma unroll
+                        for (int jj = 0; jj < 2; jj++) {
+                            const int blk = KIND == 4 ? 2 * u + jj : u;     // 32-value block of the stage
+                            const int e = KIND == 4 ? blk : 2 * u + jj;     // A block (expanded for Q6_K)
+                            mma_i8(tmem + buf * 2 * kQNT + jj * kQNT, smem_desc_sw128(base + (e >> 2) * kQM * 128, e & 3),
+                                   smem_desc_sw128(base + L::kA, blk), idesc);
+                        }
+                        mma_commit(&acc_full[buf]);
+                    }
+                    if (give_up) break;
+                    mma_commit(&empty[s]);
+                }
+            }
+        }
+    } else {
+        // ---- epilogue: lane quarter q = warp % 4 owns tile rows 32 q .. 32 q + 31; warp half h the 16 tokens
+        // 16 h .. 16 h + 15. A warp without tokens in a tile still waits and arrives on every barrier ----
+        const int q = warp & 3, h = (warp - 2) >> 2;
+        const int row = 32 * q + lane;
+        int sg = 0, g2 = 0;
+        for (int it = blockIdx.x; it < items && !give_up; it += gridDim.x) {
+            int m0, nz, live_all, tn;
+            tile_of(it, m0, nz, live_all, tn);
+            const bool has = 16 * h < nz;
+            const int live = live_all - 16 * h;
+            float acc[16];
+            int isum[16], msum[16];
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+                acc[i] = 0.0f;
+                isum[i] = 0;
+                msum[i] = 0;
+            }
+            for (int st = 0; st < nstage && !give_up; st++, sg++) {
+                const int s = sg % S;
+                const uint8_t * base = smem + s * L::kStage;
+                const uint8_t * sc = base + L::kA + L::kB;
+                const float4 ddv = reinterpret_cast<const float4 *>(sc + L::kSc)[row];
+                const float * dx = reinterpret_cast<const float *>(sc + L::kSc + L::kDd);
+                const int * bs = reinterpret_cast<const int *>(sc + L::kSc + L::kDd + L::kDx);
+                const int kbs = st * kQKB;
+                constexpr int kPerStage = KIND == 4 ? kQKB / 2 : kQKB;
+                for (int u = 0; u < kPerStage; u++, g2++) {
+                    const int buf = g2 % kQBufs, use = g2 / kQBufs;
+                    if (!mbar_wait_sleep(&acc_full[buf], use & 1)) {
+                        if (lane == 0) atomicOr(p.err, kErrTimeout);
+                        give_up = 1;
+                        break;
+                    }
+                    tc_fence_after();
+                    if (!has) {
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&acc_empty[buf]);
+                        continue;
+                    }
+                    // the buffer's two accumulators one at a time (16 sums each); released after the second load
+                    const uint32_t ta = tmem + ((uint32_t) (32 * q) << 16) + buf * 2 * kQNT + 16 * h;
+#pragma unroll
+                    for (int jj = 0; jj < 2; jj++) {
+                        int v[16];
+                        tmem_ld16(ta + jj * kQNT, v);
+                        tmem_wait_ld();
+                        if (jj == 1) {
+                            tc_fence_before();
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(&acc_empty[buf]);
+                        }
+                        if (KIND == 4) {
+                            const int blk = 2 * u + jj;
+                            const int e = reinterpret_cast<const uint16_t *>(sc)[row * 8 + (kbs & 7) + blk];
+                            const int scv = e & 0xFF, mv = e >> 8;
+                            const int * bsb = bs + blk * kQNT + 16 * h;
+#pragma unroll
+                            for (int i = 0; i < 16; i++) {
+                                if (i >= live) break;
+                                isum[i] += scv * v[i];
+                                msum[i] += mv * bsb[i];
+                            }
+                        } else {
+                            const int scv = reinterpret_cast<const int8_t *>(sc)[row * 16 + ((2 * kbs) & 15) + 2 * u + jj];
+#pragma unroll
+                            for (int i = 0; i < 16; i++) {
+                                if (i >= live) break;
+                                isum[i] += scv * v[i];
+                            }
+                        }
+                    }
+                }
+                if (has && !give_up && ((kbs + kQKB) & 7) == 0) {  // end of a super-block: one float step, in order
+#pragma unroll
+                    for (int i = 0; i < 16; i++) {
+                        if (i >= live) break;
+                        const float dxv = dx[16 * h + i];
+                        acc[i] = fmaf(__fmul_rn(dxv, ddv.x), (float) isum[i], acc[i]);
+                        if (KIND == 4) acc[i] = fmaf(-__fmul_rn(dxv, ddv.y), (float) msum[i], acc[i]);
+                        isum[i] = 0;
+                        msum[i] = 0;
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[s]);  // the stage's scales are read: it may be refilled
+            }
+            if (give_up) break;
+            if (!has) continue;
+            const int64_t grow = (int64_t) tn * kQM + row;
+            if (grow < p.N)
+#pragma unroll
+                for (int i = 0; i < 16; i++) {
+                    if (i >= live) break;
+                    p.y[(int64_t) (m0 + 16 * h + i) * p.ldy + grow] = acc[i];
+                }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kQBufs * kQNT));
+    }
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------------------------------------------------------
+// Host: the expansion cache and the launcher
+// ------------------------------------------------------------------------------------------------------------------
+bool gemm_kq_tc_supported(const WeightView & w, int64_t M) {
+    return (w.type == B200_TYPE_Q4_K || w.type == B200_TYPE_Q6_K) && M >= 32 && w.K % 256 == 0 && w.K <= (int64_t) 1 << 29 &&
+           w.rows < ((int64_t) 1 << 31) && tensor_maps_available();
+}
+
+void kq_release(b200_context * ctx, const void * data) {
+    auto it = ctx->kq.find(data);
+    if (it == ctx->kq.end()) return;
+    cudaFreeAsync(it->second.mem, ctx->stream);  // stream-ordered: kernels already queued still read it
+    ctx->kq.erase(it);
+}
+
+void kq_release_all(b200_context * ctx) {
+    for (auto & e : ctx->kq) cudaFree(e.second.mem);
+    ctx->kq.clear();
+}
+
+// The expanded copy of w (created on first use, on the context stream).
+static cudaError_t kq_get(b200_context * ctx, const b200_weight * wt, KqExpansion ** out) {
+    auto it = ctx->kq.find(wt->data);
+    if (it != ctx->kq.end()) {
+        *out = &it->second;
+        return cudaSuccess;
+    }
+    const WeightView w = view_of(wt);
+    const int64_t rows = w.rows, K = w.K, nsb = K / 256;
+    auto up = [](size_t v) { return (v + 255) & ~(size_t) 255; };
+    const size_t qb = up((size_t) rows * K * (w.type == B200_TYPE_Q6_K ? 2 : 1));
+    const size_t sb = w.type == B200_TYPE_Q4_K ? up((size_t) rows * (K / 32) * 2) : 0;
+    const size_t db = up((size_t) rows * nsb * 16);
+    KqExpansion e;
+    e.type = w.type;
+    e.bytes = qb + sb + db;
+    cudaError_t err = cudaMallocAsync(&e.mem, e.bytes, ctx->stream);
+    if (err != cudaSuccess) return err;
+    uint8_t * m = (uint8_t *) e.mem;
+    e.q = (int8_t *) m;
+    e.scm = sb ? (uint16_t *) (m + qb) : nullptr;
+    e.dd = (float *) (m + qb + sb);
+    const int64_t work = rows * nsb;
+    int64_t blocks = (work + 7) / 8;
+    if (blocks > (int64_t) ctx->num_sms * 16) blocks = (int64_t) ctx->num_sms * 16;
+    if (w.type == B200_TYPE_Q4_K) expand_q4k_kernel<<<(unsigned) blocks, 256, 0, ctx->stream>>>(w, e.q, e.scm, (float4 *) e.dd);
+    else expand_q6k_kernel<<<(unsigned) blocks, 256, 0, ctx->stream>>>(w, e.q, (float4 *) e.dd);
+    err = cudaGetLastError();
+    if (err != cudaSuccess) {
+        cudaFreeAsync(e.mem, ctx->stream);
+        return err;
+    }
+    auto ins = ctx->kq.emplace(wt->data, e);
+    *out = &ins.first->second;
+    return cudaSuccess;
+}
+
+template <int KIND>
+static cudaError_t launch_kq(const WeightView & w, const KqExpansion & e, int64_t row0, int64_t N, const int8_t * q, const float * dxT,
+                             const int32_t * bsT, int64_t ld, int64_t M, float * y, int64_t ldy, unsigned * err, int num_sms, cudaStream_t st) {
+    using L = KqLayout<KIND>;
+    const int64_t K = w.K;
+    CUtensorMap ta, tb, tsc, tdd, tdx, tbs;
+    const uint64_t aK = (uint64_t) (KIND == 6 ? 2 * K : K);
+    bool ok = make_map_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, e.q, aK, (uint64_t) w.rows, aK, 128, kQM, CU_TENSOR_MAP_SWIZZLE_128B) &&
+              make_map_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, q, (uint64_t) K, (uint64_t) M, (uint64_t) K, 128, 16, CU_TENSOR_MAP_SWIZZLE_128B) &&
+              make_map_2d(&tdd, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, e.dd, (uint64_t) (4 * (K / 256)), (uint64_t) w.rows, (uint64_t) (K / 256) * 16, 4,
+                          kQM, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+              make_map_2d(&tdx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, dxT, (uint64_t) ld, (uint64_t) (K / 256), (uint64_t) ld * 4, kQNT, 1,
+                          CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (KIND == 4)
+        ok = ok && make_map_2d(&tsc, CU_TENSOR_MAP_DATA_TYPE_UINT16, e.scm, (uint64_t) (K / 32), (uint64_t) w.rows, (uint64_t) (K / 32) * 2, 8, kQM,
+                               CU_TENSOR_MAP_SWIZZLE_NONE) &&
+             make_map_2d(&tbs, CU_TENSOR_MAP_DATA_TYPE_INT32, bsT, (uint64_t) ld, (uint64_t) (K / 32), (uint64_t) ld * 4, kQNT, kQKB,
+                         CU_TENSOR_MAP_SWIZZLE_NONE);
+    else {
+        ok = ok && make_map_2d(&tsc, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.f2, (uint64_t) (K / 16), (uint64_t) w.rows, (uint64_t) (K / 16), 16, kQM,
+                               CU_TENSOR_MAP_SWIZZLE_NONE);
+        tbs = tdx;  // unused
+    }
+    if (!ok) return cudaErrorInvalidValue;
+    KqParams p;
+    p.N = N;
+    p.K = K;
+    p.row0 = row0;
+    p.M = (int) M;
+    p.tiles_m = (int) ((M + kQNT - 1) / kQNT);
+    p.tiles_n = (int) ((N + kQM - 1) / kQM);
+    p.y = y;
+    p.ldy = ldy;
+    p.err = err;
+    static int configured = 0;
+    if (!configured) {
+        cudaError_t e2 = cudaFuncSetAttribute(gemm_kq_tc_kernel<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
+        if (e2 != cudaSuccess) return e2;
+        configured = 1;
+    }
+    gemm_kq_tc_kernel<KIND><<<2 * num_sms, kQThreads, L::kTotal, st>>>(ta, tb, tsc, tdd, tdx, tbs, p);
+    return cudaGetLastError();
+}
+
+size_t gemm_kq_tc_act_bytes(int64_t K, int64_t M) {
+    const int64_t ld = (M + 15) & ~(int64_t) 15;
+    auto up = [](size_t v) { return (v + 255) & ~(size_t) 255; };
+    return up((size_t) M * K) + up((size_t) (K / 256) * ld * 4) + up((size_t) (K / 32) * ld * 4);
+}
+
+cudaError_t launch_gemm_kq_tc(b200_context * ctx, const b200_weight * wt, int64_t row0, int64_t N, const float * x, int64_t M, float * y,
+                              int64_t ldy, void * act) {
+    const WeightView w = view_of(wt);
+    if (!gemm_kq_tc_supported(w, M) || row0 + N > w.rows || ((uintptr_t) x & 15)) return cudaErrorInvalidValue;
+    KqExpansion * e = nullptr;
+    cudaError_t err = kq_get(ctx, wt, &e);
+    if (err != cudaSuccess) return err;
+    const int64_t K = w.K, ld = (M + 15) & ~(int64_t) 15;
+    auto up = [](size_t v) { return (v + 255) & ~(size_t) 255; };
+    uint8_t * a = (uint8_t *) act;
+    int8_t * q = (int8_t *) a;
+    float * dxT = (float *) (a + up((size_t) M * K));
+    int32_t * bsT = (int32_t *) (a + up((size_t) M * K) + up((size_t) (K / 256) * ld * 4));
+    int64_t blocks = (M * (K / 256) + 7) / 8;
+    if (blocks > (int64_t) ctx->num_sms * 8) blocks = (int64_t) ctx->num_sms * 8;
+    quantize_q8k_tc_kernel<<<(unsigned) blocks, 256, 0, ctx->stream>>>(x, K, M, q, dxT, bsT, ld);
+    err = cudaGetLastError();
+    if (err != cudaSuccess) return err;
+    if (w.type == B200_TYPE_Q4_K)
+        return launch_kq<4>(w, *e, row0, N, q, dxT, bsT, ld, M, y, ldy, ctx->dev_err, ctx->num_sms, ctx->stream);
+    return launch_kq<6>(w, *e, row0, N, q, dxT, bsT, ld, M, y, ldy, ctx->dev_err, ctx->num_sms, ctx->stream);
+}
+
+}  // namespace b200

@@ -5,6 +5,7 @@
 
 #include <cstring>
 #include <string>
+#include <unordered_map>
 
 #include "../../include/b200.h"
 #include "common.cuh"
@@ -14,6 +15,16 @@
 #define B200_DEVERR_ROWS 1u     // GET_ROWS id out of range
 #define B200_DEVERR_EXPERT 2u   // MUL_MAT_ID id out of range
 #define B200_DEVERR_TIMEOUT 4u  // a bounded wait gave up
+
+// A K-quant weight expanded to int8 for the tensor cores (gemm_kq_tc.cu): one device allocation.
+struct KqExpansion {
+    int type = 0;
+    void * mem = nullptr;
+    size_t bytes = 0;
+    int8_t * q = nullptr;      // Q4_K: [rows][K] 0..15; Q6_K: [rows][2K], zero-masked halves of q - 32
+    uint16_t * scm = nullptr;  // Q4_K: [rows][K/32] sc | m << 8
+    float * dd = nullptr;      // [rows][K/256][4]: d, dmin (Q4_K) or d (Q6_K)
+};
 
 struct b200_context {
     int device = 0;
@@ -31,6 +42,9 @@ struct b200_context {
     // The last kernel launched on the stream wrote weight bytes (an upload). A product launched with programmatic
     // dependent launch reads weights before griddepcontrol.wait, so it must not directly follow an upload.
     bool upload_pending = false;
+    // Expanded copies of K-quant weights used with many activation rows, by weight data pointer; dropped when the
+    // weight is written or freed.
+    std::unordered_map<const void *, KqExpansion> kq;
 };
 
 namespace b200 {
@@ -73,6 +87,14 @@ cudaError_t launch_gemm_tc_grouped(const WeightView & w, int64_t N, const int4 *
 // A dense Q8_0 product on the same kernel: q int8 [M][K] in token order, dT [K/32][ldP] (ldP % 16 == 0, >= M).
 cudaError_t launch_gemm_tc_dense(const WeightView & w, int64_t row0, int64_t N, const int8_t * q, const float * dT, int64_t ldP,
                                  int64_t M, float * y, int64_t ldy, unsigned * err, int num_sms, cudaStream_t st);
+// K-quant (Q4_K, Q6_K) products with M >= 32 on the tensor cores (gemm_kq_tc.cu). act: scratch of
+// gemm_kq_tc_act_bytes(K, M) bytes (quantized activations).
+bool gemm_kq_tc_supported(const WeightView & w, int64_t M);
+size_t gemm_kq_tc_act_bytes(int64_t K, int64_t M);
+cudaError_t launch_gemm_kq_tc(b200_context * ctx, const b200_weight * w, int64_t row0, int64_t N, const float * x, int64_t M, float * y,
+                              int64_t ldy, void * act);
+void kq_release(b200_context * ctx, const void * data);
+void kq_release_all(b200_context * ctx);
 int64_t moe_max_slots(int64_t P, int64_t E);
 int64_t moe_max_tiles(int64_t P, int64_t E);
 cudaError_t launch_moe_route(const int32_t * ids, int64_t T, int64_t top_k, int64_t nb1, int64_t E, int64_t e0, int64_t total,
