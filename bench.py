@@ -355,7 +355,8 @@ def config4_batched(pkg, ctx, stream, reps=10):
 def config3_prefill(pkg, ctx, stream, reps=2):
     """Config 3's prefill: the Qwen3-ASR 1.7B-shaped decoder's products (28 x {q|k|v 2048->4096, o 2048->2048,
     gate|up 2048->12288 Q4_K; down 6144->2048 Q6_K}) for M = 1500 rows (the head runs on the last row only: one
-    2048 -> 151936 Q6_K product, M = 1). K-quant products with many rows run on the GEMV kernels in column chunks."""
+    2048 -> 151936 Q6_K product, M = 1). K-quant products with many rows run on the int8 tensor cores over an
+    int8 expansion of the weights made on the first product (the untimed warm-up pass)."""
     layers = _product_stack(pkg, ctx, [(pkg.Q4_K, 2048, 4096), (pkg.Q4_K, 2048, 2048), (pkg.Q4_K, 2048, 12288),
                                        (pkg.Q6_K, 6144, 2048)], 28, 43)
     head = _product_stack(pkg, ctx, [(pkg.Q6_K, 2048, 151936)], 1, 44)
@@ -368,7 +369,7 @@ def config3_prefill(pkg, ctx, stream, reps=2):
     total = ms + ms_head
     return {"M": 1500, "ms": total, "rows_per_s": 1500 * 1000.0 / total, "weight_bytes": nbytes + head_bytes,
             "gbs": (nbytes + head_bytes) / total / 1e6, "int8_tops": ops / total / 1e9,
-            "path": "GEMV kernels in 16-column chunks (no K-quant tensor-core path yet)"}
+            "path": "int8 tensor cores (gemm_kq_tc_kernel) over the cached int8 expansion of the K-quant weights"}
 
 
 def config3_decode(pkg, ctx, stream, steps=128):
@@ -749,6 +750,36 @@ def run_batched(args, pkg, ctx, dist, world, rank, local):
     }
 
 
+def run_prefill(args, pkg, ctx, dist, world, rank, local):
+    """Config 3's prefill as its own line: M = 1500 rows through the Qwen3-ASR 1.7B-shaped product stack (Q4_K / Q6_K)
+    plus the head on the last row. Single stream per GPU: with N > 1, N independent replicas."""
+    import torch
+
+    stream = ctx.torch_stream()
+    if dist:
+        dist.barrier()
+    with Clocks(local) as clk:
+        r = config3_prefill(pkg, ctx, stream, reps=max(2, args.moe_steps // 5))
+    ms = r["ms"]
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    peak, peak_kind = peaks()
+    return {
+        "metric": "prefill rows/s, Qwen3-ASR 1.7B-shaped decoder products (Q4_K / Q6_K), M = 1500", "value": world * 1500 * 1000.0 / ms,
+        "unit": "rows/s", "n_gpus": world, "steps": max(2, args.moe_steps // 5), "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "dtype": "int8xint8->int32, f32 accumulate", "data": "synthetic",
+        "config": {"workload": "config 3 prefill: 28 x {q|k|v 2048->4096, o 2048->2048, gate|up 2048->12288 Q4_K, down 6144->2048 Q6_K}"
+                               " x 1500 rows + head 2048->151936 Q6_K x 1 row", "global_batch": 1500 * world,
+                   "parallelism": f"replicas x{world}" if world > 1 else "single"},
+        "roofline": {"bound": "tensor", "kernel": "gemm_kq_tc_kernel", "achieved": r["int8_tops"], "unit": "TOP/s int8",
+                     "peak": 4500.0, "frac": r["int8_tops"] / 4500.0, "peak_source": "nominal dense int8 (not measured on this pool)",
+                     "traffic": None},
+        "clocks": clk.summary(), "gpu_launches": (28 * 4 * 2 + 1) * max(2, args.moe_steps // 5),
+    }
+
+
 def run_b200(args):
     import torch
 
@@ -770,8 +801,8 @@ def run_b200(args):
 
     pkg = load_package()
     ctx = pkg.Context(local)
-    if args.workload in ("moe", "batched"):
-        res = (run_moe if args.workload == "moe" else run_batched)(args, pkg, ctx, dist, world, rank, local)
+    if args.workload in ("moe", "batched", "prefill"):
+        res = {"moe": run_moe, "batched": run_batched, "prefill": run_prefill}[args.workload](args, pkg, ctx, dist, world, rank, local)
         ctx.close()
         if dist:
             dist.barrier()
@@ -921,9 +952,9 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-configs", action="store_true", help="skip the config 1 and config 3 side measurements")
-    ap.add_argument("--workload", default="decode", choices=["decode", "moe", "batched"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "moe", "batched", "prefill"],
                     help="decode: config 2 decode step (the headline line); moe: config 5 MoE FFN stack, expert-parallel; "
-                         "batched: config 4 product stack, column-split")
+                         "batched: config 4 product stack, column-split; prefill: config 3 prefill")
     ap.add_argument("--moe-steps", type=int, default=20, help="timed steps of the MoE and batched workloads")
     ap.add_argument("--moe-layers", type=int, default=48, help="MoE layers per step (48 = config 5; fewer only for profiling)")
     args = ap.parse_args()
