@@ -81,7 +81,6 @@ __global__ void __launch_bounds__(kGThreads, 2)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nstage = (int) (p.K / 32 / kGKB);
-    const int items = (p.tiles ? *p.ntiles : (p.dense_m + 31) / 32) * p.tiles_n;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kGStages; s++) {
@@ -103,6 +102,11 @@ __global__ void __launch_bounds__(kGThreads, 2)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // Set-up above overlaps the previous kernel under programmatic dependent launch; the tile list, the activations
+    // and the outputs' previous readers come from kernels before this one.
+    pdl_wait();
+    pdl_launch_dependents();
+    const int items = (p.tiles ? *p.ntiles : (p.dense_m + 31) / 32) * p.tiles_n;
 
     if (warp == 0) {
         // ---- TMA producer ----
@@ -306,8 +310,17 @@ cudaError_t launch_grouped(const WeightView & w, int64_t N, int64_t row0, int de
         if (e != cudaSuccess) return e;
         configured = 1;
     }
-    gemm_q8_0_tc_grouped_kernel<<<2 * num_sms, kGThreads, L::kTotal, st>>>(ta, tb, tdw, tdx, p);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned) (2 * num_sms), 1, 1);
+    cfg.blockDim = dim3(kGThreads, 1, 1);
+    cfg.dynamicSmemBytes = L::kTotal;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gemm_q8_0_tc_grouped_kernel, ta, tb, tdw, tdx, p);
 }
 
 }  // namespace

@@ -13,6 +13,8 @@ namespace b200 {
 __global__ void moe_route_kernel(const int32_t * __restrict__ ids, int64_t P, int64_t top_k, int64_t nb1, int E, int e0, int total,
                                  int32_t * grp_off, int32_t * col_src, int32_t * col_dst, int32_t * inv, int4 * tiles, int * ntiles,
                                  unsigned * err) {
+    pdl_wait();  // launched with programmatic dependent launch: the previous kernel's writes are visible after this
+    pdl_launch_dependents();
     extern __shared__ int sh[];
     int * cnt = sh;            // [E] pairs
     int * pos = sh + E;        // [E] placement cursor
@@ -89,6 +91,8 @@ __global__ void moe_route_kernel(const int32_t * __restrict__ ids, int64_t P, in
 template <int U>
 __global__ void moe_quant_slots_kernel(const float * __restrict__ x, int64_t K, int64_t ldx, int vec, const int32_t * __restrict__ col_src,
                                        const int32_t * __restrict__ n_slots, int8_t * q, float * dT, int64_t ldP) {
+    pdl_wait();
+    pdl_launch_dependents();
     const int lane = threadIdx.x & 31;
     const int warps = gridDim.x * (blockDim.x >> 5);
     const int S = *n_slots;
@@ -123,6 +127,8 @@ __global__ void moe_quant_slots_kernel(const float * __restrict__ x, int64_t K, 
 template <int U>
 __global__ void moe_swiglu_slots_kernel(const float * __restrict__ gu, int64_t F, const int32_t * __restrict__ col_src,
                                         const int32_t * __restrict__ n_slots, int8_t * q, float * dT, int64_t ldP) {
+    pdl_wait();
+    pdl_launch_dependents();
     const int lane = threadIdx.x & 31;
     const int warps = gridDim.x * (blockDim.x >> 5);
     const int S = *n_slots;
@@ -161,6 +167,8 @@ __global__ void moe_swiglu_slots_kernel(const float * __restrict__ gu, int64_t F
 // vec: out allows 16-byte stores and H % 4 == 0.
 __global__ void moe_combine_slots_kernel(const float * __restrict__ down, const float * __restrict__ w, const int32_t * __restrict__ inv,
                                          int64_t top_k, int64_t H, int vec, float * __restrict__ out) {
+    pdl_wait();
+    pdl_launch_dependents();
     extern __shared__ int cslot[];  // [top_k] slots, then [top_k] weights
     float * cw = reinterpret_cast<float *>(cslot + top_k);
     const int64_t t = blockIdx.x;
@@ -209,16 +217,31 @@ __global__ void moe_combine_slots_kernel(const float * __restrict__ down, const 
     }
 }
 
+// Launches a kernel with programmatic dependent launch (its CTAs may start while the previous kernel finishes; every
+// kernel here calls griddepcontrol.wait before reading anything a previous kernel wrote).
+template <class... Params, class... Args>
+static cudaError_t launch_pdl(void (*kern)(Params...), unsigned grid, unsigned block, size_t smem, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(block, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<Params>(args)...);
+}
+
 int64_t moe_max_slots(int64_t P, int64_t E) { return ((P + 15 * E) + 15) & ~(int64_t) 15; }
 int64_t moe_max_tiles(int64_t P, int64_t E) { return moe_max_slots(P, E) / 16 + E + 1; }
 
 cudaError_t launch_moe_route(const int32_t * ids, int64_t T, int64_t top_k, int64_t nb1, int64_t E, int64_t e0, int64_t total,
                              int32_t * grp_off, int32_t * col_src, int32_t * col_dst, int32_t * inv, int4 * tiles, int * ntiles,
                              unsigned * err, cudaStream_t st) {
-    moe_route_kernel<<<1, 1024, (size_t) 4 * E * sizeof(int), st>>>(ids, T * top_k, top_k, nb1, (int) E, (int) e0,
-                                                                    (int) (total > 0 ? total : E), grp_off, col_src, col_dst, inv,
-                                                                    tiles, ntiles, err);
-    return cudaGetLastError();
+    return launch_pdl(moe_route_kernel, 1, 1024, (size_t) 4 * E * sizeof(int), st, ids, T * top_k, top_k, nb1, (int) E, (int) e0,
+                      (int) (total > 0 ? total : E), grp_off, col_src, col_dst, inv, tiles, ntiles, err);
 }
 
 static unsigned glue_blocks(int64_t work_warps, int num_sms) {
@@ -232,22 +255,19 @@ static unsigned glue_blocks(int64_t work_warps, int num_sms) {
 cudaError_t launch_moe_quant_slots(const float * x, int64_t K, int64_t ldx, const int32_t * col_src, const int32_t * n_slots,
                                    int64_t max_slots, int8_t * q, float * dT, int64_t ldP, int num_sms, cudaStream_t st) {
     const int vec = ((uintptr_t) x % 16 == 0 && ldx % 4 == 0) ? 1 : 0;
-    moe_quant_slots_kernel<8><<<glue_blocks(max_slots, num_sms), 256, 0, st>>>(x, K, ldx, vec, col_src, n_slots, q, dT, ldP);
-    return cudaGetLastError();
+    return launch_pdl(moe_quant_slots_kernel<8>, glue_blocks(max_slots, num_sms), 256, 0, st, x, K, ldx, vec, col_src, n_slots, q, dT, ldP);
 }
 
 cudaError_t launch_moe_swiglu_slots(const float * gu, int64_t F, const int32_t * col_src, const int32_t * n_slots, int64_t max_slots,
                                     int8_t * q, float * dT, int64_t ldP, int num_sms, cudaStream_t st) {
-    moe_swiglu_slots_kernel<4><<<glue_blocks(max_slots, num_sms), 256, 0, st>>>(gu, F, col_src, n_slots, q, dT, ldP);
-    return cudaGetLastError();
+    return launch_pdl(moe_swiglu_slots_kernel<4>, glue_blocks(max_slots, num_sms), 256, 0, st, gu, F, col_src, n_slots, q, dT, ldP);
 }
 
 cudaError_t launch_moe_combine_slots(const float * down, const float * w, const int32_t * inv, int64_t T, int64_t top_k, int64_t H,
                                      float * out, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
     const int vec = ((uintptr_t) out % 16 == 0 && H % 4 == 0) ? 1 : 0;
-    moe_combine_slots_kernel<<<(unsigned) T, 256, (size_t) top_k * 8, st>>>(down, w, inv, top_k, H, vec, out);
-    return cudaGetLastError();
+    return launch_pdl(moe_combine_slots_kernel, (unsigned) T, 256, (size_t) top_k * 8, st, down, w, inv, top_k, H, vec, out);
 }
 
 }  // namespace b200
