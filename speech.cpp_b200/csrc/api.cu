@@ -159,18 +159,32 @@ b200_status mul_mat_impl(b200_context * ctx, const b200_weight * w, int64_t row0
     }
     // Many columns of Q8_0: int8 tensor cores (tcgen05) over the once-quantized activations: the persistent tile
     // kernel (32-token tiles x 128-row weight tiles, eight K blocks in flight) or the split-K GEMM.
-    // Used for up to 128 rows with at least 48 (token tile x 128-row tile) items; fewer items (long K, few rows) or
+    // Up to 128 rows: the persistent tile kernel, with K split across CTAs when there are few (token x row) tiles;
     // more rows run faster on the split-K GEMM below (measured on B200).
-    const int64_t tile_items = ((M + 31) / 32) * ((n + 127) / 128);
-    if (M >= 32 && M <= 128 && tile_items >= 48 && gemm_tc_grouped_supported(p.w)) {
+    if (M >= 32 && M <= 128 && gemm_tc_grouped_supported(p.w)) {
         const int64_t ld = (M + 15) & ~(int64_t) 15;
-        b200_status s = ensure_scratch(ctx, quantized_act_bytes(B200_TYPE_Q8_0, K, ld) + 512);
+        const int ks = gemm_tc_dense_splits(p.w, n, M, ctx->num_sms);
+        const size_t wsb = gemm_tc_dense_ws_bytes(n, M, ks);
+        const int64_t out_tiles = ((M + 31) / 32) * ((n + 127) / 128);
+        b200_status s = ensure_scratch(ctx, quantized_act_bytes(B200_TYPE_Q8_0, K, ld) + wsb + 1024);
         if (s != B200_OK) return s;
+        if (ks > 1 && (size_t) out_tiles > ctx->ntickets) {
+            CK(ctx, cudaStreamSynchronize(ctx->stream));
+            if (ctx->tickets) cudaFree(ctx->tickets);
+            ctx->tickets = nullptr;
+            ctx->ntickets = 0;
+            const size_t nt = (size_t) out_tiles < 4096 ? 4096 : (size_t) out_tiles;
+            CK(ctx, cudaMalloc(&ctx->tickets, nt * sizeof(unsigned)));
+            CK(ctx, cudaMemset(ctx->tickets, 0, nt * sizeof(unsigned)));
+            ctx->ntickets = nt;
+        }
         Carve c{(uint8_t *) ctx->scratch};
         int8_t * q = c.take<int8_t>((size_t) M * K);
         float * d = c.take<float>((size_t) ld * (K / 32));
+        float * ws = ks > 1 ? c.take<float>(wsb / 4) : nullptr;
         CK(ctx, launch_quantize(kind, x, K, M, nullptr, q, d, nullptr, ctx->stream, ld));
-        const cudaError_t e = launch_gemm_tc_dense(p.w, row0, n, q, d, ld, M, dst, ld_dst, ctx->dev_err, ctx->num_sms, ctx->stream);
+        const cudaError_t e = launch_gemm_tc_dense(p.w, row0, n, q, d, ld, M, dst, ld_dst, ctx->dev_err, ctx->num_sms, ctx->stream, ks, ws,
+                                                   ctx->tickets);
         if (e == cudaSuccess) return B200_OK;
         if (e != cudaErrorInvalidValue) return cuda_fail(ctx, e, "launch_gemm_tc_dense");
         // a tensor map the driver refused: the paths below compute the same product

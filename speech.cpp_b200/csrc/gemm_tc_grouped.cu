@@ -51,6 +51,9 @@ struct GroupedParams {
     const int4 * tiles;       // {expert, first slot, slots (16 or 32), routed slots (the rest is padding)}
     const int * ntiles;       // number of tiles (device)
     int tiles_n;              // 128-row tiles per expert
+    int ksplit;               // dense products: K ranges per output tile (partials summed in split order), else 1
+    float * ws;               // split partial tiles [output tile][split][kGNT][kGM]
+    unsigned * tickets;       // one per output tile, zero between launches
     const int32_t * row_map;  // output row of each slot (< 0: none); null: the slot itself
     float * y;
     int64_t ldy;
@@ -76,7 +79,9 @@ __global__ void __launch_bounds__(kGThreads, 2)
     uint64_t * empty = bars + kGStages;
     uint64_t * acc_full = bars + 2 * kGStages;   // [bufs] a block pair's int32 sums ready in tensor memory
     uint64_t * acc_empty = acc_full + kGBufs;    // [bufs] epilogue has read them
-    uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + kGBufs);
+    uint64_t * xbar = acc_empty + kGBufs;        // [2] split-K: every epilogue warp stored its partial / ticket taken
+    uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(xbar + 2);
+    __shared__ int last_split;
     __shared__ volatile int give_up;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -91,6 +96,8 @@ __global__ void __launch_bounds__(kGThreads, 2)
             mbar_init(&acc_full[b], 1);
             mbar_init(&acc_empty[b], kGEpiWarps);
         }
+        mbar_init(&xbar[0], kGEpiWarps);
+        mbar_init(&xbar[1], 1);
         fence_mbar_init();
         give_up = 0;
     }
@@ -106,18 +113,21 @@ __global__ void __launch_bounds__(kGThreads, 2)
     // and the outputs' previous readers come from kernels before this one.
     pdl_wait();
     pdl_launch_dependents();
-    const int items = (p.tiles ? *p.ntiles : (p.dense_m + 31) / 32) * p.tiles_n;
+    // item = (output tile, K split), the split fastest: the splits of one tile run at the same time on different CTAs
+    const int items = (p.tiles ? *p.ntiles : (p.dense_m + 31) / 32) * p.tiles_n * p.ksplit;
+    const int spl = nstage / p.ksplit;  // stages per split
 
     if (warp == 0) {
         // ---- TMA producer ----
         if (lane == 0) {
             int sg = 0;
             for (int it = blockIdx.x; it < items && !give_up; it += gridDim.x) {
-                const int4 t = g_tile(p, it / p.tiles_n);
-                const int arow = (int) ((int64_t) t.x * p.N + p.row0 + (int64_t) (it % p.tiles_n) * kGM);
+                const int ot = it / p.ksplit, ks = it % p.ksplit;
+                const int4 t = g_tile(p, ot / p.tiles_n);
+                const int arow = (int) ((int64_t) t.x * p.N + p.row0 + (int64_t) (ot % p.tiles_n) * kGM);
                 const int nsub = t.z / 16;
                 const uint32_t bytes = (uint32_t) (L::kA + t.z * 256 + L::kDw + L::kDx);
-                for (int st = 0; st < nstage; st++, sg++) {
+                for (int st = ks * spl; st < (ks + 1) * spl; st++, sg++) {
                     const int s = sg % kGStages, use = sg / kGStages;
                     if (use > 0 && !mbar_wait_sleep(&empty[s], (use - 1) & 1)) {
                         atomicOr(p.err, kErrTimeout);
@@ -143,9 +153,9 @@ __global__ void __launch_bounds__(kGThreads, 2)
         if (lane == 0) {
             int sg = 0, g2 = 0;
             for (int it = blockIdx.x; it < items && !give_up; it += gridDim.x) {
-                const int4 t = g_tile(p, it / p.tiles_n);
+                const int4 t = g_tile(p, it / p.ksplit / p.tiles_n);
                 const uint32_t idesc = idesc_i8_n(t.z);
-                for (int st = 0; st < nstage && !give_up; st++, sg++) {
+                for (int st = 0; st < spl && !give_up; st++, sg++) {
                     const int s = sg % kGStages;
                     if (!mbar_wait_sleep(&full[s], (sg / kGStages) & 1)) {
                         atomicOr(p.err, kErrTimeout);
@@ -181,16 +191,17 @@ __global__ void __launch_bounds__(kGThreads, 2)
         const int q = warp & 3, h = (warp - 2) >> 2;
         const int row = 32 * q + lane;
         const float2 neg_magic = make_float2(-12582912.0f, -12582912.0f);
-        int sg = 0, g2 = 0;
+        int sg = 0, g2 = 0, xi = 0;
         for (int it = blockIdx.x; it < items && !give_up; it += gridDim.x) {
-            const int4 t = g_tile(p, it / p.tiles_n);
-            const int tn = it % p.tiles_n;
+            const int ot = it / p.ksplit, ks = it % p.ksplit;
+            const int4 t = g_tile(p, ot / p.tiles_n);
+            const int tn = ot % p.tiles_n;
             const bool has = h < t.z / 16;
             const int live = t.w - 16 * h;  // routed slots in this warp's chunk (the rest is padding: no math)
             float2 acc[8];
 #pragma unroll
             for (int i = 0; i < 8; i++) acc[i] = make_float2(0.0f, 0.0f);
-            for (int st = 0; st < nstage && !give_up; st++, sg++) {
+            for (int st = 0; st < spl && !give_up; st++, sg++) {
                 const int s = sg % kGStages;
                 const uint8_t * base = smem + s * L::kStage;
                 const __half2 * dw2 = reinterpret_cast<const __half2 *>(base + L::kA + L::kB) + row * (kGKB / 2);
@@ -245,9 +256,46 @@ __global__ void __launch_bounds__(kGThreads, 2)
                 if (lane == 0) mbar_arrive(&empty[s]);
             }
             if (give_up) break;
+            const int64_t grow = (int64_t) tn * kGM + row;
+            if (p.ksplit > 1) {
+                // ---- split K: store this split's partial tile; the last split of the tile (an atomic ticket) adds
+                // the partials in split order, so the result does not depend on timing. Every epilogue warp takes
+                // part (bounded mbarrier waits, no unbounded named barrier) ----
+                float * part = p.ws + ((int64_t) ot * p.ksplit + ks) * kGNT * kGM;
+                if (has)
+#pragma unroll
+                    for (int i = 0; i < 16; i++) part[(16 * h + i) * kGM + row] = (i & 1) ? acc[i / 2].y : acc[i / 2].x;
+                __threadfence();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&xbar[0]);
+                if (warp == 2 && lane == 0) {
+                    if (!mbar_wait_sleep(&xbar[0], xi & 1)) {
+                        atomicOr(p.err, kErrTimeout);
+                        give_up = 1;
+                    }
+                    const unsigned ticket = atomicAdd(&p.tickets[ot], 1u);
+                    last_split = ticket == (unsigned) (p.ksplit - 1);
+                    if (last_split) p.tickets[ot] = 0u;  // ready for the next launch
+                    mbar_arrive(&xbar[1]);
+                }
+                if (!mbar_wait_sleep(&xbar[1], xi & 1)) {
+                    if (lane == 0) atomicOr(p.err, kErrTimeout);
+                    give_up = 1;
+                }
+                xi++;
+                if (give_up || !last_split || !has || grow >= p.N) continue;
+                __threadfence();
+                const float * parts = p.ws + (int64_t) ot * p.ksplit * kGNT * kGM;
+                for (int i = 0; i < 16; i++) {
+                    if (i >= live) break;
+                    float sum = 0.0f;
+                    for (int z = 0; z < p.ksplit; z++) sum += __ldcg(parts + ((int64_t) z * kGNT + 16 * h + i) * kGM + row);
+                    p.y[(int64_t) (t.y + 16 * h + i) * p.ldy + grow] = sum;
+                }
+                continue;
+            }
             if (!has) continue;
             // ---- output: one weight row per lane, so each slot's store is one coalesced 128-byte line ----
-            const int64_t grow = (int64_t) tn * kGM + row;
             if (grow < p.N) {
 #pragma unroll
                 for (int i = 0; i < 16; i++) {
@@ -279,7 +327,8 @@ namespace {
 
 cudaError_t launch_grouped(const WeightView & w, int64_t N, int64_t row0, int dense_m, const int4 * tiles, const int * ntiles,
                            const int8_t * q, const float * dT, int64_t ldP, int64_t slots, const int32_t * row_map, float * y,
-                           int64_t ldy, unsigned * err, int num_sms, cudaStream_t st) {
+                           int64_t ldy, unsigned * err, int num_sms, cudaStream_t st, int ksplit = 1, float * ws = nullptr,
+                           unsigned * tickets = nullptr) {
     using L = GLayout;
     const int64_t K = w.K, KB = K / 32;
     if (!gemm_tc_grouped_supported(w) || ldP % 16 || slots > ldP || slots < 1) return cudaErrorInvalidValue;
@@ -300,6 +349,9 @@ cudaError_t launch_grouped(const WeightView & w, int64_t N, int64_t row0, int de
     p.tiles = tiles;
     p.ntiles = ntiles;
     p.tiles_n = (int) ((N + kGM - 1) / kGM);
+    p.ksplit = ksplit;
+    p.ws = ws;
+    p.tickets = tickets;
     p.row_map = row_map;
     p.y = y;
     p.ldy = ldy;
@@ -332,10 +384,24 @@ cudaError_t launch_gemm_tc_grouped(const WeightView & w, int64_t N, const int4 *
     return launch_grouped(w, N, 0, 0, tiles, ntiles, q, dT, ldP, slots, row_map, y, ldy, err, num_sms, st);
 }
 
+int gemm_tc_dense_splits(const WeightView & w, int64_t N, int64_t M, int num_sms) {
+    const int64_t tiles = ((M + 31) / 32) * ((N + kGM - 1) / kGM);
+    const int nstage = (int) (w.K / 32 / kGKB);
+    int ks = 1;
+    while (ks * 2 <= 8 && tiles * ks * 2 <= 2 * (int64_t) num_sms && nstage % (ks * 2) == 0) ks *= 2;
+    return ks;
+}
+
+size_t gemm_tc_dense_ws_bytes(int64_t N, int64_t M, int ksplit) {
+    return ksplit > 1 ? (size_t) ((M + 31) / 32) * ((N + kGM - 1) / kGM) * ksplit * kGNT * kGM * 4 : 0;
+}
+
 cudaError_t launch_gemm_tc_dense(const WeightView & w, int64_t row0, int64_t N, const int8_t * q, const float * dT, int64_t ldP,
-                                 int64_t M, float * y, int64_t ldy, unsigned * err, int num_sms, cudaStream_t st) {
-    if (M < 1 || M > (1 << 30) || row0 + N > w.rows) return cudaErrorInvalidValue;
-    return launch_grouped(w, N, row0, (int) M, nullptr, nullptr, q, dT, ldP, M, nullptr, y, ldy, err, num_sms, st);
+                                 int64_t M, float * y, int64_t ldy, unsigned * err, int num_sms, cudaStream_t st, int ksplit, float * ws,
+                                 unsigned * tickets) {
+    if (M < 1 || M > (1 << 30) || row0 + N > w.rows || ksplit < 1 || (w.K / 32 / kGKB) % ksplit || (ksplit > 1 && (!ws || !tickets)))
+        return cudaErrorInvalidValue;
+    return launch_grouped(w, N, row0, (int) M, nullptr, nullptr, q, dT, ldP, M, nullptr, y, ldy, err, num_sms, st, ksplit, ws, tickets);
 }
 
 }  // namespace b200

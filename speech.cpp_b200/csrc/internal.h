@@ -85,8 +85,12 @@ cudaError_t launch_gemm_tc_grouped(const WeightView & w, int64_t N, const int4 *
                                    const float * dT, int64_t ldP, int64_t slots, const int32_t * row_map, float * y, int64_t ldy,
                                    unsigned * err, int num_sms, cudaStream_t st);
 // A dense Q8_0 product on the same kernel: q int8 [M][K] in token order, dT [K/32][ldP] (ldP % 16 == 0, >= M).
+// Split-K (ksplit > 1): partial tiles in ws (gemm_tc_dense_ws_bytes) and one zeroed ticket per output tile.
+int gemm_tc_dense_splits(const WeightView & w, int64_t N, int64_t M, int num_sms);
+size_t gemm_tc_dense_ws_bytes(int64_t N, int64_t M, int ksplit);
 cudaError_t launch_gemm_tc_dense(const WeightView & w, int64_t row0, int64_t N, const int8_t * q, const float * dT, int64_t ldP,
-                                 int64_t M, float * y, int64_t ldy, unsigned * err, int num_sms, cudaStream_t st);
+                                 int64_t M, float * y, int64_t ldy, unsigned * err, int num_sms, cudaStream_t st, int ksplit = 1,
+                                 float * ws = nullptr, unsigned * tickets = nullptr);
 // K-quant (Q4_K, Q6_K) products with M >= 32 on the tensor cores (gemm_kq_tc.cu). act: scratch of
 // gemm_kq_tc_act_bytes(K, M) bytes (quantized activations).
 bool gemm_kq_tc_supported(const WeightView & w, int64_t M);
