@@ -120,6 +120,10 @@ __global__ void __launch_bounds__(kGThreads, 2)
     if (warp == 0) {
         // ---- TMA producer ----
         if (lane == 0) {
+            prefetch_tensormap(&tmA);
+            prefetch_tensormap(&tmB);
+            prefetch_tensormap(&tmDw);
+            prefetch_tensormap(&tmDx);
             int sg = 0;
             for (int it = blockIdx.x; it < items && !give_up; it += gridDim.x) {
                 const int ot = it / p.ksplit, ks = it % p.ksplit;
@@ -127,6 +131,10 @@ __global__ void __launch_bounds__(kGThreads, 2)
                 const int arow = (int) ((int64_t) t.x * p.N + p.row0 + (int64_t) (ot % p.tiles_n) * kGM);
                 const int nsub = t.z / 16;
                 const uint32_t bytes = (uint32_t) (L::kA + t.z * 256 + L::kDw + L::kDx);
+                // the item's weight tiles beyond the first two stages: into L2 now, so their loads below do not wait
+                // on HBM
+                for (int st = ks * spl + kGStages; st < (ks + 1) * spl; st++)
+                    for (int jj = 0; jj < 2; jj++) prefetch_l2_2d(&tmA, (st * kGKB + 4 * jj) * 32, arow);
                 for (int st = ks * spl; st < (ks + 1) * spl; st++, sg++) {
                     const int s = sg % kGStages, use = sg / kGStages;
                     if (use > 0 && !mbar_wait_sleep(&empty[s], (use - 1) & 1)) {
@@ -285,13 +293,22 @@ __global__ void __launch_bounds__(kGThreads, 2)
                 xi++;
                 if (give_up || !last_split || !has || grow >= p.N) continue;
                 __threadfence();
-                const float * parts = p.ws + (int64_t) ot * p.ksplit * kGNT * kGM;
-                for (int i = 0; i < 16; i++) {
-                    if (i >= live) break;
-                    float sum = 0.0f;
-                    for (int z = 0; z < p.ksplit; z++) sum += __ldcg(parts + ((int64_t) z * kGNT + 16 * h + i) * kGM + row);
-                    p.y[(int64_t) (t.y + 16 * h + i) * p.ldy + grow] = sum;
+                // partials summed in split order; each split's 16 values are read together (one L2 round trip per
+                // split, not per value)
+                const float * parts = p.ws + (int64_t) ot * p.ksplit * kGNT * kGM + (int64_t) (16 * h) * kGM + row;
+                float sum[16];
+#pragma unroll
+                for (int i = 0; i < 16; i++) sum[i] = 0.0f;
+                for (int z = 0; z < p.ksplit; z++) {
+                    float v[16];
+#pragma unroll
+                    for (int i = 0; i < 16; i++) v[i] = __ldcg(parts + ((int64_t) z * kGNT + i) * kGM);
+#pragma unroll
+                    for (int i = 0; i < 16; i++) sum[i] += v[i];
                 }
+#pragma unroll
+                for (int i = 0; i < 16; i++)
+                    if (i < live) p.y[(int64_t) (t.y + 16 * h + i) * p.ldy + grow] = sum[i];
                 continue;
             }
             if (!has) continue;

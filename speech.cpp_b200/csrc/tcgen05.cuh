@@ -74,6 +74,16 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, int * r) {
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// Fetches a tensor map's descriptor ahead of its first use (a __grid_constant__ kernel parameter).
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap * m) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
+}
+
+// Asks L2 to fetch a 2-D tile ahead of its TMA load (no shared-memory destination, no multicast).
+__device__ __forceinline__ void prefetch_l2_2d(const CUtensorMap * map, int c0, int c1) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(map), "r"(c0), "r"(c1) : "memory");
+}
+
 // Host: a 2-D tensor map (inner extent, outer extent, row pitch in bytes, box), cached by its arguments. False when
 // the driver entry point is missing or refuses the map (base not 16-byte aligned, pitch not a multiple of 16, ...).
 bool make_map_2d(CUtensorMap * m, CUtensorMapDataType dt, const void * base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
