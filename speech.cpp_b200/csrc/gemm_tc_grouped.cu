@@ -131,10 +131,6 @@ __global__ void __launch_bounds__(kGThreads, 2)
                 const int arow = (int) ((int64_t) t.x * p.N + p.row0 + (int64_t) (ot % p.tiles_n) * kGM);
                 const int nsub = t.z / 16;
                 const uint32_t bytes = (uint32_t) (L::kA + t.z * 256 + L::kDw + L::kDx);
-                // the item's weight tiles beyond the first two stages: into L2 now, so their loads below do not wait
-                // on HBM
-                for (int st = ks * spl + kGStages; st < (ks + 1) * spl; st++)
-                    for (int jj = 0; jj < 2; jj++) prefetch_l2_2d(&tmA, (st * kGKB + 4 * jj) * 32, arow);
                 for (int st = ks * spl; st < (ks + 1) * spl; st++, sg++) {
                     const int s = sg % kGStages, use = sg / kGStages;
                     if (use > 0 && !mbar_wait_sleep(&empty[s], (use - 1) & 1)) {
