@@ -146,6 +146,26 @@ b200_status b200_moe_ffn(b200_context * ctx, const b200_weight * gate_up, const 
                          int64_t n_expert_total, const float * x, const int32_t * ids, const float * w, int64_t top_k, int64_t T,
                          float * out);
 
+/* Expert parallelism over NVLink peer memory: the combine step of b200_moe_ffn fused with a two-shot all-reduce.
+ * The reference runs a layer's routed experts on one device (src/families/drama3/text-model.cpp:198-221); this is its
+ * multi-GPU extension. Every rank of a group of `world` (<= 8) GPUs allocates a mailbox and shares its IPC handle
+ * (64 bytes, exchanged by the caller, e.g. over torch.distributed); every rank opens the others' mailboxes and creates
+ * the group with all mailbox pointers (its own at index rank). b200_moe_ffn_ep then runs the rank's experts like
+ * b200_moe_ffn and leaves in `out` the FULL weighted sum over all ranks' experts (every rank gets the same out). All
+ * ranks must call it in the same order with the same T (<= max_tokens) and H. A rank that never arrives makes the
+ * others give up after a bounded wait (B200_ERR_TIMEOUT from b200_synchronize). */
+typedef struct b200_ep_group b200_ep_group;
+b200_status b200_ep_mailbox_alloc(b200_context * ctx, int world, int64_t max_tokens, int64_t hidden, void ** mailbox, void * ipc_handle);
+b200_status b200_ep_mailbox_open(b200_context * ctx, const void * ipc_handle, void ** peer_mailbox);
+b200_status b200_ep_mailbox_close(b200_context * ctx, void * peer_mailbox);
+b200_status b200_ep_mailbox_free(b200_context * ctx, void * mailbox);
+b200_status b200_ep_create(b200_context * ctx, int rank, int world, int64_t max_tokens, int64_t hidden, void * const * mailboxes,
+                           b200_ep_group ** out);
+void b200_ep_destroy(b200_ep_group * group);
+b200_status b200_moe_ffn_ep(b200_context * ctx, const b200_weight * gate_up, const b200_weight * down, int64_t expert0,
+                            int64_t n_expert_total, const float * x, const int32_t * ids, const float * w, int64_t top_k, int64_t T,
+                            float * out, b200_ep_group * group);
+
 /* GET_ROWS of a weight table (talker.cpp:131-133, decoder.cpp:319): dst [n][K] = dequantize(row ids[i]), bit for bit
  * as ggml's CPU dequantizers. An id outside [0, N * E) is skipped (its row is left untouched) and reported by
  * b200_synchronize() as B200_ERR_RANGE. */

@@ -33,6 +33,8 @@ EXPORTS = [
     "b200_block_sums", "b200_mul_mat_host", "b200_decoder_create", "b200_decoder_destroy", "b200_decoder_set_tensor",
     "b200_decoder_step", "b200_decoder_step_host", "b200_decoder_launches", "b200_decoder_weight_bytes",
     "b200_decoder_set_launch", "b200_mul_mat_id_noalloc", "b200_moe_ffn",
+    "b200_ep_mailbox_alloc", "b200_ep_mailbox_open", "b200_ep_mailbox_close", "b200_ep_mailbox_free", "b200_ep_create",
+    "b200_ep_destroy", "b200_moe_ffn_ep",
 ]
 
 DEC_ATTN_Q, DEC_ATTN_K, DEC_ATTN_V, DEC_ATTN_O, DEC_FFN_GATE, DEC_FFN_UP, DEC_FFN_DOWN = range(7)
@@ -131,6 +133,13 @@ def lib():
         "b200_decoder_set_launch": (i32, [vp, i32, i32, i32]),
         "b200_mul_mat_id_noalloc": (i32, [vp, W, vp, i64, vp, i64, i64, vp]),
         "b200_moe_ffn": (i32, [vp, W, W, i64, i64, vp, vp, vp, i64, i64, vp]),
+        "b200_ep_mailbox_alloc": (i32, [vp, ctypes.c_int, i64, i64, ctypes.POINTER(vp), vp]),
+        "b200_ep_mailbox_open": (i32, [vp, vp, ctypes.POINTER(vp)]),
+        "b200_ep_mailbox_close": (i32, [vp, vp]),
+        "b200_ep_mailbox_free": (i32, [vp, vp]),
+        "b200_ep_create": (i32, [vp, ctypes.c_int, ctypes.c_int, i64, i64, ctypes.POINTER(vp), ctypes.POINTER(vp)]),
+        "b200_ep_destroy": (None, [vp]),
+        "b200_moe_ffn_ep": (i32, [vp, W, W, i64, i64, vp, vp, vp, i64, i64, vp, vp]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -296,6 +305,19 @@ class Context:
         self._sync_in()
         self.check(self.L.b200_moe_ffn(self.h, ctypes.byref(gate_up), ctypes.byref(down), expert0, n_expert_total, _ptr(x), _ptr(ids),
                                        _ptr(w), top_k, T, _ptr(out)))
+        self._sync_out()
+        return out
+
+    def moe_ffn_ep(self, gate_up, down, x, ids, w, expert0, n_expert_total, group, out=None):
+        """b200_moe_ffn_ep: this rank's experts, combined with every other rank's over NVLink peer memory; out
+        [T, H] is the full sum (the same on every rank). group: a handle from expert_parallel.PeerCombine."""
+        import torch
+
+        T, top_k = ids.shape
+        out = torch.empty((T, gate_up.ne0), dtype=torch.float32, device=x.device) if out is None else out
+        self._sync_in()
+        self.check(self.L.b200_moe_ffn_ep(self.h, ctypes.byref(gate_up), ctypes.byref(down), expert0, n_expert_total, _ptr(x),
+                                          _ptr(ids), _ptr(w), top_k, T, _ptr(out), group))
         self._sync_out()
         return out
 

@@ -509,7 +509,8 @@ struct MoeSlots {
 // The expert FFN on the tensor cores: route into padded slots, quantize x per slot, gate|up grouped GEMM, SwiGLU +
 // re-quantization per slot, down grouped GEMM, weighted combine. Both expert matrices Q8_0 with K % 256 == 0.
 b200_status moe_ffn_tc(b200_context * ctx, const b200_weight * gate_up, const b200_weight * down, int64_t expert0, int64_t total,
-                       const float * x, const int32_t * ids, const float * w, int64_t top_k, int64_t T, float * out) {
+                       const float * x, const int32_t * ids, const float * w, int64_t top_k, int64_t T, float * out,
+                       const b200_ep_group * ep = nullptr) {
     const int64_t H = gate_up->ne0, F2 = gate_up->ne1, E = gate_up->ne2, F = F2 / 2, P = T * top_k;
     const int64_t S = moe_max_slots(P, E);
     auto up = [](size_t v) { return (v + 255) & ~(size_t) 255; };
@@ -537,6 +538,12 @@ b200_status moe_ffn_tc(b200_context * ctx, const b200_weight * gate_up, const b2
     CK(ctx, launch_moe_swiglu_slots(gu, F, m.col_src, m.grp_off + E, S, q2, d2, S, ctx->num_sms, st));
     e = launch_gemm_tc_grouped(view_of(down), H, m.tiles, m.ntiles, q2, d2, S, S, nullptr, dn, H, ctx->dev_err, ctx->num_sms, st);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "gemm_tc_grouped");
+    if (ep) {
+        e = launch_moe_combine_allreduce(dn, w, m.inv, T, top_k, H, ep, out, ctx->dev_err, ctx->num_sms, st);
+        if (e != cudaSuccess) return e == cudaErrorInvalidValue ? fail(ctx, B200_ERR_INVALID, "moe_ffn_ep: tokens, hidden or out do not fit the group")
+                                                                : cuda_fail(ctx, e, "moe_combine_allreduce");
+        return B200_OK;
+    }
     CK(ctx, launch_moe_combine_slots(dn, w, m.inv, T, top_k, H, out, st));
     return B200_OK;
 }
@@ -680,6 +687,22 @@ b200_status b200_moe_ffn(b200_context * ctx, const b200_weight * gate_up, const 
     CK(ctx, launch_gemv(p2, nc2, (int) E, st, false, ctx->num_sms));
     CK(ctx, launch_moe_combine(dn, w, ids, T, top_k, H, expert0, E, out, st));
     return B200_OK;
+}
+
+b200_status b200_moe_ffn_ep(b200_context * ctx, const b200_weight * gate_up, const b200_weight * down, int64_t expert0,
+                            int64_t n_expert_total, const float * x, const int32_t * ids, const float * w, int64_t top_k, int64_t T,
+                            float * out, b200_ep_group * group) {
+    if (!group) return fail(ctx, B200_ERR_INVALID, "moe_ffn_ep: NULL group");
+    if (!check_weight(ctx, gate_up) || !check_weight(ctx, down)) return fail(ctx, B200_ERR_INVALID, "moe_ffn_ep: bad experts");
+    const int64_t H = gate_up->ne0, F2 = gate_up->ne1, E = gate_up->ne2, F = F2 / 2;
+    if (F2 % 2 || down->ne0 != F || down->ne1 != H || down->ne2 != E)
+        return fail(ctx, B200_ERR_INVALID, "moe_ffn_ep: gate_up must be [H, 2F, E] and down [F, H, E]");
+    if (top_k <= 0 || T < 0 || expert0 < 0 || n_expert_total <= 0 || expert0 + E > n_expert_total || !x || !ids || !w || !out)
+        return fail(ctx, B200_ERR_INVALID, "moe_ffn_ep: bad shape, expert range or NULL argument");
+    if (!(gemm_tc_grouped_supported(view_of(gate_up)) && gemm_tc_grouped_supported(view_of(down)) && F % 256 == 0))
+        return fail(ctx, B200_ERR_UNSUPPORTED, "moe_ffn_ep: Q8_0 experts with rows of whole 256-value groups");
+    if (T == 0) return B200_OK;
+    return moe_ffn_tc(ctx, gate_up, down, expert0, n_expert_total, x, ids, w, top_k, T, out, group);
 }
 
 b200_status b200_get_rows(b200_context * ctx, const b200_weight * table, const int32_t * ids, int64_t n, float * dst) {

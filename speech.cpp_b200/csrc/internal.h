@@ -16,6 +16,16 @@
 #define B200_DEVERR_EXPERT 2u   // MUL_MAT_ID id out of range
 #define B200_DEVERR_TIMEOUT 4u  // a bounded wait gave up
 
+// An expert-parallel group's view of every rank's mailbox (peer.cu): inbox [G][ceil(T_max / G)][H] float, final
+// [T_max][H] float, two arrival counters; peer[g] is rank g's mailbox mapped into this process (peer[rank] its own).
+constexpr int kEpMaxRanks = 8;
+struct b200_ep_group {
+    int rank = 0, G = 1;
+    int64_t T_max = 0, H = 0;
+    void * peer[kEpMaxRanks] = {};
+    unsigned * calls = nullptr;  // this rank's calls so far (the counters' epoch)
+};
+
 // A K-quant weight expanded to int8 for the tensor cores (gemm_kq_tc.cu): one device allocation.
 struct KqExpansion {
     int type = 0;
@@ -91,6 +101,9 @@ size_t gemm_tc_dense_ws_bytes(int64_t N, int64_t M, int ksplit);
 cudaError_t launch_gemm_tc_dense(const WeightView & w, int64_t row0, int64_t N, const int8_t * q, const float * dT, int64_t ldP,
                                  int64_t M, float * y, int64_t ldy, unsigned * err, int num_sms, cudaStream_t st, int ksplit = 1,
                                  float * ws = nullptr, unsigned * tickets = nullptr);
+size_t peer_mailbox_bytes(int G, int T_max, int H);
+cudaError_t launch_moe_combine_allreduce(const float * down, const float * w, const int32_t * inv, int64_t T, int64_t top_k, int64_t H,
+                                         const b200_ep_group * ep, float * out, unsigned * err, int num_sms, cudaStream_t st);
 // K-quant (Q4_K, Q6_K) products with M >= 32 on the tensor cores (gemm_kq_tc.cu). act: scratch of
 // gemm_kq_tc_act_bytes(K, M) bytes (quantized activations).
 bool gemm_kq_tc_supported(const WeightView & w, int64_t M);

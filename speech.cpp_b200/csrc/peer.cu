@@ -1,0 +1,233 @@
+// peer.cu — the combine step of expert parallelism over NVLink peer memory: the router-weighted sum of this rank's
+// experts (TextModel::experts, src/families/drama3/text-model.cpp:198-221) fused with a two-shot all-reduce.
+//
+// Every rank of an expert-parallel group holds a "mailbox" device buffer (cudaMalloc, shared with the other ranks by
+// CUDA IPC handles): inbox [G][Ts][H] float (partial sums of the owner's token slice from each rank), final [T][H]
+// float (the reduced output), and two arrival counters. Token slice g = tokens [g Ts, (g + 1) Ts) belongs to rank g.
+// One cooperative kernel per layer:
+//   1. every CTA computes its tokens' partial sums over this rank's experts and stores each token's row into the
+//      owner's inbox (a plain store through the peer mapping; the owner's own rows stay local), then, after a
+//      system-scope fence, adds 1 to every rank's first counter;
+//   2. once the first counter shows every CTA of every rank (bounded wait), the CTAs sum their share of this rank's
+//      slice over the G inboxes in rank order (the result does not depend on timing) and store the sums into every
+//      rank's final buffer, then add 1 to every rank's second counter;
+//   3. once the second counter shows every CTA of every rank (bounded wait), the CTAs copy final to the caller's
+//      output.
+// Counters only grow: the targets of call k are (k + 1) x CTAs x G, with k a device word this rank advances at the end
+// of the call, so no reset is needed between layers or steps (also under graph replay). A rank starts writing call
+// k + 1 only after every rank finished reading call k (step 3 waits for all of step 2). Every wait is bounded: one that
+// gives up records B200_DEVERR_TIMEOUT and the kernel skips the rest (results are then garbage, the GPU keeps
+// answering). No multicast, no NVLS: plain peer loads and stores.
+#include "internal.h"
+
+namespace b200 {
+
+// The device side of a b200_ep_group: every rank's mailbox parts.
+struct PeerGroupDev {
+    float * inbox[kEpMaxRanks];      // rank g's inbox
+    float * final_[kEpMaxRanks];     // rank g's final buffer
+    unsigned * flags[kEpMaxRanks];   // rank g's counters: [0] step 1 arrivals, [1] step 2 arrivals
+};
+
+namespace {
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned * p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void red_release_sys(unsigned * p, unsigned v) {
+    asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Waits (thread 0 of the CTA) until *p >= target; false after kSpinLimit polls.
+__device__ __forceinline__ bool wait_at_least(const unsigned * p, unsigned target) {
+    for (uint32_t i = 0; i < kSpinLimit; i++) {
+        if ((int) (ld_acquire_sys(p) - target) >= 0) return true;
+        __nanosleep(64);
+    }
+    return false;
+}
+
+__global__ void __launch_bounds__(256) moe_combine_allreduce_kernel(const float * __restrict__ down, const float * __restrict__ w,
+                                                                    const int32_t * __restrict__ inv, int T, int top_k, int H,
+                                                                    int rank, int G, int Ts, PeerGroupDev grp, unsigned * calls,
+                                                                    float * __restrict__ out, unsigned * err) {
+    __shared__ int ok;
+    const int nct = gridDim.x, c = blockIdx.x;
+    const unsigned k = *reinterpret_cast<volatile unsigned *>(calls);
+    const unsigned target = (k + 1u) * (unsigned) nct * (unsigned) G;
+    const int H4 = H / 4;
+    // ---- 1. partial sums of this rank's experts, pushed to each token's owner ----
+    for (int t = c; t < T; t += nct) {
+        const int g = t / Ts, tl = t - g * Ts;
+        float4 * dst = reinterpret_cast<float4 *>(grp.inbox[g] + ((int64_t) rank * Ts + tl) * H);
+        for (int h4 = threadIdx.x; h4 < H4; h4 += blockDim.x) {
+            float4 sum = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            bool any = false;
+            for (int s = 0; s < top_k; s++) {
+                const int32_t slot = inv[(int64_t) t * top_k + s];
+                if (slot < 0) continue;
+                const float ws = w[(int64_t) t * top_k + s];
+                const float4 d = reinterpret_cast<const float4 *>(down + (int64_t) slot * H)[h4];
+                const float4 v = make_float4(__fmul_rn(d.x, ws), __fmul_rn(d.y, ws), __fmul_rn(d.z, ws), __fmul_rn(d.w, ws));
+                sum = any ? make_float4(__fadd_rn(sum.x, v.x), __fadd_rn(sum.y, v.y), __fadd_rn(sum.z, v.z), __fadd_rn(sum.w, v.w)) : v;
+                any = true;
+            }
+            dst[h4] = sum;
+        }
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int g = 0; g < G; g++) red_release_sys(&grp.flags[g][0], 1u);
+        ok = wait_at_least(&grp.flags[rank][0], target);
+        if (!ok) atomicOr(err, B200_DEVERR_TIMEOUT);
+    }
+    __syncthreads();
+    if (ok) {
+        // ---- 2. this rank's slice: sum over the G inboxes in rank order, stored to every rank's final buffer ----
+        const int t0 = rank * Ts, t1 = min(T, t0 + Ts);
+        for (int t = t0 + c; t < t1; t += nct) {
+            const int tl = t - t0;
+            for (int h4 = threadIdx.x; h4 < H4; h4 += blockDim.x) {
+                // written by other GPUs since the last call: read through L2 (__ldcg), never from a stale L1 line
+                float4 sum = __ldcg(reinterpret_cast<const float4 *>(grp.inbox[rank] + (int64_t) tl * H) + h4);
+                for (int g = 1; g < G; g++) {
+                    const float4 v = __ldcg(reinterpret_cast<const float4 *>(grp.inbox[rank] + ((int64_t) g * Ts + tl) * H) + h4);
+                    sum = make_float4(__fadd_rn(sum.x, v.x), __fadd_rn(sum.y, v.y), __fadd_rn(sum.z, v.z), __fadd_rn(sum.w, v.w));
+                }
+                for (int g = 0; g < G; g++) reinterpret_cast<float4 *>(grp.final_[g] + (int64_t) t * H)[h4] = sum;
+            }
+        }
+        __threadfence_system();
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            for (int g = 0; g < G; g++) red_release_sys(&grp.flags[g][1], 1u);
+            ok = wait_at_least(&grp.flags[rank][1], target);
+            if (!ok) atomicOr(err, B200_DEVERR_TIMEOUT);
+        }
+        __syncthreads();
+    }
+    if (ok) {
+        // ---- 3. the reduced output, every token ----
+        for (int t = c; t < T; t += nct) {
+            const float4 * src = reinterpret_cast<const float4 *>(grp.final_[rank] + (int64_t) t * H);
+            float4 * o = reinterpret_cast<float4 *>(out + (int64_t) t * H);
+            for (int h4 = threadIdx.x; h4 < H4; h4 += blockDim.x) o[h4] = __ldcg(src + h4);
+        }
+    }
+    // the call is over for this CTA; CTA 0 advances the call count once every CTA of this rank is past step 2 (the
+    // step 2 wait proves it: all CTAs of all ranks arrived there after reading k)
+    if (c == 0 && threadIdx.x == 0) atomicAdd(calls, 1u);
+}
+
+}  // namespace
+
+size_t peer_mailbox_bytes(int G, int T_max, int H) {
+    const int Ts = (T_max + G - 1) / G;
+    return (((size_t) G * Ts * H * 4 + 255) & ~(size_t) 255) + (((size_t) T_max * H * 4 + 255) & ~(size_t) 255) + 256;
+}
+
+cudaError_t launch_moe_combine_allreduce(const float * down, const float * w, const int32_t * inv, int64_t T, int64_t top_k, int64_t H,
+                                         const b200_ep_group * ep, float * out, unsigned * err, int num_sms, cudaStream_t st) {
+    if (T <= 0) return cudaSuccess;
+    if (!ep || H % 4 || T > ep->T_max || H != ep->H || ((uintptr_t) out & 15)) return cudaErrorInvalidValue;
+    PeerGroupDev grp;
+    std::memset(&grp, 0, sizeof grp);
+    const int Ts = (int) ((ep->T_max + ep->G - 1) / ep->G);
+    for (int g = 0; g < ep->G; g++) {
+        uint8_t * base = (uint8_t *) ep->peer[g];
+        grp.inbox[g] = (float *) base;
+        grp.final_[g] = (float *) (base + (((size_t) ep->G * Ts * ep->H * 4 + 255) & ~(size_t) 255));
+        grp.flags[g] = (unsigned *) (base + (((size_t) ep->G * Ts * ep->H * 4 + 255) & ~(size_t) 255) +
+                                     (((size_t) ep->T_max * ep->H * 4 + 255) & ~(size_t) 255));
+    }
+    int per_sm = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, moe_combine_allreduce_kernel, 256, 0);
+    if (e != cudaSuccess) return e;
+    const int nct = num_sms < per_sm * num_sms ? num_sms : per_sm * num_sms;  // one CTA per SM: all co-resident
+    int Ti = (int) T, ki = (int) top_k, Hi = (int) H, r = ep->rank, G = ep->G, Tsi = Ts;
+    unsigned * calls = ep->calls;
+    void * args[] = {(void *) &down, (void *) &w, (void *) &inv, &Ti, &ki, &Hi, &r, &G, &Tsi, &grp, &calls, (void *) &out, &err};
+    return cudaLaunchCooperativeKernel((const void *) moe_combine_allreduce_kernel, dim3((unsigned) nct), dim3(256), args, 0, st);
+}
+
+}  // namespace b200
+
+using namespace b200;
+
+extern "C" {
+
+b200_status b200_ep_mailbox_alloc(b200_context * ctx, int world, int64_t max_tokens, int64_t hidden, void ** mailbox, void * ipc_handle) {
+    if (!ctx || !mailbox || !ipc_handle || world < 1 || world > kEpMaxRanks || max_tokens < 1 || hidden < 4 || hidden % 4) {
+        if (ctx) ctx->last_error = "ep_mailbox_alloc: bad arguments";
+        return B200_ERR_INVALID;
+    }
+    *mailbox = nullptr;
+    const size_t bytes = peer_mailbox_bytes(world, (int) max_tokens, (int) hidden);
+    cudaError_t e = cudaMalloc(mailbox, bytes);
+    if (e == cudaSuccess) e = cudaMemset(*mailbox, 0, bytes);
+    cudaIpcMemHandle_t h;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, *mailbox);
+    if (e != cudaSuccess) {
+        if (*mailbox) cudaFree(*mailbox);
+        *mailbox = nullptr;
+        ctx->last_error = std::string("ep_mailbox_alloc: ") + cudaGetErrorString(e);
+        return e == cudaErrorMemoryAllocation ? B200_ERR_ALLOC : B200_ERR_DEVICE;
+    }
+    std::memcpy(ipc_handle, &h, sizeof h);
+    return B200_OK;
+}
+
+b200_status b200_ep_mailbox_open(b200_context * ctx, const void * ipc_handle, void ** peer_mailbox) {
+    if (!ctx || !ipc_handle || !peer_mailbox) return B200_ERR_INVALID;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, ipc_handle, sizeof h);
+    const cudaError_t e = cudaIpcOpenMemHandle(peer_mailbox, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+        ctx->last_error = std::string("ep_mailbox_open: ") + cudaGetErrorString(e);
+        return B200_ERR_DEVICE;
+    }
+    return B200_OK;
+}
+
+b200_status b200_ep_mailbox_close(b200_context * ctx, void * peer_mailbox) {
+    if (!ctx || !peer_mailbox) return B200_ERR_INVALID;
+    return cudaIpcCloseMemHandle(peer_mailbox) == cudaSuccess ? B200_OK : B200_ERR_DEVICE;
+}
+
+b200_status b200_ep_mailbox_free(b200_context * ctx, void * mailbox) {
+    if (!ctx || !mailbox) return B200_ERR_INVALID;
+    return cudaFree(mailbox) == cudaSuccess ? B200_OK : B200_ERR_DEVICE;
+}
+
+b200_status b200_ep_create(b200_context * ctx, int rank, int world, int64_t max_tokens, int64_t hidden, void * const * mailboxes,
+                           b200_ep_group ** out) {
+    if (!ctx || !out || !mailboxes || world < 1 || world > kEpMaxRanks || rank < 0 || rank >= world || max_tokens < 1 || hidden % 4) {
+        if (ctx) ctx->last_error = "ep_create: bad arguments";
+        return B200_ERR_INVALID;
+    }
+    b200_ep_group * g = new b200_ep_group();
+    g->rank = rank;
+    g->G = world;
+    g->T_max = max_tokens;
+    g->H = hidden;
+    for (int i = 0; i < world; i++) g->peer[i] = mailboxes[i];
+    if (cudaMalloc(&g->calls, sizeof(unsigned)) != cudaSuccess || cudaMemset(g->calls, 0, sizeof(unsigned)) != cudaSuccess) {
+        delete g;
+        ctx->last_error = "ep_create: device allocation";
+        return B200_ERR_ALLOC;
+    }
+    *out = g;
+    return B200_OK;
+}
+
+void b200_ep_destroy(b200_ep_group * g) {
+    if (!g) return;
+    if (g->calls) cudaFree(g->calls);
+    delete g;
+}
+
+}  // extern "C"

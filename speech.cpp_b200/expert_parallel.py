@@ -5,7 +5,8 @@ ggml_backend_sched, src/engines/drama3-engine.cpp:51-88). Here the experts of ev
 one node: rank r holds experts [r E/N, (r+1) E/N). The router runs on every rank and the token activations are
 replicated (they come out of the replicated attention / mixer part of the layer), so dispatch moves no bytes: each
 rank's b200_moe_ffn skips the (token, slot) pairs routed to other ranks and leaves its experts' partial weighted sum,
-and one all-reduce per layer adds the partial sums into the layer output every rank needs next.
+and one all-reduce per layer adds the partial sums into the layer output every rank needs next: an NCCL all-reduce,
+or (PeerCombine) the combine kernel itself, over NVLink peer memory.
 
 With 256 tokens x top-8 of 128 experts, an all-to-all dispatch + combine would move each token-slot's activation row
 (2176 B as q8_0) out and its 8 KB f32 output row back for 7/8 of the 2048 slots, about 16.8 MB per layer over the
@@ -13,6 +14,8 @@ node; the all-reduce of the [256, 2048] f32 output moves 2 MB per rank.
 """
 
 from __future__ import annotations
+
+import ctypes
 
 
 def expert_shard(n_expert: int, world: int, rank: int) -> tuple[int, int]:
@@ -25,17 +28,66 @@ def expert_shard(n_expert: int, world: int, rank: int) -> tuple[int, int]:
     return rank * n, n
 
 
+class PeerCombine:
+    """The mailboxes of an expert-parallel group (b200_ep_*): each rank allocates one, the 64-byte CUDA IPC handles
+    are exchanged over the torch.distributed group, each rank maps the others' and creates the group. Then
+    b200_moe_ffn_ep combines the ranks' partial sums in one kernel over NVLink peer memory (a two-shot all-reduce:
+    partial rows pushed to each token's owner, owners' sums pushed to every rank) instead of an NCCL all-reduce."""
+
+    def __init__(self, ctx, group, max_tokens: int, hidden: int):
+        import torch.distributed as dist
+
+        self.ctx, self.group = ctx, group
+        L = ctx.L
+        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        self.own = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(64)
+        ctx.check(L.b200_ep_mailbox_alloc(ctx.h, self.world, max_tokens, hidden, ctypes.byref(self.own), handle))
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle.raw, group=group)
+        self.peers, ptrs = [], []
+        for g in range(self.world):
+            if g == self.rank:
+                ptrs.append(self.own.value)
+                continue
+            p = ctypes.c_void_p()
+            ctx.check(L.b200_ep_mailbox_open(ctx.h, ctypes.create_string_buffer(handles[g], 64), ctypes.byref(p)))
+            self.peers.append(p)
+            ptrs.append(p.value)
+        arr = (ctypes.c_void_p * self.world)(*ptrs)
+        self.handle = ctypes.c_void_p()
+        ctx.check(L.b200_ep_create(ctx.h, self.rank, self.world, max_tokens, hidden, arr, ctypes.byref(self.handle)))
+        dist.barrier(group=group)  # every rank has mapped every mailbox before any rank writes into one
+
+    def close(self):
+        """Collective: every rank's kernels are done before any mailbox is unmapped or freed."""
+        import torch.distributed as dist
+
+        if self.handle is None:
+            return
+        self.ctx.synchronize()
+        dist.barrier(group=self.group)
+        L = self.ctx.L
+        L.b200_ep_destroy(self.handle)
+        for p in self.peers:
+            L.b200_ep_mailbox_close(self.ctx.h, p)
+        dist.barrier(group=self.group)
+        L.b200_ep_mailbox_free(self.ctx.h, self.own)
+        self.handle = None
+
+
 class ExpertParallelMoe:
     """One rank's share of an MoE FFN stack: per layer (gate_up, down) expert weights of experts
     [expert0, expert0 + n_local) of n_expert. `ffn(ctx-like)` is any object with moe_ffn(gate_up, down, x, ids, w,
     expert0=, n_expert_total=, out=) (a speech.cpp_b200 Context); `group` a torch.distributed process group or None."""
 
-    def __init__(self, ffn, layers, expert0: int, n_expert: int, group=None):
+    def __init__(self, ffn, layers, expert0: int, n_expert: int, group=None, peer: PeerCombine | None = None):
         self.ffn = ffn
         self.layers = list(layers)
         self.expert0 = expert0
         self.n_expert = n_expert
         self.group = group
+        self.peer = peer  # when set: the combine and the all-reduce are one kernel over peer memory
 
     def _all_reduce(self, t):
         if self.group is None:
@@ -48,6 +100,8 @@ class ExpertParallelMoe:
     def layer(self, l: int, x, ids, w, out):
         """out = the full weighted sum of layer l's routed experts for tokens x (every rank gets the same out)."""
         gu, dn = self.layers[l]
+        if self.peer is not None:
+            return self.ffn.moe_ffn_ep(gu, dn, x, ids, w, self.expert0, self.n_expert, self.peer.handle, out=out)
         self.ffn.moe_ffn(gu, dn, x, ids, w, expert0=self.expert0, n_expert_total=self.n_expert, out=out)
         self._all_reduce(out)
         return out
