@@ -23,7 +23,7 @@ struct b200_ep_group {
     int rank = 0, G = 1;
     int64_t T_max = 0, H = 0;
     void * peer[kEpMaxRanks] = {};
-    unsigned * calls = nullptr;  // this rank's calls so far (the counters' epoch)
+    unsigned * calls = nullptr;  // [3]: this rank's calls so far (the counters' epoch), its CTAs done with steps 1 and 2
 };
 
 // A K-quant weight expanded to int8 for the tensor cores (gemm_kq_tc.cu): one device allocation.

@@ -13,8 +13,10 @@
 //      rank's final buffer, then add 1 to every rank's second counter;
 //   3. once the second counter shows every CTA of every rank (bounded wait), the CTAs copy final to the caller's
 //      output.
-// Counters only grow: the targets of call k are (k + 1) x CTAs x G, with k a device word this rank advances at the end
-// of the call, so no reset is needed between layers or steps (also under graph replay). A rank starts writing call
+// Counters only grow: a rank's CTAs count themselves in a local counter, and the one that completes the count adds 1
+// to every rank's counter, so the targets of call k are (k + 1) x CTAs locally and (k + 1) x G remotely, with k a
+// device word this rank advances at the end of the call: no reset is needed between layers or steps (also under graph
+// replay). A rank starts writing call
 // k + 1 only after every rank finished reading call k (step 3 waits for all of step 2). Every wait is bounded: one that
 // gives up records B200_DEVERR_TIMEOUT and the kernel skips the rest (results are then garbage, the GPU keeps
 // answering). No multicast, no NVLS: plain peer loads and stores.
@@ -41,13 +43,22 @@ __device__ __forceinline__ void red_release_sys(unsigned * p, unsigned v) {
     asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Waits (thread 0 of the CTA) until *p >= target; false after kSpinLimit polls.
+// Waits (thread 0 of the CTA) until *p >= target; false after kSpinLimit polls (spinning first, then sleeping).
 __device__ __forceinline__ bool wait_at_least(const unsigned * p, unsigned target) {
     for (uint32_t i = 0; i < kSpinLimit; i++) {
         if ((int) (ld_acquire_sys(p) - target) >= 0) return true;
-        __nanosleep(64);
+        if (i > 256) __nanosleep(64);
     }
     return false;
+}
+
+// This CTA's part of a step is stored (and fenced at system scope): counts it in the rank's local counter; the CTA
+// that completes the count tells every rank with one release each (G remote updates per step, not CTAs x G).
+__device__ __forceinline__ void arrive_all(unsigned * local, unsigned local_target, unsigned * const * flags, int G, int which) {
+    unsigned old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(local), "r"(1u) : "memory");
+    if (old + 1u == local_target)
+        for (int g = 0; g < G; g++) red_release_sys(&flags[g][which], 1u);
 }
 
 __global__ void __launch_bounds__(256) moe_combine_allreduce_kernel(const float * __restrict__ down, const float * __restrict__ w,
@@ -57,7 +68,9 @@ __global__ void __launch_bounds__(256) moe_combine_allreduce_kernel(const float 
     __shared__ int ok;
     const int nct = gridDim.x, c = blockIdx.x;
     const unsigned k = *reinterpret_cast<volatile unsigned *>(calls);
-    const unsigned target = (k + 1u) * (unsigned) nct * (unsigned) G;
+    const unsigned target = (k + 1u) * (unsigned) G;              // remote arrivals: one per rank per call
+    const unsigned local_target = (k + 1u) * (unsigned) nct;       // this rank's CTAs per call
+    unsigned * local = calls + 1;                                  // [2] this rank's CTAs done with steps 1 and 2
     const int H4 = H / 4;
     // ---- 1. partial sums of this rank's experts, pushed to each token's owner ----
     for (int t = c; t < T; t += nct) {
@@ -81,7 +94,7 @@ __global__ void __launch_bounds__(256) moe_combine_allreduce_kernel(const float 
     __threadfence_system();
     __syncthreads();
     if (threadIdx.x == 0) {
-        for (int g = 0; g < G; g++) red_release_sys(&grp.flags[g][0], 1u);
+        arrive_all(&local[0], local_target, grp.flags, G, 0);
         ok = wait_at_least(&grp.flags[rank][0], target);
         if (!ok) atomicOr(err, B200_DEVERR_TIMEOUT);
     }
@@ -104,7 +117,7 @@ __global__ void __launch_bounds__(256) moe_combine_allreduce_kernel(const float 
         __threadfence_system();
         __syncthreads();
         if (threadIdx.x == 0) {
-            for (int g = 0; g < G; g++) red_release_sys(&grp.flags[g][1], 1u);
+            arrive_all(&local[1], local_target, grp.flags, G, 1);
             ok = wait_at_least(&grp.flags[rank][1], target);
             if (!ok) atomicOr(err, B200_DEVERR_TIMEOUT);
         }
@@ -215,7 +228,7 @@ b200_status b200_ep_create(b200_context * ctx, int rank, int world, int64_t max_
     g->T_max = max_tokens;
     g->H = hidden;
     for (int i = 0; i < world; i++) g->peer[i] = mailboxes[i];
-    if (cudaMalloc(&g->calls, sizeof(unsigned)) != cudaSuccess || cudaMemset(g->calls, 0, sizeof(unsigned)) != cudaSuccess) {
+    if (cudaMalloc(&g->calls, 3 * sizeof(unsigned)) != cudaSuccess || cudaMemset(g->calls, 0, 3 * sizeof(unsigned)) != cudaSuccess) {
         delete g;
         ctx->last_error = "ep_create: device allocation";
         return B200_ERR_ALLOC;
