@@ -39,8 +39,7 @@ struct GLayout {
     static constexpr int kDw = kGM * kGKB * 2;   // fp16 weight scales [128][8]
     static constexpr int kDx = kGKB * kGNT * 4;  // f32 activation scales [8][32]
     static constexpr int kStage = kA + kB + kDw + kDx;
-    static constexpr int kXch = 4 * 32 * 16 * 4;  // 16-slot tiles: the odd blocks' sums, [quarter][lane][16] float
-    static constexpr int kTotal = kGStages * kStage + kXch + 1024 + 1024;  // + barriers + alignment slack
+    static constexpr int kTotal = kGStages * kStage + 1024 + 1024;  // + barriers + alignment slack
     static_assert(kA % 1024 == 0 && kB % 1024 == 0 && kStage % 1024 == 0, "stage regions stay 1024-aligned");
 };
 
@@ -75,16 +74,13 @@ __global__ void __launch_bounds__(kGThreads, 2)
     using L = GLayout;
     extern __shared__ uint8_t smem_raw[];
     uint8_t * smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t) 1023);
-    float * xch = reinterpret_cast<float *>(smem + kGStages * L::kStage);
-    uint64_t * bars = reinterpret_cast<uint64_t *>(smem + kGStages * L::kStage + L::kXch);
+    uint64_t * bars = reinterpret_cast<uint64_t *>(smem + kGStages * L::kStage);
     uint64_t * full = bars;
     uint64_t * empty = bars + kGStages;
     uint64_t * acc_full = bars + 2 * kGStages;   // [bufs] a block pair's int32 sums ready in tensor memory
     uint64_t * acc_empty = acc_full + kGBufs;    // [bufs] epilogue has read them
     uint64_t * xbar = acc_empty + kGBufs;        // [2] split-K: every epilogue warp stored its partial / ticket taken
-    uint64_t * nbar = xbar + 2;                  // [4] 16-slot tiles: lane quarter q's odd-block sums are in xch
-    uint64_t * nfree = nbar + 4;                 // [4] ... and have been read (xch[q] may be written again)
-    uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(nfree + 4);
+    uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(xbar + 2);
     __shared__ int last_split;
     __shared__ volatile int give_up;
 
@@ -102,10 +98,6 @@ __global__ void __launch_bounds__(kGThreads, 2)
         }
         mbar_init(&xbar[0], kGEpiWarps);
         mbar_init(&xbar[1], 1);
-        for (int i = 0; i < 4; i++) {
-            mbar_init(&nbar[i], 1);
-            mbar_init(&nfree[i], 1);
-        }
         fence_mbar_init();
         give_up = 0;
     }
@@ -197,23 +189,19 @@ __global__ void __launch_bounds__(kGThreads, 2)
         }
     } else {
         // ---- epilogue: lane quarter q = warp % 4 owns tile rows 32 q .. 32 q + 31 (one per lane); warp half h takes
-        // the tile's 16-slot column chunk h, or, in a tile of one chunk, block h of every pair. Every epilogue warp
-        // waits and arrives on every accumulator barrier, so no warp runs a phase ahead of the others: parity waits
-        // cannot tell phase n from phase n + 2 ----
+        // the tile's 16-slot column chunk h. A warp without columns (h = 1 in a tile of 16 slots) still waits and
+        // arrives on every barrier, so no warp runs a phase ahead of the others: parity waits cannot tell phase n
+        // from phase n + 2 ----
         const int q = warp & 3, h = (warp - 2) >> 2;
         const int row = 32 * q + lane;
         const float2 neg_magic = make_float2(-12582912.0f, -12582912.0f);
-        int sg = 0, g2 = 0, xi = 0, xn = 0;
+        int sg = 0, g2 = 0, xi = 0;
         for (int it = blockIdx.x; it < items && !give_up; it += gridDim.x) {
             const int ot = it / p.ksplit, ks = it % p.ksplit;
             const int4 t = g_tile(p, ot / p.tiles_n);
             const int tn = ot % p.tiles_n;
-            // a tile of one 16-slot chunk ("narrow"): both warp halves work on it, h taking block h of every pair;
-            // otherwise warp half h takes the chunk h of both blocks
-            const bool narrow = t.z == 16;
-            bool has = narrow || h < t.z / 16;
-            const int ch = narrow ? 0 : h;             // this warp's column chunk
-            const int live = t.w - 16 * ch;            // routed slots in it (the rest is padding: no math)
+            const bool has = h < t.z / 16;
+            const int live = t.w - 16 * h;  // routed slots in this warp's chunk (the rest is padding: no math)
             float2 acc[8];
 #pragma unroll
             for (int i = 0; i < 8; i++) acc[i] = make_float2(0.0f, 0.0f);
@@ -235,16 +223,11 @@ __global__ void __launch_bounds__(kGThreads, 2)
                         if (lane == 0) mbar_arrive(&acc_empty[buf]);
                         continue;
                     }
-                    // the pair's blocks in registers (a narrow tile: this half's one block), then the buffer is released
+                    // both blocks of the pair in registers, then the buffer is released
                     int v[2][16];
-                    const uint32_t ta = tmem + ((uint32_t) (32 * q) << 16) + buf * 2 * kGNT + 16 * ch;
-                    if (narrow) {  // static register indices: v[h] with a run-time h would go to local memory
-                        if (h == 0) tmem_ld16(ta, v[0]);
-                        else tmem_ld16(ta + kGNT, v[1]);
-                    } else {
-                        tmem_ld16(ta, v[0]);
-                        tmem_ld16(ta + kGNT, v[1]);
-                    }
+                    const uint32_t ta = tmem + ((uint32_t) (32 * q) << 16) + buf * 2 * kGNT + 16 * h;
+                    tmem_ld16(ta, v[0]);
+                    tmem_ld16(ta + kGNT, v[1]);
                     tmem_wait_ld();
                     tc_fence_before();
                     __syncwarp();
@@ -254,10 +237,9 @@ __global__ void __launch_bounds__(kGThreads, 2)
                     // through the float 12582912 + sum (bit pattern 0x4B400000 + sum)
 #pragma unroll
                     for (int jj = 0; jj < 2; jj++) {
-                        if (narrow && jj != h) continue;
                         const float dwr = jj ? dwp.y : dwp.x;
                         const float2 w2 = make_float2(dwr, dwr);
-                        const float4 * dx4 = reinterpret_cast<const float4 *>(dxT + (j + jj) * kGNT + 16 * ch);
+                        const float4 * dx4 = reinterpret_cast<const float4 *>(dxT + (j + jj) * kGNT + 16 * h);
 #pragma unroll
                         for (int t4 = 0; t4 < 4; t4++) {
                             if (4 * t4 >= live) break;
@@ -278,39 +260,6 @@ __global__ void __launch_bounds__(kGThreads, 2)
                 if (lane == 0) mbar_arrive(&empty[s]);
             }
             if (give_up) break;
-            if (narrow) {
-                // the odd blocks' sums (h = 1) join the even blocks' (h = 0) through shared memory: a fixed two-term
-                // sum per value, so the result does not depend on timing
-                // (a return handshake keeps the halves within one tile of each other: the buffer and both barriers are
-                // never a phase ahead of their reader)
-                float * xq = xch + (q * 32 + lane) * 16;
-                if (h == 1) {
-                    if (xn > 0 && !mbar_wait_sleep(&nfree[q], (xn - 1) & 1)) {
-                        if (lane == 0) atomicOr(p.err, kErrTimeout);
-                        give_up = 1;
-                        break;
-                    }
-#pragma unroll
-                    for (int i = 0; i < 8; i++) reinterpret_cast<float2 *>(xq)[i] = acc[i];
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&nbar[q]);
-                    has = false;  // the partner writes the tile
-                } else {
-                    if (!mbar_wait_sleep(&nbar[q], xn & 1)) {
-                        if (lane == 0) atomicOr(p.err, kErrTimeout);
-                        give_up = 1;
-                        break;
-                    }
-#pragma unroll
-                    for (int i = 0; i < 8; i++) {
-                        const float2 o = reinterpret_cast<const float2 *>(xq)[i];
-                        acc[i] = make_float2(__fadd_rn(acc[i].x, o.x), __fadd_rn(acc[i].y, o.y));
-                    }
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&nfree[q]);
-                }
-                xn++;
-            }
             const int64_t grow = (int64_t) tn * kGM + row;
             if (p.ksplit > 1) {
                 // ---- split K: store this split's partial tile; the last split of the tile (an atomic ticket) adds
@@ -319,7 +268,7 @@ __global__ void __launch_bounds__(kGThreads, 2)
                 float * part = p.ws + ((int64_t) ot * p.ksplit + ks) * kGNT * kGM;
                 if (has)
 #pragma unroll
-                    for (int i = 0; i < 16; i++) part[(16 * ch + i) * kGM + row] = (i & 1) ? acc[i / 2].y : acc[i / 2].x;
+                    for (int i = 0; i < 16; i++) part[(16 * h + i) * kGM + row] = (i & 1) ? acc[i / 2].y : acc[i / 2].x;
                 __threadfence();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&xbar[0]);
@@ -342,7 +291,7 @@ __global__ void __launch_bounds__(kGThreads, 2)
                 __threadfence();
                 // partials summed in split order; each split's 16 values are read together (one L2 round trip per
                 // split, not per value)
-                const float * parts = p.ws + (int64_t) ot * p.ksplit * kGNT * kGM + (int64_t) (16 * ch) * kGM + row;
+                const float * parts = p.ws + (int64_t) ot * p.ksplit * kGNT * kGM + (int64_t) (16 * h) * kGM + row;
                 float sum[16];
 #pragma unroll
                 for (int i = 0; i < 16; i++) sum[i] = 0.0f;
@@ -355,7 +304,7 @@ __global__ void __launch_bounds__(kGThreads, 2)
                 }
 #pragma unroll
                 for (int i = 0; i < 16; i++)
-                    if (i < live) p.y[(int64_t) (t.y + 16 * ch + i) * p.ldy + grow] = sum[i];
+                    if (i < live) p.y[(int64_t) (t.y + 16 * h + i) * p.ldy + grow] = sum[i];
                 continue;
             }
             if (!has) continue;
@@ -364,7 +313,7 @@ __global__ void __launch_bounds__(kGThreads, 2)
 #pragma unroll
                 for (int i = 0; i < 16; i++) {
                     if (i >= live) break;
-                    const int slot = t.y + 16 * ch + i;
+                    const int slot = t.y + 16 * h + i;
                     const int64_t orow = p.row_map ? (int64_t) p.row_map[slot] : (int64_t) slot;
                     const float2 a = acc[i / 2];
                     if (orow >= 0) p.y[orow * p.ldy + grow] = (i & 1) ? a.y : a.x;
