@@ -68,6 +68,9 @@ __device__ __forceinline__ int4 g_tile(const GroupedParams & p, int i) {
     return make_int4(0, m0, (live + 15) & ~15, live);
 }
 
+// kSplit: K may be split across CTAs (dense products with few output tiles); the expert products compile without
+// that code.
+template <bool kSplit>
 __global__ void __launch_bounds__(kGThreads, 2)
     gemm_q8_0_tc_grouped_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                                 const __grid_constant__ CUtensorMap tmDw, const __grid_constant__ CUtensorMap tmDx, GroupedParams p) {
@@ -109,13 +112,14 @@ __global__ void __launch_bounds__(kGThreads, 2)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    // Set-up above overlaps the previous kernel under programmatic dependent launch; the tile list, the activations
-    // and the outputs' previous readers come from kernels before this one.
+    // the tile list and the activations come from the kernels before this one (no-ops unless launched with
+    // programmatic dependent launch); the next kernel may launch its CTAs once these have started
     pdl_wait();
     pdl_launch_dependents();
     // item = (output tile, K split), the split fastest: the splits of one tile run at the same time on different CTAs
-    const int items = (p.tiles ? *p.ntiles : (p.dense_m + 31) / 32) * p.tiles_n * p.ksplit;
-    const int spl = nstage / p.ksplit;  // stages per split
+    const int ksplit = kSplit ? p.ksplit : 1;
+    const int items = (p.tiles ? *p.ntiles : (p.dense_m + 31) / 32) * p.tiles_n * ksplit;
+    const int spl = nstage / ksplit;  // stages per split
 
     if (warp == 0) {
         // ---- TMA producer ----
@@ -126,7 +130,7 @@ __global__ void __launch_bounds__(kGThreads, 2)
             prefetch_tensormap(&tmDx);
             int sg = 0;
             for (int it = blockIdx.x; it < items && !give_up; it += gridDim.x) {
-                const int ot = it / p.ksplit, ks = it % p.ksplit;
+                const int ot = kSplit ? it / ksplit : it, ks = kSplit ? it % ksplit : 0;
                 const int4 t = g_tile(p, ot / p.tiles_n);
                 const int arow = (int) ((int64_t) t.x * p.N + p.row0 + (int64_t) (ot % p.tiles_n) * kGM);
                 const int nsub = t.z / 16;
@@ -157,7 +161,7 @@ __global__ void __launch_bounds__(kGThreads, 2)
         if (lane == 0) {
             int sg = 0, g2 = 0;
             for (int it = blockIdx.x; it < items && !give_up; it += gridDim.x) {
-                const int4 t = g_tile(p, it / p.ksplit / p.tiles_n);
+                const int4 t = g_tile(p, (kSplit ? it / ksplit : it) / p.tiles_n);
                 const uint32_t idesc = idesc_i8_n(t.z);
                 for (int st = 0; st < spl && !give_up; st++, sg++) {
                     const int s = sg % kGStages;
@@ -197,7 +201,7 @@ __global__ void __launch_bounds__(kGThreads, 2)
         const float2 neg_magic = make_float2(-12582912.0f, -12582912.0f);
         int sg = 0, g2 = 0, xi = 0;
         for (int it = blockIdx.x; it < items && !give_up; it += gridDim.x) {
-            const int ot = it / p.ksplit, ks = it % p.ksplit;
+            const int ot = kSplit ? it / ksplit : it, ks = kSplit ? it % ksplit : 0;
             const int4 t = g_tile(p, ot / p.tiles_n);
             const int tn = ot % p.tiles_n;
             const bool has = h < t.z / 16;
@@ -261,11 +265,11 @@ __global__ void __launch_bounds__(kGThreads, 2)
             }
             if (give_up) break;
             const int64_t grow = (int64_t) tn * kGM + row;
-            if (p.ksplit > 1) {
+            if (kSplit && ksplit > 1) {
                 // ---- split K: store this split's partial tile; the last split of the tile (an atomic ticket) adds
                 // the partials in split order, so the result does not depend on timing. Every epilogue warp takes
                 // part (bounded mbarrier waits, no unbounded named barrier) ----
-                float * part = p.ws + ((int64_t) ot * p.ksplit + ks) * kGNT * kGM;
+                float * part = p.ws + ((int64_t) ot * ksplit + ks) * kGNT * kGM;
                 if (has)
 #pragma unroll
                     for (int i = 0; i < 16; i++) part[(16 * h + i) * kGM + row] = (i & 1) ? acc[i / 2].y : acc[i / 2].x;
@@ -278,7 +282,7 @@ __global__ void __launch_bounds__(kGThreads, 2)
                         give_up = 1;
                     }
                     const unsigned ticket = atomicAdd(&p.tickets[ot], 1u);
-                    last_split = ticket == (unsigned) (p.ksplit - 1);
+                    last_split = ticket == (unsigned) (ksplit - 1);
                     if (last_split) p.tickets[ot] = 0u;  // ready for the next launch
                     mbar_arrive(&xbar[1]);
                 }
@@ -291,11 +295,11 @@ __global__ void __launch_bounds__(kGThreads, 2)
                 __threadfence();
                 // partials summed in split order; each split's 16 values are read together (one L2 round trip per
                 // split, not per value)
-                const float * parts = p.ws + (int64_t) ot * p.ksplit * kGNT * kGM + (int64_t) (16 * h) * kGM + row;
+                const float * parts = p.ws + (int64_t) ot * ksplit * kGNT * kGM + (int64_t) (16 * h) * kGM + row;
                 float sum[16];
 #pragma unroll
                 for (int i = 0; i < 16; i++) sum[i] = 0.0f;
-                for (int z = 0; z < p.ksplit; z++) {
+                for (int z = 0; z < ksplit; z++) {
                     float v[16];
 #pragma unroll
                     for (int i = 0; i < 16; i++) v[i] = __ldcg(parts + ((int64_t) z * kGNT + i) * kGM);
@@ -371,21 +375,16 @@ cudaError_t launch_grouped(const WeightView & w, int64_t N, int64_t row0, int de
     p.err = err;
     static int configured = 0;
     if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_q8_0_tc_grouped_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
+        cudaError_t e = cudaFuncSetAttribute(gemm_q8_0_tc_grouped_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(gemm_q8_0_tc_grouped_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
         if (e != cudaSuccess) return e;
         configured = 1;
     }
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned) (2 * num_sms), 1, 1);
-    cfg.blockDim = dim3(kGThreads, 1, 1);
-    cfg.dynamicSmemBytes = L::kTotal;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, gemm_q8_0_tc_grouped_kernel, ta, tb, tdw, tdx, p);
+    // Launched without programmatic dependent launch: CTAs started early would hold the SMs' shared memory while the
+    // previous kernel drains (measured slower).
+    if (ksplit > 1) gemm_q8_0_tc_grouped_kernel<true><<<2 * num_sms, kGThreads, L::kTotal, st>>>(ta, tb, tdw, tdx, p);
+    else gemm_q8_0_tc_grouped_kernel<false><<<2 * num_sms, kGThreads, L::kTotal, st>>>(ta, tb, tdw, tdx, p);
+    return cudaGetLastError();
 }
 
 }  // namespace
