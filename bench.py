@@ -59,7 +59,7 @@ DECODE_TRAFFIC = {"dram_bytes_per_step": 471756800 + 3960064,
 
 # DRAM bytes of one layer's two gemm_q8_0_tc_grouped_kernel launches (gate|up + down) from the ncu capture of the
 # 2-layer case summarised in profiles/gemm_q8_0_tc_grouped_config5.md; the step's traffic scales with its layers.
-MOE_TRAFFIC_PER_LAYER = 434741504 + 16279808 + 216521216 + 16315904
+MOE_TRAFFIC_PER_LAYER = 434762496 + 12986368 + 216577024 + 12018688
 
 
 def profile_traffic():
