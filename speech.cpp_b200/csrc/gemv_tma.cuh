@@ -3,7 +3,7 @@
 //
 // Each CTA owns a contiguous slice of rows. One producer warp streams that slice through a ring of shared-memory
 // stages with bulk asynchronous copies (cp.async.bulk, one per field per stage, no multicast), each stage tracked by
-// an mbarrier's transaction count; eight consumer warps stage the activations, then reduce each landed row from
+// an mbarrier's transaction count; 8 or 16 consumer warps stage the activations, then reduce each landed row from
 // shared memory and hand the stage back. The producer issues its first stages before griddepcontrol.wait: weights
 // depend on nothing, so in a chain of products (a decode step) a product's whole weight slice is in flight while
 // the previous product finishes, and the memory system sees every byte of the slice requested at once.
@@ -86,17 +86,106 @@ __device__ __forceinline__ void smem_rows_lpr(const uint8_t * const * f, int64_t
     }
 }
 
-// Lanes per row: 8 for rows of up to 64 units (a warp reduces 4 rows at once), 32 for longer rows. A function of K
-// alone, so a row's summation order does not depend on how rows are chunked (launch geometry never changes results).
+// dp4a of unsigned bytes (a) with signed bytes (b), accumulating into c.
+__device__ __forceinline__ int dp4a_us(unsigned a, int b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// Bits [pos, pos + len) of v (len 0: zero).
+__device__ __forceinline__ unsigned bfe_u32(unsigned v, unsigned pos, unsigned len) {
+    unsigned d;
+    asm("bfe.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(v), "r"(pos), "r"(len));
+    return d;
+}
+
+// Q4_K rows from shared memory, single column: 16 lanes per row, two rows per warp pass. Lane li of a row takes the
+// super-blocks sb = e, e + 2, ... (e = li / 8) and, in each, the 16-byte piece p = li % 8 of its 128 quant bytes:
+// with g = p / 2 and h = p % 2, the piece's low nibbles are values [16h, 16h + 16) of sub-block 2g and its high nibbles
+// the same values of sub-block 2g + 1. Eight lanes read one super-block's 128 contiguous quant bytes, and lanes with
+// g >= 2 load the high sub-block's activations first, so every 128-bit shared load of an 8-lane phase touches 32
+// distinct banks. Per piece the int32 sums are exact (dp4a; high nibbles are masked in place and their sum, a multiple
+// of 16, is shifted down exactly), scaled by the sub-blocks' 6-bit scales and mins as integers (ggml's sumi and summ
+// restricted to the piece), then accumulated in float32 with the super-block's dx * d and dx * dmin.
+template <class Store>
+__device__ __forceinline__ void smem_rows_q4k(const uint8_t * const * f, int64_t K, int rows, const Act & a, int warp,
+                                              int nwarps, Store store) {
+    const int lane = threadIdx.x & 31;
+    const int sub = lane >> 4, li = lane & 15, e = li >> 3, p = li & 7, g = p >> 1, h = p & 1;
+    const int nsb = (int) (K / 256);
+    const bool swap = g >= 2;  // this lane's first activation load is the high sub-block's
+    const unsigned maskA = swap ? 0xF0F0F0F0u : 0x0F0F0F0Fu, maskB = ~maskA;
+    const int offA = 64 * g + 16 * h + (swap ? 32 : 0), offB = 64 * g + 16 * h + (swap ? 0 : 32);
+    // 6-bit scale / min of sub-blocks 2g and 2g + 1 from meta words y (scale bytes 0..3), z (4..7), w (8..11):
+    // j < 4: byte j of y / z; j >= 4: low four bits from byte j - 4 of w (scale: low nibble, min: high nibble), top
+    // two bits from bits 6..7 of byte j - 4 of y / z
+    const unsigned sh0 = 8u * (unsigned) ((2 * g) & 3), sh1 = sh0 + 8u;
+    const unsigned lenlo = swap ? 4u : 6u, himask = swap ? 0x30u : 0u;
+    const int bs0 = 4 * g + h, bs1 = 4 * g + 2 + h;  // 16-value activation sums of the two halves this piece covers
+    for (int j0 = warp * 2; j0 < rows; j0 += nwarps * 2) {
+        const int j = j0 + sub;
+        float acc = 0.0f;
+        if (j < rows) {
+            const uint8_t * qr = f[0] + (size_t) j * (size_t) (K / 2) + 16 * p;
+            const int4 * mr = reinterpret_cast<const int4 *>(f[1]) + (size_t) j * nsb;
+#pragma unroll 2
+            for (int sb = e; sb < nsb; sb += 2) {
+                const int4 wq = *reinterpret_cast<const int4 *>(qr + 128 * sb);
+                const int4 m = mr[sb];
+                const int8_t * xs = a.q + 256 * sb;
+                const int4 xa = *reinterpret_cast<const int4 *>(xs + offA);
+                const int4 xb = *reinterpret_cast<const int4 *>(xs + offB);
+                int sA = dp4a_us((unsigned) wq.x & maskA, xa.x, 0);
+                int sB = dp4a_us((unsigned) wq.x & maskB, xb.x, 0);
+                sA = dp4a_us((unsigned) wq.y & maskA, xa.y, sA);
+                sB = dp4a_us((unsigned) wq.y & maskB, xb.y, sB);
+                sA = dp4a_us((unsigned) wq.z & maskA, xa.z, sA);
+                sB = dp4a_us((unsigned) wq.z & maskB, xb.z, sB);
+                sA = dp4a_us((unsigned) wq.w & maskA, xa.w, sA);
+                sB = dp4a_us((unsigned) wq.w & maskB, xb.w, sB);
+                const int il = swap ? sB : sA;
+                const int ih = (swap ? sA : sB) >> 4;  // exact: every term of the high-nibble sum is a multiple of 16
+                const unsigned my = (unsigned) m.y, mz = (unsigned) m.z, mw = (unsigned) m.w;
+                const unsigned srcs = swap ? mw : my, srcm = swap ? (mw >> 4) : mz;
+                const int sc0 = (int) (bfe_u32(srcs, sh0, lenlo) | ((my >> (sh0 + 2u)) & himask));
+                const int sc1 = (int) (bfe_u32(srcs, sh1, lenlo) | ((my >> (sh1 + 2u)) & himask));
+                const int mn0 = (int) (bfe_u32(srcm, sh0, lenlo) | ((mz >> (sh0 + 2u)) & himask));
+                const int mn1 = (int) (bfe_u32(srcm, sh1, lenlo) | ((mz >> (sh1 + 2u)) & himask));
+                const int si = sc0 * il + sc1 * ih;
+                const int16_t * bs = a.bs + 16 * sb;
+                const int sm = mn0 * (int) bs[bs0] + mn1 * (int) bs[bs1];
+                const float dx = a.d[sb];
+                const float dw = __half2float(__ushort_as_half((unsigned short) ((unsigned) m.x & 0xFFFFu)));
+                const float dmw = __half2float(__ushort_as_half((unsigned short) ((unsigned) m.x >> 16)));
+                acc += __fmul_rn(dx, dw) * (float) si;
+                acc -= __fmul_rn(dx, dmw) * (float) sm;
+            }
+        }
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (j < rows && li == 0) store(j, acc);
+    }
+}
+
+// Lanes per row: 8 for rows of up to 64 units (a warp reduces 4 rows at once), 32 for longer rows; Q4_K: its own
+// 16-lane form. A function of K alone, so a row's summation order does not depend on how rows are chunked (launch
+// geometry never changes results).
 template <class T, class Store>
 __device__ __forceinline__ void smem_rows(const uint8_t * const * f, int64_t K, int rows, const Act & a, const WeightView & w,
                                           int warp, int nwarps, Store store) {
-    if (T::units_per_row(K) <= 64) smem_rows_lpr<T, 8>(f, K, rows, a, w, warp, nwarps, store);
+    if constexpr (std::is_same<T, TQ4_K>::value) smem_rows_q4k(f, K, rows, a, warp, nwarps, store);
+    else if (T::units_per_row(K) <= 64) smem_rows_lpr<T, 8>(f, K, rows, a, w, warp, nwarps, store);
     else smem_rows_lpr<T, 32>(f, K, rows, a, w, warp, nwarps, store);
 }
 
-template <class T, int NC>
-__global__ void __launch_bounds__(kTmaThreads, 2) gemv_tma_kernel(GemvParams p) {
+// CW consumer warps: 8 (two CTAs per SM fit, for chains whose next product's CTA should start beside this one) or 16
+// (one CTA per SM: twice the warps to hide the reduction's shared-memory and dp4a latencies). Ring slot s belongs to
+// the group of CW / 8 warps g = s % 8, which splits each of the slot's chunks by rows.
+template <class T, int NC, int CW>
+__global__ void __launch_bounds__(32 * (CW + 1), CW == kTmaConsumerWarps ? 2 : 1) gemv_tma_kernel(GemvParams p) {
+    static_assert(CW % kTmaConsumerWarps == 0, "consumer warps come in groups of one warp per ring slot owner");
+    constexpr int kGroup = CW / kTmaConsumerWarps;  // warps per slot owner
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t K = p.w.K;
@@ -116,13 +205,13 @@ __global__ void __launch_bounds__(kTmaThreads, 2) gemv_tma_kernel(GemvParams p) 
     if (threadIdx.x == 0) {
         for (int s = 0; s < stages; s++) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);  // released by the one warp that consumed it
+            mbar_init(&empty[s], kGroup);  // released by each warp of the group that consumed it
         }
         fence_mbar_init();
     }
     __syncthreads();
 
-    if (warp == kTmaConsumerWarps) {
+    if (warp == CW) {
         // ---- producer ----
         if (lane == 0) {
             const uint8_t * fb[4] = {p.w.f0, p.w.f1, p.w.f2, p.w.f3};
@@ -149,7 +238,8 @@ __global__ void __launch_bounds__(kTmaThreads, 2) gemv_tma_kernel(GemvParams p) 
         return;
     }
 
-    // ---- consumers (threads 0 .. 255) ----
+    // ---- consumers (threads 0 .. 32 CW - 1); the first 256 stage the activations (the same reduction order at
+    // every CW, so the consumer count never changes results) ----
     const int nthr = 32 * kTmaConsumerWarps;
     pdl_launch_dependents();
     pdl_wait();
@@ -173,16 +263,21 @@ __global__ void __launch_bounds__(kTmaThreads, 2) gemv_tma_kernel(GemvParams p) 
     }
     const int nc = p.ncols < NC ? p.ncols : NC;
     float * xs = reinterpret_cast<float *>(act_base + act_base_bytes(p.w.type, K, NC));
-    if (NC == 1 && !p.aq && single_fast(K)) stage_one(p, a, kind, nc > 0 ? column_src(p, 0) : p.x, xs, xs + 2 * K, nthr);
-    else stage_activations<NC>(p, a, kind, 0, nc, nthr);
+    if (warp < kTmaConsumerWarps) {
+        if (NC == 1 && !p.aq && single_fast(K)) stage_one(p, a, kind, nc > 0 ? column_src(p, 0) : p.x, xs, xs + 2 * K, nthr);
+        else stage_activations<NC>(p, a, kind, 0, nc, nthr);
+    }
+    if constexpr (CW > kTmaConsumerWarps) asm volatile("bar.sync 2, %0;" ::"n"(32 * CW) : "memory");
 
     const int64_t upr = T::units_per_row(K);
     const int nsums = T::sums_per_row(K);
-    // chunk c belongs to consumer warp c % W (W = min(8, stages); the host makes stages a multiple of W), so every
-    // ring slot is consumed by one warp, which waits for the slot's phases strictly in order (a parity wait cannot
-    // tell phase n from phase n + 2: a slot shared between warps could be taken a phase early)
+    // chunk c belongs to warp group c % W (W = min(8, stages); the host makes stages a multiple of W), so every ring
+    // slot is consumed by one group, whose warps each wait for the slot's phases strictly in order. A parity wait cannot
+    // tell phase n from phase n + 2, but a slot's phase n + 1 needs every warp of its group to have released phase n,
+    // so no warp of the group can be more than one phase ahead.
     const int W = stages < kTmaConsumerWarps ? stages : kTmaConsumerWarps;
-    for (int64_t c = warp; warp < W && c < nchunks; c += W) {
+    const int grp = warp % kTmaConsumerWarps, member = warp / kTmaConsumerWarps;
+    for (int64_t c = grp; grp < W && c < nchunks; c += W) {
         const int s = (int) (c % stages);
         if (!mbar_wait(&full[s], (uint32_t) ((c / stages) & 1))) {
             if (lane == 0) atomicOr(p.err, kDevErrTimeout);
@@ -199,14 +294,14 @@ __global__ void __launch_bounds__(kTmaThreads, 2) gemv_tma_kernel(GemvParams p) 
         }
         const int64_t base = r_begin + c * rps;
         if (NC == 1 && !p.sums) {
-            smem_rows<T>(f, K, (int) rows, a, p.w, 0, 1, [&](int j, float v) {
+            smem_rows<T>(f, K, (int) rows, a, p.w, member, kGroup, [&](int j, float v) {
                 if (nc > 0) {
                     const int64_t r = base + j;
                     p.y[r] = p.res ? __fadd_rn(p.res[r], v) : v;
                 }
             });
         } else {
-            for (int64_t j = 0; j < rows; j++) {
+            for (int64_t j = member; j < rows; j += kGroup) {
                 const int64_t r = base + j;  // output row
                 int32_t * sums = p.sums ? p.sums + r * nsums : nullptr;
                 float acc[NC];

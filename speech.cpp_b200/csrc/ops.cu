@@ -348,9 +348,30 @@ static cudaError_t launch_one(const GemvParams & p, int grid_y, cudaStream_t st,
 }
 
 // TMA-streamed launch (gemv_tma.cuh): grid and ring geometry.
+template <class T, int NC, int CW>
+static cudaError_t launch_tma_cw(const GemvParams & p, int64_t gx, size_t smem, cudaStream_t st, bool pdl) {
+    auto kern = gemv_tma_kernel<T, NC, CW>;
+    static int configured = 0;
+    if ((int) smem > configured) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+        if (e != cudaSuccess) return e;
+        configured = 220 * 1024;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned) gx, 1, 1);
+    cfg.blockDim = dim3(32 * (CW + 1), 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
 template <class T, int NC>
 static cudaError_t launch_tma(const GemvParams & p0, cudaStream_t st, bool pdl, int num_sms, int cap_per_sm) {
-    auto kern = gemv_tma_kernel<T, NC>;
     GemvParams p = p0;
     const int64_t K = p.w.K;
     const int64_t row_bytes = tma_row_bytes<T>(K);
@@ -387,23 +408,13 @@ static cudaError_t launch_tma(const GemvParams & p0, cudaStream_t st, bool pdl, 
     p.stages = (int) stages;
     const size_t smem = tma_smem_bytes<T, NC>(p.w.type, K, (int) rps, (int) stages);
     if (smem > 220 * 1024) return cudaErrorInvalidValue;
-    static int configured = 0;
-    if ((int) smem > configured) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-        if (e != cudaSuccess) return e;
-        configured = 220 * 1024;
+    // one CTA per SM: 16 consumer warps (single column; measured faster for the large HBM-bound products);
+    // B200_TMA_WARPS=8 keeps 8 (tuning)
+    static const int env_warps = [] { const char * e = getenv("B200_TMA_WARPS"); return e ? atoi(e) : 16; }();
+    if constexpr (NC == 1) {
+        if (per_sm == 1 && env_warps == 16) return launch_tma_cw<T, NC, 2 * kTmaConsumerWarps>(p, gx, smem, st, pdl);
     }
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned) gx, 1, 1);
-    cfg.blockDim = dim3(kTmaThreads, 1, 1);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, kern, p);
+    return launch_tma_cw<T, NC, kTmaConsumerWarps>(p, gx, smem, st, pdl);
 }
 
 template <class T, int NC>
