@@ -139,11 +139,13 @@ b200_status mul_mat_impl(b200_context * ctx, const b200_weight * w, int64_t row0
     if (M <= maxnc) {
         // Few columns: one GEMV launch. Launched with programmatic dependent launch (its CTAs start streaming weights
         // while the previous kernel finishes; activations are read after griddepcontrol.wait), except right after an
-        // upload; a product of at most 64 MB of weights runs two CTAs per SM so the next launch's CTAs fit beside.
+        // upload; a product of at most 64 MB of weights leaves room on every SM for the next launch's CTAs (up to 16 MB:
+        // one CTA per SM with a half-size ring; up to 64 MB: two such CTAs per SM).
         p.ncols = (int) M;
         const bool pdl = !ctx->upload_pending;
-        const bool small = (double) n * (double) w->nbytes / (double) (w->ne1 * w->ne2) <= 64.0 * 1024 * 1024;
-        CK(ctx, launch_gemv(p, pow2_at_least(M), 1, ctx->stream, pdl, ctx->num_sms, small ? 2 : 0));
+        const double bytes = (double) n * (double) w->nbytes / (double) (w->ne1 * w->ne2);
+        const int cap = bytes <= 16.0 * 1024 * 1024 ? 3 : bytes <= 64.0 * 1024 * 1024 ? 2 : 0;
+        CK(ctx, launch_gemv(p, pow2_at_least(M), 1, ctx->stream, pdl, ctx->num_sms, cap));
         ctx->upload_pending = false;
         return B200_OK;
     }

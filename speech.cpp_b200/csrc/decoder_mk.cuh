@@ -49,12 +49,16 @@ struct MkStage {
 };
 
 // Phase timestamps for latency studies (clock64 of the CTA's thread 0 / producer lane), compiled in only with
-// -DB200_MK_PROBE: probe[cta][product][8].
+// -DB200_MK_PROBE: probe[cta][product][8], slots 0/1 product start, 7 inputs ready, 2 staged, 3 first weight chunk
+// landed, 5 thread 0's rows done, 4 every consumer warp done, 6 producer issued the product's first chunk.
 #ifdef B200_MK_PROBE
 #define MK_PROBE(slot) \
     do { if (P.probe) P.probe[((size_t) blockIdx.x * P.nstages + s) * 8 + (slot)] = clock64(); } while (0)
+__shared__ long long mk_probe_ready;  // thread 0's clock when its input loads were all ready
+#define MK_PROBE_READY() do { if (threadIdx.x == 0) mk_probe_ready = clock64(); } while (0)
 #else
 #define MK_PROBE(slot) do { } while (0)
+#define MK_PROBE_READY() do { } while (0)
 #endif
 
 struct MkParams {
@@ -216,6 +220,7 @@ __device__ __forceinline__ int mk_stage_input(const MkStage & S, const Act & a, 
                 }
             }
         }
+        MK_PROBE_READY();
 #pragma unroll
         for (int i = 0; i < kMax; i++)
             if (i < K / 2048)
@@ -272,6 +277,7 @@ __device__ __forceinline__ int mk_stage_input(const MkStage & S, const Act & a, 
                 }
             }
         }
+        MK_PROBE_READY();
 #pragma unroll
         for (int i = 0; i < kMax; i++) {
             if (i < K / 1024) {
@@ -327,6 +333,16 @@ __device__ __forceinline__ int mk_stage_input(const MkStage & S, const Act & a, 
 
 constexpr int kMkResRows = 64;  // residual values of a CTA's slice kept in shared memory (more: read from L2)
 
+// Output row r of product S: value v (+ the residual), one {value, tag} word when tagged.
+__device__ __forceinline__ void mk_store(const MkStage & S, int64_t r, int64_t r0, const float * res_s, float v, unsigned tag) {
+    float out = v;
+    if (S.res) out = __fadd_rn(r - r0 < kMkResRows ? res_s[r - r0] : __ldcg(S.res + (S.res_tagged ? 2 * r : r)), v);
+    if (S.y_tagged)
+        asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(S.y + 2 * r), "r"(__float_as_uint(out)), "r"(tag) : "memory");
+    else
+        S.y[r] = out;
+}
+
 // Rows of one landed chunk, two per warp at a time. res_s holds the residuals of the CTA's rows [r0, r0 + 64).
 template <class T>
 __device__ __forceinline__ void mk_rows(const MkStage & S, const Act & a, const uint8_t * slot, int64_t rps, int64_t rows,
@@ -339,17 +355,7 @@ __device__ __forceinline__ void mk_rows(const MkStage & S, const Act & a, const 
         f[i] = b;
         if (i < T::kFields) b += rps * T::field_row_bytes(K, i);
     }
-    smem_rows<T>(f, K, (int) rows, a, S.w, warp, kMkConsumerWarps, [&](int j, float v) {
-        {
-            const int64_t r = first + j;
-            float out = v;
-            if (S.res) out = __fadd_rn(r - r0 < kMkResRows ? res_s[r - r0] : __ldcg(S.res + (S.res_tagged ? 2 * r : r)), v);
-            if (S.y_tagged)
-                asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(S.y + 2 * r), "r"(__float_as_uint(out)), "r"(tag) : "memory");
-            else
-                S.y[r] = out;
-        }
-    });
+    smem_rows<T>(f, K, (int) rows, a, S.w, warp, kMkConsumerWarps, [&](int j, float v) { mk_store(S, first + j, r0, res_s, v, tag); });
 }
 
 template <class T>
@@ -453,6 +459,9 @@ __global__ void __launch_bounds__(kMkThreads, 1) decoder_mk_kernel(MkParams P) {
             break;
         }
         if (threadIdx.x == 0) MK_PROBE(2);
+#ifdef B200_MK_PROBE
+        if (threadIdx.x == 0 && P.probe) P.probe[((size_t) blockIdx.x * P.nstages + s) * 8 + 7] = mk_probe_ready;
+#endif
         // the descriptor after next goes to the third buffer (this one, s % 3, stays readable during product s)
         if (s + 2 < P.nstages && threadIdx.x < kDescWords)
             cp_async4(reinterpret_cast<uint32_t *>(&desc[(s + 2) % 3]) + threadIdx.x, reinterpret_cast<const uint32_t *>(&P.stages[s + 2]) + threadIdx.x);
@@ -477,6 +486,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decoder_mk_kernel(MkParams P) {
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
         }
+        if (threadIdx.x == 0) MK_PROBE(5);
         cp_async_wait_all();  // the next descriptor has landed
         mk_sync();  // all outputs of this CTA for product s are written; the act arrays may be reused
         if (threadIdx.x == 0) MK_PROBE(4);
