@@ -397,7 +397,10 @@ def config3_decode(pkg, ctx, stream, steps=128):
     return out
 
 
-def large_gemv(pkg, ctx, stream, reps=20):
+GEMV_CASES = ("q8_0", "q4_k", "q6_k_head_asr17")
+
+
+def large_gemv(pkg, ctx, stream, reps=20, warmup=3, only=None):
     """Weight GB/s of single large products (matrices far larger than L2), one launch each, CUDA events on the
     context stream: the HBM-bound GEMV kernels without the decode step's dependency chain."""
     import ctypes
@@ -409,6 +412,8 @@ def large_gemv(pkg, ctx, stream, reps=20):
              ("q6_k_head_asr17", pkg.Q6_K, 2048, 151936)]
     g = torch.Generator(device="cuda").manual_seed(3)
     for name, t, K, N in cases:
+        if only and name != only:
+            continue
         w = ctx.weight(t, K, N)
         for r0 in range(0, N, 16384):  # quantize in pieces (device-side, bit-identical to the oracle's quantizer)
             rows = min(16384, N - r0)
@@ -421,7 +426,7 @@ def large_gemv(pkg, ctx, stream, reps=20):
         y = torch.empty((1, N), device="cuda")
         ctx.synchronize()
         call = lambda: ctx.check(ctx.L.b200_mul_mat(ctx.h, ctypes.byref(w), ctypes.c_void_p(x.data_ptr()), 1, ctypes.c_void_p(y.data_ptr())))
-        for _ in range(3):
+        for _ in range(warmup):
             call()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
@@ -808,6 +813,21 @@ def run_b200(args):
 
     pkg = load_package()
     ctx = pkg.Context(local)
+    if args.workload == "gemv":
+        # one large single-column product (profiling and tuning of the HBM-bound GEMV kernel): --steps timed launches
+        # after --warmup untimed ones
+        r = large_gemv(pkg, ctx, ctx.torch_stream(), reps=max(args.steps, 1), warmup=args.warmup, only=args.gemv_case)
+        peak, kind = peaks()
+        v = r[args.gemv_case]
+        emit({"metric": "weight GB/s of one large single-column product (TMA GEMV)", "value": v["gbs"], "unit": "GB/s",
+              "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": v["us"] / 1000.0,
+              "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 x q8",
+              "data": "synthetic", "config": {"workload": f"single product {args.gemv_case}", "K": v["K"], "N": v["N"],
+                                              "l2": "weights > 126 MB L2"},
+              "roofline": {"bound": "hbm", "achieved": v["gbs"], "peak": peak, "unit": "GB/s", "frac": v["gbs"] / peak,
+                           "peak_source": kind}})
+        ctx.close()
+        return 0
     if args.workload in ("moe", "batched", "prefill"):
         res = {"moe": run_moe, "batched": run_batched, "prefill": run_prefill}[args.workload](args, pkg, ctx, dist, world, rank, local)
         ctx.close()
@@ -959,9 +979,11 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-configs", action="store_true", help="skip the config 1 and config 3 side measurements")
-    ap.add_argument("--workload", default="decode", choices=["decode", "moe", "batched", "prefill"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "moe", "batched", "prefill", "gemv"],
                     help="decode: config 2 decode step (the headline line); moe: config 5 MoE FFN stack, expert-parallel; "
-                         "batched: config 4 product stack, column-split; prefill: config 3 prefill")
+                         "batched: config 4 product stack, column-split; prefill: config 3 prefill; gemv: one large "
+                         "single-column product (--gemv-case)")
+    ap.add_argument("--gemv-case", default="q8_0", choices=list(GEMV_CASES), help="product of --workload gemv")
     ap.add_argument("--moe-steps", type=int, default=20, help="timed steps of the MoE and batched workloads")
     ap.add_argument("--moe-layers", type=int, default=48, help="MoE layers per step (48 = config 5; fewer only for profiling)")
     ap.add_argument("--moe-combine", default="peer", choices=["peer", "nccl"],
