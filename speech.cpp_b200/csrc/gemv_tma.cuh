@@ -100,50 +100,64 @@ __device__ __forceinline__ unsigned bfe_u32(unsigned v, unsigned pos, unsigned l
     return d;
 }
 
-// Q4_K rows from shared memory, single column: 16 lanes per row, two rows per warp pass. Lane li of a row takes the
-// super-blocks sb = e, e + 2, ... (e = li / 8) and, in each, the 16-byte piece p = li % 8 of its 128 quant bytes:
-// with g = p / 2 and h = p % 2, the piece's low nibbles are values [16h, 16h + 16) of sub-block 2g and its high nibbles
-// the same values of sub-block 2g + 1. Eight lanes read one super-block's 128 contiguous quant bytes, and lanes with
-// g >= 2 load the high sub-block's activations first, so every 128-bit shared load of an 8-lane phase touches 32
-// distinct banks. Per piece the int32 sums are exact (dp4a; high nibbles are masked in place and their sum, a multiple
-// of 16, is shifted down exactly), scaled by the sub-blocks' 6-bit scales and mins as integers (ggml's sumi and summ
-// restricted to the piece), then accumulated in float32 with the super-block's dx * d and dx * dmin.
+// Q4_K rows from shared memory, single column, by 32-byte chunks: 16 lanes per row, two rows per warp pass. Lane li
+// of a row takes chunk g = li % 4 of the super-blocks sb = e, e + 4, ... (e = li / 4): the chunk's low nibbles are the
+// 32 values of sub-block 2g and its high nibbles those of sub-block 2g + 1, so a lane forms both sub-blocks' exact int32
+// sums (dp4a; high nibbles masked in place, their sum a multiple of 16 shifted down exactly), applies their 6-bit scales
+// and mins as integers (ggml's sumi and summ restricted to the chunk), then one float32 step with the super-block's
+// dx * d and dx * dmin. Each chunk is read as two 16-byte halves, odd super-blocks' lanes taking the second half
+// first, and lanes with g >= 2 read the high sub-block's activations first: every 128-bit shared load of an 8-lane
+// phase then touches 32 distinct banks.
 template <class Store>
 __device__ __forceinline__ void smem_rows_q4k(const uint8_t * const * f, int64_t K, int rows, const Act & a, int warp,
                                               int nwarps, Store store) {
     const int lane = threadIdx.x & 31;
-    const int sub = lane >> 4, li = lane & 15, e = li >> 3, p = li & 7, g = p >> 1, h = p & 1;
+    const int sub = lane >> 4, li = lane & 15, g = li & 3, e = li >> 2, h1 = e & 1, h2 = h1 ^ 1;
     const int nsb = (int) (K / 256);
-    const bool swap = g >= 2;  // this lane's first activation load is the high sub-block's
+    const bool swap = g >= 2;  // this lane reads the high sub-block's activations first
     const unsigned maskA = swap ? 0xF0F0F0F0u : 0x0F0F0F0Fu, maskB = ~maskA;
-    const int offA = 64 * g + 16 * h + (swap ? 32 : 0), offB = 64 * g + 16 * h + (swap ? 0 : 32);
+    const int xoA = 64 * g + (swap ? 32 : 0), xoB = 64 * g + (swap ? 0 : 32);
     // 6-bit scale / min of sub-blocks 2g and 2g + 1 from meta words y (scale bytes 0..3), z (4..7), w (8..11):
     // j < 4: byte j of y / z; j >= 4: low four bits from byte j - 4 of w (scale: low nibble, min: high nibble), top
     // two bits from bits 6..7 of byte j - 4 of y / z
     const unsigned sh0 = 8u * (unsigned) ((2 * g) & 3), sh1 = sh0 + 8u;
     const unsigned lenlo = swap ? 4u : 6u, himask = swap ? 0x30u : 0u;
-    const int bs0 = 4 * g + h, bs1 = 4 * g + 2 + h;  // 16-value activation sums of the two halves this piece covers
     for (int j0 = warp * 2; j0 < rows; j0 += nwarps * 2) {
         const int j = j0 + sub;
         float acc = 0.0f;
         if (j < rows) {
-            const uint8_t * qr = f[0] + (size_t) j * (size_t) (K / 2) + 16 * p;
+            const uint8_t * qr = f[0] + (size_t) j * (size_t) (K / 2) + 32 * g;
             const int4 * mr = reinterpret_cast<const int4 *>(f[1]) + (size_t) j * nsb;
 #pragma unroll 2
-            for (int sb = e; sb < nsb; sb += 2) {
-                const int4 wq = *reinterpret_cast<const int4 *>(qr + 128 * sb);
-                const int4 m = mr[sb];
+            for (int sb = e; sb < nsb; sb += 4) {
+                const uint8_t * q = qr + 128 * sb;
                 const int8_t * xs = a.q + 256 * sb;
-                const int4 xa = *reinterpret_cast<const int4 *>(xs + offA);
-                const int4 xb = *reinterpret_cast<const int4 *>(xs + offB);
-                int sA = dp4a_us((unsigned) wq.x & maskA, xa.x, 0);
-                int sB = dp4a_us((unsigned) wq.x & maskB, xb.x, 0);
-                sA = dp4a_us((unsigned) wq.y & maskA, xa.y, sA);
-                sB = dp4a_us((unsigned) wq.y & maskB, xb.y, sB);
-                sA = dp4a_us((unsigned) wq.z & maskA, xa.z, sA);
-                sB = dp4a_us((unsigned) wq.z & maskB, xb.z, sB);
-                sA = dp4a_us((unsigned) wq.w & maskA, xa.w, sA);
-                sB = dp4a_us((unsigned) wq.w & maskB, xb.w, sB);
+                const int4 w1 = *reinterpret_cast<const int4 *>(q + 16 * h1);
+                const int4 w2 = *reinterpret_cast<const int4 *>(q + 16 * h2);
+                const int4 a1 = *reinterpret_cast<const int4 *>(xs + xoA + 16 * h1);
+                const int4 b1 = *reinterpret_cast<const int4 *>(xs + xoB + 16 * h1);
+                const int4 a2 = *reinterpret_cast<const int4 *>(xs + xoA + 16 * h2);
+                const int4 b2 = *reinterpret_cast<const int4 *>(xs + xoB + 16 * h2);
+                const int4 m = mr[sb];
+                const int * bs2 = reinterpret_cast<const int *>(a.bs + 16 * sb);
+                const int p0 = bs2[2 * g], p1 = bs2[2 * g + 1];  // 16-value sums of sub-blocks 2g and 2g + 1, in pairs
+                const float dx = a.d[sb];
+                int sA = dp4a_us((unsigned) w1.x & maskA, a1.x, 0);
+                int sB = dp4a_us((unsigned) w1.x & maskB, b1.x, 0);
+                sA = dp4a_us((unsigned) w1.y & maskA, a1.y, sA);
+                sB = dp4a_us((unsigned) w1.y & maskB, b1.y, sB);
+                sA = dp4a_us((unsigned) w1.z & maskA, a1.z, sA);
+                sB = dp4a_us((unsigned) w1.z & maskB, b1.z, sB);
+                sA = dp4a_us((unsigned) w1.w & maskA, a1.w, sA);
+                sB = dp4a_us((unsigned) w1.w & maskB, b1.w, sB);
+                sA = dp4a_us((unsigned) w2.x & maskA, a2.x, sA);
+                sB = dp4a_us((unsigned) w2.x & maskB, b2.x, sB);
+                sA = dp4a_us((unsigned) w2.y & maskA, a2.y, sA);
+                sB = dp4a_us((unsigned) w2.y & maskB, b2.y, sB);
+                sA = dp4a_us((unsigned) w2.z & maskA, a2.z, sA);
+                sB = dp4a_us((unsigned) w2.z & maskB, b2.z, sB);
+                sA = dp4a_us((unsigned) w2.w & maskA, a2.w, sA);
+                sB = dp4a_us((unsigned) w2.w & maskB, b2.w, sB);
                 const int il = swap ? sB : sA;
                 const int ih = (swap ? sA : sB) >> 4;  // exact: every term of the high-nibble sum is a multiple of 16
                 const unsigned my = (unsigned) m.y, mz = (unsigned) m.z, mw = (unsigned) m.w;
@@ -153,9 +167,7 @@ __device__ __forceinline__ void smem_rows_q4k(const uint8_t * const * f, int64_t
                 const int mn0 = (int) (bfe_u32(srcm, sh0, lenlo) | ((mz >> (sh0 + 2u)) & himask));
                 const int mn1 = (int) (bfe_u32(srcm, sh1, lenlo) | ((mz >> (sh1 + 2u)) & himask));
                 const int si = sc0 * il + sc1 * ih;
-                const int16_t * bs = a.bs + 16 * sb;
-                const int sm = mn0 * (int) bs[bs0] + mn1 * (int) bs[bs1];
-                const float dx = a.d[sb];
+                const int sm = mn0 * ((int) (int16_t) (p0 & 0xFFFF) + (p0 >> 16)) + mn1 * ((int) (int16_t) (p1 & 0xFFFF) + (p1 >> 16));
                 const float dw = __half2float(__ushort_as_half((unsigned short) ((unsigned) m.x & 0xFFFFu)));
                 const float dmw = __half2float(__ushort_as_half((unsigned short) ((unsigned) m.x >> 16)));
                 acc += __fmul_rn(dx, dw) * (float) si;
