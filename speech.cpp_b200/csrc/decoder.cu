@@ -52,6 +52,7 @@ struct b200_decoder {
     uint2 * t_qkv = nullptr;  // q|k|v outputs,
     uint2 * t_gu = nullptr;   // gate|up outputs
     int mk_n = 0;
+    bool mk_forms = false;  // some product has K-quant weights: the instantiation with their row forms
 };
 
 namespace {
@@ -217,7 +218,10 @@ b200_status prepare_mk(b200_decoder * d, const std::vector<GemvParams> & v) {
     DCK(d, cudaMalloc(&d->mk_stages, sizeof(MkStage) * st.size()));
     DCK(d, cudaMemcpy(d->mk_stages, st.data(), sizeof(MkStage) * st.size(), cudaMemcpyHostToDevice));
     d->mk_n = (int) st.size();
-    DCK(d, cudaFuncSetAttribute(decoder_mk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) kMkSmemBytes));
+    d->mk_forms = false;
+    for (const GemvParams & p : v) d->mk_forms |= p.w.type == B200_TYPE_Q4_K || p.w.type == B200_TYPE_Q6_K;
+    auto kern = d->mk_forms ? decoder_mk_kernel<true> : decoder_mk_kernel<false>;
+    DCK(d, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) kMkSmemBytes));
     return B200_OK;
 }
 
@@ -242,7 +246,7 @@ b200_status enqueue_mk(b200_decoder * d) {
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    DCK(d, cudaLaunchKernelEx(&cfg, decoder_mk_kernel, P));
+    DCK(d, cudaLaunchKernelEx(&cfg, d->mk_forms ? decoder_mk_kernel<true> : decoder_mk_kernel<false>, P));
     d->launches = 1;
     return B200_OK;
 }

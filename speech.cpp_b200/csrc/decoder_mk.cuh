@@ -344,7 +344,7 @@ __device__ __forceinline__ void mk_store(const MkStage & S, int64_t r, int64_t r
 }
 
 // Rows of one landed chunk, two per warp at a time. res_s holds the residuals of the CTA's rows [r0, r0 + 64).
-template <class T>
+template <class T, bool kForms>
 __device__ __forceinline__ void mk_rows(const MkStage & S, const Act & a, const uint8_t * slot, int64_t rps, int64_t rows,
                                         int64_t first, int64_t r0, const float * res_s, unsigned tag) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -355,7 +355,10 @@ __device__ __forceinline__ void mk_rows(const MkStage & S, const Act & a, const 
         f[i] = b;
         if (i < T::kFields) b += rps * T::field_row_bytes(K, i);
     }
-    smem_rows<T>(f, K, (int) rows, a, S.w, warp, kMkConsumerWarps, [&](int j, float v) { mk_store(S, first + j, r0, res_s, v, tag); });
+    auto store = [&](int j, float v) { mk_store(S, first + j, r0, res_s, v, tag); };
+    if constexpr (kForms) smem_rows<T>(f, K, (int) rows, a, S.w, warp, kMkConsumerWarps, store);
+    else if (T::units_per_row(K) <= 64) smem_rows_lpr<T, 8>(f, K, (int) rows, a, S.w, warp, kMkConsumerWarps, store);
+    else smem_rows_lpr<T, 32>(f, K, (int) rows, a, S.w, warp, kMkConsumerWarps, store);
 }
 
 template <class T>
@@ -369,6 +372,11 @@ __device__ __forceinline__ void mk_issue(const MkStage & S, uint8_t * slot, int6
     }
 }
 
+// kForms: the K-quant rows use their own lane layouts (smem_rows) rather than the generic unit reduction. The two
+// instantiations differ only there, but register allocation is per kernel: a step whose products are all Q8_0 runs
+// the generic one (measured on B200, config 2 step: 495 us against 552 us with the K-quant forms compiled in), a step
+// with K-quant products the other (config 3 step: 845 us against 890 us).
+template <bool kForms>
 __global__ void __launch_bounds__(kMkThreads, 1) decoder_mk_kernel(MkParams P) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float part[kMkConsumerWarps];
@@ -478,10 +486,10 @@ __global__ void __launch_bounds__(kMkThreads, 1) decoder_mk_kernel(MkParams P) {
             const int64_t rows = r1 - first < rps ? r1 - first : rps;
             const uint8_t * sp = ring + (size_t) slot * kMkSlotBytes;
             switch (S.w.type) {
-            case B200_TYPE_Q8_0: mk_rows<TQ8_0>(S, a, sp, rps, rows, first, r0, res_s, out_tag); break;
-            case B200_TYPE_Q4_K: mk_rows<TQ4_K>(S, a, sp, rps, rows, first, r0, res_s, out_tag); break;
-            case B200_TYPE_Q6_K: mk_rows<TQ6_K>(S, a, sp, rps, rows, first, r0, res_s, out_tag); break;
-            default: mk_rows<TBF16>(S, a, sp, rps, rows, first, r0, res_s, out_tag); break;
+            case B200_TYPE_Q8_0: mk_rows<TQ8_0, kForms>(S, a, sp, rps, rows, first, r0, res_s, out_tag); break;
+            case B200_TYPE_Q4_K: mk_rows<TQ4_K, kForms>(S, a, sp, rps, rows, first, r0, res_s, out_tag); break;
+            case B200_TYPE_Q6_K: mk_rows<TQ6_K, kForms>(S, a, sp, rps, rows, first, r0, res_s, out_tag); break;
+            default: mk_rows<TBF16, kForms>(S, a, sp, rps, rows, first, r0, res_s, out_tag); break;
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
