@@ -7,12 +7,14 @@
 //   Q6_K: sumi = sum_g sc_g * (sum_l (q_l - 32) x_l) over the 16 groups g of 16 (int8 scales), then
 //         sumf += (d * dx) * sumi.
 // Here the same integers come from the tensor cores. Each weight matrix is expanded once (on the first product with
-// many rows; cached until the weight is written or freed) into int8 values: Q4_K's nibbles as 0..15; Q6_K's q - 32 as
-// two zero-masked 32-value blocks per 32 values ([q_0..q_15, 0 x 16] and [0 x 16, q_16..q_31]), because its scale
-// changes every 16 values while one tcgen05.mma kind::i8 spans K = 32. One MMA (two for Q6_K) of M = 128 weight rows x
-// N = 32 tokens x K = 32 gives exact int32 sums into tensor memory; epilogue warps fold them into int32 super-block
-// sums with the integer scales (and, for Q4_K, the mins times the activations' 32-value sums), and convert once per
-// super-block to float, in super-block order. Pipeline as in the grouped Q8_0 kernel (gemm_tc_grouped.cu): warp 0 =
+// many rows; cached until the weight is written or freed) into int8 values.
+//   Q4_K: three planes with the sub-block scales inside (sc = 8 a + b: a * q, b * q, and the min m at every value), so
+//   three accumulators over a whole super-block (24 MMAs of M = 128 weight rows x N = 32 tokens x K = 32,
+//   accumulating in tensor memory) hold sumi = 8 A0 + A1 and summ = A2 exactly; the epilogue runs once per super-block.
+//   Q6_K: q - 32 as two zero-masked 32-value blocks per 32 values ([q_0..q_15, 0 x 16] and [0 x 16, q_16..q_31]),
+//   because its scale changes every 16 values while one tcgen05.mma kind::i8 spans K = 32; one MMA per half gives the
+//   group's exact int32 sum, and epilogue warps fold the groups into the super-block sum with the integer scales.
+// Either way the epilogue converts once per super-block to float, in super-block order (ggml's float steps). Pipeline as in the grouped Q8_0 kernel (gemm_tc_grouped.cu): warp 0 =
 // TMA producer (no multicast), warp 1 = tensor-memory allocator and MMA issuer, warps 2..9 = epilogue; four
 // accumulator buffers of 2 x 32 columns; every wait bounded.
 #include <unordered_map>
@@ -25,10 +27,13 @@ namespace b200 {
 // ------------------------------------------------------------------------------------------------------------------
 // Expansion
 // ------------------------------------------------------------------------------------------------------------------
-// Q4_K: q int8 [rows][K] (0..15), scm uint16 [rows][K/32] (sc | m << 8), dd float4 [rows][K/256] (d, dmin, 0, 0).
-__global__ void expand_q4k_kernel(WeightView w, int8_t * q, uint16_t * scm, float4 * dd) {
+// Q4_K: three int8 planes q [3][rows][K] and dd float4 [rows][K/256] (d, dmin, 0, 0). With the sub-block's six-bit
+// scale written in base 8, sc = 8 a + b (a, b <= 7), plane 0 holds a * q, plane 1 b * q (q the nibble, 0..15; both
+// <= 105) and plane 2 the sub-block's min m (<= 63) at every value: over a super-block, 8 (plane 0 . x) + (plane 1 . x)
+// is ggml's sumi = sum_s sc_s sum_l q_l x_l and (plane 2 . x) its summ = sum_s m_s sum_l x_l, exactly.
+__global__ void expand_q4k_kernel(WeightView w, int8_t * q, float4 * dd) {
     const int lane = threadIdx.x & 31;
-    const int64_t nsb = w.K / 256, total = w.rows * nsb;
+    const int64_t nsb = w.K / 256, total = w.rows * nsb, plane = w.rows * w.K;
     const int64_t warps = (int64_t) gridDim.x * (blockDim.x >> 5);
     for (int64_t i = (int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); i < total; i += warps) {
         const int64_t r = i / nsb, sb = i % nsb;
@@ -37,18 +42,23 @@ __global__ void expand_q4k_kernel(WeightView w, int8_t * q, uint16_t * scm, floa
         const int s = lane >> 2, l0 = (lane & 3) * 8;  // this lane: values 8 lane .. 8 lane + 7 = sub-block s, l0..
         const uint8_t * src = qs + (s >> 1) * 32 + l0;
         const int shift = (s & 1) * 4;
-        uint32_t lo = 0, hi = 0;
+        int sc, m;
+        TQ4_K::scale_min(meta + 4, s, sc, m);
+        const uint32_t da = (uint32_t) (sc >> 3), db = (uint32_t) (sc & 7);
+        uint32_t a0 = 0, a1 = 0, b0 = 0, b1 = 0;
 #pragma unroll
         for (int j = 0; j < 4; j++) {
-            lo |= (uint32_t) ((src[j] >> shift) & 15) << (8 * j);
-            hi |= (uint32_t) ((src[4 + j] >> shift) & 15) << (8 * j);
+            const uint32_t n0 = (src[j] >> shift) & 15, n1 = (src[4 + j] >> shift) & 15;
+            a0 |= (da * n0) << (8 * j);
+            a1 |= (da * n1) << (8 * j);
+            b0 |= (db * n0) << (8 * j);
+            b1 |= (db * n1) << (8 * j);
         }
-        *reinterpret_cast<uint2 *>(q + r * w.K + sb * 256 + lane * 8) = make_uint2(lo, hi);
-        if (lane < 8) {
-            int sc, m;
-            TQ4_K::scale_min(meta + 4, lane, sc, m);
-            scm[r * (w.K / 32) + sb * 8 + lane] = (uint16_t) (sc | (m << 8));
-        }
+        const uint32_t mm = (uint32_t) m * 0x01010101u;
+        int8_t * dst = q + r * w.K + sb * 256 + lane * 8;
+        *reinterpret_cast<uint2 *>(dst) = make_uint2(a0, a1);
+        *reinterpret_cast<uint2 *>(dst + plane) = make_uint2(b0, b1);
+        *reinterpret_cast<uint2 *>(dst + 2 * plane) = make_uint2(mm, mm);
         if (lane == 0) {
             const float d = __half2float(*reinterpret_cast<const __half *>(meta));
             const float dmin = __half2float(*reinterpret_cast<const __half *>(meta + 2));
@@ -129,20 +139,20 @@ constexpr unsigned kErrTimeout = 4u;
 
 template <int KIND>
 struct KqLayout {
-    static constexpr int kAT = KIND == 6 ? 2 : 1;          // A tiles ([128 rows][128 B], swizzled) per stage
+    static constexpr int kAT = KIND == 6 ? 2 : 3;          // A tiles ([128 rows][128 B], swizzled) per stage
     static constexpr int kA = kAT * kQM * 128;
     static constexpr int kB = kQKB * kQNT * 32;            // activations: [32 rows][128 B] swizzled
-    static constexpr int kSc = kQM * 16;                   // 16-byte box per row of scales (this stage's half)
+    static constexpr int kSc = KIND == 6 ? kQM * 16 : 0;   // Q6_K: 16-byte box per row of scales (this stage's half)
     static constexpr int kDd = kQM * 16;                   // float4 (d, dmin) per row
     static constexpr int kDx = kQNT * 4;                   // the super-block's activation scales
-    static constexpr int kBs = KIND == 4 ? kQKB * kQNT * 4 : 0;  // activation sums of 32 (Q4_K's min term)
-    static constexpr int kStage = (kA + kB + kSc + kDd + kDx + kBs + 1023) & ~1023;
-    static constexpr int kStages = KIND == 4 ? 3 : 2;
+    static constexpr int kStage = (kA + kB + kSc + kDd + kDx + 1023) & ~1023;
+    static constexpr int kStages = 2;
     static constexpr int kTotal = kStages * kStage + 1024 + 1024;
 };
 
 struct KqParams {
     int64_t N, K, row0;
+    int64_t plane_rows;  // Q4_K: rows of one expansion plane (the weight's rows)
     int M;
     int tiles_m, tiles_n;
     float * y;
@@ -210,7 +220,7 @@ __global__ void __launch_bounds__(kQThreads, 2)
                 int m0, nz, live, tn;
                 tile_of(it, m0, nz, live, tn);
                 const int arow = (int) (p.row0 + (int64_t) tn * kQM);
-                const uint32_t bytes = (uint32_t) (L::kA + nz * 128 + L::kSc + L::kDd + L::kDx + L::kBs);
+                const uint32_t bytes = (uint32_t) (L::kA + nz * 128 + L::kSc + L::kDd + L::kDx);
                 for (int st = 0; st < nstage; st++, sg++) {
                     const int s = sg % S, use = sg / S;
                     if (use > 0 && !mbar_wait_sleep(&empty[s], (use - 1) & 1)) {
@@ -222,18 +232,17 @@ __global__ void __launch_bounds__(kQThreads, 2)
                     mbar_arrive_expect_tx(&full[s], bytes);
                     const int kbs = st * kQKB;  // first 32-value block of the stage
                     if (KIND == 4) {
-                        tma_load_2d(base, &tmA, kbs * 32, arow, &full[s]);
+                        for (int pl = 0; pl < 3; pl++)
+                            tma_load_2d(base + pl * kQM * 128, &tmA, kbs * 32, (int) (pl * p.plane_rows) + arow, &full[s]);
                     } else {
                         tma_load_2d(base, &tmA, 2 * kbs * 32, arow, &full[s]);
                         tma_load_2d(base + kQM * 128, &tmA, 2 * kbs * 32 + 128, arow, &full[s]);
                     }
                     for (int r = 0; r < nz / 16; r++) tma_load_2d(base + L::kA + r * 16 * 128, &tmB, kbs * 32, m0 + 16 * r, &full[s]);
                     uint8_t * sc = base + L::kA + L::kB;
-                    if (KIND == 4) tma_load_2d(sc, &tmSc, kbs & ~7, arow, &full[s]);         // 8 (sc | m << 8)
-                    else tma_load_2d(sc, &tmSc, (2 * kbs) & ~15, arow, &full[s]);             // 16 int8 scales
+                    if (KIND == 6) tma_load_2d(sc, &tmSc, (2 * kbs) & ~15, arow, &full[s]);  // 16 int8 scales
                     tma_load_2d(sc + L::kSc, &tmDd, 4 * (kbs / 8), arow, &full[s]);
                     tma_load_2d(sc + L::kSc + L::kDd, &tmDx, m0, kbs / 8, &full[s]);
-                    if (KIND == 4) tma_load_2d(sc + L::kSc + L::kDd + L::kDx, &tmBs, m0, kbs, &full[s]);
                 }
             }
         }
@@ -254,7 +263,29 @@ __global__ void __launch_bounds__(kQThreads, 2)
                     }
                     tc_fence_after();
                     uint8_t * base = smem + s * L::kStage;
-                    constexpr int kPerStage = KIND == 4 ? kQKB / 2 : kQKB;  // buffers per stage
+                    if constexpr (KIND == 4) {
+                        // a super-block is two stages; its three accumulators take one buffer of 3 x 32 columns
+                        const int sbpos = st & 1, buf = g2 % 2, use = g2 / 2;
+                        if (sbpos == 0 && use > 0 && !mbar_wait_sleep(&acc_empty[buf], (use - 1) & 1)) {
+                            atomicOr(p.err, kErrTimeout);
+                            give_up = 1;
+                            break;
+                        }
+                        tc_fence_after();
+                        for (int blk = 0; blk < kQKB; blk++) {
+#pragma unroll
+                            for (int pl = 0; pl < 3; pl++)
+                                mma_i8_acc(tmem + buf * 3 * kQNT + pl * kQNT, smem_desc_sw128(base + pl * kQM * 128, blk),
+                                           smem_desc_sw128(base + L::kA, blk), idesc, (uint32_t) (sbpos | blk));
+                        }
+                        mma_commit(&empty[s]);
+                        if (sbpos == 1) {
+                            mma_commit(&acc_full[buf]);
+                            g2++;
+                        }
+                        continue;
+                    }
+                    constexpr int kPerStage = kQKB;  // Q6_K: buffers per stage
                     for (int u = 0; u < kPerStage; u++, g2++) {
                         const int buf = g2 % kQBufs, use = g2 / kQBufs;
                         if (use > 0 && !mbar_wait_sleep(&acc_empty[buf], (use - 1) & 1)) {
@@ -265,8 +296,8 @@ __global__ void __launch_bounds__(kQThreads, 2)
                         tc_fence_after();
 #pragma unroll
                         for (int jj = 0; jj < 2; jj++) {
-                            const int blk = KIND == 4 ? 2 * u + jj : u;     // 32-value block of the stage
-                            const int e = KIND == 4 ? blk : 2 * u + jj;     // A block (expanded for Q6_K)
+                            const int blk = u;           // 32-value block of the stage
+                            const int e = 2 * u + jj;    // A block (expanded)
                             mma_i8(tmem + buf * 2 * kQNT + jj * kQNT, smem_desc_sw128(base + (e >> 2) * kQM * 128, e & 3),
                                    smem_desc_sw128(base + L::kA, blk), idesc);
                         }
@@ -289,22 +320,60 @@ __global__ void __launch_bounds__(kQThreads, 2)
             const bool has = 16 * h < nz;
             const int live = live_all - 16 * h;
             float acc[16];
-            int isum[16], msum[16];
+            int isum[16];
 #pragma unroll
             for (int i = 0; i < 16; i++) {
                 acc[i] = 0.0f;
                 isum[i] = 0;
-                msum[i] = 0;
             }
             for (int st = 0; st < nstage && !give_up; st++, sg++) {
                 const int s = sg % S;
                 const uint8_t * base = smem + s * L::kStage;
                 const uint8_t * sc = base + L::kA + L::kB;
-                const float4 ddv = reinterpret_cast<const float4 *>(sc + L::kSc)[row];
+                // the stage's (d, dmin) and dx are read only after an accumulator wait: the MMAs that filled it
+                // consumed this stage, so its bulk copies have landed
+                const float4 * ddp = reinterpret_cast<const float4 *>(sc + L::kSc) + row;
                 const float * dx = reinterpret_cast<const float *>(sc + L::kSc + L::kDd);
-                const int * bs = reinterpret_cast<const int *>(sc + L::kSc + L::kDd + L::kDx);
                 const int kbs = st * kQKB;
-                constexpr int kPerStage = KIND == 4 ? kQKB / 2 : kQKB;
+                if constexpr (KIND == 4) {
+                    // the super-block's three accumulators, after its second stage: one integer and one float step
+                    if ((st & 1) == 1) {
+                        const int buf = g2 % 2, use = g2 / 2;
+                        g2++;
+                        if (!mbar_wait_sleep(&acc_full[buf], use & 1)) {
+                            if (lane == 0) atomicOr(p.err, kErrTimeout);
+                            give_up = 1;
+                            break;
+                        }
+                        tc_fence_after();
+                        int va[16], vb[16], vm[16];
+                        if (has) {
+                            const uint32_t ta = tmem + ((uint32_t) (32 * q) << 16) + buf * 3 * kQNT + 16 * h;
+                            tmem_ld16(ta, va);
+                            tmem_ld16(ta + kQNT, vb);
+                            tmem_ld16(ta + 2 * kQNT, vm);
+                            tmem_wait_ld();
+                        }
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&acc_empty[buf]);
+                        if (has) {
+                            const float4 ddv = *ddp;
+#pragma unroll
+                            for (int i = 0; i < 16; i++) {
+                                if (i >= live) break;
+                                const float dxv = dx[16 * h + i];
+                                const int sumi = 8 * va[i] + vb[i];
+                                acc[i] = fmaf(__fmul_rn(dxv, ddv.x), (float) sumi, acc[i]);
+                                acc[i] = fmaf(-__fmul_rn(dxv, ddv.y), (float) vm[i], acc[i]);
+                            }
+                        }
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&empty[s]);
+                    continue;
+                }
+                constexpr int kPerStage = kQKB;
                 for (int u = 0; u < kPerStage; u++, g2++) {
                     const int buf = g2 % kQBufs, use = g2 / kQBufs;
                     if (!mbar_wait_sleep(&acc_full[buf], use & 1)) {
@@ -330,36 +399,22 @@ __global__ void __launch_bounds__(kQThreads, 2)
                             __syncwarp();
                             if (lane == 0) mbar_arrive(&acc_empty[buf]);
                         }
-                        if (KIND == 4) {
-                            const int blk = 2 * u + jj;
-                            const int e = reinterpret_cast<const uint16_t *>(sc)[row * 8 + (kbs & 7) + blk];
-                            const int scv = e & 0xFF, mv = e >> 8;
-                            const int * bsb = bs + blk * kQNT + 16 * h;
+                        const int scv = reinterpret_cast<const int8_t *>(sc)[row * 16 + ((2 * kbs) & 15) + 2 * u + jj];
 #pragma unroll
-                            for (int i = 0; i < 16; i++) {
-                                if (i >= live) break;
-                                isum[i] += scv * v[i];
-                                msum[i] += mv * bsb[i];
-                            }
-                        } else {
-                            const int scv = reinterpret_cast<const int8_t *>(sc)[row * 16 + ((2 * kbs) & 15) + 2 * u + jj];
-#pragma unroll
-                            for (int i = 0; i < 16; i++) {
-                                if (i >= live) break;
-                                isum[i] += scv * v[i];
-                            }
+                        for (int i = 0; i < 16; i++) {
+                            if (i >= live) break;
+                            isum[i] += scv * v[i];
                         }
                     }
                 }
                 if (has && !give_up && ((kbs + kQKB) & 7) == 0) {  // end of a super-block: one float step, in order
+                    const float4 ddv = *ddp;
 #pragma unroll
                     for (int i = 0; i < 16; i++) {
                         if (i >= live) break;
                         const float dxv = dx[16 * h + i];
                         acc[i] = fmaf(__fmul_rn(dxv, ddv.x), (float) isum[i], acc[i]);
-                        if (KIND == 4) acc[i] = fmaf(-__fmul_rn(dxv, ddv.y), (float) msum[i], acc[i]);
                         isum[i] = 0;
-                        msum[i] = 0;
                     }
                 }
                 __syncwarp();
@@ -391,7 +446,7 @@ __global__ void __launch_bounds__(kQThreads, 2)
 // ------------------------------------------------------------------------------------------------------------------
 bool gemm_kq_tc_supported(const WeightView & w, int64_t M) {
     return (w.type == B200_TYPE_Q4_K || w.type == B200_TYPE_Q6_K) && M >= 32 && w.K % 256 == 0 && w.K <= (int64_t) 1 << 29 &&
-           w.rows < ((int64_t) 1 << 31) && tensor_maps_available();
+           3 * w.rows < ((int64_t) 1 << 31) && tensor_maps_available();
 }
 
 void kq_release(b200_context * ctx, const void * data) {
@@ -416,22 +471,20 @@ static cudaError_t kq_get(b200_context * ctx, const b200_weight * wt, KqExpansio
     const WeightView w = view_of(wt);
     const int64_t rows = w.rows, K = w.K, nsb = K / 256;
     auto up = [](size_t v) { return (v + 255) & ~(size_t) 255; };
-    const size_t qb = up((size_t) rows * K * (w.type == B200_TYPE_Q6_K ? 2 : 1));
-    const size_t sb = w.type == B200_TYPE_Q4_K ? up((size_t) rows * (K / 32) * 2) : 0;
+    const size_t qb = up((size_t) rows * K * (w.type == B200_TYPE_Q6_K ? 2 : 3));
     const size_t db = up((size_t) rows * nsb * 16);
     KqExpansion e;
     e.type = w.type;
-    e.bytes = qb + sb + db;
+    e.bytes = qb + db;
     cudaError_t err = cudaMallocAsync(&e.mem, e.bytes, ctx->stream);
     if (err != cudaSuccess) return err;
     uint8_t * m = (uint8_t *) e.mem;
     e.q = (int8_t *) m;
-    e.scm = sb ? (uint16_t *) (m + qb) : nullptr;
-    e.dd = (float *) (m + qb + sb);
+    e.dd = (float *) (m + qb);
     const int64_t work = rows * nsb;
     int64_t blocks = (work + 7) / 8;
     if (blocks > (int64_t) ctx->num_sms * 16) blocks = (int64_t) ctx->num_sms * 16;
-    if (w.type == B200_TYPE_Q4_K) expand_q4k_kernel<<<(unsigned) blocks, 256, 0, ctx->stream>>>(w, e.q, e.scm, (float4 *) e.dd);
+    if (w.type == B200_TYPE_Q4_K) expand_q4k_kernel<<<(unsigned) blocks, 256, 0, ctx->stream>>>(w, e.q, (float4 *) e.dd);
     else expand_q6k_kernel<<<(unsigned) blocks, 256, 0, ctx->stream>>>(w, e.q, (float4 *) e.dd);
     err = cudaGetLastError();
     if (err != cudaSuccess) {
@@ -450,27 +503,27 @@ static cudaError_t launch_kq(const WeightView & w, const KqExpansion & e, int64_
     const int64_t K = w.K;
     CUtensorMap ta, tb, tsc, tdd, tdx, tbs;
     const uint64_t aK = (uint64_t) (KIND == 6 ? 2 * K : K);
-    bool ok = make_map_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, e.q, aK, (uint64_t) w.rows, aK, 128, kQM, CU_TENSOR_MAP_SWIZZLE_128B) &&
+    const uint64_t arows = (uint64_t) (KIND == 6 ? w.rows : 3 * w.rows);  // Q4_K: three planes, one after the other
+    bool ok = make_map_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, e.q, aK, arows, aK, 128, kQM, CU_TENSOR_MAP_SWIZZLE_128B) &&
               make_map_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, q, (uint64_t) K, (uint64_t) M, (uint64_t) K, 128, 16, CU_TENSOR_MAP_SWIZZLE_128B) &&
               make_map_2d(&tdd, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, e.dd, (uint64_t) (4 * (K / 256)), (uint64_t) w.rows, (uint64_t) (K / 256) * 16, 4,
                           kQM, CU_TENSOR_MAP_SWIZZLE_NONE) &&
               make_map_2d(&tdx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, dxT, (uint64_t) ld, (uint64_t) (K / 256), (uint64_t) ld * 4, kQNT, 1,
                           CU_TENSOR_MAP_SWIZZLE_NONE);
-    if (KIND == 4)
-        ok = ok && make_map_2d(&tsc, CU_TENSOR_MAP_DATA_TYPE_UINT16, e.scm, (uint64_t) (K / 32), (uint64_t) w.rows, (uint64_t) (K / 32) * 2, 8, kQM,
-                               CU_TENSOR_MAP_SWIZZLE_NONE) &&
-             make_map_2d(&tbs, CU_TENSOR_MAP_DATA_TYPE_INT32, bsT, (uint64_t) ld, (uint64_t) (K / 32), (uint64_t) ld * 4, kQNT, kQKB,
-                         CU_TENSOR_MAP_SWIZZLE_NONE);
-    else {
+    if (KIND == 4) {
+        tsc = tdd;  // unused: the scales are inside the expansion planes
+    } else {
         ok = ok && make_map_2d(&tsc, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.f2, (uint64_t) (K / 16), (uint64_t) w.rows, (uint64_t) (K / 16), 16, kQM,
                                CU_TENSOR_MAP_SWIZZLE_NONE);
-        tbs = tdx;  // unused
     }
+    tbs = tdx;  // unused
+    (void) bsT;
     if (!ok) return cudaErrorInvalidValue;
     KqParams p;
     p.N = N;
     p.K = K;
     p.row0 = row0;
+    p.plane_rows = w.rows;
     p.M = (int) M;
     p.tiles_m = (int) ((M + kQNT - 1) / kQNT);
     p.tiles_n = (int) ((N + kQM - 1) / kQM);

@@ -31,8 +31,7 @@ struct KqExpansion {
     int type = 0;
     void * mem = nullptr;
     size_t bytes = 0;
-    int8_t * q = nullptr;      // Q4_K: [rows][K] 0..15; Q6_K: [rows][2K], zero-masked halves of q - 32
-    uint16_t * scm = nullptr;  // Q4_K: [rows][K/32] sc | m << 8
+    int8_t * q = nullptr;      // Q4_K: [3][rows][K] planes (sc / 8) * q, (sc % 8) * q, m; Q6_K: [rows][2K], zero-masked halves of q - 32
     float * dd = nullptr;      // [rows][K/256][4]: d, dmin (Q4_K) or d (Q6_K)
 };
 
