@@ -67,33 +67,42 @@ __global__ void expand_q4k_kernel(WeightView w, int8_t * q, float4 * dd) {
     }
 }
 
-// Q6_K: q int8 [rows][2K] (32-value block b -> expanded blocks 2b = [q - 32 of values 0..15, 0 x 16] and
-// 2b + 1 = [0 x 16, q - 32 of values 16..31]), dd float4 [rows][K/256] (d, 0, 0, 0). The int8 scales stay in the
-// weight's own sc field, [rows][K/16].
+// Q6_K: four int8 planes q [4][rows][K] and dd float4 [rows][K/256] (d, 0, 0, 0). The 16-value group's int8 scale is
+// written in balanced base 5, sc = e0 + 5 e1 + 25 e2 + 125 e3 with every e in -2..2, and plane k holds e_k * (q - 32)
+// (|.| <= 64): over a super-block, (plane 0 . x) + 5 (plane 1 . x) + 25 (plane 2 . x) + 125 (plane 3 . x) is ggml's
+// sumi = sum_g sc_g sum_l (q_l - 32) x_l, exactly.
 __global__ void expand_q6k_kernel(WeightView w, int8_t * q, float4 * dd) {
     const int lane = threadIdx.x & 31;
-    const int64_t nsb = w.K / 256, total = w.rows * nsb;
+    const int64_t nsb = w.K / 256, total = w.rows * nsb, plane = w.rows * w.K;
     const int64_t warps = (int64_t) gridDim.x * (blockDim.x >> 5);
     for (int64_t i = (int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); i < total; i += warps) {
         const int64_t r = i / nsb, sb = i % nsb;
         const uint8_t * ql = w.f0 + r * (w.K / 2) + sb * 128;
         const uint8_t * qh = w.f1 + r * (w.K / 4) + sb * 64;
-        const int b = lane >> 2, p0 = (lane & 3) * 8;  // values 8 lane .. 8 lane + 7: block b, positions p0..p0+7
-        const int h = b >> 2, t = b & 3;
-        uint32_t v0 = 0, v1 = 0;
+        // this lane: values v = 8 lane .. 8 lane + 7 of the super-block: half hh, quarter t, positions l0 .. l0 + 7
+        const int v0 = 8 * lane, hh = v0 >> 7, t = (v0 >> 5) & 3, l0 = v0 & 31;
+        int sc = (int) reinterpret_cast<const int8_t *>(w.f2)[r * (w.K / 16) + sb * 16 + (v0 >> 4)];
+        int e[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            int d = ((sc % 5) + 5) % 5;  // 0..4
+            if (d > 2) d -= 5;           // -2..2
+            e[k] = d;
+            sc = (sc - d) / 5;
+        }
+        uint32_t out[4][2] = {};
 #pragma unroll
         for (int j = 0; j < 8; j++) {
-            const int l = p0 + j;
-            const int lo4 = (ql[h * 64 + (t & 1) * 32 + l] >> ((t >> 1) * 4)) & 15;
-            const int hi2 = (qh[h * 32 + l] >> (2 * t)) & 3;
-            const uint32_t v = (uint32_t) (uint8_t) (int8_t) ((lo4 | (hi2 << 4)) - 32);
-            if (j < 4) v0 |= v << (8 * j);
-            else v1 |= v << (8 * (j - 4));
+            const int l = l0 + j;
+            const int lo4 = (ql[hh * 64 + (t & 1) * 32 + l] >> ((t >> 1) * 4)) & 15;
+            const int hi2 = (qh[hh * 32 + l] >> (2 * t)) & 3;
+            const int qv = (lo4 | (hi2 << 4)) - 32;
+#pragma unroll
+            for (int k = 0; k < 4; k++) out[k][j >> 2] |= (uint32_t) (uint8_t) (int8_t) (e[k] * qv) << (8 * (j & 3));
         }
-        int8_t * base = q + r * (2 * w.K) + sb * 512 + b * 64;
-        const uint2 vals = make_uint2(v0, v1), zero = make_uint2(0u, 0u);
-        *reinterpret_cast<uint2 *>(base + p0) = p0 < 16 ? vals : zero;
-        *reinterpret_cast<uint2 *>(base + 32 + p0) = p0 < 16 ? zero : vals;
+        int8_t * dst = q + r * w.K + sb * 256 + v0;
+#pragma unroll
+        for (int k = 0; k < 4; k++) *reinterpret_cast<uint2 *>(dst + k * plane) = make_uint2(out[k][0], out[k][1]);
         if (lane == 0) dd[r * nsb + sb] = make_float4(__half2float(reinterpret_cast<const __half *>(w.f3)[r * nsb + sb]), 0.0f, 0.0f, 0.0f);
     }
 }
@@ -139,20 +148,21 @@ constexpr unsigned kErrTimeout = 4u;
 
 template <int KIND>
 struct KqLayout {
-    static constexpr int kAT = KIND == 6 ? 2 : 3;          // A tiles ([128 rows][128 B], swizzled) per stage
-    static constexpr int kA = kAT * kQM * 128;
+    static constexpr int kPlanes = KIND == 6 ? 4 : 3;      // expansion planes = accumulators per super-block
+    static constexpr int kA = kPlanes * kQM * 128;        // A tiles ([128 rows][128 B], swizzled), one per plane
     static constexpr int kB = kQKB * kQNT * 32;            // activations: [32 rows][128 B] swizzled
-    static constexpr int kSc = KIND == 6 ? kQM * 16 : 0;   // Q6_K: 16-byte box per row of scales (this stage's half)
     static constexpr int kDd = kQM * 16;                   // float4 (d, dmin) per row
     static constexpr int kDx = kQNT * 4;                   // the super-block's activation scales
-    static constexpr int kStage = (kA + kB + kSc + kDd + kDx + 1023) & ~1023;
-    static constexpr int kStages = 2;
+    static constexpr int kStage = (kA + kB + kDd + kDx + 1023) & ~1023;
+    static constexpr int kStages = KIND == 6 ? 3 : 2;
+    static constexpr int kCtasPerSm = KIND == 6 ? 1 : 2;  // shared memory: Q6_K's stages take most of an SM
     static constexpr int kTotal = kStages * kStage + 1024 + 1024;
+    static_assert(2 * kPlanes * kQNT <= 2 * kQBufs * kQNT, "two super-block buffers fit the tensor-memory allocation");
 };
 
 struct KqParams {
     int64_t N, K, row0;
-    int64_t plane_rows;  // Q4_K: rows of one expansion plane (the weight's rows)
+    int64_t plane_rows;  // rows of one expansion plane (the weight's rows)
     int M;
     int tiles_m, tiles_n;
     float * y;
@@ -160,25 +170,36 @@ struct KqParams {
     unsigned * err;
 };
 
+// ggml's super-block integers from the accumulators A of the expansion planes (see the expansion kernels).
 template <int KIND>
-__global__ void __launch_bounds__(kQThreads, 2)
+__device__ __forceinline__ void kq_combine(int (*A)[16], int i, int & sumi, int & summ) {
+    if (KIND == 4) {
+        sumi = 8 * A[0][i] + A[1][i];
+        summ = A[2][i];
+    } else {
+        sumi = A[0][i] + 5 * A[1][i] + 25 * A[2][i] + 125 * A[3][i];
+        summ = 0;
+    }
+}
+
+template <int KIND>
+__global__ void __launch_bounds__(kQThreads, KqLayout<KIND>::kCtasPerSm)
     gemm_kq_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                      const __grid_constant__ CUtensorMap tmSc, const __grid_constant__ CUtensorMap tmDd,
-                      const __grid_constant__ CUtensorMap tmDx, const __grid_constant__ CUtensorMap tmBs, KqParams p) {
+                      const __grid_constant__ CUtensorMap tmDd, const __grid_constant__ CUtensorMap tmDx, KqParams p) {
     using L = KqLayout<KIND>;
-    constexpr int S = L::kStages;
+    constexpr int S = L::kStages, P = L::kPlanes;
     extern __shared__ uint8_t smem_raw[];
     uint8_t * smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t) 1023);
     uint64_t * bars = reinterpret_cast<uint64_t *>(smem + S * L::kStage);
     uint64_t * full = bars;
     uint64_t * empty = bars + S;
     uint64_t * acc_full = bars + 2 * S;
-    uint64_t * acc_empty = acc_full + kQBufs;
-    uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + kQBufs);
+    uint64_t * acc_empty = acc_full + 2;
+    uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
     __shared__ volatile int give_up;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nstage = (int) (p.K / 32 / kQKB);
+    const int nstage = (int) (p.K / 32 / kQKB);  // two per super-block
     const int items = p.tiles_m * p.tiles_n;
 
     if (threadIdx.x == 0) {
@@ -186,7 +207,7 @@ __global__ void __launch_bounds__(kQThreads, 2)
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1 + kQEpiWarps);
         }
-        for (int b = 0; b < kQBufs; b++) {
+        for (int b = 0; b < 2; b++) {
             mbar_init(&acc_full[b], 1);
             mbar_init(&acc_empty[b], kQEpiWarps);
         }
@@ -220,7 +241,7 @@ __global__ void __launch_bounds__(kQThreads, 2)
                 int m0, nz, live, tn;
                 tile_of(it, m0, nz, live, tn);
                 const int arow = (int) (p.row0 + (int64_t) tn * kQM);
-                const uint32_t bytes = (uint32_t) (L::kA + nz * 128 + L::kSc + L::kDd + L::kDx);
+                const uint32_t bytes = (uint32_t) (L::kA + nz * 128 + L::kDd + L::kDx);
                 for (int st = 0; st < nstage; st++, sg++) {
                     const int s = sg % S, use = sg / S;
                     if (use > 0 && !mbar_wait_sleep(&empty[s], (use - 1) & 1)) {
@@ -231,23 +252,17 @@ __global__ void __launch_bounds__(kQThreads, 2)
                     uint8_t * base = smem + s * L::kStage;
                     mbar_arrive_expect_tx(&full[s], bytes);
                     const int kbs = st * kQKB;  // first 32-value block of the stage
-                    if (KIND == 4) {
-                        for (int pl = 0; pl < 3; pl++)
-                            tma_load_2d(base + pl * kQM * 128, &tmA, kbs * 32, (int) (pl * p.plane_rows) + arow, &full[s]);
-                    } else {
-                        tma_load_2d(base, &tmA, 2 * kbs * 32, arow, &full[s]);
-                        tma_load_2d(base + kQM * 128, &tmA, 2 * kbs * 32 + 128, arow, &full[s]);
-                    }
+                    for (int pl = 0; pl < P; pl++)
+                        tma_load_2d(base + pl * kQM * 128, &tmA, kbs * 32, (int) (pl * p.plane_rows) + arow, &full[s]);
                     for (int r = 0; r < nz / 16; r++) tma_load_2d(base + L::kA + r * 16 * 128, &tmB, kbs * 32, m0 + 16 * r, &full[s]);
-                    uint8_t * sc = base + L::kA + L::kB;
-                    if (KIND == 6) tma_load_2d(sc, &tmSc, (2 * kbs) & ~15, arow, &full[s]);  // 16 int8 scales
-                    tma_load_2d(sc + L::kSc, &tmDd, 4 * (kbs / 8), arow, &full[s]);
-                    tma_load_2d(sc + L::kSc + L::kDd, &tmDx, m0, kbs / 8, &full[s]);
+                    uint8_t * dd = base + L::kA + L::kB;
+                    tma_load_2d(dd, &tmDd, 4 * (kbs / 8), arow, &full[s]);
+                    tma_load_2d(dd + L::kDd, &tmDx, m0, kbs / 8, &full[s]);
                 }
             }
         }
     } else if (warp == 1) {
-        // ---- MMA issuer: a buffer takes two accumulators: Q4_K two blocks, Q6_K one block's two halves ----
+        // ---- MMA issuer: a super-block is two stages; its P accumulators take one buffer of P x 32 columns ----
         if (lane == 0) {
             int sg = 0, g2 = 0;
             for (int it = blockIdx.x; it < items && !give_up; it += gridDim.x) {
@@ -263,48 +278,24 @@ __global__ void __launch_bounds__(kQThreads, 2)
                     }
                     tc_fence_after();
                     uint8_t * base = smem + s * L::kStage;
-                    if constexpr (KIND == 4) {
-                        // a super-block is two stages; its three accumulators take one buffer of 3 x 32 columns
-                        const int sbpos = st & 1, buf = g2 % 2, use = g2 / 2;
-                        if (sbpos == 0 && use > 0 && !mbar_wait_sleep(&acc_empty[buf], (use - 1) & 1)) {
-                            atomicOr(p.err, kErrTimeout);
-                            give_up = 1;
-                            break;
-                        }
-                        tc_fence_after();
-                        for (int blk = 0; blk < kQKB; blk++) {
-#pragma unroll
-                            for (int pl = 0; pl < 3; pl++)
-                                mma_i8_acc(tmem + buf * 3 * kQNT + pl * kQNT, smem_desc_sw128(base + pl * kQM * 128, blk),
-                                           smem_desc_sw128(base + L::kA, blk), idesc, (uint32_t) (sbpos | blk));
-                        }
-                        mma_commit(&empty[s]);
-                        if (sbpos == 1) {
-                            mma_commit(&acc_full[buf]);
-                            g2++;
-                        }
-                        continue;
+                    const int sbpos = st & 1, buf = g2 % 2, use = g2 / 2;
+                    if (sbpos == 0 && use > 0 && !mbar_wait_sleep(&acc_empty[buf], (use - 1) & 1)) {
+                        atomicOr(p.err, kErrTimeout);
+                        give_up = 1;
+                        break;
                     }
-                    constexpr int kPerStage = kQKB;  // Q6_K: buffers per stage
-                    for (int u = 0; u < kPerStage; u++, g2++) {
-                        const int buf = g2 % kQBufs, use = g2 / kQBufs;
-                        if (use > 0 && !mbar_wait_sleep(&acc_empty[buf], (use - 1) & 1)) {
-                            atomicOr(p.err, kErrTimeout);
-                            give_up = 1;
-                            break;
-                        }
-                        tc_fence_after();
+                    tc_fence_after();
+                    for (int blk = 0; blk < kQKB; blk++) {
 #pragma unroll
-                        for (int jj = 0; jj < 2; jj++) {
-                            const int blk = u;           // 32-value block of the stage
-                            const int e = 2 * u + jj;    // A block (expanded)
-                            mma_i8(tmem + buf * 2 * kQNT + jj * kQNT, smem_desc_sw128(base + (e >> 2) * kQM * 128, e & 3),
-                                   smem_desc_sw128(base + L::kA, blk), idesc);
-                        }
-                        mma_commit(&acc_full[buf]);
+                        for (int pl = 0; pl < P; pl++)
+                            mma_i8_acc(tmem + buf * P * kQNT + pl * kQNT, smem_desc_sw128(base + pl * kQM * 128, blk),
+                                       smem_desc_sw128(base + L::kA, blk), idesc, (uint32_t) (sbpos | blk));
                     }
-                    if (give_up) break;
                     mma_commit(&empty[s]);
+                    if (sbpos == 1) {
+                        mma_commit(&acc_full[buf]);
+                        g2++;
+                    }
                 }
             }
         }
@@ -320,101 +311,45 @@ __global__ void __launch_bounds__(kQThreads, 2)
             const bool has = 16 * h < nz;
             const int live = live_all - 16 * h;
             float acc[16];
-            int isum[16];
 #pragma unroll
-            for (int i = 0; i < 16; i++) {
-                acc[i] = 0.0f;
-                isum[i] = 0;
-            }
+            for (int i = 0; i < 16; i++) acc[i] = 0.0f;
             for (int st = 0; st < nstage && !give_up; st++, sg++) {
                 const int s = sg % S;
-                const uint8_t * base = smem + s * L::kStage;
-                const uint8_t * sc = base + L::kA + L::kB;
-                // the stage's (d, dmin) and dx are read only after an accumulator wait: the MMAs that filled it
-                // consumed this stage, so its bulk copies have landed
-                const float4 * ddp = reinterpret_cast<const float4 *>(sc + L::kSc) + row;
-                const float * dx = reinterpret_cast<const float *>(sc + L::kSc + L::kDd);
-                const int kbs = st * kQKB;
-                if constexpr (KIND == 4) {
-                    // the super-block's three accumulators, after its second stage: one integer and one float step
-                    if ((st & 1) == 1) {
-                        const int buf = g2 % 2, use = g2 / 2;
-                        g2++;
-                        if (!mbar_wait_sleep(&acc_full[buf], use & 1)) {
-                            if (lane == 0) atomicOr(p.err, kErrTimeout);
-                            give_up = 1;
-                            break;
-                        }
-                        tc_fence_after();
-                        int va[16], vb[16], vm[16];
-                        if (has) {
-                            const uint32_t ta = tmem + ((uint32_t) (32 * q) << 16) + buf * 3 * kQNT + 16 * h;
-                            tmem_ld16(ta, va);
-                            tmem_ld16(ta + kQNT, vb);
-                            tmem_ld16(ta + 2 * kQNT, vm);
-                            tmem_wait_ld();
-                        }
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&acc_empty[buf]);
-                        if (has) {
-                            const float4 ddv = *ddp;
-#pragma unroll
-                            for (int i = 0; i < 16; i++) {
-                                if (i >= live) break;
-                                const float dxv = dx[16 * h + i];
-                                const int sumi = 8 * va[i] + vb[i];
-                                acc[i] = fmaf(__fmul_rn(dxv, ddv.x), (float) sumi, acc[i]);
-                                acc[i] = fmaf(-__fmul_rn(dxv, ddv.y), (float) vm[i], acc[i]);
-                            }
-                        }
-                    }
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&empty[s]);
-                    continue;
-                }
-                constexpr int kPerStage = kQKB;
-                for (int u = 0; u < kPerStage; u++, g2++) {
-                    const int buf = g2 % kQBufs, use = g2 / kQBufs;
+                if ((st & 1) == 1) {
+                    // the super-block's accumulators, after its second stage: one integer and one float step, in
+                    // super-block order. The stage's (d, dmin) and dx are read after the accumulator wait: the MMAs
+                    // that filled it consumed this stage, so its bulk copies have landed.
+                    const int buf = g2 % 2, use = g2 / 2;
+                    g2++;
                     if (!mbar_wait_sleep(&acc_full[buf], use & 1)) {
                         if (lane == 0) atomicOr(p.err, kErrTimeout);
                         give_up = 1;
                         break;
                     }
                     tc_fence_after();
-                    if (!has) {
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&acc_empty[buf]);
-                        continue;
-                    }
-                    // the buffer's two accumulators one at a time (16 sums each); released after the second load
-                    const uint32_t ta = tmem + ((uint32_t) (32 * q) << 16) + buf * 2 * kQNT + 16 * h;
+                    int A[P][16];
+                    if (has) {
+                        const uint32_t ta = tmem + ((uint32_t) (32 * q) << 16) + buf * P * kQNT + 16 * h;
 #pragma unroll
-                    for (int jj = 0; jj < 2; jj++) {
-                        int v[16];
-                        tmem_ld16(ta + jj * kQNT, v);
+                        for (int pl = 0; pl < P; pl++) tmem_ld16(ta + pl * kQNT, A[pl]);
                         tmem_wait_ld();
-                        if (jj == 1) {
-                            tc_fence_before();
-                            __syncwarp();
-                            if (lane == 0) mbar_arrive(&acc_empty[buf]);
-                        }
-                        const int scv = reinterpret_cast<const int8_t *>(sc)[row * 16 + ((2 * kbs) & 15) + 2 * u + jj];
+                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&acc_empty[buf]);
+                    if (has) {
+                        const uint8_t * dd = smem + s * L::kStage + L::kA + L::kB;
+                        const float4 ddv = reinterpret_cast<const float4 *>(dd)[row];
+                        const float * dx = reinterpret_cast<const float *>(dd + L::kDd);
 #pragma unroll
                         for (int i = 0; i < 16; i++) {
                             if (i >= live) break;
-                            isum[i] += scv * v[i];
+                            const float dxv = dx[16 * h + i];
+                            int sumi, summ;
+                            kq_combine<KIND>(A, i, sumi, summ);
+                            acc[i] = fmaf(__fmul_rn(dxv, ddv.x), (float) sumi, acc[i]);
+                            if (KIND == 4) acc[i] = fmaf(-__fmul_rn(dxv, ddv.y), (float) summ, acc[i]);
                         }
-                    }
-                }
-                if (has && !give_up && ((kbs + kQKB) & 7) == 0) {  // end of a super-block: one float step, in order
-                    const float4 ddv = *ddp;
-#pragma unroll
-                    for (int i = 0; i < 16; i++) {
-                        if (i >= live) break;
-                        const float dxv = dx[16 * h + i];
-                        acc[i] = fmaf(__fmul_rn(dxv, ddv.x), (float) isum[i], acc[i]);
-                        isum[i] = 0;
                     }
                 }
                 __syncwarp();
@@ -446,7 +381,7 @@ __global__ void __launch_bounds__(kQThreads, 2)
 // ------------------------------------------------------------------------------------------------------------------
 bool gemm_kq_tc_supported(const WeightView & w, int64_t M) {
     return (w.type == B200_TYPE_Q4_K || w.type == B200_TYPE_Q6_K) && M >= 32 && w.K % 256 == 0 && w.K <= (int64_t) 1 << 29 &&
-           3 * w.rows < ((int64_t) 1 << 31) && tensor_maps_available();
+           4 * w.rows < ((int64_t) 1 << 31) && tensor_maps_available();
 }
 
 void kq_release(b200_context * ctx, const void * data) {
@@ -471,7 +406,7 @@ static cudaError_t kq_get(b200_context * ctx, const b200_weight * wt, KqExpansio
     const WeightView w = view_of(wt);
     const int64_t rows = w.rows, K = w.K, nsb = K / 256;
     auto up = [](size_t v) { return (v + 255) & ~(size_t) 255; };
-    const size_t qb = up((size_t) rows * K * (w.type == B200_TYPE_Q6_K ? 2 : 3));
+    const size_t qb = up((size_t) rows * K * (w.type == B200_TYPE_Q6_K ? 4 : 3));
     const size_t db = up((size_t) rows * nsb * 16);
     KqExpansion e;
     e.type = w.type;
@@ -501,22 +436,14 @@ static cudaError_t launch_kq(const WeightView & w, const KqExpansion & e, int64_
                              const int32_t * bsT, int64_t ld, int64_t M, float * y, int64_t ldy, unsigned * err, int num_sms, cudaStream_t st) {
     using L = KqLayout<KIND>;
     const int64_t K = w.K;
-    CUtensorMap ta, tb, tsc, tdd, tdx, tbs;
-    const uint64_t aK = (uint64_t) (KIND == 6 ? 2 * K : K);
-    const uint64_t arows = (uint64_t) (KIND == 6 ? w.rows : 3 * w.rows);  // Q4_K: three planes, one after the other
-    bool ok = make_map_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, e.q, aK, arows, aK, 128, kQM, CU_TENSOR_MAP_SWIZZLE_128B) &&
+    CUtensorMap ta, tb, tdd, tdx;
+    const uint64_t arows = (uint64_t) L::kPlanes * (uint64_t) w.rows;  // the planes, one after the other
+    bool ok = make_map_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, e.q, (uint64_t) K, arows, (uint64_t) K, 128, kQM, CU_TENSOR_MAP_SWIZZLE_128B) &&
               make_map_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, q, (uint64_t) K, (uint64_t) M, (uint64_t) K, 128, 16, CU_TENSOR_MAP_SWIZZLE_128B) &&
               make_map_2d(&tdd, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, e.dd, (uint64_t) (4 * (K / 256)), (uint64_t) w.rows, (uint64_t) (K / 256) * 16, 4,
                           kQM, CU_TENSOR_MAP_SWIZZLE_NONE) &&
               make_map_2d(&tdx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, dxT, (uint64_t) ld, (uint64_t) (K / 256), (uint64_t) ld * 4, kQNT, 1,
                           CU_TENSOR_MAP_SWIZZLE_NONE);
-    if (KIND == 4) {
-        tsc = tdd;  // unused: the scales are inside the expansion planes
-    } else {
-        ok = ok && make_map_2d(&tsc, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.f2, (uint64_t) (K / 16), (uint64_t) w.rows, (uint64_t) (K / 16), 16, kQM,
-                               CU_TENSOR_MAP_SWIZZLE_NONE);
-    }
-    tbs = tdx;  // unused
     (void) bsT;
     if (!ok) return cudaErrorInvalidValue;
     KqParams p;
@@ -536,7 +463,7 @@ static cudaError_t launch_kq(const WeightView & w, const KqExpansion & e, int64_
         if (e2 != cudaSuccess) return e2;
         configured = 1;
     }
-    gemm_kq_tc_kernel<KIND><<<2 * num_sms, kQThreads, L::kTotal, st>>>(ta, tb, tsc, tdd, tdx, tbs, p);
+    gemm_kq_tc_kernel<KIND><<<L::kCtasPerSm * num_sms, kQThreads, L::kTotal, st>>>(ta, tb, tdd, tdx, p);
     return cudaGetLastError();
 }
 

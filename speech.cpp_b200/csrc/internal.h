@@ -31,7 +31,8 @@ struct KqExpansion {
     int type = 0;
     void * mem = nullptr;
     size_t bytes = 0;
-    int8_t * q = nullptr;      // Q4_K: [3][rows][K] planes (sc / 8) * q, (sc % 8) * q, m; Q6_K: [rows][2K], zero-masked halves of q - 32
+    int8_t * q = nullptr;      // planes [P][rows][K] with the scales inside: Q4_K (P = 3) (sc / 8) q, (sc % 8) q, m;
+                               // Q6_K (P = 4) e_k (q - 32), sc's balanced base-5 digits e_k
     float * dd = nullptr;      // [rows][K/256][4]: d, dmin (Q4_K) or d (Q6_K)
 };
 
