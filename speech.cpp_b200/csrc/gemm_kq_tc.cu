@@ -139,25 +139,26 @@ __global__ void quantize_q8k_tc_kernel(const float * __restrict__ x, int64_t K, 
 namespace {
 
 constexpr int kQM = 128;       // weight rows per tile
-constexpr int kQNT = 32;       // tokens per tile
+constexpr int kQNT = 64;       // tokens per tile
 constexpr int kQKB = 4;        // 32-value blocks per stage
 constexpr int kQThreads = 320; // producer, MMA, 8 epilogue warps
 constexpr int kQEpiWarps = 8;
-constexpr int kQBufs = 4;      // tensor-memory buffers of 2 x kQNT columns
+constexpr int kQTmemCols = 512; // tensor memory of the one CTA per SM: two super-block buffers of planes x kQNT
 constexpr unsigned kErrTimeout = 4u;
 
 template <int KIND>
 struct KqLayout {
     static constexpr int kPlanes = KIND == 6 ? 4 : 3;      // expansion planes = accumulators per super-block
     static constexpr int kA = kPlanes * kQM * 128;        // A tiles ([128 rows][128 B], swizzled), one per plane
-    static constexpr int kB = kQKB * kQNT * 32;            // activations: [32 rows][128 B] swizzled
+    static constexpr int kB = kQKB * kQNT * 32;            // activations: [64 rows][128 B] swizzled
     static constexpr int kDd = kQM * 16;                   // float4 (d, dmin) per row
     static constexpr int kDx = kQNT * 4;                   // the super-block's activation scales
     static constexpr int kStage = (kA + kB + kDd + kDx + 1023) & ~1023;
-    static constexpr int kStages = KIND == 6 ? 3 : 2;
-    static constexpr int kCtasPerSm = KIND == 6 ? 1 : 2;  // shared memory: Q6_K's stages take most of an SM
-    static constexpr int kTotal = kStages * kStage + 1024 + 1024;
-    static_assert(2 * kPlanes * kQNT <= 2 * kQBufs * kQNT, "two super-block buffers fit the tensor-memory allocation");
+    static constexpr int kStages = 3;
+    static constexpr int kCtasPerSm = 1;
+    static constexpr int kTotal = kStages * kStage + 1024 + 256;  // + alignment slack + barriers
+    static_assert(2 * kPlanes * kQNT <= kQTmemCols, "two super-block buffers fit the tensor-memory allocation");
+    static_assert(kTotal + 64 <= 227 * 1024, "shared memory of one CTA");
 };
 
 struct KqParams {
@@ -215,7 +216,7 @@ __global__ void __launch_bounds__(kQThreads, KqLayout<KIND>::kCtasPerSm)
         give_up = 0;
     }
     if (warp == 1) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)), "r"(2 * kQBufs * kQNT));
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)), "r"(kQTmemCols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     tc_fence_before();
@@ -300,19 +301,19 @@ __global__ void __launch_bounds__(kQThreads, KqLayout<KIND>::kCtasPerSm)
             }
         }
     } else {
-        // ---- epilogue: lane quarter q = warp % 4 owns tile rows 32 q .. 32 q + 31; warp half h the 16 tokens
-        // 16 h .. 16 h + 15. A warp without tokens in a tile still waits and arrives on every barrier ----
+        // ---- epilogue: lane quarter q = warp % 4 owns tile rows 32 q .. 32 q + 31; warp half h the 32 tokens
+        // 32 h .. 32 h + 31, read as two groups of 16. A warp without tokens in a tile still waits and arrives on
+        // every barrier ----
         const int q = warp & 3, h = (warp - 2) >> 2;
         const int row = 32 * q + lane;
         int sg = 0, g2 = 0;
         for (int it = blockIdx.x; it < items && !give_up; it += gridDim.x) {
             int m0, nz, live_all, tn;
             tile_of(it, m0, nz, live_all, tn);
-            const bool has = 16 * h < nz;
-            const int live = live_all - 16 * h;
-            float acc[16];
+            const int live = live_all - 32 * h;
+            float acc[32];
 #pragma unroll
-            for (int i = 0; i < 16; i++) acc[i] = 0.0f;
+            for (int i = 0; i < 32; i++) acc[i] = 0.0f;
             for (int st = 0; st < nstage && !give_up; st++, sg++) {
                 const int s = sg % S;
                 if ((st & 1) == 1) {
@@ -327,42 +328,43 @@ __global__ void __launch_bounds__(kQThreads, KqLayout<KIND>::kCtasPerSm)
                         break;
                     }
                     tc_fence_after();
-                    int A[P][16];
-                    if (has) {
-                        const uint32_t ta = tmem + ((uint32_t) (32 * q) << 16) + buf * P * kQNT + 16 * h;
+                    const uint8_t * dd = smem + s * L::kStage + L::kA + L::kB;
+                    const float4 ddv = reinterpret_cast<const float4 *>(dd)[row];
+                    const float * dx = reinterpret_cast<const float *>(dd + L::kDd);
+#pragma unroll
+                    for (int hf = 0; hf < 2; hf++) {
+                        if (32 * h + 16 * hf >= nz) break;  // warp-uniform
+                        int A[P][16];
+                        const uint32_t ta = tmem + ((uint32_t) (32 * q) << 16) + buf * P * kQNT + 32 * h + 16 * hf;
 #pragma unroll
                         for (int pl = 0; pl < P; pl++) tmem_ld16(ta + pl * kQNT, A[pl]);
                         tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 16; i++) {
+                            if (16 * hf + i >= live) break;
+                            const float dxv = dx[32 * h + 16 * hf + i];
+                            int sumi, summ;
+                            kq_combine<KIND>(A, i, sumi, summ);
+                            float & a = acc[16 * hf + i];
+                            a = fmaf(__fmul_rn(dxv, ddv.x), (float) sumi, a);
+                            if (KIND == 4) a = fmaf(-__fmul_rn(dxv, ddv.y), (float) summ, a);
+                        }
                     }
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&acc_empty[buf]);
-                    if (has) {
-                        const uint8_t * dd = smem + s * L::kStage + L::kA + L::kB;
-                        const float4 ddv = reinterpret_cast<const float4 *>(dd)[row];
-                        const float * dx = reinterpret_cast<const float *>(dd + L::kDd);
-#pragma unroll
-                        for (int i = 0; i < 16; i++) {
-                            if (i >= live) break;
-                            const float dxv = dx[16 * h + i];
-                            int sumi, summ;
-                            kq_combine<KIND>(A, i, sumi, summ);
-                            acc[i] = fmaf(__fmul_rn(dxv, ddv.x), (float) sumi, acc[i]);
-                            if (KIND == 4) acc[i] = fmaf(-__fmul_rn(dxv, ddv.y), (float) summ, acc[i]);
-                        }
-                    }
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[s]);  // the stage's scales are read: it may be refilled
             }
             if (give_up) break;
-            if (!has) continue;
+            if (live <= 0) continue;
             const int64_t grow = (int64_t) tn * kQM + row;
             if (grow < p.N)
 #pragma unroll
-                for (int i = 0; i < 16; i++) {
+                for (int i = 0; i < 32; i++) {
                     if (i >= live) break;
-                    p.y[(int64_t) (m0 + 16 * h + i) * p.ldy + grow] = acc[i];
+                    p.y[(int64_t) (m0 + 32 * h + i) * p.ldy + grow] = acc[i];
                 }
         }
     }
@@ -370,7 +372,7 @@ __global__ void __launch_bounds__(kQThreads, KqLayout<KIND>::kCtasPerSm)
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kQBufs * kQNT));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kQTmemCols));
     }
 }
 
