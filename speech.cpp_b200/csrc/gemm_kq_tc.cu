@@ -107,9 +107,10 @@ __global__ void expand_q6k_kernel(WeightView w, int8_t * q, float4 * dd) {
     }
 }
 
-// q8_K of M activation rows for the tensor-core products: q int8 [M][K], dxT float [K/256][ld] (transposed scales),
-// bsT int32 [K/32][ld] (sums of each 32 values). One warp per 256-block; bit-identical to quantize_row_q8_K.
-__global__ void quantize_q8k_tc_kernel(const float * __restrict__ x, int64_t K, int64_t M, int8_t * q, float * dxT, int32_t * bsT, int64_t ld) {
+// q8_K of M activation rows for the tensor-core products: q int8 [M][K], dxT float [K/256][ld] (transposed scales;
+// the block sums that q8_K also carries are not needed: Q4_K's min term comes from its m plane). One warp per
+// 256-block; bit-identical to quantize_row_q8_K.
+__global__ void quantize_q8k_tc_kernel(const float * __restrict__ x, int64_t K, int64_t M, int8_t * q, float * dxT, int64_t ld) {
     const int lane = threadIdx.x & 31;
     const int64_t nsb = K / 256;
     const int64_t warps = (int64_t) gridDim.x * (blockDim.x >> 5);
@@ -129,9 +130,6 @@ __global__ void quantize_q8k_tc_kernel(const float * __restrict__ x, int64_t K, 
             hi |= (uint32_t) (uint8_t) qv[4 + j] << (8 * j);
         }
         *reinterpret_cast<uint2 *>(q + m * K + sb * 256 + lane * 8) = make_uint2(lo, hi);
-        // lanes 4j .. 4j + 3 hold the 32 values of block j; bsum is the sum of the lane pair's 16
-        const int s32 = (int) bsum + __shfl_down_sync(0xffffffffu, (int) bsum, 2);
-        if ((lane & 3) == 0) bsT[(sb * 8 + lane / 4) * ld + m] = s32;
         if (lane == 0) dxT[sb * ld + m] = df;
     }
 }
@@ -435,7 +433,7 @@ static cudaError_t kq_get(b200_context * ctx, const b200_weight * wt, KqExpansio
 
 template <int KIND>
 static cudaError_t launch_kq(const WeightView & w, const KqExpansion & e, int64_t row0, int64_t N, const int8_t * q, const float * dxT,
-                             const int32_t * bsT, int64_t ld, int64_t M, float * y, int64_t ldy, unsigned * err, int num_sms, cudaStream_t st) {
+                             int64_t ld, int64_t M, float * y, int64_t ldy, unsigned * err, int num_sms, cudaStream_t st) {
     using L = KqLayout<KIND>;
     const int64_t K = w.K;
     CUtensorMap ta, tb, tdd, tdx;
@@ -446,7 +444,6 @@ static cudaError_t launch_kq(const WeightView & w, const KqExpansion & e, int64_
                           kQM, CU_TENSOR_MAP_SWIZZLE_NONE) &&
               make_map_2d(&tdx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, dxT, (uint64_t) ld, (uint64_t) (K / 256), (uint64_t) ld * 4, kQNT, 1,
                           CU_TENSOR_MAP_SWIZZLE_NONE);
-    (void) bsT;
     if (!ok) return cudaErrorInvalidValue;
     KqParams p;
     p.N = N;
@@ -472,7 +469,7 @@ static cudaError_t launch_kq(const WeightView & w, const KqExpansion & e, int64_
 size_t gemm_kq_tc_act_bytes(int64_t K, int64_t M) {
     const int64_t ld = (M + 15) & ~(int64_t) 15;
     auto up = [](size_t v) { return (v + 255) & ~(size_t) 255; };
-    return up((size_t) M * K) + up((size_t) (K / 256) * ld * 4) + up((size_t) (K / 32) * ld * 4);
+    return up((size_t) M * K) + up((size_t) (K / 256) * ld * 4);
 }
 
 cudaError_t launch_gemm_kq_tc(b200_context * ctx, const b200_weight * wt, int64_t row0, int64_t N, const float * x, int64_t M, float * y,
@@ -487,15 +484,14 @@ cudaError_t launch_gemm_kq_tc(b200_context * ctx, const b200_weight * wt, int64_
     uint8_t * a = (uint8_t *) act;
     int8_t * q = (int8_t *) a;
     float * dxT = (float *) (a + up((size_t) M * K));
-    int32_t * bsT = (int32_t *) (a + up((size_t) M * K) + up((size_t) (K / 256) * ld * 4));
     int64_t blocks = (M * (K / 256) + 7) / 8;
     if (blocks > (int64_t) ctx->num_sms * 8) blocks = (int64_t) ctx->num_sms * 8;
-    quantize_q8k_tc_kernel<<<(unsigned) blocks, 256, 0, ctx->stream>>>(x, K, M, q, dxT, bsT, ld);
+    quantize_q8k_tc_kernel<<<(unsigned) blocks, 256, 0, ctx->stream>>>(x, K, M, q, dxT, ld);
     err = cudaGetLastError();
     if (err != cudaSuccess) return err;
     if (w.type == B200_TYPE_Q4_K)
-        return launch_kq<4>(w, *e, row0, N, q, dxT, bsT, ld, M, y, ldy, ctx->dev_err, ctx->num_sms, ctx->stream);
-    return launch_kq<6>(w, *e, row0, N, q, dxT, bsT, ld, M, y, ldy, ctx->dev_err, ctx->num_sms, ctx->stream);
+        return launch_kq<4>(w, *e, row0, N, q, dxT, ld, M, y, ldy, ctx->dev_err, ctx->num_sms, ctx->stream);
+    return launch_kq<6>(w, *e, row0, N, q, dxT, ld, M, y, ldy, ctx->dev_err, ctx->num_sms, ctx->stream);
 }
 
 }  // namespace b200
