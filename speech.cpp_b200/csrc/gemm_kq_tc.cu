@@ -7,16 +7,17 @@
 //   Q6_K: sumi = sum_g sc_g * (sum_l (q_l - 32) x_l) over the 16 groups g of 16 (int8 scales), then
 //         sumf += (d * dx) * sumi.
 // Here the same integers come from the tensor cores. Each weight matrix is expanded once (on the first product with
-// many rows; cached until the weight is written or freed) into int8 values.
-//   Q4_K: three planes with the sub-block scales inside (sc = 8 a + b: a * q, b * q, and the min m at every value), so
-//   three accumulators over a whole super-block (24 MMAs of M = 128 weight rows x N = 32 tokens x K = 32,
-//   accumulating in tensor memory) hold sumi = 8 A0 + A1 and summ = A2 exactly; the epilogue runs once per super-block.
-//   Q6_K: q - 32 as two zero-masked 32-value blocks per 32 values ([q_0..q_15, 0 x 16] and [0 x 16, q_16..q_31]),
-//   because its scale changes every 16 values while one tcgen05.mma kind::i8 spans K = 32; one MMA per half gives the
-//   group's exact int32 sum, and epilogue warps fold the groups into the super-block sum with the integer scales.
-// Either way the epilogue converts once per super-block to float, in super-block order (ggml's float steps). Pipeline as in the grouped Q8_0 kernel (gemm_tc_grouped.cu): warp 0 =
-// TMA producer (no multicast), warp 1 = tensor-memory allocator and MMA issuer, warps 2..9 = epilogue; four
-// accumulator buffers of 2 x 32 columns; every wait bounded.
+// many rows; cached until the weight is written or freed) into int8 planes that carry the integer scales, because a
+// scale times a quant does not fit int8 but the scale's digits do:
+//   Q4_K: three planes, sc = 8 a + b (a, b <= 7): a * q, b * q and the min m at every value;
+//         sumi = 8 A0 + A1 and summ = A2;
+//   Q6_K: four planes, sc = e0 + 5 e1 + 25 e2 + 125 e3 (balanced base 5, e in -2..2): e_k * (q - 32);
+//         sumi = A0 + 5 A1 + 25 A2 + 125 A3,
+// where A_k is plane k's accumulator over a whole 256-value super-block: one tcgen05.mma kind::i8 per plane per
+// 32-value block (M = 128 weight rows x N = 64 tokens x K = 32) accumulates in tensor memory, and the epilogue runs
+// once per super-block, converting to float in super-block order (ggml's float steps). Warp 0 = TMA producer (no
+// multicast), warp 1 = tensor-memory allocator and MMA issuer, warps 2..9 = epilogue; one CTA per SM with 512
+// tensor-memory columns (two super-block buffers) and three shared-memory stages; every wait bounded.
 #include <unordered_map>
 
 #include "internal.h"
