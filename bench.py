@@ -53,7 +53,7 @@ def peaks():
 
 # DRAM bytes (read + write) of one decoder_mk_kernel launch of this step, from the ncu capture summarised in
 # profiles/decoder_mk_kernel_tts06_decode_step.md (dram__bytes_read.sum + dram__bytes_write.sum).
-DECODE_TRAFFIC = {"dram_bytes_per_step": 471756800 + 3960064,
+DECODE_TRAFFIC = {"dram_bytes_per_step": 471652608 + 4275968,
                   "source": "ncu --set full of one decoder_mk_kernel launch (profiles/decoder_mk_kernel_tts06_decode_step.md)"}
 
 
