@@ -316,9 +316,21 @@ __global__ void __launch_bounds__(kQThreads, KqLayout<KIND>::kCtasPerSm)
             for (int st = 0; st < nstage && !give_up; st++, sg++) {
                 const int s = sg % S;
                 if ((st & 1) == 1) {
-                    // the super-block's accumulators, after its second stage: one integer and one float step, in
-                    // super-block order. The stage's (d, dmin) and dx are read after the accumulator wait: the MMAs
-                    // that filled it consumed this stage, so its bulk copies have landed.
+                    // the super-block's (d, dmin) and dx come with its second stage: read them into registers as soon
+                    // as the stage has landed and hand the stage back, so the ring is paced by the MMAs alone; then
+                    // one integer and one float step on the accumulators, in super-block order
+                    if (!mbar_wait_sleep(&full[s], (sg / S) & 1)) {
+                        if (lane == 0) atomicOr(p.err, kErrTimeout);
+                        give_up = 1;
+                        break;
+                    }
+                    const uint8_t * dd = smem + s * L::kStage + L::kA + L::kB;
+                    const float4 ddv = reinterpret_cast<const float4 *>(dd)[row];
+                    float dxr[32];
+#pragma unroll
+                    for (int i = 0; i < 32; i++) dxr[i] = reinterpret_cast<const float *>(dd + L::kDd)[32 * h + i];
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&empty[s]);
                     const int buf = g2 % 2, use = g2 / 2;
                     g2++;
                     if (!mbar_wait_sleep(&acc_full[buf], use & 1)) {
@@ -327,9 +339,6 @@ __global__ void __launch_bounds__(kQThreads, KqLayout<KIND>::kCtasPerSm)
                         break;
                     }
                     tc_fence_after();
-                    const uint8_t * dd = smem + s * L::kStage + L::kA + L::kB;
-                    const float4 ddv = reinterpret_cast<const float4 *>(dd)[row];
-                    const float * dx = reinterpret_cast<const float *>(dd + L::kDd);
 #pragma unroll
                     for (int hf = 0; hf < 2; hf++) {
                         if (32 * h + 16 * hf >= nz) break;  // warp-uniform
@@ -341,7 +350,7 @@ __global__ void __launch_bounds__(kQThreads, KqLayout<KIND>::kCtasPerSm)
 #pragma unroll
                         for (int i = 0; i < 16; i++) {
                             if (16 * hf + i >= live) break;
-                            const float dxv = dx[32 * h + 16 * hf + i];
+                            const float dxv = dxr[16 * hf + i];
                             int sumi, summ;
                             kq_combine<KIND>(A, i, sumi, summ);
                             float & a = acc[16 * hf + i];
@@ -352,9 +361,10 @@ __global__ void __launch_bounds__(kQThreads, KqLayout<KIND>::kCtasPerSm)
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&acc_empty[buf]);
+                    continue;
                 }
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[s]);  // the stage's scales are read: it may be refilled
+                if (lane == 0) mbar_arrive(&empty[s]);  // nothing of the super-block's first stage is read here
             }
             if (give_up) break;
             if (live <= 0) continue;
