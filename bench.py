@@ -1,15 +1,21 @@
-"""bench.py — decode tokens/s of the Qwen3-TTS 0.6B talker decode-step matmul stack on B200.
+"""bench.py — MoE tokens/s of the Drama3-like routed-expert FFN stack on 1, 2, 4 or 8 B200s.
 
 Contract (the driver's): `python bench.py --gpus N --steps K --warmup W [--impl reference]` prints ONE JSON line.
-A step is one decode step: 28 layers x {q|k|v, o, gate|up, down} Q8_0 products plus the 1024 -> 3072 codec head,
-with the decoder's glue (RMSNorm, SwiGLU, residuals) fused into the products, for one token. Weights are random
-N(0, 0.02) quantized on the device by the backend's own Q8_0 quantizer (bit-identical to ggml's reference row
-quantizer); the input row is N(0, 1). The weights (471 MB) are larger than L2 (126 MB), so every step streams them
-from HBM. The single-stream step does not shard: with N > 1 each rank runs an independent replica ("replicas only")
-and `value` is the sum over ranks (N x steps / max-over-ranks time).
+A step is one pass of config 5's stack over one batch: 48 layers of b200_moe_ffn (gate|up MUL_MAT_ID 2048 -> 1536,
+SwiGLU, down MUL_MAT_ID 768 -> 2048, router-weighted sum; TextModel::experts, src/families/drama3/text-model.cpp:198-221)
+over 128 Q8_0 experts, top-8 routes of N(0, 1) router logits, 256 N(0, 1) tokens, each layer's output the next layer's
+input. With N GPUs the experts are split across the ranks (expert parallelism: rank r holds experts [r E/N, (r+1) E/N)
+of every layer) and the ranks' partial sums are added over NVLink every layer, so every rank holds the full layer
+output; the same 256 tokens at every N (strong scaling). `value` = tokens/s of the whole job (256 x K / the
+max-over-ranks device time).
 
-`--impl reference` times the CPU restatement of ggml's CPU backend (oracle/, the reference's own CPU path restated;
-ggml itself is absent from the reference checkout) on a bounded sample of the same step, with all host threads.
+At N = 1 the line also carries the other configurations of BASELINE.json as side keys (`configs`): config 2's decode
+step, config 1's single GEMV, config 3's decode step and prefill (as a fraction of the measured int8 tensor peak),
+config 4's batched stack and single large GEMVs; and, in the CPU-baseline leg, a parity check of the timed stack's
+first layer against the CPU oracle on the same weights and inputs.
+
+`--impl reference` times the CPU restatement of ggml's CPU backend (oracle/; ggml itself is absent from the reference
+checkout) on the same stack — all 48 layers, chained — for a sample of the tokens, with every host thread.
 """
 
 import argparse
@@ -23,9 +29,32 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-CONFIG = "tts06"
-METRIC = "decode tok/s, Qwen3-TTS 0.6B talker decode-step matmul stack (Q8_0, batch 1)"
 UNIT = "tok/s"
+MOE = {"n_expert": 128, "top_k": 8, "hidden": 2048, "ffn": 768, "n_layer": 48, "tokens": 256}
+MOE_METRIC = "MoE tok/s, Drama3-like MoE FFN stack (48 layers x 128 Q8_0 experts, top-8, 2048<->768), 256 tokens per step"
+MOE_WORKLOAD = ("config 5: 48 chained layers of b200_moe_ffn (gate|up 2048->1536, SwiGLU, down 768->2048, weighted sum) over "
+                "128 Q8_0 experts, top-8 of N(0,1) router logits, 256 N(0,1) tokens")
+# kernels of this library launched per MoE layer (route+quantize, gate|up with SwiGLU, down, combine; at N > 1 the
+# combine also adds the ranks' partial sums over NVLink, or an NCCL all-reduce follows it)
+MOE_KERNELS_PER_LAYER = 6
+
+Q8_0, Q4_K, Q6_K = 8, 12, 14
+# Decoder stacks of BASELINE.json: the Qwen3-TTS 0.6B talker (config 2), the Qwen3-ASR 1.7B-shaped decoder (config 3)
+DECODERS = {
+    "tts06": dict(n_layer=28, hidden=1024, n_head=16, n_kv_head=8, head_dim=128, ffn=3072, n_vocab=3072,
+                  type_attn=Q8_0, type_ffn_up=Q8_0, type_ffn_down=Q8_0, type_head=Q8_0),
+    "asr17": dict(n_layer=28, hidden=2048, n_head=16, n_kv_head=8, head_dim=128, ffn=6144, n_vocab=151936,
+                  type_attn=Q4_K, type_ffn_up=Q4_K, type_ffn_down=Q6_K, type_head=Q6_K),
+}
+
+
+def decoder_tensor_shapes(c):
+    """(type, K, N) of each matrix of one decoder layer, and of the head."""
+    attn, kv = c["n_head"] * c["head_dim"], c["n_kv_head"] * c["head_dim"]
+    h, f = c["hidden"], c["ffn"]
+    return {"attn_q": (c["type_attn"], h, attn), "attn_k": (c["type_attn"], h, kv), "attn_v": (c["type_attn"], h, kv),
+            "attn_o": (c["type_attn"], attn, h), "ffn_gate": (c["type_ffn_up"], h, f), "ffn_up": (c["type_ffn_up"], h, f),
+            "ffn_down": (c["type_ffn_down"], f, h), "output": (c["type_head"], h, c["n_vocab"])}
 
 
 def load_package():
@@ -51,19 +80,25 @@ def peaks():
         return 6650.0, "fallback"
 
 
-# DRAM bytes (read + write) of one decoder_mk_kernel launch of this step, from the ncu capture summarised in
-# profiles/decoder_mk_kernel_tts06_decode_step.md (dram__bytes_read.sum + dram__bytes_write.sum).
-DECODE_TRAFFIC = {"dram_bytes_per_step": 471652608 + 4275968,
-                  "source": "ncu --set full of one decoder_mk_kernel launch (profiles/decoder_mk_kernel_tts06_decode_step.md)"}
+def peak_fields(peak, kind):
+    return {"peak": peak, "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if kind == "measured" else "fallback 6650 GB/s"}
 
 
-# DRAM bytes of one layer's two gemm_q8_0_tc_grouped_kernel launches (gate|up + down) from the ncu capture of the
-# 2-layer case summarised in profiles/gemm_q8_0_tc_grouped_config5.md; the step's traffic scales with its layers.
+def host_threads():
+    """Every host thread this process may run on (torchrun sets OMP_NUM_THREADS=1 for its ranks; the CPU legs pass
+    this count to the oracle explicitly)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+# DRAM bytes (read + write) of one decoder_mk_kernel launch of the config-2 step, from an ncu capture of that launch
+# (dram__bytes_read.sum + dram__bytes_write.sum).
+DECODE_TRAFFIC = 471652608 + 4275968
+# DRAM bytes of one MoE layer's two gemm_q8_0_tc_grouped_kernel launches (gate|up + down) from an ncu capture of the
+# 2-layer case on one GPU; the step's traffic scales with its layers and, across N ranks, divides by N.
 MOE_TRAFFIC_PER_LAYER = 434762496 + 12986368 + 216577024 + 12018688
-
-
-def profile_traffic():
-    return DECODE_TRAFFIC
 
 
 class Clocks:
@@ -114,98 +149,307 @@ class Clocks:
                 "samples": len(sm)}
 
 
-def dist_setup(args):
+def dist_setup():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     return world, rank, local
 
 
-class CpuStep:
-    """The oracle's CPU step on a bounded sample (2 of the 28 layers + the head), scaled to tokens/s of the full step:
-    per token = median layer time x 28 + head time. All host threads (OpenMP) unless nthreads is given."""
+def moe_routes(c, seed=11):
+    """Per layer: router logits N(0, 1) -> softmax -> top-k (ties broken by a seeded permutation of the experts)
+    -> weights renormalised over the chosen k. Returns ids int32 [L, T, k], w float32 [L, T, k]."""
+    import numpy as np
 
-    def __init__(self, nthreads=0):
+    rng = np.random.default_rng(seed)
+    L, T, E, k = c["n_layer"], c["tokens"], c["n_expert"], c["top_k"]
+    ids = np.empty((L, T, k), dtype=np.int32)
+    w = np.empty((L, T, k), dtype=np.float32)
+    for l in range(L):
+        logits = rng.normal(0, 1, size=(T, E)).astype(np.float32)
+        p = np.exp(logits - logits.max(1, keepdims=True))
+        p /= p.sum(1, keepdims=True)
+        rank = rng.permutation(E)
+        order = np.lexsort((np.broadcast_to(rank, (T, E)), -p), axis=1)[:, :k]
+        ids[l] = order
+        sel = np.take_along_axis(p, order, 1)
+        w[l] = sel / sel.sum(1, keepdims=True)
+    return ids, w
+
+
+class CpuMoe:
+    """The CPU oracle's MoE stack (oracle/: ggml-CPU semantics restated; the reference's own CPU path): per layer the
+    gate|up MUL_MAT_ID, SwiGLU and the down MUL_MAT_ID, then the router-weighted sum in slot order, with `nthreads`
+    host threads. Used only by the reference arm, the CPU-baseline leg and its parity check.
+
+    For timing, one layer's worth of random valid Q8_0 expert blocks (641 MB, larger than any CPU cache) stands in for
+    every layer's experts: the CPU's time per layer does not depend on the weight values, and every layer still
+    streams its experts from DRAM. The routes are config 5's own (all 48 layers); `tokens` of the 256 run (a bounded
+    sample: the oracle's cost is the same for every (token, slot) pair)."""
+
+    def __init__(self, c, tokens, nthreads):
         import numpy as np
 
-        from oracle import oracle, stack
+        from oracle import oracle
 
-        self.stack = stack
-        self.c = stack.CONFIGS[CONFIG]
-        self.nthreads = nthreads
-        self.model = stack.random_model(self.c, seed=99, n_layer=2, nthreads=nthreads)
-        self.x = np.random.default_rng(5).normal(0, 1, size=self.c["hidden"]).astype(np.float32)
-        self.cores = oracle.max_threads() if nthreads <= 0 else nthreads
-        self.t_layer, self.t_head = [], []
+        self.o, self.c, self.nthreads, self.tokens = oracle, c, nthreads, tokens
+        rng = np.random.default_rng(17)
+        H, F, E = c["hidden"], c["ffn"], c["n_expert"]
 
-    def once(self):
-        st, c = self.stack, self.c
-        for L in self.model["layers"]:
-            a = time.perf_counter()
-            st.layer(c, L, self.x, 1e-6, self.nthreads)
-            self.t_layer.append(time.perf_counter() - a)
+        def blocks(rows, K):
+            b = rng.integers(-127, 128, size=(rows * (K // 32), 34), dtype=np.int8).view(np.uint8)
+            b[:, :2] = (rng.random(rows * (K // 32)) * 2e-4 + 1e-4).astype(np.float16).view(np.uint8).reshape(-1, 2)
+            return b.reshape(rows, -1)
+
+        self.gu, self.dn = blocks(E * 2 * F, H), blocks(E * H, F)
+        ids, w = moe_routes(c)
+        self.ids, self.w = ids[:, :tokens], w[:, :tokens]
+        self.x = rng.normal(0, 1, size=(tokens, H)).astype(np.float32)
+
+    def layer(self, gu, dn, x, ids, w):
+        import numpy as np
+
+        o, c = self.o, self.c
+        H, F, E = c["hidden"], c["ffn"], c["n_expert"]
+        gu_out = o.mul_mat_id(o.Q8_0, gu, H, 2 * F, E, x[:, None, :], ids, self.nthreads)
+        g, u = gu_out[..., :F], gu_out[..., F:]
+        act = (g / (np.float32(1.0) + np.exp(-g)) * u).astype(np.float32)
+        dn_out = o.mul_mat_id(o.Q8_0, dn, F, H, E, act, ids, self.nthreads)
+        out = np.zeros((x.shape[0], H), dtype=np.float32)
+        for s in range(ids.shape[1]):
+            out = (out + dn_out[:, s] * w[:, s:s + 1]).astype(np.float32)
+        return out
+
+    def step(self):
+        x = self.x
+        for l in range(self.c["n_layer"]):
+            x = self.layer(self.gu, self.dn, x, self.ids[l], self.w[l])
+        return x
+
+    def sample_text(self, steps):
+        return (f"{steps} steps of all {self.c['n_layer']} chained layers for {self.tokens} of the {self.c['tokens']} tokens "
+                f"(their config-5 routes), one layer's random Q8_0 experts (641 MB) standing in for every layer's")
+
+
+def cpu_moe_rate(c, tokens, nthreads, warmup, steps):
+    """Tokens/s of the oracle's 48-layer stack over `tokens` tokens: total tokens / total time of `steps` steps."""
+    cm = CpuMoe(c, tokens, nthreads)
+    for _ in range(warmup):
+        cm.step()
+    times = []
+    for _ in range(steps):
         a = time.perf_counter()
-        st.head(c, self.model, self.x, 1e-6, self.nthreads)
-        self.t_head.append(time.perf_counter() - a)
-        return 1.0 / ((self.t_layer[-1] + self.t_layer[-2]) / 2 * c["n_layer"] + self.t_head[-1])
-
-    def rate(self):
-        return 1.0 / (statistics.median(self.t_layer) * self.c["n_layer"] + statistics.median(self.t_head))
-
-    def sample_text(self, reps):
-        return f"{reps} passes of 2 of the 28 layers + the head (Q8_0, batch 1); median layer x 28 + median head"
+        cm.step()
+        times.append(time.perf_counter() - a)
+    return tokens * steps / sum(times), cm.sample_text(steps), times
 
 
-def cpu_sample(seconds_target=12.0, nthreads=0):
-    cs = CpuStep(nthreads)
-    cs.once()
-    reps = 0
-    t0 = time.perf_counter()
-    while time.perf_counter() - t0 < seconds_target or reps < 3:
-        cs.once()
-        reps += 1
-    return cs.rate(), cs.cores, cs.sample_text(reps)
+def moe_parity(pkg, ctx, gu, dn, x, ids, w, got, nthreads):
+    """Layer 0 of the timed GPU stack against the CPU oracle on the same weights (read back from the device as GGUF
+    bytes) and inputs: per-token cosine similarity (bar >= 0.9999, the decoder-stack bar: the SwiGLU output is
+    re-quantized) and max |err| / max |ref|."""
+    import numpy as np
+
+    from oracle import oracle
+
+    c = MOE
+    H, F, E = c["hidden"], c["ffn"], c["n_expert"]
+    gub = ctx.get_weight(gu).reshape(E * 2 * F, -1)
+    dnb = ctx.get_weight(dn).reshape(E * H, -1)
+    cm = CpuMoe.__new__(CpuMoe)
+    cm.o, cm.c, cm.nthreads = oracle, c, nthreads
+    want = cm.layer(gub, dnb, x, ids, w)
+    cos = (got * want).sum(1) / (np.linalg.norm(got, axis=1) * np.linalg.norm(want, axis=1))
+    return {"check": "layer 0 of the timed stack vs the CPU oracle on the same weights and inputs", "tokens": int(x.shape[0]),
+            "min_token_cosine": float(cos.min()), "bar": 0.9999, "max_abs_err_over_max_abs": float(np.abs(got - want).max() / np.abs(want).max()),
+            "pass": bool(cos.min() >= 0.9999)}
 
 
 def run_reference(args):
-    world, rank, local = dist_setup(args)
+    """The reference arm: the CPU oracle's stack, rank 0 only (the other ranks exit at once), all host threads."""
+    world, rank, local = dist_setup()
     if rank != 0:
         return 0
-    cs = CpuStep()
-    for _ in range(args.warmup):
-        cs.once()
-    cs.t_layer, cs.t_head = [], []
+    nthreads = host_threads()
     t0 = time.perf_counter()
-    vals = [cs.once() for _ in range(args.steps)]
+    value, sample, times = cpu_moe_rate(MOE, args.ref_tokens, nthreads, args.warmup, args.steps)
     wall = time.perf_counter() - t0
-    value = statistics.median(vals)
-    line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": 1000.0 / value, "higher_is_better": True, "scaling": "weak",
+    emit({
+        "impl": "reference", "metric": MOE_METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1000.0 * MOE["tokens"] / value, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int8xint8->int32, f32 accumulate", "data": "synthetic",
-        "config": {"workload": "qwen3-tts-0.6b talker decode step (config 2), Q8_0, batch 1", "global_batch": 1,
-                   "seq_len": 1, "parallelism": "cpu"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cs.cores, "kind": "port", "sample": cs.sample_text(args.steps)},
+        "config": {"workload": MOE_WORKLOAD, "global_batch": MOE["tokens"], "parallelism": f"cpu, {nthreads} threads"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": nthreads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "wall_s": wall,
-        "note": "CPU restatement of ggml's CPU quantized vec_dot (oracle/); ggml itself is absent from the reference checkout",
-    }
-    emit(line)
+        "wall_s": wall, "step_s_median": statistics.median(times),
+        "note": "CPU restatement of ggml's CPU quantized vec_dot (oracle/); ggml itself is absent from the reference checkout. "
+                "ms_per_step is for the full 256 tokens at this rate",
+    })
     return 0
 
 
-def make_decoder(pkg, ctx, seed, name=CONFIG):
-    """A decoder stack of stack.CONFIGS[name] with device-generated random weights: Q8_0 tensors are N(0, 0.02)
-    quantized on the device by b200_quantize_rows; K-quant tensors are random valid blocks."""
+def moe_weights(pkg, ctx, c, e0, E_local):
+    """Layer weights of experts [e0, e0 + E_local): gate|up [H, 2F, E_local] and down [F, H, E_local], Q8_0. Each
+    expert's values are N(0, 0.02) from a generator seeded by (layer, expert), quantized on the device by the backend's
+    Q8_0 quantizer, so a shard holds exactly the bytes the same experts have on one GPU."""
     import torch
 
-    from oracle import stack
+    H, F = c["hidden"], c["ffn"]
+    g = torch.Generator(device="cuda")
+    gus, dns = [], []
+    rs_gu, rs_dn = 2 * F * pkg.row_size(pkg.Q8_0, H), H * pkg.row_size(pkg.Q8_0, F)
+    for l in range(c["n_layer"]):
+        gu = ctx.weight(pkg.Q8_0, H, 2 * F, E_local)
+        dn = ctx.weight(pkg.Q8_0, F, H, E_local)
+        for j in range(E_local):
+            g.manual_seed(1_000_003 * l + e0 + j)
+            ctx.set_weight(gu, ctx.quantize_rows(pkg.Q8_0, torch.randn((2 * F, H), generator=g, device="cuda") * 0.02), offset=j * rs_gu)
+            ctx.set_weight(dn, ctx.quantize_rows(pkg.Q8_0, torch.randn((H, F), generator=g, device="cuda") * 0.02), offset=j * rs_dn)
+        gus.append(gu)
+        dns.append(dn)
+    ctx.synchronize()
+    return gus, dns
 
-    c = stack.CONFIGS[name]
+
+def run_moe(args, pkg, ctx, dist, world, rank, local):
+    """Expert parallelism: rank r holds experts [r E/N, (r+1) E/N) of every layer; activations and routes are
+    replicated (the router runs on every rank), so dispatch moves nothing; each rank computes its experts' pairs, and
+    the ranks' partial sums are added every layer (in the combine kernel over NVLink peer memory, or by an NCCL
+    all-reduce), so every rank holds the next layer's input. The 48-layer step is captured in one CUDA graph."""
+    import numpy as np
+    import torch
+
+    c = dict(MOE, n_layer=args.moe_layers)
+    E, T, H, k, L = c["n_expert"], c["tokens"], c["hidden"], c["top_k"], c["n_layer"]
+    import importlib
+
+    ep = importlib.import_module(pkg.__name__ + ".expert_parallel")
+    e0, E_local = ep.expert_shard(E, world, rank)
+    gus, dns = moe_weights(pkg, ctx, c, e0, E_local)
+    combine = args.moe_combine if world > 1 else "local"
+    peer = ep.PeerCombine(ctx, dist.group.WORLD, T, H) if combine == "peer" else None
+    moe = ep.ExpertParallelMoe(ctx, zip(gus, dns), e0, E, group=dist.group.WORLD if dist else None, peer=peer)
+    ids_h, w_h = moe_routes(c)
+    ids = torch.from_numpy(ids_h).cuda()
+    wts = torch.from_numpy(w_h).cuda()
+    xs = [torch.randn((T, H), generator=torch.Generator(device="cuda").manual_seed(7), device="cuda")]
+    xs += [torch.empty((T, H), device="cuda") for _ in range(L)]
+    stream = ctx.torch_stream()
+
+    def step():
+        moe.step(xs, ids, wts)
+
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            step()
+    torch.cuda.synchronize()
+    ctx.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    torch.cuda.synchronize()
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize()
+    ctx.synchronize()  # any device-side error (a timed-out wait) surfaces here
+
+    steps = args.steps
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for _ in range(steps):
+                graph.replay()
+            ev1.record(stream)
+        ev1.synchronize()
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    if dist:
+        dist.barrier()
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / steps
+    value = T * steps / (ms / 1000.0)
+
+    # end to end: pinned host activations and routes in, the last layer's output out, every step
+    x_pin = torch.empty((T, H), pin_memory=True).copy_(xs[0].cpu())
+    ids_pin = torch.from_numpy(ids_h).pin_memory()
+    w_pin = torch.from_numpy(w_h).pin_memory()
+    out_pin = torch.empty((T, H), pin_memory=True)
+
+    def e2e_step():
+        with torch.cuda.stream(stream):
+            xs[0].copy_(x_pin, non_blocking=True)
+            ids.copy_(ids_pin, non_blocking=True)
+            wts.copy_(w_pin, non_blocking=True)
+            graph.replay()
+            out_pin.copy_(xs[L], non_blocking=True)
+        stream.synchronize()
+
+    for _ in range(2):
+        e2e_step()
+    if dist:
+        dist.barrier()
+    e0v, e1v = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0v.record(stream)
+    for _ in range(steps):
+        e2e_step()
+    e1v.record(stream)
+    e1v.synchronize()
+    ems = e0v.elapsed_time(e1v)
+    if dist:
+        dist.barrier()
+        t = torch.tensor([ems], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ems = float(t.item())
+    del graph
+    torch.cuda.synchronize()
+    ctx.synchronize()
+    if peer is not None:
+        peer.close()
+    # what the parity check needs: layer 0's input and output (the graph's last replay) and its weights
+    keep = {"x0": xs[0].cpu().numpy(), "y0": xs[1].cpu().numpy(), "ids0": ids_h[0], "w0": w_h[0], "weights": gus + dns}
+    wbytes = sum(w.nbytes for w in gus) + sum(w.nbytes for w in dns)
+    peak, peak_kind = peaks()
+    achieved = wbytes / (ms_step / 1000.0) / 1e9
+    res = {
+        "metric": MOE_METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": steps, "warmup": args.warmup,
+        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "int8xint8->int32, f32 accumulate", "data": "synthetic",
+        "config": {"workload": MOE_WORKLOAD if L == MOE["n_layer"] else MOE_WORKLOAD.replace("48 chained", f"{L} chained"),
+                   "global_batch": T, "seq_len": 1,
+                   "parallelism": (f"expert-parallel x{world}, " + ("partial sums added by the combine kernel over NVLink peer memory"
+                                   if combine == "peer" else "NCCL all-reduce of the partial sums")) if world > 1 else "single",
+                   "l2": f"expert weights {wbytes / 1e9:.1f} GB per GPU > 126 MB L2 (each step streams them from HBM; no flush needed)"},
+        "roofline": dict({"bound": "hbm", "kernel": "the MoE layer stack per GPU (gemm_q8_0_tc_grouped_kernel, the dominant kernel, "
+                                                    "and the route / SwiGLU / combine kernels)",
+                          "achieved": achieved, "unit": "GB/s", "frac": achieved / peak,
+                          "algorithmic_bytes_per_step": wbytes, "algorithmic_unit": "expert weight bytes of this GPU's shard per step",
+                          "traffic": MOE_TRAFFIC_PER_LAYER * L // world,
+                          "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the expert GEMMs of a 2-layer "
+                                            "one-GPU capture, scaled to the step's layers and this GPU's share"}, **peak_fields(peak, peak_kind)),
+        "e2e": {"value": T * steps / (ems / 1000.0), "unit": UNIT, "h2d_bytes_per_step": T * H * 4 + ids_h[0].nbytes * L + w_h[0].nbytes * L,
+                "d2h_bytes_per_step": T * H * 4},
+        "gpu_launches": MOE_KERNELS_PER_LAYER * L * steps,
+        "clocks": clk.summary(),
+    }
+    return res, keep
+
+
+def make_decoder(pkg, ctx, seed, name="tts06"):
+    """A decoder stack of DECODERS[name] with device-generated random weights: Q8_0 tensors are N(0, 0.02) quantized
+    on the device by b200_quantize_rows; K-quant tensors are random valid blocks."""
+    import torch
+
+    c = DECODERS[name]
     d = pkg.Decoder(ctx, **c)
     g = torch.Generator(device="cuda")
     g.manual_seed(seed)
-    sh = stack.tensor_shapes(c)
+    sh = decoder_tensor_shapes(c)
 
     def blocks(t, k, rows):
         if t == pkg.Q8_0:
@@ -224,6 +468,49 @@ def make_decoder(pkg, ctx, seed, name=CONFIG):
     d.set_tensor(0, pkg.DEC_OUTPUT_NORM, 1.0 + 0.1 * torch.randn(c["hidden"], generator=g, device="cuda"))
     ctx.synchronize()
     return d, c
+
+
+def config2_decode(pkg, ctx, stream, steps, warmup, seed=1234):
+    """Config 2: decode tokens/s of the Qwen3-TTS 0.6B talker step (28 x {q|k|v 1024->4096, o 2048->1024,
+    gate|up 1024->6144, down 3072->1024} + head 1024->3072, Q8_0, batch 1), one persistent launch per step; and the
+    same end to end through b200_decoder_step_host (input row in, logits out, every step)."""
+    import numpy as np
+    import torch
+
+    dec, c = make_decoder(pkg, ctx, seed=seed)
+    x = torch.randn(c["hidden"], generator=torch.Generator(device="cuda").manual_seed(7), device="cuda")
+    logits = torch.empty(c["n_vocab"], device="cuda")
+    for _ in range(max(warmup, 3)):
+        dec.step_raw(x.data_ptr(), logits.data_ptr())
+    ctx.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(steps):
+        dec.step_raw(x.data_ptr(), logits.data_ptr())
+    ev1.record(stream)
+    ev1.synchronize()
+    ms = ev0.elapsed_time(ev1) / steps
+    xh = x.cpu().numpy()
+    out = np.empty(c["n_vocab"], dtype=np.float32)
+    for _ in range(2):
+        dec.step_host(xh, out)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        dec.step_host(xh, out)
+    e1.record(stream)
+    e1.synchronize()
+    ems = e0.elapsed_time(e1) / steps
+    wb, launches = dec.weight_bytes, dec.launches
+    del dec
+    peak, kind = peaks()
+    gbs = wb / ms / 1e6
+    return {"workload": "config 2: qwen3-tts-0.6b talker decode step, 28 x {q|k|v 1024->4096, o 2048->1024, gate|up 1024->6144, "
+                        "down 3072->1024} + head 1024->3072, Q8_0, batch 1", "steps": steps, "ms_per_step": ms, "tok_s": 1000.0 / ms,
+            "e2e_tok_s": 1000.0 / ems, "e2e_h2d_bytes_per_step": c["hidden"] * 4, "e2e_d2h_bytes_per_step": c["n_vocab"] * 4,
+            "weight_bytes": wb, "launches_per_step": launches, "gbs": gbs, "frac": gbs / peak, "bound": "hbm",
+            "kernel": "decoder_mk_kernel (the whole step, one launch)", "traffic": DECODE_TRAFFIC,
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one decoder_mk_kernel launch", **peak_fields(peak, kind)}
 
 
 def config1_gemv(pkg, ctx, stream, copies=64, calls=256, reps=10):
@@ -455,230 +742,6 @@ def _random_kquant_blocks(t, rows, K, g):
     return b.reshape(-1)
 
 
-# ---------------------------------------------------------------------------------------------------------------------
-# Config 5: Drama3-like MoE FFN stack (TextModel::experts, src/families/drama3/text-model.cpp:198-221)
-# ---------------------------------------------------------------------------------------------------------------------
-MOE = {"n_expert": 128, "top_k": 8, "hidden": 2048, "ffn": 768, "n_layer": 48, "tokens": 256}
-MOE_METRIC = "MoE tok/s, Drama3-like MoE FFN stack (48 layers x 128 Q8_0 experts, top-8, 2048<->768), 256 tokens per step"
-
-
-def moe_routes(c, seed=11):
-    """Per layer: router logits N(0, 1) -> softmax -> top-k (ties broken by a seeded permutation of the experts)
-    -> weights renormalised over the chosen k. Returns ids int32 [L, T, k], w float32 [L, T, k]."""
-    import numpy as np
-
-    rng = np.random.default_rng(seed)
-    L, T, E, k = c["n_layer"], c["tokens"], c["n_expert"], c["top_k"]
-    ids = np.empty((L, T, k), dtype=np.int32)
-    w = np.empty((L, T, k), dtype=np.float32)
-    for l in range(L):
-        logits = rng.normal(0, 1, size=(T, E)).astype(np.float32)
-        p = np.exp(logits - logits.max(1, keepdims=True))
-        p /= p.sum(1, keepdims=True)
-        rank = rng.permutation(E)
-        order = np.lexsort((np.broadcast_to(rank, (T, E)), -p), axis=1)[:, :k]
-        ids[l] = order
-        sel = np.take_along_axis(p, order, 1)
-        w[l] = sel / sel.sum(1, keepdims=True)
-    return ids, w
-
-
-def moe_weights(pkg, ctx, c, e0, E_local):
-    """Layer weights of experts [e0, e0 + E_local): gate|up [H, 2F, E_local] and down [F, H, E_local], Q8_0. Each
-    expert's values are N(0, 0.02) from a generator seeded by (layer, expert), quantized on the device by the backend's
-    Q8_0 quantizer, so a shard holds exactly the bytes the same experts have on one GPU."""
-    import torch
-
-    H, F = c["hidden"], c["ffn"]
-    g = torch.Generator(device="cuda")
-    gus, dns = [], []
-    rs_gu, rs_dn = 2 * F * pkg.row_size(pkg.Q8_0, H), H * pkg.row_size(pkg.Q8_0, F)
-    for l in range(c["n_layer"]):
-        gu = ctx.weight(pkg.Q8_0, H, 2 * F, E_local)
-        dn = ctx.weight(pkg.Q8_0, F, H, E_local)
-        for j in range(E_local):
-            g.manual_seed(1_000_003 * l + e0 + j)
-            ctx.set_weight(gu, ctx.quantize_rows(pkg.Q8_0, torch.randn((2 * F, H), generator=g, device="cuda") * 0.02), offset=j * rs_gu)
-            ctx.set_weight(dn, ctx.quantize_rows(pkg.Q8_0, torch.randn((H, F), generator=g, device="cuda") * 0.02), offset=j * rs_dn)
-        gus.append(gu)
-        dns.append(dn)
-    ctx.synchronize()
-    return gus, dns
-
-
-class CpuMoe:
-    """The oracle's MoE layer (two MUL_MAT_ID products + SwiGLU + weighted sum) on one layer's worth of random valid
-    Q8_0 expert blocks, all host threads; tokens/s of the 48-layer step = 1 / (median layer time x 48)."""
-
-    def __init__(self, c):
-        import numpy as np
-
-        from oracle import oracle
-
-        self.o, self.c = oracle, c
-        rng = np.random.default_rng(17)
-        H, F, E = c["hidden"], c["ffn"], c["n_expert"]
-
-        def blocks(rows, K):
-            b = rng.integers(-127, 128, size=(rows * (K // 32), 34), dtype=np.int8).view(np.uint8)
-            b[:, :2] = (rng.random(rows * (K // 32)) * 2e-4 + 1e-4).astype(np.float16).view(np.uint8).reshape(-1, 2)
-            return b.reshape(rows, -1)
-
-        self.gu, self.dn = blocks(E * 2 * F, H), blocks(E * H, F)
-        self.x = rng.normal(0, 1, size=(c["tokens"], H)).astype(np.float32)
-        ids, w = moe_routes(dict(c, n_layer=1), seed=23)
-        self.ids, self.w = ids[0], w[0]
-        self.cores = oracle.max_threads()
-        self.t = []
-
-    def once(self):
-        import numpy as np
-
-        c, o = self.c, self.o
-        H, F, E = c["hidden"], c["ffn"], c["n_expert"]
-        a = time.perf_counter()
-        gu = o.mul_mat_id(o.Q8_0, self.gu, H, 2 * F, E, self.x[:, None, :], self.ids)
-        g, u = gu[..., :F], gu[..., F:]
-        act = (g / (np.float32(1.0) + np.exp(-g)) * u).astype(np.float32)
-        dn = o.mul_mat_id(o.Q8_0, self.dn, F, H, E, act, self.ids)
-        (dn * self.w[..., None]).sum(1)
-        self.t.append(time.perf_counter() - a)
-        return c["tokens"] / (self.t[-1] * c["n_layer"])
-
-    def rate(self):
-        return self.c["tokens"] / (statistics.median(self.t) * self.c["n_layer"])
-
-    def sample_text(self, reps):
-        return f"{reps} passes of 1 of the 48 MoE layers (128 experts, 256 tokens x top-8); median layer x 48"
-
-
-def run_moe(args, pkg, ctx, dist, world, rank, local):
-    """Expert parallelism: rank r holds experts [r E/N, (r+1) E/N) of every layer; activations and routes are
-    replicated (the router runs on every rank), so dispatch moves nothing; each rank's b200_moe_ffn leaves its
-    experts' partial sum and one all-reduce per layer combines them into the next layer's input. The 48-layer step
-    is captured in one CUDA graph. Strong scaling: the same 256 tokens per step at every N."""
-    import numpy as np
-    import torch
-
-    c = dict(MOE, n_layer=args.moe_layers)
-    E, T, H, k, L = c["n_expert"], c["tokens"], c["hidden"], c["top_k"], c["n_layer"]
-    import importlib
-
-    ep = importlib.import_module(pkg.__name__ + ".expert_parallel")
-    e0, E_local = ep.expert_shard(E, world, rank)
-    gus, dns = moe_weights(pkg, ctx, c, e0, E_local)
-    peer = ep.PeerCombine(ctx, dist.group.WORLD, T, H) if dist and args.moe_combine == "peer" else None
-    moe = ep.ExpertParallelMoe(ctx, zip(gus, dns), e0, E, group=dist.group.WORLD if dist else None, peer=peer)
-    ids_h, w_h = moe_routes(c)
-    ids = torch.from_numpy(ids_h).cuda()
-    wts = torch.from_numpy(w_h).cuda()
-    xs = [torch.randn((T, H), generator=torch.Generator(device="cuda").manual_seed(7), device="cuda")]
-    xs += [torch.empty((T, H), device="cuda") for _ in range(L)]
-    stream = ctx.torch_stream()
-
-    def step():
-        moe.step(xs, ids, wts)
-
-    with torch.cuda.stream(stream):
-        for _ in range(2):
-            step()
-    torch.cuda.synchronize()
-    ctx.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        step()
-    torch.cuda.synchronize()
-    for _ in range(max(args.warmup, 3)):
-        graph.replay()
-    torch.cuda.synchronize()
-    ctx.synchronize()  # any device-side error (a timed-out wait) surfaces here
-
-    steps = args.moe_steps
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
-    with Clocks(local) as clk:
-        with torch.cuda.stream(stream):
-            ev0.record(stream)
-            for _ in range(steps):
-                graph.replay()
-            ev1.record(stream)
-        ev1.synchronize()
-    torch.cuda.synchronize()
-    ms = ev0.elapsed_time(ev1)
-    if dist:
-        dist.barrier()
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    ms_step = ms / steps
-    value = T * steps / (ms / 1000.0)
-
-    # end to end: pinned host activations and routes in, the last layer's output out, every step
-    x_pin = torch.empty((T, H), pin_memory=True).copy_(xs[0].cpu())
-    ids_pin = torch.from_numpy(ids_h).pin_memory()
-    w_pin = torch.from_numpy(w_h).pin_memory()
-    out_pin = torch.empty((T, H), pin_memory=True)
-
-    def e2e_step():
-        with torch.cuda.stream(stream):
-            xs[0].copy_(x_pin, non_blocking=True)
-            ids.copy_(ids_pin, non_blocking=True)
-            wts.copy_(w_pin, non_blocking=True)
-            graph.replay()
-            out_pin.copy_(xs[L], non_blocking=True)
-        stream.synchronize()
-
-    for _ in range(2):
-        e2e_step()
-    if dist:
-        dist.barrier()
-    e0v, e1v = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0v.record(stream)
-    for _ in range(steps):
-        e2e_step()
-    e1v.record(stream)
-    e1v.synchronize()
-    ems = e0v.elapsed_time(e1v)
-    if dist:
-        dist.barrier()
-        t = torch.tensor([ems], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ems = float(t.item())
-    del graph
-    torch.cuda.synchronize()
-    ctx.synchronize()
-    if peer is not None:
-        peer.close()
-    wbytes = sum(w.nbytes for w in gus) + sum(w.nbytes for w in dns)
-    for w in gus + dns:
-        ctx.free_weight(w)
-    peak, peak_kind = peaks()
-    achieved = wbytes / (ms_step / 1000.0) / 1e9
-    res = {
-        "metric": MOE_METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": steps, "ms_per_step": ms_step,
-        "higher_is_better": True, "scaling": "strong", "dtype": "int8xint8->int32, f32 accumulate", "data": "synthetic",
-        "config": {"workload": f"config 5: {L} x b200_moe_ffn (gate|up 2048->1536, SwiGLU, down 768->2048, weighted sum) "
-                               "over 128 Q8_0 experts, top-8 of N(0,1) router logits, 256 N(0,1) tokens",
-                   "global_batch": T,
-                   "parallelism": (f"expert-parallel x{world}, " + ("combine fused with a two-shot all-reduce over NVLink peer memory"
-                                   if peer is not None else "NCCL all-reduce of the combined outputs")) if world > 1 else "single",
-                   "l2": f"expert weights {wbytes / 1e9:.1f} GB per GPU > 126 MB L2 (no flush needed)"},
-        "roofline": {"bound": "hbm", "kernel": "the b200_moe_ffn stack (gemm_q8_0_tc_grouped_kernel x 2 + 4 glue kernels per layer)",
-                     "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6650",
-                     "algorithmic_bytes_per_step": wbytes,
-                     "traffic": MOE_TRAFFIC_PER_LAYER * L // world,
-                     "traffic_source": "ncu capture of the 2-layer case (profiles/gemm_q8_0_tc_grouped_config5.md), scaled by layers and shards"},
-        "e2e": {"value": T * steps / (ems / 1000.0), "unit": UNIT, "h2d_bytes_per_step": T * H * 4 + ids_h.nbytes + w_h.nbytes,
-                "d2h_bytes_per_step": T * H * 4},
-        "gpu_launches": 6 * L * steps,
-        "clocks": clk.summary(),
-    }
-    return res
-
-
 def run_batched(args, pkg, ctx, dist, world, rank, local):
     """Config 4 over N GPUs: the Qwen3-TTS 1.7B-shaped talker's products (28 x {q|k|v 2048->4096, o 2048->2048,
     gate|up 2048->12288, down 6144->2048}, Q8_0) for M = 64 streams, every product split by output rows (rank r holds
@@ -722,7 +785,7 @@ def run_batched(args, pkg, ctx, dist, world, rank, local):
     for _ in range(max(args.warmup, 3)):
         graph.replay()
     torch.cuda.synchronize()
-    steps = args.moe_steps
+    steps = args.steps
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if dist:
         dist.barrier()
@@ -800,7 +863,7 @@ def run_prefill(args, pkg, ctx, dist, world, rank, local):
     if dist:
         dist.barrier()
     with Clocks(local) as clk:
-        r = config3_prefill(pkg, ctx, stream, reps=max(2, args.moe_steps // 5))
+        r = config3_prefill(pkg, ctx, stream, reps=max(2, args.steps // 5))
     ms = r["ms"]
     if dist:
         t = torch.tensor([ms], device="cuda")
@@ -812,35 +875,55 @@ def run_prefill(args, pkg, ctx, dist, world, rank, local):
         ipeak, ipeak_src = 4500.0, "nominal dense int8 (the library int8 GEMM was unavailable)"
     return {
         "metric": "prefill rows/s, Qwen3-ASR 1.7B-shaped decoder products (Q4_K / Q6_K), M = 1500", "value": world * 1500 * 1000.0 / ms,
-        "unit": "rows/s", "n_gpus": world, "steps": max(2, args.moe_steps // 5), "ms_per_step": ms, "higher_is_better": True,
+        "unit": "rows/s", "n_gpus": world, "steps": max(2, args.steps // 5), "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "dtype": "int8xint8->int32, f32 accumulate", "data": "synthetic",
         "config": {"workload": "config 3 prefill: 28 x {q|k|v 2048->4096, o 2048->2048, gate|up 2048->12288 Q4_K, down 6144->2048 Q6_K}"
                                " x 1500 rows + head 2048->151936 Q6_K x 1 row", "global_batch": 1500 * world,
                    "parallelism": f"replicas x{world}" if world > 1 else "single"},
         "roofline": {"bound": "tensor", "kernel": "gemm_kq_tc_kernel", "achieved": r["int8_tops"], "unit": "TOP/s int8",
                      "peak": ipeak, "frac": r["int8_tops"] / ipeak, "peak_source": ipeak_src, "traffic": None},
-        "clocks": clk.summary(), "gpu_launches": (28 * 4 * 2 + 1) * max(2, args.moe_steps // 5),
+        "clocks": clk.summary(), "gpu_launches": (28 * 4 * 2 + 1) * max(2, args.steps // 5),
     }
+
+
+def side_configs(args, pkg, ctx):
+    """BASELINE.json's other configurations at one GPU, each with its roofline fraction."""
+    stream = ctx.torch_stream()
+    peak, kind = peaks()
+    out = {"c2_tts06_decode": config2_decode(pkg, ctx, stream, steps=max(args.steps, 100), warmup=args.warmup)}
+    r = config1_gemv(pkg, ctx, stream)
+    out["c1_gemv_q8_0"] = dict(r, frac=r["gbs"] / peak, bound="hbm", **peak_fields(peak, kind))
+    r = config3_decode(pkg, ctx, stream)
+    out["c3_asr17_decode"] = dict(r, frac=r["gbs"] / peak, bound="hbm", **peak_fields(peak, kind))
+    r = config3_prefill(pkg, ctx, stream)
+    ipeak, isrc = int8_peak_or_nominal()
+    out["c3_asr17_prefill"] = dict(r, bound="int8 tensor", frac=r["int8_tops"] / ipeak, peak=ipeak, peak_unit="TOP/s int8", peak_source=isrc,
+                                   hbm_frac=r["gbs"] / peak)
+    r = config4_batched(pkg, ctx, stream)
+    out["c4_batched_m64"] = dict(r, frac=r["gbs"] / peak, bound="hbm", int8_frac=r["int8_tops"] / ipeak, **peak_fields(peak, kind))
+    out["gemv_large"] = {k: dict(v, frac=v["gbs"] / peak) for k, v in large_gemv(pkg, ctx, stream).items()}
+    return out
+
+
+def int8_peak_or_nominal():
+    ipeak = int8_peak_tops()
+    if ipeak:
+        return ipeak, "measured: torch._int_mm (cuBLASLt) int8 8192^3, best of 5-launch means over 1 s"
+    return 4500.0, "nominal dense int8 (the library int8 GEMM was unavailable)"
 
 
 def run_b200(args):
     import torch
 
-    world, rank, local = dist_setup(args)
+    world, rank, local = dist_setup()
     dist = None
+    torch.cuda.set_device(local)
     if world > 1:
         import datetime
 
         import torch.distributed as dist
 
-        torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
-    else:
-        torch.cuda.set_device(local)
-
-    def barrier():
-        if dist:
-            dist.barrier()
 
     pkg = load_package()
     ctx = pkg.Context(local)
@@ -855,123 +938,58 @@ def run_b200(args):
               "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 x q8",
               "data": "synthetic", "config": {"workload": f"single product {args.gemv_case}", "K": v["K"], "N": v["N"],
                                               "l2": "weights > 126 MB L2"},
-              "roofline": {"bound": "hbm", "achieved": v["gbs"], "peak": peak, "unit": "GB/s", "frac": v["gbs"] / peak,
-                           "peak_source": kind}})
+              "roofline": dict({"bound": "hbm", "achieved": v["gbs"], "unit": "GB/s", "frac": v["gbs"] / peak}, **peak_fields(peak, kind))})
         ctx.close()
         return 0
-    if args.workload in ("moe", "batched", "prefill"):
-        res = {"moe": run_moe, "batched": run_batched, "prefill": run_prefill}[args.workload](args, pkg, ctx, dist, world, rank, local)
+    if args.workload == "decode":
+        r = config2_decode(pkg, ctx, ctx.torch_stream(), steps=args.steps, warmup=args.warmup, seed=1234 + rank)
+        ctx.close()
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
+        if rank == 0:
+            emit({"metric": "decode tok/s, Qwen3-TTS 0.6B talker decode-step matmul stack (Q8_0, batch 1)", "value": r["tok_s"],
+                  "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
+                  "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xint8->int32, f32 accumulate",
+                  "data": "synthetic", "config": {"workload": r["workload"], "global_batch": 1, "seq_len": 1, "parallelism": "single"},
+                  "roofline": {k: r[k] for k in ("bound", "kernel", "frac", "peak", "peak_source", "traffic", "traffic_source")} | {
+                      "achieved": r["gbs"], "unit": "GB/s"},
+                  "e2e": {"value": r["e2e_tok_s"], "unit": UNIT, "h2d_bytes_per_step": r["e2e_h2d_bytes_per_step"],
+                          "d2h_bytes_per_step": r["e2e_d2h_bytes_per_step"]}, "gpu_launches": r["launches_per_step"] * args.steps})
+        return 0
+    if args.workload in ("batched", "prefill"):
+        res = {"batched": run_batched, "prefill": run_prefill}[args.workload](args, pkg, ctx, dist, world, rank, local)
         ctx.close()
         if dist:
             dist.barrier()
             dist.destroy_process_group()
         if rank == 0:
             res.update(warmup=args.warmup, vs_baseline=None)
-            if world == 1 and not args.no_cpu and args.workload == "moe":
-                cm = CpuMoe(MOE)
-                cm.once()
-                t0 = time.perf_counter()
-                reps = 0
-                while time.perf_counter() - t0 < 12.0 or reps < 3:
-                    cm.once()
-                    reps += 1
-                res["cpu_baseline"] = {"value": cm.rate(), "unit": UNIT, "cores": cm.cores, "kind": "port", "sample": cm.sample_text(reps)}
             emit(res)
         return 0
-    dec, c = make_decoder(pkg, ctx, seed=1234 + rank)
-    stream = ctx.torch_stream()
-    x = torch.randn(c["hidden"], generator=torch.Generator(device="cuda").manual_seed(7), device="cuda")
-    logits = torch.empty(c["n_vocab"], device="cuda")
-    torch.cuda.synchronize()
-    for _ in range(max(args.warmup, 3)):
-        dec.step_raw(x.data_ptr(), logits.data_ptr())
-    ctx.synchronize()
 
-    # ---- device-resident timing: K steps back to back on the context stream ----
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    torch.cuda.synchronize()
-    with Clocks(local) as clk:
-        ev0.record(stream)
-        for _ in range(args.steps):
-            dec.step_raw(x.data_ptr(), logits.data_ptr())
-        ev1.record(stream)
-        ev1.synchronize()
-    torch.cuda.synchronize()
-    barrier()
-    ms = ev0.elapsed_time(ev1)
+    # ---- the headline: config 5 ----
+    res, keep = run_moe(args, pkg, ctx, dist, world, rank, local)
     if dist:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    ms_step = ms / args.steps
-    value = world * args.steps / (ms / 1000.0)
-
-    # ---- end to end through the public host API: pinned input in, logits out, every step ----
-    import numpy as np
-
-    xh = x.cpu().numpy()
-    out = np.empty(c["n_vocab"], dtype=np.float32)
-    for _ in range(2):
-        dec.step_host(xh, out)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    e0.record(stream)
-    for _ in range(args.steps):
-        dec.step_host(xh, out)
-    e1.record(stream)
-    e1.synchronize()
-    ems = e0.elapsed_time(e1)
-    if dist:
-        t = torch.tensor([ems], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ems = float(t.item())
-    e2e_value = world * args.steps / (ems / 1000.0)
-
-    wbytes = dec.weight_bytes
-    launches = dec.launches
-    gemv = large_gemv(pkg, ctx, stream) if world == 1 or rank == 0 else None
-    extra = None
-    if world == 1 and not args.no_configs:
-        del dec
-        dec = None
-        extra = {"c1_gemv_q8_0": config1_gemv(pkg, ctx, stream), "c3_asr17_decode": config3_decode(pkg, ctx, stream),
-                 "c4_batched_m64": config4_batched(pkg, ctx, stream), "c3_asr17_prefill": config3_prefill(pkg, ctx, stream)}
-    peak, peak_kind = peaks()
-    achieved = wbytes / (ms_step / 1000.0) / 1e9  # GB/s of algorithmic weight bytes, per GPU
-    traffic = profile_traffic()
-    result = None
-    if rank == 0:
-        result = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "int8xint8->int32, f32 accumulate", "data": "synthetic",
-            "config": {"workload": "qwen3-tts-0.6b talker decode step (config 2): 28 x {q|k|v 1024->4096, o 2048->1024, "
-                                   "gate|up 1024->6144, down 3072->1024} + head 1024->3072, Q8_0, batch 1",
-                       "global_batch": world, "seq_len": 1, "parallelism": f"replicas x{world}" if world > 1 else "single",
-                       "l2": "weights 471 MB > 126 MB L2 each step (no flush needed)"},
-            "roofline": {"bound": "hbm", "kernel": "decoder_mk_kernel (the whole step, one launch)" if launches == 1 else "gemv_tma_kernel<TQ8_0,1> (every launch of the step)",
-                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6650",
-                         "algorithmic_bytes_per_step": wbytes, "launches_per_step": launches,
-                         "traffic": traffic.get("dram_bytes_per_step") if traffic else None,
-                         "traffic_source": traffic.get("source") if traffic else None},
-            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": c["hidden"] * 4, "d2h_bytes_per_step": c["n_vocab"] * 4},
-            "gpu_launches": launches * args.steps,
-            "gemv_large": {k: dict(v, frac=v["gbs"] / peak) for k, v in (gemv or {}).items()},
-            "configs": {k: dict(v, frac=v["gbs"] / peak) for k, v in (extra or {}).items()},
-            "clocks": clk.summary(),
-        }
-    del dec
+        dist.barrier()
+    if rank == 0 and world == 1 and not args.no_cpu:
+        # the CPU-baseline leg: the oracle's stack timed on this host, and the parity check of layer 0 on the same
+        # weights and inputs as the GPU's
+        nthreads = host_threads()
+        res["parity"] = moe_parity(pkg, ctx, keep["weights"][0], keep["weights"][args.moe_layers], keep["x0"], keep["ids0"], keep["w0"],
+                                   keep["y0"], nthreads)
+        v, sample, _ = cpu_moe_rate(MOE, args.ref_tokens, nthreads, 1, 3)
+        res["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": nthreads, "kind": "port", "sample": sample}
+    for w in keep["weights"]:
+        ctx.free_weight(w)
+    if rank == 0 and world == 1 and not args.no_configs:
+        res["configs"] = side_configs(args, pkg, ctx)
     ctx.close()
     if dist:
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
-        if world == 1 and not args.no_cpu:
-            v, cores, sample = cpu_sample(12.0)
-            result["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
-        emit(result)
+        emit(res)
     return 0
 
 
@@ -1005,21 +1023,19 @@ def main():
     _QUIET = _StdoutToStderr()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
-    ap.add_argument("--no-configs", action="store_true", help="skip the config 1 and config 3 side measurements")
-    ap.add_argument("--workload", default="decode", choices=["decode", "moe", "batched", "prefill", "gemv"],
-                    help="decode: config 2 decode step (the headline line); moe: config 5 MoE FFN stack, expert-parallel; "
-                         "batched: config 4 product stack, column-split; prefill: config 3 prefill; gemv: one large "
-                         "single-column product (--gemv-case)")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline and parity leg")
+    ap.add_argument("--no-configs", action="store_true", help="skip the side measurements of configs 1-4")
+    ap.add_argument("--workload", default="moe", choices=["moe", "decode", "batched", "prefill", "gemv"],
+                    help="moe: config 5, expert-parallel (the headline line); decode: config 2's decode step alone; batched: "
+                         "config 4, column-split; prefill: config 3's prefill; gemv: one large single-column product")
     ap.add_argument("--gemv-case", default="q8_0", choices=list(GEMV_CASES), help="product of --workload gemv")
-    ap.add_argument("--moe-steps", type=int, default=20, help="timed steps of the MoE and batched workloads")
     ap.add_argument("--moe-layers", type=int, default=48, help="MoE layers per step (48 = config 5; fewer only for profiling)")
     ap.add_argument("--moe-combine", default="nccl", choices=["peer", "nccl"],
-                    help="N > 1: NCCL all-reduce of the combined outputs (default, measured faster on 2 GPUs), or the "
-                         "combine and the all-reduce in one kernel over peer memory")
+                    help="N > 1: how the ranks' partial sums are added: an NCCL all-reduce, or the combine kernel over NVLink peer memory")
+    ap.add_argument("--ref-tokens", type=int, default=32, help="tokens of the 256 the CPU legs run through the 48 layers")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)

@@ -4,8 +4,8 @@
  * speech.cpp computes every weight product as a ggml node inside a ggml backend: MUL_MAT (src/common/graph.h:15-19),
  * MUL_MAT_ID (src/common/graph.h:22-26) and quantized GET_ROWS (src/families/qwen3-tts/talker.cpp:131-133,
  * src/families/qwen3-asr/decoder.cpp:319), run by ggml_backend_graph_compute (src/common/graph.cpp:145-147). A ggml
- * backend ("ggml-b200") forwards those nodes to the functions below; INTEGRATION.md gives the ggml_backend_i /
- * buffer-type glue. Everything here takes plain pointers and sizes: no C++ or torch types, no exceptions.
+ * backend ("ggml-b200") forwards those nodes to the functions below, its buffer type's set_tensor / get_tensor to the
+ * weight functions. Everything here takes plain pointers and sizes: no C++ or torch types, no exceptions.
  *
  * Conventions
  *  - Type ids are GGUF / ggml type ids (the reference lists them in checks/compare/quantize_compare.py:27).
@@ -88,8 +88,10 @@ b200_status b200_memcpy_d2h(b200_context * ctx, void * host_dst, const void * de
  * Weight tensors: the backend's weight buffer type. speech.cpp allocates weights in the backend's default buffer
  * type (src/common/model-file.cpp:222-245) and uploads them with ggml_backend_tensor_set in 16 MiB pieces at any
  * byte offset (src/common/model-file.cpp:247-268). b200_weight_set / _get accept the same GGUF bytes at the same
- * offsets; on the device the blocks are stored field by field (a documented repacked layout), which is
- * a byte permutation, so any piece boundary works and the device holds exactly the GGUF bytes plus alignment.
+ * offsets. On the device the blocks are stored field by field, one row-contiguous array per block field, each array
+ * 256-byte aligned (Q8_0: qs int8 [R][K] | d fp16 [R][K/32]; Q4_K: qs [R][K/2] | d, dmin, scales [R][K/256][16];
+ * Q6_K: ql [R][K/2] | qh [R][K/4] | scales [R][K/256][16] | d fp16 [R][K/256]; BF16 as is). That is a byte
+ * permutation, so any piece boundary works and the device holds exactly the GGUF bytes plus alignment.
  * ------------------------------------------------------------------------------------------------------------ */
 typedef struct b200_weight {
     int32_t type;   /* B200_TYPE_* */
@@ -252,13 +254,18 @@ b200_status b200_mul_mat_host(b200_context * ctx, const b200_weight * w, const f
  * MUL_MAT_ID without allocation. No counterpart in the reference: speech.cpp's ggml backends allocate their scratch
  * themselves. This entry point is for callers that cannot call cudaMalloc — a serving runtime that owns all device
  * memory through its own arena, a latency-critical path where an allocation could synchronize the device, a process
- * whose weights already fill the GPU. It computes exactly what b200_mul_mat_id computes (same kernels, same
- * results) on `stream` (a cudaStream_t of the current device, which must be the experts' device), with its scratch in
- * a static device array of B200_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds until exit. The
- * first call on a device looks up that array's device address (cudaGetSymbolAddress); make it before any stream
- * capture. A call needs about T*nb1*K bytes of quantized activations plus 8*T*top_k + 4*E bytes of routing tables;
- * a call that needs more than the array returns B200_ERR_INVALID. Calls share the array: two calls that overlap on
- * the GPU race. Ids outside [0, E) are skipped (their dst rows are left unchanged) and not reported.
+ * whose weights already fill the GPU. It runs the grouped GEMV path of b200_mul_mat_id for every size, on `stream` (a
+ * cudaStream_t of the current device, which must be the experts' device). Its results equal b200_mul_mat_id's bit for
+ * bit wherever b200_mul_mat_id takes that path too (any type other than Q8_0, and Q8_0 with fewer than 128
+ * (token, slot) pairs); for Q8_0 with 128 pairs or more b200_mul_mat_id runs the tensor-core grouped GEMM, and the two
+ * agree within the products' tolerance, |err| <= 1e-4 * sum |w x| per element. The experts' upload must be complete
+ * before the call, or ordered before it by the caller: b200_weight_set runs on the context's stream, which nothing
+ * orders against `stream`. Its scratch is a static device array of B200_NOALLOC_SCRATCH_BYTES that every GPU loading
+ * the library holds until exit. The first call on a device looks up that array's device address
+ * (cudaGetSymbolAddress); make it before any stream capture. A call needs about T*nb1*K bytes of quantized
+ * activations plus 8*T*top_k + 4*E bytes of routing tables; a call that needs more than the array returns
+ * B200_ERR_INVALID. Calls share the array: two calls that overlap on the GPU race. Ids outside [0, E) are skipped
+ * (their dst rows are left unchanged) and not reported.
  * ------------------------------------------------------------------------------------------------------------ */
 #define B200_NOALLOC_SCRATCH_BYTES (16u << 20)
 b200_status b200_mul_mat_id_noalloc(void * stream, const b200_weight * experts, const float * b, int64_t nb1,

@@ -385,18 +385,26 @@ int oracle_dequantize_row(int type, const void * vx, float * y, int64_t k) {
 }
 
 /* ---------------------------------------------------------------------------------------------------------------
- * Dot products. Integer parts are exact; the float order is: per block, float(int32 sum) times the block scale,
- * added to one float32 accumulator in block order.
+ * Dot products. Integer parts are exact. Each (super-)block contributes ggml's term: its exact int32 sum times the
+ * float32 product of the two scales, formed as ggml's CPU vec_dot forms it (Q8_0: d_w * d_x; Q4_K: d_x * d and
+ * d_x * dmin; Q6_K: d * d_x). ggml accumulates those terms in float32, in an order that depends on its SIMD path
+ * (the generic C loop goes in block order; the AVX2, AVX-512 and NEON loops keep 8, 16 or 4 partial sums and add them
+ * at the end), so no single float32 order is ggml's. The oracle takes the one order-free definition: the exact sum of
+ * the terms, rounded once to float32. Each term is exact in double (a 24-bit float times an integer below 2^26) and
+ * the double sum's own rounding is about 1e-16 of the sum of magnitudes, so the result is the exactly rounded sum
+ * unless the true sum lies within that distance of a float32 rounding boundary. Every ggml order lies within a few
+ * float32 ulps of it, inside the products' stated tolerance (1e-4 of sum |w x|).
  * ------------------------------------------------------------------------------------------------------------- */
 
 static float dot_q8_0(const oracle_block_q8_0 * w, const oracle_block_q8_0 * x, int64_t nb) {
-    float sumf = 0.0f;
+    double sum = 0.0;
     for (int64_t i = 0; i < nb; i++) {
         int sumi = 0;
         for (int j = 0; j < 32; j++) sumi += (int) w[i].qs[j] * (int) x[i].qs[j];
-        sumf += (float) sumi * (oracle_fp16_to_fp32(w[i].d) * oracle_fp16_to_fp32(x[i].d));
+        const float d = oracle_fp16_to_fp32(w[i].d) * oracle_fp16_to_fp32(x[i].d);
+        sum += (double) d * (double) sumi;
     }
-    return sumf;
+    return (float) sum;
 }
 
 static void sums_q4_K(const oracle_block_q4_K * w, const oracle_block_q8_K * x, int32_t * sumi, int32_t * summ) {
@@ -424,25 +432,25 @@ static int32_t sums_q6_K(const oracle_block_q6_K * w, const oracle_block_q8_K * 
 }
 
 static float dot_q4_K(const oracle_block_q4_K * w, const oracle_block_q8_K * x, int64_t nb) {
-    float sumf = 0.0f;
+    double sum = 0.0;
     for (int64_t i = 0; i < nb; i++) {
         int32_t sumi, summ;
         sums_q4_K(&w[i], &x[i], &sumi, &summ);
         const float d = x[i].d * oracle_fp16_to_fp32(w[i].d);
         const float dmin = x[i].d * oracle_fp16_to_fp32(w[i].dmin);
-        sumf += d * (float) sumi;
-        sumf -= dmin * (float) summ;
+        sum += (double) d * (double) sumi;
+        sum -= (double) dmin * (double) summ;
     }
-    return sumf;
+    return (float) sum;
 }
 
 static float dot_q6_K(const oracle_block_q6_K * w, const oracle_block_q8_K * x, int64_t nb) {
-    float sumf = 0.0f;
+    double sum = 0.0;
     for (int64_t i = 0; i < nb; i++) {
         const float d = oracle_fp16_to_fp32(w[i].d) * x[i].d;
-        sumf += d * (float) sums_q6_K(&w[i], &x[i]);
+        sum += (double) d * (double) sums_q6_K(&w[i], &x[i]);
     }
-    return sumf;
+    return (float) sum;
 }
 
 static float dot_bf16(const uint16_t * w, const uint16_t * x, int64_t k) {

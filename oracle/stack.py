@@ -2,8 +2,9 @@
 
 Follows Qwen3Decoder::layers / outputs (src/common/qwen3-decoder.cpp:350-413, 422-438) for one token at the first
 position of a sequence (attention output = each query head's key/value head's value row). Products go through the
-oracle's ggml-CPU-semantics mul_mat; the glue is float32 as ggml's CPU computes it: rms_norm sums squares in double,
-scale = 1/sqrt(mean + eps) in float; silu(x) = x / (1 + exp(-x)).
+oracle's ggml-CPU-semantics mul_mat; the glue is float32 as ggml's CPU computes it, with its two order-dependent reductions defined order-free: rms_norm sums
+the squares in double (rounded once to float32 for the mean), scale = 1/sqrt(mean + eps) in float32, (x * scale) * w;
+silu(x) = x / (1 + exp(-x)) in double, rounded once.
 """
 
 import numpy as np
@@ -44,21 +45,23 @@ def weight_bytes(c):
     return per_layer * c["n_layer"] + oracle.row_size(t, k) * n
 
 
-def random_model(c, seed=1234, n_layer=None, sigma=0.02, nthreads=0):
-    """GGUF bytes of random N(0, sigma) weights (quantized by the oracle) and N(1, 0.1) norm weights."""
+def random_model(c, seed=1234, n_layer=None, sigma=0.02, nthreads=0, normal=None):
+    """GGUF bytes of random N(0, sigma) weights (quantized by the oracle) and N(1, 0.1) norm weights. `normal(shape)`,
+    when given, draws the weights' N(0, 1) values instead of NumPy (the full-size configs use a faster generator)."""
     rng = np.random.default_rng(seed)
+    draw = normal if normal is not None else (lambda shape: rng.normal(0, 1, size=shape))
     sh = tensor_shapes(c)
     layers = []
     for _ in range(c["n_layer"] if n_layer is None else n_layer):
         L = {}
         for name in TENSORS:
             t, k, n = sh[name]
-            L[name] = oracle.quantize(t, rng.normal(0, sigma, size=(n, k)).astype(np.float32), nthreads)
+            L[name] = oracle.quantize(t, (np.float32(sigma) * draw((n, k))).astype(np.float32), nthreads)
         L["attn_norm"] = rng.normal(1.0, 0.1, size=c["hidden"]).astype(np.float32)
         L["ffn_norm"] = rng.normal(1.0, 0.1, size=c["hidden"]).astype(np.float32)
         layers.append(L)
     t, k, n = sh["output"]
-    head = oracle.quantize(t, rng.normal(0, sigma, size=(n, k)).astype(np.float32), nthreads)
+    head = oracle.quantize(t, (np.float32(sigma) * draw((n, k))).astype(np.float32), nthreads)
     out_norm = rng.normal(1.0, 0.1, size=c["hidden"]).astype(np.float32)
     return {"layers": layers, "output": head, "output_norm": out_norm}
 
@@ -71,8 +74,11 @@ def rms_norm(x, w, eps):
 
 
 def silu(x):
-    x = x.astype(np.float32)
-    return (x / (np.float32(1.0) + np.exp(-x))).astype(np.float32)
+    """x / (1 + exp(-x)) evaluated in double and rounded once to float32: the order-free definition both sides
+    compute (ggml's CPU uses a float32 exp of its own; any accurate evaluation rounds to the same float32 except in
+    rare near-ties)."""
+    x = np.asarray(x, dtype=np.float32).astype(np.float64)
+    return (x / (1.0 + np.exp(-x))).astype(np.float32)
 
 
 def layer(c, L, x, eps, nthreads=0):

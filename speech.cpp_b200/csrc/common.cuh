@@ -241,8 +241,27 @@ __device__ __forceinline__ void quantize_q8_K_warp(const float v[8], int8_t q[8]
 }
 
 // SiLU as ggml's CPU defines it, x / (1 + exp(-x)), with the hardware exponential and division (relative error
-// ~1e-6: the decoder-stack parity is judged by cosine similarity, not bit equality).
+// ~1e-6). Used where the result is judged within a tolerance (the tensor-core expert path).
 __device__ __forceinline__ float silu(float x) { return __fdividef(x, __fadd_rn(1.0f, __expf(-x))); }
+
+// SiLU evaluated in double and rounded once to float32: the order-free definition the CPU oracle uses. Any accurate
+// evaluation rounds to the same float32 except in rare near-ties, so the decode step's chain of products, whose
+// activation quantization would turn a last-bit difference into a different int8, stays identical to the oracle's.
+__device__ __forceinline__ float silu_exact(float x) {
+    const double xd = (double) x;
+    return __double2float_rn(xd / (1.0 + exp(-xd)));
+}
+
+// The float32 step of a product: the exact sum of its (super-)block terms (float32 scale product times the exact int32
+// sum, each exact in double), accumulated in double and rounded once at the end; the CPU oracle defines it the same
+// way, so the result does not depend on how lanes split the blocks.
+__device__ __forceinline__ double acc_term(double acc, float scale, int sumi) { return fma((double) scale, (double) sumi, acc); }
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
 
 // Asynchronous 4-byte global -> shared copy (completes at cp_async_wait_all; the issuing thread does not stall).
 __device__ __forceinline__ void cp_async4(void * smem_dst, const void * gmem_src) {

@@ -20,10 +20,6 @@
 
 using namespace b200;
 
-#ifdef B200_MK_PROBE
-static long long * b200_mk_probe_buffer = nullptr;
-extern "C" __attribute__((visibility("default"))) void b200_mk_probe_set(void * p) { b200_mk_probe_buffer = (long long *) p; }
-#endif
 
 struct b200_decoder {
     b200_context * ctx = nullptr;
@@ -228,9 +224,6 @@ b200_status prepare_mk(b200_decoder * d, const std::vector<GemvParams> & v) {
 b200_status enqueue_mk(b200_decoder * d) {
     cudaStream_t st = d->ctx->stream;
     MkParams P;
-#ifdef B200_MK_PROBE
-    P.probe = b200_mk_probe_buffer;
-#endif
     P.stages = d->mk_stages;
     P.nstages = d->mk_n;
     P.epoch = d->mk_epoch;

@@ -48,23 +48,8 @@ struct MkStage {
     int hd_shift;     // log2(pro_k) for PRO_GQA (-1: not a power of two)
 };
 
-// Phase timestamps for latency studies (clock64 of the CTA's thread 0 / producer lane), compiled in only with
-// -DB200_MK_PROBE: probe[cta][product][8], slots 0/1 product start, 7 inputs ready, 2 staged, 3 first weight chunk
-// landed, 5 thread 0's rows done, 4 every consumer warp done, 6 producer issued the product's first chunk.
-#ifdef B200_MK_PROBE
-#define MK_PROBE(slot) \
-    do { if (P.probe) P.probe[((size_t) blockIdx.x * P.nstages + s) * 8 + (slot)] = clock64(); } while (0)
-__shared__ long long mk_probe_ready;  // thread 0's clock when its input loads were all ready
-#define MK_PROBE_READY() do { if (threadIdx.x == 0) mk_probe_ready = clock64(); } while (0)
-#else
-#define MK_PROBE(slot) do { } while (0)
-#define MK_PROBE_READY() do { } while (0)
-#endif
 
 struct MkParams {
-#ifdef B200_MK_PROBE
-    long long * probe;
-#endif
     const MkStage * stages;
     int nstages;
     unsigned * epoch;      // steps completed (tags of this launch: epoch * nstages + s + 1)
@@ -180,7 +165,8 @@ __device__ __forceinline__ float4 mk_load4(const MkStage & S, int k, unsigned ta
         const float4 g = mk_raw4(S, k, tag, wait, ok, fail);
         const float4 u = mk_raw4(S, S.pro_k + k, tag, wait, ok2, fail);
         ok &= ok2;
-        return make_float4(__fmul_rn(silu(g.x), u.x), __fmul_rn(silu(g.y), u.y), __fmul_rn(silu(g.z), u.z), __fmul_rn(silu(g.w), u.w));
+        return make_float4(__fmul_rn(silu_exact(g.x), u.x), __fmul_rn(silu_exact(g.y), u.y), __fmul_rn(silu_exact(g.z), u.z),
+                           __fmul_rn(silu_exact(g.w), u.w));
     }
     case PRO_GQA: {
         if (S.gqa_shift >= 0 && S.hd_shift >= 0)
@@ -197,7 +183,7 @@ __device__ __forceinline__ float4 mk_load4(const MkStage & S, int k, unsigned ta
 // whether any thread's tagged loads timed out).
 // q8_0 (K % 1024 == 0): thread t holds values 4t + 1024 i; eight consecutive threads form one 32-block.
 // q8_K (K % 2048 == 0): thread t holds values 8t + 2048 i; one warp forms one 256-block.
-__device__ __forceinline__ int mk_stage_input(const MkStage & S, const Act & a, float * part, unsigned tag, int * fail) {
+__device__ __forceinline__ int mk_stage_input(const MkStage & S, const Act & a, double * part, unsigned tag, int * fail) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int K = (int) S.w.K;
     const int kind = act_kind(S.w.type);
@@ -205,7 +191,7 @@ __device__ __forceinline__ int mk_stage_input(const MkStage & S, const Act & a, 
     if (kind == B200_TYPE_Q8_K) {
         constexpr int kMax = kMkMaxK / 2048;
         float v[kMax][8];
-        float sq = 0.0f;
+        double sq = 0.0;
         // every chunk read once (all reads in flight together), then re-read until ready if any was early
         int ready = 1;
 #pragma unroll
@@ -223,20 +209,19 @@ __device__ __forceinline__ int mk_stage_input(const MkStage & S, const Act & a, 
                 }
             }
         }
-        MK_PROBE_READY();
 #pragma unroll
         for (int i = 0; i < kMax; i++)
             if (i < K / 2048)
 #pragma unroll
-                for (int j = 0; j < 8; j++) sq = fmaf(v[i][j], v[i][j], sq);
+                for (int j = 0; j < 8; j++) sq = fma((double) v[i][j], (double) v[i][j], sq);
         float rms = 0.0f;
-        if (rmsnorm) {
-            sq = warp_sum(sq);
+        if (rmsnorm) {  // squares summed in double, the mean rounded once to float32 (the oracle's definition)
+            sq = warp_sum_d(sq);
             if (lane == 0) part[warp] = sq;
             mk_sync();
-            float t = 0.0f;
+            double t = 0.0;
             for (int w = 0; w < kMkConsumerWarps; w++) t += part[w];
-            rms = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(t, (float) K), S.eps)));
+            rms = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__double2float_rn(t / (double) K), S.eps)));
         }
 #pragma unroll
         for (int i = 0; i < kMax; i++) {
@@ -265,7 +250,7 @@ __device__ __forceinline__ int mk_stage_input(const MkStage & S, const Act & a, 
     } else {
         constexpr int kMax = kMkMaxK / 1024;
         float4 v[kMax];
-        float sq = 0.0f;
+        double sq = 0.0;
         // every chunk read once (all reads in flight together), then re-read until ready if any was early
         int ready = 1;
 #pragma unroll
@@ -280,24 +265,23 @@ __device__ __forceinline__ int mk_stage_input(const MkStage & S, const Act & a, 
                 }
             }
         }
-        MK_PROBE_READY();
 #pragma unroll
         for (int i = 0; i < kMax; i++) {
             if (i < K / 1024) {
-                sq = fmaf(v[i].x, v[i].x, sq);
-                sq = fmaf(v[i].y, v[i].y, sq);
-                sq = fmaf(v[i].z, v[i].z, sq);
-                sq = fmaf(v[i].w, v[i].w, sq);
+                sq = fma((double) v[i].x, (double) v[i].x, sq);
+                sq = fma((double) v[i].y, (double) v[i].y, sq);
+                sq = fma((double) v[i].z, (double) v[i].z, sq);
+                sq = fma((double) v[i].w, (double) v[i].w, sq);
             }
         }
         float rms = 0.0f;
-        if (rmsnorm) {
-            sq = warp_sum(sq);
+        if (rmsnorm) {  // squares summed in double, the mean rounded once to float32 (the oracle's definition)
+            sq = warp_sum_d(sq);
             if (lane == 0) part[warp] = sq;
             mk_sync();
-            float t = 0.0f;
+            double t = 0.0;
             for (int w = 0; w < kMkConsumerWarps; w++) t += part[w];
-            rms = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(t, (float) K), S.eps)));
+            rms = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__double2float_rn(t / (double) K), S.eps)));
         }
 #pragma unroll
         for (int i = 0; i < kMax; i++) {
@@ -382,7 +366,7 @@ __device__ __forceinline__ void mk_issue(const MkStage & S, uint8_t * slot, int6
 template <bool kForms>
 __global__ void __launch_bounds__(kMkThreads, 1) decoder_mk_kernel(MkParams P) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ float part[kMkConsumerWarps];
+    __shared__ double part[kMkConsumerWarps];
     __shared__ int give_up;
     __shared__ float res_s[kMkResRows];
     __shared__ __align__(16) MkStage desc[3];  // this product's, the next one's, and the one after (being copied)
@@ -419,7 +403,6 @@ __global__ void __launch_bounds__(kMkThreads, 1) decoder_mk_kernel(MkParams P) {
                         atomicOr(P.err, 4u);
                         return;
                     }
-                    if (first == r0) MK_PROBE(6);
                     const int64_t rows = r1 - first < rps ? r1 - first : rps;
                     mbar_arrive_expect_tx(&full[slot], (uint32_t) (rows * rb));
                     uint8_t * dst = ring + (size_t) slot * kMkSlotBytes;
@@ -447,11 +430,9 @@ __global__ void __launch_bounds__(kMkThreads, 1) decoder_mk_kernel(MkParams P) {
     mk_sync();
     uint32_t ctr = 0;
     for (int s = 0; s < P.nstages; s++) {
-        if (threadIdx.x == 0) MK_PROBE(0);
         const MkStage & S = desc[s % 3];
         const unsigned in_tag = epoch * (unsigned) P.nstages + (unsigned) s;  // written by product s - 1
         const unsigned out_tag = in_tag + 1u;
-        if (threadIdx.x == 0) MK_PROBE(1);
         int64_t r0, r1;
         mk_slice(S, cta, r0, r1);
         // residuals of this CTA's rows (its own earlier outputs): asynchronous copies, complete before the staging
@@ -469,10 +450,6 @@ __global__ void __launch_bounds__(kMkThreads, 1) decoder_mk_kernel(MkParams P) {
             if (threadIdx.x == 0) atomicOr(P.err, 4u);
             break;
         }
-        if (threadIdx.x == 0) MK_PROBE(2);
-#ifdef B200_MK_PROBE
-        if (threadIdx.x == 0 && P.probe) P.probe[((size_t) blockIdx.x * P.nstages + s) * 8 + 7] = mk_probe_ready;
-#endif
         // the descriptor after next goes to the third buffer (this one, s % 3, stays readable during product s)
         if (s + 2 < P.nstages && threadIdx.x < kDescWords)
             cp_async4(reinterpret_cast<uint32_t *>(&desc[(s + 2) % 3]) + threadIdx.x, reinterpret_cast<const uint32_t *>(&P.stages[s + 2]) + threadIdx.x);
@@ -485,7 +462,6 @@ __global__ void __launch_bounds__(kMkThreads, 1) decoder_mk_kernel(MkParams P) {
                 give_up = 1;
                 break;
             }
-            if (threadIdx.x == 0 && first == r0) MK_PROBE(3);
             const int64_t rows = r1 - first < rps ? r1 - first : rps;
             const uint8_t * sp = ring + (size_t) slot * kMkSlotBytes;
             switch (S.w.type) {
@@ -497,10 +473,8 @@ __global__ void __launch_bounds__(kMkThreads, 1) decoder_mk_kernel(MkParams P) {
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
         }
-        if (threadIdx.x == 0) MK_PROBE(5);
         cp_async_wait_all();  // the next descriptor has landed
         mk_sync();  // all outputs of this CTA for product s are written; the act arrays may be reused
-        if (threadIdx.x == 0) MK_PROBE(4);
         if (give_up) break;
     }
     // ---- end of the launch: once every CTA is here (all have read the epoch), CTA 0 advances it ----

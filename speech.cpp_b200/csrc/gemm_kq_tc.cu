@@ -363,8 +363,16 @@ __global__ void __launch_bounds__(kQThreads, KqLayout<KIND>::kCtasPerSm)
                     if (lane == 0) mbar_arrive(&acc_empty[buf]);
                     continue;
                 }
+                // nothing of the super-block's first stage is read here, but the warp still waits for the stage to
+                // land before handing it back: a parity wait tells only one phase from the next, so an arrival
+                // ahead of the landing could complete a phase that a slower warp is still reading
+                if (!mbar_wait_sleep(&full[s], (sg / S) & 1)) {
+                    if (lane == 0) atomicOr(p.err, kErrTimeout);
+                    give_up = 1;
+                    break;
+                }
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[s]);  // nothing of the super-block's first stage is read here
+                if (lane == 0) mbar_arrive(&empty[s]);
             }
             if (give_up) break;
             if (live <= 0) continue;

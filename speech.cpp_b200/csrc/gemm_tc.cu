@@ -58,14 +58,6 @@ struct TcParams {
     unsigned * tickets;  // one per tile, zero between launches
 };
 
-// Phase timestamps for latency studies, compiled in only with -DB200_TC_PROBE: tc_probe[cta][block][4].
-#ifdef B200_TC_PROBE
-__device__ long long * tc_probe_buf;
-#define TC_PROBE(blk, slot) \
-    do { if (tc_probe_buf && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) tc_probe_buf[(blk) * 4 + (slot)] = clock64(); } while (0)
-#else
-#define TC_PROBE(blk, slot) do { } while (0)
-#endif
 
 template <int NT>
 __global__ void __launch_bounds__(kTcThreads, 2)
@@ -154,7 +146,6 @@ __global__ void __launch_bounds__(kTcThreads, 2)
                         break;
                     }
                     tc_fence_after();
-                    TC_PROBE(b, 0);
                     mma_i8(tmem + buf * NT, smem_desc_sw128(base + (j / 4) * kTcM * 128, j % 4),
                            smem_desc_sw128(base + L::kA + (j / 4) * NT * 128, j % 4), idesc);
                     mma_commit(&acc_full[buf]);
@@ -186,7 +177,6 @@ __global__ void __launch_bounds__(kTcThreads, 2)
                     give_up = 1;
                     break;
                 }
-                if (warp == 2 && lane == 0) TC_PROBE(b, 1);
                 tc_fence_after();
                 int v[kCols];
                 tmem_ld32(tmem + ((uint32_t) (32 * q) << 16) + buf * NT + kCols * h, v);
@@ -194,7 +184,6 @@ __global__ void __launch_bounds__(kTcThreads, 2)
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&acc_empty[buf]);
-                if (warp == 2 && lane == 0) TC_PROBE(b, 2);
                 // acc += float(sum) * (d_x * d_w), two tokens per packed f32x2 op. The int32 block sums
                 // (|sum| <= 32 * 127 * 128 < 2^22) convert exactly: 0x4B400000 + sum is the float 12582912 + sum.
                 const float dwr = __half2float(dw[row * kTcKB + j]);
@@ -212,7 +201,6 @@ __global__ void __launch_bounds__(kTcThreads, 2)
                     acc[2 * t4] = __ffma2_rn(f01, s01, acc[2 * t4]);
                     acc[2 * t4 + 1] = __ffma2_rn(f23, s23, acc[2 * t4 + 1]);
                 }
-                if (warp == 2 && lane == 0) TC_PROBE(b, 3);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
@@ -390,11 +378,5 @@ cudaError_t launch_gemm_tc(const WeightView & w, int64_t row0, int64_t N, const 
     return launch_nt<64>(w, row0, N, q, dxT, gemm_tc_dx_ld(M), M, y, ldy, err, ws, ws_bytes, tickets, num_sms, st);
 }
 
-#ifdef B200_TC_PROBE
-extern "C" __attribute__((visibility("default"))) void b200_tc_probe_set(void * p) {
-    long long * v = (long long *) p;
-    cudaMemcpyToSymbol(tc_probe_buf, &v, sizeof v);
-}
-#endif
 
 }  // namespace b200

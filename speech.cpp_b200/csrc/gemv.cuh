@@ -98,7 +98,7 @@ __device__ __forceinline__ float pro_value(const GemvParams & p, const float * x
     if (!xc) return 0.0f;
     switch (p.pro) {
     case PRO_RMSNORM: return __fmul_rn(__fmul_rn(xc[k], rms[c]), p.norm_w[k]);
-    case PRO_SWIGLU: return __fmul_rn(silu(xc[k]), xc[p.pro_k + k]);
+    case PRO_SWIGLU: return __fmul_rn(silu_exact(xc[k]), xc[p.pro_k + k]);
     case PRO_GQA: {
         const int64_t span = p.pro_k * p.pro_rep;
         return xc[(k / span) * p.pro_k + k % p.pro_k];
@@ -122,7 +122,7 @@ __device__ __forceinline__ void sync_threads(int nthr) {
 
 __device__ __forceinline__ void stage_one(const GemvParams & p, const Act & a, int kind, const float * xc, float * xs, float * ws,
                                           int nthr) {
-    __shared__ float part[32];
+    __shared__ double part[32];
     __shared__ float rms;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = nthr >> 5;
     const int K = (int) a.K;
@@ -143,22 +143,23 @@ __device__ __forceinline__ void stage_one(const GemvParams & p, const Act & a, i
     if (p.pro == PRO_RMSNORM) copy(ws, p.norm_w, K);
     sync_threads(nthr);
     if (p.pro == PRO_RMSNORM) {
-        float sq = 0.0f;
-        for (int k = tid; k < K; k += nthr) sq = fmaf(xs[k], xs[k], sq);
-        sq = warp_sum(sq);
+        // squares summed in double (exact products; the order changes nothing that survives the rounding to float32)
+        double sq = 0.0;
+        for (int k = tid; k < K; k += nthr) sq = fma((double) xs[k], (double) xs[k], sq);
+        sq = warp_sum_d(sq);
         if (lane == 0) part[warp] = sq;
         sync_threads(nthr);
         if (warp == 0) {
-            float t = lane < nwarps ? part[lane] : 0.0f;
-            t = warp_sum(t);
-            if (lane == 0) rms = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(t, (float) K), p.eps)));
+            double t = lane < nwarps ? part[lane] : 0.0;
+            t = warp_sum_d(t);
+            if (lane == 0) rms = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__double2float_rn(t / (double) K), p.eps)));
         }
         sync_threads(nthr);
     }
     auto value = [&](int k) -> float {
         switch (p.pro) {
         case PRO_RMSNORM: return __fmul_rn(__fmul_rn(xs[k], rms), ws[k]);
-        case PRO_SWIGLU: return __fmul_rn(silu(xs[k]), xs[K + k]);
+        case PRO_SWIGLU: return __fmul_rn(silu_exact(xs[k]), xs[K + k]);
         case PRO_GQA: return xs[(k / (hd * rep)) * hd + k % hd];
         default: return xs[k];
         }
@@ -222,21 +223,21 @@ __device__ void stage_activations(const GemvParams & p, const Act & a, int kind,
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = nthr >> 5;
     const int64_t K = a.K;
     if (p.pro == PRO_RMSNORM) {
-        __shared__ float part[NC][32];
+        __shared__ double part[NC][32];
         for (int c = 0; c < NC; c++) {
             const float * xc = xcol[c];
-            float s = 0.0f;
+            double s = 0.0;
             if (xc)
-                for (int64_t k = threadIdx.x; k < K; k += nthr) s = fmaf(xc[k], xc[k], s);
-            s = warp_sum(s);
+                for (int64_t k = threadIdx.x; k < K; k += nthr) s = fma((double) xc[k], (double) xc[k], s);
+            s = warp_sum_d(s);
             if (lane == 0) part[c][warp] = s;
         }
         sync_threads(nthr);
         if (warp == 0) {
             for (int c = 0; c < NC; c++) {
-                float s = lane < nwarps ? part[c][lane] : 0.0f;
-                s = warp_sum(s);
-                if (lane == 0) rms[c] = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(s, (float) K), p.eps)));
+                double s = lane < nwarps ? part[c][lane] : 0.0;
+                s = warp_sum_d(s);
+                if (lane == 0) rms[c] = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__double2float_rn(s / (double) K), p.eps)));
             }
         }
         sync_threads(nthr);
@@ -358,7 +359,7 @@ struct TQ8_0 {
         return r;
     }
     template <int NC>
-    __device__ static void dot(const Unit & U, int64_t u, bool valid, const Act & a, float * acc, int32_t * sums) {
+    __device__ static void dot(const Unit & U, int64_t u, bool valid, const Act & a, double * acc, int32_t * sums) {
         if (!valid) return;
         const float dw = __half2float(__ushort_as_half(U.d));
         const int ui = (int) u, K = (int) a.K;
@@ -375,7 +376,7 @@ struct TQ8_0 {
             s = __dp4a(U.q1.y, x1.y, s);
             s = __dp4a(U.q1.z, x1.z, s);
             s = __dp4a(U.q1.w, x1.w, s);
-            acc[c] += (float) s * __fmul_rn(dw, a.d[c * (K / 32) + ui]);
+            acc[c] = acc_term(acc[c], __fmul_rn(dw, a.d[c * (K / 32) + ui]), s);
             if (c == 0 && sums) sums[ui] = s;
         }
     }
@@ -444,7 +445,7 @@ struct TQ4_K {
         }
     }
     template <int NC>
-    __device__ static void dot(const Unit & U, int64_t u, bool valid, const Act & a, float * acc, int32_t * sums) {
+    __device__ static void dot(const Unit & U, int64_t u, bool valid, const Act & a, double * acc, int32_t * sums) {
         const int ui = (int) u, K = (int) a.K;
         const int sb = ui >> 2, g = ui & 3, s0 = 2 * g, s1 = 2 * g + 1;
         int sc0 = 0, m0 = 0, sc1 = 0, m1 = 0;
@@ -491,8 +492,8 @@ struct TQ4_K {
             if (valid && (!sums || g == 0)) {
                 // each lane's exact partial sums, scaled in float (the super-block's scale is common to its lanes)
                 const float dx = a.d[c * (K / 256) + sb];
-                acc[c] += __fmul_rn(dx, dw) * (float) si;
-                acc[c] -= __fmul_rn(dx, dmw) * (float) sm;
+                acc[c] = acc_term(acc[c], __fmul_rn(dx, dw), si);
+                acc[c] = acc_term(acc[c], -__fmul_rn(dx, dmw), sm);
             }
         }
     }
@@ -541,7 +542,7 @@ struct TQ6_K {
         return r;
     }
     template <int NC>
-    __device__ static void dot(const Unit & U, int64_t u, bool valid, const Act & a, float * acc, int32_t * sums) {
+    __device__ static void dot(const Unit & U, int64_t u, bool valid, const Act & a, double * acc, int32_t * sums) {
         const int * A = reinterpret_cast<const int *>(&U.a);
         const int * B = reinterpret_cast<const int *>(&U.b);
         const int * H = reinterpret_cast<const int *>(&U.h);
@@ -578,7 +579,7 @@ struct TQ6_K {
             }
             if (valid && (!sums || j == 0)) {
                 const float dx = a.d[(int64_t) c * (a.K / 256) + sb];
-                acc[c] += __fmul_rn(dw, dx) * (float) si;
+                acc[c] = acc_term(acc[c], __fmul_rn(dw, dx), si);
             }
         }
     }
@@ -603,20 +604,20 @@ struct TBF16 {
         return r;
     }
     template <int NC>
-    __device__ static void dot(const Unit & U, int64_t u, bool valid, const Act & a, float * acc, int32_t *) {
+    __device__ static void dot(const Unit & U, int64_t u, bool valid, const Act & a, double * acc, int32_t *) {
         if (!valid) return;
         const __nv_bfloat162 * wv = reinterpret_cast<const __nv_bfloat162 *>(&U.q);
 #pragma unroll
         for (int c = 0; c < NC; c++) {
             const int4 xr = *reinterpret_cast<const int4 *>(a.b + (int64_t) c * a.K + u * 8);
             const __nv_bfloat162 * xv = reinterpret_cast<const __nv_bfloat162 *>(&xr);
-            float s = acc[c];
+            double s = acc[c];
 #pragma unroll
             for (int i = 0; i < 4; i++) {
                 const float2 wf = __bfloat1622float2(wv[i]);
                 const float2 xf = __bfloat1622float2(xv[i]);
-                s = fmaf(wf.x, xf.x, s);  // bf16 x bf16 is exact in f32: one rounding either way
-                s = fmaf(wf.y, xf.y, s);
+                s += (double) __fmul_rn(wf.x, xf.x);  // bf16 x bf16 is exact in f32
+                s += (double) __fmul_rn(wf.y, xf.y);
             }
             acc[c] = s;
         }
@@ -701,9 +702,9 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(GemvParams p) {
             stage_activations<NC>(p, a, kind, c0, nc, blockDim.x);
         }
 
-        float acc[NC];
+        double acc[NC];
 #pragma unroll
-        for (int c = 0; c < NC; c++) acc[c] = 0.0f;
+        for (int c = 0; c < NC; c++) acc[c] = 0.0;
         for (int64_t s = 0; s < my_steps; s++) {
             if (s + 1 < my_steps) load_step(s + 1, nxt);
             const int64_t r = gwarp + (s / steps_per_row) * warps_total;
@@ -717,14 +718,14 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(GemvParams p) {
             if (s % steps_per_row == steps_per_row - 1) {
 #pragma unroll
                 for (int c = 0; c < NC; c++) {
-                    const float v = warp_sum(acc[c]);
+                    const float v = __double2float_rn(warp_sum_d(acc[c]));
                     if (lane == 0 && c < nc && !p.sums) {
                         const int64_t col = p.col_dst ? (int64_t) p.col_dst[c0 + c] : c0 + c;
                         float out = v;
                         if (p.res) out = __fadd_rn(p.res[col * p.ldres + r], v);
                         p.y[col * p.ldy + r] = out;
                     }
-                    acc[c] = 0.0f;
+                    acc[c] = 0.0;
                 }
             }
 #pragma unroll

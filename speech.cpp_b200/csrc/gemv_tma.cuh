@@ -39,17 +39,6 @@ __host__ __device__ inline size_t tma_smem_bytes(int wtype, int64_t K, int rows_
     return ring + ((act_smem_bytes(wtype, K, NC) + 15) & ~(size_t) 15) + 16 * (size_t) stages + 16;
 }
 
-// Two warp sums at once (their shuffles interleave, halving the reduction's latency per row).
-__device__ __forceinline__ void warp_sum2(float & a, float & b) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float ta = __shfl_xor_sync(0xffffffffu, a, o);
-        const float tb = __shfl_xor_sync(0xffffffffu, b, o);
-        a += ta;
-        b += tb;
-    }
-}
-
 // Single-column products of `rows` landed rows (field pointers f, row j at local index j). A warp works on 32 / LPR
 // rows at once, LPR lanes per row, each lane taking every LPR-th unit of its row (independent units: their loads and
 // dp4a chains overlap), then an LPR-lane reduction. LPR = 8 for rows of up to 64 units, else 32. store(j, value).
@@ -63,7 +52,7 @@ __device__ __forceinline__ void smem_rows_lpr(const uint8_t * const * f, int64_t
     for (int j0 = warp * kRowsPerPass; j0 < rows; j0 += nwarps * kRowsPerPass) {
         const int j = j0 + sub;
         const bool row_ok = j < rows;
-        float acc[1] = {0.0f};
+        double acc[1] = {0.0};
         constexpr int kU = T::kSmemUnroll;
         for (int u0 = 0; u0 < upr; u0 += LPR * kU) {
             typename T::Unit U[kU];
@@ -79,10 +68,10 @@ __device__ __forceinline__ void smem_rows_lpr(const uint8_t * const * f, int64_t
                 T::template dot<1>(U[t], u, row_ok && u < upr, a, acc, nullptr);
             }
         }
-        float v = acc[0];
+        double v = acc[0];
 #pragma unroll
         for (int o = LPR / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        if (row_ok && li == 0) store(j, v);
+        if (row_ok && li == 0) store(j, __double2float_rn(v));
     }
 }
 
@@ -124,7 +113,7 @@ __device__ __forceinline__ void smem_rows_q4k(const uint8_t * const * f, int64_t
     const unsigned lenlo = swap ? 4u : 6u, himask = swap ? 0x30u : 0u;
     for (int j0 = warp * 2; j0 < rows; j0 += nwarps * 2) {
         const int j = j0 + sub;
-        float acc = 0.0f;
+        double acc = 0.0;
         if (j < rows) {
             const uint8_t * qr = f[0] + (size_t) j * (size_t) (K / 2) + 32 * g;
             const int4 * mr = reinterpret_cast<const int4 *>(f[1]) + (size_t) j * nsb;
@@ -170,13 +159,13 @@ __device__ __forceinline__ void smem_rows_q4k(const uint8_t * const * f, int64_t
                 const int sm = mn0 * ((int) (int16_t) (p0 & 0xFFFF) + (p0 >> 16)) + mn1 * ((int) (int16_t) (p1 & 0xFFFF) + (p1 >> 16));
                 const float dw = __half2float(__ushort_as_half((unsigned short) ((unsigned) m.x & 0xFFFFu)));
                 const float dmw = __half2float(__ushort_as_half((unsigned short) ((unsigned) m.x >> 16)));
-                acc += __fmul_rn(dx, dw) * (float) si;
-                acc -= __fmul_rn(dx, dmw) * (float) sm;
+                acc = acc_term(acc, __fmul_rn(dx, dw), si);
+                acc = acc_term(acc, -__fmul_rn(dx, dmw), sm);
             }
         }
 #pragma unroll
         for (int o = 8; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-        if (j < rows && li == 0) store(j, acc);
+        if (j < rows && li == 0) store(j, __double2float_rn(acc));
     }
 }
 
@@ -200,7 +189,7 @@ __device__ __forceinline__ void smem_rows_q6k(const uint8_t * const * f, int64_t
     const int offP = 64 * hh + 16 * lb + (sbpar ? 32 : 0), offQ = 64 * hh + 16 * lb + (sbpar ? 0 : 32);
     for (int j0 = warp * kRowsPerPass; j0 < rows; j0 += nwarps * kRowsPerPass) {
         const int j = j0 + sub;
-        float acc = 0.0f;
+        double acc = 0.0;
         if (j < rows) {
             const uint8_t * qlr = f[0] + (size_t) j * (size_t) (K / 2);
             const uint8_t * qhr = f[1] + (size_t) j * (size_t) (K / 4) + 32 * hh + 16 * lb;
@@ -229,12 +218,12 @@ __device__ __forceinline__ void smem_rows_q6k(const uint8_t * const * f, int64_t
                     si += (int) sc[2 * t] * s;
                 }
                 const float dw = __half2float(__ushort_as_half(dr[sb]));
-                acc += __fmul_rn(dw, a.d[sb]) * (float) si;
+                acc = acc_term(acc, __fmul_rn(dw, a.d[sb]), si);
             }
         }
 #pragma unroll
         for (int o = LPR / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-        if (j < rows && li == 0) store(j, acc);
+        if (j < rows && li == 0) store(j, __double2float_rn(acc));
     }
 }
 
@@ -288,6 +277,7 @@ __global__ void __launch_bounds__(32 * (CW + 1), CW == kTmaConsumerWarps ? 2 : 1
         // ---- producer ----
         if (lane == 0) {
             const uint8_t * fb[4] = {p.w.f0, p.w.f1, p.w.f2, p.w.f3};
+            int64_t issued = 0;  // chunks whose copies were issued
             for (int64_t c = 0; c < nchunks; c++) {
                 const int s = (int) (c % stages);
                 const int64_t it = c / stages;
@@ -295,6 +285,7 @@ __global__ void __launch_bounds__(32 * (CW + 1), CW == kTmaConsumerWarps ? 2 : 1
                     atomicOr(p.err, kDevErrTimeout);
                     break;
                 }
+                issued = c + 1;
                 const int64_t first = r_begin + c * rps;
                 const int64_t rows = nrows - c * rps < rps ? nrows - c * rps : rps;
                 mbar_arrive_expect_tx(&full[s], (uint32_t) (rows * row_bytes));
@@ -307,6 +298,11 @@ __global__ void __launch_bounds__(32 * (CW + 1), CW == kTmaConsumerWarps ? 2 : 1
                 if (c == 0) pdl_launch_dependents();
             }
             if (nchunks == 0) pdl_launch_dependents();
+            // the CTA must not exit while copies it issued still land in its shared memory: wait (bounded) for the
+            // last use of every slot. On the normal path they have landed already; after a consumer gave up they
+            // may not have, and the CTA then ends only once they did (or once this wait also gives up).
+            for (int64_t c = issued > stages ? issued - stages : 0; c < issued; c++)
+                if (!mbar_wait(&full[c % stages], (uint32_t) ((c / stages) & 1))) atomicOr(p.err, kDevErrTimeout);
         }
         return;
     }
@@ -377,9 +373,9 @@ __global__ void __launch_bounds__(32 * (CW + 1), CW == kTmaConsumerWarps ? 2 : 1
             for (int64_t j = member; j < rows; j += kGroup) {
                 const int64_t r = base + j;  // output row
                 int32_t * sums = p.sums ? p.sums + r * nsums : nullptr;
-                float acc[NC];
+                double acc[NC];
 #pragma unroll
-                for (int q = 0; q < NC; q++) acc[q] = 0.0f;
+                for (int q = 0; q < NC; q++) acc[q] = 0.0;
                 for (int64_t u0 = 0; u0 < upr; u0 += 32) {
                     const int64_t u = u0 + lane;
                     const bool valid = u < upr;
@@ -390,7 +386,7 @@ __global__ void __launch_bounds__(32 * (CW + 1), CW == kTmaConsumerWarps ? 2 : 1
                 }
 #pragma unroll
                 for (int q = 0; q < NC; q++) {
-                    const float v = warp_sum(acc[q]);
+                    const float v = __double2float_rn(warp_sum_d(acc[q]));
                     if (lane == 0 && q < nc && !p.sums) {
                         float out = v;
                         if (p.res) out = __fadd_rn(p.res[(int64_t) q * p.ldres + r], v);

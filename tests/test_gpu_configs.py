@@ -1,0 +1,227 @@
+"""Parity at the benchmarked shapes: every configuration bench.py times is also checked against the CPU oracle here,
+at its full size, through the C ABI.
+
+- Config 2: the 28-layer Qwen3-TTS 0.6B talker decode step (Q8_0, n_head 16, vocab 3072) on the persistent step
+  kernel, against oracle/stack.py (Qwen3Decoder::layers / outputs, src/common/qwen3-decoder.cpp:350-438); logits
+  cosine >= 0.9999, and the (sub-)block int32 sums of one product bit for bit.
+- Config 3, decode: the 28-layer Qwen3-ASR 1.7B-shaped step (Q4_K / Q6_K, vocab 151936, Q6_K head), same bars.
+- Config 3, prefill: one layer's four products at M = 1500 rows on the K-quant tensor-core path, plus the head on
+  the last row; |err| <= 1e-4 * sum |w x| per element on a sample of rows that includes the first and last row of
+  every 64-row token tile (rows are independent, so a sample checks the kernel's tiling fully).
+- Config 4: one layer of the Qwen3-TTS 1.7B-shaped talker at M = 64 (Q8_0, tensor cores), every element.
+- Config 5: one full MoE layer (128 experts, 2048 <-> 768, 256 tokens, top-8), through b200_mul_mat_id (per-element
+  bound) and b200_moe_ffn (TextModel::experts, src/families/drama3/text-model.cpp:198-221; cosine per token).
+
+Weights are N(0, 0.02) drawn on the GPU by torch (fast at these sizes), copied to the host and quantized by the
+oracle, so both sides read the same GGUF bytes.
+"""
+
+import numpy as np
+import pytest
+
+from conftest import load_package
+
+pytestmark = pytest.mark.gpu
+
+Q8_0, Q4_K, Q6_K, Q8_K = 8, 12, 14, 15
+VEC = {Q8_0: Q8_0, Q4_K: Q8_K, Q6_K: Q8_K}
+TOL = 1e-4
+
+
+@pytest.fixture(scope="module")
+def b200():
+    import torch
+
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    return load_package()
+
+
+@pytest.fixture(scope="module")
+def ctx(b200):
+    c = b200.Context(0)
+    yield c
+    c.close()
+
+
+def device_normal(seed):
+    """N(0, 1) float32 arrays of any shape, drawn on the GPU from a seeded generator."""
+    import torch
+
+    g = torch.Generator(device="cuda").manual_seed(seed)
+
+    def draw(shape):
+        return torch.randn(shape, generator=g, device="cuda", dtype=torch.float32).cpu().numpy()
+
+    return draw
+
+
+def cuda(a):
+    import torch
+
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def cosine(a, b):
+    a, b = a.astype(np.float64), b.astype(np.float64)
+    return float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b)))
+
+
+def bound(oracle, qtype, wb, K, x):
+    wd = oracle.dequantize(qtype, wb, K).astype(np.float64)
+    vt = VEC[qtype]
+    xd = oracle.dequantize(vt, oracle.quantize(vt, x), K).astype(np.float64)
+    return TOL * (np.abs(xd) @ np.abs(wd).T) + 1e-30
+
+
+def load_decoder(b200, ctx, c, model):
+    d = b200.Decoder(ctx, **c)
+    names = ["attn_q", "attn_k", "attn_v", "attn_o", "ffn_gate", "ffn_up", "ffn_down"]
+    for l, L in enumerate(model["layers"]):
+        for i, n in enumerate(names):
+            d.set_tensor(l, i, L[n])
+        d.set_tensor(l, b200.DEC_ATTN_NORM, L["attn_norm"])
+        d.set_tensor(l, b200.DEC_FFN_NORM, L["ffn_norm"])
+    d.set_tensor(0, b200.DEC_OUTPUT, model["output"])
+    d.set_tensor(0, b200.DEC_OUTPUT_NORM, model["output_norm"])
+    return d
+
+
+@pytest.mark.parametrize("name", ["tts06", "asr17"])
+def test_full_decode_step(b200, ctx, oracle, name):
+    """The benchmarked 28-layer step (config 2: tts06; config 3 decode: asr17) on the kernel bench.py times."""
+    from oracle import stack
+
+    c = stack.CONFIGS[name]
+    model = stack.random_model(c, seed=31, normal=device_normal(31))
+    x = np.random.default_rng(32).normal(0, 1, size=c["hidden"]).astype(np.float32)
+    want = stack.step(c, model, x)
+    d = load_decoder(b200, ctx, c, model)
+    got = d.step(cuda(x)).cpu().numpy()
+    ctx.synchronize()
+    assert d.launches == 1  # the persistent step kernel: the configuration bench.py times
+    assert got.shape == (c["n_vocab"],)
+    cos = cosine(got, want)
+    assert cos >= 0.9999, f"{name}: cosine {cos:.7f}"
+    assert np.array_equal(d.step_host(x), got)  # the host entry point runs the same step
+    d.close()
+
+    # integer partials of one product of each weight type of the config, bit for bit: layer 0's q product on its
+    # RMSNorm-ed input, and the head on a random row
+    h = stack.rms_norm(x, model["layers"][0]["attn_norm"], 1e-6)[None]
+    cases = [(stack.tensor_shapes(c)["attn_q"], model["layers"][0]["attn_q"], h),
+             (stack.tensor_shapes(c)["ffn_down"], model["layers"][0]["ffn_down"],
+              np.random.default_rng(33).normal(0, 1, size=(1, c["ffn"])).astype(np.float32))]
+    for (t, k, n), wb, xin in cases:
+        w = ctx.weight(t, k, n, data=wb)
+        sums = ctx.block_sums(w, cuda(xin)).cpu().numpy()
+        xq = oracle.quantize(VEC[t], xin)[0]
+        rows = np.unique(np.r_[0, n - 1, np.random.default_rng(34).integers(0, n, 64)])
+        want_s = np.stack([oracle.block_sums(t, wb[r], xq, k) for r in rows])
+        assert np.array_equal(sums[rows], want_s)
+        ctx.free_weight(w)
+
+
+def _check_rows(oracle, qtype, wb, K, N, x, got, rows):
+    want = oracle.mul_mat(qtype, wb, K, N, x[rows])
+    err = np.abs(got[rows].astype(np.float64) - want)
+    b = bound(oracle, qtype, wb, K, x[rows])
+    assert np.all(err <= b), f"type {qtype} K {K} N {N}: max err/bound {np.max(err / b):.3g}"
+
+
+def test_config3_prefill_layer_m1500(b200, ctx, oracle):
+    """One layer of config 3's prefill: q|k|v 2048->4096, o 2048->2048, gate|up 2048->12288 (Q4_K), down 6144->2048
+    (Q6_K), M = 1500 rows, on the K-quant tensor-core path; then the 2048->151936 Q6_K head on the last row."""
+    draw = device_normal(41)
+    M = 1500
+    rng = np.random.default_rng(42)
+    rows = np.unique(np.r_[np.arange(0, M, 64), np.arange(63, M, 64), M - 1, rng.integers(0, M, 8)])
+    for qtype, K, N in [(Q4_K, 2048, 4096), (Q4_K, 2048, 2048), (Q4_K, 2048, 12288), (Q6_K, 6144, 2048)]:
+        wb = oracle.quantize(qtype, (np.float32(0.02) * draw((N, K))).astype(np.float32))
+        x = rng.normal(0, 1, size=(M, K)).astype(np.float32)
+        w = ctx.weight(qtype, K, N, data=wb)
+        got = ctx.mul_mat(w, cuda(x)).cpu().numpy()
+        ctx.synchronize()
+        _check_rows(oracle, qtype, wb, K, N, x, got, rows)
+        ctx.free_weight(w)
+    K, N = 2048, 151936
+    wb = oracle.quantize(Q6_K, (np.float32(0.02) * draw((N, K))).astype(np.float32))
+    x = rng.normal(0, 1, size=(1, K)).astype(np.float32)
+    w = ctx.weight(Q6_K, K, N, data=wb)
+    got = ctx.mul_mat(w, cuda(x)).cpu().numpy()
+    ctx.synchronize()
+    _check_rows(oracle, Q6_K, wb, K, N, x, got, np.array([0]))
+    ctx.free_weight(w)
+
+
+def test_config4_layer_m64(b200, ctx, oracle):
+    """One layer of config 4: q|k|v 2048->4096, o 2048->2048, gate|up 2048->12288, down 6144->2048, Q8_0, M = 64
+    streams (int8 tensor cores), every element."""
+    draw = device_normal(51)
+    rng = np.random.default_rng(52)
+    M = 64
+    for K, N in [(2048, 4096), (2048, 2048), (2048, 12288), (6144, 2048)]:
+        wb = oracle.quantize(Q8_0, (np.float32(0.02) * draw((N, K))).astype(np.float32))
+        x = rng.normal(0, 1, size=(M, K)).astype(np.float32)
+        w = ctx.weight(Q8_0, K, N, data=wb)
+        got = ctx.mul_mat(w, cuda(x)).cpu().numpy()
+        ctx.synchronize()
+        _check_rows(oracle, Q8_0, wb, K, N, x, got, np.arange(M))
+        ctx.free_weight(w)
+
+
+def moe_routes(T, E, k, seed):
+    """Router logits N(0, 1) -> softmax -> top-k (ties broken by a seeded permutation) -> weights renormalised over
+    the chosen k, as config 5 draws them."""
+    rng = np.random.default_rng(seed)
+    logits = rng.normal(0, 1, size=(T, E)).astype(np.float32)
+    p = np.exp(logits - logits.max(1, keepdims=True))
+    p /= p.sum(1, keepdims=True)
+    rank = rng.permutation(E)
+    order = np.lexsort((np.broadcast_to(rank, (T, E)), -p), axis=1)[:, :k]
+    sel = np.take_along_axis(p, order, 1)
+    return order.astype(np.int32), (sel / sel.sum(1, keepdims=True)).astype(np.float32)
+
+
+def moe_reference(oracle, gu_b, dn_b, H, F, E, x, ids, w):
+    gu = oracle.mul_mat_id(Q8_0, gu_b, H, 2 * F, E, x[:, None, :], ids)
+    g, u = gu[..., :F], gu[..., F:]
+    a = (g / (np.float32(1.0) + np.exp(-g)) * u).astype(np.float32)
+    dn = oracle.mul_mat_id(Q8_0, dn_b, F, H, E, a, ids)
+    out = np.zeros((x.shape[0], H), dtype=np.float32)
+    for s in range(ids.shape[1]):
+        out = (out + dn[:, s] * w[:, s:s + 1]).astype(np.float32)
+    return gu, out
+
+
+def test_config5_moe_layer_full(b200, ctx, oracle):
+    """One full config-5 layer: 128 Q8_0 experts, gate|up 2048->1536, down 768->2048, 256 tokens, top-8."""
+    E, H, F, T, k = 128, 2048, 768, 256, 8
+    draw = device_normal(61)
+    gu_b = np.concatenate([oracle.quantize(Q8_0, (np.float32(0.02) * draw((16 * 2 * F, H))).astype(np.float32))
+                           for _ in range(E // 16)])
+    dn_b = np.concatenate([oracle.quantize(Q8_0, (np.float32(0.02) * draw((16 * H, F))).astype(np.float32))
+                           for _ in range(E // 16)])
+    x = np.random.default_rng(62).normal(0, 1, size=(T, H)).astype(np.float32)
+    ids, w = moe_routes(T, E, k, 63)
+    gu_want, want = moe_reference(oracle, gu_b, dn_b, H, F, E, x, ids, w)
+
+    gu = ctx.weight(Q8_0, H, 2 * F, E, data=gu_b)
+    dn = ctx.weight(Q8_0, F, H, E, data=dn_b)
+    # the gate|up MUL_MAT_ID alone (2048 pairs: the tensor-core grouped path), per element against the oracle
+    got_gu = ctx.mul_mat_id(gu, cuda(x[:, None, :]), cuda(ids)).cpu().numpy()
+    ctx.synchronize()
+    wd = oracle.dequantize(Q8_0, gu_b, H).astype(np.float64).reshape(E, 2 * F, H)
+    xd = oracle.dequantize(Q8_0, oracle.quantize(Q8_0, x), H).astype(np.float64)
+    for t in range(0, T, 5):
+        for s in range(k):
+            b = TOL * (np.abs(wd[ids[t, s]]) @ np.abs(xd[t])) + 1e-30
+            assert np.all(np.abs(got_gu[t, s].astype(np.float64) - gu_want[t, s]) <= b)
+    # the whole routed-expert block
+    got = ctx.moe_ffn(gu, dn, cuda(x), cuda(ids), cuda(w)).cpu().numpy()
+    ctx.synchronize()
+    cos = (got * want).sum(1) / (np.linalg.norm(got, axis=1) * np.linalg.norm(want, axis=1))
+    assert cos.min() >= 0.9999, f"min per-token cosine {cos.min():.7f}"
+    assert np.abs(got - want).max() <= 2e-3 * np.abs(want).max()
+    ctx.free_weight(gu)
+    ctx.free_weight(dn)
