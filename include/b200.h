@@ -155,7 +155,7 @@ b200_status b200_moe_ffn(b200_context * ctx, const b200_weight * gate_up, const 
  * the group with all mailbox pointers (its own at index rank). b200_moe_ffn_ep then runs the rank's experts like
  * b200_moe_ffn and leaves in `out` the FULL weighted sum over all ranks' experts (every rank gets the same out). All
  * ranks must call it in the same order with the same T (<= max_tokens) and H. A rank that never arrives makes the
- * others give up after a bounded wait (B200_ERR_TIMEOUT from b200_synchronize). */
+ * others give up after a bounded wait (B200_ERR_TIMEOUT from b200_synchronize; see b200_ep_set_timeout). */
 typedef struct b200_ep_group b200_ep_group;
 b200_status b200_ep_mailbox_alloc(b200_context * ctx, int world, int64_t max_tokens, int64_t hidden, void ** mailbox, void * ipc_handle);
 b200_status b200_ep_mailbox_open(b200_context * ctx, const void * ipc_handle, void ** peer_mailbox);
@@ -164,6 +164,10 @@ b200_status b200_ep_mailbox_free(b200_context * ctx, void * mailbox);
 b200_status b200_ep_create(b200_context * ctx, int rank, int world, int64_t max_tokens, int64_t hidden, void * const * mailboxes,
                            b200_ep_group ** out);
 void b200_ep_destroy(b200_ep_group * group);
+/* How long one wait of the combine may take before it gives up (default 2 s). After a wait gave up the group is broken
+ * (the ranks' arrival counters are out of step): every later b200_moe_ffn_ep on it reports B200_ERR_TIMEOUT without
+ * running; destroy it and create a new group on every rank. */
+b200_status b200_ep_set_timeout(b200_ep_group * group, uint64_t microseconds);
 b200_status b200_moe_ffn_ep(b200_context * ctx, const b200_weight * gate_up, const b200_weight * down, int64_t expert0,
                             int64_t n_expert_total, const float * x, const int32_t * ids, const float * w, int64_t top_k, int64_t T,
                             float * out, b200_ep_group * group);
@@ -244,6 +248,64 @@ size_t b200_decoder_weight_bytes(const b200_decoder * d);
  * else chain. */
 enum { B200_DEC_MODE_CHAIN = 0, B200_DEC_MODE_PERSISTENT = 1 };
 b200_status b200_decoder_set_launch(b200_decoder * d, int mode, int pdl, int ctas_per_sm);
+
+/* ------------------------------------------------------------------------------------------------------------
+ * Graph execution: the backend's graph_compute over ggml-shaped tensor records, so a whole decoder graph
+ * (Qwen3Decoder::layers / outputs, src/common/qwen3-decoder.cpp:350-438) runs on this backend with no other backend
+ * beside it (speech.cpp computes each graph on one backend, src/common/graph.cpp:145-147). A ggml adapter fills one
+ * b200_tensor per ggml_tensor of the graph (its op, type, ne, nb and data; sources by index) and calls
+ * b200_graph_compute once; b200_graph_supports answers ggml_backend_supports_op. Leaves (inputs, weights, the KV
+ * cache, views, reshapes, permutes and transposes: op B200_OP_NONE) carry only their data pointer and strides.
+ *
+ * Arithmetic (the CPU oracle defines the same): products of quantized weights as b200_mul_mat; products of F16 / F32
+ * matrices with the activations rounded to the matrix's type as ggml's CPU vec_dot does (F16 for an F16 matrix), the
+ * element products summed exactly and rounded once to float32; RMS_NORM, SOFT_MAX and SiLU sums and exponentials in
+ * double, rounded once; ROPE angles p * base^(-2i/n_dims) in double, their cosine and sine rounded once to float32.
+ * ------------------------------------------------------------------------------------------------------------ */
+enum {
+    B200_TYPE_I32 = 26  /* row ids and positions (ggml's GGML_TYPE_I32) */
+};
+
+typedef enum b200_op {
+    B200_OP_NONE = 0,        /* a leaf or a view: nothing to compute */
+    B200_OP_GET_ROWS = 1,    /* dst[:, i, j, k] = dequantize(src0[:, src1[i, j, k], j, k]); src0 a weight or F32 / F16 */
+    B200_OP_MUL_MAT = 2,     /* dst[n, m, i2, i3] = sum_k src0[k, n, i2 / r2, i3 / r3] * src1[k, m, i2, i3] */
+    B200_OP_RMS_NORM = 3,    /* per row: x / sqrt(mean(x^2) + eps); params[0] = eps (float bits) */
+    B200_OP_MUL = 4,         /* src0 * src1, src1 repeated to src0's shape */
+    B200_OP_ADD = 5,         /* src0 + src1, src1 repeated to src0's shape */
+    B200_OP_ROPE = 6,        /* NEOX rotation of src0 [head_dim, heads, tokens] at positions src1 (I32 [tokens]);
+                                params: [0] n_dims, [1] mode (2 = NEOX, the only one), [2] freq_base (float bits),
+                                [3] freq_scale (float bits, must be 1), [4] ext_factor (float bits, must be 0),
+                                [5] attn_factor (float bits, must be 1) */
+    B200_OP_SET_ROWS = 7,    /* dst (a view of the cache, F16 or F32) rows src1[i] = src0 row i (converted); dst is also
+                                src[2] of the record (the tensor written in place) */
+    B200_OP_CPY = 8,         /* dst = src0 element by element in row-major order (same shape), converted to dst's type;
+                                dst written in place through src[1] */
+    B200_OP_CONT = 9,        /* a contiguous copy of src0 (a permuted or transposed view) */
+    B200_OP_SOFT_MAX = 10,   /* rows of softmax(src0 * scale + src1 (mask, F16 / F32, optional)); params[0] = scale */
+    B200_OP_FLASH_ATTN = 11, /* ggml_flash_attn_ext: q src0 [D, n_q, H], k src1 [D, n_kv, H_kv] F16, v src2 [D, n_kv,
+                                H_kv] F16, mask src3 [n_kv, >= n_q] F16 (optional); dst [D, H, n_q] F32; params[0] = scale */
+    B200_OP_SWIGLU = 12,     /* ggml_swiglu_split: silu(src0) * src1 */
+    B200_OP_ARGMAX = 13,     /* dst I32 [rows]: index of the first largest value of each row of src0 */
+    B200_OP_SCALE = 14       /* src0 * params[0] + params[1] (float bits) */
+} b200_op;
+
+typedef struct b200_tensor {
+    int32_t op;                 /* b200_op */
+    int32_t type;               /* B200_TYPE_F32, F16, I32, or the weight's type when `weight` is set */
+    int64_t ne[4];              /* elements per dimension, innermost first (ggml ne) */
+    int64_t nb[4];              /* byte strides (ggml nb) */
+    void * data;                /* device address of element [0, 0, 0, 0] */
+    const b200_weight * weight; /* a weight in this backend's layout (MUL_MAT src0, GET_ROWS table), else NULL */
+    int32_t src[4];             /* indices of the source records in the same array; -1: none */
+    int32_t params[8];          /* op parameters, as listed with each op */
+} b200_tensor;
+
+/* Runs the records with an op, in array order, on the context's stream (asynchronous). A record's sources must come
+ * before it. Returns B200_ERR_UNSUPPORTED for a record b200_graph_supports rejects (nothing after it is launched). */
+b200_status b200_graph_compute(b200_context * ctx, const b200_tensor * tensors, int64_t n);
+/* Whether record i (with its sources in the same array) can run here: ggml_backend_supports_op. */
+int b200_graph_supports(const b200_tensor * tensors, int64_t n, int64_t i);
 
 /* ------------------------------------------------------------------------------------------------------------
  * Host-buffer entry points (the end-to-end path a CPU caller takes: copies in, product, copy out, synchronous).

@@ -34,7 +34,7 @@ EXPORTS = [
     "b200_decoder_step", "b200_decoder_step_host", "b200_decoder_launches", "b200_decoder_weight_bytes",
     "b200_decoder_set_launch", "b200_mul_mat_id_noalloc", "b200_moe_ffn",
     "b200_ep_mailbox_alloc", "b200_ep_mailbox_open", "b200_ep_mailbox_close", "b200_ep_mailbox_free", "b200_ep_create",
-    "b200_ep_destroy", "b200_moe_ffn_ep",
+    "b200_ep_destroy", "b200_ep_set_timeout", "b200_moe_ffn_ep", "b200_graph_compute", "b200_graph_supports",
 ]
 
 DEC_ATTN_Q, DEC_ATTN_K, DEC_ATTN_V, DEC_ATTN_O, DEC_FFN_GATE, DEC_FFN_UP, DEC_FFN_DOWN = range(7)
@@ -62,6 +62,21 @@ class Weight(ctypes.Structure):
         ("dbytes", ctypes.c_size_t),
         ("field_off", ctypes.c_int64 * 4),
     ]
+
+
+class Tensor(ctypes.Structure):
+    """struct b200_tensor (include/b200.h): one ggml-shaped record of a graph for b200_graph_compute."""
+
+    _fields_ = [
+        ("op", ctypes.c_int32), ("type", ctypes.c_int32), ("ne", ctypes.c_int64 * 4), ("nb", ctypes.c_int64 * 4),
+        ("data", ctypes.c_void_p), ("weight", ctypes.POINTER(Weight)), ("src", ctypes.c_int32 * 4),
+        ("params", ctypes.c_int32 * 8),
+    ]
+
+
+I32 = 26
+(OP_NONE, OP_GET_ROWS, OP_MUL_MAT, OP_RMS_NORM, OP_MUL, OP_ADD, OP_ROPE, OP_SET_ROWS, OP_CPY, OP_CONT, OP_SOFT_MAX,
+ OP_FLASH_ATTN, OP_SWIGLU, OP_ARGMAX, OP_SCALE) = range(15)
 
 
 class DecoderShape(ctypes.Structure):
@@ -139,7 +154,10 @@ def lib():
         "b200_ep_mailbox_free": (i32, [vp, vp]),
         "b200_ep_create": (i32, [vp, ctypes.c_int, ctypes.c_int, i64, i64, ctypes.POINTER(vp), ctypes.POINTER(vp)]),
         "b200_ep_destroy": (None, [vp]),
+        "b200_ep_set_timeout": (i32, [vp, ctypes.c_uint64]),
         "b200_moe_ffn_ep": (i32, [vp, W, W, i64, i64, vp, vp, vp, i64, i64, vp, vp]),
+        "b200_graph_compute": (i32, [vp, ctypes.POINTER(Tensor), i64]),
+        "b200_graph_supports": (i32, [ctypes.POINTER(Tensor), i64, i64]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -360,6 +378,68 @@ class Context:
         self.check(self.L.b200_mul_mat_host(self.h, ctypes.byref(w), x.ctypes.data_as(ctypes.c_void_p), x.shape[0],
                                             out.ctypes.data_as(ctypes.c_void_p)))
         return out
+
+
+class Graph:
+    """A list of b200_tensor records over torch CUDA tensors (or weights), computed by b200_graph_compute: the ggml
+    adapter's graph_compute, driven from Python. add() appends a record and returns its index; views are leaves with
+    their own strides (a permuted torch view passes its strides through)."""
+
+    _TYPES = {"torch.float32": F32, "torch.float16": F16, "torch.int32": I32}
+
+    def __init__(self, ctx):
+        self.ctx = ctx
+        self.recs = []
+        self.keep = []
+
+    def add(self, op=OP_NONE, t=None, weight=None, src=(), params=(), out=None):
+        """t: the record's tensor (a torch CUDA tensor: its data, shape and strides become data / ne / nb, innermost
+        dimension last in torch and first in ggml); weight: a Weight for a weight leaf; src: record indices."""
+        r = Tensor()
+        r.op = op
+        if weight is not None:
+            r.type = weight.type
+            r.weight = ctypes.pointer(weight)
+            r.data = weight.data
+            r.ne[:] = [weight.ne0, weight.ne1, weight.ne2, 1]
+            self.keep.append(weight)
+        else:
+            dims = list(t.shape)[::-1] + [1] * (4 - t.dim())
+            strides = [st * t.element_size() for st in list(t.stride())[::-1]] + [0] * (4 - t.dim())
+            for i in range(t.dim(), 4):
+                strides[i] = (strides[i - 1] * dims[i - 1]) if i > 0 else t.element_size()
+            r.type = self._TYPES[str(t.dtype)]
+            r.ne[:] = dims[:4]
+            r.nb[:] = strides[:4]
+            r.data = t.data_ptr()
+            self.keep.append(t)
+        srcs = list(src) + [-1] * (4 - len(src))
+        r.src[:] = srcs[:4]
+        ps = list(params) + [0] * (8 - len(params))
+        r.params[:] = [int(v) for v in ps[:8]]
+        self.recs.append(r)
+        return len(self.recs) - 1
+
+    @staticmethod
+    def fbits(x):
+        """A float parameter's bits as the int32 params[] holds them."""
+        import struct
+
+        return struct.unpack("<i", struct.pack("<f", float(x)))[0]
+
+    def array(self):
+        return (Tensor * len(self.recs))(*self.recs)
+
+    def supports(self, i):
+        arr = self.array()
+        return bool(self.ctx.L.b200_graph_supports(arr, len(self.recs), i))
+
+    def compute(self):
+        """Runs every record with an op on the context's stream, ordered after torch's current stream."""
+        arr = self.array()
+        self.ctx._sync_in()
+        self.ctx.check(self.ctx.L.b200_graph_compute(self.ctx.h, arr, len(self.recs)))
+        self.ctx._sync_out()
 
 
 class Decoder:

@@ -508,15 +508,18 @@ struct MoeSlots {
     }
 };
 
-// The expert FFN on the tensor cores: route into padded slots, quantize x per slot, gate|up grouped GEMM, SwiGLU +
-// re-quantization per slot, down grouped GEMM, weighted combine. Both expert matrices Q8_0 with K % 256 == 0.
+// The expert FFN on the tensor cores: route into padded slots and quantize x per slot (one kernel), gate|up grouped
+// GEMM with SwiGLU and the q8_0 re-quantization in its epilogue, down grouped GEMM, weighted combine (over NVLink peer
+// memory when `ep` is given). Both expert matrices Q8_0 with K % 256 == 0. When the fused route kernel's shared memory
+// or the 64-feature tiles do not fit the shape, the same steps run as separate kernels.
 b200_status moe_ffn_tc(b200_context * ctx, const b200_weight * gate_up, const b200_weight * down, int64_t expert0, int64_t total,
                        const float * x, const int32_t * ids, const float * w, int64_t top_k, int64_t T, float * out,
                        const b200_ep_group * ep = nullptr) {
     const int64_t H = gate_up->ne0, F2 = gate_up->ne1, E = gate_up->ne2, F = F2 / 2, P = T * top_k;
     const int64_t S = moe_max_slots(P, E);
     auto up = [](size_t v) { return (v + 255) & ~(size_t) 255; };
-    const size_t need = MoeSlots::bytes(P, E) + up((size_t) S * H) + up((size_t) (H / 32) * S * 4) + up((size_t) S * F2 * 4) +
+    const bool fused = moe_route_quant_fits(P, E, ctx->num_sms) && F % 64 == 0;
+    const size_t need = MoeSlots::bytes(P, E) + up((size_t) S * H) + up((size_t) (H / 32) * S * 4) + (fused ? 0 : up((size_t) S * F2 * 4)) +
                         up((size_t) S * F) + up((size_t) (F / 32) * S * 4) + up((size_t) S * H * 4);
     b200_status s = ensure_scratch(ctx, need);
     if (s != B200_OK) return s;
@@ -525,19 +528,27 @@ b200_status moe_ffn_tc(b200_context * ctx, const b200_weight * gate_up, const b2
     m.carve(c, P, E);
     int8_t * q1 = c.take<int8_t>((size_t) S * H);
     float * d1 = c.take<float>((size_t) (H / 32) * S);
-    float * gu = c.take<float>((size_t) S * F2);
+    float * gu = fused ? nullptr : c.take<float>((size_t) S * F2);
     int8_t * q2 = c.take<int8_t>((size_t) S * F);
     float * d2 = c.take<float>((size_t) (F / 32) * S);
     float * dn = c.take<float>((size_t) S * H);
     cudaStream_t st = ctx->stream;
-    CK(ctx, launch_moe_route(ids, T, top_k, 1, E, expert0, total, m.grp_off, m.col_src, m.col_dst, m.inv, m.tiles, m.ntiles,
-                             ctx->dev_err, st));
-    CK(ctx, launch_moe_quant_slots(x, H, H, m.col_src, m.grp_off + E, S, q1, d1, S, ctx->num_sms, st));
-    cudaError_t e = launch_gemm_tc_grouped(view_of(gate_up), F2, m.tiles, m.ntiles, q1, d1, S, S, nullptr, gu, F2, ctx->dev_err,
-                                           ctx->num_sms, st);
-    if (e == cudaErrorInvalidValue) return B200_ERR_UNSUPPORTED;  // a tensor map the driver refused: the GEMV path runs
-    if (e != cudaSuccess) return cuda_fail(ctx, e, "gemm_tc_grouped");
-    CK(ctx, launch_moe_swiglu_slots(gu, F, m.col_src, m.grp_off + E, S, q2, d2, S, ctx->num_sms, st));
+    cudaError_t e;
+    if (fused) {
+        CK(ctx, launch_moe_route_quant(ids, T, top_k, 1, E, expert0, total, x, H, H, m.grp_off, m.inv, nullptr, m.tiles, m.ntiles, q1, d1, S,
+                                       ctx->dev_err, ctx->num_sms, st));
+        e = launch_gemm_tc_grouped_swiglu(view_of(gate_up), F, m.tiles, m.ntiles, q1, d1, S, S, q2, d2, S, ctx->dev_err, ctx->num_sms, st);
+        if (e == cudaErrorInvalidValue) return B200_ERR_UNSUPPORTED;  // a tensor map the driver refused: the GEMV path runs
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "gemm_tc_grouped_swiglu");
+    } else {
+        CK(ctx, launch_moe_route(ids, T, top_k, 1, E, expert0, total, m.grp_off, m.col_src, m.col_dst, m.inv, m.tiles, m.ntiles,
+                                 ctx->dev_err, st));
+        CK(ctx, launch_moe_quant_slots(x, H, H, m.col_src, m.grp_off + E, S, q1, d1, S, ctx->num_sms, st));
+        e = launch_gemm_tc_grouped(view_of(gate_up), F2, m.tiles, m.ntiles, q1, d1, S, S, nullptr, gu, F2, ctx->dev_err, ctx->num_sms, st);
+        if (e == cudaErrorInvalidValue) return B200_ERR_UNSUPPORTED;  // a tensor map the driver refused: the GEMV path runs
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "gemm_tc_grouped");
+        CK(ctx, launch_moe_swiglu_slots(gu, F, m.col_src, m.grp_off + E, S, q2, d2, S, ctx->num_sms, st));
+    }
     e = launch_gemm_tc_grouped(view_of(down), H, m.tiles, m.ntiles, q2, d2, S, S, nullptr, dn, H, ctx->dev_err, ctx->num_sms, st);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "gemm_tc_grouped");
     if (ep) {
@@ -571,9 +582,14 @@ b200_status b200_mul_mat_id(b200_context * ctx, const b200_weight * experts, con
         m.carve(c, P, E);
         int8_t * q = c.take<int8_t>((size_t) S * K);
         float * d = c.take<float>((size_t) (K / 32) * S);
-        CK(ctx, launch_moe_route(ids, T, top_k, nb1, E, 0, E, m.grp_off, m.col_src, m.col_dst, m.inv, m.tiles, m.ntiles, ctx->dev_err,
-                                 ctx->stream));
-        CK(ctx, launch_moe_quant_slots(b, K, K, m.col_src, m.grp_off + E, S, q, d, S, ctx->num_sms, ctx->stream));
+        if (moe_route_quant_fits(P, E, ctx->num_sms)) {
+            CK(ctx, launch_moe_route_quant(ids, T, top_k, nb1, E, 0, E, b, K, K, m.grp_off, m.inv, m.col_dst, m.tiles, m.ntiles, q, d, S,
+                                           ctx->dev_err, ctx->num_sms, ctx->stream));
+        } else {
+            CK(ctx, launch_moe_route(ids, T, top_k, nb1, E, 0, E, m.grp_off, m.col_src, m.col_dst, m.inv, m.tiles, m.ntiles, ctx->dev_err,
+                                     ctx->stream));
+            CK(ctx, launch_moe_quant_slots(b, K, K, m.col_src, m.grp_off + E, S, q, d, S, ctx->num_sms, ctx->stream));
+        }
         const cudaError_t e = launch_gemm_tc_grouped(view_of(experts), N, m.tiles, m.ntiles, q, d, S, S, m.col_dst, dst, N, ctx->dev_err,
                                                      ctx->num_sms, ctx->stream);
         if (e == cudaSuccess) return B200_OK;

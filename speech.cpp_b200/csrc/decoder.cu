@@ -153,7 +153,8 @@ b200_status prepare_mk(b200_decoder * d, const std::vector<GemvParams> & v) {
     const unsigned init[2] = {1u, 0u};
     DCK(d, cudaMemcpy(d->mk_epoch, init, sizeof init, cudaMemcpyHostToDevice));
     // Vectors between products, tagged. Per layer: A q|k|v (x: h0) -> qkv; B o (x: the v part of qkv, res h0) -> h1;
-    // C gate|up (x: h1) -> gu; D down (x: gu, res h1) -> h0. A CTA can be one product ahead of the slowest, so no
+    // C gate|up (x: h1) -> gu, the F values silu(gate) * up (each CTA streams the gate and up rows of its own features
+    // and forms their SwiGLU once); D down (x: gu, res h1) -> h0. A CTA can be one product ahead of the slowest, so no
     // product writes a vector that the product before it reads: h1 (written by B) is not read by A, and h0 (written
     // by D) is read by A and B only, which every CTA has finished before any CTA can start D (D's input gu needs
     // every CTA's C). Layer 0 reads the step input, and the head writes the logits, untagged.
@@ -194,9 +195,12 @@ b200_status prepare_mk(b200_decoder * d, const std::vector<GemvParams> & v) {
             m.x_tagged = 1;
             m.y = reinterpret_cast<float *>(d->t_gu);
             m.y_tagged = 1;
+            m.glu = 1;
         } else {
             m.x = reinterpret_cast<const float *>(d->t_gu);
             m.x_tagged = 1;
+            m.pro = PRO_COPY;  // the SwiGLU was formed by the gate|up product
+            m.pro_k = 0;
             m.res = reinterpret_cast<const float *>(d->t_h1);
             m.res_tagged = 1;
             m.y = reinterpret_cast<float *>(d->t_h0);
@@ -204,9 +208,10 @@ b200_status prepare_mk(b200_decoder * d, const std::vector<GemvParams> & v) {
         }
         if ((((uintptr_t) m.x) & 15) != 0) return dfail(d, B200_ERR_UNSUPPORTED, "decoder: persistent step input not 16-byte aligned");
         m.row_bytes = (int) mk_row_bytes(p.w.type, p.w.K);
-        m.rps = kMkSlotBytes / m.row_bytes;
-        m.slice_base = (int) (p.N / d->ctx->num_sms);
-        m.slice_extra = (int) (p.N % d->ctx->num_sms);
+        m.rps = kMkSlotBytes / m.row_bytes / (m.glu ? 2 : 1);  // a gate|up chunk holds its features' gate and up rows
+        const int64_t units = m.glu ? p.N / 2 : p.N;         // the rows, or the features, the CTAs split
+        m.slice_base = (int) (units / d->ctx->num_sms);
+        m.slice_extra = (int) (units % d->ctx->num_sms);
         auto log2_exact = [](int64_t v) { int s = 0; while ((1ll << s) < v) s++; return (v > 0 && (1ll << s) == v) ? s : -1; };
         m.gqa_shift = p.pro == PRO_GQA ? log2_exact(p.pro_k * p.pro_rep) : -1;
         m.hd_shift = p.pro == PRO_GQA ? log2_exact(p.pro_k) : -1;
@@ -248,13 +253,15 @@ b200_status enqueue_mk(b200_decoder * d) {
 b200_status enqueue_step(b200_decoder * d) {
     std::vector<GemvParams> prods = step_products(d);
     bool persistent = d->mode == B200_DEC_MODE_PERSISTENT;
+    // the gate|up products keep their features' sums in shared memory: at most kMkResRows features per CTA
+    const bool glu_fits = (d->s.ffn + d->ctx->num_sms - 1) / d->ctx->num_sms <= kMkResRows;
     if (d->mode < 0) {
-        persistent = true;
+        persistent = glu_fits;
         for (const GemvParams & p : prods) persistent = persistent && mk_fits(p);
     }
     if (persistent) {
         for (const GemvParams & p : prods)
-            if (!mk_fits(p)) return dfail(d, B200_ERR_UNSUPPORTED, "decoder: a product does not fit the persistent step");
+            if (!mk_fits(p) || !glu_fits) return dfail(d, B200_ERR_UNSUPPORTED, "decoder: a product does not fit the persistent step");
         b200_status s = prepare_mk(d, prods);
         if (s != B200_OK) return s;
         return enqueue_mk(d);

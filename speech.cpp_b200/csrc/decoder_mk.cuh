@@ -38,7 +38,8 @@ struct MkStage {
     int x_tagged;
     int res_tagged;
     int y_tagged;
-    int pad_;
+    int glu;          // 1: a gate|up product: its rows are F gate rows then F up rows (N = 2F), a CTA's slice is a range of
+                      // F features, and it writes silu(gate) * up for them (F values)
     // precomputed by the host (no divisions on the device's critical path)
     int row_bytes;    // GGUF bytes of one weight row
     int rps;          // rows per ring slot
@@ -348,6 +349,30 @@ __device__ __forceinline__ void mk_rows(const MkStage & S, const Act & a, const 
     else smem_rows_lpr<T, 32>(f, K, (int) rows, a, S.w, warp, kMkConsumerWarps, store);
 }
 
+// A gate|up product's chunk (features [first, first + rows)): the gate rows into gu_s[0], the up rows into gu_s[1],
+// indexed by the feature's place in the CTA's slice. A slot holds per field the chunk's gate rows, then (from row
+// rps) its up rows.
+template <class T, bool kForms>
+__device__ __forceinline__ void mk_rows_glu(const MkStage & S, const Act & a, const uint8_t * slot, int64_t rps, int64_t rows,
+                                            int64_t first, int64_t r0, float (*gu_s)[kMkResRows]) {
+    const int warp = threadIdx.x >> 5;
+    const int64_t K = S.w.K;
+#pragma unroll 1
+    for (int half = 0; half < 2; half++) {  // one copy of the row code for both halves (register pressure)
+        const uint8_t * f[4];
+        const uint8_t * b = slot;
+        for (int i = 0; i < 4; i++) {
+            f[i] = b + (half ? rps * T::field_row_bytes(K, i) : 0);
+            if (i < T::kFields) b += 2 * rps * T::field_row_bytes(K, i);
+        }
+        float * out = gu_s[half] + (first - r0);
+        auto store = [&](int j, float v) { out[j] = v; };
+        if constexpr (kForms) smem_rows<T>(f, K, (int) rows, a, S.w, warp, kMkConsumerWarps, store);
+        else if (T::units_per_row(K) <= 64) smem_rows_lpr<T, 8>(f, K, (int) rows, a, S.w, warp, kMkConsumerWarps, store);
+        else smem_rows_lpr<T, 32>(f, K, (int) rows, a, S.w, warp, kMkConsumerWarps, store);
+    }
+}
+
 template <class T>
 __device__ __forceinline__ void mk_issue(const MkStage & S, uint8_t * slot, int64_t rps, int64_t first, int64_t rows, uint64_t * bar) {
     const uint8_t * fb[4] = {S.w.f0, S.w.f1, S.w.f2, S.w.f3};
@@ -355,7 +380,8 @@ __device__ __forceinline__ void mk_issue(const MkStage & S, uint8_t * slot, int6
     for (int i = 0; i < T::kFields; i++) {
         const int64_t rb = T::field_row_bytes(S.w.K, i);
         bulk_g2s(dst, fb[i] + first * rb, (uint32_t) (rows * rb), bar);
-        dst += rps * rb;
+        if (S.glu) bulk_g2s(dst + rps * rb, fb[i] + (S.N / 2 + first) * rb, (uint32_t) (rows * rb), bar);  // the up rows
+        dst += (S.glu ? 2 : 1) * rps * rb;
     }
 }
 
@@ -364,11 +390,14 @@ __device__ __forceinline__ void mk_issue(const MkStage & S, uint8_t * slot, int6
 // the generic one (measured on B200, config 2 step: 495 us against 552 us with the K-quant forms compiled in), a step
 // with K-quant products the other (config 3 step: 845 us against 890 us).
 template <bool kForms>
-__global__ void __launch_bounds__(kMkThreads, 1) decoder_mk_kernel(MkParams P) {
+// One CTA per SM of kMkThreads threads: up to 224 registers a thread fit (224 x 288 <= 65536); the default bound for
+// this launch shape (168) made the K-quant row forms spill.
+__global__ void __maxnreg__(224) decoder_mk_kernel(MkParams P) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ double part[kMkConsumerWarps];
     __shared__ int give_up;
     __shared__ float res_s[kMkResRows];
+    __shared__ float gu_s[2][kMkResRows];  // a gate|up product's sums of the CTA's features: gate, up
     __shared__ __align__(16) MkStage desc[3];  // this product's, the next one's, and the one after (being copied)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = gridDim.x, cta = blockIdx.x;
@@ -404,7 +433,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decoder_mk_kernel(MkParams P) {
                         return;
                     }
                     const int64_t rows = r1 - first < rps ? r1 - first : rps;
-                    mbar_arrive_expect_tx(&full[slot], (uint32_t) (rows * rb));
+                    mbar_arrive_expect_tx(&full[slot], (uint32_t) ((S.glu ? 2 : 1) * rows * rb));
                     uint8_t * dst = ring + (size_t) slot * kMkSlotBytes;
                     switch (S.w.type) {
                     case B200_TYPE_Q8_0: mk_issue<TQ8_0>(S, dst, rps, first, rows, &full[slot]); break;
@@ -464,6 +493,17 @@ __global__ void __launch_bounds__(kMkThreads, 1) decoder_mk_kernel(MkParams P) {
             }
             const int64_t rows = r1 - first < rps ? r1 - first : rps;
             const uint8_t * sp = ring + (size_t) slot * kMkSlotBytes;
+            if (S.glu) {
+                switch (S.w.type) {
+                case B200_TYPE_Q8_0: mk_rows_glu<TQ8_0, kForms>(S, a, sp, rps, rows, first, r0, gu_s); break;
+                case B200_TYPE_Q4_K: mk_rows_glu<TQ4_K, kForms>(S, a, sp, rps, rows, first, r0, gu_s); break;
+                case B200_TYPE_Q6_K: mk_rows_glu<TQ6_K, kForms>(S, a, sp, rps, rows, first, r0, gu_s); break;
+                default: mk_rows_glu<TBF16, kForms>(S, a, sp, rps, rows, first, r0, gu_s); break;
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[slot]);
+                continue;
+            }
             switch (S.w.type) {
             case B200_TYPE_Q8_0: mk_rows<TQ8_0, kForms>(S, a, sp, rps, rows, first, r0, res_s, out_tag); break;
             case B200_TYPE_Q4_K: mk_rows<TQ4_K, kForms>(S, a, sp, rps, rows, first, r0, res_s, out_tag); break;
@@ -476,6 +516,12 @@ __global__ void __launch_bounds__(kMkThreads, 1) decoder_mk_kernel(MkParams P) {
         cp_async_wait_all();  // the next descriptor has landed
         mk_sync();  // all outputs of this CTA for product s are written; the act arrays may be reused
         if (give_up) break;
+        if (S.glu && (int64_t) threadIdx.x < r1 - r0) {
+            // silu(gate) * up of the CTA's features, once each (SiLU evaluated exactly, as the oracle defines it)
+            const float v = __fmul_rn(silu_exact(gu_s[0][threadIdx.x]), gu_s[1][threadIdx.x]);
+            const int64_t r = r0 + threadIdx.x;
+            asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(S.y + 2 * r), "r"(__float_as_uint(v)), "r"(out_tag) : "memory");
+        }
     }
     // ---- end of the launch: once every CTA is here (all have read the epoch), CTA 0 advances it ----
     if (threadIdx.x == 0) {

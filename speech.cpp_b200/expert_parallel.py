@@ -34,7 +34,7 @@ class PeerCombine:
     b200_moe_ffn_ep combines the ranks' partial sums in one kernel over NVLink peer memory (a two-shot all-reduce:
     partial rows pushed to each token's owner, owners' sums pushed to every rank) instead of an NCCL all-reduce."""
 
-    def __init__(self, ctx, group, max_tokens: int, hidden: int):
+    def __init__(self, ctx, group, max_tokens: int, hidden: int, timeout_us: int = 0):
         import torch.distributed as dist
 
         self.ctx, self.group = ctx, group
@@ -57,6 +57,8 @@ class PeerCombine:
         arr = (ctypes.c_void_p * self.world)(*ptrs)
         self.handle = ctypes.c_void_p()
         ctx.check(L.b200_ep_create(ctx.h, self.rank, self.world, max_tokens, hidden, arr, ctypes.byref(self.handle)))
+        if timeout_us:
+            ctx.check(L.b200_ep_set_timeout(self.handle, timeout_us))
         dist.barrier(group=group)  # every rank has mapped every mailbox before any rank writes into one
 
     def close(self):

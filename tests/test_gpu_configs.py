@@ -3,7 +3,10 @@ at its full size, through the C ABI.
 
 - Config 2: the 28-layer Qwen3-TTS 0.6B talker decode step (Q8_0, n_head 16, vocab 3072) on the persistent step
   kernel, against oracle/stack.py (Qwen3Decoder::layers / outputs, src/common/qwen3-decoder.cpp:350-438); logits
-  cosine >= 0.9999, and the (sub-)block int32 sums of one product bit for bit.
+  cosine >= 0.9999 and at least 99 % of them bit-equal, and the (sub-)block int32 sums of one product bit for bit.
+  The chain re-quantizes every product's input, so a last-bit difference anywhere turns into a different int8 and
+  grows over 28 layers (the oracle itself, perturbed by one float ulp per product, lands near cosine 0.9998): the
+  kernel therefore computes every float step as the oracle defines it, exactly.
 - Config 3, decode: the 28-layer Qwen3-ASR 1.7B-shaped step (Q4_K / Q6_K, vocab 151936, Q6_K head), same bars.
 - Config 3, prefill: one layer's four products at M = 1500 rows on the K-quant tensor-core path, plus the head on
   the last row; |err| <= 1e-4 * sum |w x| per element on a sample of rows that includes the first and last row of
@@ -102,7 +105,11 @@ def test_full_decode_step(b200, ctx, oracle, name):
     assert d.launches == 1  # the persistent step kernel: the configuration bench.py times
     assert got.shape == (c["n_vocab"],)
     cos = cosine(got, want)
-    assert cos >= 0.9999, f"{name}: cosine {cos:.7f}"
+    same = float(np.mean(got == want))
+    assert cos >= 0.9999, f"{name}: cosine {cos:.7f} (bit-equal logits {same:.4f})"
+    # the step's float steps are the oracle's (exact block sums rounded once; RMSNorm and SiLU in double): its 113
+    # re-quantized products stay identical, so the logits match bit for bit except near rounding ties
+    assert same >= 0.99, f"{name}: bit-equal logits {same:.4f}"
     assert np.array_equal(d.step_host(x), got)  # the host entry point runs the same step
     d.close()
 

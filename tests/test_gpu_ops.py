@@ -131,6 +131,10 @@ def test_mul_mat_within_tolerance(ctx, oracle, qtype, K, N, M):
     err = np.abs(got.astype(np.float64) - want)
     b = bound(oracle, qtype, wb, K, x)
     assert np.all(err <= b), f"max err/bound {np.max(err / b):.3g}"
+    if M <= 16:
+        # the GEMV kernels sum the block terms in double and round once, as the oracle defines the float step: equal
+        # floats except where the exact sum lies within double rounding of a float32 rounding boundary (rare)
+        assert np.mean(got == want) >= 0.999, f"bit-equal fraction {np.mean(got == want):.5f}"
     ctx.free_weight(w)
 
 
