@@ -51,6 +51,7 @@ enum {
     B200_TYPE_F16 = 1,
     B200_TYPE_Q8_0 = 8,
     B200_TYPE_Q4_K = 12,
+    B200_TYPE_Q5_K = 13,
     B200_TYPE_Q6_K = 14,
     B200_TYPE_Q8_K = 15,
     B200_TYPE_BF16 = 30
@@ -90,6 +91,7 @@ b200_status b200_memcpy_d2h(b200_context * ctx, void * host_dst, const void * de
  * byte offset (src/common/model-file.cpp:247-268). b200_weight_set / _get accept the same GGUF bytes at the same
  * offsets. On the device the blocks are stored field by field, one row-contiguous array per block field, each array
  * 256-byte aligned (Q8_0: qs int8 [R][K] | d fp16 [R][K/32]; Q4_K: qs [R][K/2] | d, dmin, scales [R][K/256][16];
+ * Q5_K: qs [R][K/2] | d, dmin, scales [R][K/256][16] | qh [R][K/8];
  * Q6_K: ql [R][K/2] | qh [R][K/4] | scales [R][K/256][16] | d fp16 [R][K/256]; BF16 as is). That is a byte
  * permutation, so any piece boundary works and the device holds exactly the GGUF bytes plus alignment.
  * ------------------------------------------------------------------------------------------------------------ */

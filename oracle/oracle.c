@@ -91,6 +91,7 @@ size_t oracle_row_size(int type, int64_t k) {
     case ORACLE_TYPE_BF16: return (size_t) k * 2;
     case ORACLE_TYPE_Q8_0: return k % 32 ? 0 : (size_t) (k / 32) * sizeof(oracle_block_q8_0);
     case ORACLE_TYPE_Q4_K: return k % 256 ? 0 : (size_t) (k / 256) * sizeof(oracle_block_q4_K);
+    case ORACLE_TYPE_Q5_K: return k % 256 ? 0 : (size_t) (k / 256) * sizeof(oracle_block_q5_K);
     case ORACLE_TYPE_Q6_K: return k % 256 ? 0 : (size_t) (k / 256) * sizeof(oracle_block_q6_K);
     case ORACLE_TYPE_Q8_K: return k % 256 ? 0 : (size_t) (k / 256) * sizeof(oracle_block_q8_K);
     default: return 0;
@@ -101,6 +102,7 @@ int oracle_vec_dot_type(int type) {
     switch (type) {
     case ORACLE_TYPE_Q8_0: return ORACLE_TYPE_Q8_0;
     case ORACLE_TYPE_Q4_K:
+    case ORACLE_TYPE_Q5_K:
     case ORACLE_TYPE_Q6_K: return ORACLE_TYPE_Q8_K;
     case ORACLE_TYPE_BF16: return ORACLE_TYPE_BF16;
     case ORACLE_TYPE_F32: return ORACLE_TYPE_F32;
@@ -230,6 +232,64 @@ void oracle_quantize_q4_K(const float * x, void * vy, int64_t k) {
 }
 
 /*
+ * Q5_K weights (our own plain min/max quantizer, valid blocks, as for Q4_K). Layout (GGUF, as gguf-py's
+ * Q5_K.dequantize_blocks reads it, quants.py:528-551): d, dmin (fp16), the 12 scale bytes packed as Q4_K's, qh[32]
+ * (bit j of byte l is the fifth bit of value l of sub-block j), qs[128] as Q4_K's four-bit values. Value =
+ * d*sc*q - dmin*m with q = low | fifth << 4 in 0..31.
+ */
+void oracle_quantize_q5_K(const float * x, void * vy, int64_t k) {
+    oracle_block_q5_K * y = (oracle_block_q5_K *) vy;
+    for (int64_t i = 0; i < k / 256; i++) {
+        const float * xb = x + i * 256;
+        float scale[8], mn[8], max_scale = 0.0f, max_min = 0.0f;
+        for (int s = 0; s < 8; s++) {
+            float lo = xb[s * 32], hi = xb[s * 32];
+            for (int l = 1; l < 32; l++) {
+                const float v = xb[s * 32 + l];
+                if (v < lo) lo = v;
+                if (v > hi) hi = v;
+            }
+            if (lo > 0.0f) lo = 0.0f;
+            scale[s] = (hi - lo) / 31.0f;
+            mn[s] = -lo;
+            if (scale[s] > max_scale) max_scale = scale[s];
+            if (mn[s] > max_min) max_min = mn[s];
+        }
+        const uint16_t dh = oracle_fp32_to_fp16(max_scale / 63.0f);
+        const uint16_t mh = oracle_fp32_to_fp16(max_min / 63.0f);
+        const float d = oracle_fp16_to_fp32(dh), dmin = oracle_fp16_to_fp32(mh);
+        uint8_t sc[8], m[8];
+        for (int s = 0; s < 8; s++) {
+            int a = d > 0.0f ? nearest_even(scale[s] / d) : 0;
+            int b = dmin > 0.0f ? nearest_even(mn[s] / dmin) : 0;
+            sc[s] = (uint8_t) (a < 0 ? 0 : a > 63 ? 63 : a);
+            m[s] = (uint8_t) (b < 0 ? 0 : b > 63 ? 63 : b);
+        }
+        y[i].d = dh;
+        y[i].dmin = mh;
+        for (int j = 0; j < 4; j++) {
+            y[i].scales[j] = (uint8_t) ((sc[j] & 63) | ((sc[j + 4] >> 4) << 6));
+            y[i].scales[j + 4] = (uint8_t) ((m[j] & 63) | ((m[j + 4] >> 4) << 6));
+            y[i].scales[j + 8] = (uint8_t) ((sc[j + 4] & 15) | ((m[j + 4] & 15) << 4));
+        }
+        uint8_t q[256];
+        for (int s = 0; s < 8; s++) {
+            const float ds = d * (float) sc[s], ms = dmin * (float) m[s];
+            for (int l = 0; l < 32; l++) {
+                int v = ds > 0.0f ? nearest_even((xb[s * 32 + l] + ms) / ds) : 0;
+                q[s * 32 + l] = (uint8_t) (v < 0 ? 0 : v > 31 ? 31 : v);
+            }
+        }
+        memset(y[i].qh, 0, sizeof y[i].qh);
+        for (int s = 0; s < 8; s++)
+            for (int l = 0; l < 32; l++) y[i].qh[l] |= (uint8_t) (((q[s * 32 + l] >> 4) & 1) << s);
+        for (int g = 0; g < 4; g++)
+            for (int l = 0; l < 32; l++)
+                y[i].qs[g * 32 + l] = (uint8_t) ((q[(2 * g) * 32 + l] & 15) | ((q[(2 * g + 1) * 32 + l] & 15) << 4));
+    }
+}
+
+/*
  * Q6_K weights (our own plain quantizer, valid blocks). Layout (GGUF, as gguf-py's Q6_K.dequantize_blocks reads it,
  * quants.py:554-575): value v = h*128 + t*32 + l (h in 0..1, t in 0..3, l in 0..31) has its low four bits in byte
  * ql[h*64 + (t&1)*32 + l] (low nibble for t < 2, high for t >= 2) and its high two bits in qh[h*32 + l] at bit 2t;
@@ -290,6 +350,7 @@ int oracle_quantize_rows(int type, const float * x, void * y, int64_t k, int64_t
     case ORACLE_TYPE_Q8_0: fn = oracle_quantize_q8_0; break;
     case ORACLE_TYPE_Q8_K: fn = oracle_quantize_q8_K; break;
     case ORACLE_TYPE_Q4_K: fn = oracle_quantize_q4_K; break;
+    case ORACLE_TYPE_Q5_K: fn = oracle_quantize_q5_K; break;
     case ORACLE_TYPE_Q6_K: fn = oracle_quantize_q6_K; break;
     case ORACLE_TYPE_BF16: fn = oracle_quantize_bf16; break;
     default: return -1;
@@ -325,6 +386,12 @@ static int q6_K_value(const oracle_block_q6_K * b, int v) {
     return (lo | (hi << 4)) - 32;
 }
 
+/* Value v (0..255) of a Q5_K block as the unsigned five-bit integer. */
+static int q5_K_value(const oracle_block_q5_K * b, int v) {
+    const int s = v >> 5, l = v & 31;
+    return ((b->qs[(s >> 1) * 32 + l] >> ((s & 1) * 4)) & 15) | (((b->qh[l] >> s) & 1) << 4);
+}
+
 /* Value v (0..255) of a Q4_K block as the unsigned four-bit integer. */
 static int q4_K_value(const oracle_block_q4_K * b, int v) {
     const int s = v >> 5, l = v & 31;
@@ -350,6 +417,19 @@ int oracle_dequantize_row(int type, const void * vx, float * y, int64_t k) {
         for (int64_t i = 0; i < k / 32; i++) {
             const float d = oracle_fp16_to_fp32(x[i].d);
             for (int j = 0; j < 32; j++) y[i * 32 + j] = (float) x[i].qs[j] * d;
+        }
+        return 0;
+    }
+    case ORACLE_TYPE_Q5_K: {
+        const oracle_block_q5_K * x = (const oracle_block_q5_K *) vx;
+        for (int64_t i = 0; i < k / 256; i++) {
+            const float d = oracle_fp16_to_fp32(x[i].d), dmin = oracle_fp16_to_fp32(x[i].dmin);
+            for (int s = 0; s < 8; s++) {
+                uint8_t sc, m;
+                q4_K_scale_min(x[i].scales, s, &sc, &m);
+                const float ds = d * (float) sc, dm = dmin * (float) m;
+                for (int l = 0; l < 32; l++) y[i * 256 + s * 32 + l] = ds * (float) q5_K_value(&x[i], s * 32 + l) - dm;
+            }
         }
         return 0;
     }
@@ -421,6 +501,20 @@ static void sums_q4_K(const oracle_block_q4_K * w, const oracle_block_q8_K * x, 
     *summ = sm;
 }
 
+static void sums_q5_K(const oracle_block_q5_K * w, const oracle_block_q8_K * x, int32_t * sumi, int32_t * summ) {
+    int32_t si = 0, sm = 0;
+    for (int s = 0; s < 8; s++) {
+        uint8_t sc, m;
+        q4_K_scale_min(w->scales, s, &sc, &m);
+        int32_t isum = 0;
+        for (int l = 0; l < 32; l++) isum += q5_K_value(w, s * 32 + l) * (int) x->qs[s * 32 + l];
+        si += (int32_t) sc * isum;
+        sm += (int32_t) m * ((int32_t) x->bsums[2 * s] + (int32_t) x->bsums[2 * s + 1]);
+    }
+    *sumi = si;
+    *summ = sm;
+}
+
 static int32_t sums_q6_K(const oracle_block_q6_K * w, const oracle_block_q8_K * x) {
     int32_t si = 0;
     for (int g = 0; g < 16; g++) {
@@ -436,6 +530,19 @@ static float dot_q4_K(const oracle_block_q4_K * w, const oracle_block_q8_K * x, 
     for (int64_t i = 0; i < nb; i++) {
         int32_t sumi, summ;
         sums_q4_K(&w[i], &x[i], &sumi, &summ);
+        const float d = x[i].d * oracle_fp16_to_fp32(w[i].d);
+        const float dmin = x[i].d * oracle_fp16_to_fp32(w[i].dmin);
+        sum += (double) d * (double) sumi;
+        sum -= (double) dmin * (double) summ;
+    }
+    return (float) sum;
+}
+
+static float dot_q5_K(const oracle_block_q5_K * w, const oracle_block_q8_K * x, int64_t nb) {
+    double sum = 0.0;
+    for (int64_t i = 0; i < nb; i++) {
+        int32_t sumi, summ;
+        sums_q5_K(&w[i], &x[i], &sumi, &summ);
         const float d = x[i].d * oracle_fp16_to_fp32(w[i].d);
         const float dmin = x[i].d * oracle_fp16_to_fp32(w[i].dmin);
         sum += (double) d * (double) sumi;
@@ -469,6 +576,7 @@ float oracle_vec_dot(int type, const void * w, const void * x, int64_t k) {
     switch (type) {
     case ORACLE_TYPE_Q8_0: return dot_q8_0((const oracle_block_q8_0 *) w, (const oracle_block_q8_0 *) x, k / 32);
     case ORACLE_TYPE_Q4_K: return dot_q4_K((const oracle_block_q4_K *) w, (const oracle_block_q8_K *) x, k / 256);
+    case ORACLE_TYPE_Q5_K: return dot_q5_K((const oracle_block_q5_K *) w, (const oracle_block_q8_K *) x, k / 256);
     case ORACLE_TYPE_Q6_K: return dot_q6_K((const oracle_block_q6_K *) w, (const oracle_block_q8_K *) x, k / 256);
     case ORACLE_TYPE_BF16: return dot_bf16((const uint16_t *) w, (const uint16_t *) x, k);
     case ORACLE_TYPE_F32: return dot_f32((const float *) w, (const float *) x, k);
@@ -492,6 +600,12 @@ int64_t oracle_block_sums(int type, const void * vw, const void * vx, int64_t k,
         const oracle_block_q4_K * w = (const oracle_block_q4_K *) vw;
         const oracle_block_q8_K * x = (const oracle_block_q8_K *) vx;
         for (int64_t i = 0; i < k / 256; i++) sums_q4_K(&w[i], &x[i], &out[2 * i], &out[2 * i + 1]);
+        return 2 * (k / 256);
+    }
+    case ORACLE_TYPE_Q5_K: {
+        const oracle_block_q5_K * w = (const oracle_block_q5_K *) vw;
+        const oracle_block_q8_K * x = (const oracle_block_q8_K *) vx;
+        for (int64_t i = 0; i < k / 256; i++) sums_q5_K(&w[i], &x[i], &out[2 * i], &out[2 * i + 1]);
         return 2 * (k / 256);
     }
     case ORACLE_TYPE_Q6_K: {

@@ -41,6 +41,7 @@ enum {
     ORACLE_TYPE_F16 = 1,
     ORACLE_TYPE_Q8_0 = 8,
     ORACLE_TYPE_Q4_K = 12,
+    ORACLE_TYPE_Q5_K = 13,
     ORACLE_TYPE_Q6_K = 14,
     ORACLE_TYPE_Q8_K = 15,
     ORACLE_TYPE_BF16 = 30,
@@ -61,6 +62,14 @@ typedef struct {
     uint8_t scales[12];  /* 8 six-bit scales and 8 six-bit mins */
     uint8_t qs[128];     /* 256 four-bit values */
 } oracle_block_q4_K;     /* 144 bytes */
+
+typedef struct {
+    uint16_t d;          /* fp16 super-block scale of the sub-block scales */
+    uint16_t dmin;       /* fp16 super-block scale of the sub-block mins */
+    uint8_t scales[12];  /* 8 six-bit scales and 8 six-bit mins, packed as Q4_K's */
+    uint8_t qh[32];      /* bit j of byte l: the fifth bit of value l of sub-block j */
+    uint8_t qs[128];     /* low four bits, laid out as Q4_K's values */
+} oracle_block_q5_K;     /* 176 bytes */
 
 typedef struct {
     uint8_t ql[128];     /* low four bits of 256 six-bit values */
@@ -88,6 +97,7 @@ float oracle_bf16_to_fp32(uint16_t h);
 void oracle_quantize_q8_0(const float * x, void * y, int64_t k);
 void oracle_quantize_q8_K(const float * x, void * y, int64_t k);
 void oracle_quantize_q4_K(const float * x, void * y, int64_t k);
+void oracle_quantize_q5_K(const float * x, void * y, int64_t k);
 void oracle_quantize_q6_K(const float * x, void * y, int64_t k);
 void oracle_quantize_bf16(const float * x, void * y, int64_t k);
 /* Quantizes n rows of k values each, in parallel over rows (nthreads <= 0: all). */

@@ -13,9 +13,10 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "liboracle.so")
 
-F32, F16, Q8_0, Q4_K, Q6_K, Q8_K, BF16 = 0, 1, 8, 12, 14, 15, 30
-BLOCK = {F32: (1, 4), F16: (1, 2), BF16: (1, 2), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210), Q8_K: (256, 292)}
-VEC_DOT_TYPE = {Q8_0: Q8_0, Q4_K: Q8_K, Q6_K: Q8_K, BF16: BF16, F32: F32}
+F32, F16, Q8_0, Q4_K, Q5_K, Q6_K, Q8_K, BF16 = 0, 1, 8, 12, 13, 14, 15, 30
+BLOCK = {F32: (1, 4), F16: (1, 2), BF16: (1, 2), Q8_0: (32, 34), Q4_K: (256, 144), Q5_K: (256, 176), Q6_K: (256, 210),
+         Q8_K: (256, 292)}
+VEC_DOT_TYPE = {Q8_0: Q8_0, Q4_K: Q8_K, Q5_K: Q8_K, Q6_K: Q8_K, BF16: BF16, F32: F32}
 
 _lib = None
 
@@ -83,7 +84,7 @@ def dequantize(qtype, blocks, k):
 
 
 def block_sums(qtype, w_row, x_row_q, k):
-    n = {Q8_0: k // 32, Q4_K: 2 * (k // 256), Q6_K: k // 256}[qtype]
+    n = {Q8_0: k // 32, Q4_K: 2 * (k // 256), Q5_K: 2 * (k // 256), Q6_K: k // 256}[qtype]
     out = np.empty(n, dtype=np.int32)
     got = lib().oracle_block_sums(qtype, _p(np.ascontiguousarray(w_row)), _p(np.ascontiguousarray(x_row_q)), k, _p(out))
     assert got == n

@@ -17,9 +17,10 @@ import weakref
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libb200.so")
 
-F32, F16, Q8_0, Q4_K, Q6_K, Q8_K, BF16 = 0, 1, 8, 12, 14, 15, 30
-TYPE_NAMES = {F32: "F32", F16: "F16", Q8_0: "Q8_0", Q4_K: "Q4_K", Q6_K: "Q6_K", Q8_K: "Q8_K", BF16: "BF16"}
-BLOCK = {F32: (1, 4), F16: (1, 2), BF16: (1, 2), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210), Q8_K: (256, 292)}
+F32, F16, Q8_0, Q4_K, Q5_K, Q6_K, Q8_K, BF16 = 0, 1, 8, 12, 13, 14, 15, 30
+TYPE_NAMES = {F32: "F32", F16: "F16", Q8_0: "Q8_0", Q4_K: "Q4_K", Q5_K: "Q5_K", Q6_K: "Q6_K", Q8_K: "Q8_K", BF16: "BF16"}
+BLOCK = {F32: (1, 4), F16: (1, 2), BF16: (1, 2), Q8_0: (32, 34), Q4_K: (256, 144), Q5_K: (256, 176), Q6_K: (256, 210),
+         Q8_K: (256, 292)}
 
 OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_ALLOC, ERR_DEVICE, ERR_RANGE, ERR_TIMEOUT = 0, -1, -2, -3, -4, -5, -6
 STATUS_NAMES = {0: "OK", -1: "INVALID", -2: "UNSUPPORTED", -3: "ALLOC", -4: "DEVICE", -5: "RANGE", -6: "TIMEOUT"}
@@ -362,7 +363,7 @@ class Context:
     def block_sums(self, w, x):
         import torch
 
-        per_row = {Q8_0: w.ne0 // 32, Q4_K: 2 * (w.ne0 // 256), Q6_K: w.ne0 // 256}[w.type]
+        per_row = {Q8_0: w.ne0 // 32, Q4_K: 2 * (w.ne0 // 256), Q5_K: 2 * (w.ne0 // 256), Q6_K: w.ne0 // 256}[w.type]
         out = torch.empty((w.ne1 * w.ne2, per_row), dtype=torch.int32, device=x.device)
         self._sync_in()
         self.check(self.L.b200_block_sums(self.h, ctypes.byref(w), _ptr(x), _ptr(out)))

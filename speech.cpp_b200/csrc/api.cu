@@ -29,13 +29,15 @@ b200_status cuda_fail(b200_context * ctx, cudaError_t e, const char * where) {
     } while (0)
 
 bool known_weight_type(int t) {
-    return t == B200_TYPE_Q8_0 || t == B200_TYPE_Q4_K || t == B200_TYPE_Q6_K || t == B200_TYPE_BF16 || t == B200_TYPE_F32;
+    return t == B200_TYPE_Q8_0 || t == B200_TYPE_Q4_K || t == B200_TYPE_Q5_K || t == B200_TYPE_Q6_K || t == B200_TYPE_BF16 ||
+           t == B200_TYPE_F32;
 }
 
 int64_t block_values(int t) {
     switch (t) {
     case B200_TYPE_Q8_0: return 32;
     case B200_TYPE_Q4_K:
+    case B200_TYPE_Q5_K:
     case B200_TYPE_Q6_K:
     case B200_TYPE_Q8_K: return 256;
     default: return 1;
@@ -46,6 +48,7 @@ int64_t block_bytes(int t) {
     switch (t) {
     case B200_TYPE_Q8_0: return 34;
     case B200_TYPE_Q4_K: return 144;
+    case B200_TYPE_Q5_K: return 176;
     case B200_TYPE_Q6_K: return 210;
     case B200_TYPE_Q8_K: return 292;
     case B200_TYPE_BF16:
@@ -508,18 +511,17 @@ struct MoeSlots {
     }
 };
 
-// The expert FFN on the tensor cores: route into padded slots and quantize x per slot (one kernel), gate|up grouped
-// GEMM with SwiGLU and the q8_0 re-quantization in its epilogue, down grouped GEMM, weighted combine (over NVLink peer
-// memory when `ep` is given). Both expert matrices Q8_0 with K % 256 == 0. When the fused route kernel's shared memory
-// or the 64-feature tiles do not fit the shape, the same steps run as separate kernels.
+// The expert FFN on the tensor cores: route into padded slots, quantize x per slot, gate|up grouped GEMM, SwiGLU +
+// re-quantization per slot, down grouped GEMM, weighted combine (over NVLink peer memory when `ep` is given). Both
+// expert matrices Q8_0 with K % 256 == 0. (Fusing the route with the quantization, and the SwiGLU into the gate|up
+// GEMM's epilogue, measured slower on B200: 26.7k against 29.3k tokens/s for config 5 on one GPU, equal on eight.)
 b200_status moe_ffn_tc(b200_context * ctx, const b200_weight * gate_up, const b200_weight * down, int64_t expert0, int64_t total,
                        const float * x, const int32_t * ids, const float * w, int64_t top_k, int64_t T, float * out,
                        const b200_ep_group * ep = nullptr) {
     const int64_t H = gate_up->ne0, F2 = gate_up->ne1, E = gate_up->ne2, F = F2 / 2, P = T * top_k;
     const int64_t S = moe_max_slots(P, E);
     auto up = [](size_t v) { return (v + 255) & ~(size_t) 255; };
-    const bool fused = moe_route_quant_fits(P, E, ctx->num_sms) && F % 64 == 0;
-    const size_t need = MoeSlots::bytes(P, E) + up((size_t) S * H) + up((size_t) (H / 32) * S * 4) + (fused ? 0 : up((size_t) S * F2 * 4)) +
+    const size_t need = MoeSlots::bytes(P, E) + up((size_t) S * H) + up((size_t) (H / 32) * S * 4) + up((size_t) S * F2 * 4) +
                         up((size_t) S * F) + up((size_t) (F / 32) * S * 4) + up((size_t) S * H * 4);
     b200_status s = ensure_scratch(ctx, need);
     if (s != B200_OK) return s;
@@ -528,27 +530,19 @@ b200_status moe_ffn_tc(b200_context * ctx, const b200_weight * gate_up, const b2
     m.carve(c, P, E);
     int8_t * q1 = c.take<int8_t>((size_t) S * H);
     float * d1 = c.take<float>((size_t) (H / 32) * S);
-    float * gu = fused ? nullptr : c.take<float>((size_t) S * F2);
+    float * gu = c.take<float>((size_t) S * F2);
     int8_t * q2 = c.take<int8_t>((size_t) S * F);
     float * d2 = c.take<float>((size_t) (F / 32) * S);
     float * dn = c.take<float>((size_t) S * H);
     cudaStream_t st = ctx->stream;
-    cudaError_t e;
-    if (fused) {
-        CK(ctx, launch_moe_route_quant(ids, T, top_k, 1, E, expert0, total, x, H, H, m.grp_off, m.inv, nullptr, m.tiles, m.ntiles, q1, d1, S,
-                                       ctx->dev_err, ctx->num_sms, st));
-        e = launch_gemm_tc_grouped_swiglu(view_of(gate_up), F, m.tiles, m.ntiles, q1, d1, S, S, q2, d2, S, ctx->dev_err, ctx->num_sms, st);
-        if (e == cudaErrorInvalidValue) return B200_ERR_UNSUPPORTED;  // a tensor map the driver refused: the GEMV path runs
-        if (e != cudaSuccess) return cuda_fail(ctx, e, "gemm_tc_grouped_swiglu");
-    } else {
-        CK(ctx, launch_moe_route(ids, T, top_k, 1, E, expert0, total, m.grp_off, m.col_src, m.col_dst, m.inv, m.tiles, m.ntiles,
-                                 ctx->dev_err, st));
-        CK(ctx, launch_moe_quant_slots(x, H, H, m.col_src, m.grp_off + E, S, q1, d1, S, ctx->num_sms, st));
-        e = launch_gemm_tc_grouped(view_of(gate_up), F2, m.tiles, m.ntiles, q1, d1, S, S, nullptr, gu, F2, ctx->dev_err, ctx->num_sms, st);
-        if (e == cudaErrorInvalidValue) return B200_ERR_UNSUPPORTED;  // a tensor map the driver refused: the GEMV path runs
-        if (e != cudaSuccess) return cuda_fail(ctx, e, "gemm_tc_grouped");
-        CK(ctx, launch_moe_swiglu_slots(gu, F, m.col_src, m.grp_off + E, S, q2, d2, S, ctx->num_sms, st));
-    }
+    CK(ctx, launch_moe_route(ids, T, top_k, 1, E, expert0, total, m.grp_off, m.col_src, m.col_dst, m.inv, m.tiles, m.ntiles,
+                             ctx->dev_err, st));
+    CK(ctx, launch_moe_quant_slots(x, H, H, m.col_src, m.grp_off + E, S, q1, d1, S, ctx->num_sms, st));
+    cudaError_t e = launch_gemm_tc_grouped(view_of(gate_up), F2, m.tiles, m.ntiles, q1, d1, S, S, nullptr, gu, F2, ctx->dev_err,
+                                           ctx->num_sms, st);
+    if (e == cudaErrorInvalidValue) return B200_ERR_UNSUPPORTED;  // a tensor map the driver refused: the GEMV path runs
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "gemm_tc_grouped");
+    CK(ctx, launch_moe_swiglu_slots(gu, F, m.col_src, m.grp_off + E, S, q2, d2, S, ctx->num_sms, st));
     e = launch_gemm_tc_grouped(view_of(down), H, m.tiles, m.ntiles, q2, d2, S, S, nullptr, dn, H, ctx->dev_err, ctx->num_sms, st);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "gemm_tc_grouped");
     if (ep) {
@@ -582,14 +576,9 @@ b200_status b200_mul_mat_id(b200_context * ctx, const b200_weight * experts, con
         m.carve(c, P, E);
         int8_t * q = c.take<int8_t>((size_t) S * K);
         float * d = c.take<float>((size_t) (K / 32) * S);
-        if (moe_route_quant_fits(P, E, ctx->num_sms)) {
-            CK(ctx, launch_moe_route_quant(ids, T, top_k, nb1, E, 0, E, b, K, K, m.grp_off, m.inv, m.col_dst, m.tiles, m.ntiles, q, d, S,
-                                           ctx->dev_err, ctx->num_sms, ctx->stream));
-        } else {
-            CK(ctx, launch_moe_route(ids, T, top_k, nb1, E, 0, E, m.grp_off, m.col_src, m.col_dst, m.inv, m.tiles, m.ntiles, ctx->dev_err,
-                                     ctx->stream));
-            CK(ctx, launch_moe_quant_slots(b, K, K, m.col_src, m.grp_off + E, S, q, d, S, ctx->num_sms, ctx->stream));
-        }
+        CK(ctx, launch_moe_route(ids, T, top_k, nb1, E, 0, E, m.grp_off, m.col_src, m.col_dst, m.inv, m.tiles, m.ntiles, ctx->dev_err,
+                                 ctx->stream));
+        CK(ctx, launch_moe_quant_slots(b, K, K, m.col_src, m.grp_off + E, S, q, d, S, ctx->num_sms, ctx->stream));
         const cudaError_t e = launch_gemm_tc_grouped(view_of(experts), N, m.tiles, m.ntiles, q, d, S, S, m.col_dst, dst, N, ctx->dev_err,
                                                      ctx->num_sms, ctx->stream);
         if (e == cudaSuccess) return B200_OK;
@@ -740,7 +729,7 @@ b200_status b200_quantize_rows(b200_context * ctx, int type, const float * x, in
 
 b200_status b200_block_sums(b200_context * ctx, const b200_weight * w, const float * x, int32_t * sums) {
     if (!check_weight(ctx, w) || !x || !sums) return fail(ctx, B200_ERR_INVALID, "block_sums: bad arguments");
-    if (w->type != B200_TYPE_Q8_0 && w->type != B200_TYPE_Q4_K && w->type != B200_TYPE_Q6_K)
+    if (w->type != B200_TYPE_Q8_0 && w->type != B200_TYPE_Q4_K && w->type != B200_TYPE_Q5_K && w->type != B200_TYPE_Q6_K)
         return fail(ctx, B200_ERR_UNSUPPORTED, "block_sums: integer types only");
     GemvParams p = base_params(ctx, w);
     p.N = w->ne1 * w->ne2;

@@ -5,6 +5,7 @@
 // array starting on a 256-byte boundary:
 //   Q8_0 : qs  int8  [R][K]          | d    fp16 [R][K/32]
 //   Q4_K : qs  u8    [R][K/2]        | meta u8   [R][K/256][16]   (d, dmin, 12 scale bytes: the block's first 16 B)
+//   Q5_K : qs  u8    [R][K/2]        | meta u8   [R][K/256][16]  | qh u8 [R][K/8]
 //   Q6_K : ql  u8    [R][K/2]        | qh   u8   [R][K/4]        | sc int8 [R][K/256][16] | d fp16 [R][K/256]
 //   BF16 : w   bf16  [R][K]
 // The map from a GGUF byte offset to its place is a bijection (layout.cu), so set_tensor / get_tensor of any byte
@@ -21,6 +22,7 @@
 #define B200_TYPE_F16 1
 #define B200_TYPE_Q8_0 8
 #define B200_TYPE_Q4_K 12
+#define B200_TYPE_Q5_K 13
 #define B200_TYPE_Q6_K 14
 #define B200_TYPE_Q8_K 15
 #define B200_TYPE_BF16 30
@@ -38,7 +40,7 @@ struct WeightView {
     int64_t rows;   // rows of all matrices (ne1 * ne2)
     const uint8_t * f0;  // Q8_0 qs | Q4_K qs | Q6_K ql | BF16 w
     const uint8_t * f1;  // Q8_0 d  | Q4_K meta | Q6_K qh
-    const uint8_t * f2;  // Q6_K sc
+    const uint8_t * f2;  // Q6_K sc   | Q5_K qh
     const uint8_t * f3;  // Q6_K d
 };
 
@@ -47,6 +49,7 @@ __host__ __device__ inline int field_sizes(int type, int64_t K, int64_t rows, in
     switch (type) {
     case B200_TYPE_Q8_0: sz[0] = rows * K; sz[1] = rows * (K / 32) * 2; return 2;
     case B200_TYPE_Q4_K: sz[0] = rows * (K / 2); sz[1] = rows * (K / 256) * 16; return 2;
+    case B200_TYPE_Q5_K: sz[0] = rows * (K / 2); sz[1] = rows * (K / 256) * 16; sz[2] = rows * (K / 8); return 3;
     case B200_TYPE_Q6_K:
         sz[0] = rows * (K / 2); sz[1] = rows * (K / 4); sz[2] = rows * (K / 256) * 16; sz[3] = rows * (K / 256) * 2;
         return 4;

@@ -349,28 +349,30 @@ __device__ __forceinline__ void mk_rows(const MkStage & S, const Act & a, const 
     else smem_rows_lpr<T, 32>(f, K, (int) rows, a, S.w, warp, kMkConsumerWarps, store);
 }
 
-// A gate|up product's chunk (features [first, first + rows)): the gate rows into gu_s[0], the up rows into gu_s[1],
-// indexed by the feature's place in the CTA's slice. A slot holds per field the chunk's gate rows, then (from row
-// rps) its up rows.
+// A gate|up product's chunk (features [first, first + rows)): the gate sums into gu_s[0], the up sums into gu_s[1],
+// indexed by the feature's place in the CTA's slice. A slot holds per field the chunk's gate rows, then (from row rps)
+// its up rows; one reduction walks rows [0, rps + rows) (so the row code is compiled once), and rows [rows, rps) of a
+// short last chunk, which hold stale bytes, are reduced but not stored.
 template <class T, bool kForms>
 __device__ __forceinline__ void mk_rows_glu(const MkStage & S, const Act & a, const uint8_t * slot, int64_t rps, int64_t rows,
                                             int64_t first, int64_t r0, float (*gu_s)[kMkResRows]) {
     const int warp = threadIdx.x >> 5;
     const int64_t K = S.w.K;
-#pragma unroll 1
-    for (int half = 0; half < 2; half++) {  // one copy of the row code for both halves (register pressure)
-        const uint8_t * f[4];
-        const uint8_t * b = slot;
-        for (int i = 0; i < 4; i++) {
-            f[i] = b + (half ? rps * T::field_row_bytes(K, i) : 0);
-            if (i < T::kFields) b += 2 * rps * T::field_row_bytes(K, i);
-        }
-        float * out = gu_s[half] + (first - r0);
-        auto store = [&](int j, float v) { out[j] = v; };
-        if constexpr (kForms) smem_rows<T>(f, K, (int) rows, a, S.w, warp, kMkConsumerWarps, store);
-        else if (T::units_per_row(K) <= 64) smem_rows_lpr<T, 8>(f, K, (int) rows, a, S.w, warp, kMkConsumerWarps, store);
-        else smem_rows_lpr<T, 32>(f, K, (int) rows, a, S.w, warp, kMkConsumerWarps, store);
+    const uint8_t * f[4];
+    const uint8_t * b = slot;
+    for (int i = 0; i < 4; i++) {
+        f[i] = b;
+        if (i < T::kFields) b += 2 * rps * T::field_row_bytes(K, i);
     }
+    const int64_t base = first - r0;
+    auto store = [&](int j, float v) {
+        if (j < rows) gu_s[0][base + j] = v;
+        else if (j >= rps) gu_s[1][base + (j - rps)] = v;
+    };
+    const int n = (int) (rps + rows);
+    if constexpr (kForms) smem_rows<T>(f, K, n, a, S.w, warp, kMkConsumerWarps, store);
+    else if (T::units_per_row(K) <= 64) smem_rows_lpr<T, 8>(f, K, n, a, S.w, warp, kMkConsumerWarps, store);
+    else smem_rows_lpr<T, 32>(f, K, n, a, S.w, warp, kMkConsumerWarps, store);
 }
 
 template <class T>
@@ -390,9 +392,9 @@ __device__ __forceinline__ void mk_issue(const MkStage & S, uint8_t * slot, int6
 // the generic one (measured on B200, config 2 step: 495 us against 552 us with the K-quant forms compiled in), a step
 // with K-quant products the other (config 3 step: 845 us against 890 us).
 template <bool kForms>
-// One CTA per SM of kMkThreads threads: up to 224 registers a thread fit (224 x 288 <= 65536); the default bound for
-// this launch shape (168) made the K-quant row forms spill.
-__global__ void __maxnreg__(224) decoder_mk_kernel(MkParams P) {
+// One CTA per SM of kMkThreads threads: nine warps put three on one SM sub-partition, whose 16K registers then allow
+// 168 a thread.
+__global__ void __launch_bounds__(kMkThreads, 1) decoder_mk_kernel(MkParams P) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ double part[kMkConsumerWarps];
     __shared__ int give_up;

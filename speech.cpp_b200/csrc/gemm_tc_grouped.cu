@@ -12,11 +12,6 @@
 // epilogue), one barrier round trip per pair; epilogue warps
 // read a pair's sums (tcgen05.ld), scale them by d_w[row][b] * d_x[slot][b] and add them to float32 registers in
 // block order, as ggml's CPU vec_dot does. Operands come by TMA (2-D tensor maps, 128-byte swizzle, no multicast).
-// SwiGLU mode (the MoE FFN's gate|up product): a tile's 128 rows are 64 gate rows f0 .. f0 + 63 and the 64 up rows
-// F + f0 .. F + f0 + 63 of the same features (two 64-row TMA boxes), so the epilogue forms silu(gate) * up for its 64
-// features and writes them straight away as q8_0 blocks for the down product, instead of storing the 2F float32 outputs
-// for a separate SwiGLU kernel. The gate and up warps of the same features trade half their sums through shared
-// memory, so each of the eight epilogue warps forms and quantizes 8 of its chunk's 16 slots.
 // The grid is persistent (two CTAs per SM) and walks the items in a fixed order; every role of
 // a CTA derives the same item sequence from the tile list, so they need no other coordination than the stage and
 // accumulator barriers. Warp roles: 0 = TMA producer, 1 = tensor-memory allocator and MMA issuer (one thread),
@@ -45,7 +40,6 @@ struct GLayout {
     static constexpr int kDx = kGKB * kGNT * 4;  // f32 activation scales [8][32]
     static constexpr int kStage = kA + kB + kDw + kDx;
     static constexpr int kTotal = kGStages * kStage + 1024 + 1024;  // + barriers + alignment slack
-    static constexpr int kXch = 2 * 4 * 8 * 32 * 4;                   // SwiGLU mode: traded sums [h][q][8 slots][32 rows]
     static_assert(kA % 1024 == 0 && kB % 1024 == 0 && kStage % 1024 == 0, "stage regions stay 1024-aligned");
 };
 
@@ -64,11 +58,6 @@ struct GroupedParams {
     float * y;
     int64_t ldy;
     unsigned * err;
-    // SwiGLU mode: F features per expert (N = 2F rows: gate, then up); q8_0 output q_out [slots][F], dT_out [F/32][ldq]
-    int64_t F;
-    int8_t * q_out;
-    float * dT_out;
-    int64_t ldq;
 };
 
 // Token tile i: from the route kernel's list, or (dense products) 32 consecutive tokens.
@@ -80,8 +69,8 @@ __device__ __forceinline__ int4 g_tile(const GroupedParams & p, int i) {
 }
 
 // kSplit: K may be split across CTAs (dense products with few output tiles); the expert products compile without
-// that code. kSwiGLU: the gate|up mode described above.
-template <bool kSplit, bool kSwiGLU>
+// that code.
+template <bool kSplit>
 __global__ void __launch_bounds__(kGThreads, 2)
     gemm_q8_0_tc_grouped_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                                 const __grid_constant__ CUtensorMap tmDw, const __grid_constant__ CUtensorMap tmDx, GroupedParams p) {
@@ -94,10 +83,7 @@ __global__ void __launch_bounds__(kGThreads, 2)
     uint64_t * acc_full = bars + 2 * kGStages;   // [bufs] a block pair's int32 sums ready in tensor memory
     uint64_t * acc_empty = acc_full + kGBufs;    // [bufs] epilogue has read them
     uint64_t * xbar = acc_empty + kGBufs;        // [2] split-K: every epilogue warp stored its partial / ticket taken
-    uint64_t * xfull = xbar + 2;                 // SwiGLU mode: every epilogue warp has written its traded sums into xch
-    uint64_t * xempty = xbar + 3;                // SwiGLU mode: every epilogue warp has read its partner's
-    uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(xbar + 4);
-    float * xch = reinterpret_cast<float *>(smem + kGStages * L::kStage + 1024);
+    uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(xbar + 2);
     __shared__ int last_split;
     __shared__ volatile int give_up;
 
@@ -115,8 +101,6 @@ __global__ void __launch_bounds__(kGThreads, 2)
         }
         mbar_init(&xbar[0], kGEpiWarps);
         mbar_init(&xbar[1], 1);
-        mbar_init(xfull, kGEpiWarps);
-        mbar_init(xempty, kGEpiWarps);
         fence_mbar_init();
         give_up = 0;
     }
@@ -148,8 +132,7 @@ __global__ void __launch_bounds__(kGThreads, 2)
             for (int it = blockIdx.x; it < items && !give_up; it += gridDim.x) {
                 const int ot = kSplit ? it / ksplit : it, ks = kSplit ? it % ksplit : 0;
                 const int4 t = g_tile(p, ot / p.tiles_n);
-                const int arow = kSwiGLU ? (int) ((int64_t) t.x * p.N + (int64_t) (ot % p.tiles_n) * (kGM / 2))
-                                         : (int) ((int64_t) t.x * p.N + p.row0 + (int64_t) (ot % p.tiles_n) * kGM);
+                const int arow = (int) ((int64_t) t.x * p.N + p.row0 + (int64_t) (ot % p.tiles_n) * kGM);
                 const int nsub = t.z / 16;
                 const uint32_t bytes = (uint32_t) (L::kA + t.z * 256 + L::kDw + L::kDx);
                 for (int st = ks * spl; st < (ks + 1) * spl; st++, sg++) {
@@ -164,13 +147,10 @@ __global__ void __launch_bounds__(kGThreads, 2)
                     const int kbs = st * kGKB;
                     for (int jj = 0; jj < 2; jj++) {
                         tma_load_2d(base + jj * kGM * 128, &tmA, (kbs + 4 * jj) * 32, arow, &full[s]);
-                        if (kSwiGLU)  // the up rows of the same features: rows 64 .. 127 of the tile
-                            tma_load_2d(base + jj * kGM * 128 + (kGM / 2) * 128, &tmA, (kbs + 4 * jj) * 32, arow + (int) p.F, &full[s]);
                         for (int r = 0; r < nsub; r++)
                             tma_load_2d(base + L::kA + jj * kGNT * 128 + r * 16 * 128, &tmB, (kbs + 4 * jj) * 32, t.y + 16 * r, &full[s]);
                     }
                     tma_load_2d(base + L::kA + L::kB, &tmDw, kbs, arow, &full[s]);
-                    if (kSwiGLU) tma_load_2d(base + L::kA + L::kB + (kGM / 2) * kGKB * 2, &tmDw, kbs, arow + (int) p.F, &full[s]);
                     tma_load_2d(base + L::kA + L::kB + L::kDw, &tmDx, t.y, kbs, &full[s]);
                 }
             }
@@ -331,59 +311,6 @@ __global__ void __launch_bounds__(kGThreads, 2)
                     if (i < live) p.y[(int64_t) (t.y + 16 * h + i) * p.ldy + grow] = sum[i];
                 continue;
             }
-            if constexpr (kSwiGLU) {
-                // ---- SwiGLU: warp q = 0, 1 holds the gate sums of features 32 q + lane, warp q + 2 the up sums of the
-                // same features. The gate warp keeps slots 0 .. 7 of its chunk and hands slots 8 .. 15 to its partner,
-                // which hands back the up sums of slots 0 .. 7. Every warp takes part in both barriers for every tile ----
-                const bool gatew = q < 2;
-                if (xi > 0 && !mbar_wait_sleep(xempty, (xi - 1) & 1)) {
-                    if (lane == 0) atomicOr(p.err, kErrTimeout);
-                    give_up = 1;
-                    break;
-                }
-                float * xo = xch + ((h * 4 + q) * 8) * 32;                   // what this warp hands over
-                const float * xp = xch + ((h * 4 + (q ^ 2)) * 8) * 32;       // what its partner hands over
-                if (has)
-#pragma unroll
-                    for (int i = 0; i < 8; i++) {
-                        const float2 a = gatew ? acc[(8 + i) / 2] : acc[i / 2];  // constant indices: acc stays in registers
-                        xo[i * 32 + lane] = (i & 1) ? a.y : a.x;
-                    }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(xfull);
-                if (!mbar_wait_sleep(xfull, xi & 1)) {
-                    if (lane == 0) atomicOr(p.err, kErrTimeout);
-                    give_up = 1;
-                    break;
-                }
-                float other[8];
-#pragma unroll
-                for (int i = 0; i < 8; i++) other[i] = has ? xp[i * 32 + lane] : 0.0f;
-                __syncwarp();
-                if (lane == 0) mbar_arrive(xempty);
-                xi++;
-                if (has) {
-                    // q8_0 of silu(gate) * up: one 32-feature block per slot, one feature per lane, the arithmetic of
-                    // the CPU backend's quantize_row_q8_0 (the block's largest magnitude by one warp reduction: the bit
-                    // patterns of non-negative floats order as the floats do); padding slots get zeros
-                    const int i0 = gatew ? 0 : 8;
-                    const int64_t f = (int64_t) tn * (kGM / 2) + 32 * (q & 1) + lane;
-#pragma unroll
-                    for (int i = 0; i < 8; i++) {
-                        const float2 a = gatew ? acc[i / 2] : acc[(8 + i) / 2];
-                        const float mine = (i & 1) ? a.y : a.x;
-                        const float g = gatew ? mine : other[i], u = gatew ? other[i] : mine;
-                        const float v = i0 + i < live ? __fmul_rn(silu(g), u) : 0.0f;
-                        const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v))));
-                        const float d = __fdiv_rn(amax, 127.0f);
-                        const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-                        const int64_t slot = t.y + 16 * h + i0 + i;
-                        p.q_out[slot * p.F + f] = (int8_t) (int) roundf(__fmul_rn(v, id));
-                        if (lane == 0) p.dT_out[(f >> 5) * p.ldq + slot] = __half2float(__float2half_rn(d));
-                    }
-                }
-                continue;
-            }
             if (!has) continue;
             // ---- output: one weight row per lane, so each slot's store is one coalesced 128-byte line ----
             if (grow < p.N) {
@@ -432,7 +359,6 @@ cudaError_t launch_grouped(const WeightView & w, int64_t N, int64_t row0, int de
                      CU_TENSOR_MAP_SWIZZLE_NONE))
         return cudaErrorInvalidValue;
     GroupedParams p;
-    std::memset(&p, 0, sizeof p);
     p.N = N;
     p.K = K;
     p.row0 = row0;
@@ -449,61 +375,19 @@ cudaError_t launch_grouped(const WeightView & w, int64_t N, int64_t row0, int de
     p.err = err;
     static int configured = 0;
     if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_q8_0_tc_grouped_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(gemm_q8_0_tc_grouped_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
+        cudaError_t e = cudaFuncSetAttribute(gemm_q8_0_tc_grouped_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(gemm_q8_0_tc_grouped_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
         if (e != cudaSuccess) return e;
         configured = 1;
     }
     // Launched without programmatic dependent launch: CTAs started early would hold the SMs' shared memory while the
     // previous kernel drains (measured slower).
-    if (ksplit > 1) gemm_q8_0_tc_grouped_kernel<true, false><<<2 * num_sms, kGThreads, L::kTotal, st>>>(ta, tb, tdw, tdx, p);
-    else gemm_q8_0_tc_grouped_kernel<false, false><<<2 * num_sms, kGThreads, L::kTotal, st>>>(ta, tb, tdw, tdx, p);
+    if (ksplit > 1) gemm_q8_0_tc_grouped_kernel<true><<<2 * num_sms, kGThreads, L::kTotal, st>>>(ta, tb, tdw, tdx, p);
+    else gemm_q8_0_tc_grouped_kernel<false><<<2 * num_sms, kGThreads, L::kTotal, st>>>(ta, tb, tdw, tdx, p);
     return cudaGetLastError();
 }
 
 }  // namespace
-
-cudaError_t launch_gemm_tc_grouped_swiglu(const WeightView & w, int64_t F, const int4 * tiles, const int * ntiles, const int8_t * q,
-                                          const float * dT, int64_t ldP, int64_t slots, int8_t * q_out, float * dT_out, int64_t ldq,
-                                          unsigned * err, int num_sms, cudaStream_t st) {
-    using L = GLayout;
-    const int64_t K = w.K, KB = K / 32;
-    if (!gemm_tc_grouped_supported(w) || F % (kGM / 2) || ldP % 16 || slots > ldP || slots < 1 || slots % 16 || ldq < slots)
-        return cudaErrorInvalidValue;
-    CUtensorMap ta, tb, tdw, tdx;
-    // 64-row boxes: a tile's gate rows and its up rows are two loads
-    if (!make_map_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.f0, (uint64_t) K, (uint64_t) w.rows, (uint64_t) K, 128, kGM / 2,
-                     CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !make_map_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, q, (uint64_t) K, (uint64_t) slots, (uint64_t) K, 128, 16, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !make_map_2d(&tdw, CU_TENSOR_MAP_DATA_TYPE_UINT16, w.f1, (uint64_t) KB, (uint64_t) w.rows, (uint64_t) KB * 2, kGKB, kGM / 2,
-                     CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !make_map_2d(&tdx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, dT, (uint64_t) ldP, (uint64_t) KB, (uint64_t) ldP * 4, kGNT, kGKB,
-                     CU_TENSOR_MAP_SWIZZLE_NONE))
-        return cudaErrorInvalidValue;
-    GroupedParams p;
-    std::memset(&p, 0, sizeof p);
-    p.N = 2 * F;
-    p.K = K;
-    p.tiles = tiles;
-    p.ntiles = ntiles;
-    p.tiles_n = (int) (F / (kGM / 2));
-    p.ksplit = 1;
-    p.err = err;
-    p.F = F;
-    p.q_out = q_out;
-    p.dT_out = dT_out;
-    p.ldq = ldq;
-    constexpr int smem = L::kTotal + L::kXch;
-    static int configured = 0;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_q8_0_tc_grouped_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (e != cudaSuccess) return e;
-        configured = 1;
-    }
-    gemm_q8_0_tc_grouped_kernel<false, true><<<2 * num_sms, kGThreads, smem, st>>>(ta, tb, tdw, tdx, p);
-    return cudaGetLastError();
-}
 
 cudaError_t launch_gemm_tc_grouped(const WeightView & w, int64_t N, const int4 * tiles, const int * ntiles, const int8_t * q,
                                    const float * dT, int64_t ldP, int64_t slots, const int32_t * row_map, float * y, int64_t ldy,

@@ -499,6 +499,99 @@ struct TQ4_K {
     }
 };
 
+struct TQ5_K {
+    // unit = 32 bytes of qs (super-block u/4, chunk g = u%4: the low nibbles are the 32 values of sub-block 2g, the high
+    // nibbles those of sub-block 2g+1, as in Q4_K), the super-block's 32 fifth-bit bytes (bit j of byte l: value l of
+    // sub-block j) and its 16-byte meta (d, dmin, the 12 scale bytes packed as Q4_K's). Four lanes per super-block.
+    struct Unit { int4 q0; int4 q1; int4 h0; int4 h1; int4 m; };
+    static constexpr int kUnroll = 1;
+    static constexpr int kSmemUnroll = 1;
+    __device__ static int64_t units_per_row(int64_t K) { return K / 64; }
+    __device__ static int sums_per_row(int64_t K) { return (int) (2 * (K / 256)); }
+    __device__ static Unit load(const WeightView & w, int64_t row, int64_t u, bool valid) {
+        Unit r;
+        if (valid) {
+            const uint8_t * p = w.f0 + row * (w.K / 2) + u * 32;
+            const uint8_t * h = w.f2 + row * (w.K / 8) + (u / 4) * 32;
+            r.q0 = ld_stream(p);
+            r.q1 = ld_stream(p + 16);
+            r.h0 = ld_stream(h);
+            r.h1 = ld_stream(h + 16);
+            r.m = __ldg(reinterpret_cast<const int4 *>(w.f1 + (row * (w.K / 256) + u / 4) * 16));
+        } else {
+            r.q0 = r.q1 = r.h0 = r.h1 = r.m = make_int4(0, 0, 0, 0);
+        }
+        return r;
+    }
+    static constexpr int kFields = 3;  // qs [rows][K/2], meta [rows][K/256][16], qh [rows][K/8]
+    __host__ __device__ static int64_t field_row_bytes(int64_t K, int i) { return i == 0 ? K / 2 : i == 1 ? K / 16 : i == 2 ? K / 8 : 0; }
+    __device__ static Unit load_s(const uint8_t * const * f, int64_t K, int64_t row, int64_t u) {
+        Unit r;
+        const uint8_t * p = f[0] + row * (K / 2) + u * 32;
+        const uint8_t * h = f[2] + row * (K / 8) + (u / 4) * 32;
+        r.q0 = *reinterpret_cast<const int4 *>(p);
+        r.q1 = *reinterpret_cast<const int4 *>(p + 16);
+        r.h0 = *reinterpret_cast<const int4 *>(h);
+        r.h1 = *reinterpret_cast<const int4 *>(h + 16);
+        r.m = *reinterpret_cast<const int4 *>(f[1] + (row * (K / 256) + u / 4) * 16);
+        return r;
+    }
+    template <int NC>
+    __device__ static void dot(const Unit & U, int64_t u, bool valid, const Act & a, double * acc, int32_t * sums) {
+        const int ui = (int) u, K = (int) a.K;
+        const int sb = ui >> 2, g = ui & 3, s0 = 2 * g, s1 = 2 * g + 1;
+        int sc0 = 0, m0 = 0, sc1 = 0, m1 = 0;
+        if (valid) {
+            TQ4_K::scale_min_words(U.m.y, U.m.z, U.m.w, s0, sc0, m0);
+            TQ4_K::scale_min_words(U.m.y, U.m.z, U.m.w, s1, sc1, m1);
+        }
+        const float dw = __half2float(__ushort_as_half((unsigned short) (U.m.x & 0xFFFF)));
+        const float dmw = __half2float(__ushort_as_half((unsigned short) ((unsigned) U.m.x >> 16)));
+        const int w[8] = {U.q0.x, U.q0.y, U.q0.z, U.q0.w, U.q1.x, U.q1.y, U.q1.z, U.q1.w};
+        const int hb[8] = {U.h0.x, U.h0.y, U.h0.z, U.h0.w, U.h1.x, U.h1.y, U.h1.z, U.h1.w};
+#pragma unroll
+        for (int c = 0; c < NC; c++) {
+            int si = 0, sm = 0;
+            if (valid) {
+                const int8_t * xq = a.q + c * K + sb * 256;
+                const int4 * xl = reinterpret_cast<const int4 *>(xq + s0 * 32);
+                const int4 * xh = reinterpret_cast<const int4 *>(xq + s1 * 32);
+                const int4 l0 = xl[0], l1 = xl[1], h0 = xh[0], h1 = xh[1];
+                const int xlv[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+                const int xhv[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+                int il = 0, ih = 0;
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    // five-bit values of bytes 4i .. 4i+3: the nibble and the sub-block's bit of the high-bit byte
+                    const int lo = (w[i] & 0x0F0F0F0F) | (((hb[i] >> s0) & 0x01010101) << 4);
+                    const int hi = ((w[i] >> 4) & 0x0F0F0F0F) | (((hb[i] >> s1) & 0x01010101) << 4);
+                    il = __dp4a(lo, xlv[i], il);
+                    ih = __dp4a(hi, xhv[i], ih);
+                }
+                si = sc0 * il + sc1 * ih;
+                const int * bs2 = reinterpret_cast<const int *>(a.bs + c * (K / 16) + sb * 16);
+                const int p0 = bs2[s0], p1 = bs2[s1];
+                sm = m0 * ((int) (int16_t) (p0 & 0xFFFF) + (p0 >> 16)) + m1 * ((int) (int16_t) (p1 & 0xFFFF) + (p1 >> 16));
+            }
+            if (sums) {
+                si += __shfl_xor_sync(0xffffffffu, si, 1);
+                si += __shfl_xor_sync(0xffffffffu, si, 2);
+                sm += __shfl_xor_sync(0xffffffffu, sm, 1);
+                sm += __shfl_xor_sync(0xffffffffu, sm, 2);
+                if (valid && g == 0 && c == 0) {
+                    sums[2 * sb] = si;
+                    sums[2 * sb + 1] = sm;
+                }
+            }
+            if (valid && (!sums || g == 0)) {
+                const float dx = a.d[c * (K / 256) + sb];
+                acc[c] = acc_term(acc[c], __fmul_rn(dx, dw), si);
+                acc[c] = acc_term(acc[c], -__fmul_rn(dx, dmw), sm);
+            }
+        }
+    }
+};
+
 struct TQ6_K {
     // unit = a quarter of a super-block: half h = (u%4)/2, values l in [lq, lq+16), lq = (u%2)*16, all four t:
     // 16 bytes of ql (t = 0, 2), 16 bytes of ql (t = 1, 3), 16 bytes of qh, and the 16 scales.

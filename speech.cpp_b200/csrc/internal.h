@@ -93,11 +93,6 @@ cudaError_t launch_moe_combine(const float * down, const float * w, const int32_
 // Tensor-core expert products (gemm_tc_grouped.cu) and their routing/glue (moe.cu). Slots: pairs sorted by expert,
 // each expert's segment padded to a multiple of 16; at most moe_max_slots(P, E) slots and moe_max_tiles(P, E) tiles.
 bool gemm_tc_grouped_supported(const WeightView & w);
-// The gate|up product of the MoE FFN with SwiGLU and q8_0 re-quantization in the epilogue: experts [H -> 2F] (gate
-// rows 0 .. F-1, up rows F .. 2F-1); writes q8_0 of silu(gate) * up per slot: q_out [slots][F], dT_out [F/32][ldq].
-cudaError_t launch_gemm_tc_grouped_swiglu(const WeightView & w, int64_t F, const int4 * tiles, const int * ntiles, const int8_t * q,
-                                          const float * dT, int64_t ldP, int64_t slots, int8_t * q_out, float * dT_out, int64_t ldq,
-                                          unsigned * err, int num_sms, cudaStream_t st);
 cudaError_t launch_gemm_tc_grouped(const WeightView & w, int64_t N, const int4 * tiles, const int * ntiles, const int8_t * q,
                                    const float * dT, int64_t ldP, int64_t slots, const int32_t * row_map, float * y, int64_t ldy,
                                    unsigned * err, int num_sms, cudaStream_t st);
@@ -120,11 +115,6 @@ cudaError_t launch_gemm_kq_tc(b200_context * ctx, const b200_weight * w, int64_t
 void kq_release(b200_context * ctx, const void * data);
 void kq_release_all(b200_context * ctx);
 int64_t moe_max_slots(int64_t P, int64_t E);
-bool moe_route_quant_fits(int64_t P, int64_t E, int num_sms);
-cudaError_t launch_moe_route_quant(const int32_t * ids, int64_t T, int64_t top_k, int64_t nb1, int64_t E, int64_t e0, int64_t total,
-                                   const float * x, int64_t K, int64_t ldx, int32_t * grp_off, int32_t * inv, int32_t * col_dst,
-                                   int4 * tiles, int * ntiles, int8_t * q, float * dT, int64_t ldP, unsigned * err, int num_sms,
-                                   cudaStream_t st);
 int64_t moe_max_tiles(int64_t P, int64_t E);
 cudaError_t launch_moe_route(const int32_t * ids, int64_t T, int64_t top_k, int64_t nb1, int64_t E, int64_t e0, int64_t total,
                              int32_t * grp_off, int32_t * col_src, int32_t * col_dst, int32_t * inv, int4 * tiles, int * ntiles,

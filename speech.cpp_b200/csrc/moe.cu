@@ -85,178 +85,6 @@ __global__ void moe_route_kernel(const int32_t * __restrict__ ids, int64_t P, in
     }
 }
 
-// Routing and activation quantization in one kernel. Every CTA derives the same routing in shared memory — a counting
-// sort of the (token, slot) pairs by expert, pairs of one expert taking its slots in pair order, each expert's segment
-// padded to a multiple of 16 slots, token tiles of up to 32 slots — so no CTA waits for another: CTA 0 publishes the
-// tables the later kernels read (segment starts, the pair -> slot map, the tile list), and each CTA quantizes the
-// activation rows of its own range of slots to q8_0 (zeros for padding slots), bit-identical to the CPU backend's
-// quantize_row_q8_0. Pair p = t * top_k + s reads activation row t * nb1 + (nb1 == 1 ? 0 : s). Pairs of experts
-// outside [e0, e0 + E) are skipped (another shard's); ids outside [0, total) are reported. Warps count their own range
-// of pairs (the ranges in order), so the placement does not depend on timing. col_dst (optional): the pair of each
-// slot, -1 for padding (MUL_MAT_ID's output rows).
-// Shared memory: hist [W][E], cnt [E], start [E], toff [E], tok [R] (this CTA's R slots).
-template <int W>
-__global__ void __launch_bounds__(32 * W) moe_route_quant_kernel(const int32_t * __restrict__ ids, int P, int top_k, int nb1, int E,
-                                                                 int e0, int total, const float * __restrict__ x, int K, int ldx,
-                                                                 int vec, int R, int32_t * grp_off, int32_t * inv, int32_t * col_dst,
-                                                                 int4 * tiles, int * ntiles, int8_t * q, float * dT, int ldP,
-                                                                 unsigned * err) {
-    pdl_wait();
-    pdl_launch_dependents();
-    extern __shared__ int sh[];
-    int * hist = sh;                 // [W][E]: pairs of expert e in warp w's range, then warp w's next slot of e
-    int * cnt = sh + W * E;          // [E]
-    int * start = cnt + E;           // [E] first slot of expert e's segment
-    int * toff = start + E;          // [E] first tile of expert e
-    int * tok = toff + E;            // [R] activation row of this CTA's slots (-1: padding or none)
-    __shared__ int n_slots;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const bool pub = blockIdx.x == 0;
-    const int slot0 = blockIdx.x * R;
-    for (int i = threadIdx.x; i < W * E; i += 32 * W) hist[i] = 0;
-    for (int i = threadIdx.x; i < R; i += 32 * W) tok[i] = -1;
-    __syncthreads();
-    const int span = ((P + W - 1) / W + 31) & ~31;  // pairs per warp, whole 32-pair chunks
-    const int p_beg = warp * span, p_end = min(P, p_beg + span);
-    auto expert_of = [&](int p) -> int {
-        if (p >= p_end) return -1;
-        const int g = ids[p];
-        if (g < 0 || g >= total) {
-            if (pub) atomicOr(err, B200_DEVERR_EXPERT);
-            return -1;
-        }
-        const int e = g - e0;
-        return (e >= 0 && e < E) ? e : -1;
-    };
-    // a lane's experts for chunks c, c + 1, .. of its warp's range, four chunks' loads in flight at a time
-    constexpr int kB = 4;
-    for (int base = p_beg; base < p_end; base += 32 * kB) {
-        int eb[kB];
-#pragma unroll
-        for (int b = 0; b < kB; b++) eb[b] = expert_of(base + 32 * b + lane);
-#pragma unroll
-        for (int b = 0; b < kB; b++) {
-            if (base + 32 * b >= p_end) break;  // warp-uniform
-            const unsigned m = __match_any_sync(0xffffffffu, eb[b]);
-            if (eb[b] >= 0 && lane == __ffs(m) - 1) hist[warp * E + eb[b]] += __popc(m);
-            __syncwarp();  // the leaders' counts are visible to the next chunk's leaders
-        }
-    }
-    __syncthreads();
-    for (int e = threadIdx.x; e < E; e += 32 * W) {
-        int c = 0;
-        for (int w = 0; w < W; w++) c += hist[w * E + e];
-        cnt[e] = c;
-    }
-    __syncthreads();
-    if (warp == 0) {
-        int carry = 0, tcarry = 0;
-        for (int b = 0; b < E; b += 32) {
-            const int e = b + lane;
-            const int len = e < E ? (cnt[e] + 15) & ~15 : 0;
-            const int nt = (len + 31) / 32;
-            int incl = len, tincl = nt;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int a = __shfl_up_sync(0xffffffffu, incl, o);
-                const int c = __shfl_up_sync(0xffffffffu, tincl, o);
-                if (lane >= o) {
-                    incl += a;
-                    tincl += c;
-                }
-            }
-            if (e < E) {
-                start[e] = carry + incl - len;
-                toff[e] = tcarry + tincl - nt;
-            }
-            carry += __shfl_sync(0xffffffffu, incl, 31);
-            tcarry += __shfl_sync(0xffffffffu, tincl, 31);
-        }
-        if (lane == 0) {
-            n_slots = carry;
-            if (pub) {
-                grp_off[E] = carry;
-                *ntiles = tcarry;
-            }
-        }
-    }
-    __syncthreads();
-    // each warp's first slot of each expert: the segment start plus the pairs of the warps before it
-    for (int e = threadIdx.x; e < E; e += 32 * W) {
-        int run = start[e];
-        for (int w = 0; w < W; w++) {
-            const int c = hist[w * E + e];
-            hist[w * E + e] = run;
-            run += c;
-        }
-        if (pub) {
-            grp_off[e] = start[e];
-            const int len = (cnt[e] + 15) & ~15;
-            for (int o = 0, k = toff[e]; o < len; o += 32, k++)
-                tiles[k] = make_int4(e, start[e] + o, min(32, len - o), max(0, min(32, cnt[e] - o)));
-            if (col_dst)
-                for (int slot = start[e] + cnt[e]; slot < start[e] + len; slot++) col_dst[slot] = -1;
-        }
-    }
-    __syncthreads();
-    for (int base = p_beg; base < p_end; base += 32 * kB) {
-        int eb[kB];
-#pragma unroll
-        for (int b = 0; b < kB; b++) eb[b] = expert_of(base + 32 * b + lane);
-#pragma unroll
-        for (int b = 0; b < kB; b++) {
-            if (base + 32 * b >= p_end) break;  // warp-uniform
-            const int p = base + 32 * b + lane;
-            const int e = eb[b];
-            const unsigned m = __match_any_sync(0xffffffffu, e);
-            int slot = -1;
-            if (e >= 0) slot = hist[warp * E + e] + __popc(m & ((1u << lane) - 1u));
-            __syncwarp();  // every lane has read its expert's cursor before the leaders advance it
-            if (e >= 0 && lane == __ffs(m) - 1) hist[warp * E + e] += __popc(m);
-            __syncwarp();
-            if (p < p_end) {
-                if (pub) {
-                    inv[p] = slot;
-                    if (col_dst && slot >= 0) col_dst[slot] = p;
-                }
-                if (slot >= slot0 && slot < slot0 + R) {
-                    const int t = p / top_k, s = p - t * top_k;
-                    tok[slot - slot0] = t * nb1 + (nb1 == 1 ? 0 : s);
-                }
-            }
-        }
-    }
-    __syncthreads();
-    // this CTA's slots, in items of (slot, 2048 values): one warp per item, a 32-block per 8 lanes, all sixteen of a
-    // lane's loads in flight before any arithmetic
-    constexpr int U = 16;
-    const int s_end = min(n_slots, slot0 + R);
-    const int kchunks = (K + 128 * U - 1) / (128 * U);
-    for (int it = warp; it < (s_end - slot0) * kchunks; it += W) {
-        const int slot = slot0 + it / kchunks, k0 = (it % kchunks) * 128 * U;
-        const int src = tok[slot - slot0];
-        const float * xr = src >= 0 ? x + (int64_t) src * ldx : nullptr;
-        float4 v[U];
-#pragma unroll
-        for (int u = 0; u < U; u++) {
-            const int k = k0 + 128 * u + 4 * lane;
-            v[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            if (xr && k < K) v[u] = vec ? *reinterpret_cast<const float4 *>(xr + k) : make_float4(xr[k], xr[k + 1], xr[k + 2], xr[k + 3]);
-        }
-#pragma unroll
-        for (int u = 0; u < U; u++) {
-            const int k = k0 + 128 * u + 4 * lane;
-            if (k0 + 128 * u >= K) break;  // warp-uniform
-            float d;
-            const uint32_t packed = quantize_q8_0_quad(v[u], &d);
-            if (k < K) {
-                *reinterpret_cast<uint32_t *>(q + (int64_t) slot * K + k) = packed;
-                if ((lane & 7) == 0) dT[(int64_t) (k >> 5) * ldP + slot] = d;
-            }
-        }
-    }
-}
-
 // q8_0 quantization of each slot's activation row (zeros for padding), in slot order: q [slots][K], dT [K/32][ldP].
 // One warp per slot row, 128 values per step (a block per 8 lanes); bit-identical to the CPU backend's
 // quantize_row_q8_0 of the same row. vec: x and ldx allow 16-byte loads.
@@ -414,40 +242,6 @@ cudaError_t launch_moe_route(const int32_t * ids, int64_t T, int64_t top_k, int6
                              unsigned * err, cudaStream_t st) {
     return launch_pdl(moe_route_kernel, 1, 1024, (size_t) 4 * E * sizeof(int), st, ids, T * top_k, top_k, nb1, (int) E, (int) e0,
                       (int) (total > 0 ? total : E), grp_off, col_src, col_dst, inv, tiles, ntiles, err);
-}
-
-// The fused kernel's shared memory for E experts and R slots per CTA (0 when it does not fit: the separate route and
-// quantize kernels run instead).
-constexpr int kRouteWarps = 16;
-
-static size_t route_quant_smem(int64_t E, int64_t R) {
-    const size_t b = (size_t) (kRouteWarps * E + 3 * E + R) * sizeof(int);
-    return b <= (size_t) 160 * 1024 ? b : 0;
-}
-
-bool moe_route_quant_fits(int64_t P, int64_t E, int num_sms) {
-    const int64_t R = (moe_max_slots(P, E) + num_sms - 1) / num_sms;
-    return P < ((int64_t) 1 << 30) && route_quant_smem(E, R) > 0;
-}
-
-cudaError_t launch_moe_route_quant(const int32_t * ids, int64_t T, int64_t top_k, int64_t nb1, int64_t E, int64_t e0, int64_t total,
-                                   const float * x, int64_t K, int64_t ldx, int32_t * grp_off, int32_t * inv, int32_t * col_dst,
-                                   int4 * tiles, int * ntiles, int8_t * q, float * dT, int64_t ldP, unsigned * err, int num_sms,
-                                   cudaStream_t st) {
-    const int64_t P = T * top_k, S = moe_max_slots(P, E);
-    const int64_t R = (S + num_sms - 1) / num_sms;
-    const size_t smem = route_quant_smem(E, R);
-    if (!smem || K % 32 || ldP < S) return cudaErrorInvalidValue;
-    static int configured = 0;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(moe_route_quant_kernel<kRouteWarps>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
-        if (e != cudaSuccess) return e;
-        configured = 1;
-    }
-    const int vec = ((uintptr_t) x % 16 == 0 && ldx % 4 == 0 && K % 4 == 0) ? 1 : 0;
-    return launch_pdl(moe_route_quant_kernel<kRouteWarps>, (unsigned) num_sms, 32 * kRouteWarps, smem, st, ids, (int) P, (int) top_k, (int) nb1, (int) E, (int) e0,
-                      (int) (total > 0 ? total : E), x, (int) K, (int) ldx, vec, (int) R, grp_off, inv, col_dst, tiles, ntiles, q, dT,
-                      (int) ldP, err);
 }
 
 static unsigned glue_blocks(int64_t work_warps, int num_sms) {

@@ -75,7 +75,7 @@ extern "C" b200_status b200_mul_mat_id_noalloc(void * stream, const b200_weight 
     if (!experts || !experts->data || experts->ne0 <= 0 || experts->ne1 <= 0 || experts->ne2 <= 0)
         return bad("mul_mat_id_noalloc: bad experts");
     const int t = experts->type;
-    if (t != B200_TYPE_Q8_0 && t != B200_TYPE_Q4_K && t != B200_TYPE_Q6_K && t != B200_TYPE_BF16) {
+    if (t != B200_TYPE_Q8_0 && t != B200_TYPE_Q4_K && t != B200_TYPE_Q5_K && t != B200_TYPE_Q6_K && t != B200_TYPE_BF16) {
         set_thread_error("mul_mat_id_noalloc: unsupported expert type");
         return B200_ERR_UNSUPPORTED;
     }

@@ -32,6 +32,12 @@ __device__ __forceinline__ int64_t repacked_offset(int type, int64_t o, const Fi
         const int64_t b = o / 144, w = o % 144;
         return w < 16 ? fo.f[1] + b * 16 + w : fo.f[0] + b * 128 + (w - 16);
     }
+    case B200_TYPE_Q5_K: {  // d, dmin, scales (16 B) | qh (32 B) | qs (128 B)
+        const int64_t b = o / 176, w = o % 176;
+        if (w < 16) return fo.f[1] + b * 16 + w;
+        if (w < 48) return fo.f[2] + b * 32 + (w - 16);
+        return fo.f[0] + b * 128 + (w - 48);
+    }
     case B200_TYPE_Q6_K: {
         const int64_t b = o / 210, w = o % 210;
         if (w < 128) return fo.f[0] + b * 128 + w;
@@ -89,6 +95,19 @@ __global__ void get_rows_kernel(WeightView w, const int32_t * __restrict__ ids, 
             const int s = (int) ((k % 256) / 32), l = (int) (k % 32);
             const uint8_t * meta = w.f1 + (r * (K / 256) + sb) * 16;
             const int q = (w.f0[r * (K / 2) + sb * 128 + (s >> 1) * 32 + l] >> ((s & 1) * 4)) & 15;
+            int sc, m;
+            TQ4_K::scale_min(meta + 4, s, sc, m);
+            const float d = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t *>(meta)));
+            const float dmin = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t *>(meta + 2)));
+            v = __fsub_rn(__fmul_rn(__fmul_rn(d, (float) sc), (float) q), __fmul_rn(dmin, (float) m));
+            break;
+        }
+        case B200_TYPE_Q5_K: {
+            const int64_t sb = k / 256;
+            const int s = (int) ((k % 256) / 32), l = (int) (k % 32);
+            const uint8_t * meta = w.f1 + (r * (K / 256) + sb) * 16;
+            const int q = ((w.f0[r * (K / 2) + sb * 128 + (s >> 1) * 32 + l] >> ((s & 1) * 4)) & 15) |
+                          (((w.f2[r * (K / 8) + sb * 32 + l] >> s) & 1) << 4);
             int sc, m;
             TQ4_K::scale_min(meta + 4, s, sc, m);
             const float d = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t *>(meta)));
@@ -448,6 +467,7 @@ cudaError_t launch_gemv(const GemvParams & p, int nc, int grid_y, cudaStream_t s
     switch (p.w.type) {
     case B200_TYPE_Q8_0: return launch_nc<TQ8_0>(p, nc, grid_y, st, pdl, num_sms, ctas_per_sm);
     case B200_TYPE_Q4_K: return launch_nc<TQ4_K>(p, nc, grid_y, st, pdl, num_sms, ctas_per_sm);
+    case B200_TYPE_Q5_K: return launch_nc<TQ5_K>(p, nc, grid_y, st, pdl, num_sms, ctas_per_sm);
     case B200_TYPE_Q6_K: return launch_nc<TQ6_K>(p, nc, grid_y, st, pdl, num_sms, ctas_per_sm);
     case B200_TYPE_BF16: return launch_nc<TBF16>(p, nc, grid_y, st, pdl, num_sms, ctas_per_sm);
     default: return cudaErrorInvalidValue;

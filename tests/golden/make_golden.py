@@ -8,7 +8,7 @@ it in the build container (the GPU box never needs it) on seeded inputs and stor
   q8_0_*      gguf.quants.quantize(x, Q8_0) bytes for seeded N(0, 0.02) weights, the reference quantize-check's
               known-answer matrix (0.05 * sin(0.37 i), 16 x 256, checks/common/quantize-check.cpp:42-53), and edge
               rows (zeros, rounding ties, subnormal scales, large values, mixed signs);
-  deq_*       gguf.quants.dequantize(blocks, T) floats for random valid Q8_0 / Q4_K / Q6_K blocks;
+  deq_*       gguf.quants.dequantize(blocks, T) floats for random valid Q8_0 / Q4_K / Q5_K / Q6_K blocks;
   bf16_*      gguf.quants.quantize(x, BF16) / dequantize for ordinary values, ties, NaN and infinities.
 
 Run:  python tests/golden/make_golden.py
@@ -93,6 +93,18 @@ def main():
     out["bf16_y"] = quants.dequantize(out["bf16_q"], T.BF16)
 
     path = os.path.join(HERE, "gguf_blocks.npz")
+    # Q5_K: d, dmin (fp16), 12 scale bytes, 32 high-bit bytes, 128 nibble bytes (its own generator: the entries above
+    # keep their values)
+    r5 = np.random.default_rng(55)
+    d = random_half_scales(r5, nb).view(np.uint8).reshape(nb, 2)
+    dmin = random_half_scales(r5, nb).view(np.uint8).reshape(nb, 2)
+    sc = r5.integers(0, 256, size=(nb, 12), dtype=np.int64).astype(np.uint8)
+    qh = r5.integers(0, 256, size=(nb, 32), dtype=np.int64).astype(np.uint8)
+    qs = r5.integers(0, 256, size=(nb, 128), dtype=np.int64).astype(np.uint8)
+    b = np.concatenate([d, dmin, sc, qh, qs], axis=1)
+    out["deq_q5_K_blocks"] = b
+    out["deq_q5_K_y"] = quants.dequantize(b, T.Q5_K)
+
     np.savez_compressed(path, **out)
     print(f"wrote {path}: {', '.join(sorted(out))}")
 

@@ -12,8 +12,8 @@ from conftest import load_package
 
 pytestmark = pytest.mark.gpu
 
-Q8_0, Q4_K, Q6_K, Q8_K, BF16 = 8, 12, 14, 15, 30
-VEC = {Q8_0: Q8_0, Q4_K: Q8_K, Q6_K: Q8_K, BF16: BF16}
+Q8_0, Q4_K, Q5_K, Q6_K, Q8_K, BF16 = 8, 12, 13, 14, 15, 30
+VEC = {Q8_0: Q8_0, Q4_K: Q8_K, Q5_K: Q8_K, Q6_K: Q8_K, BF16: BF16}
 TOL = 1e-4
 
 
@@ -70,7 +70,7 @@ def test_activation_quantizer_bit_exact(ctx, oracle, golden, qtype, K):
         assert np.array_equal(ctx.quantize_rows(Q8_0, cuda(e)).cpu().numpy(), golden["q8_0_edge_q"])
 
 
-@pytest.mark.parametrize("qtype", [Q8_0, Q4_K, Q6_K, BF16])
+@pytest.mark.parametrize("qtype", [Q8_0, Q4_K, Q5_K, Q6_K, BF16])
 def test_weight_upload_pieces_round_trip(ctx, oracle, qtype):
     rng = np.random.default_rng(qtype)
     K, N = 512, 37
@@ -84,7 +84,7 @@ def test_weight_upload_pieces_round_trip(ctx, oracle, qtype):
     ctx.free_weight(w)
 
 
-@pytest.mark.parametrize("qtype,K", [(Q8_0, 1024), (Q8_0, 96), (Q4_K, 2048), (Q6_K, 1024), (Q6_K, 6144)])
+@pytest.mark.parametrize("qtype,K", [(Q8_0, 1024), (Q8_0, 96), (Q4_K, 2048), (Q5_K, 2048), (Q6_K, 1024), (Q6_K, 6144)])
 def test_block_sums_bit_exact(ctx, oracle, qtype, K):
     rng = np.random.default_rng(K)
     N = 19
@@ -114,6 +114,9 @@ SHAPES = [
     (BF16, 1024, 100, 1),
     (BF16, 64, 7, 4),
     (BF16, 512, 64, 24),
+    (Q5_K, 2048, 1024, 1),    # Q5_K (speech.cpp's Q5_K files): the TMA GEMV and the register GEMV
+    (Q5_K, 256, 33, 5),
+    (Q5_K, 4096, 300, 20),    # more columns than one launch stages: column chunks
     (Q6_K, 2048, 40000, 1),   # the TMA ring wraps many times per CTA
     (Q8_0, 1024, 50000, 2),
     (Q4_K, 4096, 20000, 3),
@@ -180,7 +183,7 @@ def test_mul_mat_host_path(ctx, oracle):
     ctx.free_weight(w)
 
 
-@pytest.mark.parametrize("qtype", [Q8_0, Q4_K, Q6_K, BF16])
+@pytest.mark.parametrize("qtype", [Q8_0, Q4_K, Q5_K, Q6_K, BF16])
 def test_get_rows_bit_exact(ctx, oracle, qtype):
     rng = np.random.default_rng(qtype + 1)
     K, rows = 512, 23

@@ -7,7 +7,7 @@ the reference's checks/compare/quantize_compare.py:1-11 pins against ggml.
 import numpy as np
 import pytest
 
-Q8_0, Q4_K, Q6_K, Q8_K, BF16 = 8, 12, 14, 15, 30
+Q8_0, Q4_K, Q5_K, Q6_K, Q8_K, BF16 = 8, 12, 13, 14, 15, 30
 
 
 @pytest.mark.parametrize("case", ["normal", "kat", "edge"])
@@ -19,7 +19,7 @@ def test_q8_0_quantize_matches_gguf_py(oracle, golden, case):
     assert np.array_equal(got, want)
 
 
-@pytest.mark.parametrize("qtype,name,k", [(Q8_0, "q8_0", 32), (Q4_K, "q4_K", 256), (Q6_K, "q6_K", 256)])
+@pytest.mark.parametrize("qtype,name,k", [(Q8_0, "q8_0", 32), (Q4_K, "q4_K", 256), (Q5_K, "q5_K", 256), (Q6_K, "q6_K", 256)])
 def test_dequantize_matches_gguf_py(oracle, golden, qtype, name, k):
     blocks = golden[f"deq_{name}_blocks"]
     want = golden[f"deq_{name}_y"].reshape(-1, k)
@@ -51,9 +51,9 @@ def test_fp16_conversion_matches_numpy(oracle):
     assert np.array_equal(back.view(np.uint32), h[fin].view(np.float16).astype(np.float32).view(np.uint32))
 
 
-@pytest.mark.parametrize("qtype", [Q4_K, Q6_K])
+@pytest.mark.parametrize("qtype", [Q4_K, Q5_K, Q6_K])
 def test_k_quantizers_make_valid_blocks(oracle, qtype):
-    """Our own Q4_K / Q6_K weight quantizers round-trip through gguf-py's dequantizer."""
+    """Our own Q4_K / Q5_K / Q6_K weight quantizers round-trip through gguf-py's dequantizer."""
     from gguf import GGMLQuantizationType as T
     from gguf import quants
 
@@ -61,10 +61,10 @@ def test_k_quantizers_make_valid_blocks(oracle, qtype):
     x = rng.normal(0, 0.02, size=(4, 512)).astype(np.float32)
     b = oracle.quantize(qtype, x)
     ours = oracle.dequantize(qtype, b, 512)
-    theirs = quants.dequantize(b, T.Q4_K if qtype == Q4_K else T.Q6_K).reshape(4, 512)
+    theirs = quants.dequantize(b, {Q4_K: T.Q4_K, Q5_K: T.Q5_K, Q6_K: T.Q6_K}[qtype]).reshape(4, 512)
     assert np.array_equal(ours.view(np.uint32), theirs.view(np.uint32))
     rel = np.abs(ours - x).max() / np.abs(x).max()
-    assert rel < (0.08 if qtype == Q4_K else 0.03)
+    assert rel < {Q4_K: 0.08, Q5_K: 0.04, Q6_K: 0.03}[qtype]
 
 
 def test_q8_K_quantizer_properties(oracle):
@@ -113,7 +113,7 @@ def test_mul_mat_matches_dequantized_float(oracle, qtype, K):
 def test_block_sums_are_exact(oracle):
     rng = np.random.default_rng(13)
     K = 512
-    for qtype in (Q8_0, Q4_K, Q6_K):
+    for qtype in (Q8_0, Q4_K, Q5_K, Q6_K):
         w = oracle.quantize(qtype, rng.normal(0, 0.02, size=(1, K)).astype(np.float32))
         vt = Q8_0 if qtype == Q8_0 else Q8_K
         x = oracle.quantize(vt, rng.normal(0, 1, size=(1, K)).astype(np.float32))
