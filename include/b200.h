@@ -174,6 +174,29 @@ b200_status b200_moe_ffn_ep(b200_context * ctx, const b200_weight * gate_up, con
                             int64_t n_expert_total, const float * x, const int32_t * ids, const float * w, int64_t top_k, int64_t T,
                             float * out, b200_ep_group * group);
 
+/* Asks L2 to fetch a weight's device bytes ahead of the kernels that will read it, on `stream` (a cudaStream_t of the
+ * weight's device; NULL: the context's stream). No counterpart in the reference. Returns once the request is queued;
+ * nothing waits for the data. Useful when the weight fits in L2 (126 MB on B200) and the GPU's memory would otherwise
+ * sit idle, e.g. for the next layer's experts while an expert-parallel combine crosses NVLink. */
+b200_status b200_weight_prefetch_l2(b200_context * ctx, const b200_weight * w, void * stream);
+
+/* Where a mixture-of-experts model's routed experts go on the GPUs of one node. speech.cpp keeps as many layers'
+ * experts on its one GPU as its free memory holds and computes the rest on the CPU (src/families/drama3/
+ * placement.cpp:58-74, used by src/engines/drama3-engine.cpp:51-88); here they spread over GPUs instead: rank r of
+ * `ranks` holds experts [r E/ranks, (r+1) E/ranks) of every layer (b200_moe_ffn_ep) and every rank holds the rest of
+ * the model. Given the free bytes of n_devices devices (b200_device_info), each layer's routed-expert bytes (all E
+ * experts) and the bytes every rank needs beside its experts (the other weights, caches and working memory), the plan
+ * is the fewest ranks (a power of two dividing n_expert, at most n_devices and 8) whose share fits each of the first
+ * `ranks` devices. B200_ERR_ALLOC (out->ranks 0) when no such count fits. Host only. */
+typedef struct b200_ep_plan {
+    int32_t ranks;             /* GPUs that share the experts (1: one GPU holds them all) */
+    int32_t experts_per_rank;  /* experts of each layer a rank holds */
+    uint64_t bytes_per_rank;   /* its experts plus the rest */
+    uint64_t expert_bytes;     /* the routed experts of all layers */
+} b200_ep_plan;
+b200_status b200_ep_place(int n_devices, const size_t * free_bytes, int n_layers, const uint64_t * expert_bytes, int n_expert,
+                          uint64_t rest_bytes, b200_ep_plan * out);
+
 /* GET_ROWS of a weight table (talker.cpp:131-133, decoder.cpp:319): dst [n][K] = dequantize(row ids[i]), bit for bit
  * as ggml's CPU dequantizers. An id outside [0, N * E) is skipped (its row is left untouched) and reported by
  * b200_synchronize() as B200_ERR_RANGE. */

@@ -36,6 +36,7 @@ EXPORTS = [
     "b200_decoder_set_launch", "b200_mul_mat_id_noalloc", "b200_moe_ffn",
     "b200_ep_mailbox_alloc", "b200_ep_mailbox_open", "b200_ep_mailbox_close", "b200_ep_mailbox_free", "b200_ep_create",
     "b200_ep_destroy", "b200_ep_set_timeout", "b200_moe_ffn_ep", "b200_graph_compute", "b200_graph_supports",
+    "b200_weight_prefetch_l2", "b200_ep_place",
 ]
 
 DEC_ATTN_Q, DEC_ATTN_K, DEC_ATTN_V, DEC_ATTN_O, DEC_FFN_GATE, DEC_FFN_UP, DEC_FFN_DOWN = range(7)
@@ -78,6 +79,26 @@ class Tensor(ctypes.Structure):
 I32 = 26
 (OP_NONE, OP_GET_ROWS, OP_MUL_MAT, OP_RMS_NORM, OP_MUL, OP_ADD, OP_ROPE, OP_SET_ROWS, OP_CPY, OP_CONT, OP_SOFT_MAX,
  OP_FLASH_ATTN, OP_SWIGLU, OP_ARGMAX, OP_SCALE) = range(15)
+
+
+class EpPlan(ctypes.Structure):
+    """struct b200_ep_plan (include/b200.h)."""
+
+    _fields_ = [("ranks", ctypes.c_int32), ("experts_per_rank", ctypes.c_int32), ("bytes_per_rank", ctypes.c_uint64),
+                ("expert_bytes", ctypes.c_uint64)]
+
+
+def ep_place(free_bytes, expert_bytes, n_expert, rest_bytes):
+    """b200_ep_place: the fewest GPUs (a power of two) whose share of the experts fits beside the rest. Returns the
+    EpPlan, or raises B200Error (ALLOC) when no count fits."""
+    L = lib()
+    fb = (ctypes.c_size_t * len(free_bytes))(*free_bytes)
+    eb = (ctypes.c_uint64 * len(expert_bytes))(*expert_bytes)
+    plan = EpPlan()
+    s = L.b200_ep_place(len(free_bytes), fb, len(expert_bytes), eb, n_expert, rest_bytes, ctypes.byref(plan))
+    if s != OK:
+        raise B200Error(s, f"{plan.expert_bytes} bytes of experts plus {rest_bytes} per GPU fit no count of the {len(free_bytes)} GPUs")
+    return plan
 
 
 class DecoderShape(ctypes.Structure):
@@ -158,6 +179,9 @@ def lib():
         "b200_ep_set_timeout": (i32, [vp, ctypes.c_uint64]),
         "b200_moe_ffn_ep": (i32, [vp, W, W, i64, i64, vp, vp, vp, i64, i64, vp, vp]),
         "b200_graph_compute": (i32, [vp, ctypes.POINTER(Tensor), i64]),
+        "b200_weight_prefetch_l2": (i32, [vp, W, vp]),
+        "b200_ep_place": (i32, [ctypes.c_int, ctypes.POINTER(sz), ctypes.c_int, ctypes.POINTER(ctypes.c_uint64), ctypes.c_int,
+                                ctypes.c_uint64, ctypes.POINTER(EpPlan)]),
         "b200_graph_supports": (i32, [ctypes.POINTER(Tensor), i64, i64]),
     }
     for name, (res, args) in sig.items():
@@ -339,6 +363,10 @@ class Context:
                                           _ptr(ids), _ptr(w), top_k, T, _ptr(out), group))
         self._sync_out()
         return out
+
+    def prefetch_l2(self, w, stream=None):
+        """b200_weight_prefetch_l2: queue an L2 prefetch of the weight on `stream` (a torch stream; None: the context's)."""
+        self.check(self.L.b200_weight_prefetch_l2(self.h, ctypes.byref(w), ctypes.c_void_p(stream.cuda_stream) if stream is not None else None))
 
     def get_rows(self, table, ids, out=None):
         import torch

@@ -712,6 +712,14 @@ b200_status b200_moe_ffn_ep(b200_context * ctx, const b200_weight * gate_up, con
     return moe_ffn_tc(ctx, gate_up, down, expert0, n_expert_total, x, ids, w, top_k, T, out, group);
 }
 
+b200_status b200_weight_prefetch_l2(b200_context * ctx, const b200_weight * w, void * stream) {
+    if (!check_weight(ctx, w)) return fail(ctx, B200_ERR_INVALID, "weight_prefetch_l2: bad weight");
+    const int64_t base = (int64_t) (((uintptr_t) w->data + 15) & ~(uintptr_t) 15) - (int64_t) (uintptr_t) w->data;
+    if ((size_t) base >= w->dbytes) return B200_OK;
+    CK(ctx, launch_prefetch_l2((const uint8_t *) w->data + base, w->dbytes - (size_t) base, stream ? (cudaStream_t) stream : ctx->stream));
+    return B200_OK;
+}
+
 b200_status b200_get_rows(b200_context * ctx, const b200_weight * table, const int32_t * ids, int64_t n, float * dst) {
     if (!check_weight(ctx, table)) return fail(ctx, B200_ERR_INVALID, "get_rows: bad table");
     if (n < 0 || (n > 0 && (!ids || !dst))) return fail(ctx, B200_ERR_INVALID, "get_rows: bad arguments");

@@ -260,6 +260,16 @@ __device__ __forceinline__ float silu_exact(float x) {
 // way, so the result does not depend on how lanes split the blocks.
 __device__ __forceinline__ double acc_term(double acc, float scale, int sumi) { return fma((double) scale, (double) sumi, acc); }
 
+// The mean of K squares summed in double, rounded once to float32: sum / K, where a power-of-two K scales exactly by
+// 2^-log2(K) (a multiplication gives the same double as the division, without its latency on the decode step's chain).
+__device__ __forceinline__ float mean_rounded(double sum, int64_t K) {
+    if ((K & (K - 1)) == 0) {
+        const int lg = 63 - __clzll((unsigned long long) K);
+        return __double2float_rn(sum * __longlong_as_double((long long) (1023 - lg) << 52));
+    }
+    return __double2float_rn(sum / (double) K);
+}
+
 __device__ __forceinline__ double warp_sum_d(double v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

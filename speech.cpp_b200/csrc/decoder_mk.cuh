@@ -220,9 +220,9 @@ __device__ __forceinline__ int mk_stage_input(const MkStage & S, const Act & a, 
             sq = warp_sum_d(sq);
             if (lane == 0) part[warp] = sq;
             mk_sync();
-            double t = 0.0;
-            for (int w = 0; w < kMkConsumerWarps; w++) t += part[w];
-            rms = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__double2float_rn(t / (double) K), S.eps)));
+            static_assert(kMkConsumerWarps == 8, "the warps' partial sums are added as a tree of eight");
+            const double t = ((part[0] + part[1]) + (part[2] + part[3])) + ((part[4] + part[5]) + (part[6] + part[7]));
+            rms = __fdiv_rn(1.0f, sqrtf(__fadd_rn(mean_rounded(t, K), S.eps)));
         }
 #pragma unroll
         for (int i = 0; i < kMax; i++) {
@@ -280,9 +280,9 @@ __device__ __forceinline__ int mk_stage_input(const MkStage & S, const Act & a, 
             sq = warp_sum_d(sq);
             if (lane == 0) part[warp] = sq;
             mk_sync();
-            double t = 0.0;
-            for (int w = 0; w < kMkConsumerWarps; w++) t += part[w];
-            rms = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__double2float_rn(t / (double) K), S.eps)));
+            static_assert(kMkConsumerWarps == 8, "the warps' partial sums are added as a tree of eight");
+            const double t = ((part[0] + part[1]) + (part[2] + part[3])) + ((part[4] + part[5]) + (part[6] + part[7]));
+            rms = __fdiv_rn(1.0f, sqrtf(__fadd_rn(mean_rounded(t, K), S.eps)));
         }
 #pragma unroll
         for (int i = 0; i < kMax; i++) {

@@ -152,7 +152,7 @@ __device__ __forceinline__ void stage_one(const GemvParams & p, const Act & a, i
         if (warp == 0) {
             double t = lane < nwarps ? part[lane] : 0.0;
             t = warp_sum_d(t);
-            if (lane == 0) rms = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__double2float_rn(t / (double) K), p.eps)));
+            if (lane == 0) rms = __fdiv_rn(1.0f, sqrtf(__fadd_rn(mean_rounded(t, K), p.eps)));
         }
         sync_threads(nthr);
     }
@@ -237,7 +237,7 @@ __device__ void stage_activations(const GemvParams & p, const Act & a, int kind,
             for (int c = 0; c < NC; c++) {
                 double s = lane < nwarps ? part[c][lane] : 0.0;
                 s = warp_sum_d(s);
-                if (lane == 0) rms[c] = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__double2float_rn(s / (double) K), p.eps)));
+                if (lane == 0) rms[c] = __fdiv_rn(1.0f, sqrtf(__fadd_rn(mean_rounded(s, K), p.eps)));
             }
         }
         sync_threads(nthr);

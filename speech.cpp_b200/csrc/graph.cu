@@ -95,7 +95,7 @@ __global__ void k_rms_norm(TView x, TView y, float eps) {
             sq = fma(v, v, sq);
         }
         sq = warp_sum_d(sq);
-        const float scale = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__double2float_rn(sq / (double) x.ne[0]), eps)));
+        const float scale = __fdiv_rn(1.0f, sqrtf(__fadd_rn(mean_rounded(sq, x.ne[0]), eps)));
         for (int64_t i0 = lane; i0 < x.ne[0]; i0 += 32) st(y, i0, i1, i2, i3, __fmul_rn(ld(x, i0, i1, i2, i3), scale));
     }
 }

@@ -71,6 +71,7 @@ cudaError_t launch_gemv(const GemvParams & p, int nc, int grid_y, cudaStream_t s
 int gemv_max_columns(int wtype, int64_t K);  // largest NC whose staging fits in shared memory
 cudaError_t launch_repack(int type, const b200_weight * w, const uint8_t * src, int64_t off0, int64_t n, bool to_device_layout,
                           uint8_t * gather_dst, cudaStream_t st);
+cudaError_t launch_prefetch_l2(const void * base, size_t bytes, cudaStream_t st);
 cudaError_t launch_get_rows(const WeightView & w, const int32_t * ids, int64_t n, float * dst, unsigned * err, cudaStream_t st);
 // Activation quantization: gguf != null writes GGUF blocks there; else the internal layout (q, d, bs).
 cudaError_t launch_quantize(int kind, const float * x, int64_t K, int64_t M, uint8_t * gguf, int8_t * q, float * d, int16_t * bs,

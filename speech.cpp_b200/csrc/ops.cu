@@ -71,6 +71,28 @@ cudaError_t launch_repack(int type, const b200_weight * w, const uint8_t * src, 
 }
 
 // ------------------------------------------------------------------------------------------------------------------
+// L2 prefetch of a byte range (a weight that the next kernels will read): each thread asks L2 for one 64 KB piece with
+// one bulk prefetch and the kernel ends; nothing waits for the data.
+// ------------------------------------------------------------------------------------------------------------------
+__global__ void prefetch_l2_kernel(const uint8_t * base, size_t bytes) {
+    constexpr size_t kPiece = 64 * 1024;
+    const size_t n = (bytes + kPiece - 1) / kPiece;
+    for (size_t i = blockIdx.x * (size_t) blockDim.x + threadIdx.x; i < n; i += (size_t) gridDim.x * blockDim.x) {
+        const size_t off = i * kPiece;
+        const uint32_t sz = (uint32_t) ((bytes - off < kPiece ? bytes - off : kPiece) & ~(size_t) 15);
+        if (sz) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base + off), "r"(sz) : "memory");
+    }
+}
+
+cudaError_t launch_prefetch_l2(const void * base, size_t bytes, cudaStream_t st) {
+    if (!bytes) return cudaSuccess;
+    const size_t pieces = (bytes + 65535) / 65536;
+    const unsigned blocks = (unsigned) ((pieces + 255) / 256 < 1024 ? (pieces + 255) / 256 : 1024);
+    prefetch_l2_kernel<<<blocks, 256, 0, st>>>((const uint8_t *) base, bytes);
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------------------------------------------
 // GET_ROWS
 // ------------------------------------------------------------------------------------------------------------------
 __global__ void get_rows_kernel(WeightView w, const int32_t * __restrict__ ids, float * __restrict__ dst, unsigned * err) {

@@ -80,16 +80,23 @@ class PeerCombine:
 
 class ExpertParallelMoe:
     """One rank's share of an MoE FFN stack: per layer (gate_up, down) expert weights of experts
-    [expert0, expert0 + n_local) of n_expert. `ffn(ctx-like)` is any object with moe_ffn(gate_up, down, x, ids, w,
-    expert0=, n_expert_total=, out=) (a speech.cpp_b200 Context); `group` a torch.distributed process group or None."""
+    [expert0, expert0 + n_local) of n_expert. `ffn` is any object with moe_ffn(gate_up, down, x, ids, w, expert0=,
+    n_expert_total=, out=) and prefetch_l2(weight, stream) (a speech.cpp_b200 Context); `group` a torch.distributed
+    process group or None.
 
-    def __init__(self, ffn, layers, expert0: int, n_expert: int, group=None, peer: PeerCombine | None = None):
+    prefetch: ask L2 for layer l + 1's experts on a side stream once layer l's kernels are queued, so they could arrive
+    while layer l's partial sums cross NVLink. Off unless asked for: on one GPU running one rank's share of config 5
+    (no NVLink wait to hide it in) it slowed a layer from 57 to 148 us, and it has not been measured on eight GPUs."""
+
+    def __init__(self, ffn, layers, expert0: int, n_expert: int, group=None, peer: PeerCombine | None = None, prefetch=False):
         self.ffn = ffn
         self.layers = list(layers)
         self.expert0 = expert0
         self.n_expert = n_expert
         self.group = group
         self.peer = peer  # when set: the combine and the all-reduce are one kernel over peer memory
+        self.prefetch = bool(prefetch) and hasattr(ffn, "prefetch_l2")
+        self._side = None
 
     def _all_reduce(self, t):
         if self.group is None:
@@ -99,17 +106,37 @@ class ExpertParallelMoe:
         if dist.get_world_size(self.group) > 1:
             dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
 
+    def _prefetch(self, l: int):
+        """Layer l's experts into L2 on the side stream, after the work queued so far on the current stream."""
+        import torch
+
+        if self._side is None:
+            self._side = torch.cuda.Stream()
+        self._side.wait_stream(torch.cuda.current_stream())
+        gu, dn = self.layers[l]
+        self.ffn.prefetch_l2(gu, self._side)
+        self.ffn.prefetch_l2(dn, self._side)
+
     def layer(self, l: int, x, ids, w, out):
         """out = the full weighted sum of layer l's routed experts for tokens x (every rank gets the same out)."""
         gu, dn = self.layers[l]
         if self.peer is not None:
-            return self.ffn.moe_ffn_ep(gu, dn, x, ids, w, self.expert0, self.n_expert, self.peer.handle, out=out)
+            self.ffn.moe_ffn_ep(gu, dn, x, ids, w, self.expert0, self.n_expert, self.peer.handle, out=out)
+            if self.prefetch and l + 1 < len(self.layers):
+                self._prefetch(l + 1)
+            return out
         self.ffn.moe_ffn(gu, dn, x, ids, w, expert0=self.expert0, n_expert_total=self.n_expert, out=out)
+        if self.prefetch and l + 1 < len(self.layers):
+            self._prefetch(l + 1)
         self._all_reduce(out)
         return out
 
     def step(self, xs, ids, w):
         """Runs every layer, layer l reading xs[l] and writing xs[l + 1]; ids [L, T, k], w [L, T, k]."""
+        import torch
+
         for l in range(len(self.layers)):
             self.layer(l, xs[l], ids[l], w[l], xs[l + 1])
+        if self._side is not None:
+            torch.cuda.current_stream().wait_stream(self._side)  # the side stream joins back (graph capture needs it)
         return xs[len(self.layers)]

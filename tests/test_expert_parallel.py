@@ -127,3 +127,24 @@ def test_two_gloo_ranks_match_one(oracle):
     for r in range(2):
         assert np.allclose(outs[r], want, rtol=1e-5, atol=1e-6 * np.abs(want).max())
     assert np.array_equal(outs[0], outs[1])
+
+
+def test_ep_place_fewest_ranks_that_fit():
+    """b200_ep_place (host code, no GPU): config 5's 48 layers of 128 Q8_0 experts (641,728,512 B a layer) with 2 GB
+    of the rest on each GPU: one B200 (about 178 GiB free) holds them all; GPUs of 20 GiB need 2 ranks; of 6 GiB, 8;
+    of 3 GiB, none. Uneven free memory: the first `ranks` devices must each fit."""
+    from conftest import load_package
+
+    b200 = load_package()
+    layers = [641_728_512] * 48
+    GiB = 1 << 30
+    p = b200.ep_place([178 * GiB] * 8, layers, 128, 2 * GiB)
+    assert (p.ranks, p.experts_per_rank) == (1, 128) and p.expert_bytes == 48 * 641_728_512
+    assert b200.ep_place([20 * GiB] * 8, layers, 128, 2 * GiB).ranks == 2
+    p = b200.ep_place([6 * GiB] * 8, layers, 128, 2 * GiB)
+    assert (p.ranks, p.experts_per_rank) == (8, 16) and p.bytes_per_rank == 2 * GiB + 48 * (641_728_512 // 8)
+    assert b200.ep_place([20 * GiB, 10 * GiB, 20 * GiB, 20 * GiB], layers, 128, 2 * GiB).ranks == 4  # device 1 is short
+    with pytest.raises(b200.B200Error):
+        b200.ep_place([3 * GiB] * 8, layers, 128, 2 * GiB)
+    with pytest.raises(b200.B200Error):
+        b200.ep_place([6 * GiB] * 4, layers, 128, 2 * GiB)  # would need 8 ranks, only 4 devices
