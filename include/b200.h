@@ -16,9 +16,12 @@
  *    host memory and copy inside the call.
  *  - Calls are asynchronous on the context's stream unless they say otherwise. b200_synchronize() waits and reports
  *    errors found on the device (an id out of range, a bounded wait that gave up).
- *  - Results are computed as ggml's CPU backend computes them: each activation row is quantized to the weight type's
- *    vec_dot type (q8_0 for Q8_0, q8_K for Q4_K / Q6_K, bf16 for BF16) bit-identically, each (sub-)block's int32 sum
- *    is exact, and sums are scaled and accumulated in float32.
+ *  - Results follow ggml's CPU backend: each activation row is quantized to the weight type's vec_dot type (q8_0 for
+ *    Q8_0, q8_K for Q4_K / Q5_K / Q6_K, bf16 for BF16) bit-identically and each (sub-)block's int32 sum is exact. The
+ *    float step is defined without an order: each block's term fl32(d_w d_x) * sum is added exactly (in double) and
+ *    the total is rounded once to float32. Products of up to 31 activation rows and the decode step compute exactly
+ *    that; the tensor-core products (Q8_0 / Q4_K / Q6_K weights, 32 or more rows) accumulate the same terms in float32,
+ *    within 1e-4 of sum |w x|.
  */
 #ifndef SPEECH_B200_H
 #define SPEECH_B200_H
@@ -312,7 +315,10 @@ typedef enum b200_op {
                                 H_kv] F16, mask src3 [n_kv, >= n_q] F16 (optional); dst [D, H, n_q] F32; params[0] = scale */
     B200_OP_SWIGLU = 12,     /* ggml_swiglu_split: silu(src0) * src1 */
     B200_OP_ARGMAX = 13,     /* dst I32 [rows]: index of the first largest value of each row of src0 */
-    B200_OP_SCALE = 14       /* src0 * params[0] + params[1] (float bits) */
+    B200_OP_SCALE = 14,      /* src0 * params[0] + params[1] (float bits) */
+    B200_OP_FILL = 15,       /* every element of dst (a view, written in place; src0 optional, the same tensor) =
+                                params[0] (float bits): ggml_fill_inplace of the KV cache's tail */
+    B200_OP_CONCAT = 16      /* src0 and src1 joined along dimension params[0] (the others equal) */
 } b200_op;
 
 typedef struct b200_tensor {

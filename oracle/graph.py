@@ -4,8 +4,8 @@ b200_graph_compute; the product path never imports it).
 ggml defines these ops in its own source, which is absent from the reference checkout; what follows restates their
 documented behaviour as Qwen3Decoder::layers / outputs uses them (src/common/qwen3-decoder.cpp:350-438) — ggml_rms_norm,
 ggml_mul / ggml_add with the second operand repeated, ggml_rope_ext in NEOX mode, ggml_set_rows into the F16 KV cache,
-ggml_soft_max_ext with a mask, ggml_flash_attn_ext, ggml_swiglu_split, ggml_argmax, ggml_mul_mat of F16 / F32
-matrices — with the order-dependent reductions defined order-free, as the device computes them: sums and exponentials
+ggml_soft_max_ext with a mask, ggml_flash_attn_ext, ggml_swiglu_split, ggml_argmax, ggml_concat (the talker's code
+predictor input, src/families/qwen3-tts/talker.cpp:55), ggml_mul_mat of F16 / F32 matrices — with the order-dependent reductions defined order-free, as the device computes them: sums and exponentials
 in double, rounded once to float32.
 
 Arrays are numpy arrays in torch order: shape (ne3, ne2, ne1, ne0) of the ggml tensor, innermost dimension last.
@@ -37,6 +37,12 @@ def mul(a, b):
 
 def add(a, b):
     return (np.asarray(a, F32) + repeat_to(b, np.shape(a)).astype(F32)).astype(F32)
+
+
+def concat(a, b, dim):
+    """ggml_concat along ggml dimension `dim` (0 = innermost = the last numpy axis)."""
+    a, b = np.asarray(a), np.asarray(b)
+    return np.concatenate([a, b], axis=a.ndim - 1 - dim)
 
 
 def silu(x):

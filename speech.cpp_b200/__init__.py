@@ -78,7 +78,7 @@ class Tensor(ctypes.Structure):
 
 I32 = 26
 (OP_NONE, OP_GET_ROWS, OP_MUL_MAT, OP_RMS_NORM, OP_MUL, OP_ADD, OP_ROPE, OP_SET_ROWS, OP_CPY, OP_CONT, OP_SOFT_MAX,
- OP_FLASH_ATTN, OP_SWIGLU, OP_ARGMAX, OP_SCALE) = range(15)
+ OP_FLASH_ATTN, OP_SWIGLU, OP_ARGMAX, OP_SCALE, OP_FILL, OP_CONCAT) = range(17)
 
 
 class EpPlan(ctypes.Structure):
@@ -550,3 +550,13 @@ class Decoder:
 
 def device_count():
     return lib().b200_device_count()
+
+
+def device_info(device: int):
+    """b200_device_info: (name, free bytes, total bytes) of one device, as ggml_backend_dev_memory reports them."""
+    name = ctypes.create_string_buffer(256)
+    free, total = ctypes.c_size_t(), ctypes.c_size_t()
+    s = lib().b200_device_info(device, name, 256, ctypes.byref(free), ctypes.byref(total))
+    if s != OK:
+        raise B200Error(s, f"device_info({device})")
+    return name.value.decode(), free.value, total.value

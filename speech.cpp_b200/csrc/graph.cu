@@ -1,5 +1,6 @@
 // graph.cu — the backend's graph_compute: the ops of a Qwen3 decoder graph besides the quantized products
-// (Qwen3Decoder::layers / outputs, src/common/qwen3-decoder.cpp:350-438), over ggml-shaped tensor records
+// (Qwen3Decoder::layers / outputs, src/common/qwen3-decoder.cpp:350-438; the cache's FILL at :320-321 and the talker's
+// CONCAT, src/families/qwen3-tts/talker.cpp:55, 174), over ggml-shaped tensor records
 // (b200_graph_compute, include/b200.h).
 //
 // Tensors are strided views: element [i0, i1, i2, i3] of a record lives at data + i0 nb0 + i1 nb1 + i2 nb2 + i3 nb3,
@@ -62,12 +63,17 @@ __device__ __forceinline__ int64_t n_elems(const TView & t) { return t.ne[0] * t
 
 // ---- element-wise ----
 
-// kind 0: ADD, 1: MUL (src1 repeated), 2: SWIGLU (silu(a) * b, same shapes), 3: SCALE (a * s + b), 4: copy / convert
+// kind 0: ADD, 1: MUL (src1 repeated), 2: SWIGLU (silu(a) * b, same shapes), 3: SCALE (a * s + b), 4: copy / convert,
+// 5: FILL (every element s; a is not read)
 __global__ void k_elementwise(TView a, TView b, TView d, int kind, float s, float bias) {
     const int64_t n = n_elems(d);
     for (int64_t i = blockIdx.x * (int64_t) blockDim.x + threadIdx.x; i < n; i += (int64_t) gridDim.x * blockDim.x) {
         int64_t i0, i1, i2, i3;
         unflat(i, d.ne, i0, i1, i2, i3);
+        if (kind == 5) {
+            st(d, i0, i1, i2, i3, s);
+            continue;
+        }
         const float x = ld(a, i0, i1, i2, i3);
         float y;
         switch (kind) {
@@ -78,6 +84,25 @@ __global__ void k_elementwise(TView a, TView b, TView d, int kind, float s, floa
         default: y = x; break;
         }
         st(d, i0, i1, i2, i3, y);
+    }
+}
+
+// CONCAT along dimension `dim`: d's index there below a.ne[dim] reads a, the rest read b shifted down by a.ne[dim].
+__global__ void k_concat(TView a, TView b, TView d, int dim) {
+    const int64_t n = n_elems(d);
+    for (int64_t i = blockIdx.x * (int64_t) blockDim.x + threadIdx.x; i < n; i += (int64_t) gridDim.x * blockDim.x) {
+        int64_t c[4];
+        unflat(i, d.ne, c[0], c[1], c[2], c[3]);
+        const int64_t k = c[dim];
+        float v;
+        if (k < a.ne[dim]) {
+            v = ld(a, c[0], c[1], c[2], c[3]);
+        } else {
+            c[dim] = k - a.ne[dim];
+            v = ld(b, c[0], c[1], c[2], c[3]);
+            c[dim] = k;
+        }
+        st(d, c[0], c[1], c[2], c[3], v);
     }
 }
 
@@ -382,6 +407,15 @@ bool supports(const b200_tensor * ts, int64_t n, int64_t i) {
     }
     case B200_OP_ARGMAX:
         return a && plain_float(*a) && t.type == B200_TYPE_I32 && t.nb[0] == 4 && t.ne[0] == a->ne[1] * a->ne[2] * a->ne[3];
+    case B200_OP_FILL:
+        return plain_float(t) && (!a || same_shape(*a, t));
+    case B200_OP_CONCAT: {
+        const int dim = t.params[0];
+        if (!a || !b || !plain_float(*a) || !plain_float(*b) || !plain_float(t) || dim < 0 || dim > 3) return false;
+        for (int d = 0; d < 4; d++)
+            if (d == dim ? t.ne[d] != a->ne[d] + b->ne[d] : (a->ne[d] != t.ne[d] || b->ne[d] != t.ne[d])) return false;
+        return true;
+    }
     default: return false;
     }
 }
@@ -443,6 +477,12 @@ b200_status b200_graph_compute(b200_context * ctx, const b200_tensor * ts, int64
             break;
         case B200_OP_CPY:
             k_elementwise<<<grid_for(ne, 256, sms), 256, 0, st>>>(view(*a), none, view(*b), 4, 0.0f, 0.0f);
+            break;
+        case B200_OP_FILL:
+            k_elementwise<<<grid_for(ne, 256, sms), 256, 0, st>>>(none, none, d, 5, fparam(t, 0), 0.0f);
+            break;
+        case B200_OP_CONCAT:
+            k_concat<<<grid_for(ne, 256, sms), 256, 0, st>>>(view(*a), view(*b), d, t.params[0]);
             break;
         case B200_OP_ROPE:
             k_rope_neox<<<grid_for(ne, 256, sms), 256, 0, st>>>(view(*a), (const int32_t *) b->data, d, t.params[0], (double) fparam(t, 2));

@@ -28,6 +28,22 @@ def expert_shard(n_expert: int, world: int, rank: int) -> tuple[int, int]:
     return rank * n, n
 
 
+def place_experts(expert_bytes, n_expert: int, rest_bytes: int, free_bytes=None):
+    """How many of this node's GPUs the routed experts need: the counterpart of the reference's place_experts
+    (src/engines/drama3-engine.cpp:51-88 with expert_layers_on_device, src/families/drama3/placement.cpp:58-74), which
+    keeps the layers whose experts fit on its one GPU and computes the rest on the CPU. Here every layer's experts stay
+    on GPUs: b200_ep_place returns the fewest ranks (a power of two dividing n_expert) whose expert shard fits each
+    GPU's free memory beside `rest_bytes` (the replicated weights, caches and working memory). `expert_bytes` holds
+    each layer's routed-expert bytes; `free_bytes` defaults to every visible device's free memory (b200_device_info).
+    Raises B200Error (ALLOC) when the experts fit no count of the GPUs, as the reference raises OutOfMemory when the
+    rest of the model does not fit."""
+    from . import device_count, device_info, ep_place
+
+    if free_bytes is None:
+        free_bytes = [device_info(d)[1] for d in range(device_count())]
+    return ep_place(list(free_bytes), list(expert_bytes), n_expert, rest_bytes)
+
+
 class PeerCombine:
     """The mailboxes of an expert-parallel group (b200_ep_*): each rank allocates one, the 64-byte CUDA IPC handles
     are exchanged over the torch.distributed group, each rank maps the others' and creates the group. Then

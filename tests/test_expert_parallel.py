@@ -148,3 +148,9 @@ def test_ep_place_fewest_ranks_that_fit():
         b200.ep_place([3 * GiB] * 8, layers, 128, 2 * GiB)
     with pytest.raises(b200.B200Error):
         b200.ep_place([6 * GiB] * 4, layers, 128, 2 * GiB)  # would need 8 ranks, only 4 devices
+    import importlib
+
+    ep = importlib.import_module(b200.__name__ + ".expert_parallel")
+    # the facade: given free memory, as place_experts reads it from every device when none is given
+    p = ep.place_experts(layers, 128, 2 * GiB, free_bytes=[40 * GiB] * 2)
+    assert (p.ranks, p.experts_per_rank) == (1, 128)

@@ -71,6 +71,9 @@ def test_elementwise_and_norm_ops(b200, ctx):
     w = rng.normal(1, 0.1, size=128).astype(F32)
     y = rng.normal(0, 1, size=(5, 16, 128)).astype(F32)
     outs = {k: torch.empty((5, 16, 128), device="cuda") for k in ("norm", "mul", "add", "swiglu", "scale")}
+    outs["fill"] = cu(x)                                      # rows 2..4 set to 0 in place (a view), rows 0..1 kept
+    outs["concat"] = torch.empty((5, 16, 256), device="cuda")  # along dimension 0
+    outs["concat1"] = torch.empty((5, 32, 128), device="cuda")  # along dimension 1
 
     def build(g):
         X, W, Y = g.add(t=cu(x)), g.add(t=cu(w)), g.add(t=cu(y))
@@ -79,6 +82,9 @@ def test_elementwise_and_norm_ops(b200, ctx):
         g.add(b200.OP_ADD, outs["add"], src=[X, Y])
         g.add(b200.OP_SWIGLU, outs["swiglu"], src=[X, Y])
         g.add(b200.OP_SCALE, outs["scale"], src=[X], params=[g.fbits(0.125), g.fbits(0.5)])
+        g.add(b200.OP_FILL, outs["fill"][2:], params=[g.fbits(0.0)])
+        g.add(b200.OP_CONCAT, outs["concat"], src=[X, Y], params=[0])
+        g.add(b200.OP_CONCAT, outs["concat1"], src=[X, Y], params=[1])
         return outs
 
     got = {k: v.cpu().numpy() for k, v in run(b200, ctx, build).items()}
@@ -88,6 +94,8 @@ def test_elementwise_and_norm_ops(b200, ctx):
     assert np.array_equal(got["add"], og.add(x, y))
     close_and_mostly_equal(got["swiglu"], og.swiglu(x, y))
     assert np.array_equal(got["scale"], (x * F32(0.125) + F32(0.5)).astype(F32))
+    assert np.array_equal(got["fill"][:2], x[:2]) and not got["fill"][2:].any()
+    assert np.array_equal(got["concat"], og.concat(x, y, 0)) and np.array_equal(got["concat1"], og.concat(x, y, 1))
 
 
 def test_rope_cache_rows_softmax_attention_products(b200, ctx):
@@ -152,7 +160,10 @@ def test_rope_cache_rows_softmax_attention_products(b200, ctx):
 
 def test_qwen3_decoder_layer_with_kv_cache(b200, ctx, oracle):
     """One decoder layer of the Qwen3-TTS 0.6B talker's shapes (hidden 1024, 16 / 8 heads of 128, ffn 3072, Q8_0) with
-    37 cached positions, for a step (1 row) and a verify block (5 rows), then the head and argmax."""
+    37 cached positions, for a step (1 row), a verify block (5 rows: src/common/qwen3-decoder.cpp:492-510) and a
+    prefill block (64 rows), then the head and argmax. From 32 rows the Q8_0 products run on the int8 tensor cores,
+    whose per-block float steps are summed in a different order: that block is checked within 1e-4 of the largest
+    value, its caches within one F16 rounding and its argmax wherever the top two logits are apart."""
     import torch
 
     from oracle import graph as og
@@ -178,11 +189,12 @@ def test_qwen3_decoder_layer_with_kv_cache(b200, ctx, oracle):
     def mm(w, x, n, k):
         return oracle.mul_mat(Q8, w, k, n, x)
 
-    for rows in (1, 5):
+    for rows in (1, 5, 64):
+        exact = rows < 32
         x0 = rng.normal(0, 1, size=(rows, hid)).astype(F32)
         pos = np.arange(n_past, n_past + rows, dtype=np.int32)
         n_kv = 256  # the cache rows attention reads: whole blocks, the rest masked
-        mask = np.full((8, n_kv), -np.inf, dtype=F16)
+        mask = np.full((max(8, rows), n_kv), -np.inf, dtype=F16)
         for i in range(rows):
             mask[i, : n_past + i + 1] = 0
 
@@ -258,9 +270,90 @@ def test_qwen3_decoder_layer_with_kv_cache(b200, ctx, oracle):
             return T
 
         run(b200, ctx, build)
-        close_and_mostly_equal(T["x2"].cpu().numpy(), x2)
-        close_and_mostly_equal(T["logits"].cpu().numpy(), logits)
-        assert np.array_equal(ck_d.cpu().numpy(), ck) and np.array_equal(cv_d.cpu().numpy(), cv)
-        assert np.array_equal(pick.cpu().numpy(), og.argmax(logits))
+        if exact:
+            close_and_mostly_equal(T["x2"].cpu().numpy(), x2)
+            close_and_mostly_equal(T["logits"].cpu().numpy(), logits)
+            assert np.array_equal(ck_d.cpu().numpy(), ck) and np.array_equal(cv_d.cpu().numpy(), cv)
+            assert np.array_equal(pick.cpu().numpy(), og.argmax(logits))
+            continue
+        close_and_mostly_equal(T["x2"].cpu().numpy(), x2, rtol=1e-4, frac=0.0)
+        close_and_mostly_equal(T["logits"].cpu().numpy(), logits, rtol=1e-4, frac=0.0)
+        for got, want in ((ck_d, ck), (cv_d, cv)):
+            g32, w32 = got.cpu().numpy().astype(F32), want.astype(F32)
+            assert np.all(np.abs(g32 - w32) <= np.abs(w32) * 2.0 ** -10 + 2.0 ** -24)
+        srt = np.sort(logits, axis=-1)
+        apart = srt[:, -1] - srt[:, -2] > 1e-3 * np.abs(logits).max()
+        assert np.array_equal(pick.cpu().numpy()[apart], og.argmax(logits)[apart]) and apart.mean() > 0.5
     for w in dev.values():
+        ctx.free_weight(w)
+
+
+def test_block_equals_steps(b200, ctx, oracle):
+    """Blocked computation equals step-by-step computation (the property speech.cpp's qwen3-decoder-check asserts,
+    checks/common/qwen3-decoder-check.cpp): a decoder layer run over a block of 6 rows, and the same 6 rows run as 6
+    one-row steps that each append to the KV cache, give bit-identical outputs and caches. With fewer than 32 rows
+    every product quantizes and sums each row on its own, and attention reads the same cache prefix either way."""
+    import torch
+
+    Q8 = b200.Q8_0
+    hid, H, Hkv, D, ffn, n_past, cap, n_kv, rows = 256, 4, 2, 64, 512, 11, 64, 64, 6
+    base = 1e6
+    rng = np.random.default_rng(5)
+
+    def wq(n, k):
+        return ctx.weight(Q8, k, n, data=oracle.quantize(Q8, rng.normal(0, 0.05, size=(n, k)).astype(F32)))
+
+    Wq, Wk, Wv, Wo, Wg, Wu, Wd = wq(H * D, hid), wq(Hkv * D, hid), wq(Hkv * D, hid), wq(hid, H * D), wq(ffn, hid), wq(ffn, hid), wq(hid, ffn)
+    norms = [cu(rng.normal(1, 0.1, size=n).astype(F32)) for n in (hid, D, D, hid)]
+    cache_k0 = rng.normal(0, 1, size=(cap, Hkv * D)).astype(F16)
+    cache_v0 = rng.normal(0, 1, size=(cap, Hkv * D)).astype(F16)
+    x_all = rng.normal(0, 1, size=(rows, hid)).astype(F32)
+
+    def layer(x, first, ck_d, cv_d):
+        n = x.shape[0]
+        pos = np.arange(first, first + n, dtype=np.int32)
+        mask = np.full((max(8, n), n_kv), -np.inf, dtype=F16)
+        for i in range(n):
+            mask[i, : first + i + 1] = 0
+        T = {k: torch.empty(s, device="cuda") for k, s in
+             {"h0": (n, hid), "h": (n, hid), "q": (n, H * D), "k": (n, Hkv * D), "v": (n, Hkv * D), "qn0": (n, H, D),
+              "qn": (n, H, D), "kn0": (n, Hkv, D), "kn": (n, Hkv, D), "qr": (n, H, D), "kr": (n, Hkv, D),
+              "att": (n, H, D), "o": (n, hid), "x1": (n, hid), "f0": (n, hid), "f": (n, hid), "g": (n, ffn),
+              "u": (n, ffn), "a": (n, ffn), "d": (n, hid), "x2": (n, hid)}.items()}
+        g = b200.Graph(ctx)
+        e = g.fbits(1e-6)
+        X, P, M = g.add(t=cu(x)), g.add(t=cu(pos)), g.add(t=cu(mask))
+        W = [g.add(weight=w) for w in (Wq, Wk, Wv, Wo, Wg, Wu, Wd)]
+        an, qw, kw, fw = (g.add(t=t) for t in norms)
+        hh = g.add(b200.OP_MUL, T["h"], src=[g.add(b200.OP_RMS_NORM, T["h0"], src=[X], params=[e]), an])
+        q_, k_, v_ = (g.add(b200.OP_MUL_MAT, T[nm], src=[W[j], hh]) for j, nm in enumerate("qkv"))
+        q3, k3 = g.add(t=T["q"].view(n, H, D)), g.add(t=T["k"].view(n, Hkv, D))
+        qn = g.add(b200.OP_MUL, T["qn"], src=[g.add(b200.OP_RMS_NORM, T["qn0"], src=[q3], params=[e]), qw])
+        kn = g.add(b200.OP_MUL, T["kn"], src=[g.add(b200.OP_RMS_NORM, T["kn0"], src=[k3], params=[e]), kw])
+        CK, CV = g.add(t=ck_d), g.add(t=cv_d)
+        g.add(b200.OP_SET_ROWS, cv_d, src=[v_, P, CV])
+        rope = [D, 2, g.fbits(base), g.fbits(1.0), 0, g.fbits(1.0)]
+        g.add(b200.OP_ROPE, T["qr"], src=[qn, P], params=rope)
+        g.add(b200.OP_ROPE, T["kr"], src=[kn, P], params=rope)
+        g.add(b200.OP_SET_ROWS, ck_d, src=[g.add(t=T["kr"].view(n, Hkv * D)), P, CK])
+        keys = g.add(t=ck_d[:n_kv].view(n_kv, Hkv, D).permute(1, 0, 2))
+        vals = g.add(t=cv_d[:n_kv].view(n_kv, Hkv, D).permute(1, 0, 2))
+        g.add(b200.OP_FLASH_ATTN, T["att"], src=[g.add(t=T["qr"].permute(1, 0, 2)), keys, vals, M], params=[g.fbits(D ** -0.5)])
+        o = g.add(b200.OP_MUL_MAT, T["o"], src=[W[3], g.add(t=T["att"].view(n, H * D))])
+        x1 = g.add(b200.OP_ADD, T["x1"], src=[X, o])
+        f = g.add(b200.OP_MUL, T["f"], src=[g.add(b200.OP_RMS_NORM, T["f0"], src=[x1], params=[e]), fw])
+        ga, up = g.add(b200.OP_MUL_MAT, T["g"], src=[W[4], f]), g.add(b200.OP_MUL_MAT, T["u"], src=[W[5], f])
+        dn = g.add(b200.OP_MUL_MAT, T["d"], src=[W[6], g.add(b200.OP_SWIGLU, T["a"], src=[ga, up])])
+        g.add(b200.OP_ADD, T["x2"], src=[x1, dn])
+        g.compute()
+        ctx.synchronize()
+        return T["x2"].cpu().numpy()
+
+    ck_b, cv_b = cu(cache_k0), cu(cache_v0)
+    block = layer(x_all, n_past, ck_b, cv_b)
+    ck_s, cv_s = cu(cache_k0), cu(cache_v0)
+    steps = np.concatenate([layer(x_all[i : i + 1], n_past + i, ck_s, cv_s) for i in range(rows)])
+    assert np.array_equal(block, steps)
+    assert torch.equal(ck_b, ck_s) and torch.equal(cv_b, cv_s)
+    for w in (Wq, Wk, Wv, Wo, Wg, Wu, Wd):
         ctx.free_weight(w)
