@@ -162,8 +162,9 @@ def test_qwen3_decoder_layer_with_kv_cache(b200, ctx, oracle):
     """One decoder layer of the Qwen3-TTS 0.6B talker's shapes (hidden 1024, 16 / 8 heads of 128, ffn 3072, Q8_0) with
     37 cached positions, for a step (1 row), a verify block (5 rows: src/common/qwen3-decoder.cpp:492-510) and a
     prefill block (64 rows), then the head and argmax. From 32 rows the Q8_0 products run on the int8 tensor cores,
-    whose per-block float steps are summed in a different order: that block is checked within 1e-4 of the largest
-    value, its caches within one F16 rounding and its argmax wherever the top two logits are apart."""
+    whose per-block float steps are summed in a different order: that block is checked by row cosine (>= 0.99999 for
+    the layer output, >= 0.9999 for the logits), its caches within one F16 rounding and its argmax wherever the top
+    two logits are apart."""
     import torch
 
     from oracle import graph as og
@@ -276,8 +277,14 @@ def test_qwen3_decoder_layer_with_kv_cache(b200, ctx, oracle):
             assert np.array_equal(ck_d.cpu().numpy(), ck) and np.array_equal(cv_d.cpu().numpy(), cv)
             assert np.array_equal(pick.cpu().numpy(), og.argmax(logits))
             continue
-        close_and_mostly_equal(T["x2"].cpu().numpy(), x2, rtol=1e-4, frac=0.0)
-        close_and_mostly_equal(T["logits"].cpu().numpy(), logits, rtol=1e-4, frac=0.0)
+        # a float difference inside a product can move an activation across a q8_0 rounding boundary of a later
+        # product, which changes that element by a quantization step and the later product's whole row with it: rows
+        # are compared by cosine, elements only against a bound a quantization step cannot reach past
+        for got, want, bar in ((T["x2"].cpu().numpy(), x2, 0.99999), (T["logits"].cpu().numpy(), logits, 0.9999)):
+            g64, w64 = got.astype(np.float64), want.astype(np.float64)
+            cos = (g64 * w64).sum(-1) / np.sqrt((g64 * g64).sum(-1) * (w64 * w64).sum(-1))
+            assert cos.min() >= bar, f"row cosine {cos.min():.7f}"
+            assert np.abs(g64 - w64).max() <= 1e-2 * np.abs(w64).max()
         for got, want in ((ck_d, ck), (cv_d, cv)):
             g32, w32 = got.cpu().numpy().astype(F32), want.astype(F32)
             assert np.all(np.abs(g32 - w32) <= np.abs(w32) * 2.0 ** -10 + 2.0 ** -24)
