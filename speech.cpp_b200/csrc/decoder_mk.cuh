@@ -344,7 +344,7 @@ __device__ __forceinline__ void mk_rows(const MkStage & S, const Act & a, const 
         if (i < T::kFields) b += rps * T::field_row_bytes(K, i);
     }
     auto store = [&](int j, float v) { mk_store(S, first + j, r0, res_s, v, tag); };
-    if constexpr (kForms) smem_rows<T>(f, K, (int) rows, a, S.w, warp, kMkConsumerWarps, store);
+    if constexpr (kForms) smem_rows<T, false>(f, K, (int) rows, a, S.w, warp, kMkConsumerWarps, store);
     else if (T::units_per_row(K) <= 64) smem_rows_lpr<T, 8>(f, K, (int) rows, a, S.w, warp, kMkConsumerWarps, store);
     else smem_rows_lpr<T, 32>(f, K, (int) rows, a, S.w, warp, kMkConsumerWarps, store);
 }
@@ -370,7 +370,7 @@ __device__ __forceinline__ void mk_rows_glu(const MkStage & S, const Act & a, co
         else if (j >= rps) gu_s[1][base + (j - rps)] = v;
     };
     const int n = (int) (rps + rows);
-    if constexpr (kForms) smem_rows<T>(f, K, n, a, S.w, warp, kMkConsumerWarps, store);
+    if constexpr (kForms) smem_rows<T, false>(f, K, n, a, S.w, warp, kMkConsumerWarps, store);
     else if (T::units_per_row(K) <= 64) smem_rows_lpr<T, 8>(f, K, n, a, S.w, warp, kMkConsumerWarps, store);
     else smem_rows_lpr<T, 32>(f, K, n, a, S.w, warp, kMkConsumerWarps, store);
 }

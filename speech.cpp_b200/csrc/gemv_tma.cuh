@@ -169,7 +169,91 @@ __device__ __forceinline__ void smem_rows_q4k(const uint8_t * const * f, int64_t
     }
 }
 
-// Q6_K rows from shared memory, single column: LPR lanes per row; lane li takes the units u = li, li + LPR, ... of its
+// Q6_K rows from shared memory, single column: LPR lanes per pair of rows; lane li takes the units u = li, li + LPR, ...
+// of both rows, unit u being a quarter of super-block sb = u / 4: half hh and values l in [lq, lq + 16) of that half
+// (ggml's layout: quant bytes ql[64 hh + l] and ql[64 hh + 32 + l] hold values 128 hh + 32 t + l for t = 0, 2 (low,
+// high nibble) and t = 1, 3; bits 2t, 2t + 1 of qh[32 hh + l] are their top bits). The unit's activations are read
+// once for both rows (shared memory bandwidth bounds this form). The four 16-value groups t of a unit are visited in
+// the order t = k ^ (sb % 2 + 2 hh), k = 0..3, and odd super-blocks load their t-odd quant bytes first: so the 8
+// lanes of every 128-bit shared-memory phase (two super-blocks) touch 8 distinct 16-byte bank groups, for the
+// activations as for the weights. Per group the int32 sum is exact, sum (q - 32) x = sum q x - 32 bsum, times the
+// group's int8 scale; per unit one float32 scale d * dx (as in gemv's unit). Each row's terms are added in the same
+// order as with one row per lane.
+template <int LPR, class Store>
+__device__ __forceinline__ void smem_rows_q6k(const uint8_t * const * f, int64_t K, int rows, const Act & a, int warp,
+                                              int nwarps, Store store) {
+    const int lane = threadIdx.x & 31;
+    constexpr int kPairsPerPass = 32 / LPR;
+    const int sub = lane / LPR, li = lane % LPR;
+    const int nsb = (int) (K / 256), upr = 4 * nsb;
+    const int hh = (li >> 1) & 1, lb = li & 1, sbpar = (li >> 2) & 1;  // LPR is a multiple of 8: fixed per lane
+    const int tx = sbpar | (hh << 1);
+    const int offP = 64 * hh + 16 * lb + (sbpar ? 32 : 0), offQ = 64 * hh + 16 * lb + (sbpar ? 0 : 32);
+    for (int j0 = warp * 2 * kPairsPerPass; j0 < rows; j0 += nwarps * 2 * kPairsPerPass) {
+        const int ja = j0 + 2 * sub, jb = ja + 1;
+        double acca = 0.0, accb = 0.0;
+        if (ja < rows) {
+            const int jr = jb < rows ? jb : ja;  // a lone last row computes itself twice and stores once
+            const uint8_t * qla = f[0] + (size_t) ja * (size_t) (K / 2);
+            const uint8_t * qlb = f[0] + (size_t) jr * (size_t) (K / 2);
+            const uint8_t * qha = f[1] + (size_t) ja * (size_t) (K / 4) + 32 * hh + 16 * lb;
+            const uint8_t * qhb = f[1] + (size_t) jr * (size_t) (K / 4) + 32 * hh + 16 * lb;
+            const int8_t * sca = reinterpret_cast<const int8_t *>(f[2]) + (size_t) ja * nsb * 16 + 8 * hh + lb;
+            const int8_t * scb = reinterpret_cast<const int8_t *>(f[2]) + (size_t) jr * nsb * 16 + 8 * hh + lb;
+            const uint16_t * dra = reinterpret_cast<const uint16_t *>(f[3]) + (size_t) ja * nsb;
+            const uint16_t * drb = reinterpret_cast<const uint16_t *>(f[3]) + (size_t) jr * nsb;
+            for (int u = li; u < upr; u += LPR) {
+                const int sb = u >> 2;
+                const int4 Pa = *reinterpret_cast<const int4 *>(qla + 128 * sb + offP);  // the t with t % 2 == sb % 2
+                const int4 Qa = *reinterpret_cast<const int4 *>(qla + 128 * sb + offQ);
+                const int4 Ha = *reinterpret_cast<const int4 *>(qha + 64 * sb);
+                const int4 Pb = *reinterpret_cast<const int4 *>(qlb + 128 * sb + offP);
+                const int4 Qb = *reinterpret_cast<const int4 *>(qlb + 128 * sb + offQ);
+                const int4 Hb = *reinterpret_cast<const int4 *>(qhb + 64 * sb);
+                const int8_t * xq = a.q + 256 * sb + 128 * hh + 16 * lb;
+                const int16_t * bs = a.bs + 16 * sb + 8 * hh + lb;
+                int sia = 0, sib = 0;
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    const int t = k ^ tx;
+                    const int ns = 4 * (t >> 1), hs = 2 * t;
+                    const int4 xv = *reinterpret_cast<const int4 *>(xq + 32 * t);
+                    const int bsum = 32 * (int) bs[2 * t];
+                    {
+                        const int4 src = (k & 1) ? Qa : Pa;
+                        int s = __dp4a((int) ((((unsigned) src.x >> ns) & 0x0F0F0F0Fu) | ((((unsigned) Ha.x >> hs) & 0x03030303u) << 4)), xv.x, 0);
+                        s = __dp4a((int) ((((unsigned) src.y >> ns) & 0x0F0F0F0Fu) | ((((unsigned) Ha.y >> hs) & 0x03030303u) << 4)), xv.y, s);
+                        s = __dp4a((int) ((((unsigned) src.z >> ns) & 0x0F0F0F0Fu) | ((((unsigned) Ha.z >> hs) & 0x03030303u) << 4)), xv.z, s);
+                        s = __dp4a((int) ((((unsigned) src.w >> ns) & 0x0F0F0F0Fu) | ((((unsigned) Ha.w >> hs) & 0x03030303u) << 4)), xv.w, s);
+                        sia += (int) sca[16 * sb + 2 * t] * (s - bsum);
+                    }
+                    {
+                        const int4 src = (k & 1) ? Qb : Pb;
+                        int s = __dp4a((int) ((((unsigned) src.x >> ns) & 0x0F0F0F0Fu) | ((((unsigned) Hb.x >> hs) & 0x03030303u) << 4)), xv.x, 0);
+                        s = __dp4a((int) ((((unsigned) src.y >> ns) & 0x0F0F0F0Fu) | ((((unsigned) Hb.y >> hs) & 0x03030303u) << 4)), xv.y, s);
+                        s = __dp4a((int) ((((unsigned) src.z >> ns) & 0x0F0F0F0Fu) | ((((unsigned) Hb.z >> hs) & 0x03030303u) << 4)), xv.z, s);
+                        s = __dp4a((int) ((((unsigned) src.w >> ns) & 0x0F0F0F0Fu) | ((((unsigned) Hb.w >> hs) & 0x03030303u) << 4)), xv.w, s);
+                        sib += (int) scb[16 * sb + 2 * t] * (s - bsum);
+                    }
+                }
+                const float dx = a.d[sb];
+                acca = acc_term(acca, __fmul_rn(__half2float(__ushort_as_half(dra[sb])), dx), sia);
+                accb = acc_term(accb, __fmul_rn(__half2float(__ushort_as_half(drb[sb])), dx), sib);
+            }
+        }
+#pragma unroll
+        for (int o = LPR / 2; o > 0; o >>= 1) {
+            acca += __shfl_xor_sync(0xffffffffu, acca, o);
+            accb += __shfl_xor_sync(0xffffffffu, accb, o);
+        }
+        if (li == 0) {
+            if (ja < rows) store(ja, __double2float_rn(acca));
+            if (jb < rows) store(jb, __double2float_rn(accb));
+        }
+    }
+}
+
+// Q6_K rows from shared memory, one row per lane group (the form for kernels short of registers): LPR lanes per row; lane li takes the units u = li, li + LPR, ... of its
 // row, unit u being a quarter of super-block sb = u / 4: half hh and values l in [lq, lq + 16) of that half (ggml's
 // layout: quant bytes ql[64 hh + l] and ql[64 hh + 32 + l] hold values 128 hh + 32 t + l for t = 0, 2 (low, high
 // nibble) and t = 1, 3; bits 2t, 2t + 1 of qh[32 hh + l] are their top bits). The four 16-value groups t of a unit are
@@ -178,7 +262,7 @@ __device__ __forceinline__ void smem_rows_q4k(const uint8_t * const * f, int64_t
 // activations as for the weights. Per group the int32 sum is exact, sum (q - 32) x = sum q x - 32 bsum, times the
 // group's int8 scale; per unit one float32 scale d * dx (as in gemv's unit).
 template <int LPR, class Store>
-__device__ __forceinline__ void smem_rows_q6k(const uint8_t * const * f, int64_t K, int rows, const Act & a, int warp,
+__device__ __forceinline__ void smem_rows_q6k_single(const uint8_t * const * f, int64_t K, int rows, const Act & a, int warp,
                                               int nwarps, Store store) {
     const int lane = threadIdx.x & 31;
     constexpr int kRowsPerPass = 32 / LPR;
@@ -229,14 +313,18 @@ __device__ __forceinline__ void smem_rows_q6k(const uint8_t * const * f, int64_t
 
 // Lanes per row: 8 for rows of up to 64 units (a warp reduces 4 rows at once), 32 for longer rows; Q4_K and Q6_K have
 // their own forms. A function of K alone, so a row's summation order does not depend on how rows are chunked (launch
-// geometry never changes results).
-template <class T, class Store>
+// geometry never changes results). kPairedQ6: Q6_K rows two per lane group (fewer shared-memory reads); the persistent
+// decode step, short of registers, takes the single-row form, which adds each row's terms in the same order.
+template <class T, bool kPairedQ6 = true, class Store>
 __device__ __forceinline__ void smem_rows(const uint8_t * const * f, int64_t K, int rows, const Act & a, const WeightView & w,
                                           int warp, int nwarps, Store store) {
     if constexpr (std::is_same<T, TQ4_K>::value) smem_rows_q4k(f, K, rows, a, warp, nwarps, store);
-    else if constexpr (std::is_same<T, TQ6_K>::value) {
+    else if constexpr (std::is_same<T, TQ6_K>::value && kPairedQ6) {
         if (T::units_per_row(K) <= 64) smem_rows_q6k<8>(f, K, rows, a, warp, nwarps, store);
         else smem_rows_q6k<32>(f, K, rows, a, warp, nwarps, store);
+    } else if constexpr (std::is_same<T, TQ6_K>::value) {
+        if (T::units_per_row(K) <= 64) smem_rows_q6k_single<8>(f, K, rows, a, warp, nwarps, store);
+        else smem_rows_q6k_single<32>(f, K, rows, a, warp, nwarps, store);
     } else if (T::units_per_row(K) <= 64) smem_rows_lpr<T, 8>(f, K, rows, a, w, warp, nwarps, store);
     else smem_rows_lpr<T, 32>(f, K, rows, a, w, warp, nwarps, store);
 }
