@@ -112,14 +112,32 @@ __global__ void __launch_bounds__(kGThreads, 2)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // item = (output tile, K split), the split fastest: the splits of one tile run at the same time on different CTAs
+    const int ksplit = kSplit ? p.ksplit : 1;
+    const int spl = nstage / ksplit;  // stages per split
+    // Dense products are launched with programmatic dependent launch: their weight tiles depend on no earlier kernel,
+    // so the producer streams the weights (and weight scales) of its first item's first stages now, while the
+    // activations are still being quantized; those stages' activation loads follow the wait below.
+    int pre = 0;
+    if (!p.tiles && warp == 0 && lane == 0 && (int) blockIdx.x < ((p.dense_m + 31) / 32) * p.tiles_n * ksplit) {
+        const int it = blockIdx.x;
+        const int ot = kSplit ? it / ksplit : it, ks = kSplit ? it % ksplit : 0;
+        const int4 t = g_tile(p, ot / p.tiles_n);
+        const int arow = (int) ((int64_t) t.x * p.N + p.row0 + (int64_t) (ot % p.tiles_n) * kGM);
+        const uint32_t bytes = (uint32_t) (L::kA + t.z * 256 + L::kDw + L::kDx);
+        for (; pre < kGStages && pre < spl; pre++) {
+            uint8_t * base = smem + pre * L::kStage;
+            mbar_arrive_expect_tx(&full[pre], bytes);
+            const int kbs = (ks * spl + pre) * kGKB;
+            for (int jj = 0; jj < 2; jj++) tma_load_2d(base + jj * kGM * 128, &tmA, (kbs + 4 * jj) * 32, arow, &full[pre]);
+            tma_load_2d(base + L::kA + L::kB, &tmDw, kbs, arow, &full[pre]);
+        }
+    }
     // the tile list and the activations come from the kernels before this one (no-ops unless launched with
     // programmatic dependent launch); the next kernel may launch its CTAs once these have started
     pdl_wait();
     pdl_launch_dependents();
-    // item = (output tile, K split), the split fastest: the splits of one tile run at the same time on different CTAs
-    const int ksplit = kSplit ? p.ksplit : 1;
     const int items = (p.tiles ? *p.ntiles : (p.dense_m + 31) / 32) * p.tiles_n * ksplit;
-    const int spl = nstage / ksplit;  // stages per split
 
     if (warp == 0) {
         // ---- TMA producer ----
@@ -137,20 +155,21 @@ __global__ void __launch_bounds__(kGThreads, 2)
                 const uint32_t bytes = (uint32_t) (L::kA + t.z * 256 + L::kDw + L::kDx);
                 for (int st = ks * spl; st < (ks + 1) * spl; st++, sg++) {
                     const int s = sg % kGStages, use = sg / kGStages;
+                    const bool early = sg < pre;  // weights already issued before the wait
                     if (use > 0 && !mbar_wait_sleep(&empty[s], (use - 1) & 1)) {
                         atomicOr(p.err, kErrTimeout);
                         give_up = 1;
                         break;
                     }
                     uint8_t * base = smem + s * L::kStage;
-                    mbar_arrive_expect_tx(&full[s], bytes);
+                    if (!early) mbar_arrive_expect_tx(&full[s], bytes);
                     const int kbs = st * kGKB;
                     for (int jj = 0; jj < 2; jj++) {
-                        tma_load_2d(base + jj * kGM * 128, &tmA, (kbs + 4 * jj) * 32, arow, &full[s]);
+                        if (!early) tma_load_2d(base + jj * kGM * 128, &tmA, (kbs + 4 * jj) * 32, arow, &full[s]);
                         for (int r = 0; r < nsub; r++)
                             tma_load_2d(base + L::kA + jj * kGNT * 128 + r * 16 * 128, &tmB, (kbs + 4 * jj) * 32, t.y + 16 * r, &full[s]);
                     }
-                    tma_load_2d(base + L::kA + L::kB, &tmDw, kbs, arow, &full[s]);
+                    if (!early) tma_load_2d(base + L::kA + L::kB, &tmDw, kbs, arow, &full[s]);
                     tma_load_2d(base + L::kA + L::kB + L::kDw, &tmDx, t.y, kbs, &full[s]);
                 }
             }
@@ -380,11 +399,21 @@ cudaError_t launch_grouped(const WeightView & w, int64_t N, int64_t row0, int de
         if (e != cudaSuccess) return e;
         configured = 1;
     }
-    // Launched without programmatic dependent launch: CTAs started early would hold the SMs' shared memory while the
-    // previous kernel drains (measured slower).
-    if (ksplit > 1) gemm_q8_0_tc_grouped_kernel<true><<<2 * num_sms, kGThreads, L::kTotal, st>>>(ta, tb, tdw, tdx, p);
-    else gemm_q8_0_tc_grouped_kernel<false><<<2 * num_sms, kGThreads, L::kTotal, st>>>(ta, tb, tdw, tdx, p);
-    return cudaGetLastError();
+    // Expert products are launched without programmatic dependent launch: CTAs started early would hold the SMs'
+    // shared memory while the previous kernel drains (measured slower). Dense products are: their CTAs stream weights
+    // while the activations are quantized.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned) (2 * num_sms), 1, 1);
+    cfg.blockDim = dim3(kGThreads, 1, 1);
+    cfg.dynamicSmemBytes = L::kTotal;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = tiles ? 0 : 1;
+    if (ksplit > 1) return cudaLaunchKernelEx(&cfg, gemm_q8_0_tc_grouped_kernel<true>, ta, tb, tdw, tdx, p);
+    return cudaLaunchKernelEx(&cfg, gemm_q8_0_tc_grouped_kernel<false>, ta, tb, tdw, tdx, p);
 }
 
 }  // namespace

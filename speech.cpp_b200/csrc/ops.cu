@@ -170,6 +170,10 @@ cudaError_t launch_get_rows(const WeightView & w, const int32_t * ids, int64_t n
 // ------------------------------------------------------------------------------------------------------------------
 __global__ void quantize_act_kernel(int kind, const float * __restrict__ x, int64_t K, int64_t M, uint8_t * gguf, int8_t * q,
                                     float * d, int16_t * bs, int64_t dT_ld) {
+    // launched with programmatic dependent launch: x is read after the previous kernel's writes are visible; the next
+    // kernel (a tensor-core product streaming its weights) may start now
+    pdl_wait();
+    pdl_launch_dependents();
     const int lane = threadIdx.x & 31;
     const int64_t warps = (int64_t) gridDim.x * (blockDim.x >> 5);
     const int64_t bsz = kind == B200_TYPE_Q8_0 ? 32 : 256;
@@ -223,8 +227,16 @@ cudaError_t launch_quantize(int kind, const float * x, int64_t K, int64_t M, uin
     const int threads = 256;
     int64_t blocks = (nb + 7) / 8;
     if (blocks > 148 * 8) blocks = 148 * 8;
-    quantize_act_kernel<<<(unsigned) blocks, threads, 0, st>>>(kind, x, K, M, gguf, q, d, bs, dT_ld);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned) blocks, 1, 1);
+    cfg.blockDim = dim3(threads, 1, 1);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, quantize_act_kernel, kind, x, K, M, gguf, q, d, bs, dT_ld);
 }
 
 // ------------------------------------------------------------------------------------------------------------------
