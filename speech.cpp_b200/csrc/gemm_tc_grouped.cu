@@ -115,14 +115,18 @@ __global__ void __launch_bounds__(kGThreads, 2)
     // item = (output tile, K split), the split fastest: the splits of one tile run at the same time on different CTAs
     const int ksplit = kSplit ? p.ksplit : 1;
     const int spl = nstage / ksplit;  // stages per split
-    // Dense products are launched with programmatic dependent launch: their weight tiles depend on no earlier kernel,
-    // so the producer streams the weights (and weight scales) of its first item's first stages now, while the
-    // activations are still being quantized; those stages' activation loads follow the wait below.
+    // Launched with programmatic dependent launch, the producer streams the weights (and weight scales) of its first
+    // item's first stages now, while the kernel before this one (activation quantization, or the SwiGLU between the
+    // expert products) still runs; those stages' activation loads follow the wait below. Weight tiles depend on no
+    // earlier kernel for dense products, and on the routing's tile list for expert products: the routing ran two or
+    // more launches earlier and had completed before the previous kernel passed its own wait, which preceded this
+    // launch; the list is read through L2.
     int pre = 0;
-    if (!p.tiles && warp == 0 && lane == 0 && (int) blockIdx.x < ((p.dense_m + 31) / 32) * p.tiles_n * ksplit) {
+    const int items_early = p.tiles ? (int) __ldcg(p.ntiles) * p.tiles_n * ksplit : ((p.dense_m + 31) / 32) * p.tiles_n * ksplit;
+    if (warp == 0 && lane == 0 && (int) blockIdx.x < items_early) {
         const int it = blockIdx.x;
         const int ot = kSplit ? it / ksplit : it, ks = kSplit ? it % ksplit : 0;
-        const int4 t = g_tile(p, ot / p.tiles_n);
+        const int4 t = p.tiles ? __ldcg(p.tiles + ot / p.tiles_n) : g_tile(p, ot / p.tiles_n);
         const int arow = (int) ((int64_t) t.x * p.N + p.row0 + (int64_t) (ot % p.tiles_n) * kGM);
         const uint32_t bytes = (uint32_t) (L::kA + t.z * 256 + L::kDw + L::kDx);
         for (; pre < kGStages && pre < spl; pre++) {
@@ -399,9 +403,7 @@ cudaError_t launch_grouped(const WeightView & w, int64_t N, int64_t row0, int de
         if (e != cudaSuccess) return e;
         configured = 1;
     }
-    // Expert products are launched without programmatic dependent launch: CTAs started early would hold the SMs'
-    // shared memory while the previous kernel drains (measured slower). Dense products are: their CTAs stream weights
-    // while the activations are quantized.
+    // Programmatic dependent launch: the CTAs stream their first weight stages while the previous kernel finishes.
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned) (2 * num_sms), 1, 1);
     cfg.blockDim = dim3(kGThreads, 1, 1);
@@ -411,7 +413,7 @@ cudaError_t launch_grouped(const WeightView & w, int64_t N, int64_t row0, int de
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = tiles ? 0 : 1;
+    cfg.numAttrs = 1;
     if (ksplit > 1) return cudaLaunchKernelEx(&cfg, gemm_q8_0_tc_grouped_kernel<true>, ta, tb, tdw, tdx, p);
     return cudaLaunchKernelEx(&cfg, gemm_q8_0_tc_grouped_kernel<false>, ta, tb, tdw, tdx, p);
 }
