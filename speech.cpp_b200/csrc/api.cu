@@ -628,8 +628,11 @@ b200_status b200_moe_ffn(b200_context * ctx, const b200_weight * gate_up, const 
     const int64_t H = gate_up->ne0, F2 = gate_up->ne1, E = gate_up->ne2, F = F2 / 2;
     if (F2 % 2 || down->ne0 != F || down->ne1 != H || down->ne2 != E || F % 32)
         return fail(ctx, B200_ERR_INVALID, "moe_ffn: gate_up must be [H, 2F, E] and down [F, H, E]");
-    if (down->type != B200_TYPE_Q8_0 || gate_up->type == B200_TYPE_F32 || gate_up->type == B200_TYPE_BF16)
-        return fail(ctx, B200_ERR_UNSUPPORTED, "moe_ffn: quantized gate_up and Q8_0 down experts");
+    const bool kdown = down->type == B200_TYPE_Q4_K || down->type == B200_TYPE_Q5_K || down->type == B200_TYPE_Q6_K;
+    if ((down->type != B200_TYPE_Q8_0 && !kdown) || gate_up->type == B200_TYPE_F32 || gate_up->type == B200_TYPE_BF16)
+        return fail(ctx, B200_ERR_UNSUPPORTED, "moe_ffn: quantized experts (Q8_0, Q4_K, Q5_K or Q6_K)");
+    if (kdown && F % 256)
+        return fail(ctx, B200_ERR_INVALID, "moe_ffn: K-quant down experts need whole 256-value super-blocks");
     if (top_k <= 0 || T < 0 || expert0 < 0 || (n_expert_total > 0 && expert0 + E > n_expert_total))
         return fail(ctx, B200_ERR_INVALID, "moe_ffn: bad shape or expert range");
     if (T == 0) return B200_OK;
@@ -643,8 +646,9 @@ b200_status b200_moe_ffn(b200_context * ctx, const b200_weight * gate_up, const 
     const int nc1 = gemv_max_columns(gate_up->type, H), nc2 = gemv_max_columns(down->type, F);
     if (!nc1 || !nc2) return fail(ctx, B200_ERR_UNSUPPORTED, "moe_ffn: rows too long for the staging buffer");
     auto up = [](size_t v) { return (v + 255) & ~(size_t) 255; };
+    const int kind2 = act_kind(down->type);  // q8_0 for Q8_0 down experts, q8_K for K-quants
     const size_t need = up((size_t) (E + 1) * 4) + 3 * up((size_t) P * 4) + quantized_act_bytes(kind, H, T) + up((size_t) P * F2 * 4) +
-                        quantized_act_bytes(B200_TYPE_Q8_0, F, P) + up((size_t) P * H * 4);
+                        quantized_act_bytes(kind2, F, P) + up((size_t) P * H * 4);
     b200_status s = ensure_scratch(ctx, need);
     if (s != B200_OK) return s;
     Carve c{(uint8_t *) ctx->scratch};
@@ -657,7 +661,8 @@ b200_status b200_moe_ffn(b200_context * ctx, const b200_weight * gate_up, const 
     int16_t * xbs = kind == B200_TYPE_Q8_K ? c.take<int16_t>((size_t) T * (H / 16)) : nullptr;
     float * gu = c.take<float>((size_t) P * F2);
     int8_t * aq = c.take<int8_t>((size_t) P * F);
-    float * ad = c.take<float>((size_t) P * (F / 32));
+    float * ad = c.take<float>((size_t) P * (F / (kdown ? 256 : 32)));
+    int16_t * abs = kdown ? c.take<int16_t>((size_t) P * (F / 16)) : nullptr;
     float * dn = c.take<float>((size_t) P * H);
     cudaStream_t st = ctx->stream;
     CK(ctx, launch_quantize(kind, x, H, T, nullptr, xq, xd, xbs, st));
@@ -677,7 +682,8 @@ b200_status b200_moe_ffn(b200_context * ctx, const b200_weight * gate_up, const 
     p1.grp_off = grp_off;
     p1.grp_rows = F2;
     CK(ctx, launch_gemv(p1, nc1, (int) E, st, false, ctx->num_sms));
-    CK(ctx, launch_swiglu_quant_pairs(gu, F, col_dst, grp_off + E, P, aq, ad, st));
+    if (kdown) CK(ctx, launch_swiglu_quant_pairs_k(gu, F, col_dst, grp_off + E, P, aq, ad, abs, st));
+    else CK(ctx, launch_swiglu_quant_pairs(gu, F, col_dst, grp_off + E, P, aq, ad, st));
     // down of every routed pair: rows p of dn
     GemvParams p2 = base_params(ctx, down);
     p2.N = H;
@@ -685,6 +691,7 @@ b200_status b200_moe_ffn(b200_context * ctx, const b200_weight * gate_up, const 
     p2.ldx = F;
     p2.aq = aq;
     p2.ad = ad;
+    p2.abs = abs;
     p2.y = dn;
     p2.ldy = H;
     p2.col_src = col_dst;

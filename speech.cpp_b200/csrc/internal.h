@@ -89,6 +89,9 @@ cudaError_t launch_route(const int32_t * ids, int64_t T, int64_t top_k, int64_t 
                          int32_t * col_tok = nullptr);
 cudaError_t launch_swiglu_quant_pairs(const float * gu, int64_t F, const int32_t * col_dst, const int32_t * n_pairs, int64_t max_pairs,
                                       int8_t * q, float * d, cudaStream_t st);
+// q8_K of the SwiGLU rows (K-quant down experts): q [rows][F], d [rows][F/256], bs [rows][F/16]; F % 256 == 0.
+cudaError_t launch_swiglu_quant_pairs_k(const float * gu, int64_t F, const int32_t * col_dst, const int32_t * n_pairs, int64_t max_pairs,
+                                        int8_t * q, float * d, int16_t * bs, cudaStream_t st);
 cudaError_t launch_moe_combine(const float * down, const float * w, const int32_t * ids, int64_t T, int64_t top_k, int64_t H, int64_t e0,
                                int64_t E, float * out, cudaStream_t st);
 // Tensor-core expert products (gemm_tc_grouped.cu) and their routing/glue (moe.cu). Slots: pairs sorted by expert,

@@ -325,6 +325,32 @@ __global__ void swiglu_quant_pairs_kernel(const float * __restrict__ gu, int64_t
     }
 }
 
+// The same for K-quant down experts: q8_K of each pair's SwiGLU row, one warp per (pair slot, 256-block), as
+// quantize_act_kernel lays q8_K out (q [rows][F], d [rows][F/256], bs [rows][F/16]); bit-identical to
+// quantize_row_q8_K of the SwiGLU row.
+__global__ void swiglu_quant_pairs_k_kernel(const float * __restrict__ gu, int64_t F, const int32_t * __restrict__ col_dst,
+                                            const int32_t * __restrict__ n_pairs, int8_t * q, float * d, int16_t * bs) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nb = F / 256;
+    const int64_t total = (int64_t) (*n_pairs) * nb;
+    const int64_t warps = (int64_t) gridDim.x * (blockDim.x >> 5);
+    for (int64_t i = (int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); i < total; i += warps) {
+        const int64_t p = col_dst[i / nb], b = i % nb;
+        const float * row = gu + p * 2 * F + b * 256 + lane * 8;
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[j] = __fmul_rn(silu(row[j]), row[F + j]);
+        int8_t qv[8];
+        int16_t bsum;
+        float df;
+        quantize_q8_K_warp(v, qv, &bsum, &df);
+#pragma unroll
+        for (int j = 0; j < 8; j++) q[p * F + b * 256 + lane * 8 + j] = qv[j];
+        if ((lane & 1) == 0) bs[p * (F / 16) + b * 16 + lane / 2] = bsum;
+        if (lane == 0) d[p * nb + b] = df;
+    }
+}
+
 __global__ void moe_combine_kernel(const float * __restrict__ down, const float * __restrict__ w, const int32_t * __restrict__ ids,
                                    int64_t top_k, int64_t H, int e0, int E, float * __restrict__ out) {
     const int64_t t = blockIdx.x;
@@ -348,6 +374,15 @@ cudaError_t launch_swiglu_quant_pairs(const float * gu, int64_t F, const int32_t
     if (blocks > 148 * 8) blocks = 148 * 8;
     if (blocks < 1) blocks = 1;
     swiglu_quant_pairs_kernel<<<(unsigned) blocks, 256, 0, st>>>(gu, F, col_dst, n_pairs, q, d);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_swiglu_quant_pairs_k(const float * gu, int64_t F, const int32_t * col_dst, const int32_t * n_pairs, int64_t max_pairs,
+                                        int8_t * q, float * d, int16_t * bs, cudaStream_t st) {
+    int64_t blocks = (max_pairs * (F / 256) + 7) / 8;
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    if (blocks < 1) blocks = 1;
+    swiglu_quant_pairs_k_kernel<<<(unsigned) blocks, 256, 0, st>>>(gu, F, col_dst, n_pairs, q, d, bs);
     return cudaGetLastError();
 }
 
