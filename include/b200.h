@@ -144,8 +144,9 @@ b200_status b200_mul_mat_id(b200_context * ctx, const b200_weight * experts, con
 /* The routed-expert block of a mixture-of-experts FFN, as TextModel::experts builds it from ggml nodes
  * (src/families/drama3/text-model.cpp:198-221): for each token t and slot s with expert e = ids[t][s],
  *   out[t] = sum over s (in slot order) of w[t][s] * Wdown_e (silu(Wgate_e x_t) * Wup_e x_t),
- * with gate and up stored as one expert matrix: gate_up [H, 2F, E] (rows 0..F-1 gate, F..2F-1 up; any quantized
- * type) and down [F, H, E] (Q8_0). x [T][H], ids int32 [T][top_k], w float [T][top_k] (the router's softmax weights,
+ * with gate and up stored as one expert matrix: gate_up [H, 2F, E] (rows 0..F-1 gate, F..2F-1 up) and down [F, H, E],
+ * each Q8_0, Q4_K, Q5_K or Q6_K (K-quant down experts need F % 256 == 0). Q8_0 experts with H and F multiples of 256
+ * run on the tensor cores; the others on the routed GEMV. x [T][H], ids int32 [T][top_k], w float [T][top_k] (the router's softmax weights,
  * computed upstream), out [T][H]. Expert parallelism: these experts are experts [expert0, expert0 + E) of
  * n_expert_total (0: all); pairs routed to other experts are skipped, so out is this shard's partial sum, and the
  * shards' outputs add up to the full result. Ids outside [0, n_expert_total) are reported by b200_synchronize(). */
@@ -159,7 +160,8 @@ b200_status b200_moe_ffn(b200_context * ctx, const b200_weight * gate_up, const 
  * (64 bytes, exchanged by the caller, e.g. over torch.distributed); every rank opens the others' mailboxes and creates
  * the group with all mailbox pointers (its own at index rank). b200_moe_ffn_ep then runs the rank's experts like
  * b200_moe_ffn and leaves in `out` the FULL weighted sum over all ranks' experts (every rank gets the same out). All
- * ranks must call it in the same order with the same T (<= max_tokens) and H. A rank that never arrives makes the
+ * ranks must call it in the same order with the same T (<= max_tokens) and H; the experts are Q8_0 (tensor-core path).
+ * A rank that never arrives makes the
  * others give up after a bounded wait (B200_ERR_TIMEOUT from b200_synchronize; see b200_ep_set_timeout). */
 typedef struct b200_ep_group b200_ep_group;
 b200_status b200_ep_mailbox_alloc(b200_context * ctx, int world, int64_t max_tokens, int64_t hidden, void ** mailbox, void * ipc_handle);
