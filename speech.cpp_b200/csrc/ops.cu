@@ -478,7 +478,8 @@ static cudaError_t launch_tma(const GemvParams & p0, cudaStream_t st, bool pdl, 
     gx = (p.N + rpc - 1) / rpc;
     // Ring geometry: 8 stages (one chunk in flight per consumer warp) of ring / 8 bytes; measured on B200 with large
     // Q8_0 / Q4_K / Q6_K products, a 192 KB ring of 24 KB stages at one CTA per SM streamed fastest.
-    // B200_TMA_RING_KB / B200_TMA_STAGES / B200_TMA_CTAS_PER_SM override it (tuning).
+    // B200_TMA_RING_KB / B200_TMA_STAGES / B200_TMA_CTAS_PER_SM override it: the ring-geometry tests run other
+    // shapes through these (results must not change with the geometry).
     static const int64_t env_ring = [] { const char * e = getenv("B200_TMA_RING_KB"); return e ? atoll(e) * 1024 : 0; }();
     static const int64_t env_stages = [] { const char * e = getenv("B200_TMA_STAGES"); return e ? atoll(e) : 8; }();
     const size_t act = act_smem_bytes(p.w.type, K, NC) + 256;
@@ -501,7 +502,7 @@ static cudaError_t launch_tma(const GemvParams & p0, cudaStream_t st, bool pdl, 
     const size_t smem = tma_smem_bytes<T, NC>(p.w.type, K, (int) rps, (int) stages);
     if (smem > 220 * 1024) return cudaErrorInvalidValue;
     // one CTA per SM: 16 consumer warps (single column; measured faster for the large HBM-bound products);
-    // B200_TMA_WARPS=8 keeps 8 (tuning)
+    // B200_TMA_WARPS=8 keeps 8 (the geometry tests' other form)
     static const int env_warps = [] { const char * e = getenv("B200_TMA_WARPS"); return e ? atoi(e) : 16; }();
     if constexpr (NC == 1) {
         if (per_sm == 1 && env_warps == 16) return launch_tma_cw<T, NC, 2 * kTmaConsumerWarps>(p, gx, smem, st, pdl);
