@@ -19,12 +19,15 @@
 // An expert-parallel group's view of every rank's mailbox (peer.cu): inbox [G][ceil(T_max / G)][H] float, final
 // [T_max][H] float, two arrival counters; peer[g] is rank g's mailbox mapped into this process (peer[rank] its own).
 constexpr int kEpMaxRanks = 8;
+constexpr int kEpStateCtas = 4;    // words of an expert-parallel group's state before the per-CTA call counts
+constexpr int kEpMaxCtas = 1024;   // CTAs of the combine kernel at most (one per SM)
+
 struct b200_ep_group {
     int rank = 0, G = 1;
     int64_t T_max = 0, H = 0;
     void * peer[kEpMaxRanks] = {};
-    unsigned * calls = nullptr;  // [4]: this rank's calls so far (the counters' epoch), its CTAs done with steps 1 and 2,
-                                 // and the broken flag (a wait gave up)
+    unsigned * calls = nullptr;  // [1]: the broken flag (a poll gave up); [kEpStateCtas + c]: the calls CTA c has
+                                 // completed (its tags)
     uint64_t timeout_ns = 2000000000ull;  // how long one wait of the combine may take
 };
 

@@ -2,47 +2,35 @@
 // experts (TextModel::experts, src/families/drama3/text-model.cpp:198-221) fused with a two-shot all-reduce.
 //
 // Every rank of an expert-parallel group holds a "mailbox" device buffer (cudaMalloc, shared with the other ranks by
-// CUDA IPC handles): inbox [G][Ts][H] float (partial sums of the owner's token slice from each rank), final [T][H]
-// float (the reduced output), and two arrival counters. Token slice g = tokens [g Ts, (g + 1) Ts) belongs to rank g.
-// One cooperative kernel per layer:
+// CUDA IPC handles): inbox [G][Ts][H] and final [T][H], both of tagged words. Token slice g = tokens [g Ts, (g + 1) Ts)
+// belongs to rank g. One cooperative kernel per layer (one CTA per SM, all resident):
 //   1. every CTA computes its tokens' partial sums over this rank's experts and stores each token's row into the
-//      owner's inbox (a plain store through the peer mapping; the owner's own rows stay local);
-//   2. once every CTA of every rank has stored its rows, the CTAs sum their share of this rank's slice over the G
-//      inboxes in rank order (the result does not depend on timing) and store the sums into every rank's final
-//      buffer;
-//   3. once every rank's sums are stored, the CTAs copy final to the caller's output.
-// Arrival: after a CTA barrier, one thread per CTA makes the CTA's stores visible at system scope (one fence per
-// CTA) and counts the CTA in a local counter; the CTA that completes the count tells every rank with one system-scope
-// release each (G remote updates per step). Counters only grow: the targets of call k are (k + 1) x CTAs locally and
-// (k + 1) x G remotely, k a device word this rank advances at the end of the call, so no reset is needed between
-// layers or steps (also under graph replay). A rank starts writing call k + 1 only after every rank finished reading
-// call k (step 3 waits for all of step 2).
-// Every wait is bounded in time (the group's limit, 2 s unless set). A wait that gives up records B200_DEVERR_TIMEOUT
-// and marks the group broken: the counters of the ranks are then out of step, so every later call on the group
-// returns at once with the same error (b200_synchronize reports B200_ERR_TIMEOUT) until the group is destroyed and a
-// new one created. No multicast, no NVLS: plain peer loads and stores.
+//      owner's inbox (plain stores through the peer mapping; the owner's own rows stay local);
+//   2. the CTAs sum their share of this rank's slice over the G inboxes in rank order (the result does not depend on
+//      timing) and store the sums into every rank's final buffer;
+//   3. the CTAs copy final to the caller's output.
+// Every value travels with its call's tag in one 8-byte word {float bits, tag}, written by one store: a reader polls
+// the words it needs until their tags are the current call's, so a value proves its own arrival and no fence, counter
+// or barrier separates the steps (the stores of one word are single-copy atomic over NVLink as in local memory). The
+// tag of call k is k + 1, k the calls this CTA has completed (a per-CTA device word): every CTA of every rank takes
+// part in every call, so all agree. A rank writes call k + 1's inbox words only after it has read all of call k's
+// final words, each stored by its owner after that owner had read the corresponding inbox words, so no word is
+// overwritten before it has been read.
+// Every poll is bounded in time (the group's limit, 2 s unless set). One that gives up records B200_DEVERR_TIMEOUT
+// and marks the group broken: the ranks' call counts are then out of step, so every later call on the group returns at
+// once with the same error (b200_synchronize reports B200_ERR_TIMEOUT) until the group is destroyed and a new one
+// created. No multicast, no NVLS: plain peer loads and stores.
 #include "internal.h"
 
 namespace b200 {
 
 // The device side of a b200_ep_group: every rank's mailbox parts.
 struct PeerGroupDev {
-    float * inbox[kEpMaxRanks];      // rank g's inbox
-    float * final_[kEpMaxRanks];     // rank g's final buffer
-    unsigned * flags[kEpMaxRanks];   // rank g's counters: [0] step 1 arrivals, [1] step 2 arrivals
+    unsigned long long * inbox[kEpMaxRanks];   // rank g's inbox [G][Ts][H] of {value, tag}
+    unsigned long long * final_[kEpMaxRanks];  // rank g's final buffer [T][H] of {value, tag}
 };
 
 namespace {
-
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned * p) {
-    unsigned v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
-__device__ __forceinline__ void red_release_sys(unsigned * p, unsigned v) {
-    asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
 
 __device__ __forceinline__ uint64_t global_ns() {
     uint64_t t;
@@ -50,46 +38,65 @@ __device__ __forceinline__ uint64_t global_ns() {
     return t;
 }
 
-// Waits (one thread) until *p >= target; false once timeout_ns have passed (or after 2^26 polls, whichever first).
-__device__ __forceinline__ bool wait_at_least(const unsigned * p, unsigned target, uint64_t timeout_ns) {
-    const uint64_t t0 = global_ns();
-    for (uint32_t i = 0; i < (1u << 26); i++) {
-        if ((int) (ld_acquire_sys(p) - target) >= 0) return true;
-        if ((i & 63) == 63 && global_ns() - t0 > timeout_ns) return false;
-        if (i > 512) __nanosleep(32);
+__device__ __forceinline__ unsigned long long tagged(float v, unsigned tag) {
+    return (unsigned long long) __float_as_uint(v) | ((unsigned long long) tag << 32);
+}
+
+// Two tagged words to (possibly peer) global memory, one 16-byte store.
+__device__ __forceinline__ void st_pair(unsigned long long * p, unsigned long long a, unsigned long long b) {
+    asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+}
+
+__device__ __forceinline__ void ld_pair(const unsigned long long * p, unsigned long long & a, unsigned long long & b) {
+    asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
+// Polls two tagged words until both carry `tag`; false once timeout_ns have passed or another thread of the CTA gave
+// up (failed).
+__device__ __forceinline__ bool poll_pair(const unsigned long long * p, unsigned tag, uint64_t timeout_ns, volatile int * failed,
+                                          float & x, float & y) {
+    unsigned long long a, b;
+    ld_pair(p, a, b);
+    if ((unsigned) (a >> 32) == tag && (unsigned) (b >> 32) == tag) {
+        x = __uint_as_float((unsigned) a);
+        y = __uint_as_float((unsigned) b);
+        return true;
     }
+    const uint64_t t0 = global_ns();
+    for (uint32_t i = 1; i < (1u << 26); i++) {
+        if (*failed) return false;
+        ld_pair(p, a, b);
+        if ((unsigned) (a >> 32) == tag && (unsigned) (b >> 32) == tag) {
+            x = __uint_as_float((unsigned) a);
+            y = __uint_as_float((unsigned) b);
+            return true;
+        }
+        if ((i & 63) == 63 && global_ns() - t0 > timeout_ns) break;
+        if (i > 256) __nanosleep(64);
+    }
+    *failed = 1;
     return false;
 }
 
-// This CTA's part of a step is stored (the caller has passed a CTA barrier): one system-scope fence makes it visible
-// beyond this GPU, then the CTA counts itself; the CTA that completes the count tells every rank.
-__device__ __forceinline__ void arrive_all(unsigned * local, unsigned local_target, unsigned * const * flags, int G, int which) {
-    __threadfence_system();
-    unsigned old;
-    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(local), "r"(1u) : "memory");
-    if (old + 1u == local_target)
-        for (int g = 0; g < G; g++) red_release_sys(&flags[g][which], 1u);
-}
-
-// state: [0] calls completed (the counters' epoch), [1] [2] this rank's CTAs done with steps 1 and 2, [3] broken.
+// state: [1] broken (a poll gave up), [kEpStateCtas + c] the calls CTA c has completed.
 __global__ void __launch_bounds__(256) moe_combine_allreduce_kernel(const float * __restrict__ down, const float * __restrict__ w,
                                                                     const int32_t * __restrict__ inv, int T, int top_k, int H,
                                                                     int rank, int G, int Ts, PeerGroupDev grp, unsigned * state,
                                                                     uint64_t timeout_ns, float * __restrict__ out, unsigned * err) {
-    __shared__ int ok;
+    __shared__ volatile int failed;
     const int nct = gridDim.x, c = blockIdx.x;
-    const unsigned k = *reinterpret_cast<volatile unsigned *>(state);
-    if (*reinterpret_cast<volatile unsigned *>(state + 3)) {  // a wait of an earlier call gave up: refuse at once
+    if (*reinterpret_cast<volatile unsigned *>(state + 1)) {  // a poll of an earlier call gave up: refuse at once
         if (c == 0 && threadIdx.x == 0) atomicOr(err, B200_DEVERR_TIMEOUT);
         return;
     }
-    const unsigned target = (k + 1u) * (unsigned) G;         // remote arrivals: one per rank per call
-    const unsigned local_target = (k + 1u) * (unsigned) nct;  // this rank's CTAs per call
-    const int H4 = H / 4;
+    if (threadIdx.x == 0) failed = 0;
+    const unsigned tag = *reinterpret_cast<volatile unsigned *>(state + kEpStateCtas + c) + 1u;
+    __syncthreads();
+    const int H4 = H / 4, H2 = H / 2;
     // ---- 1. partial sums of this rank's experts, pushed to each token's owner ----
     for (int t = c; t < T; t += nct) {
         const int g = t / Ts, tl = t - g * Ts;
-        float4 * dst = reinterpret_cast<float4 *>(grp.inbox[g] + ((int64_t) rank * Ts + tl) * H);
+        unsigned long long * dst = grp.inbox[g] + ((int64_t) rank * Ts + tl) * H;
         for (int h4 = threadIdx.x; h4 < H4; h4 += blockDim.x) {
             float4 sum = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
             bool any = false;
@@ -102,61 +109,50 @@ __global__ void __launch_bounds__(256) moe_combine_allreduce_kernel(const float 
                 sum = any ? make_float4(__fadd_rn(sum.x, v.x), __fadd_rn(sum.y, v.y), __fadd_rn(sum.z, v.z), __fadd_rn(sum.w, v.w)) : v;
                 any = true;
             }
-            dst[h4] = sum;
+            st_pair(dst + 4 * h4, tagged(sum.x, tag), tagged(sum.y, tag));
+            st_pair(dst + 4 * h4 + 2, tagged(sum.z, tag), tagged(sum.w, tag));
+        }
+    }
+    // ---- 2. this rank's slice: the G ranks' partials summed in rank order, stored to every rank's final buffer ----
+    const int t0 = rank * Ts, t1 = min(T, t0 + Ts);
+    for (int t = t0 + c; t < t1 && !failed; t += nct) {
+        const int tl = t - t0;
+        for (int h2 = threadIdx.x; h2 < H2 && !failed; h2 += blockDim.x) {
+            float sx = 0.0f, sy = 0.0f;
+            for (int g = 0; g < G; g++) {
+                float x, y;
+                if (!poll_pair(grp.inbox[rank] + ((int64_t) g * Ts + tl) * H + 2 * h2, tag, timeout_ns, &failed, x, y)) break;
+                sx = g ? __fadd_rn(sx, x) : x;
+                sy = g ? __fadd_rn(sy, y) : y;
+            }
+            if (failed) break;
+            const unsigned long long a = tagged(sx, tag), b = tagged(sy, tag);
+            for (int g = 0; g < G; g++) st_pair(grp.final_[g] + (int64_t) t * H + 2 * h2, a, b);
+        }
+    }
+    // ---- 3. the reduced output, every token ----
+    for (int t = c; t < T && !failed; t += nct) {
+        for (int h2 = threadIdx.x; h2 < H2 && !failed; h2 += blockDim.x) {
+            float x, y;
+            if (!poll_pair(grp.final_[rank] + (int64_t) t * H + 2 * h2, tag, timeout_ns, &failed, x, y)) break;
+            reinterpret_cast<float2 *>(out + (int64_t) t * H)[h2] = make_float2(x, y);
         }
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-        arrive_all(&state[1], local_target, grp.flags, G, 0);
-        ok = wait_at_least(&grp.flags[rank][0], target, timeout_ns);
-    }
-    __syncthreads();
-    if (ok) {
-        // ---- 2. this rank's slice: sum over the G inboxes in rank order, stored to every rank's final buffer ----
-        const int t0 = rank * Ts, t1 = min(T, t0 + Ts);
-        for (int t = t0 + c; t < t1; t += nct) {
-            const int tl = t - t0;
-            for (int h4 = threadIdx.x; h4 < H4; h4 += blockDim.x) {
-                // written by other GPUs since the last call: read through L2 (__ldcg), never from a stale L1 line
-                float4 v[kEpMaxRanks];
-#pragma unroll
-                for (int g = 0; g < kEpMaxRanks; g++)
-                    if (g < G) v[g] = __ldcg(reinterpret_cast<const float4 *>(grp.inbox[rank] + ((int64_t) g * Ts + tl) * H) + h4);
-                float4 sum = v[0];
-#pragma unroll
-                for (int g = 1; g < kEpMaxRanks; g++)
-                    if (g < G) sum = make_float4(__fadd_rn(sum.x, v[g].x), __fadd_rn(sum.y, v[g].y), __fadd_rn(sum.z, v[g].z), __fadd_rn(sum.w, v[g].w));
-                for (int g = 0; g < G; g++) reinterpret_cast<float4 *>(grp.final_[g] + (int64_t) t * H)[h4] = sum;
-            }
+        if (failed) {
+            atomicOr(err, B200_DEVERR_TIMEOUT);
+            atomicExch(state + 1, 1u);  // the ranks' call counts are out of step from here on
         }
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            arrive_all(&state[2], local_target, grp.flags, G, 1);
-            ok = wait_at_least(&grp.flags[rank][1], target, timeout_ns);
-        }
-        __syncthreads();
+        state[kEpStateCtas + c] = tag;  // this CTA's call is over
     }
-    if (ok) {
-        // ---- 3. the reduced output, every token ----
-        for (int t = c; t < T; t += nct) {
-            const float4 * src = reinterpret_cast<const float4 *>(grp.final_[rank] + (int64_t) t * H);
-            float4 * o = reinterpret_cast<float4 *>(out + (int64_t) t * H);
-            for (int h4 = threadIdx.x; h4 < H4; h4 += blockDim.x) o[h4] = __ldcg(src + h4);
-        }
-    } else if (threadIdx.x == 0) {
-        atomicOr(err, B200_DEVERR_TIMEOUT);
-        atomicExch(state + 3, 1u);  // the ranks' counters are out of step from here on
-    }
-    // the call is over for this CTA; CTA 0 advances the call count once every CTA of this rank is past step 2 (the
-    // step 2 wait proves it: all CTAs of all ranks arrived there after reading k)
-    if (c == 0 && threadIdx.x == 0) atomicAdd(state, 1u);
 }
 
 }  // namespace
 
 size_t peer_mailbox_bytes(int G, int T_max, int H) {
     const int Ts = (T_max + G - 1) / G;
-    return (((size_t) G * Ts * H * 4 + 255) & ~(size_t) 255) + (((size_t) T_max * H * 4 + 255) & ~(size_t) 255) + 256;
+    return (((size_t) G * Ts * H * 8 + 255) & ~(size_t) 255) + (((size_t) T_max * H * 8 + 255) & ~(size_t) 255);
 }
 
 cudaError_t launch_moe_combine_allreduce(const float * down, const float * w, const int32_t * inv, int64_t T, int64_t top_k, int64_t H,
@@ -168,15 +164,14 @@ cudaError_t launch_moe_combine_allreduce(const float * down, const float * w, co
     const int Ts = (int) ((ep->T_max + ep->G - 1) / ep->G);
     for (int g = 0; g < ep->G; g++) {
         uint8_t * base = (uint8_t *) ep->peer[g];
-        grp.inbox[g] = (float *) base;
-        grp.final_[g] = (float *) (base + (((size_t) ep->G * Ts * ep->H * 4 + 255) & ~(size_t) 255));
-        grp.flags[g] = (unsigned *) (base + (((size_t) ep->G * Ts * ep->H * 4 + 255) & ~(size_t) 255) +
-                                     (((size_t) ep->T_max * ep->H * 4 + 255) & ~(size_t) 255));
+        grp.inbox[g] = (unsigned long long *) base;
+        grp.final_[g] = (unsigned long long *) (base + (((size_t) ep->G * Ts * ep->H * 8 + 255) & ~(size_t) 255));
     }
     int per_sm = 0;
     cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, moe_combine_allreduce_kernel, 256, 0);
     if (e != cudaSuccess) return e;
-    const int nct = num_sms < per_sm * num_sms ? num_sms : per_sm * num_sms;  // one CTA per SM: all co-resident
+    int nct = num_sms < per_sm * num_sms ? num_sms : per_sm * num_sms;  // one CTA per SM: all co-resident
+    if (nct > kEpMaxCtas) nct = kEpMaxCtas;
     int Ti = (int) T, ki = (int) top_k, Hi = (int) H, r = ep->rank, G = ep->G, Tsi = Ts;
     unsigned * state = ep->calls;
     uint64_t timeout_ns = ep->timeout_ns;
@@ -245,7 +240,8 @@ b200_status b200_ep_create(b200_context * ctx, int rank, int world, int64_t max_
     g->T_max = max_tokens;
     g->H = hidden;
     for (int i = 0; i < world; i++) g->peer[i] = mailboxes[i];
-    if (cudaMalloc(&g->calls, 4 * sizeof(unsigned)) != cudaSuccess || cudaMemset(g->calls, 0, 4 * sizeof(unsigned)) != cudaSuccess) {
+    const size_t cb = (kEpStateCtas + kEpMaxCtas) * sizeof(unsigned);
+    if (cudaMalloc(&g->calls, cb) != cudaSuccess || cudaMemset(g->calls, 0, cb) != cudaSuccess) {
         delete g;
         ctx->last_error = "ep_create: device allocation";
         return B200_ERR_ALLOC;
